@@ -1,0 +1,411 @@
+#!/usr/bin/env python
+"""Benchmark of the routed-expert int4 MoE hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl wisp|reference]
+
+Default workload (the configuration its metric is
+quoted on at 1/2/4/8 GPUs): a stack of 4 MoE layers, 384 routed experts + 1
+shared expert, hidden 7168, moe_intermediate 2048, softmax top-8, int4 group
+128 weights, 256 decode tokens per step, bf16 activations, seed 3. A step is
+one pass of the 256 tokens through the 4 layers (router, dispatch, grouped
+gate/up + SwiGLU, grouped down + weighted combine; between layers the output
+is RMS-rescaled to the next layer's bf16 input). With N GPUs the routed
+experts are sharded N ways and tokens are exchanged with NCCL all-to-all
+(strong scaling: the total work is fixed).
+
+The metric is MoE-layer tokens/s = tokens x layers per second (whole job).
+Every step streams ~35 GB of expert weights, far larger than the 126 MB L2,
+so no flush is needed between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MoE-layer tokens/s; int4 weight GB/s vs 8 TB/s HBM at 1/2/4/8 B200"
+UNIT = "tokens/s"
+
+
+def _peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d.get("hbm_gbs", 6650.0), "bf16_tflops": d.get("bf16_tflops", 1590.0),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"unavailable": "nvidia-smi not runnable"}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"unavailable": "no samples"}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# Reference CPU path (the reference engine's own compiled C code)
+# ---------------------------------------------------------------------------
+
+def _cpu_sample_setup(spec, n_blobs: int = 16, seed: int = 0):
+    """Host-side inputs for the reference CPU path: the fp16 router of the
+    configuration's shape and n_blobs distinct expert blobs addressed
+    cyclically by expert id (timing only; parity is tested in tests/)."""
+    import numpy as np
+    from wisp_b200.blob import Int4Matrix, pack_blob
+
+    rng = np.random.default_rng(seed)
+    M, I, gs = spec.hidden, spec.inter, spec.group_size
+
+    def mat(rows, cols):
+        n = rows * cols
+        return Int4Matrix(rng.integers(0, 256, n // 2, dtype=np.uint8),
+                          np.float16(rng.uniform(0.004, 0.02, n // gs)).view(np.uint16),
+                          None, rows, cols)
+
+    blobs = [np.frombuffer(pack_blob(mat(I, M), mat(I, M), mat(M, I), gs), np.uint8)
+             for _ in range(n_blobs)]
+    router = np.float16(rng.standard_normal((spec.n_experts, M)) * 0.02).view(np.uint16)
+    xs = [rng.standard_normal(M).astype(np.float32) for _ in range(8)]
+    return router, blobs, xs
+
+
+def _cpu_token_time(ref, spec, router, blobs, xs, n_tokens: int) -> float:
+    """Seconds for n_tokens single-token passes through one layer."""
+    E = spec.n_experts
+    table = [blobs[e % len(blobs)] for e in range(E)]
+    shared = blobs[-1] if spec.has_shared else None
+    t0 = time.perf_counter()
+    for i in range(n_tokens):
+        ref.moe_token(router, None, xs[i % len(xs)], spec.top_k, table, shared)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(spec, budget_s: float = 12.0) -> dict:
+    from oracle.oracle import RefCPU
+    if not RefCPU.available():
+        return {"unavailable": "oracle/_ref/libwisp_ref.so not built"}
+    ref = RefCPU()
+    router, blobs, xs = _cpu_sample_setup(spec)
+    _cpu_token_time(ref, spec, router, blobs, xs, 1)  # warm
+    n, el = 0, 0.0
+    while el < budget_s and n < 256:
+        el += _cpu_token_time(ref, spec, router, blobs, xs, 1)
+        n += 1
+    res = {"value": n / el, "unit": UNIT, "cores": ref.threads(), "kind": "reference",
+           "sample": f"{n} single-token passes through one layer of the configuration via the "
+                     f"reference's scalar/OpenMP CPU run_moe branch (router + shared + top-{spec.top_k} "
+                     f"experts), {len(blobs)} distinct expert blobs"}
+    if RefCPU.available(avx512=True):
+        ra = RefCPU(avx512=True)
+        _cpu_token_time(ra, spec, router, blobs, xs, 1)
+        m = max(2, n // 2)
+        t = _cpu_token_time(ra, spec, router, blobs, xs, m)
+        res["avx512_build"] = {"value": m / t, "unit": UNIT, "valid_output": False,
+                               "note": "reference's own -Ofast -march=icelake-server build; "
+                                       "its AVX-512 int4 GEMV returns wrong values"}
+    return res
+
+
+def reference_arm(args, spec) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle.oracle import RefCPU
+    cfg = {"workload": spec.name, "layers": spec.layers, "tokens_per_step": spec.tokens,
+           "hidden": spec.hidden, "inter": spec.inter, "experts": spec.n_experts,
+           "shared_experts": int(spec.has_shared), "top_k": spec.top_k,
+           "group_size": spec.group_size}
+    line = {"impl": "reference", "metric": METRIC, "unit": UNIT, "higher_is_better": True,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "dtype": "f32", "data": "synthetic", "config": cfg, "vs_baseline": None}
+    if not RefCPU.available():
+        line.update({"unavailable": "reference CPU library oracle/_ref/libwisp_ref.so not built"})
+        print(json.dumps(line))
+        return
+    ref = RefCPU()
+    router, blobs, xs = _cpu_sample_setup(spec)
+    tokens_per_step = 1
+    for _ in range(args.warmup):
+        _cpu_token_time(ref, spec, router, blobs, xs, tokens_per_step)
+    t = _cpu_token_time(ref, spec, router, blobs, xs, tokens_per_step * args.steps)
+    value = tokens_per_step * args.steps / t
+    line.update({"value": value, "ms_per_step": 1e3 * t / args.steps, "scaling": "strong",
+                 "cpu_baseline": {"value": value, "unit": UNIT, "cores": ref.threads(),
+                                  "kind": "reference",
+                                  "sample": "one token through one MoE layer per step (reference "
+                                            "scalar/OpenMP CPU run_moe branch)"},
+                 "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                         "d2h_bytes_per_step": 0}})
+    print(json.dumps(line))
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="ep_stack")
+    ap.add_argument("--impl", default="wisp", choices=["wisp", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel-reps", type=int, default=5)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    from wisp_b200 import synth
+    spec = synth.CONFIGS[args.config]
+    if args.impl == "reference":
+        reference_arm(args, spec)
+        return
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import ctypes as C
+    from wisp_b200 import abi
+    from wisp_b200.moe import MoeLayer
+    from wisp_b200.ep import EpLayer, block_range
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    lib = abi.lib()
+    stream = torch.cuda.current_stream()
+    T_all, L = spec.tokens, spec.layers
+
+    # -- model ------------------------------------------------------------
+    keep = None if world == 1 else range(*block_range(spec.n_experts, world, rank))
+    layers_w, x_all = synth.make_model(spec, dev, keep=keep)
+    t0, t1 = block_range(T_all, world, rank)
+    x0 = x_all[t0:t1].contiguous()
+    T = t1 - t0
+    if world == 1:
+        layers = [MoeLayer(lw, T) for lw in layers_w]
+    else:
+        layers = [EpLayer(spec, lw, T, rank, world) for lw in layers_w]
+    outs = [torch.empty((T, spec.hidden), dtype=torch.float32, device=dev) for _ in range(L)]
+    xs = [x0] + [torch.empty_like(x0) for _ in range(L - 1)]
+
+    def step(x_in):
+        xs[0] = x_in
+        for l in range(L):
+            if world == 1:
+                layers[l].forward(xs[l], outs[l])
+            else:
+                layers[l].forward(xs[l], outs[l])
+            if l + 1 < L:
+                abi.call("wisp_b200_rms_rescale", outs[l].data_ptr(), xs[l + 1].data_ptr(), T,
+                         spec.hidden, 1e-6, stream.cuda_stream)
+        return outs[-1]
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step(x0)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step(x0)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = T_all * L / (ms / 1e3)
+
+    # error words of the tensor-core kernels
+    if world == 1:
+        for lay in layers:
+            lay.check()
+
+    # -- algorithmic bytes of one step (routing is identical every step) --
+    used = []
+    for l in range(L):
+        if world == 1:
+            idx = layers[l].idx
+        else:
+            idx = layers[l].idx
+        u = torch.zeros(spec.n_experts, dtype=torch.int32, device=dev)
+        u[idx.reshape(-1).long()] = 1
+        if world > 1:
+            dist.all_reduce(u, op=dist.ReduceOp.MAX)
+        used.append(int(u.sum().item()))
+    eb = spec.expert_bytes()
+    router_bytes = spec.n_experts * spec.hidden * 2
+    shared_reads = world if spec.has_shared else 0   # every rank reads the shared expert
+    step_bytes = sum((u * eb + shared_reads * eb + world * router_bytes) for u in used)
+    hbm_gbs = step_bytes / (ms / 1e3) / 1e9
+
+    # -- dominant kernel: the grouped int4 FFN (gate/up + down), timed with
+    #    CUDA events around its launches on the launching stream (N=1) ------
+    peaks = _peaks()
+    roofline = None
+    if world == 1:
+        lay = layers[0]
+        cfg = lay.cfg
+        V = spec.n_virtual
+        R = T * spec.top_k + (T if spec.has_shared else 0)
+        counts = torch.empty(V, dtype=torch.int32, device=dev)
+        segs = torch.empty(16 * V, dtype=torch.uint8, device=dev)
+        row_token = torch.empty(R, dtype=torch.int32, device=dev)
+        row_w = torch.empty(R, dtype=torch.float32, device=dev)
+        xp = torch.empty((R, spec.hidden), dtype=torch.float16, device=dev)
+        h = torch.empty((R, spec.inter), dtype=torch.float16, device=dev)
+        tiles = torch.empty(lib.wisp_b200_tiles_words(V), dtype=torch.int32, device=dev)
+        flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        out = torch.zeros((T, spec.hidden), dtype=torch.float32, device=dev)
+        abi.call("wisp_b200_dispatch_plan", C.byref(cfg), lay.idx.data_ptr(), lay.wt.data_ptr(),
+                 counts.data_ptr(), segs.data_ptr(), row_token.data_ptr(), row_w.data_ptr(),
+                 stream.cuda_stream)
+        abi.call("wisp_b200_pack_rows", x0.data_ptr(), row_token.data_ptr(), R, spec.hidden,
+                 xp.data_ptr(), stream.cuda_stream)
+        table = [lw.table for lw in layers_w]
+        evs = []
+        for rep in range(args.kernel_reps):
+            for l in range(L):   # rotate the layers' weights so L2 never holds them
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                abi.call("wisp_b200_grouped_ffn", C.byref(cfg), table[l].data_ptr(), segs.data_ptr(), V, R,
+                         xp.data_ptr(), h.data_ptr(), 0, row_token.data_ptr(), row_w.data_ptr(),
+                         out.data_ptr(), tiles.data_ptr(), flag.data_ptr(), stream.cuda_stream)
+                b.record(stream)
+                evs.append((a, b))
+        torch.cuda.synchronize()
+        abi.call("wisp_b200_check_error_flag", flag.data_ptr(), stream.cuda_stream)
+        kms = statistics.mean(a.elapsed_time(b) for a, b in evs[L:])   # first pass = warm-up
+        k_bytes = (used[0] + (1 if spec.has_shared else 0)) * eb
+        achieved = k_bytes / (kms / 1e3) / 1e9
+        roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                    "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                    "traffic": None, "kernel": "grouped int4 FFN (gate/up+SwiGLU, down+combine)",
+                    "kernel_ms": round(kms, 4), "algorithmic_bytes": k_bytes,
+                    "peak_source": peaks["source"], "vs_8tbs": round(achieved / 8000.0, 4)}
+
+    # -- end to end through the public API with host buffers ---------------
+    e2e = None
+    x_host = x0.cpu().pin_memory()
+    out_host = torch.empty((T, spec.hidden), dtype=torch.float32).pin_memory()
+    x_dev = torch.empty_like(x0)
+    for _ in range(2):
+        x_dev.copy_(x_host, non_blocking=True)
+        step(x_dev)
+        out_host.copy_(outs[-1], non_blocking=True)
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        x_dev.copy_(x_host, non_blocking=True)
+        step(x_dev)
+        out_host.copy_(outs[-1], non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ems = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ems], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ems = float(t.item())
+    e2e = {"value": T_all * L / (ems / 1e3), "unit": UNIT,
+           "h2d_bytes_per_step": x_host.numel() * 2 * world,
+           "d2h_bytes_per_step": out_host.numel() * 4 * world}
+
+    launches_per_layer = 11 if world == 1 else 12 + (4 if spec.has_shared else 0)
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int4 weights, fp16 MMA operands, fp32 accumulate",
+        "data": "synthetic (seeded, BASELINE distributions)",
+        "config": {"workload": spec.name, "layers": L, "tokens_per_step": T_all,
+                   "hidden": spec.hidden, "inter": spec.inter, "experts": spec.n_experts,
+                   "shared_experts": int(spec.has_shared), "top_k": spec.top_k,
+                   "group_size": spec.group_size, "parallelism": f"ep{world}",
+                   "l2": f"inputs larger than L2 ({step_bytes / 1e9:.1f} GB of expert weights per step)"},
+        "hbm": {"step_bytes": step_bytes, "achieved_gbs": round(hbm_gbs, 1),
+                "frac_of_measured": round(hbm_gbs / peaks["hbm_gbs"], 4),
+                "frac_of_8tbs": round(hbm_gbs / 8000.0, 4), "experts_touched_per_layer": used},
+        "roofline": roofline, "e2e": e2e, "clocks": clk,
+        "gpu_launches": launches_per_layer * L * args.steps,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(spec)
+    if rank == 0:
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

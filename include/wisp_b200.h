@@ -1,0 +1,292 @@
+/*
+ * wisp_b200.h -- C ABI of libwisp_b200.so, the B200-native (sm_100a)
+ * routed-expert int4 FFN hot path for the WISP engine.
+ *
+ * Part 1 re-exports the reference engine's GPU launcher ABI with identical
+ * names and signatures, so the reference C engine links against this
+ * library in place of its csrc/cuda/*.cu objects.
+ * Part 2 adds the fused entry points the reference's gpu_expert_ffn /
+ * run_moe would call instead of the dequant -> gemv -> scale_accum chain.
+ *
+ * No entry point allocates device memory per call: the caller passes every
+ * buffer (workspace sizes come from the *_workspace_bytes queries). All
+ * pointers named d_* are device pointers; launches are asynchronous on the
+ * given stream.
+ */
+#ifndef WISP_B200_H
+#define WISP_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* --------------------------------------------------------------------------
+ * Engine types shared with the reference ABI. A translation unit that has
+ * already included the reference's csrc/core/wisp_engine.h defines
+ * WISP_B200_NO_ENGINE_TYPES before including this header.
+ * Layouts are identical to csrc/core/wisp_engine.h:32-40, 50-64, 214-251.
+ * ------------------------------------------------------------------------ */
+#ifndef WISP_B200_NO_ENGINE_TYPES
+typedef uint16_t wisp_half; /* raw fp16 bits (the reference's C view) */
+
+typedef enum {
+    WISP_OK = 0,
+    WISP_ERR_OOM = 1,
+    WISP_ERR_IO = 2,
+    WISP_ERR_CUDA = 3,
+    WISP_ERR_INVALID_ARG = 4,
+    WISP_ERR_EXPERT_MISS = 5,
+    WISP_ERR_MODEL = 6,
+    WISP_ERR_TIMEOUT = 7,
+} WispError;
+
+typedef struct {
+    WispError code;
+    char message[512];
+    const char* file;
+    int line;
+} WispErrCtx;
+
+#define WISP_EXPERT_MAGIC 0x57455850u
+#define WISP_EXPERT_VERSION 1u
+#define WISP_EXPERT_NMATS 3
+
+#pragma pack(push, 1)
+typedef struct {
+    uint32_t rows;
+    uint32_t cols;
+    uint64_t packed_bytes;
+    uint64_t scales_bytes;
+    uint64_t zeros_bytes;
+} WispExpertMat;
+
+typedef struct {
+    uint32_t magic;
+    uint32_t version;
+    uint32_t layer_id;
+    uint32_t expert_id;
+    uint32_t group_size;
+    uint32_t n_mats;
+    WispExpertMat mats[WISP_EXPERT_NMATS];
+} WispExpertHeader; /* exactly 120 bytes */
+#pragma pack(pop)
+
+typedef struct {
+    size_t packed_off[WISP_EXPERT_NMATS];
+    size_t scales_off[WISP_EXPERT_NMATS];
+    size_t zeros_off[WISP_EXPERT_NMATS];
+    uint32_t rows[WISP_EXPERT_NMATS];
+    uint32_t cols[WISP_EXPERT_NMATS];
+    uint32_t group_size;
+    size_t total_bytes;
+    int valid;
+} WispExpertMeta;
+#endif /* WISP_B200_NO_ENGINE_TYPES */
+
+/* ==========================================================================
+ * Part 1 -- reference launcher ABI (drop-in)
+ * ======================================================================== */
+
+/* Replaces csrc/cuda/expert_loader.cu:46-63 (declared at
+ * csrc/core/wisp_engine.h:545-550). cudaErrorInvalidValue when
+ * n_elements <= 0 or group_size <= 0, else the launch status. */
+cudaError_t launch_dequant_expert(const uint8_t* d_packed, const wisp_half* d_scales,
+                                  const wisp_half* d_zeros, wisp_half* d_output,
+                                  int n_elements, int group_size, cudaStream_t stream);
+
+/* Replaces csrc/cuda/expert_loader.cu:67-97 (wisp_engine.h:551-559). */
+cudaError_t async_load_expert(const uint8_t* h_packed, const wisp_half* h_scales,
+                              const wisp_half* h_zeros, uint8_t* d_packed_tmp,
+                              wisp_half* d_scales_tmp, wisp_half* d_zeros_tmp,
+                              wisp_half* d_output, int n_elements, int group_size,
+                              cudaStream_t stream);
+
+/* Replaces csrc/cuda/matmul.cu:58-65 (wisp_engine.h:499-500): y = W x. */
+void wisp_gpu_gemv_f16(const wisp_half* W, const float* x, float* y, int rows, int cols,
+                       cudaStream_t s);
+
+/* Replaces csrc/cuda/matmul.cu:141-148 (wisp_engine.h:507-508). */
+void wisp_gpu_swiglu(const float* gate, const float* up, float* out, int n, cudaStream_t s);
+
+/* Replaces csrc/cuda/matmul.cu:198-205 (wisp_engine.h:509-511):
+ * h[r] = silu(Wg[r].x) * (Wu[r].x). */
+void wisp_gpu_swiglu_ffn(const wisp_half* Wg, const wisp_half* Wu, const float* x, float* h,
+                         int inter, int cols, cudaStream_t s);
+
+/* Replaces csrc/cuda/matmul.cu:156-161 (wisp_engine.h:512-513): acc += w x. */
+void wisp_gpu_scale_accum(float* acc, const float* x, float w, int n, cudaStream_t s);
+
+/* Replaces csrc/cuda/router.cu:140-171 (wisp_engine.h:534-537). Softmax
+ * top-k with renormalised weights; ties go to the lower expert index.
+ * out_idx / out_w are host (pinned) buffers filled by async copies on `s`;
+ * the caller synchronises `s` before reading them. top_k is clamped to 64;
+ * n_experts must be <= 1024. */
+void wisp_gpu_router_topk(const wisp_half* W, const wisp_half* bias, const float* x,
+                          float* logits_scratch, int n_experts, int hidden, int top_k,
+                          int* out_idx, float* out_w, cudaStream_t s);
+
+/* ==========================================================================
+ * Part 2 -- fused entry points
+ * ======================================================================== */
+
+/* Parse an expert blob header held in HOST memory. Same contract as the
+ * reference's wisp_expert_parse_header (csrc/core/wisp_engine.c:268-303):
+ * WISP_ERR_MODEL on a bad magic/version/n_mats or a truncated blob. */
+WispError wisp_b200_parse_expert_header(const void* blob, size_t blob_size,
+                                        WispExpertMeta* meta, WispErrCtx* err);
+
+/* One token, several experts, reference precision (fp32 activations):
+ *   d_acc[hidden] += sum_j weights[j] * down_j(silu(gate_j x) * up_j x)
+ * Replaces the per-expert loop of gpu_expert_ffn (csrc/core/wisp_engine.c:
+ * 1507-1531) as called from run_moe (:1666-1670), plus an int4 shared
+ * expert passed as one more blob with weight 1.0. d_blobs[j] is the device
+ * address of blob j (header at offset 0; the packed weights must be at least
+ * 8-byte aligned). weights is a HOST array. 1 <= n_blobs <= 16. The scratch
+ * holds the intermediate activations; its size comes from
+ * wisp_b200_expert_ffn_scratch_bytes. */
+size_t wisp_b200_expert_ffn_scratch_bytes(const WispExpertMeta* meta, int n_blobs);
+WispError wisp_b200_expert_ffn(const WispExpertMeta* meta, const void* const* d_blobs,
+                               const float* weights, int n_blobs, const float* d_x,
+                               float* d_acc, void* d_scratch, size_t scratch_bytes,
+                               cudaStream_t stream, WispErrCtx* err);
+
+/* --------------------------------------------------------------------------
+ * Batched MoE layer (T tokens, bf16 activations).
+ * ------------------------------------------------------------------------ */
+enum { WISP_SCORE_SOFTMAX = 0, WISP_SCORE_SIGMOID_GROUPED = 1 };
+
+typedef struct {
+    int tokens;        /* T */
+    int hidden;        /* M: multiple of 128 */
+    int inter;         /* I: multiple of 128 */
+    int n_experts;     /* routed experts E (<= 1024) */
+    int top_k;         /* <= 16 */
+    int group_size;    /* int4 quantisation group along K: 64 or 128 */
+    int scoring;       /* WISP_SCORE_* */
+    int n_groups;      /* sigmoid scoring: expert groups (E % n_groups == 0) */
+    int topk_groups;   /* sigmoid scoring: groups kept */
+    float routed_scaling; /* sigmoid scoring: weight multiplier */
+    int has_shared;    /* 1: an always-on shared expert of the same shape */
+    int router_fp16;   /* router weight dtype: 0 = bf16, 1 = fp16 (the
+                          reference's router ABI, wisp_engine.h:534-537) */
+} WispMoeConfig;
+
+/* One int4 matrix in the reference's packing (low nibble = even index,
+ * value = (nibble - 8) * scale + zero, groups along K). zeros may be NULL
+ * (symmetric). packed / scales / zeros must be 16-byte aligned. */
+typedef struct {
+    const uint8_t* packed;
+    const wisp_half* scales;
+    const wisp_half* zeros;
+} WispInt4Mat;
+
+/* gate [I x M], up [I x M], down [M x I]. */
+typedef struct {
+    WispInt4Mat gate, up, down;
+} WispInt4Expert;
+
+typedef struct {
+    const uint16_t* router_w;       /* bf16 or fp16 [E x M] (cfg->router_fp16) */
+    const float* router_bias;       /* fp32 [E], added before scoring; may be NULL */
+    const WispInt4Expert* experts;  /* DEVICE array: E routed experts, then the
+                                       shared expert when cfg->has_shared */
+} WispMoeWeights;
+
+size_t wisp_b200_moe_workspace_bytes(const WispMoeConfig* cfg);
+
+/* out[T x M] (fp32) = sum_k w[t,k] * expert_{idx[t,k]}(x_t) + shared(x_t).
+ * x: bf16 [T x M]. topk_idx / topk_w ([T x k], int32 / fp32) receive the
+ * routing and may be NULL. */
+WispError wisp_b200_moe_forward(const WispMoeConfig* cfg, const WispMoeWeights* w,
+                                const uint16_t* d_x, float* d_out, int* d_topk_idx,
+                                float* d_topk_w, void* d_workspace, size_t workspace_bytes,
+                                cudaStream_t stream, WispErrCtx* err);
+
+/* --------------------------------------------------------------------------
+ * Building blocks (used by the expert-parallel path and by tests).
+ * ------------------------------------------------------------------------ */
+
+/* Router only: d_idx / d_w [T x k]; d_logits (fp32 [T x E]) receives the
+ * logits, bias included. */
+WispError wisp_b200_route(const WispMoeConfig* cfg, const WispMoeWeights* w, const uint16_t* d_x,
+                          float* d_logits, int* d_idx, float* d_w, cudaStream_t stream,
+                          WispErrCtx* err);
+
+/* A contiguous run of activation rows that all go through one expert. */
+typedef struct {
+    int32_t expert;    /* index into the expert table */
+    int32_t row_begin; /* first row in the activation buffer */
+    int32_t rows;      /* number of rows (0 allowed) */
+    int32_t reserved;
+} WispSegment;
+
+/* Grouped expert FFN over pre-permuted rows.
+ *   d_xp:   fp16 [R x M] activation rows in interleaved K order (within each
+ *           8 K: 0,4,1,5,2,6,3,7) -- produced by wisp_b200_pack_rows.
+ *   d_segs: DEVICE array of n_segs segments.
+ *   d_h:    fp16 [R x I] scratch (interleaved K order).
+ *   mode 0: d_out[row_token[p] * M + m] += row_weight[p] * y[p, m] (atomic fp32)
+ *   mode 1: d_y[p * M + m] = y[p, m] (fp32 rows, no weighting)
+ * d_tiles: int32 scratch of wisp_b200_tiles_words(n_segs) words.
+ * d_error_flag: device int set to nonzero if a bounded wait gave up (may be
+ * NULL); check it with wisp_b200_check_error_flag. */
+size_t wisp_b200_tiles_words(int n_segs);
+WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const WispInt4Expert* d_experts,
+                                const WispSegment* d_segs, int n_segs, int rows_capacity,
+                                const uint16_t* d_xp, uint16_t* d_h, int mode,
+                                const int* d_row_token, const float* d_row_weight,
+                                float* d_out, int32_t* d_tiles, int* d_error_flag,
+                                cudaStream_t stream, WispErrCtx* err);
+
+/* Dispatch plan from a routing: one segment per expert (then the shared
+ * expert with every token when cfg->has_shared), rows sorted by (token,
+ * slot) inside each expert. d_counts [V], d_segs [V], d_row_token /
+ * d_row_weight [T*k (+T)], V = E (+1). Deterministic. */
+WispError wisp_b200_dispatch_plan(const WispMoeConfig* cfg, const int* d_idx, const float* d_w,
+                                  int* d_counts, WispSegment* d_segs, int* d_row_token,
+                                  float* d_row_weight, cudaStream_t stream, WispErrCtx* err);
+
+/* d_out[row_token[p]] += row_weight[p] * d_y[p] for p < n_rows (fp32 rows;
+ * atomic adds): the combine step of the expert-parallel path. */
+WispError wisp_b200_combine_rows(const float* d_y, const int* d_row_token, const float* d_row_weight,
+                                 int n_rows, int hidden, float* d_out, cudaStream_t stream,
+                                 WispErrCtx* err);
+
+/* Between stacked layers: d_out[t] = bf16(d_in[t] / rms(d_in[t])), fp32 in. */
+WispError wisp_b200_rms_rescale(const float* d_in, uint16_t* d_out, int tokens, int hidden,
+                                float eps, cudaStream_t stream, WispErrCtx* err);
+
+/* Copy bf16 rows into fp16 interleaved-K rows: xp[p] = x[src[p]] for
+ * p < n_rows (src may be NULL: identity). */
+WispError wisp_b200_pack_rows(const uint16_t* d_x, const int* d_src, int n_rows, int hidden,
+                              uint16_t* d_xp, cudaStream_t stream, WispErrCtx* err);
+
+/* Device error word written by the tcgen05 kernels when a bounded wait gave
+ * up (nonzero = the results of that launch are invalid). */
+WispError wisp_b200_check_error_flag(const int* d_error_flag, cudaStream_t stream,
+                                     WispErrCtx* err);
+
+/* Address of the device error word inside a wisp_b200_moe_forward
+ * workspace (cleared at the start of every forward). */
+int* wisp_b200_moe_error_word(const WispMoeConfig* cfg, void* d_workspace);
+
+/* Library version string. */
+const char* wisp_b200_version(void);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WISP_B200_H */

@@ -1,0 +1,328 @@
+"""GPU parity: every CUDA entry point against the oracle (and the reference's
+golden outputs), called through the C ABI. Tolerances: see helpers.py."""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+from wisp_b200 import abi
+from wisp_b200.blob import Int4Matrix, pack_blob, parse_blob
+from wisp_b200.moe import MoeLayer, expert_ffn_decode, parse_header
+from wisp_b200 import synth
+
+from helpers import (assert_close, bf16_to_f64, check_routing, oracle_outputs, oracle_route,
+                     rel_errors)
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _dev_u16(a: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).to(DEV)
+
+
+def _rand_mat(rng, rows, cols, gs, zeros=True):
+    n = rows * cols
+    return Int4Matrix(rng.integers(0, 256, n // 2, dtype=np.uint8),
+                      np.float16(rng.uniform(0.004, 0.02, n // gs)).view(np.uint16),
+                      np.float16(rng.uniform(-0.01, 0.01, n // gs)).view(np.uint16) if zeros else None,
+                      rows, cols)
+
+
+def _blob_on_device(blob: bytes, packed_align16: bool) -> tuple[torch.Tensor, int]:
+    """Copy a blob to device memory. packed_align16: place it at 8 mod 16 so
+    the packed data (at +120) is 16-byte aligned; else at a 16-byte boundary
+    (packed 8 bytes off) as the reference's own buffers are."""
+    buf = torch.empty(len(blob) + 64, dtype=torch.uint8, device=DEV)
+    base = buf.data_ptr()
+    off = 0
+    while (base + off) % 16 != (8 if packed_align16 else 0):
+        off += 1
+    buf[off:off + len(blob)] = torch.frombuffer(bytearray(blob), dtype=torch.uint8).to(DEV)
+    return buf, base + off
+
+
+# ---------------------------------------------------------------------------
+# Reference launcher ABI
+# ---------------------------------------------------------------------------
+
+def test_launch_dequant_expert_bitexact(orc):
+    rng = np.random.default_rng(0)
+    L = abi.lib()
+    for rows, cols, gs in [(64, 128, 64), (33, 64, 16), (7, 9, 3)]:
+        n = rows * cols
+        m = _rand_mat(rng, rows, cols, gs)
+        nb = (n + 1) // 2
+        ng = (n + gs - 1) // gs
+        m.packed = m.packed[:nb] if m.packed.size >= nb else np.pad(m.packed, (0, nb - m.packed.size))
+        m.scales = np.float16(rng.uniform(0.004, 0.02, ng)).view(np.uint16)
+        m.zeros = np.float16(rng.uniform(-0.01, 0.01, ng)).view(np.uint16)
+        p = torch.from_numpy(m.packed).to(DEV)
+        s = _dev_u16(m.scales)
+        z = _dev_u16(m.zeros)
+        out = torch.empty(n, dtype=torch.float16, device=DEV)
+        rc = L.launch_dequant_expert(p.data_ptr(), s.data_ptr(), z.data_ptr(), out.data_ptr(), n, gs, _stream())
+        assert rc == 0
+        ref = orc.dequant(m, n, gs).astype(np.float16)
+        np.testing.assert_array_equal(out.cpu().numpy(), ref)
+    assert L.launch_dequant_expert(None, None, None, None, 0, 64, None) != 0   # invalid value
+    assert L.launch_dequant_expert(None, None, None, None, 10, 0, None) != 0
+
+
+def test_gemv_swiglu_scale_accum_launchers():
+    L = abi.lib()
+    torch.manual_seed(0)
+    for rows, cols in [(256, 512), (37, 100), (1, 8)]:
+        W = (torch.randn(rows, cols, device=DEV) * 0.05).half()
+        x = torch.randn(cols, device=DEV)
+        y = torch.empty(rows, device=DEV)
+        L.wisp_gpu_gemv_f16(W.data_ptr(), x.data_ptr(), y.data_ptr(), rows, cols, _stream())
+        ref = W.double() @ x.double()
+        assert_close(y.cpu().numpy(), ref.cpu().numpy(), 1e-5, 1e-5, "gemv_f16")
+        Wu = (torch.randn(rows, cols, device=DEV) * 0.05).half()
+        h = torch.empty(rows, device=DEV)
+        L.wisp_gpu_swiglu_ffn(W.data_ptr(), Wu.data_ptr(), x.data_ptr(), h.data_ptr(), rows, cols, _stream())
+        g = W.double() @ x.double()
+        u = Wu.double() @ x.double()
+        assert_close(h.cpu().numpy(), (g / (1 + torch.exp(-g)) * u).cpu().numpy(), 1e-5, 1e-5, "swiglu_ffn")
+    g = torch.randn(1000, device=DEV)
+    u = torch.randn(1000, device=DEV)
+    o = torch.empty(1000, device=DEV)
+    L.wisp_gpu_swiglu(g.data_ptr(), u.data_ptr(), o.data_ptr(), 1000, _stream())
+    assert_close(o.cpu().numpy(), (g.double() / (1 + torch.exp(-g.double())) * u.double()).cpu().numpy(), 1e-6, 1e-6)
+    acc = torch.randn(1000, device=DEV)
+    a0 = acc.clone()
+    L.wisp_gpu_scale_accum(acc.data_ptr(), g.data_ptr(), 0.25, 1000, _stream())
+    assert torch.allclose(acc, a0 + 0.25 * g)
+    L.wisp_gpu_scale_accum(acc.data_ptr(), g.data_ptr(), 0.25, 0, _stream())   # silently ignored
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("E,M,k", [(8, 4096, 2), (256, 7168, 8), (384, 7168, 8), (5, 64, 5)])
+def test_router_topk_launcher(orc, E, M, k):
+    L = abi.lib()
+    g = torch.Generator().manual_seed(E * 7 + M)
+    W = (torch.randn(E, M, generator=g) * 0.02).half()
+    bias = (torch.randn(E, generator=g) * 0.1).half()
+    x = torch.randn(M, generator=g)
+    Wd, bd, xd = W.to(DEV), bias.to(DEV), x.to(DEV)
+    logits = torch.empty(E, device=DEV)
+    idx = torch.empty(k, dtype=torch.int32).pin_memory()
+    w = torch.empty(k, dtype=torch.float32).pin_memory()
+    L.wisp_gpu_router_topk(Wd.data_ptr(), bd.data_ptr(), xd.data_ptr(), logits.data_ptr(), E, M, k,
+                           idx.data_ptr(), w.data_ptr(), _stream())
+    torch.cuda.synchronize()
+    lg = orc.router_logits(W.view(torch.int16).numpy().view(np.uint16), 1,
+                           bias.float().numpy().astype(np.float64), x.numpy()[None, :].astype(np.float64))
+    i_ref, w_ref, mg = orc.topk(lg, k)
+    check_routing(idx.numpy()[None, :], w.numpy()[None, :], i_ref, w_ref, mg)
+
+
+# ---------------------------------------------------------------------------
+# Fused decode entry (fp32 activations, reference blobs)
+# ---------------------------------------------------------------------------
+
+def _golden(golden_dir):
+    return np.load(golden_dir / "moe_small.npz")
+
+
+@pytest.mark.parametrize("packed_align16", [True, False])
+def test_expert_ffn_decode_matches_reference_golden(golden_dir, packed_align16):
+    g = _golden(golden_dir)
+    M, I, E, k, gs, T = (int(v) for v in g["dims"])
+    blobs = [b.tobytes() for b in g["blobs"]]
+    meta = parse_header(blobs[0])
+    dev = [_blob_on_device(b, packed_align16) for b in blobs]
+    scratch = torch.empty(abi.lib().wisp_b200_expert_ffn_scratch_bytes(C.byref(meta), k + 1) // 4,
+                          dtype=torch.float32, device=DEV)
+    for t in range(T):
+        x = torch.from_numpy(g["x"][t]).float().to(DEV)
+        acc = torch.zeros(M, device=DEV)
+        ptrs = [dev[int(e)][1] for e in g["idx"][t]] + [dev[E][1]]
+        wts = [float(v) for v in g["w"][t]] + [1.0]
+        expert_ffn_decode(meta, ptrs, wts, x, acc, scratch)
+        torch.cuda.synchronize()
+        mr, me = rel_errors(acc.cpu().numpy(), g["out"][t])
+        assert mr < 1e-4 and me < 1e-4, (t, mr, me)
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("name", ["mixtral_b1", "ds_b1"])
+def test_expert_ffn_decode_full_size(orc, name):
+    spec = synth.CONFIGS[name]
+    rng = np.random.default_rng(11)
+    M, I, gs = spec.hidden, spec.inter, spec.group_size
+    n = spec.top_k + (1 if spec.has_shared else 0)
+    experts = [[_rand_mat(rng, I, M, gs, zeros=False), _rand_mat(rng, I, M, gs, zeros=False),
+                _rand_mat(rng, M, I, gs, zeros=False)] for _ in range(n)]
+    blobs = [pack_blob(*e, group_size=gs) for e in experts]
+    meta = parse_header(blobs[0])
+    dev = [_blob_on_device(b, True) for b in blobs]
+    x = torch.randn(M, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16).float()
+    w = list(rng.uniform(0.05, 0.5, n))
+    scratch = torch.empty(n * I, dtype=torch.float32, device=DEV)
+    acc = torch.zeros(M, device=DEV)
+    expert_ffn_decode(meta, [d[1] for d in dev], w, x.to(DEV), acc, scratch)
+    torch.cuda.synchronize()
+    ref = np.zeros(M)
+    for e, wt in zip(experts, w):
+        orc.expert_ffn(e, gs, x.numpy().astype(np.float64), wt, ref)
+    assert_close(acc.cpu().numpy(), ref, 1e-4, 1e-4, name)
+
+
+# ---------------------------------------------------------------------------
+# Batched MoE layer (router + dispatch + tcgen05 grouped FFN + combine)
+# ---------------------------------------------------------------------------
+
+def _layer_from_golden(g):
+    """LayerWeights from the golden reference blobs (fp16 router)."""
+    M, I, E, k, gs, T = (int(v) for v in g["dims"])
+    spec = synth.MoeSpec("golden", M, I, E, k, group_size=gs, has_shared=True, tokens=T)
+    arenas = []
+    for mi, (rows, cols) in enumerate([(I, M), (I, M), (M, I)]):
+        packed = torch.empty((E + 1, rows, cols // 2), dtype=torch.uint8)
+        scales = torch.empty((E + 1, rows, cols // gs), dtype=torch.float16)
+        zeros = torch.empty_like(scales)
+        for v in range(E + 1):
+            b = g["blobs"][v]
+            pm = parse_blob(b.tobytes())
+            nn = rows * cols
+            packed[v] = torch.from_numpy(b[pm.packed_off[mi]:pm.packed_off[mi] + nn // 2].copy()).view(rows, cols // 2)
+            scales[v] = torch.from_numpy(b[pm.scales_off[mi]:pm.scales_off[mi] + 2 * nn // gs].copy()
+                                         .view(np.int16)).view(torch.float16).view(rows, cols // gs)
+            zeros[v] = torch.from_numpy(b[pm.zeros_off[mi]:pm.zeros_off[mi] + 2 * nn // gs].copy()
+                                        .view(np.int16)).view(torch.float16).view(rows, cols // gs)
+        arenas.append(synth.Int4Arena(packed.to(DEV), scales.to(DEV), zeros.to(DEV)))
+    rw = torch.from_numpy(g["router_w16"].copy()).view(torch.float16).to(DEV)
+    lw = synth.LayerWeights(spec, rw, None, *arenas)
+    lw.build_table()
+    return lw
+
+
+def test_moe_forward_matches_reference_golden(golden_dir):
+    g = _golden(golden_dir)
+    M, I, E, k, gs, T = (int(v) for v in g["dims"])
+    lw = _layer_from_golden(g)
+    layer = MoeLayer(lw, T)
+    layer.cfg.router_fp16 = 1
+    x = torch.from_numpy(g["x"]).to(torch.bfloat16).to(DEV)
+    out = layer.forward(x)
+    torch.cuda.synchronize()
+    layer.check()
+    np.testing.assert_array_equal(layer.idx.cpu().numpy(), g["idx"])
+    np.testing.assert_allclose(layer.wt.cpu().numpy(), g["w"], rtol=1e-5)
+    assert_close(out.cpu().numpy(), g["out"], what="golden moe")
+
+
+SMALL = [
+    dict(hidden=512, inter=256, n_experts=16, top_k=4, group_size=128),
+    dict(hidden=256, inter=384, n_experts=8, top_k=2, group_size=64, has_shared=True),
+    dict(hidden=768, inter=256, n_experts=64, top_k=8, group_size=128, has_shared=True,
+         scoring=abi.WISP_SCORE_SIGMOID_GROUPED, n_groups=8, topk_groups=4, routed_scaling=2.5),
+    dict(hidden=256, inter=256, n_experts=32, top_k=6, group_size=64, skew=True),
+]
+
+
+@pytest.mark.parametrize("zeros", [False, True])
+@pytest.mark.parametrize("T", [1, 5, 37, 300])
+@pytest.mark.parametrize("si", range(len(SMALL)))
+def test_moe_forward_small(orc, si, T, zeros):
+    spec = synth.MoeSpec(f"small{si}", tokens=T, seed=100 + si, **SMALL[si])
+    layers, x = synth.make_model(spec, DEV, zeros=zeros)
+    lw = layers[0]
+    layer = MoeLayer(lw, T)
+    out = layer.forward(x)
+    torch.cuda.synchronize()
+    layer.check()
+    idx = layer.idx.cpu().numpy()
+    w = layer.wt.cpu().numpy()
+    i_ref, w_ref, mg = oracle_route(orc, lw, x)
+    check_routing(idx, w, i_ref, w_ref, mg)
+    tokens = list(range(T)) if T <= 40 else list(range(0, T, 13))
+    ref = oracle_outputs(orc, lw, x, idx, w.astype(np.float64), tokens)
+    assert_close(out.cpu().numpy()[tokens], ref, what=spec.name)
+
+
+def _segments_device(segs):
+    arr = (abi.WispSegment * len(segs))()
+    for i, (e, b, r) in enumerate(segs):
+        arr[i].expert, arr[i].row_begin, arr[i].rows = e, b, r
+    return torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).to(DEV)
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_grouped_ffn_tile_boundaries(orc, mode):
+    """Segments of 0, 1, 15, 16, 17, 32, 33, 64, 65, 128, 129 and 300 rows
+    (every BN choice and its ragged edge) through the grouped kernels."""
+    counts = [0, 1, 15, 16, 17, 32, 33, 64, 65, 128, 129, 300]
+    spec = synth.MoeSpec("tiles", 256, 256, len(counts), 1, group_size=128, tokens=1, seed=7)
+    lw = synth.make_model(spec, DEV)[0][0]
+    R = sum(counts)
+    T = R
+    g = torch.Generator(device=DEV).manual_seed(3)
+    x = torch.randn((T, spec.hidden), generator=g, device=DEV).to(torch.bfloat16)
+    segs, b = [], 0
+    for e, c in enumerate(counts):
+        segs.append((e, b, c))
+        b += c
+    row_token = torch.arange(R, dtype=torch.int32, device=DEV)   # row p holds token p
+    row_w = torch.rand(R, generator=g, device=DEV) + 0.5
+    xp = torch.empty((R, spec.hidden), dtype=torch.float16, device=DEV)
+    h = torch.empty((R, spec.inter), dtype=torch.float16, device=DEV)
+    out = torch.zeros((R, spec.hidden), dtype=torch.float32, device=DEV)
+    tiles = torch.empty(abi.lib().wisp_b200_tiles_words(len(segs)), dtype=torch.int32, device=DEV)
+    flag = torch.zeros(1, dtype=torch.int32, device=DEV)
+    dsegs = _segments_device(segs)
+    cfg = spec.cfg(T)
+    abi.call("wisp_b200_pack_rows", x.data_ptr(), None, R, spec.hidden, xp.data_ptr(), _stream())
+    abi.call("wisp_b200_grouped_ffn", C.byref(cfg), lw.table.data_ptr(), dsegs.data_ptr(), len(segs), R,
+             xp.data_ptr(), h.data_ptr(), mode, row_token.data_ptr(), row_w.data_ptr(), out.data_ptr(),
+             tiles.data_ptr(), flag.data_ptr(), _stream())
+    abi.call("wisp_b200_check_error_flag", flag.data_ptr(), _stream())
+    got = out.cpu().numpy()
+    xs = bf16_to_f64(x)
+    wv = row_w.cpu().numpy()
+    for e, b0, c in segs:
+        if c == 0:
+            continue
+        mats = lw.expert_host(e)
+        for p in sorted({b0, b0 + c - 1, b0 + c // 2}):
+            ref = orc.expert_ffn(mats, spec.group_size, xs[p], wv[p] if mode == 0 else 1.0)
+            assert_close(got[p], ref, what=f"seg {e} rows {c} row {p}")
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("name", ["mixtral_b1", "mixtral_b64", "ds_b1", "ds_b128", "ds_prefill"])
+def test_moe_forward_full_size(orc, name):
+    spec = synth.CONFIGS[name]
+    layers, x = synth.make_model(spec, DEV)
+    lw = layers[0]
+    layer = MoeLayer(lw, spec.tokens)
+    out = layer.forward(x)
+    torch.cuda.synchronize()
+    layer.check()
+    idx = layer.idx.cpu().numpy()
+    w = layer.wt.cpu().numpy()
+    T = spec.tokens
+    # routing of every token (oracle router in fp64)
+    i_ref, w_ref, mg = oracle_route(orc, lw, x)
+    near = check_routing(idx, w, i_ref, w_ref, mg)
+    assert len(near) <= max(2, T // 200)
+    # expert outputs of sampled tokens under the GPU's routing
+    tokens = sorted({0, T - 1, T // 2, T // 3})
+    ref = oracle_outputs(orc, lw, x, idx, w.astype(np.float64), tokens)
+    assert_close(out.cpu().numpy()[tokens], ref, what=name)
+    # size-independent property: permuting the tokens permutes the outputs
+    if T > 1:
+        perm = torch.randperm(T, generator=torch.Generator().manual_seed(0)).to(DEV)
+        out2 = layer.forward(x[perm].contiguous())
+        torch.cuda.synchronize()
+        assert_close(out2.cpu().numpy(), out[perm].cpu().numpy(), 1e-5, 1e-6, "permutation")

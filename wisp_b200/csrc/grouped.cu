@@ -1,0 +1,582 @@
+// grouped.cu -- grouped int4 expert FFN on the 5th-generation tensor cores.
+//
+// Replaces, for batched and prefill tokens, the reference's per-token loop
+// of dequant -> fp16 GEMV -> scale_accum (csrc/core/wisp_engine.c:1507-1531
+// called from run_moe :1563-1674 and, for prefill, decode_step per token
+// :2292-2307). Rows of activations are pre-grouped by expert ("segments");
+// each CTA tile computes 128 weight rows x BN token rows:
+//
+//   GATEUP: H[p, i] = silu(gate[i] . x_p) * (up[i] . x_p)   (fp16 H out)
+//   DOWN:   out[token(p), m] += w_p * (down[m] . H_p)        (fp32 atomics)
+//           or y[p, m] = down[m] . H_p                        (mode 1)
+//
+// The weights are the MMA's A operand (M = 128 lanes), the tokens its B
+// operand (N = BN in {16, 32, 64, 128}, chosen per segment so small groups
+// do not pay for padding). Roles inside one persistent CTA per SM:
+//   warps 0-7   dequantise: each thread owns one weight row of the tile,
+//               fetches its packed nibbles with cp.async into a private
+//               ring (6 stages ahead, across tile boundaries), converts them
+//               to fp16 ((n-8)*s + z, one rounding) and writes them straight
+//               into tensor memory with tcgen05.st -- the dequantised tile
+//               never touches shared memory, so the MMA's shared-memory
+//               bandwidth goes to the activation operand alone.
+//   warp 12     TMA producer for the activation tiles (128-byte swizzle).
+//   warp 13     MMA issuer: tcgen05.mma kind::f16, A from TMEM, B from smem,
+//               fp32 accumulators in TMEM; completion via tcgen05.commit.
+//   warps 8-11  epilogue: tcgen05.ld of the accumulators, SwiGLU (GATEUP) or
+//               the weighted scatter-combine (DOWN).
+// TMEM columns: [0,128) gate / single accumulator, [128,256) up accumulator,
+// [256,512) four 64-column A stages. Every wait is bounded; a wait that gives
+// up raises a CTA-wide abort and the device error word.
+//
+// The K order inside every group of 8 activations is 0,4,1,5,2,6,3,7: that
+// is the order the nibble conversion produces the weights in, so the
+// activation operands (Xp, H) are stored in the same interleaved order.
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+#include "internal.h"
+
+using namespace wb;
+
+namespace {
+
+constexpr int kThreads = 448;
+constexpr int kDqThreads = 256;
+constexpr int kEpiWarp0 = 8;
+constexpr int kTmaWarp = 12;
+constexpr int kMmaWarp = 13;
+constexpr int kAStages = 4;
+constexpr int kRaw = 6;  // cp.async ring depth per dequant thread
+constexpr int BM = 128;
+constexpr int kBNMax = 128;
+constexpr int kTmemCols = 512;
+constexpr int kAColBase = 256;
+
+enum { GATEUP = 0, DOWN = 1 };
+
+template <int MODE>
+struct Shape {
+  static constexpr int KS = MODE == GATEUP ? 64 : 128;           // K per stage
+  static constexpr int kBoxes = KS / 64;                          // 64-K boxes per stage
+  static constexpr int kBStageBytes = kBoxes * kBNMax * 128;      // 16 / 32 KB
+  static constexpr int kBStages = MODE == GATEUP ? 8 : 4;
+};
+
+struct GemmParams {
+  CUtensorMap tmap[4];  // activation tensor, boxes {64, 16 << i}
+  const WispInt4Expert* experts;
+  const WispSegment* segs;
+  const int32_t* tiles;  // [0, S]: tile prefix; [S+1, 2S+1): bn per segment
+  int nseg;
+  int M, I, gs;
+  int mblocks;  // weight-row tiles per expert
+  __half* h_out;
+  const int* row_token;
+  const float* row_weight;
+  float* out;
+  int mode;
+  int* error_flag;
+};
+
+struct SmemLayout {
+  uint64_t bfull[8], bempty[8];
+  uint64_t afull[kAStages], aempty[kAStages];
+  uint64_t accfull, accempty, final_bar;
+  uint32_t tmem_base;
+  int abort;
+};
+
+struct TileInfo {
+  int seg, expert, row0, nvalid, bn, mblk;
+};
+
+__device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int tile) {
+  // Largest segment s with tiles[s] <= tile (segments with no tiles are
+  // skipped because their prefix equals the next one).
+  int lo = 0, hi = p.nseg - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(p.tiles + mid) <= tile) lo = mid; else hi = mid - 1;
+  }
+  const int s = lo;
+  const WispSegment sg = p.segs[s];
+  const int bn = __ldg(p.tiles + p.nseg + 1 + s);
+  const int nblk = (sg.rows + bn - 1) / bn;
+  const int local = tile - __ldg(p.tiles + s);
+  TileInfo t;
+  t.seg = s;
+  t.expert = sg.expert;
+  t.mblk = local / nblk;
+  const int nb = local % nblk;
+  t.bn = bn;
+  t.row0 = sg.row_begin + nb * bn;
+  t.nvalid = min(bn, sg.rows - nb * bn);
+  return t;
+}
+
+__device__ __forceinline__ int bn_slot(int bn) { return bn == 16 ? 0 : bn == 32 ? 1 : bn == 64 ? 2 : 3; }
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_constant__ GemmParams p) {
+  using S = Shape<MODE>;
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment for the swizzled activation tiles.
+  const uint32_t base_u32 = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (base_u32 & 1023)) & 1023);
+  uint8_t* b_ring = smem;                                            // kBStages * kBStageBytes
+  uint8_t* raw_ring = b_ring + S::kBStages * S::kBStageBytes;        // kRaw * 2 * 256 * 16
+  uint32_t* scale_ring = reinterpret_cast<uint32_t*>(raw_ring + kRaw * 2 * kDqThreads * 16);
+  uint32_t* zero_ring = scale_ring + kRaw * kDqThreads;
+  SmemLayout* L = reinterpret_cast<SmemLayout*>(zero_ring + kRaw * kDqThreads);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ntiles = __ldg(p.tiles + p.nseg);
+  const int nks = (MODE == GATEUP ? p.M : p.I) / S::KS;
+  volatile int* abort = &L->abort;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S::kBStages; i++) {
+      mbar_init(&L->bfull[i], 1);
+      mbar_init(&L->bempty[i], 1);
+    }
+    for (int i = 0; i < kAStages; i++) {
+      mbar_init(&L->afull[i], kDqThreads / 32);
+      mbar_init(&L->aempty[i], 1);
+    }
+    mbar_init(&L->accfull, 1);
+    mbar_init(&L->accempty, 4);
+    mbar_init(&L->final_bar, 1);
+    L->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(&L->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = L->tmem_base;
+
+  if (warp < 8) {
+    // ------------------------------------------------------------------
+    // Dequantisation warps.
+    // ------------------------------------------------------------------
+    const int t = threadIdx.x;          // 0..255
+    const int wg = t >> 7;              // which half of the A stage
+    const int r = t & 127;              // weight row within the tile == TMEM lane
+    const int K = MODE == GATEUP ? p.M : p.I;
+    const int gpr = K / p.gs;           // scale groups per weight row
+    // Producer cursor (cp.async issue) runs kRaw-1 items ahead.
+    int ptile = blockIdx.x, pks = 0;
+    TileInfo pti;
+    if (ptile < ntiles) pti = decode_tile(p, ptile);
+    auto issue = [&](int slot) {
+      if (ptile < ntiles) {
+        const WispInt4Expert& ex = p.experts[pti.expert];
+        const WispInt4Mat& mt = MODE == GATEUP ? (wg == 0 ? ex.gate : ex.up) : ex.down;
+        const int row = pti.mblk * BM + r;
+        const int k0 = pks * S::KS + (MODE == GATEUP ? 0 : wg * 64);
+        const uint8_t* src = mt.packed + (size_t)row * (K / 2) + (k0 >> 1);
+        uint8_t* dst0 = raw_ring + ((slot * 2 + 0) * kDqThreads + t) * 16;
+        uint8_t* dst1 = raw_ring + ((slot * 2 + 1) * kDqThreads + t) * 16;
+        cp_async_16(dst0, src);
+        cp_async_16(dst1, src + 16);
+        const size_t gidx = (size_t)row * gpr + k0 / p.gs;
+        cp_async_4(scale_ring + slot * kDqThreads + t,
+                   reinterpret_cast<const uint8_t*>(mt.scales) + ((gidx & ~(size_t)1) * 2));
+        if (mt.zeros)
+          cp_async_4(zero_ring + slot * kDqThreads + t,
+                     reinterpret_cast<const uint8_t*>(mt.zeros) + ((gidx & ~(size_t)1) * 2));
+        if (++pks == nks) {
+          pks = 0;
+          ptile += gridDim.x;
+          if (ptile < ntiles) pti = decode_tile(p, ptile);
+        }
+      }
+      cp_async_commit();
+    };
+    for (int i = 0; i < kRaw - 1; i++) issue(i);
+    int slot = 0, sa = 0;
+    uint32_t aphase = 0;
+    int item = 0;
+    for (int tile = blockIdx.x; tile < ntiles && !*abort; tile += gridDim.x) {
+      const TileInfo ti = decode_tile(p, tile);
+      const WispInt4Expert& ex = p.experts[ti.expert];
+      const WispInt4Mat& mt = MODE == GATEUP ? (wg == 0 ? ex.gate : ex.up) : ex.down;
+      const bool has_zero = mt.zeros != nullptr;
+      const int row = ti.mblk * BM + r;
+      for (int ks = 0; ks < nks; ks++, item++) {
+        issue((slot + kRaw - 1) % kRaw);
+        cp_async_wait<kRaw - 1>();
+        const uint4 q0 = *reinterpret_cast<const uint4*>(raw_ring + ((slot * 2 + 0) * kDqThreads + t) * 16);
+        const uint4 q1 = *reinterpret_cast<const uint4*>(raw_ring + ((slot * 2 + 1) * kDqThreads + t) * 16);
+        const int k0 = ks * S::KS + (MODE == GATEUP ? 0 : wg * 64);
+        const size_t gidx = (size_t)row * gpr + k0 / p.gs;
+        const uint32_t sw = scale_ring[slot * kDqThreads + t];
+        const __half s = __ushort_as_half((unsigned short)((gidx & 1) ? (sw >> 16) : (sw & 0xffff)));
+        __half z = __float2half(0.f);
+        if (has_zero) {
+          const uint32_t zw = zero_ring[slot * kDqThreads + t];
+          z = __ushort_as_half((unsigned short)((gidx & 1) ? (zw >> 16) : (zw & 0xffff)));
+        }
+        slot = (slot + 1) % kRaw;
+        const __half2 s2 = __halves2half2(s, s), z2 = __halves2half2(z, z);
+        uint32_t v[32];
+        const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+        for (int w = 0; w < 8; w++) {
+          uint32_t o[4];
+          nib8_dequant(words[w], s2, z2, o);
+          v[4 * w + 0] = o[0];
+          v[4 * w + 1] = o[1];
+          v[4 * w + 2] = o[2];
+          v[4 * w + 3] = o[3];
+        }
+        if (item >= kAStages) {
+          if (!mbar_wait(&L->aempty[sa], aphase ^ 1, abort)) break;
+        }
+        tc_fence_after();
+        const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16) +
+                               (uint32_t)(kAColBase + sa * 64 + wg * 32);
+        tmem_st32(taddr, v);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&L->afull[sa]);
+        if (++sa == kAStages) {
+          sa = 0;
+          aphase ^= 1;
+        }
+      }
+    }
+    cp_async_wait_all();
+  } else if (warp == kTmaWarp) {
+    // ------------------------------------------------------------------
+    // TMA producer for the activation tiles.
+    // ------------------------------------------------------------------
+    if (lane == 0) {
+      for (int i = 0; i < 4; i++) tma_prefetch_desc(&p.tmap[i]);
+      int sb = 0;
+      uint32_t bphase = 0;
+      int item = 0;
+      int last_phase[8];
+      for (int i = 0; i < 8; i++) last_phase[i] = -1;
+      for (int tile = blockIdx.x; tile < ntiles && !*abort; tile += gridDim.x) {
+        const TileInfo ti = decode_tile(p, tile);
+        const CUtensorMap* tm = &p.tmap[bn_slot(ti.bn)];
+        const uint32_t bytes = (uint32_t)(ti.bn * 128 * S::kBoxes);
+        bool ok = true;
+        for (int ks = 0; ks < nks; ks++, item++) {
+          if (item >= S::kBStages) {
+            if (!mbar_wait(&L->bempty[sb], bphase ^ 1, abort)) { ok = false; break; }
+          }
+          mbar_arrive_expect_tx(&L->bfull[sb], bytes);
+          uint8_t* dst = b_ring + sb * S::kBStageBytes;
+#pragma unroll
+          for (int bx = 0; bx < S::kBoxes; bx++)
+            tma_load_2d(dst + bx * (kBNMax * 128), tm, &L->bfull[sb], ks * S::KS + bx * 64, ti.row0);
+          last_phase[sb] = (int)bphase;
+          if (++sb == S::kBStages) {
+            sb = 0;
+            bphase ^= 1;
+          }
+        }
+        if (!ok) break;
+      }
+      // Every issued load completes on its own; wait for the last one of
+      // each stage so no copy is still landing when the CTA exits.
+      for (int i = 0; i < S::kBStages; i++)
+        if (last_phase[i] >= 0) mbar_wait(&L->bfull[i], (uint32_t)last_phase[i], abort, 200000000LL);
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------------
+    // MMA issuer (one thread).
+    // ------------------------------------------------------------------
+    if (lane == 0) {
+      int sa = 0, sb = 0;
+      uint32_t aphase = 0, bphase = 0, accphase = 0;
+      int ntile_local = 0;
+      for (int tile = blockIdx.x; tile < ntiles && !*abort; tile += gridDim.x, ntile_local++) {
+        const TileInfo ti = decode_tile(p, tile);
+        const uint32_t idesc = idesc_f16_m128(ti.bn);
+        if (ntile_local > 0) {
+          if (!mbar_wait(&L->accempty, accphase ^ 1, abort)) break;
+        }
+        tc_fence_after();
+        bool ok = true;
+        for (int ks = 0; ks < nks; ks++) {
+          if (!mbar_wait(&L->afull[sa], aphase, abort) || !mbar_wait(&L->bfull[sb], bphase, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_col = tmem + kAColBase + sa * 64;
+          const uint32_t b_addr = smem_u32(b_ring + sb * S::kBStageBytes);
+          if (MODE == GATEUP) {
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) {
+              const uint64_t bd = smem_desc_sw128(b_addr + kk * 32);
+              const uint32_t acc = (ks | kk) ? 1u : 0u;
+              mma_f16_ts(tmem + 0, a_col + kk * 8, bd, idesc, acc);
+              mma_f16_ts(tmem + 128, a_col + 32 + kk * 8, bd, idesc, acc);
+            }
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < 8; kk++) {
+              const uint64_t bd = smem_desc_sw128(b_addr + (kk >> 2) * (kBNMax * 128) + (kk & 3) * 32);
+              mma_f16_ts(tmem + 0, a_col + kk * 8, bd, idesc, (ks | kk) ? 1u : 0u);
+            }
+          }
+          mma_commit(&L->aempty[sa]);
+          mma_commit(&L->bempty[sb]);
+          if (++sa == kAStages) { sa = 0; aphase ^= 1; }
+          if (++sb == S::kBStages) { sb = 0; bphase ^= 1; }
+        }
+        if (!ok) break;
+        mma_commit(&L->accfull);
+        accphase ^= 1;
+      }
+      // Drain: make sure no MMA is still running before TMEM is released.
+      mma_commit(&L->final_bar);
+      mbar_wait(&L->final_bar, 0, abort, 200000000LL);
+    }
+  } else {
+    // ------------------------------------------------------------------
+    // Epilogue warps 8-11.
+    // ------------------------------------------------------------------
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    uint32_t accphase = 0;
+    for (int tile = blockIdx.x; tile < ntiles && !*abort; tile += gridDim.x) {
+      const TileInfo ti = decode_tile(p, tile);
+      if (!mbar_wait(&L->accfull, accphase, abort)) break;
+      accphase ^= 1;
+      tc_fence_after();
+      const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+      if (MODE == GATEUP) {
+        const int i = ti.mblk * BM + r;
+        const int islot = k_interleave_slot(i);
+        for (int c0 = 0; c0 < ti.bn; c0 += 16) {
+          uint32_t g[16], u[16];
+          tmem_ld16(lane_addr + c0, g);
+          tmem_ld16(lane_addr + 128 + c0, u);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; j++) {
+            const int tt = c0 + j;
+            if (tt < ti.nvalid) {
+              const float hv = silu(__uint_as_float(g[j])) * __uint_as_float(u[j]);
+              p.h_out[(size_t)(ti.row0 + tt) * p.I + islot] = __float2half(hv);
+            }
+          }
+        }
+      } else {
+        const int m = ti.mblk * BM + r;
+        for (int c0 = 0; c0 < ti.bn; c0 += 16) {
+          uint32_t y[16];
+          tmem_ld16(lane_addr + c0, y);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; j++) {
+            const int tt = c0 + j;
+            if (tt < ti.nvalid) {
+              const int prow = ti.row0 + tt;
+              const float yv = __uint_as_float(y[j]);
+              if (p.mode == 0) {
+                const int tok = __ldg(p.row_token + prow);
+                const float wgt = __ldg(p.row_weight + prow);
+                red_add_f32(p.out + (size_t)tok * p.M + m, wgt * yv);
+              } else {
+                p.out[(size_t)prow * p.M + m] = yv;
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&L->accempty);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && L->abort && p.error_flag) atomicExch(p.error_flag, 1);
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// Per segment: BN (16/32/64/128 by row count) and the prefix sum of tiles.
+__global__ void plan_tiles_kernel(const WispSegment* __restrict__ segs, int nseg, int mblocks,
+                                  int32_t* __restrict__ tiles) {
+  __shared__ int32_t warp_tot[32];
+  __shared__ int32_t carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (int base = 0; base < nseg; base += blockDim.x) {
+    const int s = base + threadIdx.x;
+    int n = 0, bn = 16;
+    if (s < nseg) {
+      const int rows = segs[s].rows;
+      bn = rows <= 16 ? 16 : rows <= 32 ? 32 : rows <= 64 ? 64 : 128;
+      n = rows > 0 ? ((rows + bn - 1) / bn) * mblocks : 0;
+      tiles[nseg + 1 + s] = bn;
+    }
+    // block inclusive scan of n
+    int v = n;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += y;
+    }
+    if (lane == 31) warp_tot[w] = v;
+    __syncthreads();
+    if (w == 0) {
+      int tv = lane < (int)(blockDim.x >> 5) ? warp_tot[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, tv, o);
+        if (lane >= o) tv += y;
+      }
+      warp_tot[lane] = tv;
+    }
+    __syncthreads();
+    const int incl = v + (w > 0 ? warp_tot[w - 1] : 0) + carry;
+    if (s < nseg) tiles[s] = incl - n;
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = incl;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) tiles[nseg] = carry;
+}
+
+// ---------------------------------------------------------------------------
+// Host side.
+// ---------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+bool encode_rows_map(CUtensorMap* m, const void* base, int rows, int cols, int box_rows) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+template <int MODE>
+size_t smem_bytes() {
+  using S = Shape<MODE>;
+  return 1024 + (size_t)S::kBStages * S::kBStageBytes + (size_t)kRaw * 2 * kDqThreads * 16 +
+         (size_t)kRaw * kDqThreads * 4 * 2 + sizeof(SmemLayout);
+}
+
+int num_sms() {
+  static int sms[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  return sms[dev] > 0 ? sms[dev] : 148;
+}
+
+}  // namespace
+
+// Two tables (gate/up and down), each [prefix S+1 | bn S].
+extern "C" size_t wisp_b200_tiles_words(int n_segs) { return (size_t)(2 * (2 * n_segs + 1)); }
+
+extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const WispInt4Expert* d_experts,
+                                           const WispSegment* d_segs, int n_segs, int rows_capacity,
+                                           const uint16_t* d_xp, uint16_t* d_h, int mode,
+                                           const int* d_row_token, const float* d_row_weight,
+                                           float* d_out, int32_t* d_tiles, int* d_error_flag,
+                                           cudaStream_t stream, WispErrCtx* err) {
+  if (!cfg || !d_experts || !d_segs || !d_xp || !d_h || !d_out || !d_tiles)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "grouped_ffn: null pointer argument");
+  const int M = cfg->hidden, I = cfg->inter, gs = cfg->group_size;
+  if (M <= 0 || I <= 0 || M % 128 || I % 128)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "grouped_ffn: hidden (%d) and inter (%d) must be multiples of 128", M, I);
+  if (gs != 64 && gs != 128)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "grouped_ffn: group_size must be 64 or 128 (got %d)", gs);
+  if (n_segs <= 0 || rows_capacity <= 0)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "grouped_ffn: n_segs=%d rows=%d", n_segs, rows_capacity);
+  if (mode == 0 && (!d_row_token || !d_row_weight))
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "grouped_ffn: mode 0 needs row_token and row_weight");
+  if (((uintptr_t)d_xp | (uintptr_t)d_h) & 15)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "grouped_ffn: activation buffers must be 16-byte aligned");
+
+  GemmParams gu, dn;
+  memset(&gu, 0, sizeof gu);
+  for (int i = 0; i < 4; i++) {
+    if (!encode_rows_map(&gu.tmap[i], d_xp, rows_capacity, M, 16 << i))
+      return WB_FAIL(WISP_ERR_CUDA, "grouped_ffn: cuTensorMapEncodeTiled failed (activations)");
+  }
+  gu.experts = d_experts;
+  gu.segs = d_segs;
+  gu.tiles = d_tiles;
+  gu.nseg = n_segs;
+  gu.M = M;
+  gu.I = I;
+  gu.gs = gs;
+  gu.mblocks = I / BM;
+  gu.h_out = reinterpret_cast<__half*>(d_h);
+  gu.error_flag = d_error_flag;
+  dn = gu;
+  for (int i = 0; i < 4; i++) {
+    if (!encode_rows_map(&dn.tmap[i], d_h, rows_capacity, I, 16 << i))
+      return WB_FAIL(WISP_ERR_CUDA, "grouped_ffn: cuTensorMapEncodeTiled failed (H)");
+  }
+  dn.mblocks = M / BM;
+  dn.row_token = d_row_token;
+  dn.row_weight = d_row_weight;
+  dn.out = d_out;
+  dn.mode = mode;
+
+  // Both launches share the per-segment BN choice; only the tile prefix
+  // differs (mblocks), so each gets its own tile table.
+  const size_t tw = (size_t)(2 * n_segs + 1);
+  int32_t* tiles_gu = d_tiles;
+  int32_t* tiles_dn = d_tiles + tw;
+  gu.tiles = tiles_gu;
+  dn.tiles = tiles_dn;
+  plan_tiles_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, I / BM, tiles_gu);
+  plan_tiles_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, M / BM, tiles_dn);
+
+  const int grid = num_sms();
+  const size_t sm_gu = smem_bytes<GATEUP>(), sm_dn = smem_bytes<DOWN>();
+  WB_CUDA_CHECK(cudaFuncSetAttribute(grouped_ffn_kernel<GATEUP>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_gu));
+  WB_CUDA_CHECK(cudaFuncSetAttribute(grouped_ffn_kernel<DOWN>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_dn));
+  grouped_ffn_kernel<GATEUP><<<grid, kThreads, sm_gu, stream>>>(gu);
+  grouped_ffn_kernel<DOWN><<<grid, kThreads, sm_dn, stream>>>(dn);
+  WB_CUDA_CHECK(cudaGetLastError());
+  return WISP_OK;
+}

@@ -1,0 +1,37 @@
+// internal.h -- host-side helpers shared by the wisp_b200 translation units.
+#pragma once
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "wisp_b200.h"
+
+namespace wb {
+
+// Fill a WispErrCtx the way the reference's WISP_ERR_SET does
+// (csrc/core/wisp_engine.h:66-72) and return the code.
+inline WispError set_err(WispErrCtx* err, WispError code, const char* file, int line,
+                         const char* fmt, ...) {
+  if (err) {
+    err->code = code;
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(err->message, sizeof(err->message), fmt, ap);
+    va_end(ap);
+    err->file = file;
+    err->line = line;
+  }
+  return code;
+}
+
+}  // namespace wb
+
+#define WB_FAIL(code, ...) ::wb::set_err(err, code, __FILE__, __LINE__, __VA_ARGS__)
+
+#define WB_CUDA_CHECK(call)                                                          \
+  do {                                                                               \
+    cudaError_t _e = (call);                                                         \
+    if (_e != cudaSuccess)                                                           \
+      return WB_FAIL(WISP_ERR_CUDA, "CUDA error: %s", cudaGetErrorString(_e));       \
+  } while (0)

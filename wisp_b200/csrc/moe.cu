@@ -1,0 +1,201 @@
+// moe.cu -- host orchestration of the batched MoE layer and the small
+// host-side pieces of the ABI (blob header parsing, error word, version).
+//
+// wisp_b200_moe_forward runs, on one stream and without any host sync:
+//   route (logits + top-k) -> dispatch plan (segments, row -> token map)
+//   -> pack rows (bf16 -> fp16 interleaved) -> zero out
+//   -> grouped gate/up + SwiGLU (tcgen05) -> grouped down + weighted
+//      scatter-combine (tcgen05, fp32 atomics into out).
+// It is the batched counterpart of run_moe (csrc/core/wisp_engine.c:
+// 1563-1674), which the reference can only run one token at a time.
+#include <algorithm>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace wb {
+size_t router_splits(int T, int E, int M);
+WispError launch_route(const WispMoeConfig* c, const uint16_t* x, const uint16_t* W,
+                       const float* bias, float* part, size_t splits, float* logits_out, int* idx,
+                       float* w, cudaStream_t st, WispErrCtx* err);
+WispError launch_plan(const WispMoeConfig* c, const int* idx, const float* w, int* counts,
+                      WispSegment* segs, int* row_token, float* row_weight, cudaStream_t st,
+                      WispErrCtx* err);
+WispError launch_pack(const uint16_t* x, const int* src, int n_rows, int M, uint16_t* xp,
+                      cudaStream_t st, WispErrCtx* err);
+}  // namespace wb
+
+namespace {
+
+struct Carve {
+  size_t off = 0;
+  template <typename T>
+  T* take(void* base, size_t count) {
+    off = (off + 255) & ~(size_t)255;
+    T* p = base ? reinterpret_cast<T*>(static_cast<uint8_t*>(base) + off) : nullptr;
+    off += count * sizeof(T);
+    return p;
+  }
+};
+
+struct Workspace {
+  float* part;
+  int* idx;
+  float* w;
+  int* counts;
+  WispSegment* segs;
+  int* row_token;
+  float* row_weight;
+  int32_t* tiles;
+  int* error_flag;
+  uint16_t* xp;
+  uint16_t* h;
+  size_t bytes;
+  size_t splits;
+  int rows;
+};
+
+Workspace carve(const WispMoeConfig* c, void* base) {
+  Workspace ws;
+  Carve cv;
+  const int T = c->tokens, E = c->n_experts, k = c->top_k, M = c->hidden, I = c->inter;
+  const int V = E + (c->has_shared ? 1 : 0);
+  ws.rows = T * k + (c->has_shared ? T : 0);
+  ws.splits = wb::router_splits(T, E, M);
+  ws.part = cv.take<float>(base, ws.splits * (size_t)T * E);
+  ws.idx = cv.take<int>(base, (size_t)T * k);
+  ws.w = cv.take<float>(base, (size_t)T * k);
+  ws.counts = cv.take<int>(base, V);
+  ws.segs = cv.take<WispSegment>(base, V);
+  ws.row_token = cv.take<int>(base, ws.rows);
+  ws.row_weight = cv.take<float>(base, ws.rows);
+  ws.tiles = cv.take<int32_t>(base, wisp_b200_tiles_words(V));
+  ws.error_flag = cv.take<int>(base, 1);
+  ws.xp = cv.take<uint16_t>(base, (size_t)ws.rows * M);
+  ws.h = cv.take<uint16_t>(base, (size_t)ws.rows * I);
+  ws.bytes = (cv.off + 255) & ~(size_t)255;
+  return ws;
+}
+
+WispError validate(const WispMoeConfig* c, WispErrCtx* err) {
+  if (!c) return WB_FAIL(WISP_ERR_INVALID_ARG, "moe: null config");
+  if (c->tokens <= 0 || c->n_experts <= 0 || c->n_experts > 1024)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "moe: tokens=%d n_experts=%d (1..1024)", c->tokens, c->n_experts);
+  if (c->top_k <= 0 || c->top_k > 32 || c->top_k > c->n_experts)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "moe: top_k=%d (1..min(32, n_experts))", c->top_k);
+  if (c->hidden <= 0 || c->inter <= 0 || c->hidden % 128 || c->inter % 128)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "moe: hidden=%d inter=%d must be multiples of 128", c->hidden, c->inter);
+  if (c->group_size != 64 && c->group_size != 128)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "moe: group_size=%d (64 or 128)", c->group_size);
+  if (c->scoring == WISP_SCORE_SIGMOID_GROUPED) {
+    if (c->n_groups <= 0 || c->n_groups > 32 || c->n_experts % c->n_groups ||
+        c->topk_groups <= 0 || c->topk_groups > c->n_groups ||
+        c->top_k > c->topk_groups * (c->n_experts / c->n_groups))
+      return WB_FAIL(WISP_ERR_INVALID_ARG, "moe: bad group routing (E=%d groups=%d keep=%d k=%d)",
+                     c->n_experts, c->n_groups, c->topk_groups, c->top_k);
+  } else if (c->scoring != WISP_SCORE_SOFTMAX) {
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "moe: unknown scoring %d", c->scoring);
+  }
+  return WISP_OK;
+}
+
+}  // namespace
+
+extern "C" size_t wisp_b200_moe_workspace_bytes(const WispMoeConfig* cfg) {
+  if (validate(cfg, nullptr) != WISP_OK) return 0;
+  return carve(cfg, nullptr).bytes;
+}
+
+extern "C" WispError wisp_b200_route(const WispMoeConfig* cfg, const WispMoeWeights* w,
+                                     const uint16_t* d_x, float* d_logits, int* d_idx, float* d_w,
+                                     cudaStream_t stream, WispErrCtx* err) {
+  WispError e = validate(cfg, err);
+  if (e != WISP_OK) return e;
+  if (!w || !w->router_w || !d_x || !d_logits || !d_idx || !d_w)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "route: null pointer argument");
+  // d_logits serves as the (single-split) partial buffer and then receives
+  // the final logits (bias included); each token's row is read before it
+  // is rewritten by the same thread.
+  return wb::launch_route(cfg, d_x, w->router_w, w->router_bias, d_logits, 1, d_logits, d_idx, d_w,
+                          stream, err);
+}
+
+extern "C" WispError wisp_b200_moe_forward(const WispMoeConfig* cfg, const WispMoeWeights* w,
+                                           const uint16_t* d_x, float* d_out, int* d_topk_idx,
+                                           float* d_topk_w, void* d_workspace,
+                                           size_t workspace_bytes, cudaStream_t stream,
+                                           WispErrCtx* err) {
+  WispError e = validate(cfg, err);
+  if (e != WISP_OK) return e;
+  if (!w || !w->router_w || !w->experts || !d_x || !d_out || !d_workspace)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "moe_forward: null pointer argument");
+  if (((uintptr_t)d_x | (uintptr_t)w->router_w | (uintptr_t)d_workspace) & 15)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "moe_forward: x, router_w and workspace must be 16-byte aligned");
+  Workspace ws = carve(cfg, d_workspace);
+  if (workspace_bytes < ws.bytes)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "moe_forward: workspace %zu < required %zu", workspace_bytes, ws.bytes);
+  int* idx = d_topk_idx ? d_topk_idx : ws.idx;
+  float* wt = d_topk_w ? d_topk_w : ws.w;
+  const int V = cfg->n_experts + (cfg->has_shared ? 1 : 0);
+
+  e = wb::launch_route(cfg, d_x, w->router_w, w->router_bias, ws.part, ws.splits, nullptr, idx, wt,
+                       stream, err);
+  if (e != WISP_OK) return e;
+  e = wb::launch_plan(cfg, idx, wt, ws.counts, ws.segs, ws.row_token, ws.row_weight, stream, err);
+  if (e != WISP_OK) return e;
+  e = wb::launch_pack(d_x, ws.row_token, ws.rows, cfg->hidden, ws.xp, stream, err);
+  if (e != WISP_OK) return e;
+  WB_CUDA_CHECK(cudaMemsetAsync(d_out, 0, (size_t)cfg->tokens * cfg->hidden * sizeof(float), stream));
+  WB_CUDA_CHECK(cudaMemsetAsync(ws.error_flag, 0, sizeof(int), stream));
+  return wisp_b200_grouped_ffn(cfg, w->experts, ws.segs, V, ws.rows, ws.xp, ws.h, 0, ws.row_token,
+                               ws.row_weight, d_out, ws.tiles, ws.error_flag, stream, err);
+}
+
+extern "C" int* wisp_b200_moe_error_word(const WispMoeConfig* cfg, void* d_workspace) {
+  if (validate(cfg, nullptr) != WISP_OK || !d_workspace) return nullptr;
+  return carve(cfg, d_workspace).error_flag;
+}
+
+extern "C" WispError wisp_b200_check_error_flag(const int* d_error_flag, cudaStream_t stream,
+                                                WispErrCtx* err) {
+  if (!d_error_flag) return WB_FAIL(WISP_ERR_INVALID_ARG, "check_error_flag: null pointer");
+  int h = 0;
+  WB_CUDA_CHECK(cudaMemcpyAsync(&h, d_error_flag, sizeof(int), cudaMemcpyDeviceToHost, stream));
+  WB_CUDA_CHECK(cudaStreamSynchronize(stream));
+  if (h) return WB_FAIL(WISP_ERR_TIMEOUT, "a tensor-core kernel gave up waiting (device error word %d)", h);
+  return WISP_OK;
+}
+
+// Header parse on host memory; semantics of csrc/core/wisp_engine.c:268-303.
+extern "C" WispError wisp_b200_parse_expert_header(const void* blob, size_t blob_size,
+                                                   WispExpertMeta* meta, WispErrCtx* err) {
+  if (!blob || !meta) return WB_FAIL(WISP_ERR_OOM, "NULL pointer: expert_parse_header: blob");
+  if (blob_size < sizeof(WispExpertHeader))
+    return WB_FAIL(WISP_ERR_MODEL, "expert blob too small: %zu bytes", blob_size);
+  WispExpertHeader h;
+  memcpy(&h, blob, sizeof h);
+  if (h.magic != WISP_EXPERT_MAGIC || h.version != WISP_EXPERT_VERSION || h.n_mats != WISP_EXPERT_NMATS)
+    return WB_FAIL(WISP_ERR_MODEL, "expert blob corrupt: magic=%08x version=%u n_mats=%u", h.magic,
+                   h.version, h.n_mats);
+  size_t off = sizeof(WispExpertHeader);
+  for (int m = 0; m < WISP_EXPERT_NMATS; m++) {
+    meta->rows[m] = h.mats[m].rows;
+    meta->cols[m] = h.mats[m].cols;
+    meta->packed_off[m] = off;
+    off += h.mats[m].packed_bytes;
+    meta->scales_off[m] = off;
+    off += h.mats[m].scales_bytes;
+    meta->zeros_off[m] = off;
+    off += h.mats[m].zeros_bytes;
+  }
+  meta->group_size = h.group_size;
+  meta->total_bytes = off;
+  meta->valid = 1;
+  if (off > blob_size) {
+    meta->valid = 0;
+    return WB_FAIL(WISP_ERR_MODEL, "expert blob truncated: needs %zu, have %zu", off, blob_size);
+  }
+  return WISP_OK;
+}
+
+extern "C" const char* wisp_b200_version(void) { return "wisp_b200 0.1.0 (sm_100a)"; }

@@ -1,0 +1,504 @@
+// route.cu -- batched routing and token -> expert dispatch for T tokens.
+//
+//   router_logits_kernel  logits = x W^T (+ bias), bf16 inputs, fp32 sums.
+//                         Tiled 64x64 with a deterministic split-K so small
+//                         token counts still fill the GPU (partials are
+//                         summed in a fixed order by the top-k kernel).
+//   topk_kernel           one warp per token. Softmax scoring follows the
+//                         reference exactly (csrc/core/wisp_engine.c:782-818,
+//                         csrc/cuda/router.cu:67-138): softmax, k rounds of
+//                         "largest untaken probability, lower index on a
+//                         tie", renormalise. Sigmoid group-limited scoring
+//                         (DeepSeek-V3 convention; absent in the reference):
+//                         group score = sum of the top-2 sigmoid scores,
+//                         keep topk_groups groups, pick k experts among
+//                         them, w = s / sum(s) * routed_scaling.
+//   count / fill kernels  one warp per expert scans all (token, slot) pairs
+//                         in order and compacts its matches with a ballot,
+//                         so every expert's rows are sorted by token and the
+//                         permutation is deterministic. An always-on shared
+//                         expert is one more segment holding every token.
+//   pack_rows_kernel      gathers bf16 token rows into fp16 rows in the
+//                         interleaved K order the tensor-core kernel expects.
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "internal.h"
+
+using namespace wb;
+
+namespace {
+
+constexpr int kRT = 64;   // router tile: tokens
+constexpr int kRE = 64;   // router tile: experts
+constexpr int kRK = 32;   // K chunk
+
+__device__ __forceinline__ float bf16f(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+
+__device__ __forceinline__ float f16f(uint16_t b) { return __half2float(__ushort_as_half(b)); }
+
+// grid (ceil(E/64), ceil(T/64), splits); 256 threads compute 4x4 each.
+// W_FP16 selects the router weight dtype (bf16 or fp16); x is bf16.
+template <bool W_FP16>
+__global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __restrict__ x,
+                                                            const uint16_t* __restrict__ W,
+                                                            float* __restrict__ part, int T, int E,
+                                                            int M, int kspan) {
+  __shared__ float xs[kRK][kRT + 4];
+  __shared__ float ws[kRK][kRE + 4];
+  const int e0 = blockIdx.x * kRE, t0 = blockIdx.y * kRT;
+  const int kb = blockIdx.z * kspan, ke = min(M, kb + kspan);
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // 16 x 16 threads
+  float acc[4][4] = {};
+  for (int k0 = kb; k0 < ke; k0 += kRK) {
+    // 64 rows x 32 K per operand: 256 threads x 8 values.
+    {
+      const int row = threadIdx.x >> 2, kq = (threadIdx.x & 3) * 8;
+      const int t = t0 + row, e = e0 + row;
+      uint4 xv = make_uint4(0, 0, 0, 0), wv = make_uint4(0, 0, 0, 0);
+      if (t < T && k0 + kq < ke) xv = __ldg(reinterpret_cast<const uint4*>(x + (size_t)t * M + k0 + kq));
+      if (e < E && k0 + kq < ke) wv = __ldg(reinterpret_cast<const uint4*>(W + (size_t)e * M + k0 + kq));
+      const uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        xs[kq + 2 * j][row] = bf16f((uint16_t)(xa[j] & 0xffff));
+        xs[kq + 2 * j + 1][row] = bf16f((uint16_t)(xa[j] >> 16));
+        ws[kq + 2 * j][row] = W_FP16 ? f16f((uint16_t)(wa[j] & 0xffff)) : bf16f((uint16_t)(wa[j] & 0xffff));
+        ws[kq + 2 * j + 1][row] = W_FP16 ? f16f((uint16_t)(wa[j] >> 16)) : bf16f((uint16_t)(wa[j] >> 16));
+      }
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int k = 0; k < kRK; k++) {
+      const float4 a = *reinterpret_cast<const float4*>(&xs[k][ty * 4]);
+      const float4 b = *reinterpret_cast<const float4*>(&ws[k][tx * 4]);
+      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+  float* out = part + (size_t)blockIdx.z * T * E;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int t = t0 + ty * 4 + i;
+    if (t >= T) continue;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int e = e0 + tx * 4 + j;
+      if (e < E) out[(size_t)t * E + e] = acc[i][j];
+    }
+  }
+}
+
+// Warp argmax with the lower index winning ties; (v, i) = (-inf/-1, -1) for
+// an empty lane.
+__device__ __forceinline__ void warp_argmax(float& v, int& i) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+    if (oi >= 0 && (i < 0 || ov > v || (ov == v && oi < i))) {
+      v = ov;
+      i = oi;
+    }
+  }
+}
+
+constexpr int kMaxPerLane = 32;  // E <= 1024
+
+// One warp per token. Writes idx/w [T x k] and, optionally, the fp32 logits.
+__global__ void topk_kernel(const float* __restrict__ part, int splits, const float* __restrict__ bias,
+                            int T, int E, int k, int scoring, int n_groups, int topk_groups,
+                            float scaling, int* __restrict__ idx, float* __restrict__ wout,
+                            float* __restrict__ logits_out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (t >= T) return;
+  const int per = (E + 31) / 32;
+  float v[kMaxPerLane];
+#pragma unroll
+  for (int j = 0; j < kMaxPerLane; j++) {
+    v[j] = -INFINITY;
+    const int e = lane + 32 * j;
+    if (j < per && e < E) {
+      float s = 0.f;
+      for (int z = 0; z < splits; z++) s += part[((size_t)z * T + t) * E + e];
+      if (bias) s += bias[e];
+      v[j] = s;
+      if (logits_out) logits_out[(size_t)t * E + e] = s;
+    }
+  }
+  bool taken[kMaxPerLane];
+#pragma unroll
+  for (int j = 0; j < kMaxPerLane; j++) taken[j] = false;
+
+  if (scoring == WISP_SCORE_SOFTMAX) {
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kMaxPerLane; j++) mx = fmaxf(mx, v[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxPerLane; j++) {
+      v[j] = (j < per && lane + 32 * j < E) ? expf(v[j] - mx) : -1.f;
+      sum += v[j] > 0.f ? v[j] : 0.f;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float inv = 1.f / sum;
+#pragma unroll
+    for (int j = 0; j < kMaxPerLane; j++)
+      if (v[j] >= 0.f) v[j] *= inv;
+    float wsum = 0.f;
+    float myw = 0.f;
+    int myi = -1;
+    for (int r = 0; r < k; r++) {
+      float bv = -1.f;
+      int bi = -1;
+#pragma unroll
+      for (int j = 0; j < kMaxPerLane; j++) {
+        const int e = lane + 32 * j;
+        if (j < per && e < E && !taken[j] && v[j] > bv) {
+          bv = v[j];
+          bi = e;
+        }
+      }
+      warp_argmax(bv, bi);
+      if (bi >= 0 && (bi & 31) == lane) taken[bi >> 5] = true;
+      if (lane == r) {
+        myw = bv;
+        myi = bi;
+      }
+      wsum += bv;
+    }
+    if (lane < k) {
+      idx[(size_t)t * k + lane] = myi;
+      wout[(size_t)t * k + lane] = wsum > 0.f ? myw / wsum : myw;
+    }
+  } else {
+    // Sigmoid group-limited.
+    const int gsz = E / n_groups;
+#pragma unroll
+    for (int j = 0; j < kMaxPerLane; j++)
+      if (j < per && lane + 32 * j < E) v[j] = 1.f / (1.f + expf(-v[j]));
+    // Group scores: lane g scans its group through shared memory.
+    __shared__ float sval[8][1024];
+    float* mys = sval[warp];
+#pragma unroll
+    for (int j = 0; j < kMaxPerLane; j++)
+      if (j < per && lane + 32 * j < E) mys[lane + 32 * j] = v[j];
+    __syncwarp();
+    float gscore = -INFINITY;
+    if (lane < n_groups) {
+      float a = -INFINITY, b = -INFINITY;
+      for (int q = 0; q < gsz; q++) {
+        const float s = mys[lane * gsz + q];
+        if (s > a) {
+          b = a;
+          a = s;
+        } else if (s > b) {
+          b = s;
+        }
+      }
+      gscore = a + (gsz > 1 ? b : 0.f);
+    }
+    bool gsel = false;  // lane g: is group g kept
+    for (int r = 0; r < topk_groups; r++) {
+      float bv = (lane < n_groups && !gsel) ? gscore : -INFINITY;
+      int bi = (lane < n_groups && !gsel) ? lane : -1;
+      warp_argmax(bv, bi);
+      if (bi == lane) gsel = true;
+    }
+    const unsigned gmask = __ballot_sync(0xffffffffu, gsel);
+    float ssum = 0.f, myw = 0.f;
+    int myi = -1;
+    for (int r = 0; r < k; r++) {
+      float bv = -INFINITY;
+      int bi = -1;
+#pragma unroll
+      for (int j = 0; j < kMaxPerLane; j++) {
+        const int e = lane + 32 * j;
+        if (j < per && e < E && !taken[j] && ((gmask >> (e / gsz)) & 1u) && (bi < 0 || v[j] > bv)) {
+          bv = v[j];
+          bi = e;
+        }
+      }
+      warp_argmax(bv, bi);
+      if (bi >= 0 && (bi & 31) == lane) taken[bi >> 5] = true;
+      if (lane == r) {
+        myw = bv;
+        myi = bi;
+      }
+      ssum += bi >= 0 ? bv : 0.f;
+    }
+    if (lane < k) {
+      idx[(size_t)t * k + lane] = myi;
+      wout[(size_t)t * k + lane] = myw / ssum * scaling;
+    }
+  }
+}
+
+// counts[v] for the routed experts: one warp per expert over all T*k slots.
+__global__ void count_kernel(const int* __restrict__ idx, int nslots, int E, int T, int has_shared,
+                             int* __restrict__ counts) {
+  const int v = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (v >= E + has_shared) return;
+  if (v == E) {
+    if (lane == 0) counts[v] = T;
+    return;
+  }
+  int c = 0;
+  for (int base = 0; base < nslots; base += 32) {
+    const int s = base + lane;
+    const bool hit = s < nslots && __ldg(idx + s) == v;
+    c += __popc(__ballot_sync(0xffffffffu, hit));
+  }
+  if (lane == 0) counts[v] = c;
+}
+
+// Exclusive scan of counts into segments (single block).
+__global__ void segments_kernel(const int* __restrict__ counts, int V, WispSegment* __restrict__ segs) {
+  __shared__ int warp_tot[32];
+  __shared__ int carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  for (int base = 0; base < V; base += blockDim.x) {
+    const int v = base + threadIdx.x;
+    const int n = v < V ? counts[v] : 0;
+    int x = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_tot[w] = x;
+    __syncthreads();
+    if (w == 0) {
+      int tv = lane < (int)(blockDim.x >> 5) ? warp_tot[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, tv, o);
+        if (lane >= o) tv += y;
+      }
+      warp_tot[lane] = tv;
+    }
+    __syncthreads();
+    const int incl = x + (w > 0 ? warp_tot[w - 1] : 0) + carry;
+    if (v < V) {
+      WispSegment s;
+      s.expert = v;
+      s.row_begin = incl - n;
+      s.rows = n;
+      s.reserved = 0;
+      segs[v] = s;
+    }
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = incl;
+    __syncthreads();
+  }
+}
+
+// Rows of expert v sorted by (token, slot): row_token / row_weight.
+__global__ void fill_kernel(const int* __restrict__ idx, const float* __restrict__ w, int nslots,
+                            int k, int E, int T, int has_shared, const WispSegment* __restrict__ segs,
+                            int* __restrict__ row_token, float* __restrict__ row_weight) {
+  const int v = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (v >= E + has_shared) return;
+  const int begin = segs[v].row_begin;
+  if (v == E) {
+    for (int t = lane; t < T; t += 32) {
+      row_token[begin + t] = t;
+      row_weight[begin + t] = 1.f;
+    }
+    return;
+  }
+  int pos = begin;
+  for (int base = 0; base < nslots; base += 32) {
+    const int s = base + lane;
+    const bool hit = s < nslots && __ldg(idx + s) == v;
+    const unsigned m = __ballot_sync(0xffffffffu, hit);
+    if (hit) {
+      const int p = pos + __popc(m & ((1u << lane) - 1u));
+      row_token[p] = s / k;
+      row_weight[p] = w[s];
+    }
+    pos += __popc(m);
+  }
+}
+
+// xp[p] = fp16(x[src[p]]) in interleaved K order; each thread moves 8 values.
+__global__ void pack_rows_kernel(const uint16_t* __restrict__ x, const int* __restrict__ src, int n_rows,
+                                 int M, uint16_t* __restrict__ xp) {
+  const int p = blockIdx.x;
+  if (p >= n_rows) return;
+  const int s = src ? src[p] : p;
+  const uint16_t* xr = x + (size_t)s * M;
+  uint16_t* orow = xp + (size_t)p * M;
+  for (int k8 = threadIdx.x * 8; k8 < M; k8 += blockDim.x * 8) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(xr + k8));
+    const uint32_t a[4] = {v.x, v.y, v.z, v.w};
+    float f[8];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      f[2 * j] = bf16f((uint16_t)(a[j] & 0xffff));
+      f[2 * j + 1] = bf16f((uint16_t)(a[j] >> 16));
+    }
+    // logical slot j holds physical offset {0,4,1,5,2,6,3,7}[j]
+    const __half2 h0 = __floats2half2_rn(f[0], f[4]);
+    const __half2 h1 = __floats2half2_rn(f[1], f[5]);
+    const __half2 h2 = __floats2half2_rn(f[2], f[6]);
+    const __half2 h3 = __floats2half2_rn(f[3], f[7]);
+    *reinterpret_cast<uint4*>(orow + k8) = make_uint4(h22u(h0), h22u(h1), h22u(h2), h22u(h3));
+  }
+}
+
+// y[t] = bf16(x[t] / rms(x[t])): per-token RMS normalisation (no weight)
+// between stacked MoE layers. One block per token.
+__global__ void rms_rescale_kernel(const float* __restrict__ x, uint16_t* __restrict__ y, int M,
+                                   float eps) {
+  __shared__ float red[32];
+  const float* xr = x + (size_t)blockIdx.x * M;
+  float s = 0.f;
+  for (int i = threadIdx.x; i < M; i += blockDim.x) s += xr[i] * xr[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(red[0] / M + eps);
+  uint16_t* yr = y + (size_t)blockIdx.x * M;
+  for (int i = threadIdx.x; i < M; i += blockDim.x)
+    yr[i] = __bfloat16_as_ushort(__float2bfloat16_rn(xr[i] * inv));
+}
+
+// out[row_token[p]] += row_weight[p] * y[p] for p < n_rows (fp32 atomics):
+// the combine of rows returned by the expert-parallel all-to-all.
+__global__ void combine_rows_kernel(const float* __restrict__ y, const int* __restrict__ row_token,
+                                    const float* __restrict__ row_weight, int M,
+                                    float* __restrict__ out) {
+  const int p = blockIdx.x;
+  const int t = row_token[p];
+  const float w = row_weight[p];
+  const float* yr = y + (size_t)p * M;
+  float* orow = out + (size_t)t * M;
+  for (int i = threadIdx.x; i < M; i += blockDim.x) red_add_f32(orow + i, w * yr[i]);
+}
+
+int g_sms_cached = 0;
+
+}  // namespace
+
+namespace wb {
+
+// Workspace carving shared with moe.cu.
+size_t router_splits(int T, int E, int M) {
+  if (!g_sms_cached) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_sms_cached, cudaDevAttrMultiProcessorCount, dev);
+    if (g_sms_cached <= 0) g_sms_cached = 148;
+  }
+  const long long tiles = (long long)((E + kRE - 1) / kRE) * ((T + kRT - 1) / kRT);
+  long long splits = (2LL * g_sms_cached + tiles - 1) / tiles;
+  const long long max_splits = std::max(1, M / 256);
+  if (splits > max_splits) splits = max_splits;
+  if (splits < 1) splits = 1;
+  return (size_t)splits;
+}
+
+WispError launch_route(const WispMoeConfig* c, const uint16_t* x, const uint16_t* W,
+                       const float* bias, float* part, size_t splits, float* logits_out, int* idx,
+                       float* w, cudaStream_t st, WispErrCtx* err) {
+  const int T = c->tokens, E = c->n_experts, M = c->hidden;
+  int kspan = (M + (int)splits - 1) / (int)splits;
+  kspan = (kspan + kRK - 1) / kRK * kRK;
+  const int nsplit = (M + kspan - 1) / kspan;
+  dim3 g1((E + kRE - 1) / kRE, (T + kRT - 1) / kRT, nsplit);
+  if (c->router_fp16)
+    router_logits_kernel<true><<<g1, 256, 0, st>>>(x, W, part, T, E, M, kspan);
+  else
+    router_logits_kernel<false><<<g1, 256, 0, st>>>(x, W, part, T, E, M, kspan);
+  topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(part, nsplit, bias, T, E, c->top_k, c->scoring,
+                                           c->n_groups, c->topk_groups, c->routed_scaling, idx, w,
+                                           logits_out);
+  WB_CUDA_CHECK(cudaGetLastError());
+  return WISP_OK;
+}
+
+WispError launch_plan(const WispMoeConfig* c, const int* idx, const float* w, int* counts,
+                      WispSegment* segs, int* row_token, float* row_weight, cudaStream_t st,
+                      WispErrCtx* err) {
+  const int T = c->tokens, E = c->n_experts, k = c->top_k, sh = c->has_shared ? 1 : 0;
+  const int V = E + sh;
+  count_kernel<<<(V + 7) / 8, 256, 0, st>>>(idx, T * k, E, T, sh, counts);
+  segments_kernel<<<1, 1024, 0, st>>>(counts, V, segs);
+  fill_kernel<<<(V + 7) / 8, 256, 0, st>>>(idx, w, T * k, k, E, T, sh, segs, row_token, row_weight);
+  WB_CUDA_CHECK(cudaGetLastError());
+  return WISP_OK;
+}
+
+WispError launch_pack(const uint16_t* x, const int* src, int n_rows, int M, uint16_t* xp,
+                      cudaStream_t st, WispErrCtx* err) {
+  if (n_rows <= 0) return WISP_OK;
+  pack_rows_kernel<<<n_rows, 128, 0, st>>>(x, src, n_rows, M, xp);
+  WB_CUDA_CHECK(cudaGetLastError());
+  return WISP_OK;
+}
+
+}  // namespace wb
+
+extern "C" WispError wisp_b200_pack_rows(const uint16_t* d_x, const int* d_src, int n_rows,
+                                         int hidden, uint16_t* d_xp, cudaStream_t stream,
+                                         WispErrCtx* err) {
+  if (!d_x || !d_xp || hidden <= 0 || hidden % 8)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "pack_rows: bad arguments (hidden=%d)", hidden);
+  if (((uintptr_t)d_x | (uintptr_t)d_xp) & 15)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "pack_rows: buffers must be 16-byte aligned");
+  return wb::launch_pack(d_x, d_src, n_rows, hidden, d_xp, stream, err);
+}
+
+extern "C" WispError wisp_b200_dispatch_plan(const WispMoeConfig* cfg, const int* d_idx,
+                                             const float* d_w, int* d_counts, WispSegment* d_segs,
+                                             int* d_row_token, float* d_row_weight,
+                                             cudaStream_t stream, WispErrCtx* err) {
+  if (!cfg || !d_idx || !d_w || !d_counts || !d_segs || !d_row_token || !d_row_weight)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "dispatch_plan: null pointer argument");
+  if (cfg->tokens <= 0 || cfg->top_k <= 0 || cfg->n_experts <= 0)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "dispatch_plan: tokens=%d top_k=%d n_experts=%d",
+                   cfg->tokens, cfg->top_k, cfg->n_experts);
+  return wb::launch_plan(cfg, d_idx, d_w, d_counts, d_segs, d_row_token, d_row_weight, stream, err);
+}
+
+extern "C" WispError wisp_b200_rms_rescale(const float* d_in, uint16_t* d_out, int tokens,
+                                           int hidden, float eps, cudaStream_t stream,
+                                           WispErrCtx* err) {
+  if (!d_in || !d_out || tokens <= 0 || hidden <= 0)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "rms_rescale: bad arguments");
+  rms_rescale_kernel<<<tokens, 256, 0, stream>>>(d_in, d_out, hidden, eps);
+  WB_CUDA_CHECK(cudaGetLastError());
+  return WISP_OK;
+}
+
+extern "C" WispError wisp_b200_combine_rows(const float* d_y, const int* d_row_token,
+                                            const float* d_row_weight, int n_rows, int hidden,
+                                            float* d_out, cudaStream_t stream, WispErrCtx* err) {
+  if (n_rows < 0 || hidden <= 0 || (n_rows > 0 && (!d_y || !d_row_token || !d_row_weight || !d_out)))
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "combine_rows: bad arguments");
+  if (n_rows == 0) return WISP_OK;
+  combine_rows_kernel<<<n_rows, 256, 0, stream>>>(d_y, d_row_token, d_row_weight, hidden, d_out);
+  WB_CUDA_CHECK(cudaGetLastError());
+  return WISP_OK;
+}
