@@ -64,7 +64,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
@@ -268,11 +268,18 @@ def main() -> None:
 
     clocks = ClockSampler(local)
     clocks.start()
+    # keep the GPU busy while nvidia-smi starts sampling
+    t_spin = time.perf_counter()
+    while time.perf_counter() - t_spin < 1.0:
+        step(x0)
+        torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")
     ev0.record(stream)
     for _ in range(args.steps):
         step(x0)
     ev1.record(stream)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()

@@ -76,6 +76,10 @@ CONFIGS: dict[str, MoeSpec] = {
     "ds_prefill": MoeSpec("ds_prefill", tokens=4096, seed=2, skew=True, **_DS),
     "ep_stack": MoeSpec("ep_stack", 7168, 2048, 384, 8, has_shared=True, tokens=256, layers=4,
                         seed=3),
+    # One layer of the ep_stack shape with 64 experts (~1.5 GB of weights,
+    # still larger than L2): the small case for ncu captures.
+    "ep_profile": MoeSpec("ep_profile", 7168, 2048, 64, 8, has_shared=True, tokens=40, layers=1,
+                          seed=3),
 }
 
 
