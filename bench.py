@@ -337,13 +337,13 @@ def main() -> None:
                  stream.cuda_stream)
         abi.call("wisp_b200_pack_rows", x0.data_ptr(), row_token.data_ptr(), R, spec.hidden,
                  xp.data_ptr(), stream.cuda_stream)
-        table = [lw.table for lw in layers_w]
+        table = [lw.prepare() for lw in layers_w]
         evs = []
         for rep in range(args.kernel_reps):
             for l in range(L):   # rotate the layers' weights so L2 never holds them
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 a.record(stream)
-                abi.call("wisp_b200_grouped_ffn", C.byref(cfg), table[l].data_ptr(), segs.data_ptr(), V, R,
+                abi.call("wisp_b200_grouped_ffn", C.byref(cfg), table[l].data_ptr(), V, segs.data_ptr(), V, R,
                          xp.data_ptr(), h.data_ptr(), 0, row_token.data_ptr(), row_w.data_ptr(),
                          out.data_ptr(), tiles.data_ptr(), flag.data_ptr(), stream.cuda_stream)
                 b.record(stream)

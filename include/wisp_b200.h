@@ -198,7 +198,21 @@ typedef struct {
     const float* router_bias;       /* fp32 [E], added before scoring; may be NULL */
     const WispInt4Expert* experts;  /* DEVICE array: E routed experts, then the
                                        shared expert when cfg->has_shared */
+    const void* prepared;           /* from wisp_b200_prepare_experts over the
+                                       same E (+1) entries */
 } WispMoeWeights;
+
+/* One-time preparation of a weight set for the tensor-core kernels (once per
+ * layer when the weights are loaded, or when an expert blob is promoted into
+ * the VRAM tier): per matrix a TMA descriptor of its packed nibbles, and its
+ * scales / zero points transposed to [128-row tile][group][row] so each
+ * stage's scales are one contiguous run. The packed nibbles stay where they
+ * are and must stay valid. d_experts is a DEVICE array of n_entries; the call
+ * copies it to the host, so it synchronises `stream`. */
+size_t wisp_b200_prepared_bytes(const WispMoeConfig* cfg, int n_entries);
+WispError wisp_b200_prepare_experts(const WispMoeConfig* cfg, const WispInt4Expert* d_experts,
+                                    int n_entries, void* d_prepared, size_t prepared_bytes,
+                                    cudaStream_t stream, WispErrCtx* err);
 
 size_t wisp_b200_moe_workspace_bytes(const WispMoeConfig* cfg);
 
@@ -228,7 +242,8 @@ typedef struct {
     int32_t reserved;
 } WispSegment;
 
-/* Grouped expert FFN over pre-permuted rows.
+/* Grouped expert FFN over pre-permuted rows. d_prepared / n_entries: a
+ * prepared weight set (segment experts index its entries).
  *   d_xp:   fp16 [R x M] activation rows in interleaved K order (within each
  *           8 K: 0,4,1,5,2,6,3,7) -- produced by wisp_b200_pack_rows.
  *   d_segs: DEVICE array of n_segs segments.
@@ -239,7 +254,7 @@ typedef struct {
  * d_error_flag: device int set to nonzero if a bounded wait gave up (may be
  * NULL); check it with wisp_b200_check_error_flag. */
 size_t wisp_b200_tiles_words(int n_segs);
-WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const WispInt4Expert* d_experts,
+WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void* d_prepared, int n_entries,
                                 const WispSegment* d_segs, int n_segs, int rows_capacity,
                                 const uint16_t* d_xp, uint16_t* d_h, int mode,
                                 const int* d_row_token, const float* d_row_weight,

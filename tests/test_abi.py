@@ -130,10 +130,24 @@ def test_expert_ffn_argument_checks(golden_dir):
 def test_grouped_ffn_argument_checks():
     c = _cfg(group_size=32)
     err = abi.WispErrCtx()
-    rc = abi.lib().wisp_b200_grouped_ffn(C.byref(c), 16, 16, 1, 8, 16, 16, 0, 16, 16, 16, 16, None,
-                                         None, C.byref(err))
+    rc = abi.lib().wisp_b200_grouped_ffn(C.byref(c), 256, 4, 16, 1, 8, 16, 16, 0, 16, 16, 16, 16,
+                                         None, None, C.byref(err))
     assert rc == abi.WISP_ERR_INVALID_ARG and b"group_size" in err.message
     c = _cfg()
-    rc = abi.lib().wisp_b200_grouped_ffn(C.byref(c), 16, 16, 1, 8, 16, 16, 0, None, None, 16, 16,
+    rc = abi.lib().wisp_b200_grouped_ffn(C.byref(c), 256, 4, 16, 1, 8, 16, 16, 0, None, None, 16, 16,
                                          None, None, C.byref(err))
     assert rc == abi.WISP_ERR_INVALID_ARG and b"mode 0" in err.message
+    rc = abi.lib().wisp_b200_grouped_ffn(C.byref(c), 264, 4, 16, 1, 8, 16, 16, 1, None, None, 16, 16,
+                                         None, None, C.byref(err))
+    assert rc == abi.WISP_ERR_INVALID_ARG and b"256-byte" in err.message
+
+
+def test_prepared_size_and_checks():
+    c = _cfg()
+    n = abi.lib().wisp_b200_prepared_bytes(C.byref(c), 9)
+    # 27 descriptors + flags + transposed scales and zeros for 27 matrices
+    assert n >= 27 * 128 + 27 * 4 + 2 * 27 * (256 * 128 // 64) * 2
+    assert abi.lib().wisp_b200_prepared_bytes(C.byref(_cfg(group_size=32)), 9) == 0
+    err = abi.WispErrCtx()
+    rc = abi.lib().wisp_b200_prepare_experts(C.byref(c), 16, 9, 256, n - 1, None, C.byref(err))
+    assert rc == abi.WISP_ERR_INVALID_ARG and b"required" in err.message

@@ -1,0 +1,163 @@
+"""Expert-parallel exchange logic on CPU ranks (gloo, world size 2).
+
+EpLayer's dispatch/combine plumbing (count exchange, send/receive splits,
+expert-major receive layout, all-to-all ordering, weighted combine) runs for
+real over torch.distributed; the compute steps are a host implementation
+built on the fp64 oracle. The result must equal the single-process oracle
+output for every token. Also: a rank that dies before the collective makes
+the others fail within the process-group timeout instead of hanging.
+"""
+from __future__ import annotations
+
+import os
+import socket
+import tempfile
+from datetime import timedelta
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from wisp_b200 import synth
+from wisp_b200.ep import EpLayer, block_range, recv_layout, send_splits
+
+SPEC = synth.MoeSpec("ep_cpu", 256, 128, 8, 2, group_size=64, has_shared=True, tokens=10, seed=21)
+
+
+class CpuOps:
+    """Host stand-in for CudaOps: same contract, fp64 oracle arithmetic."""
+
+    def __init__(self, orc, lw):
+        self.orc, self.lw = orc, lw
+
+    def act_dtype(self):
+        return torch.float64
+
+    def route(self, cfg, lw, x, idx, w, logits):
+        from helpers import oracle_route
+        i, ww, _ = oracle_route(self.orc, lw, x)
+        idx.copy_(torch.from_numpy(i))
+        w.copy_(torch.from_numpy(ww).float())
+
+    def plan(self, cfg, idx, w, counts, segs, row_token, row_weight):
+        ii, ww = idx.numpy(), w.numpy()
+        T, k = ii.shape
+        p = 0
+        for e in range(cfg.n_experts):
+            n = 0
+            for t in range(T):
+                for j in range(k):
+                    if ii[t, j] == e:
+                        row_token[p] = t
+                        row_weight[p] = float(ww[t, j])
+                        p += 1
+                        n += 1
+            counts[e] = n
+
+    def pack(self, x, src, n_rows, xp):
+        xd = x.double()
+        xp[:n_rows] = xd if src is None else xd[src[:n_rows].long()]
+
+    def grouped(self, cfg, lw, segs, rows, xp, h, mode, row_token, row_weight, out, tiles, flag):
+        for e, b, r in segs:
+            mats = self.lw.expert_host(e)
+            for p in range(b, b + r):
+                y = self.orc.expert_ffn(mats, self.lw.spec.group_size, xp[p].numpy(), 1.0)
+                if mode == 1:
+                    out[p] = torch.from_numpy(y).float()
+                else:
+                    t = int(row_token[p])
+                    out[t] += float(row_weight[p]) * torch.from_numpy(y).float()
+
+    def combine(self, y, row_token, row_weight, n_rows, out):
+        for p in range(n_rows):
+            out[int(row_token[p])] += float(row_weight[p]) * y[p]
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, outdir, spec, mode):
+    import sys
+    from pathlib import Path
+    sys.path.insert(0, str(Path(__file__).resolve().parent))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=8))
+    try:
+        from oracle.oracle import Oracle
+        orc = Oracle()
+        keep = range(*block_range(spec.n_experts, world, rank))
+        layers, x = synth.make_model(spec, "cpu", keep=keep)
+        lw = layers[0]
+        t0, t1 = block_range(spec.tokens, world, rank)
+        layer = EpLayer(spec, lw, t1 - t0, rank, world, ops=CpuOps(orc, lw), device=torch.device("cpu"))
+        if mode == "die" and rank == 1:
+            raise SystemExit(3)          # leaves before the first collective
+        out = torch.zeros((t1 - t0, spec.hidden), dtype=torch.float32)
+        try:
+            layer.forward(x[t0:t1].contiguous(), out)
+            np.save(os.path.join(outdir, f"out{rank}.npy"), out.numpy())
+        except Exception as exc:  # noqa: BLE001 - reported to the parent
+            with open(os.path.join(outdir, f"err{rank}.txt"), "w") as f:
+                f.write(type(exc).__name__ + ": " + str(exc))
+    finally:
+        if mode != "die":
+            dist.destroy_process_group()
+
+
+def test_send_splits_and_recv_layout():
+    counts = np.array([3, 0, 2, 5, 1, 1, 0, 4])
+    assert send_splits(counts, 8, 2) == [10, 6]
+    assert send_splits(counts, 8, 4) == [3, 7, 2, 4]
+    rc = np.array([[1, 2], [0, 3], [4, 0]])       # 3 sources, 2 local experts
+    segs, per_src = recv_layout(rc)
+    assert per_src == [3, 3, 4]
+    # expert-major: expert 0 from sources 0,1,2 then expert 1 from 0,1,2
+    assert segs == [(0, 0, 1), (0, 3, 0), (0, 6, 4), (1, 1, 2), (1, 3, 3), (1, 10, 0)]
+
+
+@pytest.mark.parametrize("spec", [SPEC, synth.small(SPEC, skew=True, seed=4, tokens=7)])
+def test_ep_two_ranks_matches_single_process(orc, spec):
+    from helpers import oracle_outputs, oracle_route
+    port = _free_port()
+    with tempfile.TemporaryDirectory() as td:
+        mp.start_processes(_worker, args=(2, port, td, spec, "ok"), nprocs=2, join=True,
+                           start_method="spawn")
+        for r in range(2):
+            assert not os.path.exists(os.path.join(td, f"err{r}.txt")), open(os.path.join(td, f"err{r}.txt")).read()
+        got = np.concatenate([np.load(os.path.join(td, f"out{r}.npy")) for r in range(2)])
+    layers, x = synth.make_model(spec, "cpu")
+    lw = layers[0]
+    idx, w, _ = oracle_route(orc, lw, x)
+    ref = oracle_outputs(orc, lw, x, idx, w, list(range(spec.tokens)))
+    np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-5 * np.abs(ref).max())
+
+
+def test_ep_rank_failure_is_detected_not_hung():
+    port = _free_port()
+    with tempfile.TemporaryDirectory() as td:
+        ctx = mp.start_processes(_worker, args=(2, port, td, SPEC, "die"), nprocs=2, join=False,
+                                 start_method="spawn")
+        import time
+        deadline = time.time() + 60
+        while time.time() < deadline:
+            try:
+                if ctx.join(timeout=1):
+                    break
+            except Exception:  # noqa: BLE001 - rank 1 exits with an error on purpose
+                pass
+            if all(not p.is_alive() for p in ctx.processes):
+                break
+        alive = [p.is_alive() for p in ctx.processes]
+        for p in ctx.processes:
+            if p.is_alive():
+                p.kill()
+        assert not any(alive), "a surviving rank hung on the collective"
+        assert os.path.exists(os.path.join(td, "err0.txt")), "rank 0 did not report the failure"

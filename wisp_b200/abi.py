@@ -57,7 +57,8 @@ class WispInt4Expert(C.Structure):
 
 
 class WispMoeWeights(C.Structure):
-    _fields_ = [("router_w", C.c_void_p), ("router_bias", C.c_void_p), ("experts", C.c_void_p)]
+    _fields_ = [("router_w", C.c_void_p), ("router_bias", C.c_void_p), ("experts", C.c_void_p),
+                ("prepared", C.c_void_p)]
 
 
 class WispSegment(C.Structure):
@@ -92,8 +93,10 @@ SIGNATURES = {
     "wisp_b200_route": (_I, [C.POINTER(WispMoeConfig), C.POINTER(WispMoeWeights), _P, _P, _P,
                              _P, _P, _E]),
     "wisp_b200_tiles_words": (_SZ, [_I]),
-    "wisp_b200_grouped_ffn": (_I, [C.POINTER(WispMoeConfig), _P, _P, _I, _I, _P, _P, _I, _P, _P,
-                                   _P, _P, _P, _P, _E]),
+    "wisp_b200_grouped_ffn": (_I, [C.POINTER(WispMoeConfig), _P, _I, _P, _I, _I, _P, _P, _I, _P,
+                                   _P, _P, _P, _P, _P, _E]),
+    "wisp_b200_prepared_bytes": (_SZ, [C.POINTER(WispMoeConfig), _I]),
+    "wisp_b200_prepare_experts": (_I, [C.POINTER(WispMoeConfig), _P, _I, _P, _SZ, _P, _E]),
     "wisp_b200_pack_rows": (_I, [_P, _P, _I, _I, _P, _P, _E]),
     "wisp_b200_dispatch_plan": (_I, [C.POINTER(WispMoeConfig), _P, _P, _P, _P, _P, _P, _P, _E]),
     "wisp_b200_rms_rescale": (_I, [_P, _P, _I, _I, _F, _P, _E]),

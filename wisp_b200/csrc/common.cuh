@@ -101,13 +101,15 @@ WB_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
       ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
+// try_wait with a suspend-time hint: the warp may sleep (without taking
+// issue slots) until the phase completes or ~20 us pass.
 WB_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(20000u) : "memory");
   return ok != 0;
 }
 
@@ -143,6 +145,15 @@ WB_DEV void tma_load_2d(void* smem_dst, const CUtensorMap* m, uint64_t* bar, int
       " [%0], [%1, {%3, %4}], [%2];"
       ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)),
         "r"(x), "r"(y)
+      : "memory");
+}
+
+// Untiled bulk copy global -> shared (no multicast), completion on an
+// mbarrier. Both addresses 16-byte aligned, size a multiple of 16.
+WB_DEV void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(smem_dst)), "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
 

@@ -13,13 +13,17 @@
 // The weights are the MMA's A operand (M = 128 lanes), the tokens its B
 // operand (N = BN in {16, 32, 64, 128}, chosen per segment so small groups
 // do not pay for padding). Roles inside one persistent CTA per SM:
+//   warp 14     weight producer: per 128-K raw stage, one TMA box of packed
+//               nibbles per matrix (128 rows x 64 bytes, 64-byte swizzle)
+//               plus bulk copies of the tile's scales (and zero points) from
+//               the prepared tile-transposed copy -- whole cache lines per
+//               request, nothing for the dequant warps to address.
 //   warps 0-7   dequantise: each thread owns one weight row of the tile,
-//               fetches its packed nibbles with cp.async into a private
-//               ring (6 stages ahead, across tile boundaries), converts them
-//               to fp16 ((n-8)*s + z, one rounding) and writes them straight
-//               into tensor memory with tcgen05.st -- the dequantised tile
-//               never touches shared memory, so the MMA's shared-memory
-//               bandwidth goes to the activation operand alone.
+//               reads its 32 bytes from the raw stage, converts them to fp16
+//               ((n-8)*s + z, one rounding) and writes them straight into
+//               tensor memory with tcgen05.st -- the dequantised tile never
+//               touches shared memory, so the MMA's shared-memory bandwidth
+//               goes to the activation operand alone.
 //   warp 12     TMA producer for the activation tiles (128-byte swizzle).
 //   warp 13     MMA issuer: tcgen05.mma kind::f16, A from TMEM, B from smem,
 //               fp32 accumulators in TMEM; completion via tcgen05.commit.
@@ -34,6 +38,7 @@
 // activation operands (Xp, H) are stored in the same interleaved order.
 #include <algorithm>
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "internal.h"
@@ -42,36 +47,65 @@ using namespace wb;
 
 namespace {
 
-constexpr int kThreads = 448;
+constexpr int kThreads = 480;  // 15 warps
 constexpr int kDqThreads = 256;
-constexpr int kEpiWarp0 = 8;
-constexpr int kTmaWarp = 12;
+constexpr int kTmaBWarp = 12;
 constexpr int kMmaWarp = 13;
+constexpr int kTmaWWarp = 14;
 constexpr int kAStages = 4;
-constexpr int kRaw = 6;  // cp.async ring depth per dequant thread
 constexpr int BM = 128;
 constexpr int kBNMax = 128;
 constexpr int kTmemCols = 512;
 constexpr int kAColBase = 256;
+constexpr int kRawK = 128;           // K per raw (weight) stage
+constexpr int kBoxBytes = BM * 64;   // one matrix's nibbles for a raw stage
+constexpr int kScBytes = 512;        // room for 2 scale groups x 128 rows (fp16)
 
 enum { GATEUP = 0, DOWN = 1 };
 
 template <int MODE>
 struct Shape {
-  static constexpr int KS = MODE == GATEUP ? 64 : 128;           // K per stage
-  static constexpr int kBoxes = KS / 64;                          // 64-K boxes per stage
-  static constexpr int kBStageBytes = kBoxes * kBNMax * 128;      // 16 / 32 KB
-  static constexpr int kBStages = MODE == GATEUP ? 8 : 4;
+  static constexpr int KA = MODE == GATEUP ? 64 : 128;            // K per A stage
+  static constexpr int kSub = kRawK / KA;                          // A stages per raw stage
+  static constexpr int kMats = MODE == GATEUP ? 2 : 1;
+  // raw stage: [boxes][scales][zeros], 1 KB multiple
+  static constexpr int kScOff = kMats * kBoxBytes;
+  static constexpr int kZOff = kScOff + kMats * kScBytes;
+  static constexpr int kRawStageBytes = ((kZOff + kMats * kScBytes) + 1023) / 1024 * 1024;
+  static constexpr int kRawStages = MODE == GATEUP ? 6 : 10;
+  static constexpr int kBoxes = KA / 64;                           // 64-K activation boxes per A stage
+  static constexpr int kBStageBytes = kBoxes * kBNMax * 128;
+  static constexpr int kBStages = MODE == GATEUP ? 4 : 3;
 };
+
+// Prepared weights: per matrix entry (expert v, matrix m in gate/up/down) a
+// TMA descriptor of its packed nibbles, a zero-point flag, and its scales and
+// zero points transposed to [row tile][group][128 rows] so that the scales
+// of one raw stage are one contiguous run.
+struct PreparedLayout {
+  size_t maps, flags, scales, zeros, mat_sc_bytes, total;
+};
+
+PreparedLayout prepared_layout(const WispMoeConfig* c, int n) {
+  PreparedLayout L;
+  const size_t entries = (size_t)n * 3;
+  L.mat_sc_bytes = (size_t)c->hidden * c->inter / c->group_size * 2;
+  L.maps = 0;
+  L.flags = entries * sizeof(CUtensorMap);
+  L.scales = (L.flags + entries * 4 + 255) & ~(size_t)255;
+  L.zeros = L.scales + entries * L.mat_sc_bytes;
+  L.total = L.zeros + entries * L.mat_sc_bytes;
+  return L;
+}
 
 struct GemmParams {
   CUtensorMap tmap[4];  // activation tensor, boxes {64, 16 << i}
-  const WispInt4Expert* experts;
+  const uint8_t* prepared;
+  size_t p_flags, p_scales, p_zeros, p_mat_sc_bytes;
   const WispSegment* segs;
   const int32_t* tiles;  // [0, S]: tile prefix; [S+1, 2S+1): bn per segment
   int nseg;
   int M, I, gs;
-  int mblocks;  // weight-row tiles per expert
   __half* h_out;
   const int* row_token;
   const float* row_weight;
@@ -81,6 +115,7 @@ struct GemmParams {
 };
 
 struct SmemLayout {
+  uint64_t rfull[16], rempty[16];
   uint64_t bfull[8], bempty[8];
   uint64_t afull[kAStages], aempty[kAStages];
   uint64_t accfull, accempty, final_bar;
@@ -122,21 +157,24 @@ template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_constant__ GemmParams p) {
   using S = Shape<MODE>;
   extern __shared__ uint8_t smem_raw[];
-  // 1024-byte alignment for the swizzled activation tiles.
   const uint32_t base_u32 = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (base_u32 & 1023)) & 1023);
-  uint8_t* b_ring = smem;                                            // kBStages * kBStageBytes
-  uint8_t* raw_ring = b_ring + S::kBStages * S::kBStageBytes;        // kRaw * 2 * 256 * 16
-  uint32_t* scale_ring = reinterpret_cast<uint32_t*>(raw_ring + kRaw * 2 * kDqThreads * 16);
-  uint32_t* zero_ring = scale_ring + kRaw * kDqThreads;
-  SmemLayout* L = reinterpret_cast<SmemLayout*>(zero_ring + kRaw * kDqThreads);
+  uint8_t* raw_ring = smem;                                          // kRawStages * kRawStageBytes
+  uint8_t* b_ring = raw_ring + S::kRawStages * S::kRawStageBytes;    // kBStages * kBStageBytes
+  SmemLayout* L = reinterpret_cast<SmemLayout*>(b_ring + S::kBStages * S::kBStageBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = __ldg(p.tiles + p.nseg);
-  const int nks = (MODE == GATEUP ? p.M : p.I) / S::KS;
+  const int K = MODE == GATEUP ? p.M : p.I;
+  const int nA = K / S::KA;           // A stages per tile
+  const int nR = K / kRawK;           // raw stages per tile
   volatile int* abort = &L->abort;
 
   if (threadIdx.x == 0) {
+    for (int i = 0; i < S::kRawStages; i++) {
+      mbar_init(&L->rfull[i], 1);
+      mbar_init(&L->rempty[i], kDqThreads / 32);
+    }
     for (int i = 0; i < S::kBStages; i++) {
       mbar_init(&L->bfull[i], 1);
       mbar_init(&L->bempty[i], 1);
@@ -159,70 +197,42 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = L->tmem_base;
+  const int32_t* flags = reinterpret_cast<const int32_t*>(p.prepared + p.p_flags);
 
   if (warp < 8) {
     // ------------------------------------------------------------------
-    // Dequantisation warps.
+    // Dequantisation warps: thread = weight row of the tile = TMEM lane.
     // ------------------------------------------------------------------
-    const int t = threadIdx.x;          // 0..255
-    const int wg = t >> 7;              // which half of the A stage
-    const int r = t & 127;              // weight row within the tile == TMEM lane
-    const int K = MODE == GATEUP ? p.M : p.I;
-    const int gpr = K / p.gs;           // scale groups per weight row
-    // Producer cursor (cp.async issue) runs kRaw-1 items ahead.
-    int ptile = blockIdx.x, pks = 0;
-    TileInfo pti;
-    if (ptile < ntiles) pti = decode_tile(p, ptile);
-    auto issue = [&](int slot) {
-      if (ptile < ntiles) {
-        const WispInt4Expert& ex = p.experts[pti.expert];
-        const WispInt4Mat& mt = MODE == GATEUP ? (wg == 0 ? ex.gate : ex.up) : ex.down;
-        const int row = pti.mblk * BM + r;
-        const int k0 = pks * S::KS + (MODE == GATEUP ? 0 : wg * 64);
-        const uint8_t* src = mt.packed + (size_t)row * (K / 2) + (k0 >> 1);
-        uint8_t* dst0 = raw_ring + ((slot * 2 + 0) * kDqThreads + t) * 16;
-        uint8_t* dst1 = raw_ring + ((slot * 2 + 1) * kDqThreads + t) * 16;
-        cp_async_16(dst0, src);
-        cp_async_16(dst1, src + 16);
-        const size_t gidx = (size_t)row * gpr + k0 / p.gs;
-        cp_async_4(scale_ring + slot * kDqThreads + t,
-                   reinterpret_cast<const uint8_t*>(mt.scales) + ((gidx & ~(size_t)1) * 2));
-        if (mt.zeros)
-          cp_async_4(zero_ring + slot * kDqThreads + t,
-                     reinterpret_cast<const uint8_t*>(mt.zeros) + ((gidx & ~(size_t)1) * 2));
-        if (++pks == nks) {
-          pks = 0;
-          ptile += gridDim.x;
-          if (ptile < ntiles) pti = decode_tile(p, ptile);
-        }
-      }
-      cp_async_commit();
-    };
-    for (int i = 0; i < kRaw - 1; i++) issue(i);
-    int slot = 0, sa = 0;
-    uint32_t aphase = 0;
+    const int t = threadIdx.x;
+    const int wg = t >> 7;
+    const int r = t & 127;
+    const int sw = (r >> 1) & 3;        // 64-byte swizzle of this row
+    const int mat = MODE == GATEUP ? wg : 2;
+    int rslot = 0, sa = 0;
+    uint32_t rphase = 0, aphase = 0;
     int item = 0;
-    for (int tile = blockIdx.x; tile < ntiles && !*abort; tile += gridDim.x) {
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < ntiles && ok && !*abort; tile += gridDim.x) {
       const TileInfo ti = decode_tile(p, tile);
-      const WispInt4Expert& ex = p.experts[ti.expert];
-      const WispInt4Mat& mt = MODE == GATEUP ? (wg == 0 ? ex.gate : ex.up) : ex.down;
-      const bool has_zero = mt.zeros != nullptr;
-      const int row = ti.mblk * BM + r;
-      for (int ks = 0; ks < nks; ks++, item++) {
-        issue((slot + kRaw - 1) % kRaw);
-        cp_async_wait<kRaw - 1>();
-        const uint4 q0 = *reinterpret_cast<const uint4*>(raw_ring + ((slot * 2 + 0) * kDqThreads + t) * 16);
-        const uint4 q1 = *reinterpret_cast<const uint4*>(raw_ring + ((slot * 2 + 1) * kDqThreads + t) * 16);
-        const int k0 = ks * S::KS + (MODE == GATEUP ? 0 : wg * 64);
-        const size_t gidx = (size_t)row * gpr + k0 / p.gs;
-        const uint32_t sw = scale_ring[slot * kDqThreads + t];
-        const __half s = __ushort_as_half((unsigned short)((gidx & 1) ? (sw >> 16) : (sw & 0xffff)));
-        __half z = __float2half(0.f);
-        if (has_zero) {
-          const uint32_t zw = zero_ring[slot * kDqThreads + t];
-          z = __ushort_as_half((unsigned short)((gidx & 1) ? (zw >> 16) : (zw & 0xffff)));
+      const bool has_zero = __ldg(flags + ti.expert * 3 + mat) & 1;
+      for (int ks = 0; ks < nA; ks++, item++) {
+        const int sub = ks % S::kSub;
+        if (sub == 0 && !mbar_wait(&L->rfull[rslot], rphase, abort)) { ok = false; break; }
+        const uint8_t* rs = raw_ring + rslot * S::kRawStageBytes;
+        const uint8_t* box = rs + (MODE == GATEUP ? wg * kBoxBytes : 0);
+        const int c0 = MODE == GATEUP ? 2 * sub : 2 * wg;   // 16-byte chunk within the row
+        const uint4 q0 = *reinterpret_cast<const uint4*>(box + r * 64 + ((c0 ^ sw) << 4));
+        const uint4 q1 = *reinterpret_cast<const uint4*>(box + r * 64 + (((c0 + 1) ^ sw) << 4));
+        const int gl = (MODE == GATEUP ? 64 * sub : 64 * wg) / p.gs;
+        const int so = (MODE == GATEUP ? wg * kScBytes : 0) + (gl * BM + r) * 2;
+        const __half s = *reinterpret_cast<const __half*>(rs + S::kScOff + so);
+        const __half z = has_zero ? *reinterpret_cast<const __half*>(rs + S::kZOff + so)
+                                  : __float2half(0.f);
+        if (sub == S::kSub - 1) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&L->rempty[rslot]);
+          if (++rslot == S::kRawStages) { rslot = 0; rphase ^= 1; }
         }
-        slot = (slot + 1) % kRaw;
         const __half2 s2 = __halves2half2(s, s), z2 = __halves2half2(z, z);
         uint32_t v[32];
         const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
@@ -235,9 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
           v[4 * w + 2] = o[2];
           v[4 * w + 3] = o[3];
         }
-        if (item >= kAStages) {
-          if (!mbar_wait(&L->aempty[sa], aphase ^ 1, abort)) break;
-        }
+        if (item >= kAStages && !mbar_wait(&L->aempty[sa], aphase ^ 1, abort)) { ok = false; break; }
         tc_fence_after();
         const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16) +
                                (uint32_t)(kAColBase + sa * 64 + wg * 32);
@@ -246,16 +254,62 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&L->afull[sa]);
-        if (++sa == kAStages) {
-          sa = 0;
-          aphase ^= 1;
-        }
+        if (++sa == kAStages) { sa = 0; aphase ^= 1; }
       }
     }
-    cp_async_wait_all();
-  } else if (warp == kTmaWarp) {
+  } else if (warp == kTmaWWarp) {
     // ------------------------------------------------------------------
-    // TMA producer for the activation tiles.
+    // Weight producer: nibble boxes + scale / zero runs per raw stage.
+    // ------------------------------------------------------------------
+    if (lane == 0) {
+      const int ng = kRawK / p.gs;        // scale groups per raw stage (1 or 2)
+      const int gpr = K / p.gs;           // groups per weight row
+      int rslot = 0, item = 0;
+      uint32_t rphase = 0;
+      int last_phase[16];
+      for (int i = 0; i < 16; i++) last_phase[i] = -1;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok && !*abort; tile += gridDim.x) {
+        const TileInfo ti = decode_tile(p, tile);
+        const int m0 = MODE == GATEUP ? 0 : 2;
+        uint32_t bytes = 0;
+        bool hz[2];
+        const CUtensorMap* map[2];
+        const uint8_t* sc[2];
+        const uint8_t* zr[2];
+#pragma unroll
+        for (int j = 0; j < S::kMats; j++) {
+          const int e = ti.expert * 3 + m0 + j;
+          hz[j] = __ldg(flags + e) & 1;
+          map[j] = reinterpret_cast<const CUtensorMap*>(p.prepared + (size_t)e * sizeof(CUtensorMap));
+          sc[j] = p.prepared + p.p_scales + (size_t)e * p.p_mat_sc_bytes +
+                  (size_t)ti.mblk * gpr * BM * 2;
+          zr[j] = p.prepared + p.p_zeros + (size_t)e * p.p_mat_sc_bytes +
+                  (size_t)ti.mblk * gpr * BM * 2;
+          bytes += kBoxBytes + ng * BM * 2 * (hz[j] ? 2 : 1);
+        }
+        for (int rs = 0; rs < nR; rs++, item++) {
+          if (item >= S::kRawStages && !mbar_wait(&L->rempty[rslot], rphase ^ 1, abort)) { ok = false; break; }
+          uint8_t* dst = raw_ring + rslot * S::kRawStageBytes;
+          mbar_arrive_expect_tx(&L->rfull[rslot], bytes);
+#pragma unroll
+          for (int j = 0; j < S::kMats; j++) {
+            tma_load_2d(dst + j * kBoxBytes, map[j], &L->rfull[rslot], rs * 64, ti.mblk * BM);
+            const size_t goff = (size_t)(rs * kRawK / p.gs) * BM * 2;
+            bulk_load(dst + S::kScOff + j * kScBytes, sc[j] + goff, ng * BM * 2, &L->rfull[rslot]);
+            if (hz[j]) bulk_load(dst + S::kZOff + j * kScBytes, zr[j] + goff, ng * BM * 2, &L->rfull[rslot]);
+          }
+          last_phase[rslot] = (int)rphase;
+          if (++rslot == S::kRawStages) { rslot = 0; rphase ^= 1; }
+        }
+      }
+      // Let every issued copy land before the CTA can exit.
+      for (int i = 0; i < S::kRawStages; i++)
+        if (last_phase[i] >= 0) mbar_wait(&L->rfull[i], (uint32_t)last_phase[i], abort, 200000000LL);
+    }
+  } else if (warp == kTmaBWarp) {
+    // ------------------------------------------------------------------
+    // Activation producer.
     // ------------------------------------------------------------------
     if (lane == 0) {
       for (int i = 0; i < 4; i++) tma_prefetch_desc(&p.tmap[i]);
@@ -264,30 +318,22 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       int item = 0;
       int last_phase[8];
       for (int i = 0; i < 8; i++) last_phase[i] = -1;
-      for (int tile = blockIdx.x; tile < ntiles && !*abort; tile += gridDim.x) {
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok && !*abort; tile += gridDim.x) {
         const TileInfo ti = decode_tile(p, tile);
         const CUtensorMap* tm = &p.tmap[bn_slot(ti.bn)];
         const uint32_t bytes = (uint32_t)(ti.bn * 128 * S::kBoxes);
-        bool ok = true;
-        for (int ks = 0; ks < nks; ks++, item++) {
-          if (item >= S::kBStages) {
-            if (!mbar_wait(&L->bempty[sb], bphase ^ 1, abort)) { ok = false; break; }
-          }
+        for (int ks = 0; ks < nA; ks++, item++) {
+          if (item >= S::kBStages && !mbar_wait(&L->bempty[sb], bphase ^ 1, abort)) { ok = false; break; }
           mbar_arrive_expect_tx(&L->bfull[sb], bytes);
           uint8_t* dst = b_ring + sb * S::kBStageBytes;
 #pragma unroll
           for (int bx = 0; bx < S::kBoxes; bx++)
-            tma_load_2d(dst + bx * (kBNMax * 128), tm, &L->bfull[sb], ks * S::KS + bx * 64, ti.row0);
+            tma_load_2d(dst + bx * (kBNMax * 128), tm, &L->bfull[sb], ks * S::KA + bx * 64, ti.row0);
           last_phase[sb] = (int)bphase;
-          if (++sb == S::kBStages) {
-            sb = 0;
-            bphase ^= 1;
-          }
+          if (++sb == S::kBStages) { sb = 0; bphase ^= 1; }
         }
-        if (!ok) break;
       }
-      // Every issued load completes on its own; wait for the last one of
-      // each stage so no copy is still landing when the CTA exits.
       for (int i = 0; i < S::kBStages; i++)
         if (last_phase[i] >= 0) mbar_wait(&L->bfull[i], (uint32_t)last_phase[i], abort, 200000000LL);
     }
@@ -299,15 +345,13 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       int sa = 0, sb = 0;
       uint32_t aphase = 0, bphase = 0, accphase = 0;
       int ntile_local = 0;
-      for (int tile = blockIdx.x; tile < ntiles && !*abort; tile += gridDim.x, ntile_local++) {
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok && !*abort; tile += gridDim.x, ntile_local++) {
         const TileInfo ti = decode_tile(p, tile);
         const uint32_t idesc = idesc_f16_m128(ti.bn);
-        if (ntile_local > 0) {
-          if (!mbar_wait(&L->accempty, accphase ^ 1, abort)) break;
-        }
+        if (ntile_local > 0 && !mbar_wait(&L->accempty, accphase ^ 1, abort)) break;
         tc_fence_after();
-        bool ok = true;
-        for (int ks = 0; ks < nks; ks++) {
+        for (int ks = 0; ks < nA; ks++) {
           if (!mbar_wait(&L->afull[sa], aphase, abort) || !mbar_wait(&L->bfull[sb], bphase, abort)) {
             ok = false;
             break;
@@ -427,7 +471,6 @@ __global__ void plan_tiles_kernel(const WispSegment* __restrict__ segs, int nseg
       n = rows > 0 ? ((rows + bn - 1) / bn) * mblocks : 0;
       tiles[nseg + 1 + s] = bn;
     }
-    // block inclusive scan of n
     int v = n;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
 #pragma unroll
@@ -456,6 +499,33 @@ __global__ void plan_tiles_kernel(const WispSegment* __restrict__ segs, int nseg
   if (threadIdx.x == 0) tiles[nseg] = carry;
 }
 
+// Scales (and zero points) of every prepared matrix, transposed from
+// [rows][groups] to [row tile][group][128 rows].
+__global__ void transpose_scales_kernel(const WispInt4Expert* __restrict__ experts, int n, int M,
+                                        int I, int gs, uint8_t* __restrict__ prepared,
+                                        size_t off_scales, size_t off_zeros, size_t mat_bytes) {
+  const int e = blockIdx.y;  // matrix entry v*3 + m
+  const int v = e / 3, m = e % 3;
+  const WispInt4Expert ex = experts[v];
+  const WispInt4Mat mt = m == 0 ? ex.gate : m == 1 ? ex.up : ex.down;
+  const int rows = m == 2 ? M : I;
+  const int gpr = (m == 2 ? I : M) / gs;
+  const size_t total = (size_t)rows * gpr;
+  const uint16_t* s = reinterpret_cast<const uint16_t*>(mt.scales);
+  const uint16_t* z = reinterpret_cast<const uint16_t*>(mt.zeros);
+  uint16_t* so = reinterpret_cast<uint16_t*>(prepared + off_scales + (size_t)e * mat_bytes);
+  uint16_t* zo = reinterpret_cast<uint16_t*>(prepared + off_zeros + (size_t)e * mat_bytes);
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    // destination index i = (tile * gpr + g) * 128 + r
+    const size_t r = i % BM, rest = i / BM;
+    const size_t g = rest % gpr, tile = rest / gpr;
+    const size_t src = (tile * BM + r) * gpr + g;
+    so[i] = s[src];
+    if (z) zo[i] = z[src];
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Host side.
 // ---------------------------------------------------------------------------
@@ -478,6 +548,8 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
+// fp16 activation rows [rows x cols]: boxes of 64 columns x box_rows rows,
+// 128-byte swizzle (the canonical K-major layout of the MMA's B operand).
 bool encode_rows_map(CUtensorMap* m, const void* base, int rows, int cols, int box_rows) {
   EncodeTiledFn fn = get_encode_fn();
   if (!fn) return false;
@@ -491,11 +563,26 @@ bool encode_rows_map(CUtensorMap* m, const void* base, int rows, int cols, int b
          CUDA_SUCCESS;
 }
 
+// Packed nibbles of one matrix [rows x cols/2 bytes]: boxes of 64 bytes x
+// 128 rows with the 64-byte swizzle (conflict-free 16-byte reads per row).
+bool encode_packed_map(CUtensorMap* m, const void* base, int rows, int cols) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols / 2, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols / 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)BM};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
 template <int MODE>
 size_t smem_bytes() {
   using S = Shape<MODE>;
-  return 1024 + (size_t)S::kBStages * S::kBStageBytes + (size_t)kRaw * 2 * kDqThreads * 16 +
-         (size_t)kRaw * kDqThreads * 4 * 2 + sizeof(SmemLayout);
+  return 1024 + (size_t)S::kRawStages * S::kRawStageBytes + (size_t)S::kBStages * S::kBStageBytes +
+         sizeof(SmemLayout);
 }
 
 int num_sms() {
@@ -507,45 +594,112 @@ int num_sms() {
   return sms[dev] > 0 ? sms[dev] : 148;
 }
 
-}  // namespace
-
-// Two tables (gate/up and down), each [prefix S+1 | bn S].
-extern "C" size_t wisp_b200_tiles_words(int n_segs) { return (size_t)(2 * (2 * n_segs + 1)); }
-
-extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const WispInt4Expert* d_experts,
-                                           const WispSegment* d_segs, int n_segs, int rows_capacity,
-                                           const uint16_t* d_xp, uint16_t* d_h, int mode,
-                                           const int* d_row_token, const float* d_row_weight,
-                                           float* d_out, int32_t* d_tiles, int* d_error_flag,
-                                           cudaStream_t stream, WispErrCtx* err) {
-  if (!cfg || !d_experts || !d_segs || !d_xp || !d_h || !d_out || !d_tiles)
-    return WB_FAIL(WISP_ERR_INVALID_ARG, "grouped_ffn: null pointer argument");
+WispError check_shapes(const WispMoeConfig* cfg, WispErrCtx* err) {
   const int M = cfg->hidden, I = cfg->inter, gs = cfg->group_size;
   if (M <= 0 || I <= 0 || M % 128 || I % 128)
     return WB_FAIL(WISP_ERR_INVALID_ARG, "grouped_ffn: hidden (%d) and inter (%d) must be multiples of 128", M, I);
   if (gs != 64 && gs != 128)
     return WB_FAIL(WISP_ERR_INVALID_ARG, "grouped_ffn: group_size must be 64 or 128 (got %d)", gs);
+  return WISP_OK;
+}
+
+}  // namespace
+
+extern "C" size_t wisp_b200_prepared_bytes(const WispMoeConfig* cfg, int n_entries) {
+  if (!cfg || n_entries <= 0 || check_shapes(cfg, nullptr) != WISP_OK) return 0;
+  return prepared_layout(cfg, n_entries).total;
+}
+
+extern "C" WispError wisp_b200_prepare_experts(const WispMoeConfig* cfg,
+                                               const WispInt4Expert* d_experts, int n_entries,
+                                               void* d_prepared, size_t prepared_bytes,
+                                               cudaStream_t stream, WispErrCtx* err) {
+  if (!cfg || !d_experts || !d_prepared || n_entries <= 0)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "prepare_experts: bad arguments");
+  WispError e = check_shapes(cfg, err);
+  if (e != WISP_OK) return e;
+  const PreparedLayout PL = prepared_layout(cfg, n_entries);
+  if (prepared_bytes < PL.total)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "prepare_experts: buffer %zu < required %zu", prepared_bytes, PL.total);
+  if ((uintptr_t)d_prepared & 255)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "prepare_experts: buffer must be 256-byte aligned");
+  const int M = cfg->hidden, I = cfg->inter;
+  std::vector<WispInt4Expert> h(n_entries);
+  WB_CUDA_CHECK(cudaMemcpyAsync(h.data(), d_experts, sizeof(WispInt4Expert) * n_entries,
+                                cudaMemcpyDeviceToHost, stream));
+  WB_CUDA_CHECK(cudaStreamSynchronize(stream));
+  std::vector<CUtensorMap> maps((size_t)n_entries * 3);
+  std::vector<int32_t> flags((size_t)n_entries * 3);
+  for (int v = 0; v < n_entries; v++) {
+    const WispInt4Mat* mats[3] = {&h[v].gate, &h[v].up, &h[v].down};
+    for (int m = 0; m < 3; m++) {
+      const int rows = m == 2 ? M : I, cols = m == 2 ? I : M;
+      const WispInt4Mat& mt = *mats[m];
+      if (!mt.packed || !mt.scales)
+        return WB_FAIL(WISP_ERR_INVALID_ARG, "prepare_experts: entry %d matrix %d has no data", v, m);
+      if (((uintptr_t)mt.packed & 15) || ((uintptr_t)mt.scales & 1) || ((uintptr_t)mt.zeros & 1))
+        return WB_FAIL(WISP_ERR_INVALID_ARG,
+                       "prepare_experts: entry %d matrix %d: packed must be 16-byte aligned", v, m);
+      if (!encode_packed_map(&maps[(size_t)v * 3 + m], mt.packed, rows, cols))
+        return WB_FAIL(WISP_ERR_CUDA, "prepare_experts: cuTensorMapEncodeTiled failed (entry %d)", v);
+      flags[(size_t)v * 3 + m] = mt.zeros ? 1 : 0;
+    }
+  }
+  uint8_t* base = static_cast<uint8_t*>(d_prepared);
+  WB_CUDA_CHECK(cudaMemcpyAsync(base + PL.maps, maps.data(), maps.size() * sizeof(CUtensorMap),
+                                cudaMemcpyHostToDevice, stream));
+  WB_CUDA_CHECK(cudaMemcpyAsync(base + PL.flags, flags.data(), flags.size() * 4,
+                                cudaMemcpyHostToDevice, stream));
+  dim3 grid(64, n_entries * 3);
+  transpose_scales_kernel<<<grid, 256, 0, stream>>>(d_experts, n_entries, M, I, cfg->group_size,
+                                                    base, PL.scales, PL.zeros, PL.mat_sc_bytes);
+  WB_CUDA_CHECK(cudaGetLastError());
+  // The host vectors are read by the copies above before they are freed.
+  WB_CUDA_CHECK(cudaStreamSynchronize(stream));
+  return WISP_OK;
+}
+
+// Two tables (gate/up and down), each [prefix S+1 | bn S].
+extern "C" size_t wisp_b200_tiles_words(int n_segs) { return (size_t)(2 * (2 * n_segs + 1)); }
+
+extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void* d_prepared,
+                                           int n_entries, const WispSegment* d_segs, int n_segs,
+                                           int rows_capacity, const uint16_t* d_xp, uint16_t* d_h,
+                                           int mode, const int* d_row_token,
+                                           const float* d_row_weight, float* d_out,
+                                           int32_t* d_tiles, int* d_error_flag,
+                                           cudaStream_t stream, WispErrCtx* err) {
+  if (!cfg || !d_prepared || !d_segs || !d_xp || !d_h || !d_out || !d_tiles || n_entries <= 0)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "grouped_ffn: null pointer argument");
+  WispError e = check_shapes(cfg, err);
+  if (e != WISP_OK) return e;
+  const int M = cfg->hidden, I = cfg->inter, gs = cfg->group_size;
   if (n_segs <= 0 || rows_capacity <= 0)
     return WB_FAIL(WISP_ERR_INVALID_ARG, "grouped_ffn: n_segs=%d rows=%d", n_segs, rows_capacity);
   if (mode == 0 && (!d_row_token || !d_row_weight))
     return WB_FAIL(WISP_ERR_INVALID_ARG, "grouped_ffn: mode 0 needs row_token and row_weight");
   if (((uintptr_t)d_xp | (uintptr_t)d_h) & 15)
     return WB_FAIL(WISP_ERR_INVALID_ARG, "grouped_ffn: activation buffers must be 16-byte aligned");
+  if ((uintptr_t)d_prepared & 255)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "grouped_ffn: prepared weights must be 256-byte aligned");
 
+  const PreparedLayout PL = prepared_layout(cfg, n_entries);
   GemmParams gu, dn;
   memset(&gu, 0, sizeof gu);
   for (int i = 0; i < 4; i++) {
     if (!encode_rows_map(&gu.tmap[i], d_xp, rows_capacity, M, 16 << i))
       return WB_FAIL(WISP_ERR_CUDA, "grouped_ffn: cuTensorMapEncodeTiled failed (activations)");
   }
-  gu.experts = d_experts;
+  gu.prepared = static_cast<const uint8_t*>(d_prepared);
+  gu.p_flags = PL.flags;
+  gu.p_scales = PL.scales;
+  gu.p_zeros = PL.zeros;
+  gu.p_mat_sc_bytes = PL.mat_sc_bytes;
   gu.segs = d_segs;
-  gu.tiles = d_tiles;
   gu.nseg = n_segs;
   gu.M = M;
   gu.I = I;
   gu.gs = gs;
-  gu.mblocks = I / BM;
   gu.h_out = reinterpret_cast<__half*>(d_h);
   gu.error_flag = d_error_flag;
   dn = gu;
@@ -553,21 +707,16 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const WispI
     if (!encode_rows_map(&dn.tmap[i], d_h, rows_capacity, I, 16 << i))
       return WB_FAIL(WISP_ERR_CUDA, "grouped_ffn: cuTensorMapEncodeTiled failed (H)");
   }
-  dn.mblocks = M / BM;
   dn.row_token = d_row_token;
   dn.row_weight = d_row_weight;
   dn.out = d_out;
   dn.mode = mode;
 
-  // Both launches share the per-segment BN choice; only the tile prefix
-  // differs (mblocks), so each gets its own tile table.
   const size_t tw = (size_t)(2 * n_segs + 1);
-  int32_t* tiles_gu = d_tiles;
-  int32_t* tiles_dn = d_tiles + tw;
-  gu.tiles = tiles_gu;
-  dn.tiles = tiles_dn;
-  plan_tiles_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, I / BM, tiles_gu);
-  plan_tiles_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, M / BM, tiles_dn);
+  gu.tiles = d_tiles;
+  dn.tiles = d_tiles + tw;
+  plan_tiles_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, I / BM, d_tiles);
+  plan_tiles_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, M / BM, d_tiles + tw);
 
   const int grid = num_sms();
   const size_t sm_gu = smem_bytes<GATEUP>(), sm_dn = smem_bytes<DOWN>();

@@ -127,8 +127,8 @@ extern "C" WispError wisp_b200_moe_forward(const WispMoeConfig* cfg, const WispM
                                            WispErrCtx* err) {
   WispError e = validate(cfg, err);
   if (e != WISP_OK) return e;
-  if (!w || !w->router_w || !w->experts || !d_x || !d_out || !d_workspace)
-    return WB_FAIL(WISP_ERR_INVALID_ARG, "moe_forward: null pointer argument");
+  if (!w || !w->router_w || !w->prepared || !d_x || !d_out || !d_workspace)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "moe_forward: null pointer argument (router_w, prepared, x, out, workspace)");
   if (((uintptr_t)d_x | (uintptr_t)w->router_w | (uintptr_t)d_workspace) & 15)
     return WB_FAIL(WISP_ERR_INVALID_ARG, "moe_forward: x, router_w and workspace must be 16-byte aligned");
   Workspace ws = carve(cfg, d_workspace);
@@ -147,7 +147,7 @@ extern "C" WispError wisp_b200_moe_forward(const WispMoeConfig* cfg, const WispM
   if (e != WISP_OK) return e;
   WB_CUDA_CHECK(cudaMemsetAsync(d_out, 0, (size_t)cfg->tokens * cfg->hidden * sizeof(float), stream));
   WB_CUDA_CHECK(cudaMemsetAsync(ws.error_flag, 0, sizeof(int), stream));
-  return wisp_b200_grouped_ffn(cfg, w->experts, ws.segs, V, ws.rows, ws.xp, ws.h, 0, ws.row_token,
+  return wisp_b200_grouped_ffn(cfg, w->prepared, V, ws.segs, V, ws.rows, ws.xp, ws.h, 0, ws.row_token,
                                ws.row_weight, d_out, ws.tiles, ws.error_flag, stream, err);
 }
 

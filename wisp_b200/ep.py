@@ -89,9 +89,10 @@ class CudaOps:
         abi.call("wisp_b200_pack_rows", x.data_ptr(), None if src is None else src.data_ptr(),
                  n_rows, x.shape[1], xp.data_ptr(), _stream())
 
-    def grouped(self, cfg, table, segs, rows, xp, h, mode, row_token, row_weight, out, tiles, flag):
+    def grouped(self, cfg, lw, segs, rows, xp, h, mode, row_token, row_weight, out, tiles, flag):
         dsegs = _segments_tensor(segs, xp.device)
-        abi.call("wisp_b200_grouped_ffn", C.byref(cfg), table.data_ptr(), dsegs.data_ptr(), len(segs),
+        abi.call("wisp_b200_grouped_ffn", C.byref(cfg), lw.prepare().data_ptr(), lw.n_entries,
+                 dsegs.data_ptr(), len(segs),
                  max(rows, 1), xp.data_ptr(), h.data_ptr(), mode,
                  None if row_token is None else row_token.data_ptr(),
                  None if row_weight is None else row_weight.data_ptr(), out.data_ptr(),
@@ -175,7 +176,7 @@ class EpLayer:
                                input_split_sizes=send, group=self.group)
         # 3. local experts over the received rows (unweighted fp32 rows)
         if R > 0:
-            ops.grouped(self.cfg_loc, self.lw.table, segs, R, self.xr, self.hr, 1, None, None,
+            ops.grouped(self.cfg_loc, self.lw, segs, R, self.xr, self.hr, 1, None, None,
                         self.yr, self.tiles, self.flag)
         # 4. return rows to their tokens' ranks
         dist.all_to_all_single(self.yret, self.yr[:R], output_split_sizes=send,
@@ -184,7 +185,7 @@ class EpLayer:
         out.zero_()
         if spec.has_shared:
             ops.pack(x, None, T, self.xs)
-            ops.grouped(self.cfg_loc, self.lw.table, [(self.e_loc, 0, T)], T, self.xs, self.hr, 0,
+            ops.grouped(self.cfg_loc, self.lw, [(self.e_loc, 0, T)], T, self.xs, self.hr, 0,
                         self.sh_token, self.sh_weight, out, self.tiles, self.flag)
         ops.combine(self.yret, self.row_token, self.row_weight, T * k, out)
         return out

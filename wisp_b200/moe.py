@@ -26,6 +26,7 @@ class MoeLayer:
         self.w = weights
         self.spec: MoeSpec = weights.spec
         self.cfg = self.spec.cfg(tokens)
+        weights.prepare()
         self._wstruct = weights.weights_struct()
         nbytes = abi.lib().wisp_b200_moe_workspace_bytes(C.byref(self.cfg))
         if nbytes == 0:

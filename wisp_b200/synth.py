@@ -106,7 +106,8 @@ class LayerWeights:
     gate: Int4Arena
     up: Int4Arena
     down: Int4Arena
-    table: torch.Tensor = field(default=None)  # uint8 device copy of WispInt4Expert[V]
+    table: torch.Tensor = field(default=None)     # uint8 device copy of WispInt4Expert[V]
+    prepared: torch.Tensor = field(default=None)  # from wisp_b200_prepare_experts
 
     def build_table(self) -> None:
         V = self.gate.packed.shape[0]
@@ -118,11 +119,29 @@ class LayerWeights:
         raw = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8)
         self.table = raw.to(self.gate.packed.device)
 
+    @property
+    def n_entries(self) -> int:
+        return self.gate.packed.shape[0]
+
+    def prepare(self) -> torch.Tensor:
+        """Run wisp_b200_prepare_experts once (device weights only)."""
+        if self.prepared is None:
+            cfg = self.spec.cfg()
+            n = self.n_entries
+            nbytes = abi.lib().wisp_b200_prepared_bytes(C.byref(cfg), n)
+            if nbytes == 0:
+                raise RuntimeError("wisp engine error [4]: shapes not supported by the tensor-core path")
+            self.prepared = torch.empty(nbytes, dtype=torch.uint8, device=self.table.device)
+            abi.call("wisp_b200_prepare_experts", C.byref(cfg), self.table.data_ptr(), n,
+                     self.prepared.data_ptr(), nbytes, torch.cuda.current_stream().cuda_stream)
+        return self.prepared
+
     def weights_struct(self) -> abi.WispMoeWeights:
         w = abi.WispMoeWeights()
         w.router_w = self.router_w.data_ptr()
         w.router_bias = self.router_bias.data_ptr() if self.router_bias is not None else None
         w.experts = self.table.data_ptr()
+        w.prepared = self.prepared.data_ptr() if self.prepared is not None else None
         return w
 
     def expert_host(self, v: int):
