@@ -13,21 +13,22 @@
 // The weights are the MMA's A operand (M = 128 lanes), the tokens its B
 // operand (N = BN in {16, 32, 64, 128}, chosen per segment so small groups
 // do not pay for padding). Roles inside one persistent CTA per SM:
-//   warp 14     weight producer: per 128-K raw stage, one TMA box of packed
+//   warp 22     weight producer: per 128-K raw stage, one TMA box of packed
 //               nibbles per matrix (128 rows x 64 bytes, 64-byte swizzle)
 //               plus bulk copies of the tile's scales (and zero points) from
 //               the prepared tile-transposed copy -- whole cache lines per
 //               request, nothing for the dequant warps to address.
-//   warps 0-7   dequantise: each thread owns one weight row of the tile,
-//               reads its 32 bytes from the raw stage, converts them to fp16
-//               ((n-8)*s + z, one rounding) and writes them straight into
-//               tensor memory with tcgen05.st -- the dequantised tile never
-//               touches shared memory, so the MMA's shared-memory bandwidth
-//               goes to the activation operand alone.
-//   warp 12     TMA producer for the activation tiles (128-byte swizzle).
-//   warp 13     MMA issuer: tcgen05.mma kind::f16, A from TMEM, B from smem,
+//   warps 0-15  dequantise (four warpgroups, each covering all 128 rows =
+//               TMEM lanes): each thread reads 16 bytes of its row from the
+//               raw stage, converts them to fp16 ((n-8)*s + z, one rounding)
+//               and writes them straight into tensor memory with tcgen05.st
+//               -- the dequantised tile never touches shared memory, so the
+//               MMA's shared-memory bandwidth goes to the activation operand
+//               alone. The store of stage i drains while stage i+1 converts.
+//   warp 20     TMA producer for the activation tiles (128-byte swizzle).
+//   warp 21     MMA issuer: tcgen05.mma kind::f16, A from TMEM, B from smem,
 //               fp32 accumulators in TMEM; completion via tcgen05.commit.
-//   warps 8-11  epilogue: tcgen05.ld of the accumulators, SwiGLU (GATEUP) or
+//   warps 16-19 epilogue: tcgen05.ld of the accumulators, SwiGLU (GATEUP) or
 //               the weighted scatter-combine (DOWN).
 // TMEM columns: [0,128) gate / single accumulator, [128,256) up accumulator,
 // [256,512) four 64-column A stages. Every wait is bounded; a wait that gives
@@ -47,11 +48,13 @@ using namespace wb;
 
 namespace {
 
-constexpr int kThreads = 480;  // 15 warps
-constexpr int kDqThreads = 256;
-constexpr int kTmaBWarp = 12;
-constexpr int kMmaWarp = 13;
-constexpr int kTmaWWarp = 14;
+constexpr int kDqWarps = 16;            // four warpgroups
+constexpr int kDqThreads = kDqWarps * 32;
+constexpr int kEpiWarp0 = kDqWarps;     // four epilogue warps
+constexpr int kTmaBWarp = kDqWarps + 4;
+constexpr int kMmaWarp = kDqWarps + 5;
+constexpr int kTmaWWarp = kDqWarps + 6;
+constexpr int kThreads = (kDqWarps + 7) * 32;
 constexpr int kAStages = 4;
 constexpr int BM = 128;
 constexpr int kBNMax = 128;
@@ -184,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       mbar_init(&L->aempty[i], 1);
     }
     mbar_init(&L->accfull, 1);
-    mbar_init(&L->accempty, 4);
+    mbar_init(&L->accempty, 4);  // the four epilogue warps
     mbar_init(&L->final_bar, 1);
     L->abort = 0;
     fence_barrier_init();
@@ -199,16 +202,20 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
   const uint32_t tmem = L->tmem_base;
   const int32_t* flags = reinterpret_cast<const int32_t*>(p.prepared + p.p_flags);
 
-  if (warp < 8) {
+  if (warp < kDqWarps) {
     // ------------------------------------------------------------------
     // Dequantisation warps: thread = weight row of the tile = TMEM lane.
+    // Warpgroup q converts one 32-K quarter of each A stage:
+    //   GATEUP: q = 2*matrix + half (gate K 0-31, gate 32-63, up 0-31, up 32-63)
+    //   DOWN:   q = K quarter of the 128-K stage.
     // ------------------------------------------------------------------
     const int t = threadIdx.x;
-    const int wg = t >> 7;
+    const int q = t >> 7;
     const int r = t & 127;
     const int sw = (r >> 1) & 3;        // 64-byte swizzle of this row
-    const int mat = MODE == GATEUP ? wg : 2;
-    int rslot = 0, sa = 0;
+    const int mat = MODE == GATEUP ? (q >> 1) : 2;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    int rslot = 0, sa = 0, prev_sa = -1;
     uint32_t rphase = 0, aphase = 0;
     int item = 0;
     bool ok = true;
@@ -219,12 +226,12 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
         const int sub = ks % S::kSub;
         if (sub == 0 && !mbar_wait(&L->rfull[rslot], rphase, abort)) { ok = false; break; }
         const uint8_t* rs = raw_ring + rslot * S::kRawStageBytes;
-        const uint8_t* box = rs + (MODE == GATEUP ? wg * kBoxBytes : 0);
-        const int c0 = MODE == GATEUP ? 2 * sub : 2 * wg;   // 16-byte chunk within the row
-        const uint4 q0 = *reinterpret_cast<const uint4*>(box + r * 64 + ((c0 ^ sw) << 4));
-        const uint4 q1 = *reinterpret_cast<const uint4*>(box + r * 64 + (((c0 + 1) ^ sw) << 4));
-        const int gl = (MODE == GATEUP ? 64 * sub : 64 * wg) / p.gs;
-        const int so = (MODE == GATEUP ? wg * kScBytes : 0) + (gl * BM + r) * 2;
+        const uint8_t* box = rs + (MODE == GATEUP ? mat * kBoxBytes : 0);
+        // 16-byte chunk of the 64-byte row this thread converts
+        const int c = MODE == GATEUP ? 2 * sub + (q & 1) : q;
+        const uint4 qv = *reinterpret_cast<const uint4*>(box + r * 64 + ((c ^ sw) << 4));
+        const int gl = (c * 32) / p.gs;
+        const int so = (MODE == GATEUP ? mat * kScBytes : 0) + (gl * BM + r) * 2;
         const __half s = *reinterpret_cast<const __half*>(rs + S::kScOff + so);
         const __half z = has_zero ? *reinterpret_cast<const __half*>(rs + S::kZOff + so)
                                   : __float2half(0.f);
@@ -234,10 +241,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
           if (++rslot == S::kRawStages) { rslot = 0; rphase ^= 1; }
         }
         const __half2 s2 = __halves2half2(s, s), z2 = __halves2half2(z, z);
-        uint32_t v[32];
-        const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        uint32_t v[16];
+        const uint32_t words[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
-        for (int w = 0; w < 8; w++) {
+        for (int w = 0; w < 4; w++) {
           uint32_t o[4];
           nib8_dequant(words[w], s2, z2, o);
           v[4 * w + 0] = o[0];
@@ -245,17 +252,27 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
           v[4 * w + 2] = o[2];
           v[4 * w + 3] = o[3];
         }
+        // Publish the previous stage now that its store had a stage of work
+        // to drain behind.
+        if (prev_sa >= 0) {
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&L->afull[prev_sa]);
+          prev_sa = -1;
+        }
         if (item >= kAStages && !mbar_wait(&L->aempty[sa], aphase ^ 1, abort)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16) +
-                               (uint32_t)(kAColBase + sa * 64 + wg * 32);
-        tmem_st32(taddr, v);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&L->afull[sa]);
+        tmem_st16(tmem + lane_base + (uint32_t)(kAColBase + sa * 64 + q * 16), v);
+        prev_sa = sa;
         if (++sa == kAStages) { sa = 0; aphase ^= 1; }
       }
+    }
+    if (prev_sa >= 0) {
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&L->afull[prev_sa]);
     }
   } else if (warp == kTmaWWarp) {
     // ------------------------------------------------------------------
