@@ -103,6 +103,7 @@ SIGNATURES = {
     "wisp_b200_combine_rows": (_I, [_P, _P, _P, _I, _I, _P, _P, _E]),
     "wisp_b200_check_error_flag": (_I, [_P, _P, _E]),
     "wisp_b200_moe_error_word": (_P, [C.POINTER(WispMoeConfig), _P]),
+    "wisp_b200_debug_set_counters": (None, [_P]),
     "wisp_b200_version": (C.c_char_p, []),
 }
 

@@ -115,6 +115,35 @@ struct GemmParams {
   float* out;
   int mode;
   int* error_flag;
+  unsigned long long* counters;  // optional wait-cycle counters (diagnostics)
+};
+
+// Diagnostic counters (cycles, summed over CTAs; one recording thread per
+// warp): which wait each role spends its time in.
+enum {
+  C_DQ_RFULL, C_DQ_AEMPTY, C_DQ_WAITST, C_DQ_TOTAL,
+  C_MMA_AFULL, C_MMA_BFULL, C_MMA_ACCEMPTY, C_MMA_TOTAL,
+  C_TW_REMPTY, C_TW_TOTAL, C_TB_BEMPTY, C_TB_TOTAL,
+  C_EPI_ACCFULL, C_EPI_TOTAL, C_TILES, C_COUNT
+};
+
+struct Prof {
+  unsigned long long* out;
+  unsigned long long acc[4];
+  long long t_start;
+  __device__ explicit Prof(unsigned long long* o) : out(o), acc{0, 0, 0, 0} {
+    t_start = out ? clock64() : 0;
+  }
+  __device__ __forceinline__ long long now() const { return out ? clock64() : 0; }
+  __device__ __forceinline__ void add(int i, long long t0) {
+    if (out) acc[i] += (unsigned long long)(clock64() - t0);
+  }
+  __device__ void flush(const int (&slots)[4], int total_slot, bool recorder) {
+    if (!out || !recorder) return;
+    for (int i = 0; i < 4; i++)
+      if (slots[i] >= 0) atomicAdd(out + slots[i], acc[i]);
+    atomicAdd(out + total_slot, (unsigned long long)(clock64() - t_start));
+  }
 };
 
 struct SmemLayout {
@@ -219,12 +248,15 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
     uint32_t rphase = 0, aphase = 0;
     int item = 0;
     bool ok = true;
+    Prof pf(p.counters);
     for (int tile = blockIdx.x; tile < ntiles && ok && !*abort; tile += gridDim.x) {
       const TileInfo ti = decode_tile(p, tile);
       const bool has_zero = __ldg(flags + ti.expert * 3 + mat) & 1;
       for (int ks = 0; ks < nA; ks++, item++) {
         const int sub = ks % S::kSub;
+        long long t0 = pf.now();
         if (sub == 0 && !mbar_wait(&L->rfull[rslot], rphase, abort)) { ok = false; break; }
+        pf.add(0, t0);
         const uint8_t* rs = raw_ring + rslot * S::kRawStageBytes;
         const uint8_t* box = rs + (MODE == GATEUP ? mat * kBoxBytes : 0);
         // 16-byte chunk of the 64-byte row this thread converts
@@ -255,13 +287,17 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
         // Publish the previous stage now that its store had a stage of work
         // to drain behind.
         if (prev_sa >= 0) {
+          t0 = pf.now();
           tmem_wait_st();
+          pf.add(2, t0);
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&L->afull[prev_sa]);
           prev_sa = -1;
         }
+        t0 = pf.now();
         if (item >= kAStages && !mbar_wait(&L->aempty[sa], aphase ^ 1, abort)) { ok = false; break; }
+        pf.add(1, t0);
         tc_fence_after();
         tmem_st16(tmem + lane_base + (uint32_t)(kAColBase + sa * 64 + q * 16), v);
         prev_sa = sa;
@@ -273,6 +309,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&L->afull[prev_sa]);
+    }
+    {
+      const int slots[4] = {C_DQ_RFULL, C_DQ_AEMPTY, C_DQ_WAITST, -1};
+      pf.flush(slots, C_DQ_TOTAL, lane == 0);
     }
   } else if (warp == kTmaWWarp) {
     // ------------------------------------------------------------------
@@ -286,6 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       int last_phase[16];
       for (int i = 0; i < 16; i++) last_phase[i] = -1;
       bool ok = true;
+      Prof pf(p.counters);
       for (int tile = blockIdx.x; tile < ntiles && ok && !*abort; tile += gridDim.x) {
         const TileInfo ti = decode_tile(p, tile);
         const int m0 = MODE == GATEUP ? 0 : 2;
@@ -306,7 +347,9 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
           bytes += kBoxBytes + ng * BM * 2 * (hz[j] ? 2 : 1);
         }
         for (int rs = 0; rs < nR; rs++, item++) {
+          const long long t0 = pf.now();
           if (item >= S::kRawStages && !mbar_wait(&L->rempty[rslot], rphase ^ 1, abort)) { ok = false; break; }
+          pf.add(0, t0);
           uint8_t* dst = raw_ring + rslot * S::kRawStageBytes;
           mbar_arrive_expect_tx(&L->rfull[rslot], bytes);
 #pragma unroll
@@ -319,6 +362,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
           last_phase[rslot] = (int)rphase;
           if (++rslot == S::kRawStages) { rslot = 0; rphase ^= 1; }
         }
+      }
+      {
+        const int slots[4] = {C_TW_REMPTY, -1, -1, -1};
+        pf.flush(slots, C_TW_TOTAL, true);
       }
       // Let every issued copy land before the CTA can exit.
       for (int i = 0; i < S::kRawStages; i++)
@@ -336,12 +383,15 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       int last_phase[8];
       for (int i = 0; i < 8; i++) last_phase[i] = -1;
       bool ok = true;
+      Prof pf(p.counters);
       for (int tile = blockIdx.x; tile < ntiles && ok && !*abort; tile += gridDim.x) {
         const TileInfo ti = decode_tile(p, tile);
         const CUtensorMap* tm = &p.tmap[bn_slot(ti.bn)];
         const uint32_t bytes = (uint32_t)(ti.bn * 128 * S::kBoxes);
         for (int ks = 0; ks < nA; ks++, item++) {
+          const long long t0 = pf.now();
           if (item >= S::kBStages && !mbar_wait(&L->bempty[sb], bphase ^ 1, abort)) { ok = false; break; }
+          pf.add(0, t0);
           mbar_arrive_expect_tx(&L->bfull[sb], bytes);
           uint8_t* dst = b_ring + sb * S::kBStageBytes;
 #pragma unroll
@@ -350,6 +400,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
           last_phase[sb] = (int)bphase;
           if (++sb == S::kBStages) { sb = 0; bphase ^= 1; }
         }
+      }
+      {
+        const int slots[4] = {C_TB_BEMPTY, -1, -1, -1};
+        pf.flush(slots, C_TB_TOTAL, true);
       }
       for (int i = 0; i < S::kBStages; i++)
         if (last_phase[i] >= 0) mbar_wait(&L->bfull[i], (uint32_t)last_phase[i], abort, 200000000LL);
@@ -363,16 +417,21 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       uint32_t aphase = 0, bphase = 0, accphase = 0;
       int ntile_local = 0;
       bool ok = true;
+      Prof pf(p.counters);
       for (int tile = blockIdx.x; tile < ntiles && ok && !*abort; tile += gridDim.x, ntile_local++) {
         const TileInfo ti = decode_tile(p, tile);
         const uint32_t idesc = idesc_f16_m128(ti.bn);
+        long long t0 = pf.now();
         if (ntile_local > 0 && !mbar_wait(&L->accempty, accphase ^ 1, abort)) break;
+        pf.add(2, t0);
         tc_fence_after();
         for (int ks = 0; ks < nA; ks++) {
-          if (!mbar_wait(&L->afull[sa], aphase, abort) || !mbar_wait(&L->bfull[sb], bphase, abort)) {
-            ok = false;
-            break;
-          }
+          t0 = pf.now();
+          if (!mbar_wait(&L->afull[sa], aphase, abort)) { ok = false; break; }
+          pf.add(0, t0);
+          t0 = pf.now();
+          if (!mbar_wait(&L->bfull[sb], bphase, abort)) { ok = false; break; }
+          pf.add(1, t0);
           tc_fence_after();
           const uint32_t a_col = tmem + kAColBase + sa * 64;
           const uint32_t b_addr = smem_u32(b_ring + sb * S::kBStageBytes);
@@ -400,6 +459,11 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
         mma_commit(&L->accfull);
         accphase ^= 1;
       }
+      {
+        const int slots[4] = {C_MMA_AFULL, C_MMA_BFULL, C_MMA_ACCEMPTY, -1};
+        pf.flush(slots, C_MMA_TOTAL, true);
+        if (p.counters) atomicAdd(p.counters + C_TILES, (unsigned long long)ntile_local);
+      }
       // Drain: make sure no MMA is still running before TMEM is released.
       mma_commit(&L->final_bar);
       mbar_wait(&L->final_bar, 0, abort, 200000000LL);
@@ -411,9 +475,12 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
     const int q = warp & 3;
     const int r = q * 32 + lane;
     uint32_t accphase = 0;
+    Prof pf(p.counters);
     for (int tile = blockIdx.x; tile < ntiles && !*abort; tile += gridDim.x) {
       const TileInfo ti = decode_tile(p, tile);
+      const long long t0 = pf.now();
       if (!mbar_wait(&L->accfull, accphase, abort)) break;
+      pf.add(0, t0);
       accphase ^= 1;
       tc_fence_after();
       const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
@@ -461,6 +528,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       __syncwarp();
       if (lane == 0) mbar_arrive(&L->accempty);
     }
+    const int slots[4] = {C_EPI_ACCFULL, -1, -1, -1};
+    pf.flush(slots, C_EPI_TOTAL, lane == 0);
   }
 
   tc_fence_before();
@@ -620,7 +689,13 @@ WispError check_shapes(const WispMoeConfig* cfg, WispErrCtx* err) {
   return WISP_OK;
 }
 
+unsigned long long* g_counters = nullptr;
+
 }  // namespace
+
+extern "C" void wisp_b200_debug_set_counters(unsigned long long* d_counters) {
+  g_counters = d_counters;
+}
 
 extern "C" size_t wisp_b200_prepared_bytes(const WispMoeConfig* cfg, int n_entries) {
   if (!cfg || n_entries <= 0 || check_shapes(cfg, nullptr) != WISP_OK) return 0;
@@ -719,7 +794,9 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
   gu.gs = gs;
   gu.h_out = reinterpret_cast<__half*>(d_h);
   gu.error_flag = d_error_flag;
+  gu.counters = g_counters;
   dn = gu;
+  dn.counters = g_counters ? g_counters + C_COUNT : nullptr;
   for (int i = 0; i < 4; i++) {
     if (!encode_rows_map(&dn.tmap[i], d_h, rows_capacity, I, 16 << i))
       return WB_FAIL(WISP_ERR_CUDA, "grouped_ffn: cuTensorMapEncodeTiled failed (H)");
