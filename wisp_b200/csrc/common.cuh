@@ -243,6 +243,17 @@ WB_DEV void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32
       : "memory");
 }
 
+// Same, with the accumulate flag a compile-time constant.
+template <int ACC>
+WB_DEV void mma_f16_ts_c(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "n"(ACC)
+      : "memory");
+}
+
 // Arrive on an mbarrier once all tcgen05.mma previously issued by this
 // thread have completed.
 WB_DEV void mma_commit(uint64_t* bar) {

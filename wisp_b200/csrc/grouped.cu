@@ -31,7 +31,8 @@
 //   warps 16-19 epilogue: tcgen05.ld of the accumulators, SwiGLU (GATEUP) or
 //               the weighted scatter-combine (DOWN).
 // TMEM columns: [0,128) gate / single accumulator, [128,256) up accumulator,
-// [256,512) four 64-column A stages. Every wait is bounded; a wait that gives
+// [256,512) four 64-column A stages. A stage s and activation stage s are
+// produced separately but consumed by the same MMAs and freed by one commit. Every wait is bounded; a wait that gives
 // up raises a CTA-wide abort and the device error word.
 //
 // The K order inside every group of 8 activations is 0,4,1,5,2,6,3,7: that
@@ -55,7 +56,7 @@ constexpr int kTmaBWarp = kDqWarps + 4;
 constexpr int kMmaWarp = kDqWarps + 5;
 constexpr int kTmaWWarp = kDqWarps + 6;
 constexpr int kThreads = (kDqWarps + 7) * 32;
-constexpr int kAStages = 4;
+constexpr int kStages = 4;   // A stages (TMEM) and activation stages (smem) share an index
 constexpr int BM = 128;
 constexpr int kBNMax = 128;
 constexpr int kTmemCols = 512;
@@ -75,10 +76,9 @@ struct Shape {
   static constexpr int kScOff = kMats * kBoxBytes;
   static constexpr int kZOff = kScOff + kMats * kScBytes;
   static constexpr int kRawStageBytes = ((kZOff + kMats * kScBytes) + 1023) / 1024 * 1024;
-  static constexpr int kRawStages = MODE == GATEUP ? 6 : 10;
+  static constexpr int kRawStages = MODE == GATEUP ? 6 : 8;
   static constexpr int kBoxes = KA / 64;                           // 64-K activation boxes per A stage
   static constexpr int kBStageBytes = kBoxes * kBNMax * 128;
-  static constexpr int kBStages = MODE == GATEUP ? 4 : 3;
 };
 
 // Prepared weights: per matrix entry (expert v, matrix m in gate/up/down) a
@@ -148,8 +148,7 @@ struct Prof {
 
 struct SmemLayout {
   uint64_t rfull[16], rempty[16];
-  uint64_t bfull[8], bempty[8];
-  uint64_t afull[kAStages], aempty[kAStages];
+  uint64_t afull[kStages], bfull[kStages], empty[kStages];
   uint64_t accfull, accempty, final_bar;
   uint32_t tmem_base;
   int abort;
@@ -192,8 +191,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
   const uint32_t base_u32 = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (base_u32 & 1023)) & 1023);
   uint8_t* raw_ring = smem;                                          // kRawStages * kRawStageBytes
-  uint8_t* b_ring = raw_ring + S::kRawStages * S::kRawStageBytes;    // kBStages * kBStageBytes
-  SmemLayout* L = reinterpret_cast<SmemLayout*>(b_ring + S::kBStages * S::kBStageBytes);
+  uint8_t* b_ring = raw_ring + S::kRawStages * S::kRawStageBytes;    // kStages * kBStageBytes
+  SmemLayout* L = reinterpret_cast<SmemLayout*>(b_ring + kStages * S::kBStageBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = __ldg(p.tiles + p.nseg);
@@ -207,13 +206,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       mbar_init(&L->rfull[i], 1);
       mbar_init(&L->rempty[i], kDqThreads / 32);
     }
-    for (int i = 0; i < S::kBStages; i++) {
-      mbar_init(&L->bfull[i], 1);
-      mbar_init(&L->bempty[i], 1);
-    }
-    for (int i = 0; i < kAStages; i++) {
+    for (int i = 0; i < kStages; i++) {
       mbar_init(&L->afull[i], kDqThreads / 32);
-      mbar_init(&L->aempty[i], 1);
+      mbar_init(&L->bfull[i], 1);
+      mbar_init(&L->empty[i], 1);  // one tcgen05.commit frees both halves of the stage
     }
     mbar_init(&L->accfull, 1);
     mbar_init(&L->accempty, 4);  // the four epilogue warps
@@ -296,12 +292,12 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
           prev_sa = -1;
         }
         t0 = pf.now();
-        if (item >= kAStages && !mbar_wait(&L->aempty[sa], aphase ^ 1, abort)) { ok = false; break; }
+        if (item >= kStages && !mbar_wait(&L->empty[sa], aphase ^ 1, abort)) { ok = false; break; }
         pf.add(1, t0);
         tc_fence_after();
         tmem_st16(tmem + lane_base + (uint32_t)(kAColBase + sa * 64 + q * 16), v);
         prev_sa = sa;
-        if (++sa == kAStages) { sa = 0; aphase ^= 1; }
+        if (++sa == kStages) { sa = 0; aphase ^= 1; }
       }
     }
     if (prev_sa >= 0) {
@@ -390,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
         const uint32_t bytes = (uint32_t)(ti.bn * 128 * S::kBoxes);
         for (int ks = 0; ks < nA; ks++, item++) {
           const long long t0 = pf.now();
-          if (item >= S::kBStages && !mbar_wait(&L->bempty[sb], bphase ^ 1, abort)) { ok = false; break; }
+          if (item >= kStages && !mbar_wait(&L->empty[sb], bphase ^ 1, abort)) { ok = false; break; }
           pf.add(0, t0);
           mbar_arrive_expect_tx(&L->bfull[sb], bytes);
           uint8_t* dst = b_ring + sb * S::kBStageBytes;
@@ -398,14 +394,14 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
           for (int bx = 0; bx < S::kBoxes; bx++)
             tma_load_2d(dst + bx * (kBNMax * 128), tm, &L->bfull[sb], ks * S::KA + bx * 64, ti.row0);
           last_phase[sb] = (int)bphase;
-          if (++sb == S::kBStages) { sb = 0; bphase ^= 1; }
+          if (++sb == kStages) { sb = 0; bphase ^= 1; }
         }
       }
       {
         const int slots[4] = {C_TB_BEMPTY, -1, -1, -1};
         pf.flush(slots, C_TB_TOTAL, true);
       }
-      for (int i = 0; i < S::kBStages; i++)
+      for (int i = 0; i < kStages; i++)
         if (last_phase[i] >= 0) mbar_wait(&L->bfull[i], (uint32_t)last_phase[i], abort, 200000000LL);
     }
   } else if (warp == kMmaWarp) {
@@ -413,8 +409,9 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
     // MMA issuer (one thread).
     // ------------------------------------------------------------------
     if (lane == 0) {
-      int sa = 0, sb = 0;
-      uint32_t aphase = 0, bphase = 0, accphase = 0;
+      int sa = 0;
+      uint32_t aphase = 0, accphase = 0;
+      const uint64_t bdesc0 = smem_desc_sw128(smem_u32(b_ring));
       int ntile_local = 0;
       bool ok = true;
       Prof pf(p.counters);
@@ -430,30 +427,36 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
           if (!mbar_wait(&L->afull[sa], aphase, abort)) { ok = false; break; }
           pf.add(0, t0);
           t0 = pf.now();
-          if (!mbar_wait(&L->bfull[sb], bphase, abort)) { ok = false; break; }
+          if (!mbar_wait(&L->bfull[sa], aphase, abort)) { ok = false; break; }
           pf.add(1, t0);
           tc_fence_after();
+          // A stage and activation stage share the index: fixed TMEM columns
+          // and a descriptor that only moves by constants.
           const uint32_t a_col = tmem + kAColBase + sa * 64;
-          const uint32_t b_addr = smem_u32(b_ring + sb * S::kBStageBytes);
+          const uint64_t bd = bdesc0 + (uint64_t)(sa * (S::kBStageBytes >> 4));
           if (MODE == GATEUP) {
+            if (ks == 0) {
+              mma_f16_ts_c<0>(tmem + 0, a_col, bd, idesc);
+              mma_f16_ts_c<0>(tmem + 128, a_col + 32, bd, idesc);
+            } else {
+              mma_f16_ts_c<1>(tmem + 0, a_col, bd, idesc);
+              mma_f16_ts_c<1>(tmem + 128, a_col + 32, bd, idesc);
+            }
 #pragma unroll
-            for (int kk = 0; kk < 4; kk++) {
-              const uint64_t bd = smem_desc_sw128(b_addr + kk * 32);
-              const uint32_t acc = (ks | kk) ? 1u : 0u;
-              mma_f16_ts(tmem + 0, a_col + kk * 8, bd, idesc, acc);
-              mma_f16_ts(tmem + 128, a_col + 32 + kk * 8, bd, idesc, acc);
+            for (int kk = 1; kk < 4; kk++) {
+              mma_f16_ts_c<1>(tmem + 0, a_col + kk * 8, bd + 2 * kk, idesc);
+              mma_f16_ts_c<1>(tmem + 128, a_col + 32 + kk * 8, bd + 2 * kk, idesc);
             }
           } else {
+            if (ks == 0) mma_f16_ts_c<0>(tmem + 0, a_col, bd, idesc);
+            else mma_f16_ts_c<1>(tmem + 0, a_col, bd, idesc);
 #pragma unroll
-            for (int kk = 0; kk < 8; kk++) {
-              const uint64_t bd = smem_desc_sw128(b_addr + (kk >> 2) * (kBNMax * 128) + (kk & 3) * 32);
-              mma_f16_ts(tmem + 0, a_col + kk * 8, bd, idesc, (ks | kk) ? 1u : 0u);
-            }
+            for (int kk = 1; kk < 8; kk++)
+              mma_f16_ts_c<1>(tmem + 0, a_col + kk * 8,
+                              bd + (uint64_t)((kk >> 2) * ((kBNMax * 128) >> 4) + 2 * (kk & 3)), idesc);
           }
-          mma_commit(&L->aempty[sa]);
-          mma_commit(&L->bempty[sb]);
-          if (++sa == kAStages) { sa = 0; aphase ^= 1; }
-          if (++sb == S::kBStages) { sb = 0; bphase ^= 1; }
+          mma_commit(&L->empty[sa]);
+          if (++sa == kStages) { sa = 0; aphase ^= 1; }
         }
         if (!ok) break;
         mma_commit(&L->accfull);
@@ -667,7 +670,7 @@ bool encode_packed_map(CUtensorMap* m, const void* base, int rows, int cols) {
 template <int MODE>
 size_t smem_bytes() {
   using S = Shape<MODE>;
-  return 1024 + (size_t)S::kRawStages * S::kRawStageBytes + (size_t)S::kBStages * S::kBStageBytes +
+  return 1024 + (size_t)S::kRawStages * S::kRawStageBytes + (size_t)kStages * S::kBStageBytes +
          sizeof(SmemLayout);
 }
 
