@@ -31,8 +31,7 @@
 //   warps 16-19 epilogue: tcgen05.ld of the accumulators, SwiGLU (GATEUP) or
 //               the weighted scatter-combine (DOWN).
 // TMEM columns: [0,128) gate / single accumulator, [128,256) up accumulator,
-// [256,512) four 64-column A stages. A stage s and activation stage s are
-// produced separately but consumed by the same MMAs and freed by one commit. Every wait is bounded; a wait that gives
+// [256,512) four 64-column A stages. Every wait is bounded; a wait that gives
 // up raises a CTA-wide abort and the device error word.
 //
 // The K order inside every group of 8 activations is 0,4,1,5,2,6,3,7: that
@@ -56,7 +55,7 @@ constexpr int kTmaBWarp = kDqWarps + 4;
 constexpr int kMmaWarp = kDqWarps + 5;
 constexpr int kTmaWWarp = kDqWarps + 6;
 constexpr int kThreads = (kDqWarps + 7) * 32;
-constexpr int kStages = 4;   // A stages (TMEM) and activation stages (smem) share an index
+constexpr int kAStages = 4;  // A stages in TMEM
 constexpr int BM = 128;
 constexpr int kBNMax = 128;
 constexpr int kTmemCols = 512;
@@ -78,7 +77,11 @@ struct Shape {
   static constexpr int kRawStageBytes = ((kZOff + kMats * kScBytes) + 1023) / 1024 * 1024;
   static constexpr int kRawStages = MODE == GATEUP ? 6 : 8;
   static constexpr int kBoxes = KA / 64;                           // 64-K activation boxes per A stage
+  // An activation stage holds 128/BN consecutive A stages' worth of boxes
+  // (BN rows x 128 bytes each), so its size does not depend on BN and small
+  // token groups get a deep prefetch (32 A stages at BN = 16).
   static constexpr int kBStageBytes = kBoxes * kBNMax * 128;
+  static constexpr int kBStages = MODE == GATEUP ? 5 : 3;
 };
 
 // Prepared weights: per matrix entry (expert v, matrix m in gate/up/down) a
@@ -148,7 +151,8 @@ struct Prof {
 
 struct SmemLayout {
   uint64_t rfull[16], rempty[16];
-  uint64_t afull[kStages], bfull[kStages], empty[kStages];
+  uint64_t afull[kAStages], aempty[kAStages];
+  uint64_t bfull[8], bempty[8];
   uint64_t accfull, accempty, final_bar;
   uint32_t tmem_base;
   int abort;
@@ -191,8 +195,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
   const uint32_t base_u32 = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (base_u32 & 1023)) & 1023);
   uint8_t* raw_ring = smem;                                          // kRawStages * kRawStageBytes
-  uint8_t* b_ring = raw_ring + S::kRawStages * S::kRawStageBytes;    // kStages * kBStageBytes
-  SmemLayout* L = reinterpret_cast<SmemLayout*>(b_ring + kStages * S::kBStageBytes);
+  uint8_t* b_ring = raw_ring + S::kRawStages * S::kRawStageBytes;    // kBStages * kBStageBytes
+  SmemLayout* L = reinterpret_cast<SmemLayout*>(b_ring + S::kBStages * S::kBStageBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = __ldg(p.tiles + p.nseg);
@@ -206,10 +210,13 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       mbar_init(&L->rfull[i], 1);
       mbar_init(&L->rempty[i], kDqThreads / 32);
     }
-    for (int i = 0; i < kStages; i++) {
+    for (int i = 0; i < kAStages; i++) {
       mbar_init(&L->afull[i], kDqThreads / 32);
+      mbar_init(&L->aempty[i], 1);
+    }
+    for (int i = 0; i < S::kBStages; i++) {
       mbar_init(&L->bfull[i], 1);
-      mbar_init(&L->empty[i], 1);  // one tcgen05.commit frees both halves of the stage
+      mbar_init(&L->bempty[i], 1);
     }
     mbar_init(&L->accfull, 1);
     mbar_init(&L->accempty, 4);  // the four epilogue warps
@@ -292,12 +299,12 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
           prev_sa = -1;
         }
         t0 = pf.now();
-        if (item >= kStages && !mbar_wait(&L->empty[sa], aphase ^ 1, abort)) { ok = false; break; }
+        if (item >= kAStages && !mbar_wait(&L->aempty[sa], aphase ^ 1, abort)) { ok = false; break; }
         pf.add(1, t0);
         tc_fence_after();
         tmem_st16(tmem + lane_base + (uint32_t)(kAColBase + sa * 64 + q * 16), v);
         prev_sa = sa;
-        if (++sa == kStages) { sa = 0; aphase ^= 1; }
+        if (++sa == kAStages) { sa = 0; aphase ^= 1; }
       }
     }
     if (prev_sa >= 0) {
@@ -383,25 +390,29 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       for (int tile = blockIdx.x; tile < ntiles && ok && !*abort; tile += gridDim.x) {
         const TileInfo ti = decode_tile(p, tile);
         const CUtensorMap* tm = &p.tmap[bn_slot(ti.bn)];
-        const uint32_t bytes = (uint32_t)(ti.bn * 128 * S::kBoxes);
-        for (int ks = 0; ks < nA; ks++, item++) {
+        const int per_b = kBNMax / ti.bn;          // A stages per activation stage
+        const int box_bytes = ti.bn * 128;
+        for (int a0 = 0; a0 < nA; a0 += per_b, item++) {
+          const int na = min(per_b, nA - a0);
           const long long t0 = pf.now();
-          if (item >= kStages && !mbar_wait(&L->empty[sb], bphase ^ 1, abort)) { ok = false; break; }
+          if (item >= S::kBStages && !mbar_wait(&L->bempty[sb], bphase ^ 1, abort)) { ok = false; break; }
           pf.add(0, t0);
-          mbar_arrive_expect_tx(&L->bfull[sb], bytes);
+          mbar_arrive_expect_tx(&L->bfull[sb], (uint32_t)(na * S::kBoxes * box_bytes));
           uint8_t* dst = b_ring + sb * S::kBStageBytes;
+          for (int a = 0; a < na; a++)
 #pragma unroll
-          for (int bx = 0; bx < S::kBoxes; bx++)
-            tma_load_2d(dst + bx * (kBNMax * 128), tm, &L->bfull[sb], ks * S::KA + bx * 64, ti.row0);
+            for (int bx = 0; bx < S::kBoxes; bx++)
+              tma_load_2d(dst + (a * S::kBoxes + bx) * box_bytes, tm, &L->bfull[sb],
+                          (a0 + a) * S::KA + bx * 64, ti.row0);
           last_phase[sb] = (int)bphase;
-          if (++sb == kStages) { sb = 0; bphase ^= 1; }
+          if (++sb == S::kBStages) { sb = 0; bphase ^= 1; }
         }
       }
       {
         const int slots[4] = {C_TB_BEMPTY, -1, -1, -1};
         pf.flush(slots, C_TB_TOTAL, true);
       }
-      for (int i = 0; i < kStages; i++)
+      for (int i = 0; i < S::kBStages; i++)
         if (last_phase[i] >= 0) mbar_wait(&L->bfull[i], (uint32_t)last_phase[i], abort, 200000000LL);
     }
   } else if (warp == kMmaWarp) {
@@ -409,8 +420,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
     // MMA issuer (one thread).
     // ------------------------------------------------------------------
     if (lane == 0) {
-      int sa = 0;
-      uint32_t aphase = 0, accphase = 0;
+      int sa = 0, sb = 0;
+      uint32_t aphase = 0, bphase = 0, accphase = 0;
       const uint64_t bdesc0 = smem_desc_sw128(smem_u32(b_ring));
       int ntile_local = 0;
       bool ok = true;
@@ -418,22 +429,26 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       for (int tile = blockIdx.x; tile < ntiles && ok && !*abort; tile += gridDim.x, ntile_local++) {
         const TileInfo ti = decode_tile(p, tile);
         const uint32_t idesc = idesc_f16_m128(ti.bn);
+        const int per_b = kBNMax / ti.bn;
+        const uint32_t box16 = (uint32_t)(ti.bn * 128) >> 4;   // one box, in descriptor units
         long long t0 = pf.now();
         if (ntile_local > 0 && !mbar_wait(&L->accempty, accphase ^ 1, abort)) break;
         pf.add(2, t0);
         tc_fence_after();
+        int a = 0;   // A stage within the current activation stage
         for (int ks = 0; ks < nA; ks++) {
+          if (a == 0) {
+            t0 = pf.now();
+            if (!mbar_wait(&L->bfull[sb], bphase, abort)) { ok = false; break; }
+            pf.add(1, t0);
+          }
           t0 = pf.now();
           if (!mbar_wait(&L->afull[sa], aphase, abort)) { ok = false; break; }
           pf.add(0, t0);
-          t0 = pf.now();
-          if (!mbar_wait(&L->bfull[sa], aphase, abort)) { ok = false; break; }
-          pf.add(1, t0);
           tc_fence_after();
-          // A stage and activation stage share the index: fixed TMEM columns
-          // and a descriptor that only moves by constants.
           const uint32_t a_col = tmem + kAColBase + sa * 64;
-          const uint64_t bd = bdesc0 + (uint64_t)(sa * (S::kBStageBytes >> 4));
+          const uint64_t bd = bdesc0 + (uint64_t)((sb * S::kBStageBytes) >> 4) +
+                              (uint64_t)(a * S::kBoxes) * box16;
           if (MODE == GATEUP) {
             if (ks == 0) {
               mma_f16_ts_c<0>(tmem + 0, a_col, bd, idesc);
@@ -453,10 +468,15 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
 #pragma unroll
             for (int kk = 1; kk < 8; kk++)
               mma_f16_ts_c<1>(tmem + 0, a_col + kk * 8,
-                              bd + (uint64_t)((kk >> 2) * ((kBNMax * 128) >> 4) + 2 * (kk & 3)), idesc);
+                              bd + (uint64_t)((kk >> 2) * box16 + 2 * (kk & 3)), idesc);
           }
-          mma_commit(&L->empty[sa]);
-          if (++sa == kStages) { sa = 0; aphase ^= 1; }
+          mma_commit(&L->aempty[sa]);
+          if (++sa == kAStages) { sa = 0; aphase ^= 1; }
+          if (++a == per_b || ks == nA - 1) {
+            mma_commit(&L->bempty[sb]);
+            a = 0;
+            if (++sb == S::kBStages) { sb = 0; bphase ^= 1; }
+          }
         }
         if (!ok) break;
         mma_commit(&L->accfull);
@@ -670,7 +690,7 @@ bool encode_packed_map(CUtensorMap* m, const void* base, int rows, int cols) {
 template <int MODE>
 size_t smem_bytes() {
   using S = Shape<MODE>;
-  return 1024 + (size_t)S::kRawStages * S::kRawStageBytes + (size_t)kStages * S::kBStageBytes +
+  return 1024 + (size_t)S::kRawStages * S::kRawStageBytes + (size_t)S::kBStages * S::kBStageBytes +
          sizeof(SmemLayout);
 }
 
