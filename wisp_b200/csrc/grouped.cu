@@ -30,9 +30,8 @@
 //               fp32 accumulators in TMEM; completion via tcgen05.commit.
 //   warps 16-19 epilogue: tcgen05.ld of the accumulators, SwiGLU (GATEUP) or
 //               the weighted scatter-combine (DOWN).
-// TMEM columns: [0,256) accumulators (GATEUP: gate chains in [0,128), up
-// chains in [128,256); DOWN: chains over [0,256)), [256,512) four 64-column A
-// stages. Every wait is bounded; a wait that gives
+// TMEM columns: [0,128) gate / single accumulator, [128,256) up accumulator,
+// [256,512) four 64-column A stages. Every wait is bounded; a wait that gives
 // up raises a CTA-wide abort and the device error word.
 //
 // The K order inside every group of 8 activations is 0,4,1,5,2,6,3,7: that
@@ -188,16 +187,6 @@ __device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int tile) {
 }
 
 __device__ __forceinline__ int bn_slot(int bn) { return bn == 16 ? 0 : bn == 32 ? 1 : bn == 64 ? 2 : 3; }
-
-// Independent accumulator chains per matrix: consecutive 16-K MMAs go to
-// different accumulators so that, at small N, an MMA does not wait for the
-// previous one's result. The epilogue sums the chains. GATEUP keeps gate in
-// columns [0,128) and up in [128,256); DOWN spreads its chains over [0,256).
-template <int MODE>
-__device__ __forceinline__ int n_chains(int bn) {
-  const int c = (MODE == GATEUP ? 128 : 256) / bn;
-  return c > 8 ? 8 : c;
-}
 
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_constant__ GemmParams p) {
@@ -442,7 +431,6 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
         const uint32_t idesc = idesc_f16_m128(ti.bn);
         const int per_b = kBNMax / ti.bn;
         const uint32_t box16 = (uint32_t)(ti.bn * 128) >> 4;   // one box, in descriptor units
-        const int chains = n_chains<MODE>(ti.bn), cmask = chains - 1;
         long long t0 = pf.now();
         if (ntile_local > 0 && !mbar_wait(&L->accempty, accphase ^ 1, abort)) break;
         pf.add(2, t0);
@@ -462,23 +450,25 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
           const uint64_t bd = bdesc0 + (uint64_t)((sb * S::kBStageBytes) >> 4) +
                               (uint64_t)(a * S::kBoxes) * box16;
           if (MODE == GATEUP) {
+            if (ks == 0) {
+              mma_f16_ts_c<0>(tmem + 0, a_col, bd, idesc);
+              mma_f16_ts_c<0>(tmem + 128, a_col + 32, bd, idesc);
+            } else {
+              mma_f16_ts_c<1>(tmem + 0, a_col, bd, idesc);
+              mma_f16_ts_c<1>(tmem + 128, a_col + 32, bd, idesc);
+            }
 #pragma unroll
-            for (int kk = 0; kk < 4; kk++) {
-              const int j = ks * 4 + kk;                    // MMA index within the tile
-              const uint32_t col = (uint32_t)((j & cmask) * ti.bn);
-              const uint32_t acc = j >= chains ? 1u : 0u;
-              mma_f16_ts(tmem + col, a_col + kk * 8, bd + 2 * kk, idesc, acc);
-              mma_f16_ts(tmem + 128 + col, a_col + 32 + kk * 8, bd + 2 * kk, idesc, acc);
+            for (int kk = 1; kk < 4; kk++) {
+              mma_f16_ts_c<1>(tmem + 0, a_col + kk * 8, bd + 2 * kk, idesc);
+              mma_f16_ts_c<1>(tmem + 128, a_col + 32 + kk * 8, bd + 2 * kk, idesc);
             }
           } else {
+            if (ks == 0) mma_f16_ts_c<0>(tmem + 0, a_col, bd, idesc);
+            else mma_f16_ts_c<1>(tmem + 0, a_col, bd, idesc);
 #pragma unroll
-            for (int kk = 0; kk < 8; kk++) {
-              const int j = ks * 8 + kk;
-              const uint32_t col = (uint32_t)((j & cmask) * ti.bn);
-              mma_f16_ts(tmem + col, a_col + kk * 8,
-                         bd + (uint64_t)((kk >> 2) * box16 + 2 * (kk & 3)), idesc,
-                         j >= chains ? 1u : 0u);
-            }
+            for (int kk = 1; kk < 8; kk++)
+              mma_f16_ts_c<1>(tmem + 0, a_col + kk * 8,
+                              bd + (uint64_t)((kk >> 2) * box16 + 2 * (kk & 3)), idesc);
           }
           mma_commit(&L->aempty[sa]);
           if (++sa == kAStages) { sa = 0; aphase ^= 1; }
@@ -520,47 +510,32 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       if (MODE == GATEUP) {
         const int i = ti.mblk * BM + r;
         const int islot = k_interleave_slot(i);
-        const int chains = n_chains<MODE>(ti.bn);
         for (int c0 = 0; c0 < ti.bn; c0 += 16) {
-          float gs_[16], us_[16];
-          for (int ch = 0; ch < chains; ch++) {
-            uint32_t g[16], u[16];
-            tmem_ld16(lane_addr + ch * ti.bn + c0, g);
-            tmem_ld16(lane_addr + 128 + ch * ti.bn + c0, u);
-            tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 16; j++) {
-              gs_[j] = ch ? gs_[j] + __uint_as_float(g[j]) : __uint_as_float(g[j]);
-              us_[j] = ch ? us_[j] + __uint_as_float(u[j]) : __uint_as_float(u[j]);
-            }
-          }
+          uint32_t g[16], u[16];
+          tmem_ld16(lane_addr + c0, g);
+          tmem_ld16(lane_addr + 128 + c0, u);
+          tmem_wait_ld();
 #pragma unroll
           for (int j = 0; j < 16; j++) {
             const int tt = c0 + j;
             if (tt < ti.nvalid) {
-              const float hv = silu(gs_[j]) * us_[j];
+              const float hv = silu(__uint_as_float(g[j])) * __uint_as_float(u[j]);
               p.h_out[(size_t)(ti.row0 + tt) * p.I + islot] = __float2half(hv);
             }
           }
         }
       } else {
         const int m = ti.mblk * BM + r;
-        const int chains = n_chains<MODE>(ti.bn);
         for (int c0 = 0; c0 < ti.bn; c0 += 16) {
-          float ys[16];
-          for (int ch = 0; ch < chains; ch++) {
-            uint32_t y[16];
-            tmem_ld16(lane_addr + ch * ti.bn + c0, y);
-            tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 16; j++) ys[j] = ch ? ys[j] + __uint_as_float(y[j]) : __uint_as_float(y[j]);
-          }
+          uint32_t y[16];
+          tmem_ld16(lane_addr + c0, y);
+          tmem_wait_ld();
 #pragma unroll
           for (int j = 0; j < 16; j++) {
             const int tt = c0 + j;
             if (tt < ti.nvalid) {
               const int prow = ti.row0 + tt;
-              const float yv = ys[j];
+              const float yv = __uint_as_float(y[j]);
               if (p.mode == 0) {
                 const int tok = __ldg(p.row_token + prow);
                 const float wgt = __ldg(p.row_weight + prow);
