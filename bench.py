@@ -343,7 +343,8 @@ def main() -> None:
             for l in range(L):   # rotate the layers' weights so L2 never holds them
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 a.record(stream)
-                abi.call("wisp_b200_grouped_ffn", C.byref(cfg), table[l].data_ptr(), V, segs.data_ptr(), V, R,
+                abi.call("wisp_b200_grouped_ffn", C.byref(cfg), table[l].data_ptr(),
+                         layers_w[l].table.data_ptr(), V, segs.data_ptr(), V, R,
                          xp.data_ptr(), h.data_ptr(), 0, row_token.data_ptr(), row_w.data_ptr(),
                          out.data_ptr(), tiles.data_ptr(), flag.data_ptr(), stream.cuda_stream)
                 b.record(stream)

@@ -242,8 +242,10 @@ typedef struct {
     int32_t reserved;
 } WispSegment;
 
-/* Grouped expert FFN over pre-permuted rows. d_prepared / n_entries: a
- * prepared weight set (segment experts index its entries).
+/* Grouped expert FFN over pre-permuted rows. d_prepared / d_experts /
+ * n_entries: a prepared weight set and its device expert table (segment
+ * experts index its entries). Segments of at most 16 rows (decode) run on
+ * the register-fed tensor-core kernel, larger ones on the tcgen05 kernel.
  *   d_xp:   fp16 [R x M] activation rows in interleaved K order (within each
  *           8 K: 0,4,1,5,2,6,3,7) -- produced by wisp_b200_pack_rows.
  *   d_segs: DEVICE array of n_segs segments.
@@ -254,7 +256,8 @@ typedef struct {
  * d_error_flag: device int set to nonzero if a bounded wait gave up (may be
  * NULL); check it with wisp_b200_check_error_flag. */
 size_t wisp_b200_tiles_words(int n_segs);
-WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void* d_prepared, int n_entries,
+WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void* d_prepared,
+                                const WispInt4Expert* d_experts, int n_entries,
                                 const WispSegment* d_segs, int n_segs, int rows_capacity,
                                 const uint16_t* d_xp, uint16_t* d_h, int mode,
                                 const int* d_row_token, const float* d_row_weight,
@@ -298,6 +301,11 @@ int* wisp_b200_moe_error_word(const WispMoeConfig* cfg, void* d_workspace);
  * in each of its waits (gate/up kernel in the first 15, down in the next).
  * Pass NULL to switch off. Not thread-safe; for profiling runs only. */
 void wisp_b200_debug_set_counters(unsigned long long* d_counters);
+
+/* Largest segment (rows) routed to the register-fed kernel; 0 sends every
+ * segment to the tcgen05 kernel, a negative value restores the default (16).
+ * Process-wide; for tests and tuning. */
+void wisp_b200_set_skinny_max_rows(int rows);
 
 /* Library version string. */
 const char* wisp_b200_version(void);

@@ -130,14 +130,14 @@ def test_expert_ffn_argument_checks(golden_dir):
 def test_grouped_ffn_argument_checks():
     c = _cfg(group_size=32)
     err = abi.WispErrCtx()
-    rc = abi.lib().wisp_b200_grouped_ffn(C.byref(c), 256, 4, 16, 1, 8, 16, 16, 0, 16, 16, 16, 16,
+    rc = abi.lib().wisp_b200_grouped_ffn(C.byref(c), 256, 16, 4, 16, 1, 8, 16, 16, 0, 16, 16, 16, 16,
                                          None, None, C.byref(err))
     assert rc == abi.WISP_ERR_INVALID_ARG and b"group_size" in err.message
     c = _cfg()
-    rc = abi.lib().wisp_b200_grouped_ffn(C.byref(c), 256, 4, 16, 1, 8, 16, 16, 0, None, None, 16, 16,
+    rc = abi.lib().wisp_b200_grouped_ffn(C.byref(c), 256, 16, 4, 16, 1, 8, 16, 16, 0, None, None, 16, 16,
                                          None, None, C.byref(err))
     assert rc == abi.WISP_ERR_INVALID_ARG and b"mode 0" in err.message
-    rc = abi.lib().wisp_b200_grouped_ffn(C.byref(c), 264, 4, 16, 1, 8, 16, 16, 1, None, None, 16, 16,
+    rc = abi.lib().wisp_b200_grouped_ffn(C.byref(c), 264, 16, 4, 16, 1, 8, 16, 16, 1, None, None, 16, 16,
                                          None, None, C.byref(err))
     assert rc == abi.WISP_ERR_INVALID_ARG and b"256-byte" in err.message
 

@@ -21,6 +21,15 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
+@pytest.fixture(params=["mixed", "tcgen05"])
+def path(request):
+    """mixed: segments of <= 16 rows on the register-fed kernel, larger ones
+    on tcgen05 (the library default); tcgen05: every segment on tcgen05."""
+    abi.lib().wisp_b200_set_skinny_max_rows(0 if request.param == "tcgen05" else -1)
+    yield request.param
+    abi.lib().wisp_b200_set_skinny_max_rows(-1)
+
+
 def _stream():
     return torch.cuda.current_stream().cuda_stream
 
@@ -207,7 +216,7 @@ def _layer_from_golden(g):
     return lw
 
 
-def test_moe_forward_matches_reference_golden(golden_dir):
+def test_moe_forward_matches_reference_golden(golden_dir, path):
     g = _golden(golden_dir)
     M, I, E, k, gs, T = (int(v) for v in g["dims"])
     lw = _layer_from_golden(g)
@@ -234,7 +243,7 @@ SMALL = [
 @pytest.mark.parametrize("zeros", [False, True])
 @pytest.mark.parametrize("T", [1, 5, 37, 300])
 @pytest.mark.parametrize("si", range(len(SMALL)))
-def test_moe_forward_small(orc, si, T, zeros):
+def test_moe_forward_small(orc, si, T, zeros, path):
     """Ragged token counts, both group sizes, both scoring rules, with and
     without zero points and a shared expert."""
     spec = synth.MoeSpec(f"small{si}", tokens=T, seed=100 + si, **SMALL[si])
@@ -262,7 +271,7 @@ def _segments_device(segs):
 
 
 @pytest.mark.parametrize("mode", [0, 1])
-def test_grouped_ffn_tile_boundaries(orc, mode):
+def test_grouped_ffn_tile_boundaries(orc, mode, path):
     """Segments of 0, 1, 15, 16, 17, 32, 33, 64, 65, 128, 129 and 300 rows
     (every BN choice and its ragged edge) through the grouped kernels."""
     counts = [0, 1, 15, 16, 17, 32, 33, 64, 65, 128, 129, 300]
@@ -286,7 +295,8 @@ def test_grouped_ffn_tile_boundaries(orc, mode):
     dsegs = _segments_device(segs)
     cfg = spec.cfg(T)
     abi.call("wisp_b200_pack_rows", x.data_ptr(), None, R, spec.hidden, xp.data_ptr(), _stream())
-    abi.call("wisp_b200_grouped_ffn", C.byref(cfg), lw.prepare().data_ptr(), lw.n_entries,
+    abi.call("wisp_b200_grouped_ffn", C.byref(cfg), lw.prepare().data_ptr(), lw.table.data_ptr(),
+             lw.n_entries,
              dsegs.data_ptr(), len(segs), R,
              xp.data_ptr(), h.data_ptr(), mode, row_token.data_ptr(), row_w.data_ptr(), out.data_ptr(),
              tiles.data_ptr(), flag.data_ptr(), _stream())

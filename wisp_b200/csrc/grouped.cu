@@ -565,8 +565,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
 }
 
 // Per segment: BN (16/32/64/128 by row count) and the prefix sum of tiles.
+// Segments of at most skip_rows rows belong to the register-path kernel and
+// get no tiles here.
 __global__ void plan_tiles_kernel(const WispSegment* __restrict__ segs, int nseg, int mblocks,
-                                  int32_t* __restrict__ tiles) {
+                                  int skip_rows, int32_t* __restrict__ tiles) {
   __shared__ int32_t warp_tot[32];
   __shared__ int32_t carry;
   if (threadIdx.x == 0) carry = 0;
@@ -577,7 +579,7 @@ __global__ void plan_tiles_kernel(const WispSegment* __restrict__ segs, int nseg
     if (s < nseg) {
       const int rows = segs[s].rows;
       bn = rows <= 16 ? 16 : rows <= 32 ? 32 : rows <= 64 ? 64 : 128;
-      n = rows > 0 ? ((rows + bn - 1) / bn) * mblocks : 0;
+      n = rows > skip_rows ? ((rows + bn - 1) / bn) * mblocks : 0;
       tiles[nseg + 1 + s] = bn;
     }
     int v = n;
@@ -606,6 +608,48 @@ __global__ void plan_tiles_kernel(const WispSegment* __restrict__ segs, int nseg
     __syncthreads();
   }
   if (threadIdx.x == 0) tiles[nseg] = carry;
+}
+
+// Units of the register-path kernel: `per_seg` per segment of 1..max_rows rows.
+__global__ void plan_units_kernel(const WispSegment* __restrict__ segs, int nseg, int per_seg,
+                                  int max_rows, int32_t* __restrict__ units) {
+  __shared__ int32_t warp_tot[32];
+  __shared__ int32_t carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  for (int base = 0; base < nseg; base += blockDim.x) {
+    const int s = base + threadIdx.x;
+    int n = 0;
+    if (s < nseg) {
+      const int rows = segs[s].rows;
+      n = (rows > 0 && rows <= max_rows) ? per_seg : 0;
+    }
+    int v = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += y;
+    }
+    if (lane == 31) warp_tot[w] = v;
+    __syncthreads();
+    if (w == 0) {
+      int tv = lane < (int)(blockDim.x >> 5) ? warp_tot[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, tv, o);
+        if (lane >= o) tv += y;
+      }
+      warp_tot[lane] = tv;
+    }
+    __syncthreads();
+    const int incl = v + (w > 0 ? warp_tot[w - 1] : 0) + carry;
+    if (s < nseg) units[s] = incl - n;
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = incl;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) units[nseg] = carry;
 }
 
 // Scales (and zero points) of every prepared matrix, transposed from
@@ -713,8 +757,32 @@ WispError check_shapes(const WispMoeConfig* cfg, WispErrCtx* err) {
 }
 
 unsigned long long* g_counters = nullptr;
+int g_skinny_rows = -1;  // -1: library default
 
 }  // namespace
+
+namespace wb {
+struct SkLaunch {
+  const uint8_t* prepared;
+  size_t p_flags, p_scales, p_zeros, p_mat_sc_bytes;
+  const WispInt4Expert* experts;
+  const WispSegment* segs;
+  int nseg;
+  const int32_t* units_gu;
+  const int32_t* units_dn;
+  int M, I, gs;
+  const __half* xp;
+  __half* h;
+  const int* row_token;
+  const float* row_weight;
+  float* out;
+  int mode;
+};
+int skinny_max_rows();
+void launch_skinny(const SkLaunch& L, int phase, cudaStream_t st);
+}  // namespace wb
+
+extern "C" void wisp_b200_set_skinny_max_rows(int rows) { g_skinny_rows = rows; }
 
 extern "C" void wisp_b200_debug_set_counters(unsigned long long* d_counters) {
   g_counters = d_counters;
@@ -774,17 +842,22 @@ extern "C" WispError wisp_b200_prepare_experts(const WispMoeConfig* cfg,
   return WISP_OK;
 }
 
-// Two tables (gate/up and down), each [prefix S+1 | bn S].
-extern "C" size_t wisp_b200_tiles_words(int n_segs) { return (size_t)(2 * (2 * n_segs + 1)); }
+// Tables: tensor-core gate/up and down [prefix S+1 | bn S] each, then the
+// register path's gate/up and down unit prefixes [S+1] each.
+extern "C" size_t wisp_b200_tiles_words(int n_segs) {
+  return (size_t)(2 * (2 * n_segs + 1) + 2 * (n_segs + 1));
+}
 
 extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void* d_prepared,
+                                           const WispInt4Expert* d_experts,
                                            int n_entries, const WispSegment* d_segs, int n_segs,
                                            int rows_capacity, const uint16_t* d_xp, uint16_t* d_h,
                                            int mode, const int* d_row_token,
                                            const float* d_row_weight, float* d_out,
                                            int32_t* d_tiles, int* d_error_flag,
                                            cudaStream_t stream, WispErrCtx* err) {
-  if (!cfg || !d_prepared || !d_segs || !d_xp || !d_h || !d_out || !d_tiles || n_entries <= 0)
+  if (!cfg || !d_prepared || !d_experts || !d_segs || !d_xp || !d_h || !d_out || !d_tiles ||
+      n_entries <= 0)
     return WB_FAIL(WISP_ERR_INVALID_ARG, "grouped_ffn: null pointer argument");
   WispError e = check_shapes(cfg, err);
   if (e != WISP_OK) return e;
@@ -830,10 +903,36 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
   dn.mode = mode;
 
   const size_t tw = (size_t)(2 * n_segs + 1);
+  const int sk_rows = g_skinny_rows >= 0 ? std::min(g_skinny_rows, wb::skinny_max_rows())
+                                         : wb::skinny_max_rows();
   gu.tiles = d_tiles;
   dn.tiles = d_tiles + tw;
-  plan_tiles_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, I / BM, d_tiles);
-  plan_tiles_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, M / BM, d_tiles + tw);
+  int32_t* units_gu = d_tiles + 2 * tw;
+  int32_t* units_dn = units_gu + (n_segs + 1);
+  plan_tiles_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, I / BM, sk_rows, d_tiles);
+  plan_tiles_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, M / BM, sk_rows, d_tiles + tw);
+  plan_units_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, I / 64, sk_rows, units_gu);
+  plan_units_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, M / 128, sk_rows, units_dn);
+  wb::SkLaunch sk;
+  sk.prepared = gu.prepared;
+  sk.p_flags = PL.flags;
+  sk.p_scales = PL.scales;
+  sk.p_zeros = PL.zeros;
+  sk.p_mat_sc_bytes = PL.mat_sc_bytes;
+  sk.experts = d_experts;
+  sk.segs = d_segs;
+  sk.nseg = n_segs;
+  sk.units_gu = units_gu;
+  sk.units_dn = units_dn;
+  sk.M = M;
+  sk.I = I;
+  sk.gs = gs;
+  sk.xp = reinterpret_cast<const __half*>(d_xp);
+  sk.h = reinterpret_cast<__half*>(d_h);
+  sk.row_token = d_row_token;
+  sk.row_weight = d_row_weight;
+  sk.out = d_out;
+  sk.mode = mode;
 
   const int grid = num_sms();
   const size_t sm_gu = smem_bytes<GATEUP>(), sm_dn = smem_bytes<DOWN>();
@@ -841,7 +940,9 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_gu));
   WB_CUDA_CHECK(cudaFuncSetAttribute(grouped_ffn_kernel<DOWN>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_dn));
+  if (sk_rows > 0) wb::launch_skinny(sk, 0, stream);
   grouped_ffn_kernel<GATEUP><<<grid, kThreads, sm_gu, stream>>>(gu);
+  if (sk_rows > 0) wb::launch_skinny(sk, 1, stream);
   grouped_ffn_kernel<DOWN><<<grid, kThreads, sm_dn, stream>>>(dn);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;

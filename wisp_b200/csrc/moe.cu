@@ -147,7 +147,8 @@ extern "C" WispError wisp_b200_moe_forward(const WispMoeConfig* cfg, const WispM
   if (e != WISP_OK) return e;
   WB_CUDA_CHECK(cudaMemsetAsync(d_out, 0, (size_t)cfg->tokens * cfg->hidden * sizeof(float), stream));
   WB_CUDA_CHECK(cudaMemsetAsync(ws.error_flag, 0, sizeof(int), stream));
-  return wisp_b200_grouped_ffn(cfg, w->prepared, V, ws.segs, V, ws.rows, ws.xp, ws.h, 0, ws.row_token,
+  if (!w->experts) return WB_FAIL(WISP_ERR_INVALID_ARG, "moe_forward: null expert table");
+  return wisp_b200_grouped_ffn(cfg, w->prepared, w->experts, V, ws.segs, V, ws.rows, ws.xp, ws.h, 0, ws.row_token,
                                ws.row_weight, d_out, ws.tiles, ws.error_flag, stream, err);
 }
 

@@ -91,7 +91,8 @@ class CudaOps:
 
     def grouped(self, cfg, lw, segs, rows, xp, h, mode, row_token, row_weight, out, tiles, flag):
         dsegs = _segments_tensor(segs, xp.device)
-        abi.call("wisp_b200_grouped_ffn", C.byref(cfg), lw.prepare().data_ptr(), lw.n_entries,
+        abi.call("wisp_b200_grouped_ffn", C.byref(cfg), lw.prepare().data_ptr(), lw.table.data_ptr(),
+                 lw.n_entries,
                  dsegs.data_ptr(), len(segs),
                  max(rows, 1), xp.data_ptr(), h.data_ptr(), mode,
                  None if row_token is None else row_token.data_ptr(),
