@@ -158,6 +158,18 @@ WispError wisp_b200_expert_ffn(const WispExpertMeta* meta, const void* const* d_
                                float* d_acc, void* d_scratch, size_t scratch_bytes,
                                cudaStream_t stream, WispErrCtx* err);
 
+/* The same computation for callers that cannot allocate device memory (an
+ * engine whose VRAM budget is fully committed to the expert cache, or a
+ * host callback where cudaMalloc would synchronise the device). No
+ * counterpart in the reference. The intermediate activations use a fixed
+ * 256 KB array per device compiled into the library, so n_blobs * inter must
+ * be <= 65536 (else WISP_ERR_INVALID_ARG). The first call on a device looks
+ * up that array's device address; make it before any stream capture. Calls
+ * share the array: calls that overlap on the GPU race on it. */
+WispError wisp_b200_expert_ffn_noalloc(const WispExpertMeta* meta, const void* const* d_blobs,
+                                       const float* weights, int n_blobs, const float* d_x,
+                                       float* d_acc, cudaStream_t stream, WispErrCtx* err);
+
 /* --------------------------------------------------------------------------
  * Batched MoE layer (T tokens, bf16 activations).
  * ------------------------------------------------------------------------ */

@@ -87,6 +87,8 @@ SIGNATURES = {
     "wisp_b200_expert_ffn_scratch_bytes": (_SZ, [C.POINTER(WispExpertMeta), _I]),
     "wisp_b200_expert_ffn": (_I, [C.POINTER(WispExpertMeta), C.POINTER(_P), C.POINTER(_F), _I,
                                   _P, _P, _P, _SZ, _P, _E]),
+    "wisp_b200_expert_ffn_noalloc": (_I, [C.POINTER(WispExpertMeta), C.POINTER(_P), C.POINTER(_F),
+                                          _I, _P, _P, _P, _E]),
     "wisp_b200_moe_workspace_bytes": (_SZ, [C.POINTER(WispMoeConfig)]),
     "wisp_b200_moe_forward": (_I, [C.POINTER(WispMoeConfig), C.POINTER(WispMoeWeights), _P, _P,
                                    _P, _P, _P, _SZ, _P, _E]),

@@ -16,6 +16,7 @@
 // the weighted combine is deterministic and needs no atomics.
 #include <algorithm>
 #include <cstdio>
+#include <mutex>
 
 #include "common.cuh"
 #include "internal.h"
@@ -281,4 +282,65 @@ extern "C" WispError wisp_b200_expert_ffn(const WispExpertMeta* meta, const void
   const cudaError_t ce = cudaGetLastError();
   if (ce != cudaSuccess) return WB_FAIL(WISP_ERR_CUDA, "expert_ffn launch: %s", cudaGetErrorString(ce));
   return WISP_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant.
+//
+// Some callers cannot call cudaMalloc: an engine whose VRAM budget is fully
+// committed to the expert tier cache (a new allocation there fails, or forces
+// evicting cached experts), or a host callback in a decode loop where a
+// cudaMalloc / cudaFree would implicitly synchronise the device. For them the
+// intermediate activations live in a fixed per-device array compiled into
+// this library: 65536 floats (256 KB), held by every GPU that loads the
+// library until the process exits. n_blobs * inter must fit in it.
+//
+// The array's host-side name is only a stand-in, so its device address is
+// looked up once per device (cudaGetSymbolAddress, with that device current)
+// on the first call made on that device; make that first call before any
+// stream capture. Every call shares the array: the gate/up kernel writes all
+// of the slots the down kernel reads, so nothing needs clearing, but calls
+// whose kernels overlap on the GPU (different streams, no ordering between
+// them) race on it.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr size_t kNoAllocScratchFloats = 65536;
+__device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {nullptr};
+}  // namespace
+
+extern "C" WispError wisp_b200_expert_ffn_noalloc(const WispExpertMeta* meta,
+                                                  const void* const* d_blobs,
+                                                  const float* weights, int n_blobs,
+                                                  const float* d_x, float* d_acc,
+                                                  cudaStream_t stream, WispErrCtx* err) {
+  if (!meta || !meta->valid) return WB_FAIL(WISP_ERR_INVALID_ARG, "expert_ffn_noalloc: invalid meta");
+  if (n_blobs < 1 || n_blobs > kMaxBlobs)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "expert_ffn_noalloc: n_blobs=%d (1..%d)", n_blobs, kMaxBlobs);
+  const size_t need = (size_t)n_blobs * meta->rows[0];
+  if (need > kNoAllocScratchFloats)
+    return WB_FAIL(WISP_ERR_INVALID_ARG,
+                   "expert_ffn_noalloc: n_blobs * inter = %zu exceeds the built-in scratch of %zu "
+                   "floats; use wisp_b200_expert_ffn with a caller buffer",
+                   need, kNoAllocScratchFloats);
+  int dev = -1;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess || dev < 0 || dev >= 64)
+    return WB_FAIL(WISP_ERR_CUDA, "expert_ffn_noalloc: cudaGetDevice: %s", cudaGetErrorString(ce));
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+      void* ptr = nullptr;
+      ce = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+      if (ce != cudaSuccess || !ptr)
+        return WB_FAIL(WISP_ERR_CUDA, "expert_ffn_noalloc: cudaGetSymbolAddress: %s",
+                       cudaGetErrorString(ce));
+      g_noalloc_addr[dev] = ptr;
+    }
+    scratch = g_noalloc_addr[dev];
+  }
+  return wisp_b200_expert_ffn(meta, d_blobs, weights, n_blobs, d_x, d_acc, scratch,
+                              kNoAllocScratchFloats * sizeof(float), stream, err);
 }
