@@ -308,10 +308,12 @@ WispError wisp_b200_check_error_flag(const int* d_error_flag, cudaStream_t strea
  * workspace (cleared at the start of every forward). */
 int* wisp_b200_moe_error_word(const WispMoeConfig* cfg, void* d_workspace);
 
-/* Diagnostics: when d_counters (2 x 15 uint64, zeroed by the caller) is
+/* Diagnostics: when d_counters (38 uint64, zeroed by the caller) is
  * non-NULL, the grouped kernels accumulate the clock cycles each role spends
- * in each of its waits (gate/up kernel in the first 15, down in the next).
- * Pass NULL to switch off. Not thread-safe; for profiling runs only. */
+ * in each of its waits: the tensor-core gate/up kernel in [0,15), its down
+ * kernel in [15,30), the register-path gate/up kernel in [30,34) and its
+ * down kernel in [34,38). Pass NULL to switch off. Not thread-safe; for
+ * profiling runs only. */
 void wisp_b200_debug_set_counters(unsigned long long* d_counters);
 
 /* Largest segment (rows) routed to the register-fed kernel; 0 sends every

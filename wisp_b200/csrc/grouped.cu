@@ -84,12 +84,14 @@ struct Shape {
   static constexpr int kBStages = MODE == GATEUP ? 5 : 3;
 };
 
-// Prepared weights: per matrix entry (expert v, matrix m in gate/up/down) a
-// TMA descriptor of its packed nibbles, a zero-point flag, and its scales and
-// zero points transposed to [row tile][group][128 rows] so that the scales
-// of one raw stage are one contiguous run.
+// Prepared weights: per matrix entry (expert v, matrix m in gate/up/down) two
+// TMA descriptors of its packed nibbles (64-byte boxes with the 64-byte
+// swizzle for this kernel, 128-byte boxes with the 128-byte swizzle for the
+// register-path kernel), a zero-point flag, and its scales and zero points transposed to
+// [row tile][group][128 rows] so that the scales of one stage are one
+// contiguous run.
 struct PreparedLayout {
-  size_t maps, flags, scales, zeros, mat_sc_bytes, total;
+  size_t maps, maps_sk, flags, scales, zeros, mat_sc_bytes, total;
 };
 
 PreparedLayout prepared_layout(const WispMoeConfig* c, int n) {
@@ -97,7 +99,8 @@ PreparedLayout prepared_layout(const WispMoeConfig* c, int n) {
   const size_t entries = (size_t)n * 3;
   L.mat_sc_bytes = (size_t)c->hidden * c->inter / c->group_size * 2;
   L.maps = 0;
-  L.flags = entries * sizeof(CUtensorMap);
+  L.maps_sk = entries * sizeof(CUtensorMap);
+  L.flags = L.maps_sk + entries * sizeof(CUtensorMap);
   L.scales = (L.flags + entries * 4 + 255) & ~(size_t)255;
   L.zeros = L.scales + entries * L.mat_sc_bytes;
   L.total = L.zeros + entries * L.mat_sc_bytes;
@@ -610,9 +613,10 @@ __global__ void plan_tiles_kernel(const WispSegment* __restrict__ segs, int nseg
   if (threadIdx.x == 0) tiles[nseg] = carry;
 }
 
-// Units of the register-path kernel: `per_seg` per segment of 1..max_rows rows.
+// Units of the register-path kernel: `per_seg` row blocks per chunk of `cols`
+// rows, for every segment of 1..max_rows rows.
 __global__ void plan_units_kernel(const WispSegment* __restrict__ segs, int nseg, int per_seg,
-                                  int max_rows, int32_t* __restrict__ units) {
+                                  int cols, int max_rows, int32_t* __restrict__ units) {
   __shared__ int32_t warp_tot[32];
   __shared__ int32_t carry;
   if (threadIdx.x == 0) carry = 0;
@@ -623,7 +627,7 @@ __global__ void plan_units_kernel(const WispSegment* __restrict__ segs, int nseg
     int n = 0;
     if (s < nseg) {
       const int rows = segs[s].rows;
-      n = (rows > 0 && rows <= max_rows) ? per_seg : 0;
+      n = (rows > 0 && rows <= max_rows) ? per_seg * ((rows + cols - 1) / cols) : 0;
     }
     int v = n;
 #pragma unroll
@@ -731,6 +735,21 @@ bool encode_packed_map(CUtensorMap* m, const void* base, int rows, int cols) {
          CUDA_SUCCESS;
 }
 
+// The same nibbles in 128-byte (256-K) x 128-row boxes with the 128-byte
+// swizzle, for the register-path kernel: a box row is one 128-byte request.
+bool encode_packed_map_sk(CUtensorMap* m, const void* base, int rows, int cols) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols / 2, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols / 2};
+  cuuint32_t box[2] = {128, (cuuint32_t)BM};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
 template <int MODE>
 size_t smem_bytes() {
   using S = Shape<MODE>;
@@ -764,22 +783,27 @@ int g_skinny_rows = -1;  // -1: library default
 namespace wb {
 struct SkLaunch {
   const uint8_t* prepared;
-  size_t p_flags, p_scales, p_zeros, p_mat_sc_bytes;
-  const WispInt4Expert* experts;
+  size_t p_maps_sk, p_flags, p_scales, p_zeros, p_mat_sc_bytes;
   const WispSegment* segs;
   int nseg;
   const int32_t* units_gu;
   const int32_t* units_dn;
   int M, I, gs;
-  const __half* xp;
+  const CUtensorMap* xp_maps;
+  const CUtensorMap* h_maps;
   __half* h;
   const int* row_token;
   const float* row_weight;
   float* out;
   int mode;
+  int* error_flag;
+  unsigned long long* counters;
 };
 int skinny_max_rows();
-void launch_skinny(const SkLaunch& L, int phase, cudaStream_t st);
+int skinny_cols();
+int skinny_units_gateup(int I);
+int skinny_units_down(int M);
+cudaError_t launch_skinny(const SkLaunch& L, int phase, int grid, cudaStream_t st);
 }  // namespace wb
 
 extern "C" void wisp_b200_set_skinny_max_rows(int rows) { g_skinny_rows = rows; }
@@ -811,7 +835,7 @@ extern "C" WispError wisp_b200_prepare_experts(const WispMoeConfig* cfg,
   WB_CUDA_CHECK(cudaMemcpyAsync(h.data(), d_experts, sizeof(WispInt4Expert) * n_entries,
                                 cudaMemcpyDeviceToHost, stream));
   WB_CUDA_CHECK(cudaStreamSynchronize(stream));
-  std::vector<CUtensorMap> maps((size_t)n_entries * 3);
+  std::vector<CUtensorMap> maps((size_t)n_entries * 3), maps_sk((size_t)n_entries * 3);
   std::vector<int32_t> flags((size_t)n_entries * 3);
   for (int v = 0; v < n_entries; v++) {
     const WispInt4Mat* mats[3] = {&h[v].gate, &h[v].up, &h[v].down};
@@ -823,7 +847,8 @@ extern "C" WispError wisp_b200_prepare_experts(const WispMoeConfig* cfg,
       if (((uintptr_t)mt.packed & 15) || ((uintptr_t)mt.scales & 1) || ((uintptr_t)mt.zeros & 1))
         return WB_FAIL(WISP_ERR_INVALID_ARG,
                        "prepare_experts: entry %d matrix %d: packed must be 16-byte aligned", v, m);
-      if (!encode_packed_map(&maps[(size_t)v * 3 + m], mt.packed, rows, cols))
+      if (!encode_packed_map(&maps[(size_t)v * 3 + m], mt.packed, rows, cols) ||
+          !encode_packed_map_sk(&maps_sk[(size_t)v * 3 + m], mt.packed, rows, cols))
         return WB_FAIL(WISP_ERR_CUDA, "prepare_experts: cuTensorMapEncodeTiled failed (entry %d)", v);
       flags[(size_t)v * 3 + m] = mt.zeros ? 1 : 0;
     }
@@ -831,6 +856,9 @@ extern "C" WispError wisp_b200_prepare_experts(const WispMoeConfig* cfg,
   uint8_t* base = static_cast<uint8_t*>(d_prepared);
   WB_CUDA_CHECK(cudaMemcpyAsync(base + PL.maps, maps.data(), maps.size() * sizeof(CUtensorMap),
                                 cudaMemcpyHostToDevice, stream));
+  WB_CUDA_CHECK(cudaMemcpyAsync(base + PL.maps_sk, maps_sk.data(),
+                                maps_sk.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice,
+                                stream));
   WB_CUDA_CHECK(cudaMemcpyAsync(base + PL.flags, flags.data(), flags.size() * 4,
                                 cudaMemcpyHostToDevice, stream));
   dim3 grid(64, n_entries * 3);
@@ -911,15 +939,24 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
   int32_t* units_dn = units_gu + (n_segs + 1);
   plan_tiles_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, I / BM, sk_rows, d_tiles);
   plan_tiles_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, M / BM, sk_rows, d_tiles + tw);
-  plan_units_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, I / 64, sk_rows, units_gu);
-  plan_units_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, M / 128, sk_rows, units_dn);
+  const int skc = wb::skinny_cols();
+  plan_units_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, wb::skinny_units_gateup(I), skc,
+                                            sk_rows, units_gu);
+  plan_units_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, wb::skinny_units_down(M), skc,
+                                            sk_rows, units_dn);
+  CUtensorMap sk_xp[3], sk_h[3];
+  for (int i = 0; i < 3; i++) {
+    if (!encode_rows_map(&sk_xp[i], d_xp, rows_capacity, M, 8 << i) ||
+        !encode_rows_map(&sk_h[i], d_h, rows_capacity, I, 8 << i))
+      return WB_FAIL(WISP_ERR_CUDA, "grouped_ffn: cuTensorMapEncodeTiled failed (token rows)");
+  }
   wb::SkLaunch sk;
   sk.prepared = gu.prepared;
+  sk.p_maps_sk = PL.maps_sk;
   sk.p_flags = PL.flags;
   sk.p_scales = PL.scales;
   sk.p_zeros = PL.zeros;
   sk.p_mat_sc_bytes = PL.mat_sc_bytes;
-  sk.experts = d_experts;
   sk.segs = d_segs;
   sk.nseg = n_segs;
   sk.units_gu = units_gu;
@@ -927,12 +964,17 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
   sk.M = M;
   sk.I = I;
   sk.gs = gs;
-  sk.xp = reinterpret_cast<const __half*>(d_xp);
+  sk.xp_maps = sk_xp;
+  sk.h_maps = sk_h;
   sk.h = reinterpret_cast<__half*>(d_h);
   sk.row_token = d_row_token;
   sk.row_weight = d_row_weight;
   sk.out = d_out;
   sk.mode = mode;
+  sk.error_flag = d_error_flag;
+  // diagnostics: the register-path kernel's counters follow the two
+  // tensor-core kernels' blocks
+  sk.counters = g_counters ? g_counters + 2 * C_COUNT : nullptr;
 
   const int grid = num_sms();
   const size_t sm_gu = smem_bytes<GATEUP>(), sm_dn = smem_bytes<DOWN>();
@@ -940,9 +982,9 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_gu));
   WB_CUDA_CHECK(cudaFuncSetAttribute(grouped_ffn_kernel<DOWN>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_dn));
-  if (sk_rows > 0) wb::launch_skinny(sk, 0, stream);
+  if (sk_rows > 0) WB_CUDA_CHECK(wb::launch_skinny(sk, 0, grid, stream));
   grouped_ffn_kernel<GATEUP><<<grid, kThreads, sm_gu, stream>>>(gu);
-  if (sk_rows > 0) wb::launch_skinny(sk, 1, stream);
+  if (sk_rows > 0) WB_CUDA_CHECK(wb::launch_skinny(sk, 1, grid, stream));
   grouped_ffn_kernel<DOWN><<<grid, kThreads, sm_dn, stream>>>(dn);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;

@@ -1,24 +1,43 @@
 // skinny.cu -- grouped int4 expert FFN for small token groups (decode).
 //
-// When an expert sees at most 16 tokens (batch decode: ~5 per expert in the
+// When an expert sees a few tokens (batch decode: ~5 per expert in the
 // 256-token / 384-expert configuration), the work per weight is one int4
-// conversion plus a handful of multiply-adds. A tcgen05.mma (M=128, K=16)
+// conversion plus a handful of multiply-adds, and the kernel's only job is
+// to stream the packed weights at HBM speed. A tcgen05.mma (M=128, K=16)
 // costs a fixed ~60-95 SM cycles whatever N <= 128 is (measured on B200), so
-// at N <= 16 the 5th-generation path tops out near 2048 weights per ~60
-// cycles per SM. This kernel keeps the dequantised operand in registers:
-// every warp streams its own weight rows from HBM, converts each 32-bit word
-// of nibbles to exact (n - 8) fp16 pairs, and feeds them as A fragments to
-// m16n8k16 tensor-core MMAs (~1.6 per cycle per SM) against the tokens' B
-// fragments, accumulating fp32 per 64-K half group and applying the group's
-// scale (and zero point) to the fp32 partial sums. No shared memory, no
-// cross-warp synchronisation.
+// at small N the 5th-generation path tops out far below HBM speed; this
+// kernel feeds m16n8k16 tensor-core MMAs (~1.6 per cycle per SM) from
+// registers instead.
 //
-// Work unit = (segment, row block); 4 warps per unit:
-//   GATEUP: 64 intermediate rows i, each warp 16 gate rows + the same 16 up
-//           rows -> h = silu(g) * u written to H (fp16, interleaved K order).
-//   DOWN:   128 output rows m, each warp 32 rows -> out[token] += w * y
-//           (mode 0, fp32 atomics) or y rows (mode 1).
-// Segments with more than 16 rows are left to the tcgen05 kernel.
+// One persistent CTA per SM, warp-specialised:
+//   warp 8      producer: per 256-K stage, one TMA box of packed nibbles per
+//               128-row weight block (128 rows x 128 bytes, 128-byte
+//               swizzle: a box row is one 128-byte request; narrower boxes
+//               left the TMA unit, not HBM, as the limit), one TMA box per
+//               64-K quarter of the unit's token rows (fp16, 128-byte
+//               swizzle), and bulk copies of the stage's scales (and zero
+//               points) from the prepared tile-transposed copy, into a
+//               4-deep shared-memory ring (53 KB per stage, up to 96 KB of
+//               weights in flight per SM).
+//   warps 0-7   consumers: each takes two 16-row tiles; per 64-K quarter it
+//               reads its nibbles (conflict-free 8-byte loads: MMA row g
+//               lives in box row sigma(g) = 2(g%4) + g/4, so each
+//               half-warp's rows fall in distinct swizzle chunks) and the
+//               tokens' B fragments (conflict-free 16-byte loads), converts
+//               each 32-bit word of nibbles to exact (n - 8) fp16 pairs,
+//               runs the MMAs, and applies the group's scale (and zero
+//               point) to the fp32 partial sums. The stage is released once
+//               its last quarter has been read.
+//
+// Work unit = (segment, weight row block, chunk of up to 32 tokens):
+//   GATEUP: 128 intermediate rows i of gate and of up; warp w takes rows
+//           16w..16w+15 of both -> h = silu(g) * u written to H (fp16,
+//           interleaved K order).
+//   DOWN:   256 output rows m (two 128-row blocks); warp w takes 32 rows ->
+//           out[token] += w * y (mode 0, fp32 atomics) or y rows (mode 1).
+// Chunks of one row block are consecutive units, so CTAs that run them at
+// the same time share the weight tile through L2. Segments larger than the
+// routing threshold go to the tcgen05 kernel.
 //
 // Fragment mapping. m16n8k16 gives thread (g = lane/4, t = lane%4) the A
 // pairs (row g, k 2t..2t+1), (row g+8, same), (row g, k 2t+8..2t+9),
@@ -38,25 +57,61 @@ using namespace wb;
 
 namespace {
 
-constexpr int kSkMaxRows = 16;
-constexpr int kSkWarps = 4;
+constexpr int kCW = 8;                        // consumer warps
+constexpr int kThreads = (kCW + 1) * 32;      // + one producer warp
+constexpr int kStages = 4;
+constexpr int kCols = 32;                     // tokens per unit
+constexpr int kSkMaxRows = 256;               // default routing threshold
+constexpr int kKS = 256;                      // K per stage
+constexpr int kQ = kKS / 64;                  // 64-K quarters per stage
+constexpr int kBoxRows = 128;
+constexpr int kBoxBytes = kBoxRows * 128;     // one weight block of a stage
+constexpr int kBQBytes = kCols * 128;         // one 64-K quarter of 32 token rows
+constexpr int kScRun = 4 * kBoxRows * 2;      // up to 4 scale groups x 128 rows
+// Stage layout (bytes): [weights 2 blocks][tokens 4 quarters]
+// [scales 2 blocks][zeros 2 blocks][header].
+constexpr int kOffB = 2 * kBoxBytes;
+constexpr int kOffS = kOffB + kQ * kBQBytes;
+constexpr int kOffZ = kOffS + 2 * kScRun;
+constexpr int kOffH = kOffZ + 2 * kScRun;
+constexpr int kStageBytes = (kOffH + 64 + 1023) / 1024 * 1024;
 enum { SK_GATEUP = 0, SK_DOWN = 1 };
+enum { HF_HZ0 = 1, HF_HZ1 = 2, HF_V1 = 4 };
+
+struct __align__(16) StageHdr {
+  int prow0;  // first activation row of the unit
+  int n;      // tokens in the unit (1..32)
+  int row0;   // first weight row of the unit
+  int flags;  // HF_*: zero points of block 0 / 1, block 1 inside the matrix
+};
+
+struct SkSmem {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  int abort;
+};
 
 struct SkParams {
+  CUtensorMap act_map[3];  // token rows, boxes {64 halves, 8/16/32 rows}, 128-byte swizzle
   const uint8_t* prepared;
-  size_t p_flags, p_scales, p_zeros, p_mat_sc_bytes;
-  const WispInt4Expert* experts;   // packed nibble pointers
+  size_t p_maps_sk, p_flags, p_scales, p_zeros, p_mat_sc_bytes;
   const WispSegment* segs;
-  const int32_t* units;            // [0,S]: unit prefix (no units for large segments)
+  const int32_t* units;  // [0, S]: unit prefix per segment
   int nseg;
   int M, I, gs;
-  const __half* act;               // GATEUP: Xp rows [R x M]; DOWN: H rows [R x I]
-  __half* h_out;                   // GATEUP output
+  __half* h_out;
   const int* row_token;
   const float* row_weight;
   float* out;
   int mode;
+  int* error_flag;
+  unsigned long long* counters;  // optional wait-cycle counters (diagnostics)
 };
+
+// Diagnostic counters (cycles summed over warps): consumers' waits for a
+// full stage and their total time, the producer's waits for a free stage
+// and its total time.
+enum { SC_FULL_WAIT, SC_CONS_TOTAL, SC_EMPTY_WAIT, SC_PROD_TOTAL, SC_COUNT };
 
 __device__ __forceinline__ void hmma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                           uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -67,244 +122,427 @@ __device__ __forceinline__ void hmma16816(float (&c)[4], uint32_t a0, uint32_t a
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint2 ldg_stream_64(const void* p) {
-  uint2 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
-               : "=r"(v.x), "=r"(v.y) : "l"(p));
-  return v;
+// Waits without the abort shortcut: used to let issued copies land before
+// the CTA exits.
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, long long limit) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity))
+    if (clock64() - t0 > limit) return;
 }
 
-__device__ __forceinline__ int find_seg(const int32_t* pre, int nseg, int unit) {
-  int lo = 0, hi = nseg - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (__ldg(pre + mid) <= unit) lo = mid; else hi = mid - 1;
-  }
-  return lo;
-}
-
-// The packed words of one 16-row tile this thread needs for one 128-K group:
-// rows g and g+8, both 64-K halves (2 words each).
+// Nibbles of one 16-row tile for one 64-K quarter: rows g and g+8.
 struct RawTile {
-  uint2 w[2][2];  // [half][row g / g+8]
+  uint2 w[2];  // [row g / g+8]
 };
 
-__device__ __forceinline__ void load_tile(RawTile& r, const uint8_t* packed, int row0,
-                                          int kbytes_row, int kg, int g, int t) {
-  const uint8_t* p0 = packed + (size_t)(row0 + g) * kbytes_row + kg * 64 + 8 * t;
-  const uint8_t* p8 = p0 + (size_t)8 * kbytes_row;
-  r.w[0][0] = ldg_stream_64(p0);
-  r.w[0][1] = ldg_stream_64(p8);
-  r.w[1][0] = ldg_stream_64(p0 + 32);
-  r.w[1][1] = ldg_stream_64(p8 + 32);
-}
-
-// Activation words of one 128-K group for token column g of each n8 tile:
-// [half][word 2t / 2t+1][nt]; zero for columns beyond the segment.
+// Token words of one 64-K quarter: [word 2t / 2t+1][n8 tile].
 template <int NT>
-struct BFrag {
-  uint4 v[2][2][NT];
+struct BHalf {
+  uint4 v[2][NT];
 };
-
-template <int NT>
-__device__ __forceinline__ void load_b(BFrag<NT>& b, const __half* const (&rows)[NT],
-                                       const bool (&valid)[NT], int kg, int t) {
-#pragma unroll
-  for (int nt = 0; nt < NT; nt++) {
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-      const uint4* src = reinterpret_cast<const uint4*>(rows[nt] + kg * 128 + h * 64 + 16 * t);
-      b.v[h][0][nt] = valid[nt] ? __ldg(src) : make_uint4(0, 0, 0, 0);
-      b.v[h][1][nt] = valid[nt] ? __ldg(src + 1) : make_uint4(0, 0, 0, 0);
-    }
-  }
-}
 
 __device__ __forceinline__ uint32_t u4_get(const uint4& v, int i) {
   return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }
 
-// acc[nt] += s * (A x B) for one 16-row tile over one 128-K group; scales
-// per half group and row (g, g+8).
+// acc[nt] += s * (A x B) for one 16-row tile over one 64-K quarter; scales
+// of rows g (sg) and g+8 (s8).
 template <int NT>
-__device__ __forceinline__ void tile_group(float (&acc)[NT][4], const RawTile& w,
-                                           const BFrag<NT>& b, const float (&sg)[2],
-                                           const float (&s8)[2]) {
-#pragma unroll
-  for (int h = 0; h < 2; h++) {
-    __half2 ag[2][4], a8[2][4];
-    nib8_centered(w.w[h][0].x, ag[0]);
-    nib8_centered(w.w[h][0].y, ag[1]);
-    nib8_centered(w.w[h][1].x, a8[0]);
-    nib8_centered(w.w[h][1].y, a8[1]);
-    float ct[NT][4];
-#pragma unroll
-    for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-      for (int q = 0; q < 4; q++) ct[nt][q] = 0.f;
-#pragma unroll
-    for (int m = 0; m < 4; m++) {
-      const int wd = m >> 1, p = 2 * (m & 1);
-      const uint32_t a0 = h22u(ag[wd][p]), a2 = h22u(ag[wd][p + 1]);
-      const uint32_t a1 = h22u(a8[wd][p]), a3 = h22u(a8[wd][p + 1]);
-#pragma unroll
-      for (int nt = 0; nt < NT; nt++)
-        hmma16816(ct[nt], a0, a1, a2, a3, u4_get(b.v[h][wd][nt], p), u4_get(b.v[h][wd][nt], p + 1));
-    }
-#pragma unroll
-    for (int nt = 0; nt < NT; nt++) {
-      acc[nt][0] = fmaf(sg[h], ct[nt][0], acc[nt][0]);
-      acc[nt][1] = fmaf(sg[h], ct[nt][1], acc[nt][1]);
-      acc[nt][2] = fmaf(s8[h], ct[nt][2], acc[nt][2]);
-      acc[nt][3] = fmaf(s8[h], ct[nt][3], acc[nt][3]);
-    }
-  }
-}
-
-// Zero points: acc[row, col] += z[row] * sum_k x[col, k] over each half
-// group. xs[h][nt][j]: activation sum of column 2t+j of tile nt.
-template <int NT>
-__device__ __forceinline__ void half_sums(const BFrag<NT>& b, float (&xs)[2][NT][2], int t) {
-#pragma unroll
-  for (int h = 0; h < 2; h++)
-#pragma unroll
-    for (int nt = 0; nt < NT; nt++) {
-      float s = 0.f;
-#pragma unroll
-      for (int wd = 0; wd < 2; wd++) {
-        const uint4 v = b.v[h][wd][nt];
-        const uint32_t e[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const float2 f = __half22float2(u2h2(e[i]));
-          s += f.x + f.y;
-        }
-      }
-      // the quad (same column g, t = 0..3) holds the 64 K of the half
-      s += __shfl_xor_sync(0xffffffffu, s, 1);
-      s += __shfl_xor_sync(0xffffffffu, s, 2);
-      // column 2t+j lives in quad 2t+j
-      xs[h][nt][0] = __shfl_sync(0xffffffffu, s, (2 * t) * 4);
-      xs[h][nt][1] = __shfl_sync(0xffffffffu, s, (2 * t + 1) * 4);
-    }
-}
-
-template <int NT>
-__device__ __forceinline__ void add_zeros(float (&acc)[NT][4], const float (&xs)[2][NT][2],
-                                          const float (&zg)[2], const float (&z8)[2]) {
-#pragma unroll
-  for (int h = 0; h < 2; h++)
-#pragma unroll
-    for (int nt = 0; nt < NT; nt++) {
-      acc[nt][0] = fmaf(zg[h], xs[h][nt][0], acc[nt][0]);
-      acc[nt][1] = fmaf(zg[h], xs[h][nt][1], acc[nt][1]);
-      acc[nt][2] = fmaf(z8[h], xs[h][nt][0], acc[nt][2]);
-      acc[nt][3] = fmaf(z8[h], xs[h][nt][1], acc[nt][3]);
-    }
-}
-
-// Scale (or zero point) of rows (row, row+8) for both half groups of group kg,
-// from the prepared tile-transposed copy [tile][group][128 rows].
-__device__ __forceinline__ void group_scales(const __half* st, int gpr, int gs, int row, int kg,
-                                             float (&a)[2], float (&b)[2]) {
-  const int tile = row >> 7, r = row & 127;
-#pragma unroll
-  for (int h = 0; h < 2; h++) {
-    const int grp = (kg * 128 + h * 64) / gs;
-    const __half* base = st + ((size_t)tile * gpr + grp) * 128;
-    a[h] = __half2float(base[r]);
-    b[h] = __half2float(base[r + 8]);
-  }
-}
-
-template <int MODE, int NT>
-__device__ void sk_unit(const SkParams& p, const WispSegment& sg, int rb, int warp, int lane) {
-  const int g = lane >> 2, t = lane & 3;
-  const int K = MODE == SK_GATEUP ? p.M : p.I;
-  const int ngroups = K / 128;
-  const int gpr = K / p.gs;
-  const int kbytes_row = K / 2;
-  const int n = sg.rows;
-  const WispInt4Expert ex = p.experts[sg.expert];
-  const int32_t* flags = reinterpret_cast<const int32_t*>(p.prepared + p.p_flags);
-  const int e3 = sg.expert * 3;
-
-  const __half* rows[NT];
-  bool valid[NT];
-#pragma unroll
-  for (int nt = 0; nt < NT; nt++) {
-    const int tok = nt * 8 + g;
-    valid[nt] = tok < n;
-    rows[nt] = p.act + (size_t)(sg.row_begin + (valid[nt] ? tok : 0)) * K;
-  }
-
-  // Two 16-row tiles per warp: GATEUP: (gate, up) of rows i0..i0+15;
-  // DOWN: rows m0..m0+15 and m0+16..m0+31.
-  const int r0 = MODE == SK_GATEUP ? rb * 64 + warp * 16 : rb * 128 + warp * 32;
-  const int r1 = MODE == SK_GATEUP ? r0 : r0 + 16;
-  const uint8_t* pk0 = MODE == SK_GATEUP ? ex.gate.packed : ex.down.packed;
-  const uint8_t* pk1 = MODE == SK_GATEUP ? ex.up.packed : ex.down.packed;
-  const int m0 = MODE == SK_GATEUP ? 0 : 2, m1 = MODE == SK_GATEUP ? 1 : 2;
-  const __half* sc0 = reinterpret_cast<const __half*>(p.prepared + p.p_scales + (size_t)(e3 + m0) * p.p_mat_sc_bytes);
-  const __half* sc1 = reinterpret_cast<const __half*>(p.prepared + p.p_scales + (size_t)(e3 + m1) * p.p_mat_sc_bytes);
-  const bool hz0 = __ldg(flags + e3 + m0) & 1, hz1 = __ldg(flags + e3 + m1) & 1;
-  const __half* zr0 = reinterpret_cast<const __half*>(p.prepared + p.p_zeros + (size_t)(e3 + m0) * p.p_mat_sc_bytes);
-  const __half* zr1 = reinterpret_cast<const __half*>(p.prepared + p.p_zeros + (size_t)(e3 + m1) * p.p_mat_sc_bytes);
-
-  float acc0[NT][4], acc1[NT][4];
+__device__ __forceinline__ void tile_quarter(float (&acc)[4][4], const RawTile& w,
+                                             const BHalf<NT>& b, float sg, float s8) {
+  __half2 ag[2][4], a8[2][4];
+  nib8_centered(w.w[0].x, ag[0]);
+  nib8_centered(w.w[0].y, ag[1]);
+  nib8_centered(w.w[1].x, a8[0]);
+  nib8_centered(w.w[1].y, a8[1]);
+  float ct[NT][4];
 #pragma unroll
   for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-    for (int q = 0; q < 4; q++) acc0[nt][q] = acc1[nt][q] = 0.f;
+    for (int q = 0; q < 4; q++) ct[nt][q] = 0.f;
+#pragma unroll
+  for (int m = 0; m < 4; m++) {
+    const int wd = m >> 1, p = 2 * (m & 1);
+    const uint32_t a0 = h22u(ag[wd][p]), a2 = h22u(ag[wd][p + 1]);
+    const uint32_t a1 = h22u(a8[wd][p]), a3 = h22u(a8[wd][p + 1]);
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+      hmma16816(ct[nt], a0, a1, a2, a3, u4_get(b.v[wd][nt], p), u4_get(b.v[wd][nt], p + 1));
+  }
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++) {
+    acc[nt][0] = fmaf(sg, ct[nt][0], acc[nt][0]);
+    acc[nt][1] = fmaf(sg, ct[nt][1], acc[nt][1]);
+    acc[nt][2] = fmaf(s8, ct[nt][2], acc[nt][2]);
+    acc[nt][3] = fmaf(s8, ct[nt][3], acc[nt][3]);
+  }
+}
 
-  RawTile nx0, nx1;
-  load_tile(nx0, pk0, r0, kbytes_row, 0, g, t);
-  load_tile(nx1, pk1, r1, kbytes_row, 0, g, t);
-  for (int kg = 0; kg < ngroups; kg++) {
-    const RawTile w0 = nx0, w1 = nx1;
-    if (kg + 1 < ngroups) {
-      load_tile(nx0, pk0, r0, kbytes_row, kg + 1, g, t);
-      load_tile(nx1, pk1, r1, kbytes_row, kg + 1, g, t);
+// Zero points: acc[row, col] += z[row] * sum_k x[col, k] over the 64-K
+// quarter. xs[nt][j]: activation sum of column 2t+j of tile nt.
+template <int NT>
+__device__ __forceinline__ void half_sums(const BHalf<NT>& b, float (&xs)[NT][2], int t) {
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++) {
+    float s = 0.f;
+#pragma unroll
+    for (int wd = 0; wd < 2; wd++) {
+      const uint4 v = b.v[wd][nt];
+      const uint32_t e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const float2 f = __half22float2(u2h2(e[i]));
+        s += f.x + f.y;
+      }
     }
-    BFrag<NT> b;
-    load_b<NT>(b, rows, valid, kg, t);
-    float sa[2], sb[2], sc[2], sd[2];
-    group_scales(sc0, gpr, p.gs, r0 + g, kg, sa, sb);
-    group_scales(sc1, gpr, p.gs, r1 + g, kg, sc, sd);
-    tile_group<NT>(acc0, w0, b, sa, sb);
-    tile_group<NT>(acc1, w1, b, sc, sd);
-    if (hz0 | hz1) {
-      float xs[2][NT][2];
-      half_sums<NT>(b, xs, t);
-      if (hz0) {
-        float za[2], zb[2];
-        group_scales(zr0, gpr, p.gs, r0 + g, kg, za, zb);
-        add_zeros<NT>(acc0, xs, za, zb);
+    // the quad (same column g, t = 0..3) holds the 64 K of the quarter
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    // column 2t+j lives in quad 2t+j
+    xs[nt][0] = __shfl_sync(0xffffffffu, s, (2 * t) * 4);
+    xs[nt][1] = __shfl_sync(0xffffffffu, s, (2 * t + 1) * 4);
+  }
+}
+
+template <int NT>
+__device__ __forceinline__ void add_zeros(float (&acc)[4][4], const float (&xs)[NT][2], float zg,
+                                          float z8) {
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++) {
+    acc[nt][0] = fmaf(zg, xs[nt][0], acc[nt][0]);
+    acc[nt][1] = fmaf(zg, xs[nt][1], acc[nt][1]);
+    acc[nt][2] = fmaf(z8, xs[nt][0], acc[nt][2]);
+    acc[nt][3] = fmaf(z8, xs[nt][1], acc[nt][3]);
+  }
+}
+
+// Scale (or zero point) of rows (row, row+8) for scale group grp from the
+// stage's [group][128 rows] run.
+__device__ __forceinline__ void group_pair(const uint8_t* run, int grp, int row, float& a,
+                                           float& b) {
+  const __half* s = reinterpret_cast<const __half*>(run) + grp * kBoxRows;
+  a = __half2float(s[row]);
+  b = __half2float(s[row + 8]);
+}
+
+// The same pair as fp16 (low: row, high: row+8).
+__device__ __forceinline__ __half2 group_pair_h2(const uint8_t* run, int grp, int row) {
+  const __half* s = reinterpret_cast<const __half*>(run) + grp * kBoxRows;
+  return __halves2half2(s[row], s[row + 8]);
+}
+
+// Rows srow and srow+8 (srow = tile base + sigma(g)) of a weight block,
+// 64-K quarter q: thread t reads bytes 8t..8t+7 of the quarter's 32 bytes,
+// i.e. 16-byte chunk 2q + t/2, stored at chunk ^ (srow & 7).
+__device__ __forceinline__ void load_tile(RawTile& r, const uint8_t* st, int block, int srow,
+                                          int q, int t) {
+  const int chunk = (2 * q + (t >> 1)) ^ (srow & 7);
+  const uint8_t* a = st + block * kBoxBytes + srow * 128 + (chunk << 4) + 8 * (t & 1);
+  r.w[0] = *reinterpret_cast<const uint2*>(a);
+  r.w[1] = *reinterpret_cast<const uint2*>(a + 8 * 128);
+}
+
+// Token row r's 16-byte chunk c of a 64-K quarter: the 128-byte swizzle puts
+// it at chunk c ^ (r & 7).
+template <int NT>
+__device__ __forceinline__ void load_b(BHalf<NT>& b, const uint8_t* st, int q, int g, int t) {
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++) {
+    const int r = nt * 8 + g;
+    const uint8_t* row = st + kOffB + q * kBQBytes + r * 128;
+#pragma unroll
+    for (int wd = 0; wd < 2; wd++)
+      b.v[wd][nt] = *reinterpret_cast<const uint4*>(row + (((2 * t + wd) ^ (r & 7)) << 4));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Producer warp.
+// ---------------------------------------------------------------------------
+template <int MODE>
+__device__ void sk_producer(const SkParams& p, uint8_t* ring, SkSmem* L, int total, int lane) {
+  volatile int* abort = &L->abort;
+  const int K = MODE == SK_GATEUP ? p.M : p.I;
+  const int nk = (K + kKS - 1) / kKS;
+  const int gpr = K / p.gs;
+  const int32_t* flags = reinterpret_cast<const int32_t*>(p.prepared + p.p_flags);
+  if (lane < 3) tma_prefetch_desc(&p.act_map[lane]);
+  int slot = 0, item = 0;
+  uint32_t phase = 0;
+  int seg = 0;
+  const long long t_start = p.counters ? clock64() : 0;
+  long long wait_cycles = 0;
+  bool ok = true;
+  for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+    while (__ldg(p.units + seg + 1) <= u) seg++;
+    const WispSegment sg = p.segs[seg];
+    const int chunks = (sg.rows + kCols - 1) / kCols;
+    const int l = u - __ldg(p.units + seg);
+    const int rb = l / chunks, ch = l - rb * chunks;
+    const int col0 = ch * kCols;
+    const int n = min(kCols, sg.rows - col0);
+    const int mi = n <= 8 ? 0 : n <= 16 ? 1 : 2;  // token box of 8 / 16 / 32 rows
+    const uint32_t bq = (8u << mi) * 128;        // bytes of one token quarter box
+    const int row0 = rb * (MODE == SK_GATEUP ? kBoxRows : 2 * kBoxRows);
+    const int row1 = MODE == SK_GATEUP ? row0 : row0 + kBoxRows;
+    const bool v1 = MODE == SK_GATEUP || row1 < p.M;
+    const int e0 = sg.expert * 3 + (MODE == SK_GATEUP ? 0 : 2);
+    const int e1 = MODE == SK_GATEUP ? e0 + 1 : e0;
+    const bool hz0 = __ldg(flags + e0) & 1;
+    const bool hz1 = v1 && (__ldg(flags + e1) & 1);
+    const CUtensorMap* map0 =
+        reinterpret_cast<const CUtensorMap*>(p.prepared + p.p_maps_sk + (size_t)e0 * sizeof(CUtensorMap));
+    const CUtensorMap* map1 =
+        reinterpret_cast<const CUtensorMap*>(p.prepared + p.p_maps_sk + (size_t)e1 * sizeof(CUtensorMap));
+    const size_t t0off = (size_t)(row0 / kBoxRows) * gpr * kBoxRows * 2;
+    const size_t t1off = (size_t)(row1 / kBoxRows) * gpr * kBoxRows * 2;
+    const uint8_t* sc0 = p.prepared + p.p_scales + (size_t)e0 * p.p_mat_sc_bytes + t0off;
+    const uint8_t* sc1 = p.prepared + p.p_scales + (size_t)e1 * p.p_mat_sc_bytes + t1off;
+    const uint8_t* zr0 = p.prepared + p.p_zeros + (size_t)e0 * p.p_mat_sc_bytes + t0off;
+    const uint8_t* zr1 = p.prepared + p.p_zeros + (size_t)e1 * p.p_mat_sc_bytes + t1off;
+    StageHdr hdr;
+    hdr.prow0 = sg.row_begin + col0;
+    hdr.n = n;
+    hdr.row0 = row0;
+    hdr.flags = (hz0 ? HF_HZ0 : 0) | (hz1 ? HF_HZ1 : 0) | (v1 ? HF_V1 : 0);
+    if (lane == 0) {
+      tma_prefetch_desc(map0);
+      if (MODE == SK_GATEUP) tma_prefetch_desc(map1);
+    }
+    for (int kg = 0; kg < nk; kg++, item++) {
+      // quarters in this stage (the last one holds 2 when K % 256 == 128)
+      const int nq = min(kQ, (K - kg * kKS) / 64);
+      const uint32_t scb = (uint32_t)(nq * 64 / p.gs) * kBoxRows * 2;
+      const uint32_t bytes = (v1 ? 2 : 1) * kBoxBytes + nq * bq +
+                             scb * (1 + (v1 ? 1 : 0) + (hz0 ? 1 : 0) + (hz1 ? 1 : 0));
+      if (lane == 0 && item >= kStages) {
+        const long long tw = p.counters ? clock64() : 0;
+        ok = mbar_wait(&L->empty[slot], phase ^ 1, abort);
+        if (p.counters) wait_cycles += clock64() - tw;
       }
-      if (hz1) {
-        float za[2], zb[2];
-        group_scales(zr1, gpr, p.gs, r1 + g, kg, za, zb);
-        add_zeros<NT>(acc1, xs, za, zb);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      uint8_t* st = ring + slot * kStageBytes;
+      uint64_t* fb = &L->full[slot];
+      if (lane == 0) {
+        *reinterpret_cast<StageHdr*>(st + kOffH) = hdr;
+        mbar_arrive_expect_tx(fb, bytes);
       }
+      __syncwarp();
+      const size_t goff = (size_t)(kg * kKS / p.gs) * kBoxRows * 2;
+      if (lane < 2) {
+        if (lane == 0 || v1)
+          tma_load_2d(st + lane * kBoxBytes, lane ? map1 : map0, fb, kg * (kKS / 2),
+                      lane ? row1 : row0);
+      } else if (lane < 2 + kQ) {
+        const int q = lane - 2;
+        if (q < nq)
+          tma_load_2d(st + kOffB + q * kBQBytes, &p.act_map[mi], fb, kg * kKS + q * 64, hdr.prow0);
+      } else if (lane == 2 + kQ) {
+        bulk_load(st + kOffS, sc0 + goff, scb, fb);
+        if (v1) bulk_load(st + kOffS + kScRun, sc1 + goff, scb, fb);
+      } else if (lane == 3 + kQ) {
+        if (hz0) bulk_load(st + kOffZ, zr0 + goff, scb, fb);
+        if (hz1) bulk_load(st + kOffZ + kScRun, zr1 + goff, scb, fb);
+      }
+      if (++slot == kStages) { slot = 0; phase ^= 1; }
     }
   }
+  // Let every issued copy land before the CTA can exit: slot i was last
+  // filled by item j = the largest j < item with j % kStages == i.
+  if (lane == 0)
+    for (int i = 0; i < kStages && i < item; i++) {
+      const int j = i + (item - 1 - i) / kStages * kStages;
+      drain_wait(&L->full[i], (uint32_t)((j / kStages) & 1), 200000000LL);
+    }
+  if (p.counters && lane == 0) {
+    atomicAdd(p.counters + SC_EMPTY_WAIT, (unsigned long long)wait_cycles);
+    atomicAdd(p.counters + SC_PROD_TOTAL, (unsigned long long)(clock64() - t_start));
+  }
+}
 
-  // Epilogue. acc[nt][0..1]: row g, columns 2t, 2t+1; [2..3]: row g+8.
+// One full stage for a unit of at most 8 tokens (the decode case): all of
+// the warp's nibbles, token fragments and scales are read first and the
+// stage is released before any conversion, so the producer can refill it
+// while the MMAs run; consecutive scale groups (G per 256-K stage) use
+// alternating accumulator chains, so two groups' MMAs overlap per tile.
+template <int G>
+__device__ __forceinline__ void stage_single(float (&acc0)[4][4], float (&acc1)[4][4],
+                                             const uint8_t* st, int b0, int b1, int r0, int r1,
+                                             int g, int t, bool hz0, bool hz1, SkSmem* L, int slot,
+                                             int lane) {
+  constexpr int QPG = kQ / G;  // quarters per scale group
+  RawTile w0[kQ], w1[kQ];
+  BHalf<1> bq[kQ];
+#pragma unroll
+  for (int q = 0; q < kQ; q++) {
+    load_tile(w0[q], st, b0, r0, q, t);
+    load_tile(w1[q], st, b1, r1, q, t);
+    load_b<1>(bq[q], st, q, g, t);
+  }
+  // scales and zero points of rows (r, r+8) as fp16 pairs
+  __half2 s0[G], s1[G], z0[G], z1[G];
+#pragma unroll
+  for (int j = 0; j < G; j++) {
+    s0[j] = group_pair_h2(st + kOffS + b0 * kScRun, j, r0);
+    s1[j] = group_pair_h2(st + kOffS + b1 * kScRun, j, r1);
+    z0[j] = hz0 ? group_pair_h2(st + kOffZ + b0 * kScRun, j, r0) : __half2{};
+    z1[j] = hz1 ? group_pair_h2(st + kOffZ + b1 * kScRun, j, r1) : __half2{};
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&L->empty[slot]);
+
+  // Two chain sets per tile, alternating by scale group; a chain is folded
+  // into the accumulator (times its group's scale) after its last quarter.
+  float c0[2][4], c1[2][4];
+#pragma unroll
+  for (int j = 0; j < 2; j++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) c0[j][e] = c1[j][e] = 0.f;
+#pragma unroll
+  for (int q = 0; q < kQ; q++) {
+    const int j = q / QPG, ci = j & 1;
+    __half2 ag0[2][4], a80[2][4], ag1[2][4], a81[2][4];
+    nib8_centered(w0[q].w[0].x, ag0[0]);
+    nib8_centered(w0[q].w[0].y, ag0[1]);
+    nib8_centered(w0[q].w[1].x, a80[0]);
+    nib8_centered(w0[q].w[1].y, a80[1]);
+    nib8_centered(w1[q].w[0].x, ag1[0]);
+    nib8_centered(w1[q].w[0].y, ag1[1]);
+    nib8_centered(w1[q].w[1].x, a81[0]);
+    nib8_centered(w1[q].w[1].y, a81[1]);
+#pragma unroll
+    for (int m = 0; m < 4; m++) {
+      const int wd = m >> 1, pp = 2 * (m & 1);
+      const uint32_t b0v = u4_get(bq[q].v[wd][0], pp), b1v = u4_get(bq[q].v[wd][0], pp + 1);
+      hmma16816(c0[ci], h22u(ag0[wd][pp]), h22u(a80[wd][pp]), h22u(ag0[wd][pp + 1]),
+                h22u(a80[wd][pp + 1]), b0v, b1v);
+      hmma16816(c1[ci], h22u(ag1[wd][pp]), h22u(a81[wd][pp]), h22u(ag1[wd][pp + 1]),
+                h22u(a81[wd][pp + 1]), b0v, b1v);
+    }
+    if ((q + 1) % QPG == 0) {
+      const float2 f0 = __half22float2(s0[j]), f1 = __half22float2(s1[j]);
+      acc0[0][0] = fmaf(f0.x, c0[ci][0], acc0[0][0]);
+      acc0[0][1] = fmaf(f0.x, c0[ci][1], acc0[0][1]);
+      acc0[0][2] = fmaf(f0.y, c0[ci][2], acc0[0][2]);
+      acc0[0][3] = fmaf(f0.y, c0[ci][3], acc0[0][3]);
+      acc1[0][0] = fmaf(f1.x, c1[ci][0], acc1[0][0]);
+      acc1[0][1] = fmaf(f1.x, c1[ci][1], acc1[0][1]);
+      acc1[0][2] = fmaf(f1.y, c1[ci][2], acc1[0][2]);
+      acc1[0][3] = fmaf(f1.y, c1[ci][3], acc1[0][3]);
+#pragma unroll
+      for (int e = 0; e < 4; e++) c0[ci][e] = c1[ci][e] = 0.f;
+    }
+  }
+  if (hz0 | hz1) {
+#pragma unroll
+    for (int q = 0; q < kQ; q++) {
+      const int j = q / QPG;
+      float xs[1][2];
+      half_sums<1>(bq[q], xs, t);
+      const float2 g0 = __half22float2(z0[j]), g1 = __half22float2(z1[j]);
+      if (hz0) add_zeros<1>(acc0, xs, g0.x, g0.y);
+      if (hz1) add_zeros<1>(acc1, xs, g1.x, g1.y);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Consumer warps: one unit with NT n8 token tiles.
+// ---------------------------------------------------------------------------
+template <int MODE, int NT>
+__device__ bool sk_unit(const SkParams& p, uint8_t* ring, SkSmem* L, const StageHdr& hdr,
+                        int warp, int lane, int& slot, uint32_t& phase,
+                        long long& wait_cycles) {
+  volatile int* abort = &L->abort;
+  const int g = lane >> 2, t = lane & 3;
+  const int sig = ((g & 3) << 1) | (g >> 2);  // box row of MMA row g
+  const int K = MODE == SK_GATEUP ? p.M : p.I;
+  const int nk = (K + kKS - 1) / kKS;
+  const int qpg = p.gs / 64;  // quarters per scale group (1 or 2)
+  // Tiles: GATEUP gate rows r0.. (block 0) and up rows r0.. (block 1);
+  // DOWN rows r0.. and r0+16.. of block warp/4.
+  const int b0 = MODE == SK_GATEUP ? 0 : warp >> 2;
+  const int b1 = MODE == SK_GATEUP ? 1 : warp >> 2;
+  const int r0 = (MODE == SK_GATEUP ? 16 * warp : 32 * (warp & 3)) + sig;
+  const int r1 = MODE == SK_GATEUP ? r0 : r0 + 16;
+  const bool active = MODE == SK_GATEUP || b0 == 0 || (hdr.flags & HF_V1);
+  const bool hz0 = hdr.flags & (b0 ? HF_HZ1 : HF_HZ0);
+  const bool hz1 = hdr.flags & (b1 ? HF_HZ1 : HF_HZ0);
+
+  float acc0[4][4], acc1[4][4];
+#pragma unroll
+  for (int nt = 0; nt < 4; nt++)
+#pragma unroll
+    for (int q = 0; q < 4; q++) acc0[nt][q] = acc1[nt][q] = 0.f;
+
+  for (int kg = 0; kg < nk; kg++) {
+    if (kg > 0) {
+      const long long tw = p.counters ? clock64() : 0;
+      if (!mbar_wait(&L->full[slot], phase, abort)) return false;
+      if (p.counters) wait_cycles += clock64() - tw;
+    }
+    const uint8_t* st = ring + slot * kStageBytes;
+    const int nq = min(kQ, (K - kg * kKS) / 64);
+    if (active && NT == 1 && nq == kQ && p.gs == 128) {
+      // Single n8 token tile, full stage, two scale groups (group size 64
+      // would need more registers than 9 warps per SM leave).
+      stage_single<2>(acc0, acc1, st, b0, b1, r0, r1, g, t, hz0, hz1, L, slot, lane);
+    } else if (active) {
+#pragma unroll
+      for (int q = 0; q < kQ; q++) {
+        if (q < nq) {
+          RawTile w0, w1;
+          load_tile(w0, st, b0, r0, q, t);
+          load_tile(w1, st, b1, r1, q, t);
+          BHalf<NT> bq;
+          load_b<NT>(bq, st, q, g, t);
+          const int grp = q / qpg;
+          float sa, sb, sc, sd, za = 0.f, zb = 0.f, zc = 0.f, zd = 0.f;
+          group_pair(st + kOffS + b0 * kScRun, grp, r0, sa, sb);
+          group_pair(st + kOffS + b1 * kScRun, grp, r1, sc, sd);
+          if (hz0) group_pair(st + kOffZ + b0 * kScRun, grp, r0, za, zb);
+          if (hz1) group_pair(st + kOffZ + b1 * kScRun, grp, r1, zc, zd);
+          if (q == nq - 1) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&L->empty[slot]);
+          }
+          tile_quarter<NT>(acc0, w0, bq, sa, sb);
+          tile_quarter<NT>(acc1, w1, bq, sc, sd);
+          if (hz0 | hz1) {
+            float xs[NT][2];
+            half_sums<NT>(bq, xs, t);
+            if (hz0) add_zeros<NT>(acc0, xs, za, zb);
+            if (hz1) add_zeros<NT>(acc1, xs, zc, zd);
+          }
+        }
+      }
+    } else {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&L->empty[slot]);
+    }
+    if (++slot == kStages) { slot = 0; phase ^= 1; }
+  }
+  if (!active) return true;
+
+  // Epilogue. acc[nt][0..1]: MMA row g (box row r), columns 2t, 2t+1;
+  // [2..3]: MMA row g+8 (box row r+8).
 #pragma unroll
   for (int nt = 0; nt < NT; nt++) {
 #pragma unroll
     for (int q = 0; q < 4; q++) {
       const int col = nt * 8 + 2 * t + (q & 1);
-      if (col >= n) continue;
+      if (col >= hdr.n) continue;
       const int rr = (q >> 1) ? 8 : 0;
-      const int prow = sg.row_begin + col;
+      const int prow = hdr.prow0 + col;
       if (MODE == SK_GATEUP) {
-        const int i = r0 + g + rr;
+        const int i = hdr.row0 + r0 + rr;
         const float hv = silu(acc0[nt][q]) * acc1[nt][q];
         p.h_out[(size_t)prow * p.I + k_interleave_slot(i)] = __float2half(hv);
       } else {
+        const int base = hdr.row0 + b0 * kBoxRows;
+        const int ma = base + r0 + rr, mb = base + r1 + rr;
         const float y0 = acc0[nt][q], y1 = acc1[nt][q];
-        const int ma = r0 + g + rr, mb = r1 + g + rr;
         if (p.mode == 0) {
           const int tok = __ldg(p.row_token + prow);
           const float wgt = __ldg(p.row_weight + prow);
@@ -317,22 +555,62 @@ __device__ void sk_unit(const SkParams& p, const WispSegment& sg, int rb, int wa
       }
     }
   }
+  return true;
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(kSkWarps * 32, 4) skinny_ffn_kernel(const __grid_constant__ SkParams p) {
-  const int total = __ldg(p.units + p.nseg);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int unit = blockIdx.x; unit < total; unit += gridDim.x) {
-    const int s = find_seg(p.units, p.nseg, unit);
-    const int rb = unit - __ldg(p.units + s);
-    const WispSegment sg = p.segs[s];
-    if (sg.rows > 8)
-      sk_unit<MODE, 2>(p, sg, rb, warp, lane);
-    else
-      sk_unit<MODE, 1>(p, sg, rb, warp, lane);
+__device__ void sk_consumer(const SkParams& p, uint8_t* ring, SkSmem* L, int total, int warp,
+                            int lane) {
+  volatile int* abort = &L->abort;
+  int slot = 0;
+  uint32_t phase = 0;
+  const long long t_start = p.counters ? clock64() : 0;
+  long long wait_cycles = 0;
+  for (int u = blockIdx.x; u < total; u += gridDim.x) {
+    const long long tw = p.counters ? clock64() : 0;
+    if (!mbar_wait(&L->full[slot], phase, abort)) return;
+    if (p.counters) wait_cycles += clock64() - tw;
+    const StageHdr hdr = *reinterpret_cast<const StageHdr*>(ring + slot * kStageBytes + kOffH);
+    const int nt = (hdr.n + 7) >> 3;
+    bool ok;
+    if (nt == 1) ok = sk_unit<MODE, 1>(p, ring, L, hdr, warp, lane, slot, phase, wait_cycles);
+    else if (nt == 2) ok = sk_unit<MODE, 2>(p, ring, L, hdr, warp, lane, slot, phase, wait_cycles);
+    else if (nt == 3) ok = sk_unit<MODE, 3>(p, ring, L, hdr, warp, lane, slot, phase, wait_cycles);
+    else ok = sk_unit<MODE, 4>(p, ring, L, hdr, warp, lane, slot, phase, wait_cycles);
+    if (!ok) return;
+  }
+  if (p.counters && lane == 0) {
+    atomicAdd(p.counters + SC_FULL_WAIT, (unsigned long long)wait_cycles);
+    atomicAdd(p.counters + SC_CONS_TOTAL, (unsigned long long)(clock64() - t_start));
   }
 }
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1) skinny_ffn_kernel(const __grid_constant__ SkParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const int total = __ldg(p.units + p.nseg);
+  if ((int)blockIdx.x >= total) return;
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  SkSmem* L = reinterpret_cast<SkSmem*>(ring + kStages * kStageBytes);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; i++) {
+      mbar_init(&L->full[i], 1);
+      mbar_init(&L->empty[i], kCW);
+    }
+    L->abort = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (warp == kCW)
+    sk_producer<MODE>(p, ring, L, total, lane);
+  else
+    sk_consumer<MODE>(p, ring, L, total, warp, lane);
+  __syncthreads();
+  if (threadIdx.x == 0 && L->abort && p.error_flag) atomicExch(p.error_flag, 1);
+}
+
+constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + sizeof(SkSmem);
 
 }  // namespace
 
@@ -340,31 +618,44 @@ namespace wb {
 
 struct SkLaunch {
   const uint8_t* prepared;
-  size_t p_flags, p_scales, p_zeros, p_mat_sc_bytes;
-  const WispInt4Expert* experts;
+  size_t p_maps_sk, p_flags, p_scales, p_zeros, p_mat_sc_bytes;
   const WispSegment* segs;
   int nseg;
   const int32_t* units_gu;
   const int32_t* units_dn;
   int M, I, gs;
-  const __half* xp;
+  const CUtensorMap* xp_maps;  // [3]: boxes of 8 / 16 / 32 rows
+  const CUtensorMap* h_maps;   // [3]
   __half* h;
   const int* row_token;
   const float* row_weight;
   float* out;
   int mode;
+  int* error_flag;
+  unsigned long long* counters;
 };  // mirrored in grouped.cu
 
 int skinny_max_rows() { return kSkMaxRows; }
+int skinny_cols() { return kCols; }
+int skinny_units_gateup(int I) { return I / kBoxRows; }
+int skinny_units_down(int M) { return (M + 2 * kBoxRows - 1) / (2 * kBoxRows); }
 
-void launch_skinny(const SkLaunch& L, int phase, cudaStream_t st) {
+cudaError_t launch_skinny(const SkLaunch& L, int phase, int grid, cudaStream_t st) {
+  // The attribute belongs to the current device's context: set it per launch.
+  cudaError_t ce = phase == 0
+      ? cudaFuncSetAttribute(skinny_ffn_kernel<SK_GATEUP>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes)
+      : cudaFuncSetAttribute(skinny_ffn_kernel<SK_DOWN>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+  if (ce != cudaSuccess) return ce;
   SkParams p;
+  memset(&p, 0, sizeof p);
   p.prepared = L.prepared;
+  p.p_maps_sk = L.p_maps_sk;
   p.p_flags = L.p_flags;
   p.p_scales = L.p_scales;
   p.p_zeros = L.p_zeros;
   p.p_mat_sc_bytes = L.p_mat_sc_bytes;
-  p.experts = L.experts;
   p.segs = L.segs;
   p.nseg = L.nseg;
   p.M = L.M;
@@ -375,19 +666,18 @@ void launch_skinny(const SkLaunch& L, int phase, cudaStream_t st) {
   p.row_weight = L.row_weight;
   p.out = L.out;
   p.mode = L.mode;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int grid = sms * 4;
+  p.error_flag = L.error_flag;
+  p.counters = L.counters ? L.counters + phase * SC_COUNT : nullptr;
+  const CUtensorMap* maps = phase == 0 ? L.xp_maps : L.h_maps;
+  for (int i = 0; i < 3; i++) p.act_map[i] = maps[i];
   if (phase == 0) {
     p.units = L.units_gu;
-    p.act = L.xp;
-    skinny_ffn_kernel<SK_GATEUP><<<grid, kSkWarps * 32, 0, st>>>(p);
+    skinny_ffn_kernel<SK_GATEUP><<<grid, kThreads, kSmemBytes, st>>>(p);
   } else {
     p.units = L.units_dn;
-    p.act = L.h;
-    skinny_ffn_kernel<SK_DOWN><<<grid, kSkWarps * 32, 0, st>>>(p);
+    skinny_ffn_kernel<SK_DOWN><<<grid, kThreads, kSmemBytes, st>>>(p);
   }
+  return cudaGetLastError();
 }
 
 }  // namespace wb
