@@ -51,9 +51,11 @@ WB_DEV void nib8_centered(uint32_t q, __half2 out[4]) {
   __half2 h1 = u2h2(lop_or_and(q, 0x00F000F0u, MAGIC));
   __half2 h2 = u2h2(lop_or_and(q8, 0x000F000Fu, MAGIC));
   __half2 h3 = u2h2(lop_or_and(q8, 0x00F000F0u, MAGIC));
-  const __half2 c1032 = __floats2half2_rn(-1032.f, -1032.f);
-  const __half2 inv16 = __floats2half2_rn(0.0625f, 0.0625f);
-  const __half2 c72 = __floats2half2_rn(-72.f, -72.f);
+  // fp16 bit patterns, so the constants are immediates rather than
+  // conversions: -1032 = 0xE408, 1/16 = 0x2C00, -72 = 0xD480.
+  const __half2 c1032 = u2h2(0xE408E408u);
+  const __half2 inv16 = u2h2(0x2C002C00u);
+  const __half2 c72 = u2h2(0xD480D480u);
   out[0] = __hadd2(h0, c1032);          // (1024+n) - 1032
   out[1] = __hfma2(h1, inv16, c72);     // (1024+16n)/16 - 72
   out[2] = __hadd2(h2, c1032);

@@ -91,7 +91,7 @@ struct Shape {
 // [row tile][group][128 rows] so that the scales of one stage are one
 // contiguous run.
 struct PreparedLayout {
-  size_t maps, maps_sk, flags, scales, zeros, mat_sc_bytes, total;
+  size_t maps, maps_sk, flags, zbits, scales, zeros, mat_sc_bytes, total;
 };
 
 PreparedLayout prepared_layout(const WispMoeConfig* c, int n) {
@@ -101,7 +101,8 @@ PreparedLayout prepared_layout(const WispMoeConfig* c, int n) {
   L.maps = 0;
   L.maps_sk = entries * sizeof(CUtensorMap);
   L.flags = L.maps_sk + entries * sizeof(CUtensorMap);
-  L.scales = (L.flags + entries * 4 + 255) & ~(size_t)255;
+  L.zbits = L.flags + entries * 4;  // the same flags, one bit per entry
+  L.scales = (L.zbits + (entries + 31) / 32 * 4 + 255) & ~(size_t)255;
   L.zeros = L.scales + entries * L.mat_sc_bytes;
   L.total = L.zeros + entries * L.mat_sc_bytes;
   return L;
@@ -783,9 +784,10 @@ int g_skinny_rows = -1;  // -1: library default
 namespace wb {
 struct SkLaunch {
   const uint8_t* prepared;
-  size_t p_maps_sk, p_flags, p_scales, p_zeros, p_mat_sc_bytes;
+  size_t p_maps_sk, p_zbits, p_scales, p_zeros, p_mat_sc_bytes;
   const WispSegment* segs;
   int nseg;
+  int n_entries;
   const int32_t* units_gu;
   const int32_t* units_dn;
   int M, I, gs;
@@ -800,6 +802,8 @@ struct SkLaunch {
   unsigned long long* counters;
 };
 int skinny_max_rows();
+int skinny_max_segs();
+int skinny_max_entries();
 int skinny_cols();
 int skinny_units_gateup(int I);
 int skinny_units_down(int M);
@@ -860,6 +864,11 @@ extern "C" WispError wisp_b200_prepare_experts(const WispMoeConfig* cfg,
                                 maps_sk.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice,
                                 stream));
   WB_CUDA_CHECK(cudaMemcpyAsync(base + PL.flags, flags.data(), flags.size() * 4,
+                                cudaMemcpyHostToDevice, stream));
+  std::vector<uint32_t> zbits((flags.size() + 31) / 32, 0u);
+  for (size_t i = 0; i < flags.size(); i++)
+    if (flags[i]) zbits[i / 32] |= 1u << (i % 32);
+  WB_CUDA_CHECK(cudaMemcpyAsync(base + PL.zbits, zbits.data(), zbits.size() * 4,
                                 cudaMemcpyHostToDevice, stream));
   dim3 grid(64, n_entries * 3);
   transpose_scales_kernel<<<grid, 256, 0, stream>>>(d_experts, n_entries, M, I, cfg->group_size,
@@ -931,8 +940,11 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
   dn.mode = mode;
 
   const size_t tw = (size_t)(2 * n_segs + 1);
-  const int sk_rows = g_skinny_rows >= 0 ? std::min(g_skinny_rows, wb::skinny_max_rows())
-                                         : wb::skinny_max_rows();
+  int sk_rows = g_skinny_rows >= 0 ? std::min(g_skinny_rows, wb::skinny_max_rows())
+                                   : wb::skinny_max_rows();
+  // The register-path kernel keeps the segment table in shared memory; larger
+  // launches run on the tensor-core kernel alone.
+  if (n_segs > wb::skinny_max_segs() || n_entries > wb::skinny_max_entries()) sk_rows = 0;
   gu.tiles = d_tiles;
   dn.tiles = d_tiles + tw;
   int32_t* units_gu = d_tiles + 2 * tw;
@@ -944,8 +956,8 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
                                             sk_rows, units_gu);
   plan_units_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, wb::skinny_units_down(M), skc,
                                             sk_rows, units_dn);
-  CUtensorMap sk_xp[3], sk_h[3];
-  for (int i = 0; i < 3; i++) {
+  CUtensorMap sk_xp[2], sk_h[2];
+  for (int i = 0; i < 2; i++) {
     if (!encode_rows_map(&sk_xp[i], d_xp, rows_capacity, M, 8 << i) ||
         !encode_rows_map(&sk_h[i], d_h, rows_capacity, I, 8 << i))
       return WB_FAIL(WISP_ERR_CUDA, "grouped_ffn: cuTensorMapEncodeTiled failed (token rows)");
@@ -953,12 +965,13 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
   wb::SkLaunch sk;
   sk.prepared = gu.prepared;
   sk.p_maps_sk = PL.maps_sk;
-  sk.p_flags = PL.flags;
+  sk.p_zbits = PL.zbits;
   sk.p_scales = PL.scales;
   sk.p_zeros = PL.zeros;
   sk.p_mat_sc_bytes = PL.mat_sc_bytes;
   sk.segs = d_segs;
   sk.nseg = n_segs;
+  sk.n_entries = n_entries;
   sk.units_gu = units_gu;
   sk.units_dn = units_dn;
   sk.M = M;

@@ -17,35 +17,45 @@
 //               64-K quarter of the unit's token rows (fp16, 128-byte
 //               swizzle), and bulk copies of the stage's scales (and zero
 //               points) from the prepared tile-transposed copy, into a
-//               4-deep shared-memory ring (53 KB per stage, up to 96 KB of
-//               weights in flight per SM).
-//   warps 0-7   consumers: each takes two 16-row tiles; per 64-K quarter it
-//               reads its nibbles (conflict-free 8-byte loads: MMA row g
-//               lives in box row sigma(g) = 2(g%4) + g/4, so each
-//               half-warp's rows fall in distinct swizzle chunks) and the
-//               tokens' B fragments (conflict-free 16-byte loads), converts
-//               each 32-bit word of nibbles to exact (n - 8) fp16 pairs,
-//               runs the MMAs, and applies the group's scale (and zero
-//               point) to the fp32 partial sums. The stage is released once
-//               its last quarter has been read.
+//               5-deep shared-memory ring (44 KB per stage, up to 160 KB of
+//               weights in flight per SM: under full load a copy takes
+//               several microseconds from issue to arrival, so the bytes in
+//               flight per SM set the bandwidth). Units are looked up in a
+//               shared-memory copy of the unit prefix; the next unit's
+//               segment record is fetched one unit ahead.
+//   warps 0-7   consumers, each with two 16-row MMA tiles. Per 64-K quarter
+//               a warp reads its nibbles
+//               (conflict-free 8-byte loads: MMA row g lives in box row
+//               sigma(g) = 2(g%4) + g/4 (mod 8), so each half-warp's rows
+//               fall in distinct swizzle chunks) and the tokens' B fragments
+//               (conflict-free 16-byte loads), converts each 32-bit word of
+//               nibbles to exact (n - 8) fp16 pairs, runs a 4-MMA chain, and
+//               folds it into fp32 accumulators times the group's scale (and
+//               adds the zero-point term). The stage is released once its
+//               last quarter has been read; units of at most 8 tokens
+//               read a whole stage into registers and release it at once.
+//               (Sixteen one-tile warps, four per scheduler, measured
+//               slower: every warp re-reads the token fragments.)
 //
-// Work unit = (segment, weight row block, chunk of up to 32 tokens):
+// Work unit = (segment, weight row block, chunk of up to 16 tokens):
 //   GATEUP: 128 intermediate rows i of gate and of up; warp w takes rows
 //           16w..16w+15 of both -> h = silu(g) * u written to H (fp16,
 //           interleaved K order).
 //   DOWN:   256 output rows m (two 128-row blocks); warp w takes 32 rows ->
 //           out[token] += w * y (mode 0, fp32 atomics) or y rows (mode 1).
 // Chunks of one row block are consecutive units, so CTAs that run them at
-// the same time share the weight tile through L2. Segments larger than the
+// the same time share the weight tile through L2. Every token runs the same
+// arithmetic in the same order whatever chunk it lands in, so a token's
+// result does not depend on the batch around it. Segments larger than the
 // routing threshold go to the tcgen05 kernel.
 //
 // Fragment mapping. m16n8k16 gives thread (g = lane/4, t = lane%4) the A
 // pairs (row g, k 2t..2t+1), (row g+8, same), (row g, k 2t+8..2t+9),
 // (row g+8, same) and the B pairs (k 2t..2t+1, col g), (k 2t+8..2t+9, col g).
 // The logical k of one MMA may map to any physical K as long as A and B
-// agree. Per 64-K half group, thread t owns packed words 2t and 2t+1 (bytes
+// agree. Per 64-K quarter, thread t owns packed words 2t and 2t+1 (bytes
 // 8t..8t+7); nib8_centered turns a word into the pairs (k0,k4) (k1,k5)
-// (k2,k6) (k3,k7). MMA m (0..3) of the half takes word m/2 and pair p =
+// (k2,k6) (k3,k7). MMA m (0..3) of the quarter takes word m/2 and pair p =
 // 2(m&1) as its (2t,2t+1) slot and pair p+1 as its (2t+8,2t+9) slot. The
 // activation rows are stored interleaved (within 8 K: 0,4,1,5,2,6,3,7), so
 // pair q of word w is 32-bit element q of that word's 16 bytes: B slot 0 is
@@ -57,30 +67,33 @@ using namespace wb;
 
 namespace {
 
-constexpr int kCW = 8;                        // consumer warps
+constexpr int kCW = 8;                        // consumer warps, two 16-row tiles each
 constexpr int kThreads = (kCW + 1) * 32;      // + one producer warp
-constexpr int kStages = 4;
-constexpr int kCols = 32;                     // tokens per unit
+constexpr int kStages = 5;
+constexpr int kCols = 16;                     // tokens per unit
 constexpr int kSkMaxRows = 256;               // default routing threshold
 constexpr int kKS = 256;                      // K per stage
 constexpr int kQ = kKS / 64;                  // 64-K quarters per stage
 constexpr int kBoxRows = 128;
 constexpr int kBoxBytes = kBoxRows * 128;     // one weight block of a stage
-constexpr int kBQBytes = kCols * 128;         // one 64-K quarter of 32 token rows
+constexpr int kBQBytes = kCols * 128;         // one 64-K quarter of 16 token rows
 constexpr int kScRun = 4 * kBoxRows * 2;      // up to 4 scale groups x 128 rows
 // Stage layout (bytes): [weights 2 blocks][tokens 4 quarters]
-// [scales 2 blocks][zeros 2 blocks][header].
+// [scales 2 blocks][zeros 2 blocks]; the stage headers live apart, so a
+// stage is a whole number of KB and every TMA box keeps 1024-byte alignment.
 constexpr int kOffB = 2 * kBoxBytes;
 constexpr int kOffS = kOffB + kQ * kBQBytes;
 constexpr int kOffZ = kOffS + 2 * kScRun;
-constexpr int kOffH = kOffZ + 2 * kScRun;
-constexpr int kStageBytes = (kOffH + 64 + 1023) / 1024 * 1024;
+constexpr int kStageBytes = kOffZ + 2 * kScRun;
+static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
+constexpr int kMaxSegs = 1040;                // segments per launch (experts + shared)
+constexpr int kMaxEntries = 1536;             // prepared expert entries
 enum { SK_GATEUP = 0, SK_DOWN = 1 };
 enum { HF_HZ0 = 1, HF_HZ1 = 2, HF_V1 = 4 };
 
 struct __align__(16) StageHdr {
   int prow0;  // first activation row of the unit
-  int n;      // tokens in the unit (1..32)
+  int n;      // tokens in the unit (1..16)
   int row0;   // first weight row of the unit
   int flags;  // HF_*: zero points of block 0 / 1, block 1 inside the matrix
 };
@@ -88,16 +101,20 @@ struct __align__(16) StageHdr {
 struct SkSmem {
   uint64_t full[kStages];
   uint64_t empty[kStages];
+  StageHdr hdr[kStages];
   int abort;
+  int32_t units[kMaxSegs + 1];           // unit prefix per segment
+  uint32_t zbits[kMaxEntries * 3 / 32];  // zero-point flag per matrix entry
 };
 
 struct SkParams {
-  CUtensorMap act_map[3];  // token rows, boxes {64 halves, 8/16/32 rows}, 128-byte swizzle
+  CUtensorMap act_map[2];  // token rows, boxes {64 halves, 8/16 rows}, 128-byte swizzle
   const uint8_t* prepared;
-  size_t p_maps_sk, p_flags, p_scales, p_zeros, p_mat_sc_bytes;
+  size_t p_maps_sk, p_zbits, p_scales, p_zeros, p_mat_sc_bytes;
   const WispSegment* segs;
   const int32_t* units;  // [0, S]: unit prefix per segment
   int nseg;
+  int n_entries;
   int M, I, gs;
   __half* h_out;
   const int* row_token;
@@ -122,6 +139,16 @@ __device__ __forceinline__ void hmma16816(float (&c)[4], uint32_t a0, uint32_t a
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// The same with a zero accumulator input (the first MMA of a chain).
+__device__ __forceinline__ void hmma16816_z(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                            uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};"
+      : "=f"(c[0]), "=f"(c[1]), "=f"(c[2]), "=f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
+}
+
 // Waits without the abort shortcut: used to let issued copies land before
 // the CTA exits.
 __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, long long limit) {
@@ -130,14 +157,14 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, long 
     if (clock64() - t0 > limit) return;
 }
 
-// Nibbles of one 16-row tile for one 64-K quarter: rows g and g+8.
+// Nibbles of one 16-row tile for one 64-K quarter: MMA rows g and g+8.
 struct RawTile {
   uint2 w[2];  // [row g / g+8]
 };
 
 // Token words of one 64-K quarter: [word 2t / 2t+1][n8 tile].
 template <int NT>
-struct BHalf {
+struct BQuarter {
   uint4 v[2][NT];
 };
 
@@ -146,10 +173,10 @@ __device__ __forceinline__ uint32_t u4_get(const uint4& v, int i) {
 }
 
 // acc[nt] += s * (A x B) for one 16-row tile over one 64-K quarter; scales
-// of rows g (sg) and g+8 (s8).
+// of MMA rows g (sg) and g+8 (s8).
 template <int NT>
-__device__ __forceinline__ void tile_quarter(float (&acc)[4][4], const RawTile& w,
-                                             const BHalf<NT>& b, float sg, float s8) {
+__device__ __forceinline__ void tile_quarter(float (&acc)[2][4], const RawTile& w,
+                                             const BQuarter<NT>& b, float sg, float s8) {
   __half2 ag[2][4], a8[2][4];
   nib8_centered(w.w[0].x, ag[0]);
   nib8_centered(w.w[0].y, ag[1]);
@@ -157,17 +184,17 @@ __device__ __forceinline__ void tile_quarter(float (&acc)[4][4], const RawTile& 
   nib8_centered(w.w[1].y, a8[1]);
   float ct[NT][4];
 #pragma unroll
-  for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-    for (int q = 0; q < 4; q++) ct[nt][q] = 0.f;
-#pragma unroll
   for (int m = 0; m < 4; m++) {
     const int wd = m >> 1, p = 2 * (m & 1);
     const uint32_t a0 = h22u(ag[wd][p]), a2 = h22u(ag[wd][p + 1]);
     const uint32_t a1 = h22u(a8[wd][p]), a3 = h22u(a8[wd][p + 1]);
 #pragma unroll
-    for (int nt = 0; nt < NT; nt++)
-      hmma16816(ct[nt], a0, a1, a2, a3, u4_get(b.v[wd][nt], p), u4_get(b.v[wd][nt], p + 1));
+    for (int nt = 0; nt < NT; nt++) {
+      if (m == 0)
+        hmma16816_z(ct[nt], a0, a1, a2, a3, u4_get(b.v[wd][nt], p), u4_get(b.v[wd][nt], p + 1));
+      else
+        hmma16816(ct[nt], a0, a1, a2, a3, u4_get(b.v[wd][nt], p), u4_get(b.v[wd][nt], p + 1));
+    }
   }
 #pragma unroll
   for (int nt = 0; nt < NT; nt++) {
@@ -181,7 +208,7 @@ __device__ __forceinline__ void tile_quarter(float (&acc)[4][4], const RawTile& 
 // Zero points: acc[row, col] += z[row] * sum_k x[col, k] over the 64-K
 // quarter. xs[nt][j]: activation sum of column 2t+j of tile nt.
 template <int NT>
-__device__ __forceinline__ void half_sums(const BHalf<NT>& b, float (&xs)[NT][2], int t) {
+__device__ __forceinline__ void quarter_sums(const BQuarter<NT>& b, float (&xs)[NT][2], int t) {
 #pragma unroll
   for (int nt = 0; nt < NT; nt++) {
     float s = 0.f;
@@ -205,7 +232,7 @@ __device__ __forceinline__ void half_sums(const BHalf<NT>& b, float (&xs)[NT][2]
 }
 
 template <int NT>
-__device__ __forceinline__ void add_zeros(float (&acc)[4][4], const float (&xs)[NT][2], float zg,
+__device__ __forceinline__ void add_zeros(float (&acc)[2][4], const float (&xs)[NT][2], float zg,
                                           float z8) {
 #pragma unroll
   for (int nt = 0; nt < NT; nt++) {
@@ -216,36 +243,28 @@ __device__ __forceinline__ void add_zeros(float (&acc)[4][4], const float (&xs)[
   }
 }
 
-// Scale (or zero point) of rows (row, row+8) for scale group grp from the
-// stage's [group][128 rows] run.
-__device__ __forceinline__ void group_pair(const uint8_t* run, int grp, int row, float& a,
-                                           float& b) {
-  const __half* s = reinterpret_cast<const __half*>(run) + grp * kBoxRows;
-  a = __half2float(s[row]);
-  b = __half2float(s[row + 8]);
+// MMA rows g and g+8 of a tile for 64-K quarter q: box rows ra (block ba)
+// and rb (block bb), both = sigma(g) (mod 8). Thread t reads bytes
+// 8t..8t+7 of the quarter's 32 bytes, i.e. 16-byte chunk 2q + t/2, stored at
+// chunk ^ (row & 7).
+__device__ __forceinline__ void load_tile(RawTile& r, const uint8_t* st, int ba, int ra, int bb,
+                                          int rb, int q, int t) {
+  const int off = (((2 * q + (t >> 1)) ^ (ra & 7)) << 4) + 8 * (t & 1);
+  r.w[0] = *reinterpret_cast<const uint2*>(st + ba * kBoxBytes + ra * 128 + off);
+  r.w[1] = *reinterpret_cast<const uint2*>(st + bb * kBoxBytes + rb * 128 + off);
 }
 
-// The same pair as fp16 (low: row, high: row+8).
-__device__ __forceinline__ __half2 group_pair_h2(const uint8_t* run, int grp, int row) {
-  const __half* s = reinterpret_cast<const __half*>(run) + grp * kBoxRows;
-  return __halves2half2(s[row], s[row + 8]);
-}
-
-// Rows srow and srow+8 (srow = tile base + sigma(g)) of a weight block,
-// 64-K quarter q: thread t reads bytes 8t..8t+7 of the quarter's 32 bytes,
-// i.e. 16-byte chunk 2q + t/2, stored at chunk ^ (srow & 7).
-__device__ __forceinline__ void load_tile(RawTile& r, const uint8_t* st, int block, int srow,
-                                          int q, int t) {
-  const int chunk = (2 * q + (t >> 1)) ^ (srow & 7);
-  const uint8_t* a = st + block * kBoxBytes + srow * 128 + (chunk << 4) + 8 * (t & 1);
-  r.w[0] = *reinterpret_cast<const uint2*>(a);
-  r.w[1] = *reinterpret_cast<const uint2*>(a + 8 * 128);
+// Scale (or zero point) of box row `row` of a block for scale group grp.
+__device__ __forceinline__ float row_scale(const uint8_t* st, int off, int block, int grp,
+                                           int row) {
+  return __half2float(
+      reinterpret_cast<const __half*>(st + off + block * kScRun)[grp * kBoxRows + row]);
 }
 
 // Token row r's 16-byte chunk c of a 64-K quarter: the 128-byte swizzle puts
 // it at chunk c ^ (r & 7).
 template <int NT>
-__device__ __forceinline__ void load_b(BHalf<NT>& b, const uint8_t* st, int q, int g, int t) {
+__device__ __forceinline__ void load_b(BQuarter<NT>& b, const uint8_t* st, int q, int g, int t) {
 #pragma unroll
   for (int nt = 0; nt < NT; nt++) {
     const int r = nt * 8 + g;
@@ -265,31 +284,41 @@ __device__ void sk_producer(const SkParams& p, uint8_t* ring, SkSmem* L, int tot
   const int K = MODE == SK_GATEUP ? p.M : p.I;
   const int nk = (K + kKS - 1) / kKS;
   const int gpr = K / p.gs;
-  const int32_t* flags = reinterpret_cast<const int32_t*>(p.prepared + p.p_flags);
-  if (lane < 3) tma_prefetch_desc(&p.act_map[lane]);
+  if (lane < 2) tma_prefetch_desc(&p.act_map[lane]);
   int slot = 0, item = 0;
   uint32_t phase = 0;
-  int seg = 0;
   const long long t_start = p.counters ? clock64() : 0;
   long long wait_cycles = 0;
   bool ok = true;
+  // Units are resolved from the shared-memory prefix; the segment record of
+  // the next unit is requested one unit ahead so its latency hides behind
+  // the current unit's stages.
+  int seg = 0;
+  while (L->units[seg + 1] <= (int)blockIdx.x) seg++;
+  WispSegment sg_next = p.segs[seg];
+  int seg_next = seg;
   for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
-    while (__ldg(p.units + seg + 1) <= u) seg++;
-    const WispSegment sg = p.segs[seg];
+    const WispSegment sg = sg_next;
+    seg = seg_next;
+    const int un = u + gridDim.x;
+    if (un < total) {
+      while (L->units[seg_next + 1] <= un) seg_next++;
+      sg_next = p.segs[seg_next];
+    }
     const int chunks = (sg.rows + kCols - 1) / kCols;
-    const int l = u - __ldg(p.units + seg);
-    const int rb = l / chunks, ch = l - rb * chunks;
+    const int l = u - L->units[seg];
+    const int rbk = l / chunks, ch = l - rbk * chunks;
     const int col0 = ch * kCols;
     const int n = min(kCols, sg.rows - col0);
-    const int mi = n <= 8 ? 0 : n <= 16 ? 1 : 2;  // token box of 8 / 16 / 32 rows
+    const int mi = n <= 8 ? 0 : 1;               // token box of 8 / 16 rows
     const uint32_t bq = (8u << mi) * 128;        // bytes of one token quarter box
-    const int row0 = rb * (MODE == SK_GATEUP ? kBoxRows : 2 * kBoxRows);
+    const int row0 = rbk * (MODE == SK_GATEUP ? kBoxRows : 2 * kBoxRows);
     const int row1 = MODE == SK_GATEUP ? row0 : row0 + kBoxRows;
     const bool v1 = MODE == SK_GATEUP || row1 < p.M;
     const int e0 = sg.expert * 3 + (MODE == SK_GATEUP ? 0 : 2);
     const int e1 = MODE == SK_GATEUP ? e0 + 1 : e0;
-    const bool hz0 = __ldg(flags + e0) & 1;
-    const bool hz1 = v1 && (__ldg(flags + e1) & 1);
+    const bool hz0 = (L->zbits[e0 >> 5] >> (e0 & 31)) & 1;
+    const bool hz1 = v1 && ((L->zbits[e1 >> 5] >> (e1 & 31)) & 1);
     const CUtensorMap* map0 =
         reinterpret_cast<const CUtensorMap*>(p.prepared + p.p_maps_sk + (size_t)e0 * sizeof(CUtensorMap));
     const CUtensorMap* map1 =
@@ -325,7 +354,7 @@ __device__ void sk_producer(const SkParams& p, uint8_t* ring, SkSmem* L, int tot
       uint8_t* st = ring + slot * kStageBytes;
       uint64_t* fb = &L->full[slot];
       if (lane == 0) {
-        *reinterpret_cast<StageHdr*>(st + kOffH) = hdr;
+        L->hdr[slot] = hdr;
         mbar_arrive_expect_tx(fb, bytes);
       }
       __syncwarp();
@@ -364,44 +393,44 @@ __device__ void sk_producer(const SkParams& p, uint8_t* ring, SkSmem* L, int tot
 // One full stage for a unit of at most 8 tokens (the decode case): all of
 // the warp's nibbles, token fragments and scales are read first and the
 // stage is released before any conversion, so the producer can refill it
-// while the MMAs run; consecutive scale groups (G per 256-K stage) use
-// alternating accumulator chains, so two groups' MMAs overlap per tile.
+// while the MMAs run (G scale groups per 256-K stage). Per quarter and tile
+// a 4-MMA chain (alternating register sets, so the next quarter's MMAs need
+// not wait for this quarter's fold) is folded into the accumulator times its
+// group's scale, then the zero-point term is added: the arithmetic, in the
+// same order, of the general path in sk_unit, so a token's result does not
+// depend on which path its unit took.
 template <int G>
-__device__ __forceinline__ void stage_single(float (&acc0)[4][4], float (&acc1)[4][4],
+__device__ __forceinline__ void stage_single(float (&acc0)[2][4], float (&acc1)[2][4],
                                              const uint8_t* st, int b0, int b1, int r0, int r1,
                                              int g, int t, bool hz0, bool hz1, SkSmem* L, int slot,
                                              int lane) {
   constexpr int QPG = kQ / G;  // quarters per scale group
   RawTile w0[kQ], w1[kQ];
-  BHalf<1> bq[kQ];
+  BQuarter<1> bq[kQ];
 #pragma unroll
   for (int q = 0; q < kQ; q++) {
-    load_tile(w0[q], st, b0, r0, q, t);
-    load_tile(w1[q], st, b1, r1, q, t);
+    load_tile(w0[q], st, b0, r0, b0, r0 + 8, q, t);
+    load_tile(w1[q], st, b1, r1, b1, r1 + 8, q, t);
     load_b<1>(bq[q], st, q, g, t);
   }
-  // scales and zero points of rows (r, r+8) as fp16 pairs
+  // scales and zero points of MMA rows g (low half) and g+8 (high half)
   __half2 s0[G], s1[G], z0[G], z1[G];
 #pragma unroll
   for (int j = 0; j < G; j++) {
-    s0[j] = group_pair_h2(st + kOffS + b0 * kScRun, j, r0);
-    s1[j] = group_pair_h2(st + kOffS + b1 * kScRun, j, r1);
-    z0[j] = hz0 ? group_pair_h2(st + kOffZ + b0 * kScRun, j, r0) : __half2{};
-    z1[j] = hz1 ? group_pair_h2(st + kOffZ + b1 * kScRun, j, r1) : __half2{};
+    s0[j] = __floats2half2_rn(row_scale(st, kOffS, b0, j, r0), row_scale(st, kOffS, b0, j, r0 + 8));
+    s1[j] = __floats2half2_rn(row_scale(st, kOffS, b1, j, r1), row_scale(st, kOffS, b1, j, r1 + 8));
+    z0[j] = hz0 ? __floats2half2_rn(row_scale(st, kOffZ, b0, j, r0), row_scale(st, kOffZ, b0, j, r0 + 8))
+                : __half2{};
+    z1[j] = hz1 ? __floats2half2_rn(row_scale(st, kOffZ, b1, j, r1), row_scale(st, kOffZ, b1, j, r1 + 8))
+                : __half2{};
   }
   __syncwarp();
   if (lane == 0) mbar_arrive(&L->empty[slot]);
 
-  // Two chain sets per tile, alternating by scale group; a chain is folded
-  // into the accumulator (times its group's scale) after its last quarter.
   float c0[2][4], c1[2][4];
 #pragma unroll
-  for (int j = 0; j < 2; j++)
-#pragma unroll
-    for (int e = 0; e < 4; e++) c0[j][e] = c1[j][e] = 0.f;
-#pragma unroll
   for (int q = 0; q < kQ; q++) {
-    const int j = q / QPG, ci = j & 1;
+    const int j = q / QPG, ci = q & 1;
     __half2 ag0[2][4], a80[2][4], ag1[2][4], a81[2][4];
     nib8_centered(w0[q].w[0].x, ag0[0]);
     nib8_centered(w0[q].w[0].y, ag0[1]);
@@ -415,31 +444,30 @@ __device__ __forceinline__ void stage_single(float (&acc0)[4][4], float (&acc1)[
     for (int m = 0; m < 4; m++) {
       const int wd = m >> 1, pp = 2 * (m & 1);
       const uint32_t b0v = u4_get(bq[q].v[wd][0], pp), b1v = u4_get(bq[q].v[wd][0], pp + 1);
-      hmma16816(c0[ci], h22u(ag0[wd][pp]), h22u(a80[wd][pp]), h22u(ag0[wd][pp + 1]),
-                h22u(a80[wd][pp + 1]), b0v, b1v);
-      hmma16816(c1[ci], h22u(ag1[wd][pp]), h22u(a81[wd][pp]), h22u(ag1[wd][pp + 1]),
-                h22u(a81[wd][pp + 1]), b0v, b1v);
+      if (m == 0) {
+        hmma16816_z(c0[ci], h22u(ag0[wd][pp]), h22u(a80[wd][pp]), h22u(ag0[wd][pp + 1]),
+                    h22u(a80[wd][pp + 1]), b0v, b1v);
+        hmma16816_z(c1[ci], h22u(ag1[wd][pp]), h22u(a81[wd][pp]), h22u(ag1[wd][pp + 1]),
+                    h22u(a81[wd][pp + 1]), b0v, b1v);
+      } else {
+        hmma16816(c0[ci], h22u(ag0[wd][pp]), h22u(a80[wd][pp]), h22u(ag0[wd][pp + 1]),
+                  h22u(a80[wd][pp + 1]), b0v, b1v);
+        hmma16816(c1[ci], h22u(ag1[wd][pp]), h22u(a81[wd][pp]), h22u(ag1[wd][pp + 1]),
+                  h22u(a81[wd][pp + 1]), b0v, b1v);
+      }
     }
-    if ((q + 1) % QPG == 0) {
-      const float2 f0 = __half22float2(s0[j]), f1 = __half22float2(s1[j]);
-      acc0[0][0] = fmaf(f0.x, c0[ci][0], acc0[0][0]);
-      acc0[0][1] = fmaf(f0.x, c0[ci][1], acc0[0][1]);
-      acc0[0][2] = fmaf(f0.y, c0[ci][2], acc0[0][2]);
-      acc0[0][3] = fmaf(f0.y, c0[ci][3], acc0[0][3]);
-      acc1[0][0] = fmaf(f1.x, c1[ci][0], acc1[0][0]);
-      acc1[0][1] = fmaf(f1.x, c1[ci][1], acc1[0][1]);
-      acc1[0][2] = fmaf(f1.y, c1[ci][2], acc1[0][2]);
-      acc1[0][3] = fmaf(f1.y, c1[ci][3], acc1[0][3]);
-#pragma unroll
-      for (int e = 0; e < 4; e++) c0[ci][e] = c1[ci][e] = 0.f;
-    }
-  }
-  if (hz0 | hz1) {
-#pragma unroll
-    for (int q = 0; q < kQ; q++) {
-      const int j = q / QPG;
+    const float2 f0 = __half22float2(s0[j]), f1 = __half22float2(s1[j]);
+    acc0[0][0] = fmaf(f0.x, c0[ci][0], acc0[0][0]);
+    acc0[0][1] = fmaf(f0.x, c0[ci][1], acc0[0][1]);
+    acc0[0][2] = fmaf(f0.y, c0[ci][2], acc0[0][2]);
+    acc0[0][3] = fmaf(f0.y, c0[ci][3], acc0[0][3]);
+    acc1[0][0] = fmaf(f1.x, c1[ci][0], acc1[0][0]);
+    acc1[0][1] = fmaf(f1.x, c1[ci][1], acc1[0][1]);
+    acc1[0][2] = fmaf(f1.y, c1[ci][2], acc1[0][2]);
+    acc1[0][3] = fmaf(f1.y, c1[ci][3], acc1[0][3]);
+    if (hz0 | hz1) {
       float xs[1][2];
-      half_sums<1>(bq[q], xs, t);
+      quarter_sums<1>(bq[q], xs, t);
       const float2 g0 = __half22float2(z0[j]), g1 = __half22float2(z1[j]);
       if (hz0) add_zeros<1>(acc0, xs, g0.x, g0.y);
       if (hz1) add_zeros<1>(acc1, xs, g1.x, g1.y);
@@ -456,12 +484,13 @@ __device__ bool sk_unit(const SkParams& p, uint8_t* ring, SkSmem* L, const Stage
                         long long& wait_cycles) {
   volatile int* abort = &L->abort;
   const int g = lane >> 2, t = lane & 3;
-  const int sig = ((g & 3) << 1) | (g >> 2);  // box row of MMA row g
+  const int sig = ((g & 3) << 1) | (g >> 2);  // box row (mod 8) of MMA row g
   const int K = MODE == SK_GATEUP ? p.M : p.I;
   const int nk = (K + kKS - 1) / kKS;
   const int qpg = p.gs / 64;  // quarters per scale group (1 or 2)
-  // Tiles: GATEUP gate rows r0.. (block 0) and up rows r0.. (block 1);
-  // DOWN rows r0.. and r0+16.. of block warp/4.
+  // Two tiles per warp; a tile's MMA rows g and g+8 are box rows r and r+8.
+  // GATEUP: gate rows 16w + sig (block 0) and the same up rows (block 1);
+  // DOWN: rows 32(w%4) + sig and +16 of block w/4.
   const int b0 = MODE == SK_GATEUP ? 0 : warp >> 2;
   const int b1 = MODE == SK_GATEUP ? 1 : warp >> 2;
   const int r0 = (MODE == SK_GATEUP ? 16 * warp : 32 * (warp & 3)) + sig;
@@ -470,11 +499,25 @@ __device__ bool sk_unit(const SkParams& p, uint8_t* ring, SkSmem* L, const Stage
   const bool hz0 = hdr.flags & (b0 ? HF_HZ1 : HF_HZ0);
   const bool hz1 = hdr.flags & (b1 ? HF_HZ1 : HF_HZ0);
 
-  float acc0[4][4], acc1[4][4];
+  float acc0[2][4], acc1[2][4];
 #pragma unroll
-  for (int nt = 0; nt < 4; nt++)
+  for (int nt = 0; nt < 2; nt++)
 #pragma unroll
-    for (int q = 0; q < 4; q++) acc0[nt][q] = acc1[nt][q] = 0.f;
+    for (int e = 0; e < 4; e++) acc0[nt][e] = acc1[nt][e] = 0.f;
+
+  // The down epilogue's token indices and router weights, requested now so
+  // that their latency hides behind the unit's stages.
+  int tok[NT][2];
+  float wgt[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      const int col = nt * 8 + 2 * t + j;
+      const bool need = MODE == SK_DOWN && p.mode == 0 && active && col < hdr.n;
+      tok[nt][j] = need ? __ldg(p.row_token + hdr.prow0 + col) : 0;
+      wgt[nt][j] = need ? __ldg(p.row_weight + hdr.prow0 + col) : 0.f;
+    }
 
   for (int kg = 0; kg < nk; kg++) {
     if (kg > 0) {
@@ -484,25 +527,27 @@ __device__ bool sk_unit(const SkParams& p, uint8_t* ring, SkSmem* L, const Stage
     }
     const uint8_t* st = ring + slot * kStageBytes;
     const int nq = min(kQ, (K - kg * kKS) / 64);
-    if (active && NT == 1 && nq == kQ && p.gs == 128) {
-      // Single n8 token tile, full stage, two scale groups (group size 64
-      // would need more registers than 9 warps per SM leave).
-      stage_single<2>(acc0, acc1, st, b0, b1, r0, r1, g, t, hz0, hz1, L, slot, lane);
+    if (active && NT == 1 && nq == kQ) {
+      if (p.gs == 128)
+        stage_single<2>(acc0, acc1, st, b0, b1, r0, r1, g, t, hz0, hz1, L, slot, lane);
+      else
+        stage_single<4>(acc0, acc1, st, b0, b1, r0, r1, g, t, hz0, hz1, L, slot, lane);
     } else if (active) {
 #pragma unroll
       for (int q = 0; q < kQ; q++) {
         if (q < nq) {
           RawTile w0, w1;
-          load_tile(w0, st, b0, r0, q, t);
-          load_tile(w1, st, b1, r1, q, t);
-          BHalf<NT> bq;
+          load_tile(w0, st, b0, r0, b0, r0 + 8, q, t);
+          load_tile(w1, st, b1, r1, b1, r1 + 8, q, t);
+          BQuarter<NT> bq;
           load_b<NT>(bq, st, q, g, t);
           const int grp = q / qpg;
-          float sa, sb, sc, sd, za = 0.f, zb = 0.f, zc = 0.f, zd = 0.f;
-          group_pair(st + kOffS + b0 * kScRun, grp, r0, sa, sb);
-          group_pair(st + kOffS + b1 * kScRun, grp, r1, sc, sd);
-          if (hz0) group_pair(st + kOffZ + b0 * kScRun, grp, r0, za, zb);
-          if (hz1) group_pair(st + kOffZ + b1 * kScRun, grp, r1, zc, zd);
+          const float sa = row_scale(st, kOffS, b0, grp, r0), sb = row_scale(st, kOffS, b0, grp, r0 + 8);
+          const float sc = row_scale(st, kOffS, b1, grp, r1), sd = row_scale(st, kOffS, b1, grp, r1 + 8);
+          const float za = hz0 ? row_scale(st, kOffZ, b0, grp, r0) : 0.f;
+          const float zb = hz0 ? row_scale(st, kOffZ, b0, grp, r0 + 8) : 0.f;
+          const float zc = hz1 ? row_scale(st, kOffZ, b1, grp, r1) : 0.f;
+          const float zd = hz1 ? row_scale(st, kOffZ, b1, grp, r1 + 8) : 0.f;
           if (q == nq - 1) {
             __syncwarp();
             if (lane == 0) mbar_arrive(&L->empty[slot]);
@@ -511,7 +556,7 @@ __device__ bool sk_unit(const SkParams& p, uint8_t* ring, SkSmem* L, const Stage
           tile_quarter<NT>(acc1, w1, bq, sc, sd);
           if (hz0 | hz1) {
             float xs[NT][2];
-            half_sums<NT>(bq, xs, t);
+            quarter_sums<NT>(bq, xs, t);
             if (hz0) add_zeros<NT>(acc0, xs, za, zb);
             if (hz1) add_zeros<NT>(acc1, xs, zc, zd);
           }
@@ -530,24 +575,22 @@ __device__ bool sk_unit(const SkParams& p, uint8_t* ring, SkSmem* L, const Stage
 #pragma unroll
   for (int nt = 0; nt < NT; nt++) {
 #pragma unroll
-    for (int q = 0; q < 4; q++) {
-      const int col = nt * 8 + 2 * t + (q & 1);
+    for (int e = 0; e < 4; e++) {
+      const int j = e & 1, col = nt * 8 + 2 * t + j;
       if (col >= hdr.n) continue;
-      const int rr = (q >> 1) ? 8 : 0;
+      const int rr = (e >> 1) ? 8 : 0;
       const int prow = hdr.prow0 + col;
       if (MODE == SK_GATEUP) {
         const int i = hdr.row0 + r0 + rr;
-        const float hv = silu(acc0[nt][q]) * acc1[nt][q];
+        const float hv = silu(acc0[nt][e]) * acc1[nt][e];
         p.h_out[(size_t)prow * p.I + k_interleave_slot(i)] = __float2half(hv);
       } else {
         const int base = hdr.row0 + b0 * kBoxRows;
         const int ma = base + r0 + rr, mb = base + r1 + rr;
-        const float y0 = acc0[nt][q], y1 = acc1[nt][q];
+        const float y0 = acc0[nt][e], y1 = acc1[nt][e];
         if (p.mode == 0) {
-          const int tok = __ldg(p.row_token + prow);
-          const float wgt = __ldg(p.row_weight + prow);
-          red_add_f32(p.out + (size_t)tok * p.M + ma, wgt * y0);
-          red_add_f32(p.out + (size_t)tok * p.M + mb, wgt * y1);
+          red_add_f32(p.out + (size_t)tok[nt][j] * p.M + ma, wgt[nt][j] * y0);
+          red_add_f32(p.out + (size_t)tok[nt][j] * p.M + mb, wgt[nt][j] * y1);
         } else {
           p.out[(size_t)prow * p.M + ma] = y0;
           p.out[(size_t)prow * p.M + mb] = y1;
@@ -570,13 +613,10 @@ __device__ void sk_consumer(const SkParams& p, uint8_t* ring, SkSmem* L, int tot
     const long long tw = p.counters ? clock64() : 0;
     if (!mbar_wait(&L->full[slot], phase, abort)) return;
     if (p.counters) wait_cycles += clock64() - tw;
-    const StageHdr hdr = *reinterpret_cast<const StageHdr*>(ring + slot * kStageBytes + kOffH);
-    const int nt = (hdr.n + 7) >> 3;
+    const StageHdr hdr = L->hdr[slot];
     bool ok;
-    if (nt == 1) ok = sk_unit<MODE, 1>(p, ring, L, hdr, warp, lane, slot, phase, wait_cycles);
-    else if (nt == 2) ok = sk_unit<MODE, 2>(p, ring, L, hdr, warp, lane, slot, phase, wait_cycles);
-    else if (nt == 3) ok = sk_unit<MODE, 3>(p, ring, L, hdr, warp, lane, slot, phase, wait_cycles);
-    else ok = sk_unit<MODE, 4>(p, ring, L, hdr, warp, lane, slot, phase, wait_cycles);
+    if (hdr.n <= 8) ok = sk_unit<MODE, 1>(p, ring, L, hdr, warp, lane, slot, phase, wait_cycles);
+    else ok = sk_unit<MODE, 2>(p, ring, L, hdr, warp, lane, slot, phase, wait_cycles);
     if (!ok) return;
   }
   if (p.counters && lane == 0) {
@@ -601,6 +641,9 @@ __global__ void __launch_bounds__(kThreads, 1) skinny_ffn_kernel(const __grid_co
     L->abort = 0;
     fence_barrier_init();
   }
+  for (int i = threadIdx.x; i <= p.nseg; i += blockDim.x) L->units[i] = __ldg(p.units + i);
+  const uint32_t* zb = reinterpret_cast<const uint32_t*>(p.prepared + p.p_zbits);
+  for (int w = threadIdx.x; w < (p.n_entries * 3 + 31) / 32; w += blockDim.x) L->zbits[w] = __ldg(zb + w);
   __syncthreads();
   if (warp == kCW)
     sk_producer<MODE>(p, ring, L, total, lane);
@@ -611,6 +654,7 @@ __global__ void __launch_bounds__(kThreads, 1) skinny_ffn_kernel(const __grid_co
 }
 
 constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + sizeof(SkSmem);
+static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 
 }  // namespace
 
@@ -618,14 +662,15 @@ namespace wb {
 
 struct SkLaunch {
   const uint8_t* prepared;
-  size_t p_maps_sk, p_flags, p_scales, p_zeros, p_mat_sc_bytes;
+  size_t p_maps_sk, p_zbits, p_scales, p_zeros, p_mat_sc_bytes;
   const WispSegment* segs;
   int nseg;
+  int n_entries;
   const int32_t* units_gu;
   const int32_t* units_dn;
   int M, I, gs;
-  const CUtensorMap* xp_maps;  // [3]: boxes of 8 / 16 / 32 rows
-  const CUtensorMap* h_maps;   // [3]
+  const CUtensorMap* xp_maps;  // [2]: boxes of 8 / 16 rows
+  const CUtensorMap* h_maps;   // [2]
   __half* h;
   const int* row_token;
   const float* row_weight;
@@ -636,6 +681,8 @@ struct SkLaunch {
 };  // mirrored in grouped.cu
 
 int skinny_max_rows() { return kSkMaxRows; }
+int skinny_max_segs() { return kMaxSegs; }
+int skinny_max_entries() { return kMaxEntries; }
 int skinny_cols() { return kCols; }
 int skinny_units_gateup(int I) { return I / kBoxRows; }
 int skinny_units_down(int M) { return (M + 2 * kBoxRows - 1) / (2 * kBoxRows); }
@@ -652,12 +699,13 @@ cudaError_t launch_skinny(const SkLaunch& L, int phase, int grid, cudaStream_t s
   memset(&p, 0, sizeof p);
   p.prepared = L.prepared;
   p.p_maps_sk = L.p_maps_sk;
-  p.p_flags = L.p_flags;
+  p.p_zbits = L.p_zbits;
   p.p_scales = L.p_scales;
   p.p_zeros = L.p_zeros;
   p.p_mat_sc_bytes = L.p_mat_sc_bytes;
   p.segs = L.segs;
   p.nseg = L.nseg;
+  p.n_entries = L.n_entries;
   p.M = L.M;
   p.I = L.I;
   p.gs = L.gs;
@@ -669,7 +717,7 @@ cudaError_t launch_skinny(const SkLaunch& L, int phase, int grid, cudaStream_t s
   p.error_flag = L.error_flag;
   p.counters = L.counters ? L.counters + phase * SC_COUNT : nullptr;
   const CUtensorMap* maps = phase == 0 ? L.xp_maps : L.h_maps;
-  for (int i = 0; i < 3; i++) p.act_map[i] = maps[i];
+  for (int i = 0; i < 2; i++) p.act_map[i] = maps[i];
   if (phase == 0) {
     p.units = L.units_gu;
     skinny_ffn_kernel<SK_GATEUP><<<grid, kThreads, kSmemBytes, st>>>(p);
