@@ -240,7 +240,8 @@ def main() -> None:
     if world == 1:
         layers = [MoeLayer(lw, T) for lw in layers_w]
     else:
-        layers = [EpLayer(spec, lw, T, rank, world) for lw in layers_w]
+        t_max = max(b - a for a, b in (block_range(T_all, world, q) for q in range(world)))
+        layers = [EpLayer(spec, lw, T, rank, world, max_tokens=t_max) for lw in layers_w]
     outs = [torch.empty((T, spec.hidden), dtype=torch.float32, device=dev) for _ in range(L)]
     xs = [x0] + [torch.empty_like(x0) for _ in range(L - 1)]
 
@@ -388,7 +389,14 @@ def main() -> None:
            "h2d_bytes_per_step": x_host.numel() * 2 * world,
            "d2h_bytes_per_step": out_host.numel() * 4 * world}
 
-    launches_per_layer = 11 if world == 1 else 12 + (4 if spec.has_shared else 0)
+    # Our kernels per layer: route 2 (logits, top-k) + plan 3 (count,
+    # segments, fill) + grouped FFN 8 (4 tile/unit planners, register-path
+    # and tensor-core kernels for gate/up and down); single GPU: + pack 1;
+    # expert-parallel: + send-pack, receive-plan, gather, scatter, combine,
+    # and for the shared expert pack 1 + grouped 8. Plus one rms_rescale
+    # between layers.
+    per_layer = 14 if world == 1 else 18 + (9 if spec.has_shared else 0)
+    launches_per_step = per_layer * L + (L - 1)
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
@@ -404,7 +412,7 @@ def main() -> None:
                 "frac_of_measured": round(hbm_gbs / peaks["hbm_gbs"], 4),
                 "frac_of_8tbs": round(hbm_gbs / 8000.0, 4), "experts_touched_per_layer": used},
         "roofline": roofline, "e2e": e2e, "clocks": clk,
-        "gpu_launches": launches_per_layer * L * args.steps,
+        "gpu_launches": launches_per_step * args.steps,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(spec)

@@ -290,6 +290,51 @@ WispError wisp_b200_combine_rows(const float* d_y, const int* d_row_token, const
                                  int n_rows, int hidden, float* d_out, cudaStream_t stream,
                                  WispErrCtx* err);
 
+/* --------------------------------------------------------------------------
+ * Expert-parallel exchange (no counterpart in the reference, which runs on one
+ * GPU). Experts are sharded in contiguous blocks of n_experts/world; rows
+ * travel in fixed-size blocks of `cap` rows per rank pair (cap >= the rows
+ * one rank routes, tokens * top_k), so all counts stay on the device.
+ * ------------------------------------------------------------------------ */
+
+/* Rows of a dispatch plan (d_plan_segs / d_row_token from
+ * wisp_b200_dispatch_plan, rows sorted by expert) into the send buffer:
+ * row p goes to slot q*cap + (p - first row for rank q), q = owner of its
+ * expert, as fp16 in interleaved K order. d_xsend [world*cap x hidden];
+ * d_slot[p] receives the slot (the combine reads the returned row there). */
+WispError wisp_b200_ep_send_pack(const uint16_t* d_x, int hidden, const int* d_row_token,
+                                 const WispSegment* d_plan_segs, int n_experts, int n_rows,
+                                 int world, int cap, uint16_t* d_xsend, int* d_slot,
+                                 cudaStream_t stream, WispErrCtx* err);
+
+/* Receive side, from the per-source row counts d_recv_counts [world x e_loc]
+ * (source s's block starts at row s*cap; world * e_loc <= 1024): the
+ * received rows are gathered expert-contiguous (expert, then source) so that
+ * each local expert is one segment: d_segs [e_loc] over the gathered rows,
+ * d_src_pos[j] = receive row of gathered row j, *d_total = rows received.
+ * d_src_pos holds world*cap entries. */
+WispError wisp_b200_ep_recv_plan(const int* d_recv_counts, int world, int e_loc, int cap,
+                                 WispSegment* d_segs, int* d_src_pos, int* d_total,
+                                 cudaStream_t stream, WispErrCtx* err);
+
+/* d_sorted[j] = d_recv[d_src_pos[j]] for j < *d_total (fp16 rows; max_rows
+ * bounds the launch, normally world*cap). */
+WispError wisp_b200_ep_gather_rows(const uint16_t* d_recv, const int* d_src_pos, const int* d_total,
+                                   int max_rows, int hidden, uint16_t* d_sorted,
+                                   cudaStream_t stream, WispErrCtx* err);
+
+/* d_recv[d_src_pos[j]] = d_sorted[j] for j < *d_total (fp32 rows): FFN
+ * results back into the source blocks for the return exchange. */
+WispError wisp_b200_ep_scatter_rows(const float* d_sorted, const int* d_src_pos, const int* d_total,
+                                    int max_rows, int hidden, float* d_recv, cudaStream_t stream,
+                                    WispErrCtx* err);
+
+/* d_out[row_token[p]] += row_weight[p] * d_y[d_slot[p]] for p < n_rows (fp32
+ * rows returned in the send layout; atomic adds). */
+WispError wisp_b200_ep_combine(const float* d_y, const int* d_slot, const int* d_row_token,
+                               const float* d_row_weight, int n_rows, int hidden, float* d_out,
+                               cudaStream_t stream, WispErrCtx* err);
+
 /* Between stacked layers: d_out[t] = bf16(d_in[t] / rms(d_in[t])), fp32 in. */
 WispError wisp_b200_rms_rescale(const float* d_in, uint16_t* d_out, int tokens, int hidden,
                                 float eps, cudaStream_t stream, WispErrCtx* err);

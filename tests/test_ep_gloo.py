@@ -44,8 +44,10 @@ class CpuOps:
     def plan(self, cfg, idx, w, counts, segs, row_token, row_weight):
         ii, ww = idx.numpy(), w.numpy()
         T, k = ii.shape
+        sv = segs.numpy().view(np.int32).reshape(-1, 4)
         p = 0
         for e in range(cfg.n_experts):
+            sv[e] = (e, p, 0, 0)
             n = 0
             for t in range(T):
                 for j in range(k):
@@ -55,6 +57,50 @@ class CpuOps:
                         p += 1
                         n += 1
             counts[e] = n
+            sv[e, 2] = n
+
+    def send_pack(self, x, row_token, plan_segs, n_experts, n_rows, world, cap, xsend, slot):
+        e_loc = n_experts // world
+        begin = plan_segs.numpy().view(np.int32).reshape(-1, 4)[:, 1]
+        xd = x.double()
+        for p in range(n_rows):
+            q = max(r for r in range(world) if begin[r * e_loc] <= p)
+            d = q * cap + p - int(begin[q * e_loc])
+            slot[p] = d
+            xsend[d] = xd[int(row_token[p])]
+
+    def recv_plan(self, recv_counts, world, e_loc, cap, segs, src_pos, total):
+        rc = recv_counts.numpy().reshape(world, e_loc)
+        sv = segs.numpy().view(np.int32).reshape(-1, 4)
+        src_off = np.concatenate([np.zeros((world, 1), np.int64), np.cumsum(rc, axis=1)[:, :-1]],
+                                 axis=1) + np.arange(world)[:, None] * cap
+        j = 0
+        for e in range(e_loc):
+            b = j
+            for s in range(world):
+                for i in range(int(rc[s, e])):
+                    src_pos[j] = int(src_off[s, e]) + i
+                    j += 1
+            sv[e] = (e, b, j - b, 0)
+        total[0] = j
+
+    def gather_rows(self, recv, src_pos, total, max_rows, sorted_rows):
+        for j in range(int(total[0])):
+            sorted_rows[j] = recv[int(src_pos[j])]
+
+    def scatter_rows(self, sorted_rows, src_pos, total, max_rows, recv):
+        for j in range(int(total[0])):
+            recv[int(src_pos[j])] = sorted_rows[j]
+
+    def grouped_dev(self, cfg, lw, segs, n_segs, rows, xp, h, mode, row_token, row_weight, out,
+                    tiles, flag):
+        sv = segs.numpy().view(np.int32).reshape(-1, 4)[:n_segs]
+        self.grouped(cfg, lw, [(int(e), int(b), int(r)) for e, b, r, _ in sv], rows, xp, h, mode,
+                     row_token, row_weight, out, tiles, flag)
+
+    def ep_combine(self, y, slot, row_token, row_weight, n_rows, out):
+        for p in range(n_rows):
+            out[int(row_token[p])] += float(row_weight[p]) * y[int(slot[p])]
 
     def pack(self, x, src, n_rows, xp):
         xd = x.double()
@@ -97,7 +143,9 @@ def _worker(rank, world, port, outdir, spec, mode):
         layers, x = synth.make_model(spec, "cpu", keep=keep)
         lw = layers[0]
         t0, t1 = block_range(spec.tokens, world, rank)
-        layer = EpLayer(spec, lw, t1 - t0, rank, world, ops=CpuOps(orc, lw), device=torch.device("cpu"))
+        t_max = max(b - a for a, b in (block_range(spec.tokens, world, q) for q in range(world)))
+        layer = EpLayer(spec, lw, t1 - t0, rank, world, ops=CpuOps(orc, lw), device=torch.device("cpu"),
+                        max_tokens=t_max)
         if mode == "die" and rank == 1:
             raise SystemExit(3)          # leaves before the first collective
         out = torch.zeros((t1 - t0, spec.hidden), dtype=torch.float32)

@@ -9,13 +9,18 @@ equal the single-GPU path's. Layout:
   the shared expert and the router are replicated;
 * each rank owns a contiguous slice of the tokens.
 
-One layer on rank r:
+One layer on rank r, with every count kept on the device (no host round
+trip between routing and the expert FFN):
   route own tokens -> plan (rows grouped by expert, hence by owner rank)
-  -> pack rows (fp16) -> exchange per-expert row counts (all_to_all) ->
-  dispatch rows (all_to_all_v) -> grouped FFN over the received rows,
-  grouped expert-major (mode 1: unweighted fp32 rows) -> return rows
-  (all_to_all_v) -> shared expert on own tokens (mode 0) + weighted combine
-  of the returned rows.
+  -> pack rows (fp16) into a send buffer of `world` fixed blocks of `cap`
+  rows -> exchange per-expert row counts (all_to_all) -> exchange the row
+  blocks (all_to_all, equal splits) -> gather the received rows expert-
+  contiguous (one segment per local expert, as on one GPU) -> grouped FFN
+  (mode 1: unweighted fp32 rows) -> scatter the results into the source
+  blocks -> return the row blocks (all_to_all) -> shared expert on own
+  tokens (mode 0) + weighted combine of the returned rows.
+cap = tokens * top_k, the most rows one rank can send to one destination;
+the padding rows are exchanged but never computed or read.
 
 Collectives go through torch.distributed (NCCL between GPUs); every rank
 issues the same collectives in the same order. The compute steps go through
@@ -103,6 +108,35 @@ class CudaOps:
         abi.call("wisp_b200_combine_rows", y.data_ptr(), row_token.data_ptr(), row_weight.data_ptr(),
                  n_rows, out.shape[1], out.data_ptr(), _stream())
 
+    def send_pack(self, x, row_token, plan_segs, n_experts, n_rows, world, cap, xsend, slot):
+        abi.call("wisp_b200_ep_send_pack", x.data_ptr(), x.shape[1], row_token.data_ptr(),
+                 plan_segs.data_ptr(), n_experts, n_rows, world, cap, xsend.data_ptr(),
+                 slot.data_ptr(), _stream())
+
+    def recv_plan(self, recv_counts, world, e_loc, cap, segs, src_pos, total):
+        abi.call("wisp_b200_ep_recv_plan", recv_counts.data_ptr(), world, e_loc, cap,
+                 segs.data_ptr(), src_pos.data_ptr(), total.data_ptr(), _stream())
+
+    def gather_rows(self, recv, src_pos, total, max_rows, sorted_rows):
+        abi.call("wisp_b200_ep_gather_rows", recv.data_ptr(), src_pos.data_ptr(), total.data_ptr(),
+                 max_rows, recv.shape[1], sorted_rows.data_ptr(), _stream())
+
+    def scatter_rows(self, sorted_rows, src_pos, total, max_rows, recv):
+        abi.call("wisp_b200_ep_scatter_rows", sorted_rows.data_ptr(), src_pos.data_ptr(),
+                 total.data_ptr(), max_rows, recv.shape[1], recv.data_ptr(), _stream())
+
+    def grouped_dev(self, cfg, lw, segs, n_segs, rows, xp, h, mode, row_token, row_weight, out,
+                    tiles, flag):
+        abi.call("wisp_b200_grouped_ffn", C.byref(cfg), lw.prepare().data_ptr(), lw.table.data_ptr(),
+                 lw.n_entries, segs.data_ptr(), n_segs, max(rows, 1), xp.data_ptr(), h.data_ptr(),
+                 mode, None if row_token is None else row_token.data_ptr(),
+                 None if row_weight is None else row_weight.data_ptr(), out.data_ptr(),
+                 tiles.data_ptr(), flag.data_ptr(), _stream())
+
+    def ep_combine(self, y, slot, row_token, row_weight, n_rows, out):
+        abi.call("wisp_b200_ep_combine", y.data_ptr(), slot.data_ptr(), row_token.data_ptr(),
+                 row_weight.data_ptr(), n_rows, out.shape[1], out.data_ptr(), _stream())
+
     def act_dtype(self):
         return torch.float16
 
@@ -115,7 +149,11 @@ class EpLayer:
     weight is the full one."""
 
     def __init__(self, spec: MoeSpec, lw: LayerWeights, tokens: int, rank: int, world: int,
-                 group=None, ops=None, device=None):
+                 group=None, ops=None, device=None, max_tokens: int | None = None):
+        """``max_tokens``: the largest token count of any rank (the exchange
+        blocks must have one size on every rank); when None it is agreed on
+        with one all_reduce over the group, so every rank must construct its
+        layers in the same order."""
         assert spec.n_experts % world == 0, "experts must split evenly over the ranks"
         self.spec, self.lw, self.T, self.rank, self.world = spec, lw, tokens, rank, world
         self.group = group
@@ -141,21 +179,38 @@ class EpLayer:
         self.segs = torch.empty(16 * spec.n_experts, dtype=torch.uint8, device=dev)
         self.row_token = torch.empty(T * k, dtype=torch.int32, device=dev)
         self.row_weight = torch.empty(T * k, dtype=torch.float32, device=dev)
-        self.xp = torch.empty((T * k, M), dtype=adt, device=dev)
         self.flag = torch.zeros(1, dtype=torch.int32, device=dev)
-        nseg_max = max(self.e_loc * world, 1) + 1
-        self.tiles = torch.empty(abi.lib().wisp_b200_tiles_words(nseg_max) if adt == torch.float16 else 1,
-                                 dtype=torch.int32, device=dev)
-        # Worst case every token of every rank routes all k slots here.
-        self.cap = T * k * world
-        self.xr = torch.empty((self.cap, M), dtype=adt, device=dev)
-        self.hr = torch.empty((max(self.cap, T), I), dtype=adt, device=dev)
-        self.yr = torch.empty((self.cap, M), dtype=torch.float32, device=dev)
-        self.yret = torch.empty((T * k, M), dtype=torch.float32, device=dev)
+        # Exchange blocks: `cap` rows per rank pair (all of a rank's rows may
+        # go to one owner), the same on every rank.
+        if max_tokens is None:
+            t = torch.tensor([T], dtype=torch.int64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+            max_tokens = int(t.item())
+        self.cap = max_tokens * k
+        R = self.cap * world
+        self.slot = torch.empty(T * k, dtype=torch.int32, device=dev)
+        self.xsend = torch.empty((R, M), dtype=adt, device=dev)
+        self.xrecv = torch.empty((R, M), dtype=adt, device=dev)
+        self.hr = torch.empty((max(R, T), I), dtype=adt, device=dev)
+        self.yr = torch.empty((R, M), dtype=torch.float32, device=dev)
+        self.yback = torch.empty((R, M), dtype=torch.float32, device=dev)
+        self.xsorted = torch.empty((R, M), dtype=adt, device=dev)
+        self.ysorted = torch.empty((R, M), dtype=torch.float32, device=dev)
+        self.src_pos = torch.empty(R, dtype=torch.int32, device=dev)
+        self.total = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.cnt_recv = torch.empty(self.e_loc * world, dtype=torch.int32, device=dev)
+        self.n_rsegs = self.e_loc
+        self.rsegs = torch.empty(16 * self.n_rsegs, dtype=torch.uint8, device=dev)
+        self.tiles = torch.empty(abi.lib().wisp_b200_tiles_words(self.n_rsegs + 1)
+                                 if adt == torch.float16 else 1, dtype=torch.int32, device=dev)
         if spec.has_shared:
             self.xs = torch.empty((T, M), dtype=adt, device=dev)
             self.sh_token = torch.arange(T, dtype=torch.int32, device=dev)
             self.sh_weight = torch.ones(T, dtype=torch.float32, device=dev)
+            self.sh_seg = torch.empty(16, dtype=torch.uint8, device=dev)
+            seg = abi.WispSegment()
+            seg.expert, seg.row_begin, seg.rows = self.e_loc, 0, T
+            self.sh_seg.copy_(torch.frombuffer(bytearray(bytes(seg)), dtype=torch.uint8))
 
     def forward(self, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         """x: bf16 [T, M] (this rank's tokens) -> out fp32 [T, M]."""
@@ -163,30 +218,28 @@ class EpLayer:
         ops.route(self.cfg_route, self.lw, x, self.idx, self.w, self.logits)
         ops.plan(self.cfg_route, self.idx, self.w, self.counts, self.segs, self.row_token,
                  self.row_weight)
-        ops.pack(x, self.row_token, T * k, self.xp)
-        # 1. per-expert row counts to the owners (fixed-size exchange)
-        cnt_recv = torch.empty(self.e_loc * world, dtype=torch.int32, device=self.dev)
-        dist.all_to_all_single(cnt_recv, self.counts, group=self.group)
-        counts_h = self.counts.cpu().numpy()
-        recv_counts = cnt_recv.cpu().numpy().reshape(world, self.e_loc).astype(np.int64)
-        send = send_splits(counts_h, spec.n_experts, world)
-        segs, recv = recv_layout(recv_counts)
-        R = sum(recv)
-        # 2. dispatch rows
-        dist.all_to_all_single(self.xr[:R], self.xp[:T * k], output_split_sizes=recv,
-                               input_split_sizes=send, group=self.group)
-        # 3. local experts over the received rows (unweighted fp32 rows)
-        if R > 0:
-            ops.grouped(self.cfg_loc, self.lw, segs, R, self.xr, self.hr, 1, None, None,
-                        self.yr, self.tiles, self.flag)
-        # 4. return rows to their tokens' ranks
-        dist.all_to_all_single(self.yret, self.yr[:R], output_split_sizes=send,
-                               input_split_sizes=recv, group=self.group)
-        # 5. shared expert on own tokens, then the weighted combine
+        ops.send_pack(x, self.row_token, self.segs, spec.n_experts, T * k, world, self.cap,
+                      self.xsend, self.slot)
+        # 1. per-expert row counts to the owners, then the row blocks
+        dist.all_to_all_single(self.cnt_recv, self.counts, group=self.group)
+        dist.all_to_all_single(self.xrecv, self.xsend, group=self.group)
+        # 2. local experts over the received rows, gathered so that each
+        #    expert is one segment (unweighted fp32 rows), then scattered
+        #    back into the source blocks
+        R = self.cap * world
+        ops.recv_plan(self.cnt_recv, world, self.e_loc, self.cap, self.rsegs, self.src_pos,
+                      self.total)
+        ops.gather_rows(self.xrecv, self.src_pos, self.total, R, self.xsorted)
+        ops.grouped_dev(self.cfg_loc, self.lw, self.rsegs, self.n_rsegs, R, self.xsorted,
+                        self.hr, 1, None, None, self.ysorted, self.tiles, self.flag)
+        ops.scatter_rows(self.ysorted, self.src_pos, self.total, R, self.yr)
+        # 3. rows back to their tokens' ranks
+        dist.all_to_all_single(self.yback, self.yr, group=self.group)
+        # 4. shared expert on own tokens, then the weighted combine
         out.zero_()
         if spec.has_shared:
             ops.pack(x, None, T, self.xs)
-            ops.grouped(self.cfg_loc, self.lw, [(self.e_loc, 0, T)], T, self.xs, self.hr, 0,
-                        self.sh_token, self.sh_weight, out, self.tiles, self.flag)
-        ops.combine(self.yret, self.row_token, self.row_weight, T * k, out)
+            ops.grouped_dev(self.cfg_loc, self.lw, self.sh_seg, 1, T, self.xs, self.hr, 0,
+                            self.sh_token, self.sh_weight, out, self.tiles, self.flag)
+        ops.ep_combine(self.yback, self.slot, self.row_token, self.row_weight, T * k, out)
         return out
