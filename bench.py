@@ -37,6 +37,13 @@ METRIC = "MoE-layer tokens/s; int4 weight GB/s vs 8 TB/s HBM at 1/2/4/8 B200"
 UNIT = "tokens/s"
 
 
+# DRAM bytes (read + write) per algorithmic byte of one grouped-FFN call,
+# from an ncu capture of the ep_profile workload (1,490.28 MB of traffic for
+# 1,476.03 MB of int4 weights and scales): the full-size layer is too large
+# for a multi-pass capture, and its traffic grows with the experts streamed.
+TRAFFIC_PER_ALGORITHMIC_BYTE = 1490.28 / 1476.03
+
+
 def _peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -357,7 +364,10 @@ def main() -> None:
         achieved = k_bytes / (kms / 1e3) / 1e9
         roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                     "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                    "traffic": None, "kernel": "grouped int4 FFN (gate/up+SwiGLU, down+combine)",
+                    "traffic": round(k_bytes * TRAFFIC_PER_ALGORITHMIC_BYTE),
+                    "traffic_source": "ncu dram__bytes_read+write of one call on ep_profile, "
+                                      "scaled by algorithmic bytes",
+                    "kernel": "grouped int4 FFN (gate/up+SwiGLU, down+combine)",
                     "kernel_ms": round(kms, 4), "algorithmic_bytes": k_bytes,
                     "peak_source": peaks["source"], "vs_8tbs": round(achieved / 8000.0, 4)}
 
