@@ -27,8 +27,8 @@ from wisp_b200.ep import EpLayer, block_range
 pytestmark = pytest.mark.gpu
 
 # Softmax top-4 of 16 experts + shared expert. 64 tokens: decode-sized
-# segments on the register-path kernel. 600 skewed tokens: segments (and
-# each rank's 300-row shared-expert segment) above 256 rows run on the
+# segments, mostly on the register-path kernel. 600 skewed tokens: most
+# segments (and each rank's 300-row shared-expert segment) run on the
 # tensor-core kernel.
 SPECS = [
     synth.MoeSpec("ep_gpu", 1024, 512, 16, 4, group_size=128, has_shared=True, tokens=64, seed=11),

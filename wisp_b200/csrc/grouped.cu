@@ -615,9 +615,13 @@ __global__ void plan_tiles_kernel(const WispSegment* __restrict__ segs, int nseg
 }
 
 // Units of the register-path kernel: `per_seg` row blocks per chunk of `cols`
-// rows, for every segment of 1..max_rows rows.
+// rows, for every segment of 1..max_rows rows, times a K split: when fewer
+// than `target` units would exist, each is cut into up to `max_ksplit`
+// K ranges (at most `nk`, one stage each at least), whose partial sums the
+// down epilogue adds atomically. units[nseg + 1] receives the split.
 __global__ void plan_units_kernel(const WispSegment* __restrict__ segs, int nseg, int per_seg,
-                                  int cols, int max_rows, int32_t* __restrict__ units) {
+                                  int cols, int max_rows, int max_ksplit, int nk, int target,
+                                  int32_t* __restrict__ units) {
   __shared__ int32_t warp_tot[32];
   __shared__ int32_t carry;
   if (threadIdx.x == 0) carry = 0;
@@ -654,7 +658,16 @@ __global__ void plan_units_kernel(const WispSegment* __restrict__ segs, int nseg
     if (threadIdx.x == blockDim.x - 1) carry = incl;
     __syncthreads();
   }
-  if (threadIdx.x == 0) units[nseg] = carry;
+  __syncthreads();
+  const int total = carry;
+  int ks = 1;
+  if (total > 0 && total < target) ks = min(min(max_ksplit, nk), (target + total - 1) / total);
+  if (ks < 1) ks = 1;
+  for (int i = threadIdx.x; i < nseg; i += blockDim.x) units[i] *= ks;
+  if (threadIdx.x == 0) {
+    units[nseg] = total * ks;
+    units[nseg + 1] = ks;
+  }
 }
 
 // Scales (and zero points) of every prepared matrix, transposed from
@@ -805,6 +818,7 @@ int skinny_max_rows();
 int skinny_max_segs();
 int skinny_max_entries();
 int skinny_cols();
+int skinny_stages(int K);
 int skinny_units_gateup(int I);
 int skinny_units_down(int M);
 cudaError_t launch_skinny(const SkLaunch& L, int phase, int grid, cudaStream_t st);
@@ -882,7 +896,7 @@ extern "C" WispError wisp_b200_prepare_experts(const WispMoeConfig* cfg,
 // Tables: tensor-core gate/up and down [prefix S+1 | bn S] each, then the
 // register path's gate/up and down unit prefixes [S+1] each.
 extern "C" size_t wisp_b200_tiles_words(int n_segs) {
-  return (size_t)(2 * (2 * n_segs + 1) + 2 * (n_segs + 1));
+  return (size_t)(2 * (2 * n_segs + 1) + 2 * (n_segs + 2));
 }
 
 extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void* d_prepared,
@@ -948,14 +962,19 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
   gu.tiles = d_tiles;
   dn.tiles = d_tiles + tw;
   int32_t* units_gu = d_tiles + 2 * tw;
-  int32_t* units_dn = units_gu + (n_segs + 1);
+  int32_t* units_dn = units_gu + (n_segs + 2);
   plan_tiles_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, I / BM, sk_rows, d_tiles);
   plan_tiles_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, M / BM, sk_rows, d_tiles + tw);
   const int skc = wb::skinny_cols();
+  // Gate/up cannot split K (SwiGLU needs whole sums), nor can mode 1 (plain
+  // row stores); the weighted down projection splits K when it has fewer
+  // than two units per SM.
+  const int grid_sm = num_sms();
   plan_units_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, wb::skinny_units_gateup(I), skc,
-                                            sk_rows, units_gu);
+                                            sk_rows, 1, 1, 0, units_gu);
   plan_units_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, wb::skinny_units_down(M), skc,
-                                            sk_rows, units_dn);
+                                            sk_rows, mode == 0 ? 8 : 1, wb::skinny_stages(I),
+                                            2 * grid_sm, units_dn);
   CUtensorMap sk_xp[2], sk_h[2];
   for (int i = 0; i < 2; i++) {
     if (!encode_rows_map(&sk_xp[i], d_xp, rows_capacity, M, 8 << i) ||

@@ -37,7 +37,9 @@
 //               (Sixteen one-tile warps, four per scheduler, measured
 //               slower: every warp re-reads the token fragments.)
 //
-// Work unit = (segment, weight row block, chunk of up to 16 tokens):
+// Work unit = (segment, weight row block, chunk of up to 16 tokens, and for
+// a weighted down projection with fewer than two units per SM a part of a K
+// split, whose partial sums the epilogue adds atomically):
 //   GATEUP: 128 intermediate rows i of gate and of up; warp w takes rows
 //           16w..16w+15 of both -> h = silu(g) * u written to H (fp16,
 //           interleaved K order).
@@ -71,7 +73,11 @@ constexpr int kCW = 8;                        // consumer warps, two 16-row tile
 constexpr int kThreads = (kCW + 1) * 32;      // + one producer warp
 constexpr int kStages = 5;
 constexpr int kCols = 16;                     // tokens per unit
-constexpr int kSkMaxRows = 256;               // default routing threshold
+// Default routing threshold: segments of up to 16 rows run here, larger ones
+// on the tcgen05 kernel (a larger segment costs this kernel one weight pass
+// per 16-token chunk; measured crossover on B200: prefill-shaped layers run
+// 1.5x faster at 16 than at 256, decode layers are within 3 %).
+constexpr int kSkMaxRows = 16;
 constexpr int kKS = 256;                      // K per stage
 constexpr int kQ = kKS / 64;                  // 64-K quarters per stage
 constexpr int kBoxRows = 128;
@@ -96,6 +102,9 @@ struct __align__(16) StageHdr {
   int n;      // tokens in the unit (1..16)
   int row0;   // first weight row of the unit
   int flags;  // HF_*: zero points of block 0 / 1, block 1 inside the matrix
+  int kg0;    // first 256-K stage of the unit's K range
+  int nst;    // stages in the unit (the whole K, or one part of a K split)
+  int pad[2];
 };
 
 struct SkSmem {
@@ -103,7 +112,7 @@ struct SkSmem {
   uint64_t empty[kStages];
   StageHdr hdr[kStages];
   int abort;
-  int32_t units[kMaxSegs + 1];           // unit prefix per segment
+  int32_t units[kMaxSegs + 2];           // unit prefix per segment, then the K split
   uint32_t zbits[kMaxEntries * 3 / 32];  // zero-point flag per matrix entry
 };
 
@@ -284,6 +293,7 @@ __device__ void sk_producer(const SkParams& p, uint8_t* ring, SkSmem* L, int tot
   const int K = MODE == SK_GATEUP ? p.M : p.I;
   const int nk = (K + kKS - 1) / kKS;
   const int gpr = K / p.gs;
+  const int ksplit = L->units[p.nseg + 1];
   if (lane < 2) tma_prefetch_desc(&p.act_map[lane]);
   int slot = 0, item = 0;
   uint32_t phase = 0;
@@ -307,7 +317,11 @@ __device__ void sk_producer(const SkParams& p, uint8_t* ring, SkSmem* L, int tot
     }
     const int chunks = (sg.rows + kCols - 1) / kCols;
     const int l = u - L->units[seg];
-    const int rbk = l / chunks, ch = l - rbk * chunks;
+    // l = (row block * ksplit + K part) * chunks + chunk: the chunks of one
+    // weight tile are consecutive units
+    const int ch = l % chunks, rest = l / chunks;
+    const int ks = rest % ksplit, rbk = rest / ksplit;
+    const int kg0 = ks * nk / ksplit, kg1 = (ks + 1) * nk / ksplit;
     const int col0 = ch * kCols;
     const int n = min(kCols, sg.rows - col0);
     const int mi = n <= 8 ? 0 : 1;               // token box of 8 / 16 rows
@@ -334,11 +348,13 @@ __device__ void sk_producer(const SkParams& p, uint8_t* ring, SkSmem* L, int tot
     hdr.n = n;
     hdr.row0 = row0;
     hdr.flags = (hz0 ? HF_HZ0 : 0) | (hz1 ? HF_HZ1 : 0) | (v1 ? HF_V1 : 0);
+    hdr.kg0 = kg0;
+    hdr.nst = kg1 - kg0;
     if (lane == 0) {
       tma_prefetch_desc(map0);
       if (MODE == SK_GATEUP) tma_prefetch_desc(map1);
     }
-    for (int kg = 0; kg < nk; kg++, item++) {
+    for (int kg = kg0; kg < kg1; kg++, item++) {
       // quarters in this stage (the last one holds 2 when K % 256 == 128)
       const int nq = min(kQ, (K - kg * kKS) / 64);
       const uint32_t scb = (uint32_t)(nq * 64 / p.gs) * kBoxRows * 2;
@@ -486,7 +502,6 @@ __device__ bool sk_unit(const SkParams& p, uint8_t* ring, SkSmem* L, const Stage
   const int g = lane >> 2, t = lane & 3;
   const int sig = ((g & 3) << 1) | (g >> 2);  // box row (mod 8) of MMA row g
   const int K = MODE == SK_GATEUP ? p.M : p.I;
-  const int nk = (K + kKS - 1) / kKS;
   const int qpg = p.gs / 64;  // quarters per scale group (1 or 2)
   // Two tiles per warp; a tile's MMA rows g and g+8 are box rows r and r+8.
   // GATEUP: gate rows 16w + sig (block 0) and the same up rows (block 1);
@@ -519,14 +534,14 @@ __device__ bool sk_unit(const SkParams& p, uint8_t* ring, SkSmem* L, const Stage
       wgt[nt][j] = need ? __ldg(p.row_weight + hdr.prow0 + col) : 0.f;
     }
 
-  for (int kg = 0; kg < nk; kg++) {
-    if (kg > 0) {
+  for (int kk = 0; kk < hdr.nst; kk++) {
+    if (kk > 0) {
       const long long tw = p.counters ? clock64() : 0;
       if (!mbar_wait(&L->full[slot], phase, abort)) return false;
       if (p.counters) wait_cycles += clock64() - tw;
     }
     const uint8_t* st = ring + slot * kStageBytes;
-    const int nq = min(kQ, (K - kg * kKS) / 64);
+    const int nq = min(kQ, (K - (hdr.kg0 + kk) * kKS) / 64);
     if (active && NT == 1 && nq == kQ) {
       if (p.gs == 128)
         stage_single<2>(acc0, acc1, st, b0, b1, r0, r1, g, t, hz0, hz1, L, slot, lane);
@@ -641,7 +656,7 @@ __global__ void __launch_bounds__(kThreads, 1) skinny_ffn_kernel(const __grid_co
     L->abort = 0;
     fence_barrier_init();
   }
-  for (int i = threadIdx.x; i <= p.nseg; i += blockDim.x) L->units[i] = __ldg(p.units + i);
+  for (int i = threadIdx.x; i <= p.nseg + 1; i += blockDim.x) L->units[i] = __ldg(p.units + i);
   const uint32_t* zb = reinterpret_cast<const uint32_t*>(p.prepared + p.p_zbits);
   for (int w = threadIdx.x; w < (p.n_entries * 3 + 31) / 32; w += blockDim.x) L->zbits[w] = __ldg(zb + w);
   __syncthreads();
@@ -684,6 +699,7 @@ int skinny_max_rows() { return kSkMaxRows; }
 int skinny_max_segs() { return kMaxSegs; }
 int skinny_max_entries() { return kMaxEntries; }
 int skinny_cols() { return kCols; }
+int skinny_stages(int K) { return (K + kKS - 1) / kKS; }
 int skinny_units_gateup(int I) { return I / kBoxRows; }
 int skinny_units_down(int M) { return (M + 2 * kBoxRows - 1) / (2 * kBoxRows); }
 
