@@ -209,6 +209,7 @@ def main() -> None:
     ap.add_argument("--config", default="ep_stack")
     ap.add_argument("--impl", default="wisp", choices=["wisp", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="launch every step eagerly")
     ap.add_argument("--kernel-reps", type=int, default=5)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -250,26 +251,59 @@ def main() -> None:
         t_max = max(b - a for a, b in (block_range(T_all, world, q) for q in range(world)))
         layers = [EpLayer(spec, lw, T, rank, world, max_tokens=t_max) for lw in layers_w]
     outs = [torch.empty((T, spec.hidden), dtype=torch.float32, device=dev) for _ in range(L)]
-    xs = [x0] + [torch.empty_like(x0) for _ in range(L - 1)]
+    # xs[0] is the step's input buffer: callers copy their tokens into it
+    xs = [x0.clone()] + [torch.empty_like(x0) for _ in range(L - 1)]
 
-    def step(x_in):
-        xs[0] = x_in
+    def step_eager():
         for l in range(L):
-            if world == 1:
-                layers[l].forward(xs[l], outs[l])
-            else:
-                layers[l].forward(xs[l], outs[l])
+            layers[l].forward(xs[l], outs[l])
             if l + 1 < L:
                 abi.call("wisp_b200_rms_rescale", outs[l].data_ptr(), xs[l + 1].data_ptr(), T,
-                         spec.hidden, 1e-6, stream.cuda_stream)
+                         spec.hidden, 1e-6, torch.cuda.current_stream().cuda_stream)
         return outs[-1]
 
     def barrier():
         if world > 1:
             dist.barrier()
 
+    # One step as a CUDA graph: the layer calls (and, across GPUs, their NCCL
+    # exchanges) replay without host work between the launches. Every rank
+    # captures; if any rank fails, all run eagerly.
+    graph, graph_note = None, "off (--no-graph)"
+    if not args.no_graph:
+        try:
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                for _ in range(2):
+                    step_eager()
+            torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize()
+            barrier()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                step_eager()
+            torch.cuda.synchronize()
+            graph_note = "on"
+        except Exception as exc:  # noqa: BLE001 - reported in the JSON line
+            graph, graph_note = None, f"capture failed: {type(exc).__name__}: {str(exc)[:120]}"
+        if world > 1:
+            ok = torch.tensor([1 if graph is not None else 0], device=dev)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+            if int(ok.item()) == 0 and graph is not None:
+                graph, graph_note = None, "off (another rank failed to capture)"
+
+    def step(x_in):
+        if x_in is not xs[0]:
+            xs[0].copy_(x_in, non_blocking=True)
+        if graph is not None:
+            graph.replay()
+        else:
+            step_eager()
+        return outs[-1]
+
     for _ in range(args.warmup):
-        step(x0)
+        step(xs[0])
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
@@ -279,13 +313,13 @@ def main() -> None:
     # keep the GPU busy while nvidia-smi starts sampling
     t_spin = time.perf_counter()
     while time.perf_counter() - t_spin < 1.0:
-        step(x0)
+        step(xs[0])
         torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push("timed")
     ev0.record(stream)
     for _ in range(args.steps):
-        step(x0)
+        step(xs[0])
     ev1.record(stream)
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
@@ -375,18 +409,17 @@ def main() -> None:
     e2e = None
     x_host = x0.cpu().pin_memory()
     out_host = torch.empty((T, spec.hidden), dtype=torch.float32).pin_memory()
-    x_dev = torch.empty_like(x0)
     for _ in range(2):
-        x_dev.copy_(x_host, non_blocking=True)
-        step(x_dev)
+        xs[0].copy_(x_host, non_blocking=True)
+        step(xs[0])
         out_host.copy_(outs[-1], non_blocking=True)
     torch.cuda.synchronize()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        x_dev.copy_(x_host, non_blocking=True)
-        step(x_dev)
+        xs[0].copy_(x_host, non_blocking=True)
+        step(xs[0])
         out_host.copy_(outs[-1], non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize()
@@ -416,7 +449,7 @@ def main() -> None:
         "config": {"workload": spec.name, "layers": L, "tokens_per_step": T_all,
                    "hidden": spec.hidden, "inter": spec.inter, "experts": spec.n_experts,
                    "shared_experts": int(spec.has_shared), "top_k": spec.top_k,
-                   "group_size": spec.group_size, "parallelism": f"ep{world}",
+                   "group_size": spec.group_size, "parallelism": f"ep{world}", "cuda_graph": graph_note,
                    "l2": f"inputs larger than L2 ({step_bytes / 1e9:.1f} GB of expert weights per step)"},
         "hbm": {"step_bytes": step_bytes, "achieved_gbs": round(hbm_gbs, 1),
                 "frac_of_measured": round(hbm_gbs / peaks["hbm_gbs"], 4),
@@ -428,6 +461,10 @@ def main() -> None:
         line["cpu_baseline"] = cpu_baseline(spec)
     if rank == 0:
         print(json.dumps(line))
+    if graph is not None:   # a graph holding NCCL calls must go before the group
+        graph.reset()
+        graph = None
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -13,12 +13,12 @@ One layer on rank r, with every count kept on the device (no host round
 trip between routing and the expert FFN):
   route own tokens -> plan (rows grouped by expert, hence by owner rank)
   -> pack rows (fp16) into a send buffer of `world` fixed blocks of `cap`
-  rows -> exchange per-expert row counts (all_to_all) -> exchange the row
-  blocks (all_to_all, equal splits) -> gather the received rows expert-
-  contiguous (one segment per local expert, as on one GPU) -> grouped FFN
-  (mode 1: unweighted fp32 rows) -> scatter the results into the source
-  blocks -> return the row blocks (all_to_all) -> shared expert on own
-  tokens (mode 0) + weighted combine of the returned rows.
+  rows -> exchange per-expert row counts and the row blocks (all_to_all,
+  equal splits), meanwhile the shared expert on own tokens (mode 0) -> gather
+  the received rows expert-contiguous (one segment per local expert, as on
+  one GPU) -> grouped FFN (mode 1: unweighted fp32 rows) -> scatter the
+  results into the source blocks -> return the row blocks (all_to_all) ->
+  weighted combine of the returned rows.
 cap = tokens * top_k, the most rows one rank can send to one destination;
 the padding rows are exchanged but never computed or read.
 
@@ -220,9 +220,18 @@ class EpLayer:
                  self.row_weight)
         ops.send_pack(x, self.row_token, self.segs, spec.n_experts, T * k, world, self.cap,
                       self.xsend, self.slot)
-        # 1. per-expert row counts to the owners, then the row blocks
-        dist.all_to_all_single(self.cnt_recv, self.counts, group=self.group)
-        dist.all_to_all_single(self.xrecv, self.xsend, group=self.group)
+        # 1. per-expert row counts to the owners, then the row blocks; the
+        #    shared expert runs on this rank's own tokens while they travel
+        w_cnt = dist.all_to_all_single(self.cnt_recv, self.counts, group=self.group,
+                                       async_op=True)
+        w_rows = dist.all_to_all_single(self.xrecv, self.xsend, group=self.group, async_op=True)
+        out.zero_()
+        if spec.has_shared:
+            ops.pack(x, None, T, self.xs)
+            ops.grouped_dev(self.cfg_loc, self.lw, self.sh_seg, 1, T, self.xs, self.hr, 0,
+                            self.sh_token, self.sh_weight, out, self.tiles, self.flag)
+        w_cnt.wait()
+        w_rows.wait()
         # 2. local experts over the received rows, gathered so that each
         #    expert is one segment (unweighted fp32 rows), then scattered
         #    back into the source blocks
@@ -233,13 +242,7 @@ class EpLayer:
         ops.grouped_dev(self.cfg_loc, self.lw, self.rsegs, self.n_rsegs, R, self.xsorted,
                         self.hr, 1, None, None, self.ysorted, self.tiles, self.flag)
         ops.scatter_rows(self.ysorted, self.src_pos, self.total, R, self.yr)
-        # 3. rows back to their tokens' ranks
+        # 3. rows back to their tokens' ranks, then the weighted combine
         dist.all_to_all_single(self.yback, self.yr, group=self.group)
-        # 4. shared expert on own tokens, then the weighted combine
-        out.zero_()
-        if spec.has_shared:
-            ops.pack(x, None, T, self.xs)
-            ops.grouped_dev(self.cfg_loc, self.lw, self.sh_seg, 1, T, self.xs, self.hr, 0,
-                            self.sh_token, self.sh_weight, out, self.tiles, self.flag)
         ops.ep_combine(self.yback, self.slot, self.row_token, self.row_weight, T * k, out)
         return out
