@@ -11,8 +11,8 @@
 //           or y[p, m] = down[m] . H_p                        (mode 1)
 //
 // The weights are the MMA's A operand (M = 128 lanes), the tokens its B
-// operand (N = BN in {16, 32, 64, 128}, chosen per segment so small groups
-// do not pay for padding). Roles inside one persistent CTA per SM:
+// operand (N = BN in {16, 32, 64, 128}, and 256 for the down projection,
+// chosen per segment so small groups do not pay for padding). Roles inside one persistent CTA per SM:
 //   warp 22     weight producer: per 128-K raw stage, one TMA box of packed
 //               nibbles per matrix (128 rows x 64 bytes, 64-byte swizzle)
 //               plus bulk copies of the tile's scales (and zero points) from
@@ -57,7 +57,6 @@ constexpr int kTmaWWarp = kDqWarps + 6;
 constexpr int kThreads = (kDqWarps + 7) * 32;
 constexpr int kAStages = 4;  // A stages in TMEM
 constexpr int BM = 128;
-constexpr int kBNMax = 128;
 constexpr int kTmemCols = 512;
 constexpr int kAColBase = 256;
 constexpr int kRawK = 128;           // K per raw (weight) stage
@@ -68,6 +67,11 @@ enum { GATEUP = 0, DOWN = 1 };
 
 template <int MODE>
 struct Shape {
+  // Tokens per tile. An M=128 tcgen05.mma with A from tensor memory costs
+  // ~96 SM cycles at N <= 128 and ~141 at N = 256 (measured on B200): the
+  // down projection, whose one accumulator leaves room, runs N = 256 tiles;
+  // gate/up keeps two N <= 128 accumulators beside the A stages.
+  static constexpr int kBNMax = MODE == GATEUP ? 128 : 256;
   static constexpr int KA = MODE == GATEUP ? 64 : 128;            // K per A stage
   static constexpr int kSub = kRawK / KA;                          // A stages per raw stage
   static constexpr int kMats = MODE == GATEUP ? 2 : 1;
@@ -75,13 +79,13 @@ struct Shape {
   static constexpr int kScOff = kMats * kBoxBytes;
   static constexpr int kZOff = kScOff + kMats * kScBytes;
   static constexpr int kRawStageBytes = ((kZOff + kMats * kScBytes) + 1023) / 1024 * 1024;
-  static constexpr int kRawStages = MODE == GATEUP ? 6 : 8;
+  static constexpr int kRawStages = MODE == GATEUP ? 6 : 6;
   static constexpr int kBoxes = KA / 64;                           // 64-K activation boxes per A stage
-  // An activation stage holds 128/BN consecutive A stages' worth of boxes
+  // An activation stage holds kBNMax/BN consecutive A stages' worth of boxes
   // (BN rows x 128 bytes each), so its size does not depend on BN and small
   // token groups get a deep prefetch (32 A stages at BN = 16).
   static constexpr int kBStageBytes = kBoxes * kBNMax * 128;
-  static constexpr int kBStages = MODE == GATEUP ? 5 : 3;
+  static constexpr int kBStages = MODE == GATEUP ? 5 : 2;
 };
 
 // Prepared weights: per matrix entry (expert v, matrix m in gate/up/down) two
@@ -109,7 +113,7 @@ PreparedLayout prepared_layout(const WispMoeConfig* c, int n) {
 }
 
 struct GemmParams {
-  CUtensorMap tmap[4];  // activation tensor, boxes {64, 16 << i}
+  CUtensorMap tmap[5];  // activation tensor, boxes {64, 16 << i}
   const uint8_t* prepared;
   size_t p_flags, p_scales, p_zeros, p_mat_sc_bytes;
   const WispSegment* segs;
@@ -190,7 +194,9 @@ __device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int tile) {
   return t;
 }
 
-__device__ __forceinline__ int bn_slot(int bn) { return bn == 16 ? 0 : bn == 32 ? 1 : bn == 64 ? 2 : 3; }
+__device__ __forceinline__ int bn_slot(int bn) {
+  return bn == 16 ? 0 : bn == 32 ? 1 : bn == 64 ? 2 : bn == 128 ? 3 : 4;
+}
 
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_constant__ GemmParams p) {
@@ -383,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
     // Activation producer.
     // ------------------------------------------------------------------
     if (lane == 0) {
-      for (int i = 0; i < 4; i++) tma_prefetch_desc(&p.tmap[i]);
+      for (int i = 0; i < 5; i++) tma_prefetch_desc(&p.tmap[i]);
       int sb = 0;
       uint32_t bphase = 0;
       int item = 0;
@@ -394,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       for (int tile = blockIdx.x; tile < ntiles && ok && !*abort; tile += gridDim.x) {
         const TileInfo ti = decode_tile(p, tile);
         const CUtensorMap* tm = &p.tmap[bn_slot(ti.bn)];
-        const int per_b = kBNMax / ti.bn;          // A stages per activation stage
+        const int per_b = S::kBNMax / ti.bn;       // A stages per activation stage
         const int box_bytes = ti.bn * 128;
         for (int a0 = 0; a0 < nA; a0 += per_b, item++) {
           const int na = min(per_b, nA - a0);
@@ -433,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       for (int tile = blockIdx.x; tile < ntiles && ok && !*abort; tile += gridDim.x, ntile_local++) {
         const TileInfo ti = decode_tile(p, tile);
         const uint32_t idesc = idesc_f16_m128(ti.bn);
-        const int per_b = kBNMax / ti.bn;
+        const int per_b = S::kBNMax / ti.bn;
         const uint32_t box16 = (uint32_t)(ti.bn * 128) >> 4;   // one box, in descriptor units
         long long t0 = pf.now();
         if (ntile_local > 0 && !mbar_wait(&L->accempty, accphase ^ 1, abort)) break;
@@ -530,23 +536,30 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
         }
       } else {
         const int m = ti.mblk * BM + r;
-        for (int c0 = 0; c0 < ti.bn; c0 += 16) {
-          uint32_t y[16];
-          tmem_ld16(lane_addr + c0, y);
+        for (int c0 = 0; c0 < ti.bn; c0 += 32) {
+          // tokens and router weights of these 32 columns: one per lane,
+          // broadcast below (no dependent loads inside the store loop)
+          const int myrow = ti.row0 + c0 + lane;
+          const bool mine = c0 + lane < ti.nvalid;
+          const int tok_l = (p.mode == 0 && mine) ? __ldg(p.row_token + myrow) : 0;
+          const float w_l = (p.mode == 0 && mine) ? __ldg(p.row_weight + myrow) : 0.f;
+          // columns c0..c0+31 (past bn they are other accumulator columns,
+          // never stored)
+          uint32_t ya[16], yb[16];
+          tmem_ld16(lane_addr + c0, ya);
+          tmem_ld16(lane_addr + c0 + 16, yb);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; j++) {
+          for (int j = 0; j < 32; j++) {
             const int tt = c0 + j;
+            const int tok = __shfl_sync(0xffffffffu, tok_l, j);
+            const float wgt = __shfl_sync(0xffffffffu, w_l, j);
             if (tt < ti.nvalid) {
-              const int prow = ti.row0 + tt;
-              const float yv = __uint_as_float(y[j]);
-              if (p.mode == 0) {
-                const int tok = __ldg(p.row_token + prow);
-                const float wgt = __ldg(p.row_weight + prow);
+              const float yv = __uint_as_float(j < 16 ? ya[j] : yb[j - 16]);
+              if (p.mode == 0)
                 red_add_f32(p.out + (size_t)tok * p.M + m, wgt * yv);
-              } else {
-                p.out[(size_t)prow * p.M + m] = yv;
-              }
+              else
+                p.out[(size_t)(ti.row0 + tt) * p.M + m] = yv;
             }
           }
         }
@@ -568,11 +581,12 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
   }
 }
 
-// Per segment: BN (16/32/64/128 by row count) and the prefix sum of tiles.
+// Per segment: BN (16/32/64/128/256 by row count, at most max_bn) and the
+// prefix sum of tiles.
 // Segments of at most skip_rows rows belong to the register-path kernel and
 // get no tiles here.
 __global__ void plan_tiles_kernel(const WispSegment* __restrict__ segs, int nseg, int mblocks,
-                                  int skip_rows, int32_t* __restrict__ tiles) {
+                                  int skip_rows, int max_bn, int32_t* __restrict__ tiles) {
   __shared__ int32_t warp_tot[32];
   __shared__ int32_t carry;
   if (threadIdx.x == 0) carry = 0;
@@ -582,7 +596,7 @@ __global__ void plan_tiles_kernel(const WispSegment* __restrict__ segs, int nseg
     int n = 0, bn = 16;
     if (s < nseg) {
       const int rows = segs[s].rows;
-      bn = rows <= 16 ? 16 : rows <= 32 ? 32 : rows <= 64 ? 64 : 128;
+      bn = rows <= 16 ? 16 : rows <= 32 ? 32 : rows <= 64 ? 64 : rows <= 128 || max_bn < 256 ? 128 : 256;
       n = rows > skip_rows ? ((rows + bn - 1) / bn) * mblocks : 0;
       tiles[nseg + 1 + s] = bn;
     }
@@ -925,7 +939,7 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
   const PreparedLayout PL = prepared_layout(cfg, n_entries);
   GemmParams gu, dn;
   memset(&gu, 0, sizeof gu);
-  for (int i = 0; i < 4; i++) {
+  for (int i = 0; i < 5; i++) {
     if (!encode_rows_map(&gu.tmap[i], d_xp, rows_capacity, M, 16 << i))
       return WB_FAIL(WISP_ERR_CUDA, "grouped_ffn: cuTensorMapEncodeTiled failed (activations)");
   }
@@ -944,7 +958,7 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
   gu.counters = g_counters;
   dn = gu;
   dn.counters = g_counters ? g_counters + C_COUNT : nullptr;
-  for (int i = 0; i < 4; i++) {
+  for (int i = 0; i < 5; i++) {
     if (!encode_rows_map(&dn.tmap[i], d_h, rows_capacity, I, 16 << i))
       return WB_FAIL(WISP_ERR_CUDA, "grouped_ffn: cuTensorMapEncodeTiled failed (H)");
   }
@@ -963,8 +977,10 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
   dn.tiles = d_tiles + tw;
   int32_t* units_gu = d_tiles + 2 * tw;
   int32_t* units_dn = units_gu + (n_segs + 2);
-  plan_tiles_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, I / BM, sk_rows, d_tiles);
-  plan_tiles_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, M / BM, sk_rows, d_tiles + tw);
+  plan_tiles_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, I / BM, sk_rows,
+                                            Shape<GATEUP>::kBNMax, d_tiles);
+  plan_tiles_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, M / BM, sk_rows,
+                                            Shape<DOWN>::kBNMax, d_tiles + tw);
   const int skc = wb::skinny_cols();
   // Gate/up cannot split K (SwiGLU needs whole sums), nor can mode 1 (plain
   // row stores); the weighted down projection splits K when it has fewer
