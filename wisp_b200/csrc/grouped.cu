@@ -210,6 +210,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = __ldg(p.tiles + p.nseg);
+  // A CTA without a tile leaves before any set-up, tensor memory included.
+  if ((int)blockIdx.x >= ntiles) return;
   const int K = MODE == GATEUP ? p.M : p.I;
   const int nA = K / S::KA;           // A stages per tile
   const int nR = K / kRawK;           // raw stages per tile
@@ -585,8 +587,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
 // prefix sum of tiles.
 // Segments of at most skip_rows rows belong to the register-path kernel and
 // get no tiles here.
-__global__ void plan_tiles_kernel(const WispSegment* __restrict__ segs, int nseg, int mblocks,
-                                  int skip_rows, int max_bn, int32_t* __restrict__ tiles) {
+__device__ void plan_tiles(const WispSegment* __restrict__ segs, int nseg, int mblocks,
+                           int skip_rows, int max_bn, int32_t* __restrict__ tiles) {
   __shared__ int32_t warp_tot[32];
   __shared__ int32_t carry;
   if (threadIdx.x == 0) carry = 0;
@@ -633,9 +635,9 @@ __global__ void plan_tiles_kernel(const WispSegment* __restrict__ segs, int nseg
 // than `target` units would exist, each is cut into up to `max_ksplit`
 // K ranges (at most `nk`, one stage each at least), whose partial sums the
 // down epilogue adds atomically. units[nseg + 1] receives the split.
-__global__ void plan_units_kernel(const WispSegment* __restrict__ segs, int nseg, int per_seg,
-                                  int cols, int max_rows, int max_ksplit, int nk, int target,
-                                  int32_t* __restrict__ units) {
+__device__ void plan_units(const WispSegment* __restrict__ segs, int nseg, int per_seg,
+                           int cols, int max_rows, int max_ksplit, int nk, int target,
+                           int32_t* __restrict__ units) {
   __shared__ int32_t warp_tot[32];
   __shared__ int32_t carry;
   if (threadIdx.x == 0) carry = 0;
@@ -681,6 +683,28 @@ __global__ void plan_units_kernel(const WispSegment* __restrict__ segs, int nseg
   if (threadIdx.x == 0) {
     units[nseg] = total * ks;
     units[nseg + 1] = ks;
+  }
+}
+
+// The four plans of one call in one launch: blocks 0 and 1 tile gate/up and
+// down for the tensor-core kernel, blocks 2 and 3 cut them into register-path
+// units.
+struct PlanArgs {
+  const WispSegment* segs;
+  int nseg, sk_rows;
+  int mb_gu, mb_dn, bn_gu, bn_dn;
+  int per_gu, per_dn, cols, ks_dn, nk_dn, target;
+  int32_t *tiles_gu, *tiles_dn, *units_gu, *units_dn;
+};
+
+__global__ void __launch_bounds__(1024) plan_all_kernel(const __grid_constant__ PlanArgs a) {
+  switch (blockIdx.x) {
+    case 0: plan_tiles(a.segs, a.nseg, a.mb_gu, a.sk_rows, a.bn_gu, a.tiles_gu); break;
+    case 1: plan_tiles(a.segs, a.nseg, a.mb_dn, a.sk_rows, a.bn_dn, a.tiles_dn); break;
+    case 2: plan_units(a.segs, a.nseg, a.per_gu, a.cols, a.sk_rows, 1, 1, 0, a.units_gu); break;
+    default:
+      plan_units(a.segs, a.nseg, a.per_dn, a.cols, a.sk_rows, a.ks_dn, a.nk_dn, a.target,
+                 a.units_dn);
   }
 }
 
@@ -977,20 +1001,28 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
   dn.tiles = d_tiles + tw;
   int32_t* units_gu = d_tiles + 2 * tw;
   int32_t* units_dn = units_gu + (n_segs + 2);
-  plan_tiles_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, I / BM, sk_rows,
-                                            Shape<GATEUP>::kBNMax, d_tiles);
-  plan_tiles_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, M / BM, sk_rows,
-                                            Shape<DOWN>::kBNMax, d_tiles + tw);
-  const int skc = wb::skinny_cols();
   // Gate/up cannot split K (SwiGLU needs whole sums), nor can mode 1 (plain
   // row stores); the weighted down projection splits K when it has fewer
   // than two units per SM.
-  const int grid_sm = num_sms();
-  plan_units_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, wb::skinny_units_gateup(I), skc,
-                                            sk_rows, 1, 1, 0, units_gu);
-  plan_units_kernel<<<1, 1024, 0, stream>>>(d_segs, n_segs, wb::skinny_units_down(M), skc,
-                                            sk_rows, mode == 0 ? 8 : 1, wb::skinny_stages(I),
-                                            2 * grid_sm, units_dn);
+  PlanArgs pa;
+  pa.segs = d_segs;
+  pa.nseg = n_segs;
+  pa.sk_rows = sk_rows;
+  pa.mb_gu = I / BM;
+  pa.mb_dn = M / BM;
+  pa.bn_gu = Shape<GATEUP>::kBNMax;
+  pa.bn_dn = Shape<DOWN>::kBNMax;
+  pa.per_gu = wb::skinny_units_gateup(I);
+  pa.per_dn = wb::skinny_units_down(M);
+  pa.cols = wb::skinny_cols();
+  pa.ks_dn = mode == 0 ? 8 : 1;
+  pa.nk_dn = wb::skinny_stages(I);
+  pa.target = 2 * num_sms();
+  pa.tiles_gu = d_tiles;
+  pa.tiles_dn = d_tiles + tw;
+  pa.units_gu = units_gu;
+  pa.units_dn = units_dn;
+  plan_all_kernel<<<4, 1024, 0, stream>>>(pa);
   CUtensorMap sk_xp[2], sk_h[2];
   for (int i = 0; i < 2; i++) {
     if (!encode_rows_map(&sk_xp[i], d_xp, rows_capacity, M, 8 << i) ||

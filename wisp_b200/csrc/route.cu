@@ -120,15 +120,26 @@ __global__ void topk_kernel(const float* __restrict__ part, int splits, const fl
   const int per = (E + 31) / 32;
   float v[kMaxPerLane];
 #pragma unroll
+  for (int j = 0; j < kMaxPerLane; j++) v[j] = 0.f;
+  // Split-K partials: split-major, all of a split's loads in flight together
+  // (a per-expert loop over the splits would wait one L2 round trip per
+  // split and expert).
+  for (int z = 0; z < splits; z++) {
+    const float* pz = part + ((size_t)z * T + t) * E;
+#pragma unroll
+    for (int j = 0; j < kMaxPerLane; j++) {
+      const int e = lane + 32 * j;
+      if (j < per && e < E) v[j] += __ldg(pz + e);
+    }
+  }
+#pragma unroll
   for (int j = 0; j < kMaxPerLane; j++) {
-    v[j] = -INFINITY;
     const int e = lane + 32 * j;
     if (j < per && e < E) {
-      float s = 0.f;
-      for (int z = 0; z < splits; z++) s += part[((size_t)z * T + t) * E + e];
-      if (bias) s += bias[e];
-      v[j] = s;
-      if (logits_out) logits_out[(size_t)t * E + e] = s;
+      if (bias) v[j] += bias[e];
+      if (logits_out) logits_out[(size_t)t * E + e] = v[j];
+    } else {
+      v[j] = -INFINITY;
     }
   }
   bool taken[kMaxPerLane];
