@@ -135,6 +135,45 @@ def test_router_topk_launcher(orc, E, M, k):
     check_routing(idx.numpy()[None, :], w.numpy()[None, :], i_ref, w_ref, mg)
 
 
+@pytest.mark.parametrize("T", [1, 2, 4, 5, 70])
+@pytest.mark.parametrize("E,M,k,fp16,scoring", [(5, 128, 5, True, 0), (8, 4096, 2, False, 0),
+                                                (256, 7168, 8, False, 1), (64, 2048, 6, True, 1)])
+def test_route_logits(orc, T, E, M, k, fp16, scoring):
+    """Batched router through wisp_b200_route: logits within fp32 summation
+    error of the fp64 oracle (|err| <= 1e-5 * sum|x w|), indices exact away
+    from near-ties. T <= 4 runs the GEMV form, larger T the tiled split-K
+    form."""
+    g = torch.Generator().manual_seed(E * 31 + M + T)
+    dt = torch.float16 if fp16 else torch.bfloat16
+    W = (torch.randn(E, M, generator=g) * 0.02).to(dt)
+    bias = (torch.randn(E, generator=g) * 0.1).float() if scoring else None
+    x = torch.randn(T, M, generator=g).to(torch.bfloat16)
+    cfg = abi.WispMoeConfig(tokens=T, hidden=M, inter=128, n_experts=E, top_k=k, group_size=128,
+                            scoring=scoring, n_groups=8 if scoring else 1,
+                            topk_groups=4 if scoring else 1, routed_scaling=2.5 if scoring else 1.0,
+                            has_shared=0, router_fp16=1 if fp16 else 0)
+    Wd, xd = W.to(DEV), x.to(DEV)
+    bd = bias.to(DEV) if bias is not None else None
+    ws = abi.WispMoeWeights()
+    ws.router_w = Wd.data_ptr()
+    ws.router_bias = bd.data_ptr() if bd is not None else None
+    logits = torch.empty((T, E), device=DEV)
+    idx = torch.empty((T, k), dtype=torch.int32, device=DEV)
+    w = torch.empty((T, k), dtype=torch.float32, device=DEV)
+    abi.call("wisp_b200_route", C.byref(cfg), C.byref(ws), xd.data_ptr(), logits.data_ptr(),
+             idx.data_ptr(), w.data_ptr(), _stream())
+    torch.cuda.synchronize()
+    Wb = W.view(torch.int16).numpy().view(np.uint16)
+    b64 = bias.numpy().astype(np.float64) if bias is not None else None
+    xf = bf16_to_f64(x)
+    lg = orc.router_logits(Wb, 1 if fp16 else 2, b64, xf)
+    bound = np.abs(xf) @ np.abs(W.double().numpy()).T
+    np.testing.assert_array_less(np.abs(logits.cpu().numpy() - lg), 1e-5 * bound + 1e-7)
+    i_ref, w_ref, mg = orc.topk(lg, k, scoring, cfg.n_groups, cfg.topk_groups, cfg.routed_scaling)
+    check_routing(idx.cpu().numpy(), w.cpu().numpy(), i_ref, w_ref, mg,
+                  near_tie=NEAR_TIE if scoring == 0 else NEAR_TIE_SIGMOID)
+
+
 # ---------------------------------------------------------------------------
 # Fused decode entry (fp32 activations, reference blobs)
 # ---------------------------------------------------------------------------

@@ -4,6 +4,9 @@
 //                         Tiled 64x64 with a deterministic split-K so small
 //                         token counts still fill the GPU (partials are
 //                         summed in a fixed order by the top-k kernel).
+//   router_gemv_kernel    the same logits for T <= 4 tokens: one warp per
+//                         (expert, K quarter) with all of its weight loads
+//                         in flight, quarters summed in a fixed order.
 //   topk_kernel           one warp per token. Softmax scoring follows the
 //                         reference exactly (csrc/core/wisp_engine.c:782-818,
 //                         csrc/cuda/router.cu:67-138): softmax, k rounds of
@@ -93,6 +96,84 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __re
   }
 }
 
+constexpr int kGemvMaxT = 4;   // tokens per launch of the GEMV router
+constexpr int kGemvQ = 4;      // K quarters per expert (one warp each)
+constexpr int kGemvU = 8;      // 16-byte weight loads in flight per lane
+
+template <bool W_FP16>
+__device__ __forceinline__ float dot8(uint4 w, uint4 x, float acc) {
+  const uint32_t wa[4] = {w.x, w.y, w.z, w.w}, xa[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const float w0 = W_FP16 ? f16f((uint16_t)(wa[j] & 0xffff)) : bf16f((uint16_t)(wa[j] & 0xffff));
+    const float w1 = W_FP16 ? f16f((uint16_t)(wa[j] >> 16)) : bf16f((uint16_t)(wa[j] >> 16));
+    acc = fmaf(bf16f((uint16_t)(xa[j] & 0xffff)), w0, acc);
+    acc = fmaf(bf16f((uint16_t)(xa[j] >> 16)), w1, acc);
+  }
+  return acc;
+}
+
+// grid ceil(E/2) x 256 threads: warp w covers expert 2*blockIdx.x + w/4 over
+// K quarter w%4 (M a multiple of 8). Writes logits [T x E] (no bias).
+template <bool W_FP16>
+__global__ void __launch_bounds__(256) router_gemv_kernel(const uint16_t* __restrict__ x,
+                                                          const uint16_t* __restrict__ W,
+                                                          float* __restrict__ logits, int T, int E,
+                                                          int M) {
+  __shared__ float red[8][kGemvMaxT];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = blockIdx.x * 2 + warp / kGemvQ, q = warp % kGemvQ;
+  const int n8 = M / 8;
+  const int qb = q * n8 / kGemvQ, qe = (q + 1) * n8 / kGemvQ;
+  float acc[kGemvMaxT];
+#pragma unroll
+  for (int t = 0; t < kGemvMaxT; t++) acc[t] = 0.f;
+  if (e < E) {
+    const uint4* wr = reinterpret_cast<const uint4*>(W + (size_t)e * M);
+    for (int c0 = qb; c0 < qe; c0 += 32 * kGemvU) {
+      uint4 wv[kGemvU];
+#pragma unroll
+      for (int i = 0; i < kGemvU; i++) {
+        const int c = c0 + lane + 32 * i;
+        wv[i] = c < qe ? __ldg(wr + c) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int t = 0; t < kGemvMaxT; t++) {
+        if (t >= T) break;
+        const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)t * M);
+        uint4 xv[kGemvU];
+#pragma unroll
+        for (int i = 0; i < kGemvU; i++) {
+          const int c = c0 + lane + 32 * i;
+          xv[i] = c < qe ? __ldg(xr + c) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int i = 0; i < kGemvU; i++) acc[t] = dot8<W_FP16>(wv[i], xv[i], acc[t]);
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < kGemvMaxT; t++) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int t = 0; t < kGemvMaxT; t++) red[warp][t] = acc[t];
+  }
+  __syncthreads();
+  if (threadIdx.x < 2 * kGemvMaxT) {
+    const int el = threadIdx.x / kGemvMaxT, t = threadIdx.x % kGemvMaxT;
+    const int ee = blockIdx.x * 2 + el;
+    if (ee < E && t < T) {
+      float s = red[el * kGemvQ][t];
+#pragma unroll
+      for (int j = 1; j < kGemvQ; j++) s += red[el * kGemvQ + j][t];
+      logits[(size_t)t * E + ee] = s;
+    }
+  }
+}
+
 // Warp argmax with the lower index winning ties; (v, i) = (-inf/-1, -1) for
 // an empty lane.
 __device__ __forceinline__ void warp_argmax(float& v, int& i) {
@@ -142,9 +223,7 @@ __global__ void topk_kernel(const float* __restrict__ part, int splits, const fl
       v[j] = -INFINITY;
     }
   }
-  bool taken[kMaxPerLane];
-#pragma unroll
-  for (int j = 0; j < kMaxPerLane; j++) taken[j] = false;
+  uint32_t taken = 0;  // bit j: expert lane + 32 j already chosen
 
   if (scoring == WISP_SCORE_SOFTMAX) {
     float mx = -INFINITY;
@@ -173,13 +252,13 @@ __global__ void topk_kernel(const float* __restrict__ part, int splits, const fl
 #pragma unroll
       for (int j = 0; j < kMaxPerLane; j++) {
         const int e = lane + 32 * j;
-        if (j < per && e < E && !taken[j] && v[j] > bv) {
+        if (j < per && e < E && !((taken >> j) & 1u) && v[j] > bv) {
           bv = v[j];
           bi = e;
         }
       }
       warp_argmax(bv, bi);
-      if (bi >= 0 && (bi & 31) == lane) taken[bi >> 5] = true;
+      if (bi >= 0 && (bi & 31) == lane) taken |= 1u << (bi >> 5);
       if (lane == r) {
         myw = bv;
         myi = bi;
@@ -233,13 +312,13 @@ __global__ void topk_kernel(const float* __restrict__ part, int splits, const fl
 #pragma unroll
       for (int j = 0; j < kMaxPerLane; j++) {
         const int e = lane + 32 * j;
-        if (j < per && e < E && !taken[j] && ((gmask >> (e / gsz)) & 1u) && (bi < 0 || v[j] > bv)) {
+        if (j < per && e < E && !((taken >> j) & 1u) && ((gmask >> (e / gsz)) & 1u) && (bi < 0 || v[j] > bv)) {
           bv = v[j];
           bi = e;
         }
       }
       warp_argmax(bv, bi);
-      if (bi >= 0 && (bi & 31) == lane) taken[bi >> 5] = true;
+      if (bi >= 0 && (bi & 31) == lane) taken |= 1u << (bi >> 5);
       if (lane == r) {
         myw = bv;
         myi = bi;
@@ -422,6 +501,7 @@ size_t router_splits(int T, int E, int M) {
     cudaDeviceGetAttribute(&g_sms_cached, cudaDevAttrMultiProcessorCount, dev);
     if (g_sms_cached <= 0) g_sms_cached = 148;
   }
+  if (T <= kGemvMaxT) return 1;
   const long long tiles = (long long)((E + kRE - 1) / kRE) * ((T + kRT - 1) / kRT);
   long long splits = (2LL * g_sms_cached + tiles - 1) / tiles;
   const long long max_splits = std::max(1, M / 256);
@@ -434,14 +514,23 @@ WispError launch_route(const WispMoeConfig* c, const uint16_t* x, const uint16_t
                        const float* bias, float* part, size_t splits, float* logits_out, int* idx,
                        float* w, cudaStream_t st, WispErrCtx* err) {
   const int T = c->tokens, E = c->n_experts, M = c->hidden;
-  int kspan = (M + (int)splits - 1) / (int)splits;
-  kspan = (kspan + kRK - 1) / kRK * kRK;
-  const int nsplit = (M + kspan - 1) / kspan;
-  dim3 g1((E + kRE - 1) / kRE, (T + kRT - 1) / kRT, nsplit);
-  if (c->router_fp16)
-    router_logits_kernel<true><<<g1, 256, 0, st>>>(x, W, part, T, E, M, kspan);
-  else
-    router_logits_kernel<false><<<g1, 256, 0, st>>>(x, W, part, T, E, M, kspan);
+  int nsplit = 1;
+  if (T <= kGemvMaxT) {
+    const int g = (E + 1) / 2;
+    if (c->router_fp16)
+      router_gemv_kernel<true><<<g, 256, 0, st>>>(x, W, part, T, E, M);
+    else
+      router_gemv_kernel<false><<<g, 256, 0, st>>>(x, W, part, T, E, M);
+  } else {
+    int kspan = (M + (int)splits - 1) / (int)splits;
+    kspan = (kspan + kRK - 1) / kRK * kRK;
+    nsplit = (M + kspan - 1) / kspan;
+    dim3 g1((E + kRE - 1) / kRE, (T + kRT - 1) / kRT, nsplit);
+    if (c->router_fp16)
+      router_logits_kernel<true><<<g1, 256, 0, st>>>(x, W, part, T, E, M, kspan);
+    else
+      router_logits_kernel<false><<<g1, 256, 0, st>>>(x, W, part, T, E, M, kspan);
+  }
   topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(part, nsplit, bias, T, E, c->top_k, c->scoring,
                                            c->n_groups, c->topk_groups, c->routed_scaling, idx, w,
                                            logits_out);
