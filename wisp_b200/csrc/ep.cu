@@ -45,6 +45,8 @@ __global__ void ep_send_pack_kernel(const uint16_t* __restrict__ x, int M,
                                     const WispSegment* __restrict__ plan_segs, int e_loc,
                                     int n_rows, int world, int cap, uint16_t* __restrict__ xsend,
                                     int* __restrict__ slot) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ int dst_row;
   const int p = blockIdx.x;
   if (threadIdx.x == 0) {
@@ -85,6 +87,8 @@ __global__ void __launch_bounds__(1024) ep_recv_plan_kernel(const int* __restric
                                                             WispSegment* __restrict__ segs,
                                                             int* __restrict__ src_pos,
                                                             int* __restrict__ total_out) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ int src_off[1024];  // [s][e]: receive position of the chunk
   __shared__ int dst_off[1024];  // [s][e]: gathered position of the chunk
   __shared__ int cnt[1024];
@@ -127,6 +131,8 @@ template <bool GATHER>
 __global__ void ep_move_rows_kernel(void* __restrict__ a, void* __restrict__ b,
                                     const int* __restrict__ src_pos,
                                     const int* __restrict__ total, int row_bytes) {
+  pdl_trigger();
+  pdl_wait();
   const int j = blockIdx.x;
   if (j >= __ldg(total)) return;
   const size_t r = (size_t)__ldg(src_pos + j);
@@ -142,6 +148,8 @@ __global__ void ep_combine_kernel(const float* __restrict__ y, const int* __rest
                                   const int* __restrict__ row_token,
                                   const float* __restrict__ row_weight, int M,
                                   float* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int p = blockIdx.x;
   const float w = __ldg(row_weight + p);
   const float* yr = y + (size_t)__ldg(slot + p) * M;
@@ -171,9 +179,8 @@ extern "C" WispError wisp_b200_ep_send_pack(const uint16_t* d_x, int hidden, con
   if (((uintptr_t)d_x | (uintptr_t)d_xsend) & 15)
     return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_send_pack: row buffers must be 16-byte aligned");
   if (n_rows == 0) return WISP_OK;
-  ep_send_pack_kernel<<<n_rows, 128, 0, stream>>>(d_x, hidden, d_row_token, d_plan_segs,
-                                                  n_experts / world, n_rows, world, cap, d_xsend,
-                                                  d_slot);
+  wb::launch_k(ep_send_pack_kernel, n_rows, 128, 0, stream, d_x, hidden, d_row_token,
+               d_plan_segs, n_experts / world, n_rows, world, cap, d_xsend, d_slot);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
@@ -186,8 +193,8 @@ extern "C" WispError wisp_b200_ep_recv_plan(const int* d_recv_counts, int world,
   if (world < 1 || world > kMaxWorld || e_loc < 1 || world * e_loc > 1024 || cap < 0)
     return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_recv_plan: world=%d e_loc=%d cap=%d (world*e_loc <= 1024)",
                    world, e_loc, cap);
-  ep_recv_plan_kernel<<<1, 1024, 0, stream>>>(d_recv_counts, world, e_loc, cap, d_segs, d_src_pos,
-                                              d_total);
+  wb::launch_k(ep_recv_plan_kernel, 1, 1024, 0, stream, d_recv_counts, world, e_loc, cap, d_segs,
+               d_src_pos, d_total);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
@@ -201,8 +208,8 @@ extern "C" WispError wisp_b200_ep_gather_rows(const uint16_t* d_recv, const int*
   if (hidden % 8 || max_rows < 0 || (((uintptr_t)d_recv | (uintptr_t)d_sorted) & 15))
     return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_gather_rows: hidden=%d (rows 16-byte aligned)", hidden);
   if (max_rows == 0) return WISP_OK;
-  ep_move_rows_kernel<true><<<max_rows, 128, 0, stream>>>(
-      const_cast<uint16_t*>(d_recv), d_sorted, d_src_pos, d_total, hidden * 2);
+  wb::launch_k(ep_move_rows_kernel<true>, max_rows, 128, 0, stream,
+               const_cast<uint16_t*>(d_recv), d_sorted, d_src_pos, d_total, hidden * 2);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
@@ -216,8 +223,8 @@ extern "C" WispError wisp_b200_ep_scatter_rows(const float* d_sorted, const int*
   if (hidden % 4 || max_rows < 0 || (((uintptr_t)d_recv | (uintptr_t)d_sorted) & 15))
     return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_scatter_rows: hidden=%d (rows 16-byte aligned)", hidden);
   if (max_rows == 0) return WISP_OK;
-  ep_move_rows_kernel<false><<<max_rows, 256, 0, stream>>>(
-      d_recv, const_cast<float*>(d_sorted), d_src_pos, d_total, hidden * 4);
+  wb::launch_k(ep_move_rows_kernel<false>, max_rows, 256, 0, stream, d_recv,
+               const_cast<float*>(d_sorted), d_src_pos, d_total, hidden * 4);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
@@ -232,8 +239,8 @@ extern "C" WispError wisp_b200_ep_combine(const float* d_y, const int* d_slot,
     return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_combine: hidden=%d rows=%d (y 16-byte aligned)",
                    hidden, n_rows);
   if (n_rows == 0) return WISP_OK;
-  ep_combine_kernel<<<n_rows, 256, 0, stream>>>(d_y, d_slot, d_row_token, d_row_weight, hidden,
-                                                d_out);
+  wb::launch_k(ep_combine_kernel, n_rows, 256, 0, stream, d_y, d_slot, d_row_token, d_row_weight,
+               hidden, d_out);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }

@@ -200,6 +200,8 @@ __device__ __forceinline__ int bn_slot(int bn) {
 
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_constant__ GemmParams p) {
+  pdl_trigger();
+  pdl_wait();
   using S = Shape<MODE>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base_u32 = smem_u32(smem_raw);
@@ -698,6 +700,8 @@ struct PlanArgs {
 };
 
 __global__ void __launch_bounds__(1024) plan_all_kernel(const __grid_constant__ PlanArgs a) {
+  pdl_trigger();
+  pdl_wait();
   switch (blockIdx.x) {
     case 0: plan_tiles(a.segs, a.nseg, a.mb_gu, a.sk_rows, a.bn_gu, a.tiles_gu); break;
     case 1: plan_tiles(a.segs, a.nseg, a.mb_dn, a.sk_rows, a.bn_dn, a.tiles_dn); break;
@@ -1022,7 +1026,7 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
   pa.tiles_dn = d_tiles + tw;
   pa.units_gu = units_gu;
   pa.units_dn = units_dn;
-  plan_all_kernel<<<4, 1024, 0, stream>>>(pa);
+  wb::launch_k(plan_all_kernel, 4, 1024, 0, stream, pa);
   CUtensorMap sk_xp[2], sk_h[2];
   for (int i = 0; i < 2; i++) {
     if (!encode_rows_map(&sk_xp[i], d_xp, rows_capacity, M, 8 << i) ||
@@ -1063,9 +1067,9 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
   WB_CUDA_CHECK(cudaFuncSetAttribute(grouped_ffn_kernel<DOWN>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_dn));
   if (sk_rows > 0) WB_CUDA_CHECK(wb::launch_skinny(sk, 0, grid, stream));
-  grouped_ffn_kernel<GATEUP><<<grid, kThreads, sm_gu, stream>>>(gu);
+  wb::launch_k(grouped_ffn_kernel<GATEUP>, grid, kThreads, sm_gu, stream, gu);
   if (sk_rows > 0) WB_CUDA_CHECK(wb::launch_skinny(sk, 1, grid, stream));
-  grouped_ffn_kernel<DOWN><<<grid, kThreads, sm_dn, stream>>>(dn);
+  wb::launch_k(grouped_ffn_kernel<DOWN>, grid, kThreads, sm_dn, stream, dn);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }

@@ -1,13 +1,47 @@
 // internal.h -- host-side helpers shared by the wisp_b200 translation units.
 #pragma once
 
+#include <cuda_runtime.h>
+
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
+#include <utility>
 
 #include "wisp_b200.h"
 
 namespace wb {
+
+// Programmatic dependent launch is on unless WISP_B200_PDL=0.
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("WISP_B200_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// Launches a kernel of the per-layer chain with programmatic stream
+// serialisation: the kernel may start while its predecessor in the stream
+// runs (it begins with griddepcontrol.wait, so it sees the predecessor's
+// results), which hides the launch latency between consecutive kernels,
+// inside CUDA graphs too. Errors are left for cudaGetLastError.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                            cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Fill a WispErrCtx the way the reference's WISP_ERR_SET does
 // (csrc/core/wisp_engine.h:66-72) and return the code.

@@ -47,6 +47,8 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __re
                                                             const uint16_t* __restrict__ W,
                                                             float* __restrict__ part, int T, int E,
                                                             int M, int kspan) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float xs[kRK][kRT + 4];
   __shared__ float ws[kRK][kRE + 4];
   const int e0 = blockIdx.x * kRE, t0 = blockIdx.y * kRT;
@@ -120,6 +122,8 @@ __global__ void __launch_bounds__(256) router_gemv_kernel(const uint16_t* __rest
                                                           const uint16_t* __restrict__ W,
                                                           float* __restrict__ logits, int T, int E,
                                                           int M) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[8][kGemvMaxT];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.x * 2 + warp / kGemvQ, q = warp % kGemvQ;
@@ -195,6 +199,8 @@ __global__ void topk_kernel(const float* __restrict__ part, int splits, const fl
                             int T, int E, int k, int scoring, int n_groups, int topk_groups,
                             float scaling, int* __restrict__ idx, float* __restrict__ wout,
                             float* __restrict__ logits_out) {
+  pdl_trigger();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * (blockDim.x >> 5) + warp;
   if (t >= T) return;
@@ -335,6 +341,8 @@ __global__ void topk_kernel(const float* __restrict__ part, int splits, const fl
 // counts[v] for the routed experts: one warp per expert over all T*k slots.
 __global__ void count_kernel(const int* __restrict__ idx, int nslots, int E, int T, int has_shared,
                              int* __restrict__ counts) {
+  pdl_trigger();
+  pdl_wait();
   const int v = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (v >= E + has_shared) return;
@@ -353,6 +361,8 @@ __global__ void count_kernel(const int* __restrict__ idx, int nslots, int E, int
 
 // Exclusive scan of counts into segments (single block).
 __global__ void segments_kernel(const int* __restrict__ counts, int V, WispSegment* __restrict__ segs) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ int warp_tot[32];
   __shared__ int carry;
   if (threadIdx.x == 0) carry = 0;
@@ -398,6 +408,8 @@ __global__ void segments_kernel(const int* __restrict__ counts, int V, WispSegme
 __global__ void fill_kernel(const int* __restrict__ idx, const float* __restrict__ w, int nslots,
                             int k, int E, int T, int has_shared, const WispSegment* __restrict__ segs,
                             int* __restrict__ row_token, float* __restrict__ row_weight) {
+  pdl_trigger();
+  pdl_wait();
   const int v = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (v >= E + has_shared) return;
@@ -426,6 +438,8 @@ __global__ void fill_kernel(const int* __restrict__ idx, const float* __restrict
 // xp[p] = fp16(x[src[p]]) in interleaved K order; each thread moves 8 values.
 __global__ void pack_rows_kernel(const uint16_t* __restrict__ x, const int* __restrict__ src, int n_rows,
                                  int M, uint16_t* __restrict__ xp) {
+  pdl_trigger();
+  pdl_wait();
   const int p = blockIdx.x;
   if (p >= n_rows) return;
   const int s = src ? src[p] : p;
@@ -453,6 +467,8 @@ __global__ void pack_rows_kernel(const uint16_t* __restrict__ x, const int* __re
 // between stacked MoE layers. One block per token.
 __global__ void rms_rescale_kernel(const float* __restrict__ x, uint16_t* __restrict__ y, int M,
                                    float eps) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[32];
   const float* xr = x + (size_t)blockIdx.x * M;
   float s = 0.f;
@@ -479,6 +495,8 @@ __global__ void rms_rescale_kernel(const float* __restrict__ x, uint16_t* __rest
 __global__ void combine_rows_kernel(const float* __restrict__ y, const int* __restrict__ row_token,
                                     const float* __restrict__ row_weight, int M,
                                     float* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int p = blockIdx.x;
   const int t = row_token[p];
   const float w = row_weight[p];
@@ -518,22 +536,21 @@ WispError launch_route(const WispMoeConfig* c, const uint16_t* x, const uint16_t
   if (T <= kGemvMaxT) {
     const int g = (E + 1) / 2;
     if (c->router_fp16)
-      router_gemv_kernel<true><<<g, 256, 0, st>>>(x, W, part, T, E, M);
+      wb::launch_k(router_gemv_kernel<true>, g, 256, 0, st, x, W, part, T, E, M);
     else
-      router_gemv_kernel<false><<<g, 256, 0, st>>>(x, W, part, T, E, M);
+      wb::launch_k(router_gemv_kernel<false>, g, 256, 0, st, x, W, part, T, E, M);
   } else {
     int kspan = (M + (int)splits - 1) / (int)splits;
     kspan = (kspan + kRK - 1) / kRK * kRK;
     nsplit = (M + kspan - 1) / kspan;
     dim3 g1((E + kRE - 1) / kRE, (T + kRT - 1) / kRT, nsplit);
     if (c->router_fp16)
-      router_logits_kernel<true><<<g1, 256, 0, st>>>(x, W, part, T, E, M, kspan);
+      wb::launch_k(router_logits_kernel<true>, g1, 256, 0, st, x, W, part, T, E, M, kspan);
     else
-      router_logits_kernel<false><<<g1, 256, 0, st>>>(x, W, part, T, E, M, kspan);
+      wb::launch_k(router_logits_kernel<false>, g1, 256, 0, st, x, W, part, T, E, M, kspan);
   }
-  topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(part, nsplit, bias, T, E, c->top_k, c->scoring,
-                                           c->n_groups, c->topk_groups, c->routed_scaling, idx, w,
-                                           logits_out);
+  wb::launch_k(topk_kernel, (T + 7) / 8, 256, 0, st, part, nsplit, bias, T, E, c->top_k,
+               c->scoring, c->n_groups, c->topk_groups, c->routed_scaling, idx, w, logits_out);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
@@ -543,9 +560,10 @@ WispError launch_plan(const WispMoeConfig* c, const int* idx, const float* w, in
                       WispErrCtx* err) {
   const int T = c->tokens, E = c->n_experts, k = c->top_k, sh = c->has_shared ? 1 : 0;
   const int V = E + sh;
-  count_kernel<<<(V + 7) / 8, 256, 0, st>>>(idx, T * k, E, T, sh, counts);
-  segments_kernel<<<1, 1024, 0, st>>>(counts, V, segs);
-  fill_kernel<<<(V + 7) / 8, 256, 0, st>>>(idx, w, T * k, k, E, T, sh, segs, row_token, row_weight);
+  wb::launch_k(count_kernel, (V + 7) / 8, 256, 0, st, idx, T * k, E, T, sh, counts);
+  wb::launch_k(segments_kernel, 1, 1024, 0, st, counts, V, segs);
+  wb::launch_k(fill_kernel, (V + 7) / 8, 256, 0, st, idx, w, T * k, k, E, T, sh, segs, row_token,
+               row_weight);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
@@ -553,7 +571,7 @@ WispError launch_plan(const WispMoeConfig* c, const int* idx, const float* w, in
 WispError launch_pack(const uint16_t* x, const int* src, int n_rows, int M, uint16_t* xp,
                       cudaStream_t st, WispErrCtx* err) {
   if (n_rows <= 0) return WISP_OK;
-  pack_rows_kernel<<<n_rows, 128, 0, st>>>(x, src, n_rows, M, xp);
+  wb::launch_k(pack_rows_kernel, n_rows, 128, 0, st, x, src, n_rows, M, xp);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
@@ -587,7 +605,7 @@ extern "C" WispError wisp_b200_rms_rescale(const float* d_in, uint16_t* d_out, i
                                            WispErrCtx* err) {
   if (!d_in || !d_out || tokens <= 0 || hidden <= 0)
     return WB_FAIL(WISP_ERR_INVALID_ARG, "rms_rescale: bad arguments");
-  rms_rescale_kernel<<<tokens, 256, 0, stream>>>(d_in, d_out, hidden, eps);
+  wb::launch_k(rms_rescale_kernel, tokens, 256, 0, stream, d_in, d_out, hidden, eps);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
@@ -598,7 +616,8 @@ extern "C" WispError wisp_b200_combine_rows(const float* d_y, const int* d_row_t
   if (n_rows < 0 || hidden <= 0 || (n_rows > 0 && (!d_y || !d_row_token || !d_row_weight || !d_out)))
     return WB_FAIL(WISP_ERR_INVALID_ARG, "combine_rows: bad arguments");
   if (n_rows == 0) return WISP_OK;
-  combine_rows_kernel<<<n_rows, 256, 0, stream>>>(d_y, d_row_token, d_row_weight, hidden, d_out);
+  wb::launch_k(combine_rows_kernel, n_rows, 256, 0, stream, d_y, d_row_token, d_row_weight, hidden,
+               d_out);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }

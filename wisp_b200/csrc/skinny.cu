@@ -642,6 +642,8 @@ __device__ void sk_consumer(const SkParams& p, uint8_t* ring, SkSmem* L, int tot
 
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) skinny_ffn_kernel(const __grid_constant__ SkParams p) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ uint8_t smem_raw[];
   const int total = __ldg(p.units + p.nseg);
   if ((int)blockIdx.x >= total) return;
@@ -736,10 +738,10 @@ cudaError_t launch_skinny(const SkLaunch& L, int phase, int grid, cudaStream_t s
   for (int i = 0; i < 2; i++) p.act_map[i] = maps[i];
   if (phase == 0) {
     p.units = L.units_gu;
-    skinny_ffn_kernel<SK_GATEUP><<<grid, kThreads, kSmemBytes, st>>>(p);
+    wb::launch_k(skinny_ffn_kernel<SK_GATEUP>, grid, kThreads, kSmemBytes, st, p);
   } else {
     p.units = L.units_dn;
-    skinny_ffn_kernel<SK_DOWN><<<grid, kThreads, kSmemBytes, st>>>(p);
+    wb::launch_k(skinny_ffn_kernel<SK_DOWN>, grid, kThreads, kSmemBytes, st, p);
   }
   return cudaGetLastError();
 }
