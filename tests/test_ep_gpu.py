@@ -6,7 +6,12 @@ half of the tokens; EpLayer exchanges rows with NCCL all-to-all and runs the
 grouped FFN (register-path and tensor-core kernels) on the received rows.
 The concatenated output must match the fp64 oracle within the parity
 tolerance, and the single-GPU MoeLayer output for the same tokens within
-1e-4 (only the fp32 order of the final weighted adds differs).
+max_rel 1e-3 / mean_rel 1e-4: each local expert is one segment of the same
+rows as on one GPU and runs on the same kernel, but the tensor-core kernel
+cuts K into a number of parts that follows its tile count (the shared
+expert has half the rows per rank), so fp32 sums run in another order and
+an H element may round to the neighbouring fp16 value. A misrouted or
+misplaced row would be off by O(1).
 """
 from __future__ import annotations
 
@@ -90,9 +95,9 @@ def test_ep_two_gpus_matches_single_gpu_and_oracle(orc, spec):
     # token count, which differs between a rank's slice and the whole batch).
     clear = np.flatnonzero(margin >= NEAR_TIE)
     assert len(clear) >= spec.tokens * 0.95
-    # Each local expert is one segment of the same rows as on one GPU, so it
-    # runs on the same kernel; only the fp32 order of the final adds differs.
-    assert_close(got[clear], single[clear], 1e-4, 1e-5, "EP vs single GPU")
+    # Same kernels per segment; fp32 summation order differs (K split, final
+    # weighted adds), see the module docstring.
+    assert_close(got[clear], single[clear], 1e-3, 1e-4, "EP vs single GPU")
     toks = [int(t) for t in clear[:: max(1, len(clear) // 32)]]
     ref = oracle_outputs(orc, layers[0], x, idx, w, toks)
     assert_close(got[toks], ref, what="EP vs oracle")

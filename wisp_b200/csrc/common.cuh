@@ -294,11 +294,4 @@ WB_DEV void red_add_f32(float* addr, float v) {
 
 WB_DEV bool elect_one() { return (threadIdx.x & 31) == 0; }
 
-// Programmatic dependent launch. Every kernel of the per-layer chain lets its
-// successor launch at once (trigger) and waits for its predecessor's
-// completion and memory before touching any data (wait); both are no-ops for
-// a kernel launched without the attribute.
-WB_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-WB_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
 }  // namespace wb

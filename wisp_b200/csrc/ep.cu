@@ -45,8 +45,6 @@ __global__ void ep_send_pack_kernel(const uint16_t* __restrict__ x, int M,
                                     const WispSegment* __restrict__ plan_segs, int e_loc,
                                     int n_rows, int world, int cap, uint16_t* __restrict__ xsend,
                                     int* __restrict__ slot) {
-  pdl_trigger();
-  pdl_wait();
   __shared__ int dst_row;
   const int p = blockIdx.x;
   if (threadIdx.x == 0) {
@@ -87,8 +85,6 @@ __global__ void __launch_bounds__(1024) ep_recv_plan_kernel(const int* __restric
                                                             WispSegment* __restrict__ segs,
                                                             int* __restrict__ src_pos,
                                                             int* __restrict__ total_out) {
-  pdl_trigger();
-  pdl_wait();
   __shared__ int src_off[1024];  // [s][e]: receive position of the chunk
   __shared__ int dst_off[1024];  // [s][e]: gathered position of the chunk
   __shared__ int cnt[1024];
@@ -131,8 +127,6 @@ template <bool GATHER>
 __global__ void ep_move_rows_kernel(void* __restrict__ a, void* __restrict__ b,
                                     const int* __restrict__ src_pos,
                                     const int* __restrict__ total, int row_bytes) {
-  pdl_trigger();
-  pdl_wait();
   const int j = blockIdx.x;
   if (j >= __ldg(total)) return;
   const size_t r = (size_t)__ldg(src_pos + j);
@@ -148,8 +142,6 @@ __global__ void ep_combine_kernel(const float* __restrict__ y, const int* __rest
                                   const int* __restrict__ row_token,
                                   const float* __restrict__ row_weight, int M,
                                   float* __restrict__ out) {
-  pdl_trigger();
-  pdl_wait();
   const int p = blockIdx.x;
   const float w = __ldg(row_weight + p);
   const float* yr = y + (size_t)__ldg(slot + p) * M;

@@ -60,6 +60,14 @@ constexpr int BM = 128;
 constexpr int kTmemCols = 512;
 constexpr int kAColBase = 256;
 constexpr int kRawK = 128;           // K per raw (weight) stage
+// Split K: a call with fewer tiles than half the SMs cuts each tile's K into
+// up to kMaxSplit ranges (work items) so more SMs take part; the down
+// projection's parts add into the output with its usual atomics, gate/up
+// parts go to a scratch buffer and the last part of a tile sums them in
+// order and applies SwiGLU. At most kMaxSplitItems split work items.
+constexpr int kMaxSplit = 8;
+constexpr int kMaxSplitItems = 256;
+constexpr size_t kPartialFloats = (size_t)BM * 128 * 2;   // one gate/up work item
 constexpr int kBoxBytes = BM * 64;   // one matrix's nibbles for a raw stage
 constexpr int kScBytes = 512;        // room for 2 scale groups x 128 rows (fp16)
 
@@ -117,7 +125,9 @@ struct GemmParams {
   const uint8_t* prepared;
   size_t p_flags, p_scales, p_zeros, p_mat_sc_bytes;
   const WispSegment* segs;
-  const int32_t* tiles;  // [0, S]: tile prefix; [S+1, 2S+1): bn per segment
+  const int32_t* tiles;  // [0, S]: tile prefix; [S+1, 2S+1): bn per segment; [2S+1]: K split
+  float* partial;        // split gate/up: per work item 128 rows x 128 columns x (gate, up)
+  int* tickets;          // split gate/up: arrivals per tile
   int nseg;
   int M, I, gs;
   __half* h_out;
@@ -200,8 +210,6 @@ __device__ __forceinline__ int bn_slot(int bn) {
 
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_constant__ GemmParams p) {
-  pdl_trigger();
-  pdl_wait();
   using S = Shape<MODE>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base_u32 = smem_u32(smem_raw);
@@ -212,11 +220,17 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = __ldg(p.tiles + p.nseg);
-  // A CTA without a tile leaves before any set-up, tensor memory included.
-  if ((int)blockIdx.x >= ntiles) return;
+  const int split = __ldg(p.tiles + 2 * p.nseg + 1);
+  const int nitems = ntiles * split;  // work item = (tile, K part), parts of a tile adjacent
+  // A CTA without work leaves before any set-up, tensor memory included.
+  if ((int)blockIdx.x >= nitems) return;
   const int K = MODE == GATEUP ? p.M : p.I;
-  const int nA = K / S::KA;           // A stages per tile
-  const int nR = K / kRawK;           // raw stages per tile
+  const int nR = K / kRawK;           // raw stages of the whole K
+  // Raw stages [r0, r1) and A stages [a0, a1) of K part ks.
+  auto part_range = [&](int ks, int& r0, int& r1) {
+    r0 = ks * nR / split;
+    r1 = (ks + 1) * nR / split;
+  };
   volatile int* abort = &L->abort;
 
   if (threadIdx.x == 0) {
@@ -266,10 +280,13 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
     int item = 0;
     bool ok = true;
     Prof pf(p.counters);
-    for (int tile = blockIdx.x; tile < ntiles && ok && !*abort; tile += gridDim.x) {
+    for (int it = blockIdx.x; it < nitems && ok && !*abort; it += gridDim.x) {
+      const int tile = it / split;
+      int r0, r1;
+      part_range(it - tile * split, r0, r1);
       const TileInfo ti = decode_tile(p, tile);
       const bool has_zero = __ldg(flags + ti.expert * 3 + mat) & 1;
-      for (int ks = 0; ks < nA; ks++, item++) {
+      for (int ks = r0 * S::kSub; ks < r1 * S::kSub; ks++, item++) {
         const int sub = ks % S::kSub;
         long long t0 = pf.now();
         if (sub == 0 && !mbar_wait(&L->rfull[rslot], rphase, abort)) { ok = false; break; }
@@ -344,7 +361,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       for (int i = 0; i < 16; i++) last_phase[i] = -1;
       bool ok = true;
       Prof pf(p.counters);
-      for (int tile = blockIdx.x; tile < ntiles && ok && !*abort; tile += gridDim.x) {
+      for (int it = blockIdx.x; it < nitems && ok && !*abort; it += gridDim.x) {
+        const int tile = it / split;
+        int r0, r1;
+        part_range(it - tile * split, r0, r1);
         const TileInfo ti = decode_tile(p, tile);
         const int m0 = MODE == GATEUP ? 0 : 2;
         uint32_t bytes = 0;
@@ -363,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
                   (size_t)ti.mblk * gpr * BM * 2;
           bytes += kBoxBytes + ng * BM * 2 * (hz[j] ? 2 : 1);
         }
-        for (int rs = 0; rs < nR; rs++, item++) {
+        for (int rs = r0; rs < r1; rs++, item++) {
           const long long t0 = pf.now();
           if (item >= S::kRawStages && !mbar_wait(&L->rempty[rslot], rphase ^ 1, abort)) { ok = false; break; }
           pf.add(0, t0);
@@ -401,13 +421,17 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       for (int i = 0; i < 8; i++) last_phase[i] = -1;
       bool ok = true;
       Prof pf(p.counters);
-      for (int tile = blockIdx.x; tile < ntiles && ok && !*abort; tile += gridDim.x) {
+      for (int it = blockIdx.x; it < nitems && ok && !*abort; it += gridDim.x) {
+        const int tile = it / split;
+        int r0, r1;
+        part_range(it - tile * split, r0, r1);
+        const int a_end = r1 * S::kSub;
         const TileInfo ti = decode_tile(p, tile);
         const CUtensorMap* tm = &p.tmap[bn_slot(ti.bn)];
         const int per_b = S::kBNMax / ti.bn;       // A stages per activation stage
         const int box_bytes = ti.bn * 128;
-        for (int a0 = 0; a0 < nA; a0 += per_b, item++) {
-          const int na = min(per_b, nA - a0);
+        for (int a0 = r0 * S::kSub; a0 < a_end; a0 += per_b, item++) {
+          const int na = min(per_b, a_end - a0);
           const long long t0 = pf.now();
           if (item >= S::kBStages && !mbar_wait(&L->bempty[sb], bphase ^ 1, abort)) { ok = false; break; }
           pf.add(0, t0);
@@ -440,7 +464,11 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       int ntile_local = 0;
       bool ok = true;
       Prof pf(p.counters);
-      for (int tile = blockIdx.x; tile < ntiles && ok && !*abort; tile += gridDim.x, ntile_local++) {
+      for (int it = blockIdx.x; it < nitems && ok && !*abort; it += gridDim.x, ntile_local++) {
+        const int tile = it / split;
+        int r0, r1;
+        part_range(it - tile * split, r0, r1);
+        const int a_beg = r0 * S::kSub, a_end = r1 * S::kSub;
         const TileInfo ti = decode_tile(p, tile);
         const uint32_t idesc = idesc_f16_m128(ti.bn);
         const int per_b = S::kBNMax / ti.bn;
@@ -450,7 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
         pf.add(2, t0);
         tc_fence_after();
         int a = 0;   // A stage within the current activation stage
-        for (int ks = 0; ks < nA; ks++) {
+        for (int ks = a_beg; ks < a_end; ks++) {
           if (a == 0) {
             t0 = pf.now();
             if (!mbar_wait(&L->bfull[sb], bphase, abort)) { ok = false; break; }
@@ -464,7 +492,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
           const uint64_t bd = bdesc0 + (uint64_t)((sb * S::kBStageBytes) >> 4) +
                               (uint64_t)(a * S::kBoxes) * box16;
           if (MODE == GATEUP) {
-            if (ks == 0) {
+            if (ks == a_beg) {
               mma_f16_ts_c<0>(tmem + 0, a_col, bd, idesc);
               mma_f16_ts_c<0>(tmem + 128, a_col + 32, bd, idesc);
             } else {
@@ -477,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
               mma_f16_ts_c<1>(tmem + 128, a_col + 32 + kk * 8, bd + 2 * kk, idesc);
             }
           } else {
-            if (ks == 0) mma_f16_ts_c<0>(tmem + 0, a_col, bd, idesc);
+            if (ks == a_beg) mma_f16_ts_c<0>(tmem + 0, a_col, bd, idesc);
             else mma_f16_ts_c<1>(tmem + 0, a_col, bd, idesc);
 #pragma unroll
             for (int kk = 1; kk < 8; kk++)
@@ -486,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
           }
           mma_commit(&L->aempty[sa]);
           if (++sa == kAStages) { sa = 0; aphase ^= 1; }
-          if (++a == per_b || ks == nA - 1) {
+          if (++a == per_b || ks == a_end - 1) {
             mma_commit(&L->bempty[sb]);
             a = 0;
             if (++sb == S::kBStages) { sb = 0; bphase ^= 1; }
@@ -507,13 +535,14 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
     }
   } else {
     // ------------------------------------------------------------------
-    // Epilogue warps 8-11.
+    // Epilogue warps 16-19: warp q owns accumulator rows 32q..32q+31.
     // ------------------------------------------------------------------
     const int q = warp & 3;
     const int r = q * 32 + lane;
     uint32_t accphase = 0;
     Prof pf(p.counters);
-    for (int tile = blockIdx.x; tile < ntiles && !*abort; tile += gridDim.x) {
+    for (int it = blockIdx.x; it < nitems && !*abort; it += gridDim.x) {
+      const int tile = it / split;
       const TileInfo ti = decode_tile(p, tile);
       const long long t0 = pf.now();
       if (!mbar_wait(&L->accfull, accphase, abort)) break;
@@ -521,20 +550,67 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       accphase ^= 1;
       tc_fence_after();
       const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+      bool released = false;
       if (MODE == GATEUP) {
         const int i = ti.mblk * BM + r;
         const int islot = k_interleave_slot(i);
-        for (int c0 = 0; c0 < ti.bn; c0 += 16) {
-          uint32_t g[16], u[16];
-          tmem_ld16(lane_addr + c0, g);
-          tmem_ld16(lane_addr + 128 + c0, u);
-          tmem_wait_ld();
+        if (split == 1) {
+          for (int c0 = 0; c0 < ti.bn; c0 += 16) {
+            uint32_t g[16], u[16];
+            tmem_ld16(lane_addr + c0, g);
+            tmem_ld16(lane_addr + 128 + c0, u);
+            tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; j++) {
-            const int tt = c0 + j;
-            if (tt < ti.nvalid) {
-              const float hv = silu(__uint_as_float(g[j])) * __uint_as_float(u[j]);
-              p.h_out[(size_t)(ti.row0 + tt) * p.I + islot] = __float2half(hv);
+            for (int j = 0; j < 16; j++) {
+              const int tt = c0 + j;
+              if (tt < ti.nvalid) {
+                const float hv = silu(__uint_as_float(g[j])) * __uint_as_float(u[j]);
+                p.h_out[(size_t)(ti.row0 + tt) * p.I + islot] = __float2half(hv);
+              }
+            }
+          }
+        } else {
+          // This K part's (gate, up) sums of row r go to the scratch row;
+          // the warp that completes the tile's rows 32q.. sums all parts in
+          // order (a per-tile, per-warp arrival count decides which).
+          float* prow = p.partial + (size_t)it * kPartialFloats + (size_t)r * 256;
+          for (int c0 = 0; c0 < ti.bn; c0 += 16) {
+            uint32_t g[16], u[16];
+            tmem_ld16(lane_addr + c0, g);
+            tmem_ld16(lane_addr + 128 + c0, u);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; j += 2)
+              *reinterpret_cast<float4*>(prow + (c0 + j) * 2) =
+                  make_float4(__uint_as_float(g[j]), __uint_as_float(u[j]),
+                              __uint_as_float(g[j + 1]), __uint_as_float(u[j + 1]));
+          }
+          tc_fence_before();
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&L->accempty);
+          released = true;
+          int old = 0;
+          if (lane == 0) {
+            __threadfence();
+            old = atomicAdd(p.tickets + tile * 4 + q, 1);
+            __threadfence();
+          }
+          old = __shfl_sync(0xffffffffu, old, 0);
+          if (old == split - 1) {
+            const float* base = p.partial + (size_t)tile * split * kPartialFloats + (size_t)r * 256;
+            for (int c = 0; c < ti.nvalid; c += 2) {
+              float4 acc = __ldcg(reinterpret_cast<const float4*>(base + c * 2));
+              for (int ks = 1; ks < split; ks++) {
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(base + ks * kPartialFloats + c * 2));
+                acc.x += v.x;
+                acc.y += v.y;
+                acc.z += v.z;
+                acc.w += v.w;
+              }
+              p.h_out[(size_t)(ti.row0 + c) * p.I + islot] = __float2half(silu(acc.x) * acc.y);
+              if (c + 1 < ti.nvalid)
+                p.h_out[(size_t)(ti.row0 + c + 1) * p.I + islot] = __float2half(silu(acc.z) * acc.w);
             }
           }
         }
@@ -568,9 +644,11 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
           }
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&L->accempty);
+      if (!released) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&L->accempty);
+      }
     }
     const int slots[4] = {C_EPI_ACCFULL, -1, -1, -1};
     pf.flush(slots, C_EPI_TOTAL, lane == 0);
@@ -586,11 +664,15 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
 }
 
 // Per segment: BN (16/32/64/128/256 by row count, at most max_bn) and the
-// prefix sum of tiles.
-// Segments of at most skip_rows rows belong to the register-path kernel and
-// get no tiles here.
+// prefix sum of tiles; then the K split (tiles[2 nseg + 1]): when the tiles
+// fill fewer than half of `target` SMs, each is cut into up to max_split K
+// parts of at least one raw stage (nraw stages in all), at most
+// kMaxSplitItems parts in all. `tickets` (split gate/up arrivals, 4 per
+// tile) are zeroed. Segments of at most skip_rows rows belong to the
+// register-path kernel and get no tiles here.
 __device__ void plan_tiles(const WispSegment* __restrict__ segs, int nseg, int mblocks,
-                           int skip_rows, int max_bn, int32_t* __restrict__ tiles) {
+                           int skip_rows, int max_bn, int max_split, int target, int nraw,
+                           int32_t* __restrict__ tiles, int32_t* __restrict__ tickets) {
   __shared__ int32_t warp_tot[32];
   __shared__ int32_t carry;
   if (threadIdx.x == 0) carry = 0;
@@ -629,7 +711,16 @@ __device__ void plan_tiles(const WispSegment* __restrict__ segs, int nseg, int m
     if (threadIdx.x == blockDim.x - 1) carry = incl;
     __syncthreads();
   }
-  if (threadIdx.x == 0) tiles[nseg] = carry;
+  if (threadIdx.x == 0) {
+    const int nt = carry;
+    int split = 1;
+    if (nt > 0 && 2 * nt <= target)
+      split = min(min(max_split, target / nt), min(nraw, kMaxSplitItems / nt));
+    tiles[nseg] = nt;
+    tiles[2 * nseg + 1] = max(split, 1);
+  }
+  if (tickets)
+    for (int i = threadIdx.x; i < 4 * kMaxSplitItems; i += blockDim.x) tickets[i] = 0;
 }
 
 // Units of the register-path kernel: `per_seg` row blocks per chunk of `cols`
@@ -695,16 +786,22 @@ struct PlanArgs {
   const WispSegment* segs;
   int nseg, sk_rows;
   int mb_gu, mb_dn, bn_gu, bn_dn;
+  int split_gu, split_dn, nraw_gu, nraw_dn, sms;
+  int32_t* tickets;
   int per_gu, per_dn, cols, ks_dn, nk_dn, target;
   int32_t *tiles_gu, *tiles_dn, *units_gu, *units_dn;
 };
 
 __global__ void __launch_bounds__(1024) plan_all_kernel(const __grid_constant__ PlanArgs a) {
-  pdl_trigger();
-  pdl_wait();
   switch (blockIdx.x) {
-    case 0: plan_tiles(a.segs, a.nseg, a.mb_gu, a.sk_rows, a.bn_gu, a.tiles_gu); break;
-    case 1: plan_tiles(a.segs, a.nseg, a.mb_dn, a.sk_rows, a.bn_dn, a.tiles_dn); break;
+    case 0:
+      plan_tiles(a.segs, a.nseg, a.mb_gu, a.sk_rows, a.bn_gu, a.split_gu, a.sms, a.nraw_gu,
+                 a.tiles_gu, a.tickets);
+      break;
+    case 1:
+      plan_tiles(a.segs, a.nseg, a.mb_dn, a.sk_rows, a.bn_dn, a.split_dn, a.sms, a.nraw_dn,
+                 a.tiles_dn, nullptr);
+      break;
     case 2: plan_units(a.segs, a.nseg, a.per_gu, a.cols, a.sk_rows, 1, 1, 0, a.units_gu); break;
     default:
       plan_units(a.segs, a.nseg, a.per_dn, a.cols, a.sk_rows, a.ks_dn, a.nk_dn, a.target,
@@ -935,10 +1032,20 @@ extern "C" WispError wisp_b200_prepare_experts(const WispMoeConfig* cfg,
   return WISP_OK;
 }
 
-// Tables: tensor-core gate/up and down [prefix S+1 | bn S] each, then the
-// register path's gate/up and down unit prefixes [S+1] each.
+// Workspace (int32 words): tensor-core gate/up and down tables [prefix S+1 |
+// bn S | K split] each, the register path's gate/up and down unit prefixes
+// [S+2] each, the split gate/up arrival counts [4 x kMaxSplitItems], then
+// (16-byte aligned) the split gate/up partial sums [kMaxSplitItems x 128 x
+// 128 x 2 floats].
+namespace {
+size_t tiles_partial_offset(int n_segs) {
+  const size_t w = (size_t)2 * (2 * n_segs + 2) + (size_t)2 * (n_segs + 2) + 4 * kMaxSplitItems;
+  return (w + 3) & ~(size_t)3;
+}
+}  // namespace
+
 extern "C" size_t wisp_b200_tiles_words(int n_segs) {
-  return (size_t)(2 * (2 * n_segs + 1) + 2 * (n_segs + 2));
+  return tiles_partial_offset(n_segs) + (size_t)kMaxSplitItems * kPartialFloats;
 }
 
 extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void* d_prepared,
@@ -995,7 +1102,7 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
   dn.out = d_out;
   dn.mode = mode;
 
-  const size_t tw = (size_t)(2 * n_segs + 1);
+  const size_t tw = (size_t)(2 * n_segs + 2);
   int sk_rows = g_skinny_rows >= 0 ? std::min(g_skinny_rows, wb::skinny_max_rows())
                                    : wb::skinny_max_rows();
   // The register-path kernel keeps the segment table in shared memory; larger
@@ -1005,9 +1112,16 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
   dn.tiles = d_tiles + tw;
   int32_t* units_gu = d_tiles + 2 * tw;
   int32_t* units_dn = units_gu + (n_segs + 2);
-  // Gate/up cannot split K (SwiGLU needs whole sums), nor can mode 1 (plain
-  // row stores); the weighted down projection splits K when it has fewer
-  // than two units per SM.
+  int32_t* tickets = units_dn + (n_segs + 2);
+  float* partial = reinterpret_cast<float*>(d_tiles + tiles_partial_offset(n_segs));
+  gu.tickets = tickets;
+  gu.partial = partial;
+  // Register path: gate/up cannot split K (SwiGLU needs whole sums), nor can
+  // mode 1 (plain row stores); the weighted down projection splits K when it
+  // has fewer than two units per SM. Tensor-core path: both projections split
+  // K when their tiles fill fewer than half the SMs (gate/up through the
+  // partial sums, the weighted down projection through its atomics; mode 1
+  // does not split).
   PlanArgs pa;
   pa.segs = d_segs;
   pa.nseg = n_segs;
@@ -1022,6 +1136,12 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
   pa.ks_dn = mode == 0 ? 8 : 1;
   pa.nk_dn = wb::skinny_stages(I);
   pa.target = 2 * num_sms();
+  pa.sms = num_sms();
+  pa.split_gu = kMaxSplit;
+  pa.split_dn = mode == 0 ? kMaxSplit : 1;
+  pa.nraw_gu = M / kRawK;
+  pa.nraw_dn = I / kRawK;
+  pa.tickets = tickets;
   pa.tiles_gu = d_tiles;
   pa.tiles_dn = d_tiles + tw;
   pa.units_gu = units_gu;

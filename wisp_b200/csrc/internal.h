@@ -5,7 +5,6 @@
 
 #include <cstdarg>
 #include <cstdio>
-#include <cstdlib>
 #include <cstring>
 #include <utility>
 
@@ -13,20 +12,8 @@
 
 namespace wb {
 
-// Programmatic dependent launch is on unless WISP_B200_PDL=0.
-inline bool pdl_enabled() {
-  static const bool on = [] {
-    const char* e = std::getenv("WISP_B200_PDL");
-    return !(e && e[0] == '0');
-  }();
-  return on;
-}
-
-// Launches a kernel of the per-layer chain with programmatic stream
-// serialisation: the kernel may start while its predecessor in the stream
-// runs (it begins with griddepcontrol.wait, so it sees the predecessor's
-// results), which hides the launch latency between consecutive kernels,
-// inside CUDA graphs too. Errors are left for cudaGetLastError.
+// Launches a kernel of the per-layer chain in plain stream order (errors are
+// left for cudaGetLastError).
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                             cudaStream_t st, Args&&... args) {
@@ -35,11 +22,8 @@ inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, siz
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.attrs = nullptr;
+  cfg.numAttrs = 0;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 

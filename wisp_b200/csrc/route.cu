@@ -47,8 +47,6 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __re
                                                             const uint16_t* __restrict__ W,
                                                             float* __restrict__ part, int T, int E,
                                                             int M, int kspan) {
-  pdl_trigger();
-  pdl_wait();
   __shared__ float xs[kRK][kRT + 4];
   __shared__ float ws[kRK][kRE + 4];
   const int e0 = blockIdx.x * kRE, t0 = blockIdx.y * kRT;
@@ -122,8 +120,6 @@ __global__ void __launch_bounds__(256) router_gemv_kernel(const uint16_t* __rest
                                                           const uint16_t* __restrict__ W,
                                                           float* __restrict__ logits, int T, int E,
                                                           int M) {
-  pdl_trigger();
-  pdl_wait();
   __shared__ float red[8][kGemvMaxT];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.x * 2 + warp / kGemvQ, q = warp % kGemvQ;
@@ -192,35 +188,37 @@ __device__ __forceinline__ void warp_argmax(float& v, int& i) {
   }
 }
 
-constexpr int kMaxPerLane = 32;  // E <= 1024
+// Shared-memory index of expert e in a warp's score row: one pad word per 32
+// so that lanes scanning different groups hit different banks.
+__device__ __forceinline__ int pad32(int e) { return e + (e >> 5); }
 
-// One warp per token. Writes idx/w [T x k] and, optionally, the fp32 logits.
+// One warp per token; lane l holds experts l + 32 j for j < PER (E <= 32 PER).
+// Writes idx/w [T x k] and, optionally, the fp32 logits.
+template <int PER>
 __global__ void topk_kernel(const float* __restrict__ part, int splits, const float* __restrict__ bias,
                             int T, int E, int k, int scoring, int n_groups, int topk_groups,
                             float scaling, int* __restrict__ idx, float* __restrict__ wout,
                             float* __restrict__ logits_out) {
-  pdl_trigger();
-  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * (blockDim.x >> 5) + warp;
   if (t >= T) return;
   const int per = (E + 31) / 32;
-  float v[kMaxPerLane];
+  float v[PER];
 #pragma unroll
-  for (int j = 0; j < kMaxPerLane; j++) v[j] = 0.f;
+  for (int j = 0; j < PER; j++) v[j] = 0.f;
   // Split-K partials: split-major, all of a split's loads in flight together
   // (a per-expert loop over the splits would wait one L2 round trip per
   // split and expert).
   for (int z = 0; z < splits; z++) {
     const float* pz = part + ((size_t)z * T + t) * E;
 #pragma unroll
-    for (int j = 0; j < kMaxPerLane; j++) {
+    for (int j = 0; j < PER; j++) {
       const int e = lane + 32 * j;
       if (j < per && e < E) v[j] += __ldg(pz + e);
     }
   }
 #pragma unroll
-  for (int j = 0; j < kMaxPerLane; j++) {
+  for (int j = 0; j < PER; j++) {
     const int e = lane + 32 * j;
     if (j < per && e < E) {
       if (bias) v[j] += bias[e];
@@ -234,12 +232,12 @@ __global__ void topk_kernel(const float* __restrict__ part, int splits, const fl
   if (scoring == WISP_SCORE_SOFTMAX) {
     float mx = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < kMaxPerLane; j++) mx = fmaxf(mx, v[j]);
+    for (int j = 0; j < PER; j++) mx = fmaxf(mx, v[j]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float sum = 0.f;
 #pragma unroll
-    for (int j = 0; j < kMaxPerLane; j++) {
+    for (int j = 0; j < PER; j++) {
       v[j] = (j < per && lane + 32 * j < E) ? expf(v[j] - mx) : -1.f;
       sum += v[j] > 0.f ? v[j] : 0.f;
     }
@@ -247,7 +245,7 @@ __global__ void topk_kernel(const float* __restrict__ part, int splits, const fl
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     const float inv = 1.f / sum;
 #pragma unroll
-    for (int j = 0; j < kMaxPerLane; j++)
+    for (int j = 0; j < PER; j++)
       if (v[j] >= 0.f) v[j] *= inv;
     float wsum = 0.f;
     float myw = 0.f;
@@ -256,7 +254,7 @@ __global__ void topk_kernel(const float* __restrict__ part, int splits, const fl
       float bv = -1.f;
       int bi = -1;
 #pragma unroll
-      for (int j = 0; j < kMaxPerLane; j++) {
+      for (int j = 0; j < PER; j++) {
         const int e = lane + 32 * j;
         if (j < per && e < E && !((taken >> j) & 1u) && v[j] > bv) {
           bv = v[j];
@@ -279,20 +277,20 @@ __global__ void topk_kernel(const float* __restrict__ part, int splits, const fl
     // Sigmoid group-limited.
     const int gsz = E / n_groups;
 #pragma unroll
-    for (int j = 0; j < kMaxPerLane; j++)
+    for (int j = 0; j < PER; j++)
       if (j < per && lane + 32 * j < E) v[j] = 1.f / (1.f + expf(-v[j]));
     // Group scores: lane g scans its group through shared memory.
-    __shared__ float sval[8][1024];
+    __shared__ float sval[8][1024 + 32];
     float* mys = sval[warp];
 #pragma unroll
-    for (int j = 0; j < kMaxPerLane; j++)
-      if (j < per && lane + 32 * j < E) mys[lane + 32 * j] = v[j];
+    for (int j = 0; j < PER; j++)
+      if (j < per && lane + 32 * j < E) mys[pad32(lane + 32 * j)] = v[j];
     __syncwarp();
     float gscore = -INFINITY;
     if (lane < n_groups) {
       float a = -INFINITY, b = -INFINITY;
       for (int q = 0; q < gsz; q++) {
-        const float s = mys[lane * gsz + q];
+        const float s = mys[pad32(lane * gsz + q)];
         if (s > a) {
           b = a;
           a = s;
@@ -310,15 +308,21 @@ __global__ void topk_kernel(const float* __restrict__ part, int splits, const fl
       if (bi == lane) gsel = true;
     }
     const unsigned gmask = __ballot_sync(0xffffffffu, gsel);
+    uint32_t allow = 0;  // bit j: expert lane + 32 j lies in a kept group
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+      const int e = lane + 32 * j;
+      if (j < per && e < E && ((gmask >> (e / gsz)) & 1u)) allow |= 1u << j;
+    }
     float ssum = 0.f, myw = 0.f;
     int myi = -1;
     for (int r = 0; r < k; r++) {
       float bv = -INFINITY;
       int bi = -1;
 #pragma unroll
-      for (int j = 0; j < kMaxPerLane; j++) {
+      for (int j = 0; j < PER; j++) {
         const int e = lane + 32 * j;
-        if (j < per && e < E && !((taken >> j) & 1u) && ((gmask >> (e / gsz)) & 1u) && (bi < 0 || v[j] > bv)) {
+        if (((allow & ~taken) >> j) & 1u && (bi < 0 || v[j] > bv)) {
           bv = v[j];
           bi = e;
         }
@@ -341,8 +345,6 @@ __global__ void topk_kernel(const float* __restrict__ part, int splits, const fl
 // counts[v] for the routed experts: one warp per expert over all T*k slots.
 __global__ void count_kernel(const int* __restrict__ idx, int nslots, int E, int T, int has_shared,
                              int* __restrict__ counts) {
-  pdl_trigger();
-  pdl_wait();
   const int v = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (v >= E + has_shared) return;
@@ -361,8 +363,6 @@ __global__ void count_kernel(const int* __restrict__ idx, int nslots, int E, int
 
 // Exclusive scan of counts into segments (single block).
 __global__ void segments_kernel(const int* __restrict__ counts, int V, WispSegment* __restrict__ segs) {
-  pdl_trigger();
-  pdl_wait();
   __shared__ int warp_tot[32];
   __shared__ int carry;
   if (threadIdx.x == 0) carry = 0;
@@ -408,8 +408,6 @@ __global__ void segments_kernel(const int* __restrict__ counts, int V, WispSegme
 __global__ void fill_kernel(const int* __restrict__ idx, const float* __restrict__ w, int nslots,
                             int k, int E, int T, int has_shared, const WispSegment* __restrict__ segs,
                             int* __restrict__ row_token, float* __restrict__ row_weight) {
-  pdl_trigger();
-  pdl_wait();
   const int v = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (v >= E + has_shared) return;
@@ -438,8 +436,6 @@ __global__ void fill_kernel(const int* __restrict__ idx, const float* __restrict
 // xp[p] = fp16(x[src[p]]) in interleaved K order; each thread moves 8 values.
 __global__ void pack_rows_kernel(const uint16_t* __restrict__ x, const int* __restrict__ src, int n_rows,
                                  int M, uint16_t* __restrict__ xp) {
-  pdl_trigger();
-  pdl_wait();
   const int p = blockIdx.x;
   if (p >= n_rows) return;
   const int s = src ? src[p] : p;
@@ -467,8 +463,6 @@ __global__ void pack_rows_kernel(const uint16_t* __restrict__ x, const int* __re
 // between stacked MoE layers. One block per token.
 __global__ void rms_rescale_kernel(const float* __restrict__ x, uint16_t* __restrict__ y, int M,
                                    float eps) {
-  pdl_trigger();
-  pdl_wait();
   __shared__ float red[32];
   const float* xr = x + (size_t)blockIdx.x * M;
   float s = 0.f;
@@ -495,8 +489,6 @@ __global__ void rms_rescale_kernel(const float* __restrict__ x, uint16_t* __rest
 __global__ void combine_rows_kernel(const float* __restrict__ y, const int* __restrict__ row_token,
                                     const float* __restrict__ row_weight, int M,
                                     float* __restrict__ out) {
-  pdl_trigger();
-  pdl_wait();
   const int p = blockIdx.x;
   const int t = row_token[p];
   const float w = row_weight[p];
@@ -549,8 +541,10 @@ WispError launch_route(const WispMoeConfig* c, const uint16_t* x, const uint16_t
     else
       wb::launch_k(router_logits_kernel<false>, g1, 256, 0, st, x, W, part, T, E, M, kspan);
   }
-  wb::launch_k(topk_kernel, (T + 7) / 8, 256, 0, st, part, nsplit, bias, T, E, c->top_k,
-               c->scoring, c->n_groups, c->topk_groups, c->routed_scaling, idx, w, logits_out);
+  auto topk = E <= 32 ? topk_kernel<1> : E <= 64 ? topk_kernel<2> : E <= 128 ? topk_kernel<4>
+            : E <= 256 ? topk_kernel<8> : E <= 512 ? topk_kernel<16> : topk_kernel<32>;
+  wb::launch_k(topk, (T + 7) / 8, 256, 0, st, part, nsplit, bias, T, E, c->top_k, c->scoring,
+               c->n_groups, c->topk_groups, c->routed_scaling, idx, w, logits_out);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }

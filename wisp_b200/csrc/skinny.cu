@@ -642,8 +642,6 @@ __device__ void sk_consumer(const SkParams& p, uint8_t* ring, SkSmem* L, int tot
 
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) skinny_ffn_kernel(const __grid_constant__ SkParams p) {
-  pdl_trigger();
-  pdl_wait();
   extern __shared__ uint8_t smem_raw[];
   const int total = __ldg(p.units + p.nseg);
   if ((int)blockIdx.x >= total) return;
