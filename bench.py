@@ -455,9 +455,9 @@ def main() -> None:
     # Our kernels per layer: route 2 (logits, top-k) + plan 3 (count,
     # segments, fill) + grouped FFN 5 (one tile/unit planner, register-path
     # and tensor-core kernels for gate/up and down); single GPU: + pack 1;
-    # expert-parallel: + send-pack, receive-plan, gather, scatter, combine,
-    # and for the shared expert pack 1 + grouped 5. Plus one rms_rescale
-    # between layers.
+    # expert-parallel: + dispatch 2 (slots and entries, rows), receive-plan,
+    # gather, combine, and for the shared expert pack 1 + grouped 5. Plus one
+    # rms_rescale between layers.
     per_layer = 11 if world == 1 else 15 + (6 if spec.has_shared else 0)
     launches_per_step = per_layer * L + (L - 1)
     line = {

@@ -292,48 +292,52 @@ WispError wisp_b200_combine_rows(const float* d_y, const int* d_row_token, const
 
 /* --------------------------------------------------------------------------
  * Expert-parallel exchange (no counterpart in the reference, which runs on one
- * GPU). Experts are sharded in contiguous blocks of n_experts/world; rows
- * travel in fixed-size blocks of `cap` rows per rank pair (cap >= the rows
- * one rank routes, tokens * top_k), so all counts stay on the device.
+ * GPU). Experts are sharded in contiguous blocks of e_loc = n_experts/world.
+ * Each rank pair exchanges one fixed-size block per direction, so all counts
+ * stay on the device; a token travels to an owner rank once, whatever the
+ * number of its experts there. cap = the most tokens any rank holds. Block
+ * layout (wisp_b200_ep_block_bytes bytes, 16-byte aligned parts):
+ *   int32 n_rows, 3 pad; int32 cnt[e_loc]           header
+ *   int32 ent_row[cap*top_k]; float ent_w[cap*top_k] entries, expert-major
+ *   fp16 rows[cap][hidden]                           interleaved K order
  * ------------------------------------------------------------------------ */
+size_t wisp_b200_ep_block_bytes(int hidden, int e_loc, int cap, int top_k);
 
-/* Rows of a dispatch plan (d_plan_segs / d_row_token from
- * wisp_b200_dispatch_plan, rows sorted by expert) into the send buffer:
- * row p goes to slot q*cap + (p - first row for rank q), q = owner of its
- * expert, as fp16 in interleaved K order. d_xsend [world*cap x hidden];
- * d_slot[p] receives the slot (the combine reads the returned row there). */
-WispError wisp_b200_ep_send_pack(const uint16_t* d_x, int hidden, const int* d_row_token,
-                                 const WispSegment* d_plan_segs, int n_experts, int n_rows,
-                                 int world, int cap, uint16_t* d_xsend, int* d_slot,
-                                 cudaStream_t stream, WispErrCtx* err);
+/* Send side: d_send [world blocks] from this rank's routing (d_topk_idx
+ * [tokens x top_k], global experts) and its dispatch plan over the n_experts
+ * routed experts (d_plan_segs, d_row_token, d_row_weight from
+ * wisp_b200_dispatch_plan with has_shared = 0). d_slot [tokens x world]
+ * receives the row of each token in each block (-1: not sent there). */
+WispError wisp_b200_ep_dispatch(const uint16_t* d_x, int tokens, int hidden, const int* d_topk_idx,
+                                int top_k, const WispSegment* d_plan_segs, const int* d_row_token,
+                                const float* d_row_weight, int n_experts, int world, int cap,
+                                uint8_t* d_send, int* d_slot, cudaStream_t stream, WispErrCtx* err);
 
-/* Receive side, from the per-source row counts d_recv_counts [world x e_loc]
- * (source s's block starts at row s*cap; world * e_loc <= 1024): the
- * received rows are gathered expert-contiguous (expert, then source) so that
- * each local expert is one segment: d_segs [e_loc] over the gathered rows,
- * d_src_pos[j] = receive row of gathered row j, *d_total = rows received.
- * d_src_pos holds world*cap entries. */
-WispError wisp_b200_ep_recv_plan(const int* d_recv_counts, int world, int e_loc, int cap,
-                                 WispSegment* d_segs, int* d_src_pos, int* d_total,
-                                 cudaStream_t stream, WispErrCtx* err);
+/* Receive side, from the received blocks d_recv [world blocks] (world * e_loc
+ * <= 1024): the entries are gathered expert-contiguous (expert, then source)
+ * so each local expert is one segment: d_segs [e_loc] over the gathered
+ * rows, d_src_pos[j] = receive row (source * cap + block row) and
+ * d_weight[j] = routing weight of gathered row j, *d_total = entries.
+ * d_src_pos and d_weight hold world * cap * top_k entries. */
+WispError wisp_b200_ep_recv_plan(const uint8_t* d_recv, int world, int e_loc, int cap, int top_k,
+                                 int hidden, WispSegment* d_segs, int* d_src_pos, float* d_weight,
+                                 int* d_total, cudaStream_t stream, WispErrCtx* err);
 
-/* d_sorted[j] = d_recv[d_src_pos[j]] for j < *d_total (fp16 rows; max_rows
- * bounds the launch, normally world*cap). */
-WispError wisp_b200_ep_gather_rows(const uint16_t* d_recv, const int* d_src_pos, const int* d_total,
-                                   int max_rows, int hidden, uint16_t* d_sorted,
-                                   cudaStream_t stream, WispErrCtx* err);
+/* d_sorted[j] = receive row d_src_pos[j] for j < *d_total (fp16 rows;
+ * max_rows bounds the launch, normally world * cap * top_k). The grouped FFN
+ * then runs in mode 0 with row_token = d_src_pos and row_weight = d_weight
+ * into fp32 rows [world * cap x hidden] (zeroed first): one row per received
+ * token, which the return exchange sends back. */
+WispError wisp_b200_ep_gather_rows(const uint8_t* d_recv, int world, int e_loc, int cap, int top_k,
+                                   int hidden, const int* d_src_pos, const int* d_total,
+                                   int max_rows, uint16_t* d_sorted, cudaStream_t stream,
+                                   WispErrCtx* err);
 
-/* d_recv[d_src_pos[j]] = d_sorted[j] for j < *d_total (fp32 rows): FFN
- * results back into the source blocks for the return exchange. */
-WispError wisp_b200_ep_scatter_rows(const float* d_sorted, const int* d_src_pos, const int* d_total,
-                                    int max_rows, int hidden, float* d_recv, cudaStream_t stream,
-                                    WispErrCtx* err);
-
-/* d_out[row_token[p]] += row_weight[p] * d_y[d_slot[p]] for p < n_rows (fp32
- * rows returned in the send layout; atomic adds). */
-WispError wisp_b200_ep_combine(const float* d_y, const int* d_slot, const int* d_row_token,
-                               const float* d_row_weight, int n_rows, int hidden, float* d_out,
-                               cudaStream_t stream, WispErrCtx* err);
+/* d_out[t] += d_yback[q * cap + d_slot[t * world + q]] over q = 0..world-1
+ * with a slot >= 0, in rank order (fp32 rows; one block per token). */
+WispError wisp_b200_ep_combine(const float* d_yback, const int* d_slot, int tokens, int world,
+                               int cap, int hidden, float* d_out, cudaStream_t stream,
+                               WispErrCtx* err);
 
 /* Between stacked layers: d_out[t] = bf16(d_in[t] / rms(d_in[t])), fp32 in. */
 WispError wisp_b200_rms_rescale(const float* d_in, uint16_t* d_out, int tokens, int hidden,

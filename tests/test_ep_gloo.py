@@ -21,7 +21,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from wisp_b200 import synth
-from wisp_b200.ep import EpLayer, block_range, recv_layout, send_splits
+from wisp_b200.ep import BlockLayout, EpLayer, block_range, dispatch_reference
 
 SPEC = synth.MoeSpec("ep_cpu", 256, 128, 8, 2, group_size=64, has_shared=True, tokens=10, seed=21)
 
@@ -59,38 +59,64 @@ class CpuOps:
             counts[e] = n
             sv[e, 2] = n
 
-    def send_pack(self, x, row_token, plan_segs, n_experts, n_rows, world, cap, xsend, slot):
-        e_loc = n_experts // world
-        begin = plan_segs.numpy().view(np.int32).reshape(-1, 4)[:, 1]
-        xd = x.double()
-        for p in range(n_rows):
-            q = max(r for r in range(world) if begin[r * e_loc] <= p)
-            d = q * cap + p - int(begin[q * e_loc])
-            slot[p] = d
-            xsend[d] = xd[int(row_token[p])]
+    def block_layout(self, hidden, e_loc, cap, k):
+        self.lay = BlockLayout(hidden, e_loc, cap, k, 8)   # float64 rows
+        return self.lay
 
-    def recv_plan(self, recv_counts, world, e_loc, cap, segs, src_pos, total):
-        rc = recv_counts.numpy().reshape(world, e_loc)
+    def _views(self, buf, q, lay):
+        b = buf.numpy()[q * lay.bytes:(q + 1) * lay.bytes]
+        hdr = b[:lay.off_ent].view(np.int32)
+        ent = b[lay.off_ent:lay.off_w].view(np.int32)
+        ew = b[lay.off_w:lay.off_w + 4 * lay.cap * lay.k].view(np.float32)
+        rows = b[lay.off_rows:lay.off_rows + lay.cap * lay.hidden * 8].view(np.float64)
+        return hdr, ent, ew, rows.reshape(lay.cap, lay.hidden)
+
+    def dispatch(self, x, idx, plan_segs, row_token, row_weight, n_experts, world, cap, send, slot):
+        lay = self.lay
+        T = x.shape[0]
+        slot_ref, entries = dispatch_reference(idx.numpy(), n_experts, world)
+        slot.copy_(torch.from_numpy(slot_ref).int())
+        e_loc = n_experts // world
+        sv = plan_segs.numpy().view(np.int32).reshape(-1, 4)
+        wv = row_weight.numpy()
+        xd = x.double().numpy()
+        for q in range(world):
+            hdr, ent, ew, rows = self._views(send, q, lay)
+            hdr[0] = int((slot_ref[:, q] >= 0).sum())
+            hdr[4:4 + e_loc] = sv[q * e_loc:(q + 1) * e_loc, 2]
+            first = int(sv[q * e_loc, 1])
+            # the plan rows of q's experts, in plan order, are the entries
+            for i, (r, t, j) in enumerate(entries[q]):
+                p = first + i
+                assert int(row_token[p]) == t
+                ent[i] = r
+                ew[i] = wv[p]
+            for t in range(T):
+                if slot_ref[t, q] >= 0:
+                    rows[slot_ref[t, q]] = xd[t]
+
+    def recv_plan(self, recv, world, e_loc, cap, k, hidden, segs, src_pos, weight, total):
+        lay = self.lay
         sv = segs.numpy().view(np.int32).reshape(-1, 4)
-        src_off = np.concatenate([np.zeros((world, 1), np.int64), np.cumsum(rc, axis=1)[:, :-1]],
-                                 axis=1) + np.arange(world)[:, None] * cap
+        views = [self._views(recv, s, lay) for s in range(world)]
+        off = [np.concatenate([[0], np.cumsum(v[0][4:4 + e_loc])[:-1]]) for v in views]
         j = 0
         for e in range(e_loc):
             b = j
             for s in range(world):
-                for i in range(int(rc[s, e])):
-                    src_pos[j] = int(src_off[s, e]) + i
+                hdr, ent, ew, _ = views[s]
+                for i in range(int(hdr[4 + e])):
+                    src_pos[j] = s * cap + int(ent[off[s][e] + i])
+                    weight[j] = float(ew[off[s][e] + i])
                     j += 1
             sv[e] = (e, b, j - b, 0)
         total[0] = j
 
-    def gather_rows(self, recv, src_pos, total, max_rows, sorted_rows):
+    def gather_rows(self, recv, world, e_loc, cap, k, hidden, src_pos, total, max_rows, sorted_rows):
+        lay = self.lay
         for j in range(int(total[0])):
-            sorted_rows[j] = recv[int(src_pos[j])]
-
-    def scatter_rows(self, sorted_rows, src_pos, total, max_rows, recv):
-        for j in range(int(total[0])):
-            recv[int(src_pos[j])] = sorted_rows[j]
+            r = int(src_pos[j])
+            sorted_rows[j] = torch.from_numpy(self._views(recv, r // cap, lay)[3][r % cap].copy())
 
     def grouped_dev(self, cfg, lw, segs, n_segs, rows, xp, h, mode, row_token, row_weight, out,
                     tiles, flag):
@@ -98,9 +124,12 @@ class CpuOps:
         self.grouped(cfg, lw, [(int(e), int(b), int(r)) for e, b, r, _ in sv], rows, xp, h, mode,
                      row_token, row_weight, out, tiles, flag)
 
-    def ep_combine(self, y, slot, row_token, row_weight, n_rows, out):
-        for p in range(n_rows):
-            out[int(row_token[p])] += float(row_weight[p]) * y[int(slot[p])]
+    def ep_combine(self, yback, slot, tokens, world, cap, out):
+        sl = slot.numpy()
+        for t in range(tokens):
+            for q in range(world):
+                if sl[t, q] >= 0:
+                    out[t] += yback[q * cap + int(sl[t, q])]
 
     def pack(self, x, src, n_rows, xp):
         xd = x.double()
@@ -160,15 +189,18 @@ def _worker(rank, world, port, outdir, spec, mode):
             dist.destroy_process_group()
 
 
-def test_send_splits_and_recv_layout():
-    counts = np.array([3, 0, 2, 5, 1, 1, 0, 4])
-    assert send_splits(counts, 8, 2) == [10, 6]
-    assert send_splits(counts, 8, 4) == [3, 7, 2, 4]
-    rc = np.array([[1, 2], [0, 3], [4, 0]])       # 3 sources, 2 local experts
-    segs, per_src = recv_layout(rc)
-    assert per_src == [3, 3, 4]
-    # expert-major: expert 0 from sources 0,1,2 then expert 1 from 0,1,2
-    assert segs == [(0, 0, 1), (0, 3, 0), (0, 6, 4), (1, 1, 2), (1, 3, 3), (1, 10, 0)]
+def test_dispatch_layout():
+    """A token is sent once per owner rank; entries are expert-major, then
+    token order; the Python block layout matches the library's."""
+    idx = np.array([[0, 5], [1, 2], [7, 4], [3, 3]])   # 4 tokens, k=2, 8 experts
+    slot, entries = dispatch_reference(idx, 8, 2)       # ranks own experts 0-3 / 4-7
+    assert slot.tolist() == [[0, 0], [1, -1], [-1, 1], [2, -1]]
+    assert entries[0] == [(0, 0, 0), (1, 1, 0), (1, 1, 1), (2, 3, 0), (2, 3, 1)]
+    assert entries[1] == [(1, 2, 1), (0, 0, 1), (1, 2, 0)]
+    from wisp_b200 import abi
+    for hidden, e_loc, cap, k in [(7168, 48, 32, 8), (256, 4, 5, 2), (4096, 1, 1, 1)]:
+        assert BlockLayout(hidden, e_loc, cap, k).bytes == \
+            abi.lib().wisp_b200_ep_block_bytes(hidden, e_loc, cap, k)
 
 
 @pytest.mark.parametrize("spec", [SPEC, synth.small(SPEC, skew=True, seed=4, tokens=7)])

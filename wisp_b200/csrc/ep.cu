@@ -3,29 +3,35 @@
 // The reference engine runs on one GPU and has no expert parallelism; these
 // kernels serve the multi-GPU path (wisp_b200/ep.py), where routed experts
 // are sharded in contiguous blocks of E/N over N ranks and token rows travel
-// to their experts' owner and back through fixed-size NCCL all-to-all
+// to their experts' owners and back through fixed-size NCCL all-to-all
 // exchanges. Fixed sizes keep every count on the device: no host round trip
 // sits between routing and the expert FFN.
 //
-// Layout of the exchange buffers: rank r's send buffer holds, for each
-// destination q, a block of `cap` rows (cap = tokens * top_k, the most any
-// one destination can receive); the rows for q occupy the block's first
-// rows in expert order. After the all-to-all, the receive buffer holds the
-// source blocks in rank order, so source s's rows for local expert e start
-// at s*cap + (rows s sends for experts before e). Before the expert FFN the
-// received rows are gathered expert-contiguous, so each local expert is ONE
-// segment (its weights are streamed once, whatever the number of ranks,
-// and it runs on the same kernel as in a single-GPU call); the results are
-// scattered back into the source blocks for the return trip.
+// A token goes to an owner rank once, whatever the number of its experts
+// there: rank r's send buffer holds one block per destination q, with
+//   n_rows                 rows in the block (the tokens with >= 1 expert on q,
+//                          in token order)
+//   cnt[e_loc]             routed (token, expert) entries per local expert of q
+//   ent_row[cap*k]         the entries, expert-major (then token order): block
+//   ent_w[cap*k]           row and routing weight
+//   rows[cap][hidden]      the token rows, fp16 in interleaved K order
+// with cap = the most tokens any rank holds (a token fills at most one row
+// per block). One all-to-all moves the blocks; the owner gathers the rows
+// expert-contiguous (each local expert is ONE segment, as on one GPU), runs
+// the grouped FFN with the routing weights, which adds every expert's
+// weighted output into an fp32 row per received token, and one all-to-all
+// returns those rows; the home rank adds its rows from each owner.
 //
-//   ep_send_pack_kernel     row p of the dispatch plan (sorted by expert)
-//                           -> send slot q*cap + (p - first row for q),
-//                           bf16 -> fp16 in interleaved K order.
-//   ep_recv_plan_kernel     per-source receive counts -> one segment per
-//                           local expert over the gathered rows, and the
-//                           receive position of every gathered row.
-//   ep_move_rows_kernel     gather (fp16 rows) / scatter back (fp32 rows).
-//   ep_combine_kernel       out[token(p)] += w_p * y_back[slot(p)].
+//   ep_dispatch_kernel   one block: per destination the token -> row slots
+//                        (a scan over tokens), the block headers and the
+//                        entries from the dispatch plan.
+//   ep_pack_kernel       token rows (bf16 -> fp16 interleaved) into every
+//                        block that holds them.
+//   ep_recv_plan_kernel  one block: from the received headers and entries,
+//                        one segment per local expert over the gathered
+//                        rows, the receive row and weight of each.
+//   ep_gather_kernel     gathered fp16 rows from the receive blocks.
+//   ep_combine_kernel    out[t] += the returned rows of token t, in rank order.
 #include <cuda_bf16.h>
 
 #include "common.cuh"
@@ -37,28 +43,110 @@ namespace {
 
 constexpr int kMaxWorld = 64;
 
+struct Layout {
+  size_t off_ent, off_w, off_rows, bytes;
+  int cap;
+};
+
+__host__ __device__ inline size_t align16(size_t v) { return (v + 15) & ~(size_t)15; }
+
+// Byte layout of one exchange block (elem = bytes per row element).
+__host__ __device__ inline Layout ep_layout(int hidden, int e_loc, int cap, int top_k, int elem) {
+  Layout L;
+  L.cap = cap;
+  L.off_ent = align16(16 + 4 * (size_t)e_loc);
+  L.off_w = L.off_ent + 4 * (size_t)cap * top_k;
+  L.off_rows = align16(L.off_w + 4 * (size_t)cap * top_k);
+  L.bytes = align16(L.off_rows + (size_t)cap * hidden * elem);
+  return L;
+}
+
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t b) { return __uint_as_float(b << 16); }
 
-// One block per plan row.
-__global__ void ep_send_pack_kernel(const uint16_t* __restrict__ x, int M,
-                                    const int* __restrict__ row_token,
-                                    const WispSegment* __restrict__ plan_segs, int e_loc,
-                                    int n_rows, int world, int cap, uint16_t* __restrict__ xsend,
-                                    int* __restrict__ slot) {
-  __shared__ int dst_row;
-  const int p = blockIdx.x;
-  if (threadIdx.x == 0) {
-    // destination rank: the last q whose first row is <= p
-    int q = 0;
-    for (int r = 1; r < world; r++)
-      if (__ldg(&plan_segs[r * e_loc].row_begin) <= p) q = r;
-    const int d = q * cap + (p - __ldg(&plan_segs[q * e_loc].row_begin));
-    slot[p] = d;
-    dst_row = d;
+// Exclusive scan of one flag per thread over the block; returns the prefix
+// and leaves the block total in *total (all threads must call).
+__device__ int block_scan(int f, int* warp_tot, int* total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int v = f;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += y;
+  }
+  if (lane == 31) warp_tot[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    int tv = lane < (int)(blockDim.x >> 5) ? warp_tot[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, tv, o);
+      if (lane >= o) tv += y;
+    }
+    warp_tot[lane] = tv;
   }
   __syncthreads();
-  const uint16_t* xr = x + (size_t)__ldg(row_token + p) * M;
-  uint16_t* orow = xsend + (size_t)dst_row * M;
+  const int incl = v + (w > 0 ? warp_tot[w - 1] : 0);
+  *total = warp_tot[(blockDim.x >> 5) - 1];
+  __syncthreads();
+  return incl - f;
+}
+
+// Single block. idx [T x k] (global experts); the plan (plan_segs over the E
+// global experts, row_token / row_weight sorted by expert then token) comes
+// from the dispatch plan of the same routing. slot[t * world + q] = row of
+// token t in block q, or -1.
+__global__ void __launch_bounds__(1024) ep_dispatch_kernel(
+    const int* __restrict__ idx, const WispSegment* __restrict__ plan_segs,
+    const int* __restrict__ row_token, const float* __restrict__ row_weight, int T, int k, int E,
+    int world, Layout L, uint8_t* __restrict__ send, int* __restrict__ slot) {
+  __shared__ int warp_tot[32];
+  const int e_loc = E / world;
+  for (int q = 0; q < world; q++) {
+    int carry = 0;
+    for (int base = 0; base < T; base += blockDim.x) {
+      const int t = base + threadIdx.x;
+      int f = 0;
+      if (t < T)
+        for (int j = 0; j < k; j++) {
+          const int e = __ldg(idx + (size_t)t * k + j);
+          if (e >= 0 && e < E && e / e_loc == q) f = 1;
+        }
+      int tot;
+      const int ex = block_scan(f, warp_tot, &tot);
+      if (t < T) slot[(size_t)t * world + q] = f ? carry + ex : -1;
+      carry += tot;
+    }
+    if (threadIdx.x == 0) reinterpret_cast<int*>(send + q * L.bytes)[0] = carry;
+  }
+  for (int g = threadIdx.x; g < E; g += blockDim.x) {
+    const int q = g / e_loc;
+    reinterpret_cast<int*>(send + q * L.bytes + 16)[g - q * e_loc] = __ldg(&plan_segs[g].rows);
+  }
+  __syncthreads();  // the slots above are read back below
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int g = warp; g < E; g += blockDim.x >> 5) {
+    const int q = g / e_loc;
+    const int first = __ldg(&plan_segs[q * e_loc].row_begin);  // q's first plan row
+    const int b = __ldg(&plan_segs[g].row_begin), r = __ldg(&plan_segs[g].rows);
+    int* ent = reinterpret_cast<int*>(send + q * L.bytes + L.off_ent);
+    float* ew = reinterpret_cast<float*>(send + q * L.bytes + L.off_w);
+    for (int i = lane; i < r; i += 32) {
+      const int p = b + i;
+      ent[p - first] = slot[(size_t)__ldg(row_token + p) * world + q];
+      ew[p - first] = __ldg(row_weight + p);
+    }
+  }
+}
+
+// One block per token: its bf16 row, converted once, into each block that
+// holds it.
+__global__ void ep_pack_kernel(const uint16_t* __restrict__ x, int M, const int* __restrict__ slot,
+                               int world, Layout L, uint8_t* __restrict__ send) {
+  __shared__ int sl[kMaxWorld];
+  const int t = blockIdx.x;
+  if (threadIdx.x < world) sl[threadIdx.x] = slot[(size_t)t * world + threadIdx.x];
+  __syncthreads();
+  const uint16_t* xr = x + (size_t)t * M;
   for (int k8 = threadIdx.x * 8; k8 < M; k8 += blockDim.x * 8) {
     const uint4 v = __ldg(reinterpret_cast<const uint4*>(xr + k8));
     const uint32_t a[4] = {v.x, v.y, v.z, v.w};
@@ -69,37 +157,49 @@ __global__ void ep_send_pack_kernel(const uint16_t* __restrict__ x, int M,
       f[2 * j + 1] = bf16_bits_to_f32(a[j] >> 16);
     }
     // logical slot j holds physical offset {0,4,1,5,2,6,3,7}[j]
-    const __half2 h0 = __floats2half2_rn(f[0], f[4]);
-    const __half2 h1 = __floats2half2_rn(f[1], f[5]);
-    const __half2 h2 = __floats2half2_rn(f[2], f[6]);
-    const __half2 h3 = __floats2half2_rn(f[3], f[7]);
-    *reinterpret_cast<uint4*>(orow + k8) = make_uint4(h22u(h0), h22u(h1), h22u(h2), h22u(h3));
+    const uint4 o = make_uint4(h22u(__floats2half2_rn(f[0], f[4])), h22u(__floats2half2_rn(f[1], f[5])),
+                               h22u(__floats2half2_rn(f[2], f[6])), h22u(__floats2half2_rn(f[3], f[7])));
+    for (int q = 0; q < world; q++) {
+      const int s = sl[q];
+      if (s >= 0)
+        *reinterpret_cast<uint4*>(send + q * L.bytes + L.off_rows + ((size_t)s * M + k8) * 2) = o;
+    }
   }
 }
 
-// Single block. rc[s][e] = rows source s sends for local expert e (s <
-// world, e < e_loc, world * e_loc <= 1024). Gathered order: expert-major,
-// then source, then the source's own order.
-__global__ void __launch_bounds__(1024) ep_recv_plan_kernel(const int* __restrict__ rc, int world,
-                                                            int e_loc, int cap,
+// Single block. Gathered order: local expert, then source rank, then the
+// source's entry order. src_pos[j] = receive row (s * cap + block row) of
+// gathered row j, weight[j] its routing weight; counts and rows are clamped
+// to the block's capacity.
+__global__ void __launch_bounds__(1024) ep_recv_plan_kernel(const uint8_t* __restrict__ recv,
+                                                            int world, int e_loc, int k, Layout L,
                                                             WispSegment* __restrict__ segs,
                                                             int* __restrict__ src_pos,
+                                                            float* __restrict__ weight,
                                                             int* __restrict__ total_out) {
-  __shared__ int src_off[1024];  // [s][e]: receive position of the chunk
+  __shared__ int src_off[1024];  // [s][e]: first entry of the chunk in block s
   __shared__ int dst_off[1024];  // [s][e]: gathered position of the chunk
   __shared__ int cnt[1024];
   const int n = world * e_loc;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) cnt[i] = __ldg(rc + i);
+  const int max_ent = L.cap * k;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int s = i / e_loc, e = i - s * e_loc;
+    const int c = reinterpret_cast<const int*>(recv + s * L.bytes + 16)[e];
+    cnt[i] = min(max(c, 0), max_ent);
+  }
   __syncthreads();
   if (threadIdx.x < world) {  // prefix over the experts of one source
     const int s = threadIdx.x;
-    int off = s * cap;
+    int off = 0;
     for (int e = 0; e < e_loc; e++) {
+      const int c = min(cnt[s * e_loc + e], max_ent - off);
+      cnt[s * e_loc + e] = c;
       src_off[s * e_loc + e] = off;
-      off += cnt[s * e_loc + e];
+      off += c;
     }
   }
-  if (threadIdx.x == 32) {  // gathered order (another warp than the above)
+  __syncthreads();
+  if (threadIdx.x == 0) {  // gathered order
     int off = 0;
     for (int e = 0; e < e_loc; e++) {
       WispSegment sg;
@@ -116,123 +216,136 @@ __global__ void __launch_bounds__(1024) ep_recv_plan_kernel(const int* __restric
     *total_out = off;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < n; i += blockDim.x)
-    for (int j = 0; j < cnt[i]; j++) src_pos[dst_off[i] + j] = src_off[i] + j;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int s = i / e_loc;
+    const int* ent = reinterpret_cast<const int*>(recv + s * L.bytes + L.off_ent);
+    const float* ew = reinterpret_cast<const float*>(recv + s * L.bytes + L.off_w);
+    for (int j = 0; j < cnt[i]; j++) {
+      const int row = ent[src_off[i] + j];
+      src_pos[dst_off[i] + j] = s * L.cap + min(max(row, 0), L.cap - 1);
+      weight[dst_off[i] + j] = ew[src_off[i] + j];
+    }
+  }
 }
 
-// One block per gathered row j < *total: GATHER copies fp16 row src_pos[j]
-// of `a` to row j of `b`; otherwise fp32 row j of `b` goes back to row
-// src_pos[j] of `a`.
-template <bool GATHER>
-__global__ void ep_move_rows_kernel(void* __restrict__ a, void* __restrict__ b,
-                                    const int* __restrict__ src_pos,
-                                    const int* __restrict__ total, int row_bytes) {
+// One block per gathered row j < *total: sorted[j] = receive row src_pos[j].
+__global__ void ep_gather_kernel(const uint8_t* __restrict__ recv, Layout L, int M,
+                                 const int* __restrict__ src_pos, const int* __restrict__ total,
+                                 uint16_t* __restrict__ sorted) {
   const int j = blockIdx.x;
   if (j >= __ldg(total)) return;
-  const size_t r = (size_t)__ldg(src_pos + j);
-  const uint4* src = reinterpret_cast<const uint4*>(
-      GATHER ? static_cast<const uint8_t*>(a) + r * row_bytes
-             : static_cast<const uint8_t*>(b) + (size_t)j * row_bytes);
-  uint4* dst = reinterpret_cast<uint4*>(GATHER ? static_cast<uint8_t*>(b) + (size_t)j * row_bytes
-                                               : static_cast<uint8_t*>(a) + r * row_bytes);
-  for (int i = threadIdx.x; i < row_bytes / 16; i += blockDim.x) dst[i] = __ldg(src + i);
+  const int r = __ldg(src_pos + j);
+  const int s = r / L.cap, row = r - s * L.cap;
+  const uint4* src = reinterpret_cast<const uint4*>(recv + s * L.bytes + L.off_rows + (size_t)row * M * 2);
+  uint4* dst = reinterpret_cast<uint4*>(sorted + (size_t)j * M);
+  for (int i = threadIdx.x; i < M / 8; i += blockDim.x) dst[i] = __ldg(src + i);
 }
 
+// One block per token: out[t] += yback[q * cap + slot[t][q]] for q = 0..world-1.
 __global__ void ep_combine_kernel(const float* __restrict__ y, const int* __restrict__ slot,
-                                  const int* __restrict__ row_token,
-                                  const float* __restrict__ row_weight, int M,
-                                  float* __restrict__ out) {
-  const int p = blockIdx.x;
-  const float w = __ldg(row_weight + p);
-  const float* yr = y + (size_t)__ldg(slot + p) * M;
-  float* orow = out + (size_t)__ldg(row_token + p) * M;
+                                  int world, int cap, int M, float* __restrict__ out) {
+  __shared__ int sl[kMaxWorld];
+  const int t = blockIdx.x;
+  if (threadIdx.x < world) sl[threadIdx.x] = slot[(size_t)t * world + threadIdx.x];
+  __syncthreads();
+  float* orow = out + (size_t)t * M;
   for (int i = threadIdx.x * 4; i < M; i += blockDim.x * 4) {
-    const float4 v = __ldg(reinterpret_cast<const float4*>(yr + i));
-    red_add_f32(orow + i, w * v.x);
-    red_add_f32(orow + i + 1, w * v.y);
-    red_add_f32(orow + i + 2, w * v.z);
-    red_add_f32(orow + i + 3, w * v.w);
+    float4 acc = *reinterpret_cast<const float4*>(orow + i);
+    for (int q = 0; q < world; q++) {
+      if (sl[q] < 0) continue;
+      const float4 v = __ldg(reinterpret_cast<const float4*>(y + ((size_t)q * cap + sl[q]) * M + i));
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    *reinterpret_cast<float4*>(orow + i) = acc;
   }
+}
+
+bool bad_shape(int world, int e_loc, int cap, int top_k, int hidden) {
+  return world < 1 || world > kMaxWorld || e_loc < 1 || world * e_loc > 1024 || cap < 1 ||
+         top_k < 1 || top_k > 32 || hidden < 8 || hidden % 8;
 }
 
 }  // namespace
 
-extern "C" WispError wisp_b200_ep_send_pack(const uint16_t* d_x, int hidden, const int* d_row_token,
-                                            const WispSegment* d_plan_segs, int n_experts,
-                                            int n_rows, int world, int cap, uint16_t* d_xsend,
-                                            int* d_slot, cudaStream_t stream, WispErrCtx* err) {
-  if (!d_x || !d_row_token || !d_plan_segs || !d_xsend || !d_slot)
-    return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_send_pack: null pointer argument");
-  if (world < 1 || world > kMaxWorld || n_experts % world || hidden % 8 || n_rows < 0 ||
-      n_rows > cap)
+extern "C" size_t wisp_b200_ep_block_bytes(int hidden, int e_loc, int cap, int top_k) {
+  if (bad_shape(1, e_loc, cap, top_k, hidden)) return 0;
+  return ep_layout(hidden, e_loc, cap, top_k, 2).bytes;
+}
+
+extern "C" WispError wisp_b200_ep_dispatch(const uint16_t* d_x, int tokens, int hidden,
+                                           const int* d_topk_idx, int top_k,
+                                           const WispSegment* d_plan_segs, const int* d_row_token,
+                                           const float* d_row_weight, int n_experts, int world,
+                                           int cap, uint8_t* d_send, int* d_slot,
+                                           cudaStream_t stream, WispErrCtx* err) {
+  if (!d_x || !d_topk_idx || !d_plan_segs || !d_row_token || !d_row_weight || !d_send || !d_slot)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_dispatch: null pointer argument");
+  if (world < 1 || n_experts % world || bad_shape(world, n_experts / world, cap, top_k, hidden) ||
+      tokens < 0 || tokens > cap)
     return WB_FAIL(WISP_ERR_INVALID_ARG,
-                   "ep_send_pack: world=%d experts=%d hidden=%d rows=%d cap=%d", world,
-                   n_experts, hidden, n_rows, cap);
-  if (((uintptr_t)d_x | (uintptr_t)d_xsend) & 15)
-    return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_send_pack: row buffers must be 16-byte aligned");
-  if (n_rows == 0) return WISP_OK;
-  wb::launch_k(ep_send_pack_kernel, n_rows, 128, 0, stream, d_x, hidden, d_row_token,
-               d_plan_segs, n_experts / world, n_rows, world, cap, d_xsend, d_slot);
+                   "ep_dispatch: world=%d experts=%d hidden=%d tokens=%d cap=%d top_k=%d", world,
+                   n_experts, hidden, tokens, cap, top_k);
+  if (((uintptr_t)d_x | (uintptr_t)d_send) & 15)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_dispatch: x and the send buffer must be 16-byte aligned");
+  const Layout L = ep_layout(hidden, n_experts / world, cap, top_k, 2);
+  wb::launch_k(ep_dispatch_kernel, 1, 1024, 0, stream, d_topk_idx, d_plan_segs, d_row_token,
+               d_row_weight, tokens, top_k, n_experts, world, L, d_send, d_slot);
+  if (tokens > 0)
+    wb::launch_k(ep_pack_kernel, tokens, 128, 0, stream, d_x, hidden, d_slot, world, L, d_send);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
 
-extern "C" WispError wisp_b200_ep_recv_plan(const int* d_recv_counts, int world, int e_loc,
-                                            int cap, WispSegment* d_segs, int* d_src_pos,
-                                            int* d_total, cudaStream_t stream, WispErrCtx* err) {
-  if (!d_recv_counts || !d_segs || !d_src_pos || !d_total)
+extern "C" WispError wisp_b200_ep_recv_plan(const uint8_t* d_recv, int world, int e_loc, int cap,
+                                            int top_k, int hidden, WispSegment* d_segs,
+                                            int* d_src_pos, float* d_weight, int* d_total,
+                                            cudaStream_t stream, WispErrCtx* err) {
+  if (!d_recv || !d_segs || !d_src_pos || !d_weight || !d_total)
     return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_recv_plan: null pointer argument");
-  if (world < 1 || world > kMaxWorld || e_loc < 1 || world * e_loc > 1024 || cap < 0)
-    return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_recv_plan: world=%d e_loc=%d cap=%d (world*e_loc <= 1024)",
-                   world, e_loc, cap);
-  wb::launch_k(ep_recv_plan_kernel, 1, 1024, 0, stream, d_recv_counts, world, e_loc, cap, d_segs,
-               d_src_pos, d_total);
+  if (bad_shape(world, e_loc, cap, top_k, hidden))
+    return WB_FAIL(WISP_ERR_INVALID_ARG,
+                   "ep_recv_plan: world=%d e_loc=%d cap=%d top_k=%d hidden=%d (world*e_loc <= 1024)",
+                   world, e_loc, cap, top_k, hidden);
+  const Layout L = ep_layout(hidden, e_loc, cap, top_k, 2);
+  wb::launch_k(ep_recv_plan_kernel, 1, 1024, 0, stream, d_recv, world, e_loc, top_k, L, d_segs,
+               d_src_pos, d_weight, d_total);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
 
-extern "C" WispError wisp_b200_ep_gather_rows(const uint16_t* d_recv, const int* d_src_pos,
-                                             const int* d_total, int max_rows, int hidden,
-                                             uint16_t* d_sorted, cudaStream_t stream,
-                                             WispErrCtx* err) {
+extern "C" WispError wisp_b200_ep_gather_rows(const uint8_t* d_recv, int world, int e_loc, int cap,
+                                             int top_k, int hidden, const int* d_src_pos,
+                                             const int* d_total, int max_rows, uint16_t* d_sorted,
+                                             cudaStream_t stream, WispErrCtx* err) {
   if (!d_recv || !d_src_pos || !d_total || !d_sorted)
     return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_gather_rows: null pointer argument");
-  if (hidden % 8 || max_rows < 0 || (((uintptr_t)d_recv | (uintptr_t)d_sorted) & 15))
-    return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_gather_rows: hidden=%d (rows 16-byte aligned)", hidden);
+  if (bad_shape(world, e_loc, cap, top_k, hidden) || max_rows < 0 ||
+      (((uintptr_t)d_recv | (uintptr_t)d_sorted) & 15))
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_gather_rows: hidden=%d max_rows=%d (16-byte aligned rows)",
+                   hidden, max_rows);
   if (max_rows == 0) return WISP_OK;
-  wb::launch_k(ep_move_rows_kernel<true>, max_rows, 128, 0, stream,
-               const_cast<uint16_t*>(d_recv), d_sorted, d_src_pos, d_total, hidden * 2);
+  const Layout L = ep_layout(hidden, e_loc, cap, top_k, 2);
+  wb::launch_k(ep_gather_kernel, max_rows, 128, 0, stream, d_recv, L, hidden, d_src_pos, d_total,
+               d_sorted);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
 
-extern "C" WispError wisp_b200_ep_scatter_rows(const float* d_sorted, const int* d_src_pos,
-                                              const int* d_total, int max_rows, int hidden,
-                                              float* d_recv, cudaStream_t stream,
-                                              WispErrCtx* err) {
-  if (!d_sorted || !d_src_pos || !d_total || !d_recv)
-    return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_scatter_rows: null pointer argument");
-  if (hidden % 4 || max_rows < 0 || (((uintptr_t)d_recv | (uintptr_t)d_sorted) & 15))
-    return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_scatter_rows: hidden=%d (rows 16-byte aligned)", hidden);
-  if (max_rows == 0) return WISP_OK;
-  wb::launch_k(ep_move_rows_kernel<false>, max_rows, 256, 0, stream, d_recv,
-               const_cast<float*>(d_sorted), d_src_pos, d_total, hidden * 4);
-  WB_CUDA_CHECK(cudaGetLastError());
-  return WISP_OK;
-}
-
-extern "C" WispError wisp_b200_ep_combine(const float* d_y, const int* d_slot,
-                                         const int* d_row_token, const float* d_row_weight,
-                                         int n_rows, int hidden, float* d_out, cudaStream_t stream,
-                                         WispErrCtx* err) {
-  if (!d_y || !d_slot || !d_row_token || !d_row_weight || !d_out)
+extern "C" WispError wisp_b200_ep_combine(const float* d_yback, const int* d_slot, int tokens,
+                                         int world, int cap, int hidden, float* d_out,
+                                         cudaStream_t stream, WispErrCtx* err) {
+  if (!d_yback || !d_slot || !d_out)
     return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_combine: null pointer argument");
-  if (hidden % 4 || n_rows < 0 || ((uintptr_t)d_y & 15))
-    return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_combine: hidden=%d rows=%d (y 16-byte aligned)",
-                   hidden, n_rows);
-  if (n_rows == 0) return WISP_OK;
-  wb::launch_k(ep_combine_kernel, n_rows, 256, 0, stream, d_y, d_slot, d_row_token, d_row_weight,
-               hidden, d_out);
+  if (world < 1 || world > kMaxWorld || cap < 1 || tokens < 0 || tokens > cap || hidden % 4 ||
+      (((uintptr_t)d_yback | (uintptr_t)d_out) & 15))
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_combine: world=%d tokens=%d cap=%d hidden=%d", world,
+                   tokens, cap, hidden);
+  if (tokens == 0) return WISP_OK;
+  wb::launch_k(ep_combine_kernel, tokens, 256, 0, stream, d_yback, d_slot, world, cap, hidden,
+               d_out);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }

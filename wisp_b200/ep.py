@@ -11,16 +11,16 @@ equal the single-GPU path's. Layout:
 
 One layer on rank r, with every count kept on the device (no host round
 trip between routing and the expert FFN):
-  route own tokens -> plan (rows grouped by expert, hence by owner rank)
-  -> pack rows (fp16) into a send buffer of `world` fixed blocks of `cap`
-  rows -> exchange per-expert row counts and the row blocks (all_to_all,
-  equal splits), meanwhile the shared expert on own tokens (mode 0) -> gather
-  the received rows expert-contiguous (one segment per local expert, as on
-  one GPU) -> grouped FFN (mode 1: unweighted fp32 rows) -> scatter the
-  results into the source blocks -> return the row blocks (all_to_all) ->
-  weighted combine of the returned rows.
-cap = tokens * top_k, the most rows one rank can send to one destination;
-the padding rows are exchanged but never computed or read.
+  route own tokens -> plan (rows grouped by expert) -> one fixed-size block
+  per destination rank: a token's row once per destination that owns any of
+  its experts, plus the (row, weight) entries of its experts there
+  (wisp_b200_ep_dispatch) -> all_to_all of the blocks, meanwhile the shared
+  expert on own tokens -> gather the received rows expert-contiguous (one
+  segment per local expert, as on one GPU) -> grouped FFN in mode 0 with the
+  routing weights, into one fp32 row per received token -> all_to_all of
+  those rows back -> each token adds its rows from the owners, in rank order.
+cap = the most tokens any rank holds (a token fills at most one row of a
+block); padding rows are exchanged but never computed or read.
 
 Collectives go through torch.distributed (NCCL between GPUs); every rank
 issues the same collectives in the same order. The compute steps go through
@@ -44,26 +44,44 @@ def block_range(n: int, world: int, rank: int) -> tuple[int, int]:
     return n * rank // world, n * (rank + 1) // world
 
 
-def send_splits(counts: np.ndarray, n_experts: int, world: int) -> list[int]:
-    """Rows this rank sends to each destination (its rows are sorted by expert)."""
-    return [int(counts[slice(*block_range(n_experts, world, q))].sum()) for q in range(world)]
+class BlockLayout:
+    """Byte layout of one exchange block (mirrors ep.cu; elem = bytes per
+    row element: 2 for the fp16 rows of the CUDA path)."""
+
+    def __init__(self, hidden: int, e_loc: int, cap: int, top_k: int, elem: int = 2):
+        a16 = lambda v: (v + 15) & ~15  # noqa: E731
+        self.cap, self.k, self.e_loc, self.hidden, self.elem = cap, top_k, e_loc, hidden, elem
+        self.off_cnt = 16
+        self.off_ent = a16(16 + 4 * e_loc)
+        self.off_w = self.off_ent + 4 * cap * top_k
+        self.off_rows = a16(self.off_w + 4 * cap * top_k)
+        self.bytes = a16(self.off_rows + cap * hidden * elem)
 
 
-def recv_layout(recv_counts: np.ndarray) -> tuple[list[tuple[int, int, int]], list[int]]:
-    """recv_counts[s, e]: rows source s sends for local expert e. The receive
-    buffer holds source blocks in rank order, each sorted by expert. Returns
-    segments (local_expert, row_begin, rows) ordered expert-major (so tiles
-    of one expert are adjacent and share its weights in L2) and the per-source
-    row counts."""
-    world, e_loc = recv_counts.shape
-    per_src = recv_counts.sum(axis=1)
-    base = np.concatenate([[0], np.cumsum(per_src)[:-1]])
-    inner = np.concatenate([np.zeros((world, 1), np.int64), np.cumsum(recv_counts, axis=1)[:, :-1]], axis=1)
-    segs = []
-    for e in range(e_loc):
-        for s in range(world):
-            segs.append((e, int(base[s] + inner[s, e]), int(recv_counts[s, e])))
-    return segs, [int(v) for v in per_src]
+def dispatch_reference(idx: np.ndarray, n_experts: int, world: int):
+    """Host statement of the dispatch layout: slot[t, q] (row of token t in
+    the block for rank q, tokens in order, -1 if none of t's experts is on
+    q) and, per destination, the entries (row, k-index) expert-major then
+    token-ascending."""
+    T, k = idx.shape
+    e_loc = n_experts // world
+    slot = -np.ones((T, world), np.int64)
+    for q in range(world):
+        n = 0
+        for t in range(T):
+            if any(int(e) // e_loc == q for e in idx[t]):
+                slot[t, q] = n
+                n += 1
+    entries = []
+    for q in range(world):
+        ent = []
+        for e in range(q * e_loc, (q + 1) * e_loc):
+            for t in range(T):
+                for j in range(k):
+                    if int(idx[t, j]) == e:
+                        ent.append((int(slot[t, q]), t, j))
+        entries.append(ent)
+    return slot, entries
 
 
 def _stream() -> int:
@@ -108,22 +126,18 @@ class CudaOps:
         abi.call("wisp_b200_combine_rows", y.data_ptr(), row_token.data_ptr(), row_weight.data_ptr(),
                  n_rows, out.shape[1], out.data_ptr(), _stream())
 
-    def send_pack(self, x, row_token, plan_segs, n_experts, n_rows, world, cap, xsend, slot):
-        abi.call("wisp_b200_ep_send_pack", x.data_ptr(), x.shape[1], row_token.data_ptr(),
-                 plan_segs.data_ptr(), n_experts, n_rows, world, cap, xsend.data_ptr(),
-                 slot.data_ptr(), _stream())
+    def dispatch(self, x, idx, plan_segs, row_token, row_weight, n_experts, world, cap, send, slot):
+        abi.call("wisp_b200_ep_dispatch", x.data_ptr(), x.shape[0], x.shape[1], idx.data_ptr(),
+                 idx.shape[1], plan_segs.data_ptr(), row_token.data_ptr(), row_weight.data_ptr(),
+                 n_experts, world, cap, send.data_ptr(), slot.data_ptr(), _stream())
 
-    def recv_plan(self, recv_counts, world, e_loc, cap, segs, src_pos, total):
-        abi.call("wisp_b200_ep_recv_plan", recv_counts.data_ptr(), world, e_loc, cap,
-                 segs.data_ptr(), src_pos.data_ptr(), total.data_ptr(), _stream())
+    def recv_plan(self, recv, world, e_loc, cap, k, hidden, segs, src_pos, weight, total):
+        abi.call("wisp_b200_ep_recv_plan", recv.data_ptr(), world, e_loc, cap, k, hidden,
+                 segs.data_ptr(), src_pos.data_ptr(), weight.data_ptr(), total.data_ptr(), _stream())
 
-    def gather_rows(self, recv, src_pos, total, max_rows, sorted_rows):
-        abi.call("wisp_b200_ep_gather_rows", recv.data_ptr(), src_pos.data_ptr(), total.data_ptr(),
-                 max_rows, recv.shape[1], sorted_rows.data_ptr(), _stream())
-
-    def scatter_rows(self, sorted_rows, src_pos, total, max_rows, recv):
-        abi.call("wisp_b200_ep_scatter_rows", sorted_rows.data_ptr(), src_pos.data_ptr(),
-                 total.data_ptr(), max_rows, recv.shape[1], recv.data_ptr(), _stream())
+    def gather_rows(self, recv, world, e_loc, cap, k, hidden, src_pos, total, max_rows, sorted_rows):
+        abi.call("wisp_b200_ep_gather_rows", recv.data_ptr(), world, e_loc, cap, k, hidden,
+                 src_pos.data_ptr(), total.data_ptr(), max_rows, sorted_rows.data_ptr(), _stream())
 
     def grouped_dev(self, cfg, lw, segs, n_segs, rows, xp, h, mode, row_token, row_weight, out,
                     tiles, flag):
@@ -133,9 +147,14 @@ class CudaOps:
                  None if row_weight is None else row_weight.data_ptr(), out.data_ptr(),
                  tiles.data_ptr(), flag.data_ptr(), _stream())
 
-    def ep_combine(self, y, slot, row_token, row_weight, n_rows, out):
-        abi.call("wisp_b200_ep_combine", y.data_ptr(), slot.data_ptr(), row_token.data_ptr(),
-                 row_weight.data_ptr(), n_rows, out.shape[1], out.data_ptr(), _stream())
+    def ep_combine(self, yback, slot, tokens, world, cap, out):
+        abi.call("wisp_b200_ep_combine", yback.data_ptr(), slot.data_ptr(), tokens, world, cap,
+                 out.shape[1], out.data_ptr(), _stream())
+
+    def block_layout(self, hidden, e_loc, cap, k):
+        lay = BlockLayout(hidden, e_loc, cap, k, 2)
+        assert lay.bytes == abi.lib().wisp_b200_ep_block_bytes(hidden, e_loc, cap, k)
+        return lay
 
     def act_dtype(self):
         return torch.float16
@@ -180,25 +199,27 @@ class EpLayer:
         self.row_token = torch.empty(T * k, dtype=torch.int32, device=dev)
         self.row_weight = torch.empty(T * k, dtype=torch.float32, device=dev)
         self.flag = torch.zeros(1, dtype=torch.int32, device=dev)
-        # Exchange blocks: `cap` rows per rank pair (all of a rank's rows may
-        # go to one owner), the same on every rank.
+        # Exchange blocks: one per rank pair, `cap` token rows each (a token
+        # fills at most one row of a block), the same on every rank.
         if max_tokens is None:
             t = torch.tensor([T], dtype=torch.int64, device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
             max_tokens = int(t.item())
-        self.cap = max_tokens * k
-        R = self.cap * world
-        self.slot = torch.empty(T * k, dtype=torch.int32, device=dev)
-        self.xsend = torch.empty((R, M), dtype=adt, device=dev)
-        self.xrecv = torch.empty((R, M), dtype=adt, device=dev)
-        self.hr = torch.empty((max(R, T), I), dtype=adt, device=dev)
-        self.yr = torch.empty((R, M), dtype=torch.float32, device=dev)
-        self.yback = torch.empty((R, M), dtype=torch.float32, device=dev)
-        self.xsorted = torch.empty((R, M), dtype=adt, device=dev)
-        self.ysorted = torch.empty((R, M), dtype=torch.float32, device=dev)
-        self.src_pos = torch.empty(R, dtype=torch.int32, device=dev)
+        self.cap = max(1, max_tokens)
+        self.layout = self.ops.block_layout(M, self.e_loc, self.cap, k)
+        nb = self.layout.bytes
+        RK = world * self.cap * k          # most (token, local expert) rows received
+        self.rk = RK
+        self.slot = torch.empty((T, world), dtype=torch.int32, device=dev)
+        self.send = torch.zeros(world * nb, dtype=torch.uint8, device=dev)
+        self.recv = torch.zeros(world * nb, dtype=torch.uint8, device=dev)
+        self.xsorted = torch.empty((RK, M), dtype=adt, device=dev)
+        self.hr = torch.empty((max(RK, T), I), dtype=adt, device=dev)
+        self.yr = torch.empty((world * self.cap, M), dtype=torch.float32, device=dev)
+        self.yback = torch.empty((world * self.cap, M), dtype=torch.float32, device=dev)
+        self.src_pos = torch.empty(RK, dtype=torch.int32, device=dev)
+        self.gw = torch.empty(RK, dtype=torch.float32, device=dev)
         self.total = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.cnt_recv = torch.empty(self.e_loc * world, dtype=torch.int32, device=dev)
         self.n_rsegs = self.e_loc
         self.rsegs = torch.empty(16 * self.n_rsegs, dtype=torch.uint8, device=dev)
         self.tiles = torch.empty(abi.lib().wisp_b200_tiles_words(self.n_rsegs + 1)
@@ -215,34 +236,32 @@ class EpLayer:
     def forward(self, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         """x: bf16 [T, M] (this rank's tokens) -> out fp32 [T, M]."""
         spec, ops, T, k, world = self.spec, self.ops, self.T, self.spec.top_k, self.world
+        M = spec.hidden
         ops.route(self.cfg_route, self.lw, x, self.idx, self.w, self.logits)
         ops.plan(self.cfg_route, self.idx, self.w, self.counts, self.segs, self.row_token,
                  self.row_weight)
-        ops.send_pack(x, self.row_token, self.segs, spec.n_experts, T * k, world, self.cap,
-                      self.xsend, self.slot)
-        # 1. per-expert row counts to the owners, then the row blocks; the
-        #    shared expert runs on this rank's own tokens while they travel
-        w_cnt = dist.all_to_all_single(self.cnt_recv, self.counts, group=self.group,
-                                       async_op=True)
-        w_rows = dist.all_to_all_single(self.xrecv, self.xsend, group=self.group, async_op=True)
+        ops.dispatch(x, self.idx, self.segs, self.row_token, self.row_weight, spec.n_experts,
+                     world, self.cap, self.send, self.slot)
+        # 1. the blocks to the owners; the shared expert runs on this rank's
+        #    own tokens while they travel
+        w_rows = dist.all_to_all_single(self.recv, self.send, group=self.group, async_op=True)
         out.zero_()
         if spec.has_shared:
             ops.pack(x, None, T, self.xs)
             ops.grouped_dev(self.cfg_loc, self.lw, self.sh_seg, 1, T, self.xs, self.hr, 0,
                             self.sh_token, self.sh_weight, out, self.tiles, self.flag)
-        w_cnt.wait()
         w_rows.wait()
         # 2. local experts over the received rows, gathered so that each
-        #    expert is one segment (unweighted fp32 rows), then scattered
-        #    back into the source blocks
-        R = self.cap * world
-        ops.recv_plan(self.cnt_recv, world, self.e_loc, self.cap, self.rsegs, self.src_pos,
-                      self.total)
-        ops.gather_rows(self.xrecv, self.src_pos, self.total, R, self.xsorted)
-        ops.grouped_dev(self.cfg_loc, self.lw, self.rsegs, self.n_rsegs, R, self.xsorted,
-                        self.hr, 1, None, None, self.ysorted, self.tiles, self.flag)
-        ops.scatter_rows(self.ysorted, self.src_pos, self.total, R, self.yr)
-        # 3. rows back to their tokens' ranks, then the weighted combine
+        #    expert is one segment; the FFN adds w * y of every local expert
+        #    of a received token into that token's fp32 row
+        ops.recv_plan(self.recv, world, self.e_loc, self.cap, k, M, self.rsegs, self.src_pos,
+                      self.gw, self.total)
+        ops.gather_rows(self.recv, world, self.e_loc, self.cap, k, M, self.src_pos, self.total,
+                        self.rk, self.xsorted)
+        self.yr.zero_()
+        ops.grouped_dev(self.cfg_loc, self.lw, self.rsegs, self.n_rsegs, self.rk, self.xsorted,
+                        self.hr, 0, self.src_pos, self.gw, self.yr, self.tiles, self.flag)
+        # 3. the rows back to their tokens' ranks, added in rank order
         dist.all_to_all_single(self.yback, self.yr, group=self.group)
-        ops.ep_combine(self.yback, self.slot, self.row_token, self.row_weight, T * k, out)
+        ops.ep_combine(self.yback, self.slot, T, world, self.cap, out)
         return out
