@@ -203,16 +203,17 @@ def test_dispatch_layout():
             abi.lib().wisp_b200_ep_block_bytes(hidden, e_loc, cap, k)
 
 
-@pytest.mark.parametrize("spec", [SPEC, synth.small(SPEC, skew=True, seed=4, tokens=7)])
-def test_ep_two_ranks_matches_single_process(orc, spec):
+@pytest.mark.parametrize("world,spec", [(2, SPEC), (2, synth.small(SPEC, skew=True, seed=4, tokens=7)),
+                                        (4, synth.small(SPEC, seed=9, tokens=11))])
+def test_ep_ranks_match_single_process(orc, world, spec):
     from helpers import oracle_outputs, oracle_route
     port = _free_port()
     with tempfile.TemporaryDirectory() as td:
-        mp.start_processes(_worker, args=(2, port, td, spec, "ok"), nprocs=2, join=True,
+        mp.start_processes(_worker, args=(world, port, td, spec, "ok"), nprocs=world, join=True,
                            start_method="spawn")
-        for r in range(2):
+        for r in range(world):
             assert not os.path.exists(os.path.join(td, f"err{r}.txt")), open(os.path.join(td, f"err{r}.txt")).read()
-        got = np.concatenate([np.load(os.path.join(td, f"out{r}.npy")) for r in range(2)])
+        got = np.concatenate([np.load(os.path.join(td, f"out{r}.npy")) for r in range(world)])
     layers, x = synth.make_model(spec, "cpu")
     lw = layers[0]
     idx, w, _ = oracle_route(orc, lw, x)
