@@ -7,7 +7,10 @@ error 1e-3, both normalised by the reference output's magnitude:
     mean|got - ref| / mean|ref| <= 1e-3
 A token whose oracle routing margin (gap between the k-th pick and the best
 non-pick, fp64) is below NEAR_TIE is a near-tie: fp32 summation order may
-legitimately flip it, so its indices are reported, not asserted.
+legitimately flip it, so its indices are reported, not asserted. Routing
+weights agree within ROUTE_W_RTOL: the batched router sums bf16 products on
+the tensor cores with fp32 accumulation, whose logits differ from fp64 by
+~1e-5 relative (the weights of a softmax follow the logit differences).
 """
 from __future__ import annotations
 
@@ -17,7 +20,8 @@ import torch
 MAX_REL = 1e-2
 MEAN_REL = 1e-3
 NEAR_TIE = 1e-4           # softmax routing: margin in logit units
-NEAR_TIE_SIGMOID = 1e-5   # sigmoid routing: margin in score units (fp32 error ~1e-7)
+NEAR_TIE_SIGMOID = 5e-5   # sigmoid routing: margin in score units (tensor-core logits: ~1e-5)
+ROUTE_W_RTOL = 1e-4
 
 
 def bf16_to_f64(x: torch.Tensor) -> np.ndarray:
@@ -53,7 +57,7 @@ def oracle_route(orc, lw, x: torch.Tensor):
                     spec.topk_groups, spec.routed_scaling)
 
 
-def check_routing(idx_gpu, w_gpu, idx_ref, w_ref, margin, scoring_w_tol=1e-5, near_tie=NEAR_TIE):
+def check_routing(idx_gpu, w_gpu, idx_ref, w_ref, margin, scoring_w_tol=ROUTE_W_RTOL, near_tie=NEAR_TIE):
     """Indices exact except near-ties; weights close where indices agree.
     Returns the list of near-tie tokens."""
     idx_gpu = np.asarray(idx_gpu)

@@ -4,6 +4,11 @@
 //                         Tiled 64x64 with a deterministic split-K so small
 //                         token counts still fill the GPU (partials are
 //                         summed in a fixed order by the top-k kernel).
+//   router_mma_kernel     the same with a bf16 router weight on the tensor
+//                         cores (mma.sync m16n8k16 bf16, fp32 accumulate):
+//                         64x64 tiles, 64-K stages double-buffered by
+//                         cp.async into swizzled shared memory, ldmatrix
+//                         fragments; the same split-K partials.
 //   router_gemv_kernel    the same logits for T <= 4 tokens: one warp per
 //                         (expert, K quarter) with all of its weight loads
 //                         in flight, quarters summed in a fixed order.
@@ -94,6 +99,116 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __re
       if (e < E) out[(size_t)t * E + e] = acc[i][j];
     }
   }
+}
+
+constexpr int kMT = 64, kME = 64, kMK = 64;   // tensor-core router tile: tokens, experts, K
+
+__device__ __forceinline__ void cp_async_16_zfill(void* smem_dst, const void* gsrc, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gsrc),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                               uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// grid (ceil(E/64), ceil(T/64), splits), 128 threads; bf16 x [T x M] and W
+// [E x M] (M and kspan multiples of 64). Warp (wm, wn) owns tokens 32 wm..
+// and experts 32 wn.. of the tile. Shared rows are 64 K (128 bytes) with
+// 16-byte chunk c of row r stored at c ^ (r & 7), so each ldmatrix phase
+// reads eight distinct bank groups.
+__global__ void __launch_bounds__(128) router_mma_kernel(const uint16_t* __restrict__ x,
+                                                         const uint16_t* __restrict__ W,
+                                                         float* __restrict__ part, int T, int E,
+                                                         int M, int kspan) {
+  __shared__ __align__(128) uint16_t sa[2][kMT * kMK];
+  __shared__ __align__(128) uint16_t sb[2][kME * kMK];
+  const int e0 = blockIdx.x * kME, t0 = blockIdx.y * kMT;
+  const int kb = blockIdx.z * kspan, ke = min(M, kb + kspan);
+  const int nst = max(0, (ke - kb) / kMK);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int wm = warp & 1, wn = warp >> 1;
+  auto load = [&](int st, int buf) {
+    const int k0 = kb + st * kMK;
+    for (int c = tid; c < kMT * 8; c += blockDim.x) {
+      const int r = c >> 3, ch = c & 7;
+      const int sw = (r * kMK) + ((ch ^ (r & 7)) << 3);
+      const bool vt = t0 + r < T, ve = e0 + r < E;
+      cp_async_16_zfill(&sa[buf][sw], x + (size_t)(vt ? t0 + r : 0) * M + k0 + ch * 8, vt);
+      cp_async_16_zfill(&sb[buf][sw], W + (size_t)(ve ? e0 + r : 0) * M + k0 + ch * 8, ve);
+    }
+    cp_async_commit();
+  };
+  float c[2][4][4];
+#pragma unroll
+  for (int i = 0; i < 2; i++)
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+#pragma unroll
+      for (int v = 0; v < 4; v++) c[i][j][v] = 0.f;
+  if (nst > 0) load(0, 0);
+  const int mat = lane >> 3, lr = lane & 7;
+  for (int st = 0; st < nst; st++) {
+    const int buf = st & 1;
+    if (st + 1 < nst) {
+      load(st + 1, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const uint32_t abase = smem_u32(&sa[buf][0]), bbase = smem_u32(&sb[buf][0]);
+#pragma unroll
+    for (int kk = 0; kk < kMK / 16; kk++) {
+      uint32_t a[2][4], b[4][2];
+#pragma unroll
+      for (int mi = 0; mi < 2; mi++) {
+        // matrices: rows 0-7 / 8-15 x k 0-7, then the same x k 8-15
+        const int row = wm * 32 + mi * 16 + (mat & 1) * 8 + lr;
+        const int ch = kk * 2 + (mat >> 1);
+        ldsm_x4(abase + (uint32_t)(row * kMK + ((ch ^ (row & 7)) << 3)) * 2, a[mi][0], a[mi][1],
+                a[mi][2], a[mi][3]);
+      }
+#pragma unroll
+      for (int nj = 0; nj < 2; nj++) {
+        // matrices: experts 0-7 x k 0-7 / 8-15, then experts 8-15 likewise
+        const int row = wn * 32 + nj * 16 + (mat >> 1) * 8 + lr;
+        const int ch = kk * 2 + (mat & 1);
+        ldsm_x4(bbase + (uint32_t)(row * kMK + ((ch ^ (row & 7)) << 3)) * 2, b[2 * nj][0],
+                b[2 * nj][1], b[2 * nj + 1][0], b[2 * nj + 1][1]);
+      }
+#pragma unroll
+      for (int mi = 0; mi < 2; mi++)
+#pragma unroll
+        for (int ni = 0; ni < 4; ni++) mma_bf16_16816(c[mi][ni], a[mi], b[ni][0], b[ni][1]);
+    }
+    __syncthreads();  // the next iteration's copy overwrites this buffer
+  }
+  float* out = part + (size_t)blockIdx.z * T * E;
+  const int g = lane >> 2, t4 = lane & 3;
+#pragma unroll
+  for (int mi = 0; mi < 2; mi++)
+#pragma unroll
+    for (int ni = 0; ni < 4; ni++)
+#pragma unroll
+      for (int v = 0; v < 4; v++) {
+        const int tok = t0 + wm * 32 + mi * 16 + g + (v >> 1) * 8;
+        const int e = e0 + wn * 32 + ni * 8 + 2 * t4 + (v & 1);
+        if (tok < T && e < E) out[(size_t)tok * E + e] = c[mi][ni][v];
+      }
 }
 
 constexpr int kGemvMaxT = 4;   // tokens per launch of the GEMV router
@@ -532,14 +647,17 @@ WispError launch_route(const WispMoeConfig* c, const uint16_t* x, const uint16_t
     else
       wb::launch_k(router_gemv_kernel<false>, g, 256, 0, st, x, W, part, T, E, M);
   } else {
+    // fp16 weights stay on the fp32 SIMT kernel (the tensor cores would need
+    // the bf16 activations rounded to fp16).
+    const int gran = c->router_fp16 ? kRK : kMK;
     int kspan = (M + (int)splits - 1) / (int)splits;
-    kspan = (kspan + kRK - 1) / kRK * kRK;
+    kspan = (kspan + gran - 1) / gran * gran;
     nsplit = (M + kspan - 1) / kspan;
     dim3 g1((E + kRE - 1) / kRE, (T + kRT - 1) / kRT, nsplit);
     if (c->router_fp16)
       wb::launch_k(router_logits_kernel<true>, g1, 256, 0, st, x, W, part, T, E, M, kspan);
     else
-      wb::launch_k(router_logits_kernel<false>, g1, 256, 0, st, x, W, part, T, E, M, kspan);
+      wb::launch_k(router_mma_kernel, g1, 128, 0, st, x, W, part, T, E, M, kspan);
   }
   auto topk = E <= 32 ? topk_kernel<1> : E <= 64 ? topk_kernel<2> : E <= 128 ? topk_kernel<4>
             : E <= 256 ? topk_kernel<8> : E <= 512 ? topk_kernel<16> : topk_kernel<32>;
