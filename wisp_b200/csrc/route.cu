@@ -21,11 +21,13 @@
 //                         group score = sum of the top-2 sigmoid scores,
 //                         keep topk_groups groups, pick k experts among
 //                         them, w = s / sum(s) * routed_scaling.
-//   count / fill kernels  one warp per expert scans all (token, slot) pairs
-//                         in order and compacts its matches with a ballot,
-//                         so every expert's rows are sorted by token and the
-//                         permutation is deterministic. An always-on shared
-//                         expert is one more segment holding every token.
+//   count / fill kernels  one block per expert; its warps scan consecutive
+//                         ranges of the (token, slot) pairs, count, take
+//                         their ranges' offsets in order and compact their
+//                         matches with a ballot, so every expert's rows are
+//                         sorted by token and the permutation is
+//                         deterministic. An always-on shared expert is one
+//                         more segment holding every token.
 //   pack_rows_kernel      gathers bf16 token rows into fp16 rows in the
 //                         interleaved K order the tensor-core kernel expects.
 #include <cuda_bf16.h>
@@ -457,23 +459,44 @@ __global__ void topk_kernel(const float* __restrict__ part, int splits, const fl
   }
 }
 
-// counts[v] for the routed experts: one warp per expert over all T*k slots.
-__global__ void count_kernel(const int* __restrict__ idx, int nslots, int E, int T, int has_shared,
-                             int* __restrict__ counts) {
-  const int v = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (v >= E + has_shared) return;
+// One block of kPlanWarps warps per expert v: warp w scans the w-th
+// contiguous range of the T*k (token, slot) pairs (a multiple of 32 long).
+constexpr int kPlanWarps = 8;
+
+__device__ __forceinline__ int plan_range(int nslots) {
+  return ((nslots + kPlanWarps - 1) / kPlanWarps + 31) & ~31;
+}
+
+// Matches of expert v among slots [b, e) counted by one warp.
+__device__ __forceinline__ int warp_count(const int* __restrict__ idx, int b, int e, int v, int lane) {
+  int c = 0;
+  for (int base = b; base < e; base += 32) {
+    const int s = base + lane;
+    c += __popc(__ballot_sync(0xffffffffu, s < e && __ldg(idx + s) == v));
+  }
+  return c;
+}
+
+// counts[v] for the routed experts (the shared expert, v == E, has T rows).
+__global__ void __launch_bounds__(kPlanWarps * 32) count_kernel(const int* __restrict__ idx,
+                                                                int nslots, int E, int T,
+                                                                int* __restrict__ counts) {
+  __shared__ int part[kPlanWarps];
+  const int v = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (v == E) {
-    if (lane == 0) counts[v] = T;
+    if (threadIdx.x == 0) counts[v] = T;
     return;
   }
-  int c = 0;
-  for (int base = 0; base < nslots; base += 32) {
-    const int s = base + lane;
-    const bool hit = s < nslots && __ldg(idx + s) == v;
-    c += __popc(__ballot_sync(0xffffffffu, hit));
+  const int L = plan_range(nslots);
+  const int b = min(nslots, warp * L), e = min(nslots, b + L);
+  const int c = warp_count(idx, b, e, v, lane);
+  if (lane == 0) part[warp] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int t = 0;
+    for (int w = 0; w < kPlanWarps; w++) t += part[w];
+    counts[v] = t;
   }
-  if (lane == 0) counts[v] = c;
 }
 
 // Exclusive scan of counts into segments (single block).
@@ -519,25 +542,33 @@ __global__ void segments_kernel(const int* __restrict__ counts, int V, WispSegme
   }
 }
 
-// Rows of expert v sorted by (token, slot): row_token / row_weight.
-__global__ void fill_kernel(const int* __restrict__ idx, const float* __restrict__ w, int nslots,
-                            int k, int E, int T, int has_shared, const WispSegment* __restrict__ segs,
-                            int* __restrict__ row_token, float* __restrict__ row_weight) {
-  const int v = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (v >= E + has_shared) return;
+// Rows of expert v sorted by (token, slot): row_token / row_weight. Each
+// warp counts its range, the ranges' offsets follow in range order, then each
+// warp compacts its matches with a ballot.
+__global__ void __launch_bounds__(kPlanWarps * 32) fill_kernel(
+    const int* __restrict__ idx, const float* __restrict__ w, int nslots, int k, int E, int T,
+    const WispSegment* __restrict__ segs, int* __restrict__ row_token,
+    float* __restrict__ row_weight) {
+  __shared__ int part[kPlanWarps];
+  const int v = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int begin = segs[v].row_begin;
   if (v == E) {
-    for (int t = lane; t < T; t += 32) {
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
       row_token[begin + t] = t;
       row_weight[begin + t] = 1.f;
     }
     return;
   }
+  const int L = plan_range(nslots);
+  const int b = min(nslots, warp * L), e = min(nslots, b + L);
+  const int c = warp_count(idx, b, e, v, lane);
+  if (lane == 0) part[warp] = c;
+  __syncthreads();
   int pos = begin;
-  for (int base = 0; base < nslots; base += 32) {
+  for (int q = 0; q < warp; q++) pos += part[q];
+  for (int base = b; base < e; base += 32) {
     const int s = base + lane;
-    const bool hit = s < nslots && __ldg(idx + s) == v;
+    const bool hit = s < e && __ldg(idx + s) == v;
     const unsigned m = __ballot_sync(0xffffffffu, hit);
     if (hit) {
       const int p = pos + __popc(m & ((1u << lane) - 1u));
@@ -672,9 +703,9 @@ WispError launch_plan(const WispMoeConfig* c, const int* idx, const float* w, in
                       WispErrCtx* err) {
   const int T = c->tokens, E = c->n_experts, k = c->top_k, sh = c->has_shared ? 1 : 0;
   const int V = E + sh;
-  wb::launch_k(count_kernel, (V + 7) / 8, 256, 0, st, idx, T * k, E, T, sh, counts);
+  wb::launch_k(count_kernel, V, kPlanWarps * 32, 0, st, idx, T * k, E, T, counts);
   wb::launch_k(segments_kernel, 1, 1024, 0, st, counts, V, segs);
-  wb::launch_k(fill_kernel, (V + 7) / 8, 256, 0, st, idx, w, T * k, k, E, T, sh, segs, row_token,
+  wb::launch_k(fill_kernel, V, kPlanWarps * 32, 0, st, idx, w, T * k, k, E, T, segs, row_token,
                row_weight);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
