@@ -415,15 +415,26 @@ def main() -> None:
         abi.call("wisp_b200_check_error_flag", flag.data_ptr(), stream.cuda_stream)
         kms = statistics.mean(a.elapsed_time(b) for a, b in evs[1:]) / L   # first pass = warm-up
         k_bytes = (used[0] + (1 if spec.has_shared else 0)) * eb
+        k_flops = 6.0 * spec.hidden * spec.inter * R     # gate, up, down per routed row
         achieved = k_bytes / (kms / 1e3) / 1e9
-        roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
-                    "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+        tflops = k_flops / (kms / 1e3) / 1e12
+        # The bound is the resource the call needs longer on at peak: HBM for
+        # decode-sized groups, the tensor cores for prefill-sized ones.
+        if k_flops / (peaks["bf16_tflops"] * 1e12) > k_bytes / (peaks["hbm_gbs"] * 1e9):
+            bound = {"bound": "tensor", "achieved": round(tflops, 1), "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": round(tflops / peaks["bf16_tflops"], 4)}
+        else:
+            bound = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4)}
+        roofline = {**bound,
                     "traffic": round(k_bytes * TRAFFIC_PER_ALGORITHMIC_BYTE),
                     "traffic_source": "ncu dram__bytes_read+write of one call on ep_profile, "
                                       "scaled by algorithmic bytes",
                     "kernel": "grouped int4 FFN (gate/up+SwiGLU, down+combine)",
                     "kernel_ms": round(kms, 4), "algorithmic_bytes": k_bytes,
-                    "peak_source": peaks["source"], "vs_8tbs": round(achieved / 8000.0, 4)}
+                    "algorithmic_flops": k_flops, "hbm_gbs": round(achieved, 1),
+                    "tflops": round(tflops, 1), "peak_source": peaks["source"],
+                    "vs_8tbs": round(achieved / 8000.0, 4)}
 
     # -- end to end through the public API with host buffers ---------------
     e2e = None
