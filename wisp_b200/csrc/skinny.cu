@@ -430,11 +430,12 @@ __device__ __forceinline__ void stage_single(float (&acc0)[2][4], float (&acc1)[
     load_b<1>(bq[q], st, q, g, t);
   }
   // scales and zero points of MMA rows g (low half) and g+8 (high half)
-  __half2 s0[G], s1[G], z0[G], z1[G];
+  float2 s0[G], s1[G];
+  __half2 z0[G], z1[G];
 #pragma unroll
   for (int j = 0; j < G; j++) {
-    s0[j] = __floats2half2_rn(row_scale(st, kOffS, b0, j, r0), row_scale(st, kOffS, b0, j, r0 + 8));
-    s1[j] = __floats2half2_rn(row_scale(st, kOffS, b1, j, r1), row_scale(st, kOffS, b1, j, r1 + 8));
+    s0[j] = make_float2(row_scale(st, kOffS, b0, j, r0), row_scale(st, kOffS, b0, j, r0 + 8));
+    s1[j] = make_float2(row_scale(st, kOffS, b1, j, r1), row_scale(st, kOffS, b1, j, r1 + 8));
     z0[j] = hz0 ? __floats2half2_rn(row_scale(st, kOffZ, b0, j, r0), row_scale(st, kOffZ, b0, j, r0 + 8))
                 : __half2{};
     z1[j] = hz1 ? __floats2half2_rn(row_scale(st, kOffZ, b1, j, r1), row_scale(st, kOffZ, b1, j, r1 + 8))
@@ -472,7 +473,7 @@ __device__ __forceinline__ void stage_single(float (&acc0)[2][4], float (&acc1)[
                   h22u(a81[wd][pp + 1]), b0v, b1v);
       }
     }
-    const float2 f0 = __half22float2(s0[j]), f1 = __half22float2(s1[j]);
+    const float2 f0 = s0[j], f1 = s1[j];
     acc0[0][0] = fmaf(f0.x, c0[ci][0], acc0[0][0]);
     acc0[0][1] = fmaf(f0.x, c0[ci][1], acc0[0][1]);
     acc0[0][2] = fmaf(f0.y, c0[ci][2], acc0[0][2]);
