@@ -67,6 +67,7 @@ constexpr int kRawK = 128;           // K per raw (weight) stage
 // order and applies SwiGLU. At most kMaxSplitItems split work items.
 constexpr int kMaxSplit = 8;
 constexpr int kMaxSplitItems = 256;
+constexpr int kMaxFix = 16;   // slices one CTA may complete (<= 4 per item, <= 2 items)
 constexpr size_t kPartialFloats = (size_t)BM * 128 * 2;   // one gate/up work item
 constexpr int kBoxBytes = BM * 64;   // one matrix's nibbles for a raw stage
 constexpr int kScBytes = 512;        // room for 2 scale groups x 128 rows (fp16)
@@ -174,6 +175,8 @@ struct SmemLayout {
   uint64_t accfull, accempty, final_bar;
   uint32_t tmem_base;
   int abort;
+  int fix_n;            // split gate/up: 32-row slices this CTA completes
+  int fix[kMaxFix];     // tile * 4 + slice
 };
 
 struct TileInfo {
@@ -250,6 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
     mbar_init(&L->accempty, 4);  // the four epilogue warps
     mbar_init(&L->final_bar, 1);
     L->abort = 0;
+    L->fix_n = 0;
     fence_barrier_init();
   }
   if (warp == kMmaWarp) {
@@ -570,20 +574,22 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
             }
           }
         } else {
-          // This K part's (gate, up) sums of row r go to the scratch row;
-          // the warp that completes the tile's rows 32q.. sums all parts in
-          // order (a per-tile, per-warp arrival count decides which).
-          float* prow = p.partial + (size_t)it * kPartialFloats + (size_t)r * 256;
+          // This K part's (gate, up) sums go to the scratch item, laid out
+          // [column][gate/up][row] so that a warp's 32 rows are one
+          // contiguous run; the CTA that completes the tile's rows 32q..
+          // (a per-tile, per-warp arrival count decides which) sums all
+          // parts in order after its last item.
+          float* pit = p.partial + (size_t)it * kPartialFloats + r;
           for (int c0 = 0; c0 < ti.bn; c0 += 16) {
             uint32_t g[16], u[16];
             tmem_ld16(lane_addr + c0, g);
             tmem_ld16(lane_addr + 128 + c0, u);
             tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 16; j += 2)
-              *reinterpret_cast<float4*>(prow + (c0 + j) * 2) =
-                  make_float4(__uint_as_float(g[j]), __uint_as_float(u[j]),
-                              __uint_as_float(g[j + 1]), __uint_as_float(u[j + 1]));
+            for (int j = 0; j < 16; j++) {
+              pit[((c0 + j) * 2 + 0) * BM] = __uint_as_float(g[j]);
+              pit[((c0 + j) * 2 + 1) * BM] = __uint_as_float(u[j]);
+            }
           }
           tc_fence_before();
           __threadfence();
@@ -597,21 +603,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
             __threadfence();
           }
           old = __shfl_sync(0xffffffffu, old, 0);
-          if (old == split - 1) {
-            const float* base = p.partial + (size_t)tile * split * kPartialFloats + (size_t)r * 256;
-            for (int c = 0; c < ti.nvalid; c += 2) {
-              float4 acc = __ldcg(reinterpret_cast<const float4*>(base + c * 2));
-              for (int ks = 1; ks < split; ks++) {
-                const float4 v = __ldcg(reinterpret_cast<const float4*>(base + ks * kPartialFloats + c * 2));
-                acc.x += v.x;
-                acc.y += v.y;
-                acc.z += v.z;
-                acc.w += v.w;
-              }
-              p.h_out[(size_t)(ti.row0 + c) * p.I + islot] = __float2half(silu(acc.x) * acc.y);
-              if (c + 1 < ti.nvalid)
-                p.h_out[(size_t)(ti.row0 + c + 1) * p.I + islot] = __float2half(silu(acc.z) * acc.w);
-            }
+          if (old == split - 1 && lane == 0) {
+            const int slot = atomicAdd(&L->fix_n, 1);
+            if (slot < kMaxFix) L->fix[slot] = tile * 4 + q;
+            else atomicExch(&L->abort, 1);  // cannot happen: items per CTA are bounded
           }
         }
       } else {
@@ -656,6 +651,29 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
 
   tc_fence_before();
   __syncthreads();
+  // Split gate/up: every thread of the CTA sums the parts of the slices it
+  // completes (K parts in order), applies SwiGLU and writes H; the partial
+  // sums were published before the arrival counts (fence, then the count;
+  // the completing warp fenced after reading it, then the CTA barrier).
+  if (MODE == GATEUP && split > 1 && !L->abort) {
+    const int nfix = min(L->fix_n, kMaxFix);
+    for (int f = 0; f < nfix; f++) {
+      const int tile = L->fix[f] >> 2, q = L->fix[f] & 3;
+      const TileInfo ti = decode_tile(p, tile);
+      const float* base = p.partial + (size_t)tile * split * kPartialFloats + q * 32;
+      for (int i = threadIdx.x; i < 32 * ti.nvalid; i += blockDim.x) {
+        const int rr = i & 31, c = i >> 5;
+        const float* pc = base + (size_t)c * 2 * BM + rr;
+        float g = __ldcg(pc), u = __ldcg(pc + BM);
+        for (int ks = 1; ks < split; ks++) {
+          g += __ldcg(pc + ks * kPartialFloats);
+          u += __ldcg(pc + ks * kPartialFloats + BM);
+        }
+        const int row = ti.mblk * BM + q * 32 + rr;
+        p.h_out[(size_t)(ti.row0 + c) * p.I + k_interleave_slot(row)] = __float2half(silu(g) * u);
+      }
+    }
+  }
   if (threadIdx.x == 0 && L->abort && p.error_flag) atomicExch(p.error_flag, 1);
   if (warp == kMmaWarp) {
     tc_fence_after();
