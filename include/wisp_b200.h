@@ -264,7 +264,9 @@ typedef struct {
  *   d_h:    fp16 [R x I] scratch (interleaved K order).
  *   mode 0: d_out[row_token[p] * M + m] += row_weight[p] * y[p, m] (atomic fp32)
  *   mode 1: d_y[p * M + m] = y[p, m] (fp32 rows, no weighting)
- * d_tiles: int32 scratch of wisp_b200_tiles_words(n_segs) words.
+ * d_tiles: int32 scratch of wisp_b200_tiles_words(n_segs) words (tile and
+ *          unit plans, and ~33.5 MB for the partial sums of a K-split
+ *          gate/up); one call at a time per scratch.
  * d_error_flag: device int set to nonzero if a bounded wait gave up (may be
  * NULL); check it with wisp_b200_check_error_flag. */
 size_t wisp_b200_tiles_words(int n_segs);
