@@ -151,3 +151,33 @@ def test_prepared_size_and_checks():
     err = abi.WispErrCtx()
     rc = abi.lib().wisp_b200_prepare_experts(C.byref(c), 16, 9, 256, n - 1, None, C.byref(err))
     assert rc == abi.WISP_ERR_INVALID_ARG and b"required" in err.message
+
+
+def test_ep_exchange_argument_checks():
+    """The exchange entry points reject bad shapes before any launch."""
+    L, err = abi.lib(), abi.WispErrCtx()
+    P = 256  # a non-null, 16-byte-aligned stand-in pointer; never dereferenced here
+    assert L.wisp_b200_ep_block_bytes(7168, 48, 32, 8) > 32 * 7168 * 2
+    assert L.wisp_b200_ep_block_bytes(7168, 48, 32, 33) == 0       # top_k > 32
+    assert L.wisp_b200_ep_block_bytes(100, 48, 32, 8) == 0          # hidden % 8
+    # experts do not split over the ranks
+    rc = L.wisp_b200_ep_dispatch(P, 4, 256, P, 2, P, P, P, 8, 3, 4, P, P, None, C.byref(err))
+    assert rc == abi.WISP_ERR_INVALID_ARG and b"ep_dispatch" in err.message
+    # more tokens than the block capacity
+    rc = L.wisp_b200_ep_dispatch(P, 5, 256, P, 2, P, P, P, 8, 2, 4, P, P, None, C.byref(err))
+    assert rc == abi.WISP_ERR_INVALID_ARG
+    # misaligned send buffer
+    rc = L.wisp_b200_ep_dispatch(P, 4, 256, P, 2, P, P, P, 8, 2, 4, P + 8, P, None, C.byref(err))
+    assert rc == abi.WISP_ERR_INVALID_ARG and b"16-byte" in err.message
+    # null pointer
+    rc = L.wisp_b200_ep_dispatch(None, 4, 256, P, 2, P, P, P, 8, 2, 4, P, P, None, C.byref(err))
+    assert rc == abi.WISP_ERR_INVALID_ARG
+    # too many (rank, local expert) pairs for the single-block receive plan
+    rc = L.wisp_b200_ep_recv_plan(P, 8, 200, 4, 2, 256, P, P, P, P, None, C.byref(err))
+    assert rc == abi.WISP_ERR_INVALID_ARG and b"1024" in err.message
+    rc = L.wisp_b200_ep_gather_rows(P, 2, 4, 4, 2, 260, P, P, 16, P, None, C.byref(err))
+    assert rc == abi.WISP_ERR_INVALID_ARG
+    rc = L.wisp_b200_ep_combine(P, P, 5, 2, 4, 256, P, None, C.byref(err))
+    assert rc == abi.WISP_ERR_INVALID_ARG
+    rc = L.wisp_b200_ep_combine(P, P, 4, 2, 4, 258, P, None, C.byref(err))
+    assert rc == abi.WISP_ERR_INVALID_ARG
