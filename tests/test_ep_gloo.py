@@ -204,7 +204,8 @@ def test_dispatch_layout():
 
 
 @pytest.mark.parametrize("world,spec", [(2, SPEC), (2, synth.small(SPEC, skew=True, seed=4, tokens=7)),
-                                        (4, synth.small(SPEC, seed=9, tokens=11))])
+                                        (4, synth.small(SPEC, seed=9, tokens=11)),
+                                        (8, synth.small(SPEC, seed=12, tokens=13))])
 def test_ep_ranks_match_single_process(orc, world, spec):
     from helpers import oracle_outputs, oracle_route
     port = _free_port()
