@@ -142,7 +142,7 @@ def cpu_baseline(spec, budget_s: float = 12.0) -> dict:
     from oracle.oracle import RefCPU
     if not RefCPU.available():
         return {"unavailable": "oracle/_ref/libwisp_ref.so not built"}
-    ref = RefCPU()
+    ref = RefCPU(threads=RefCPU.host_cores())
     router, blobs, xs = _cpu_sample_setup(spec)
     _cpu_token_time(ref, spec, router, blobs, xs, 1)  # warm
     n, el = 0, 0.0
@@ -154,7 +154,7 @@ def cpu_baseline(spec, budget_s: float = 12.0) -> dict:
                      f"reference's scalar/OpenMP CPU run_moe branch (router + shared + top-{spec.top_k} "
                      f"experts), {len(blobs)} distinct expert blobs"}
     if RefCPU.available(avx512=True):
-        ra = RefCPU(avx512=True)
+        ra = RefCPU(avx512=True, threads=RefCPU.host_cores())
         _cpu_token_time(ra, spec, router, blobs, xs, 1)
         m = max(2, n // 2)
         t = _cpu_token_time(ra, spec, router, blobs, xs, m)
@@ -180,7 +180,9 @@ def reference_arm(args, spec) -> None:
         line.update({"unavailable": "reference CPU library oracle/_ref/libwisp_ref.so not built"})
         print(json.dumps(line))
         return
-    ref = RefCPU()
+    # All host cores, whatever OMP_NUM_THREADS the launcher exported
+    # (torch.distributed.run sets it to 1).
+    ref = RefCPU(threads=RefCPU.host_cores())
     router, blobs, xs = _cpu_sample_setup(spec)
     tokens_per_step = 1
     for _ in range(args.warmup):
@@ -333,10 +335,9 @@ def main() -> None:
         ms = float(t.item())
     value = T_all * L / (ms / 1e3)
 
-    # error words of the tensor-core kernels
-    if world == 1:
-        for lay in layers:
-            lay.check()
+    # error words of the bounded waits (every kernel of the step)
+    for lay in layers:
+        lay.check()
 
     # -- algorithmic bytes of one step (routing is identical every step) --
     used = []
@@ -371,7 +372,8 @@ def main() -> None:
         row_w = torch.empty(R, dtype=torch.float32, device=dev)
         xp = torch.empty((R, spec.hidden), dtype=torch.float16, device=dev)
         h = torch.empty((R, spec.inter), dtype=torch.float16, device=dev)
-        tiles = torch.empty(lib.wisp_b200_tiles_words(V), dtype=torch.int32, device=dev)
+        gws = torch.empty(lib.wisp_b200_grouped_workspace_bytes(C.byref(cfg), V, R),
+                          dtype=torch.uint8, device=dev)
         flag = torch.zeros(1, dtype=torch.int32, device=dev)
         out = torch.zeros((T, spec.hidden), dtype=torch.float32, device=dev)
         abi.call("wisp_b200_dispatch_plan", C.byref(cfg), lay.idx.data_ptr(), lay.wt.data_ptr(),
@@ -387,7 +389,7 @@ def main() -> None:
                 abi.call("wisp_b200_grouped_ffn", C.byref(cfg), table[l].data_ptr(),
                          layers_w[l].table.data_ptr(), V, segs.data_ptr(), V, R,
                          xp.data_ptr(), h.data_ptr(), 0, row_token.data_ptr(), row_w.data_ptr(),
-                         out.data_ptr(), tiles.data_ptr(), flag.data_ptr(), st)
+                         out.data_ptr(), gws.data_ptr(), gws.numel(), flag.data_ptr(), st)
 
         # The L calls replay as one CUDA graph (as in the timed step), so the
         # host's tensor-map set-up between calls stays out of the device time.

@@ -257,26 +257,31 @@ typedef struct {
 /* Grouped expert FFN over pre-permuted rows. d_prepared / d_experts /
  * n_entries: a prepared weight set and its device expert table (segment
  * experts index its entries). Segments of at most 16 rows (decode) run on
- * the register-fed tensor-core kernel, larger ones on the tcgen05 kernel.
+ * the register-fed integer tensor-core kernel, larger ones on the tcgen05
+ * kernel.
  *   d_xp:   fp16 [R x M] activation rows in interleaved K order (within each
  *           8 K: 0,4,1,5,2,6,3,7) -- produced by wisp_b200_pack_rows.
  *   d_segs: DEVICE array of n_segs segments.
- *   d_h:    fp16 [R x I] scratch (interleaved K order).
+ *   d_h:    [R x I] scratch of 2 bytes per element (the SwiGLU output: fp16
+ *           rows for tensor-core segments, 16-bit integer rows with
+ *           per-128-K scales in the workspace for register-path segments).
  *   mode 0: d_out[row_token[p] * M + m] += row_weight[p] * y[p, m] (atomic fp32)
  *   mode 1: d_y[p * M + m] = y[p, m] (fp32 rows, no weighting)
- * d_tiles: int32 scratch of wisp_b200_tiles_words(n_segs) words (tile and
- *          unit plans, and ~33.5 MB for the partial sums of a K-split
- *          gate/up); one call at a time per scratch.
+ * d_workspace: wisp_b200_grouped_workspace_bytes(cfg, n_segs, rows_capacity)
+ *          bytes, 256-byte aligned (tile and unit plans, the register path's
+ *          integer activation rows and their scales, and ~33.5 MB for the
+ *          partial sums of a K-split gate/up); one call at a time per
+ *          workspace.
  * d_error_flag: device int set to nonzero if a bounded wait gave up (may be
  * NULL); check it with wisp_b200_check_error_flag. */
-size_t wisp_b200_tiles_words(int n_segs);
+size_t wisp_b200_grouped_workspace_bytes(const WispMoeConfig* cfg, int n_segs, int rows_capacity);
 WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void* d_prepared,
                                 const WispInt4Expert* d_experts, int n_entries,
                                 const WispSegment* d_segs, int n_segs, int rows_capacity,
                                 const uint16_t* d_xp, uint16_t* d_h, int mode,
                                 const int* d_row_token, const float* d_row_weight,
-                                float* d_out, int32_t* d_tiles, int* d_error_flag,
-                                cudaStream_t stream, WispErrCtx* err);
+                                float* d_out, void* d_workspace, size_t workspace_bytes,
+                                int* d_error_flag, cudaStream_t stream, WispErrCtx* err);
 
 /* Dispatch plan from a routing: one segment per expert (then the shared
  * expert with every token when cfg->has_shared), rows sorted by (token,

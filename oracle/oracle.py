@@ -174,7 +174,9 @@ class Oracle:
 class RefCPU:
     """The reference engine's CPU hot path (compiled from its own sources)."""
 
-    def __init__(self, avx512: bool = False):
+    def __init__(self, avx512: bool = False, threads: int | None = None):
+        """threads: OpenMP threads for the reference's parallel loops; None
+        keeps the runtime's default (OMP_NUM_THREADS or all cores)."""
         name = "libwisp_ref_avx512.so" if avx512 else "libwisp_ref.so"
         path = REF_DIR / name
         if not path.exists():
@@ -195,7 +197,11 @@ class RefCPU:
         L.ref_half_to_float.restype = C.c_float
         L.ref_half_to_float.argtypes = [C.c_uint16]
         L.ref_omp_threads.restype = _I
+        L.ref_set_threads.restype = None
+        L.ref_set_threads.argtypes = [_I]
         self.L = L
+        if threads is not None:
+            L.ref_set_threads(int(threads))
 
     @staticmethod
     def available(avx512: bool = False) -> bool:
@@ -212,6 +218,14 @@ class RefCPU:
 
     def threads(self) -> int:
         return self.L.ref_omp_threads()
+
+    @staticmethod
+    def host_cores() -> int:
+        """Cores this process may run on (its CPU affinity set)."""
+        try:
+            return len(os.sched_getaffinity(0))
+        except (AttributeError, OSError):
+            return os.cpu_count() or 1
 
     def parse_header(self, blob: bytes) -> dict | None:
         buf = (C.c_int64 * 20)()

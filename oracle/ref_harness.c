@@ -162,3 +162,16 @@ int ref_omp_threads(void) {
     return 1;
 #endif
 }
+
+/* Thread count of the OpenMP regions the calling thread starts next. A
+ * launcher such as torch.distributed.run exports OMP_NUM_THREADS=1, which
+ * the OpenMP runtime reads once when it loads; the timed CPU paths call
+ * this so they use the host cores they were given whatever the launcher
+ * set. */
+void ref_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}

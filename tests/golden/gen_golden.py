@@ -27,6 +27,7 @@ from __future__ import annotations
 
 import argparse
 import sys
+import os
 import tempfile
 from pathlib import Path
 
@@ -39,8 +40,11 @@ ROOT = HERE.parent.parent
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("WISP_REFERENCE_DIR"),
+                    help="the reference project's checkout (or $WISP_REFERENCE_DIR)")
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("give --reference <path> or set WISP_REFERENCE_DIR")
     sys.path.insert(0, a.reference)
     sys.path.insert(0, str(ROOT))
     from wisp.converter.quantizer import quantize_int4, dequantize_int4  # reference code

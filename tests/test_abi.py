@@ -128,18 +128,26 @@ def test_expert_ffn_argument_checks(golden_dir):
 
 
 def test_grouped_ffn_argument_checks():
+    L, err = abi.lib(), abi.WispErrCtx()
     c = _cfg(group_size=32)
-    err = abi.WispErrCtx()
-    rc = abi.lib().wisp_b200_grouped_ffn(C.byref(c), 256, 16, 4, 16, 1, 8, 16, 16, 0, 16, 16, 16, 16,
-                                         None, None, C.byref(err))
+    assert L.wisp_b200_grouped_workspace_bytes(C.byref(c), 4, 8) == 0
+    rc = L.wisp_b200_grouped_ffn(C.byref(c), 256, 16, 4, 16, 1, 8, 16, 16, 0, 16, 16, 16, 256,
+                                 1 << 30, None, None, C.byref(err))
     assert rc == abi.WISP_ERR_INVALID_ARG and b"group_size" in err.message
     c = _cfg()
-    rc = abi.lib().wisp_b200_grouped_ffn(C.byref(c), 256, 16, 4, 16, 1, 8, 16, 16, 0, None, None, 16, 16,
-                                         None, None, C.byref(err))
+    need = L.wisp_b200_grouped_workspace_bytes(C.byref(c), 4, 8)
+    # tile plans, ~33.5 MB of split partial sums, q16 rows and their metadata
+    assert need >= 256 * 128 * 128 * 2 * 4 + 8 * 2 * c.hidden
+    assert L.wisp_b200_grouped_workspace_bytes(C.byref(c), 4, 800) > need
+    rc = L.wisp_b200_grouped_ffn(C.byref(c), 256, 16, 4, 16, 1, 8, 16, 16, 0, None, None, 16, 256,
+                                 need, None, None, C.byref(err))
     assert rc == abi.WISP_ERR_INVALID_ARG and b"mode 0" in err.message
-    rc = abi.lib().wisp_b200_grouped_ffn(C.byref(c), 264, 16, 4, 16, 1, 8, 16, 16, 1, None, None, 16, 16,
-                                         None, None, C.byref(err))
+    rc = L.wisp_b200_grouped_ffn(C.byref(c), 264, 16, 4, 16, 1, 8, 16, 16, 1, None, None, 16, 256,
+                                 need, None, None, C.byref(err))
     assert rc == abi.WISP_ERR_INVALID_ARG and b"256-byte" in err.message
+    rc = L.wisp_b200_grouped_ffn(C.byref(c), 256, 16, 4, 16, 4, 8, 16, 16, 1, None, None, 16, 256,
+                                 need - 1, None, None, C.byref(err))
+    assert rc == abi.WISP_ERR_INVALID_ARG and b"workspace" in err.message
 
 
 def test_prepared_size_and_checks():

@@ -118,6 +118,15 @@ class CpuOps:
             r = int(src_pos[j])
             sorted_rows[j] = torch.from_numpy(self._views(recv, r // cap, lay)[3][r % cap].copy())
 
+    def workspace(self, cfg, n_segs, rows, device):
+        return torch.empty(1, dtype=torch.uint8)
+
+    def clear_flag(self, flag):
+        flag.zero_()
+
+    def check_flag(self, flag):
+        assert int(flag[0]) == 0
+
     def grouped_dev(self, cfg, lw, segs, n_segs, rows, xp, h, mode, row_token, row_weight, out,
                     tiles, flag):
         sv = segs.numpy().view(np.int32).reshape(-1, 4)[:n_segs]

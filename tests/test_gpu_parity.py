@@ -329,7 +329,9 @@ def test_grouped_ffn_tile_boundaries(orc, mode, path):
     xp = torch.empty((R, spec.hidden), dtype=torch.float16, device=DEV)
     h = torch.empty((R, spec.inter), dtype=torch.float16, device=DEV)
     out = torch.zeros((R, spec.hidden), dtype=torch.float32, device=DEV)
-    tiles = torch.empty(abi.lib().wisp_b200_tiles_words(len(segs)), dtype=torch.int32, device=DEV)
+    cfg = spec.cfg(T)
+    ws = torch.empty(abi.lib().wisp_b200_grouped_workspace_bytes(C.byref(cfg), len(segs), R),
+                     dtype=torch.uint8, device=DEV)
     flag = torch.zeros(1, dtype=torch.int32, device=DEV)
     dsegs = _segments_device(segs)
     cfg = spec.cfg(T)
@@ -338,7 +340,7 @@ def test_grouped_ffn_tile_boundaries(orc, mode, path):
              lw.n_entries,
              dsegs.data_ptr(), len(segs), R,
              xp.data_ptr(), h.data_ptr(), mode, row_token.data_ptr(), row_w.data_ptr(), out.data_ptr(),
-             tiles.data_ptr(), flag.data_ptr(), _stream())
+             ws.data_ptr(), ws.numel(), flag.data_ptr(), _stream())
     abi.call("wisp_b200_check_error_flag", flag.data_ptr(), _stream())
     got = out.cpu().numpy()
     xs = bf16_to_f64(x)

@@ -81,11 +81,26 @@ def build(verbose: bool = False, clean: bool = False) -> Path:
     return LIB
 
 
+def reference_dir() -> Path | None:
+    """The reference project's checkout: $WISP_REFERENCE_DIR, else a
+    ``reference`` directory beside this repository; None when neither holds
+    the reference's C engine."""
+    cands = [os.environ.get("WISP_REFERENCE_DIR"), str(ROOT.parent / "reference")]
+    for c in cands:
+        if c and (Path(c) / "csrc" / "core" / "wisp_engine.c").exists():
+            return Path(c)
+    return None
+
+
 def build_oracle() -> None:
     """Build the test-only oracle libraries (oracle/_ref). The reference CPU
     path is compiled only where the reference sources are present."""
     make = shutil.which("make") or "make"
-    r = subprocess.run([make, "-C", str(ROOT / "oracle"), "all"], capture_output=True, text=True)
+    cmd = [make, "-C", str(ROOT / "oracle"), "all"]
+    ref = reference_dir()
+    if ref is not None:
+        cmd.append(f"REF_DIR={ref}")
+    r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"oracle build failed:\n{r.stdout}\n{r.stderr}")
 

@@ -150,6 +150,15 @@ WB_DEV void tma_load_2d(void* smem_dst, const CUtensorMap* m, uint64_t* bar, int
       : "memory");
 }
 
+WB_DEV void tma_load_3d(void* smem_dst, const CUtensorMap* m, uint64_t* bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cta.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];"
+      ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)),
+        "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
 // Untiled bulk copy global -> shared (no multicast), completion on an
 // mbarrier. Both addresses 16-byte aligned, size a multiple of 16.
 WB_DEV void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {

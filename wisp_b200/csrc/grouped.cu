@@ -43,6 +43,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "skinny.h"
 
 using namespace wb;
 
@@ -100,24 +101,38 @@ struct Shape {
 // Prepared weights: per matrix entry (expert v, matrix m in gate/up/down) two
 // TMA descriptors of its packed nibbles (64-byte boxes with the 64-byte
 // swizzle for this kernel, 128-byte boxes with the 128-byte swizzle for the
-// register-path kernel), a zero-point flag, and its scales and zero points transposed to
-// [row tile][group][128 rows] so that the scales of one stage are one
-// contiguous run.
+// register-path kernel), a zero-point flag, and its scales and zero points
+// transposed to [row tile][group][128 rows] so that the scales of one stage
+// are one contiguous run. For the register-path kernel, per expert a second
+// copy of the scales (and zero points) in its unit order: the gate/up pair
+// as [128-row block][256-K stage][gate, up][groups of the stage][128 rows]
+// and down as [256-row block][256-K stage][first, second 128 rows][groups]
+// [128 rows], so each stage of a unit takes one contiguous copy (slots
+// outside the matrix hold zeros).
 struct PreparedLayout {
-  size_t maps, maps_sk, flags, zbits, scales, zeros, mat_sc_bytes, total;
+  size_t maps, maps_sk, flags, zbits, scales, zeros, mat_sc_bytes;
+  size_t sk_scales, sk_zeros, sk_gu_bytes, sk_dn_bytes, sk_stage_bytes;
+  size_t total;
 };
 
 PreparedLayout prepared_layout(const WispMoeConfig* c, int n) {
   PreparedLayout L;
   const size_t entries = (size_t)n * 3;
-  L.mat_sc_bytes = (size_t)c->hidden * c->inter / c->group_size * 2;
+  const int M = c->hidden, I = c->inter;
+  L.mat_sc_bytes = (size_t)M * I / c->group_size * 2;
   L.maps = 0;
   L.maps_sk = entries * sizeof(CUtensorMap);
   L.flags = L.maps_sk + entries * sizeof(CUtensorMap);
   L.zbits = L.flags + entries * 4;  // the same flags, one bit per entry
   L.scales = (L.zbits + (entries + 31) / 32 * 4 + 255) & ~(size_t)255;
   L.zeros = L.scales + entries * L.mat_sc_bytes;
-  L.total = L.zeros + entries * L.mat_sc_bytes;
+  const int G = 256 / c->group_size;
+  L.sk_stage_bytes = (size_t)2 * G * BM * 2;
+  L.sk_gu_bytes = (size_t)(I / BM) * ((M + 255) / 256) * L.sk_stage_bytes;
+  L.sk_dn_bytes = (size_t)((M + 255) / 256) * ((I + 255) / 256) * L.sk_stage_bytes;
+  L.sk_scales = (L.zeros + entries * L.mat_sc_bytes + 255) & ~(size_t)255;
+  L.sk_zeros = L.sk_scales + (size_t)n * (L.sk_gu_bytes + L.sk_dn_bytes);
+  L.total = L.sk_zeros + (size_t)n * (L.sk_gu_bytes + L.sk_dn_bytes);
   return L;
 }
 
@@ -797,9 +812,69 @@ __device__ void plan_units(const WispSegment* __restrict__ segs, int nseg, int p
   }
 }
 
+// Rows of one register-path segment (0 < rows <= sk_rows): fp16 rows in
+// interleaved K order (within 8 K: 0,4,1,5,2,6,3,7) -> q16 rows (layout in
+// skinny.h). One warp per (row, 128-K block): lane l holds half l%2 of
+// packed word l/2, i.e. physical K {0,4,1,5} or {2,6,3,7} of that word; the
+// block's max |x| sets the scale, and the two lanes of a word exchange bytes
+// so each writes 8 contiguous bytes.
+__device__ void quant_segment(const WispSegment* __restrict__ segs, int s, int sk_rows,
+                              const __half* __restrict__ xp, int M, uint8_t* __restrict__ xq) {
+  const WispSegment sg = segs[s];
+  if (sg.rows <= 0 || sg.rows > sk_rows) return;
+  const int nblk = M / kQ16Block;
+  const size_t rb = q16_row_bytes(M);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int w = lane >> 1, half = lane & 1;
+  for (int pr = warp; pr < sg.rows * nblk; pr += nw) {
+    const int r = pr / nblk, b = pr - r * nblk;
+    const size_t p = (size_t)(sg.row_begin + r);
+    const uint2 raw = *reinterpret_cast<const uint2*>(xp + p * M + b * kQ16Block + w * 8 + half * 4);
+    const float2 f01 = __half22float2(u2h2(raw.x)), f23 = __half22float2(u2h2(raw.y));
+    const float f[4] = {f01.x, f01.y, f23.x, f23.y};
+    float m = fmaxf(fmaxf(fabsf(f[0]), fabsf(f[1])), fmaxf(fabsf(f[2]), fabsf(f[3])));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float inv = m > 0.f ? 32767.f / m : 0.f;
+    uint32_t oh = 0, ol = 0;
+    int sum = 0;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int v = max(-32767, min(32767, __float2int_rn(f[i] * inv)));
+      sum += v;
+      oh |= (uint32_t)((v >> 8) & 0xFF) << (8 * i);
+      ol |= (uint32_t)(v & 0xFF) << (8 * i);
+    }
+    const uint32_t ph = __shfl_xor_sync(0xffffffffu, oh, 1);
+    const uint32_t pl = __shfl_xor_sync(0xffffffffu, ol, 1);
+    // half 0 holds K {0,4,1,5}, half 1 K {2,6,3,7}: half 0 writes the high
+    // bytes (evens 0,2,4,6 then odds 1,3,5,7), half 1 the low bytes.
+    uint2 o;
+    if (half == 0) {
+      o.x = __byte_perm(oh, ph, 0x5140);
+      o.y = __byte_perm(oh, ph, 0x7362);
+    } else {
+      o.x = __byte_perm(pl, ol, 0x5140);
+      o.y = __byte_perm(pl, ol, 0x7362);
+    }
+    uint8_t* row = xq + p * rb;
+    *reinterpret_cast<uint2*>(row + q16_word_offset(b * (kQ16Block / 8) + w) + half * 8) = o;
+    // sums over K 0-63 (lanes 0-15) and 64-127 (lanes 16-31)
+#pragma unroll
+    for (int o2 = 1; o2 < 16; o2 <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o2);
+    const int sum1 = __shfl_sync(0xffffffffu, sum, 16);
+    if (lane == 0) {
+      const float sc = m / 32767.f;
+      *reinterpret_cast<float4*>(row + q16_meta_offset(b)) =
+          make_float4(sc * 0.0625f, sc * (float)sum, sc * (float)sum1, 0.f);
+    }
+  }
+}
+
 // The four plans of one call in one launch: blocks 0 and 1 tile gate/up and
 // down for the tensor-core kernel, blocks 2 and 3 cut them into register-path
-// units.
+// units; blocks 4.. (when the register path runs) quantise the rows of the
+// register-path segments, block 4 + s those of segment s.
 struct PlanArgs {
   const WispSegment* segs;
   int nseg, sk_rows;
@@ -808,6 +883,9 @@ struct PlanArgs {
   int32_t* tickets;
   int per_gu, per_dn, cols, ks_dn, nk_dn, target;
   int32_t *tiles_gu, *tiles_dn, *units_gu, *units_dn;
+  const __half* xp;
+  int M;
+  uint8_t* xq;
 };
 
 __global__ void __launch_bounds__(1024) plan_all_kernel(const __grid_constant__ PlanArgs a) {
@@ -821,9 +899,12 @@ __global__ void __launch_bounds__(1024) plan_all_kernel(const __grid_constant__ 
                  a.tiles_dn, nullptr);
       break;
     case 2: plan_units(a.segs, a.nseg, a.per_gu, a.cols, a.sk_rows, 1, 1, 0, a.units_gu); break;
-    default:
+    case 3:
       plan_units(a.segs, a.nseg, a.per_dn, a.cols, a.sk_rows, a.ks_dn, a.nk_dn, a.target,
                  a.units_dn);
+      break;
+    default:
+      quant_segment(a.segs, (int)blockIdx.x - 4, a.sk_rows, a.xp, a.M, a.xq);
   }
 }
 
@@ -851,6 +932,41 @@ __global__ void transpose_scales_kernel(const WispInt4Expert* __restrict__ exper
     const size_t src = (tile * BM + r) * gpr + g;
     so[i] = s[src];
     if (z) zo[i] = z[src];
+  }
+}
+
+// The register-path kernel's per-stage runs of scales and zero points (see
+// PreparedLayout): blockIdx.y = expert * 2 + (0: gate/up pair, 1: down).
+__global__ void skinny_scales_kernel(const WispInt4Expert* __restrict__ experts, int M, int I,
+                                     int gs, uint8_t* __restrict__ prepared, size_t off_scales,
+                                     size_t off_zeros, size_t gu_bytes, size_t dn_bytes) {
+  const int v = blockIdx.y >> 1, part = blockIdx.y & 1;
+  const WispInt4Expert ex = experts[v];
+  const int G = 256 / gs;
+  const size_t base = (size_t)v * (gu_bytes + dn_bytes) + (part ? gu_bytes : 0);
+  uint16_t* so = reinterpret_cast<uint16_t*>(prepared + off_scales + base);
+  uint16_t* zo = reinterpret_cast<uint16_t*>(prepared + off_zeros + base);
+  const size_t total = (part ? dn_bytes : gu_bytes) / 2;
+  const int K = part ? I : M;
+  const int nk = (K + 255) / 256, gpr = K / gs;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    // i = (((block * nk + kg) * 2 + half) * G + grp) * 128 + r
+    const int r = (int)(i % BM);
+    size_t rest = i / BM;
+    const int grp = (int)(rest % G);
+    rest /= G;
+    const int half = (int)(rest % 2);
+    rest /= 2;
+    const int kg = (int)(rest % nk);
+    const int blk = (int)(rest / nk);
+    const WispInt4Mat mt = part ? ex.down : (half ? ex.up : ex.gate);
+    const int row = part ? blk * 2 * BM + half * BM + r : blk * BM + r;
+    const int group = kg * G + grp;
+    const bool in = row < (part ? M : I) && group < gpr;
+    const size_t src = (size_t)row * gpr + group;
+    so[i] = in ? reinterpret_cast<const uint16_t*>(mt.scales)[src] : 0;
+    zo[i] = (in && mt.zeros) ? reinterpret_cast<const uint16_t*>(mt.zeros)[src] : 0;
   }
 }
 
@@ -886,6 +1002,23 @@ bool encode_rows_map(CUtensorMap* m, const void* base, int rows, int cols, int b
   cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+// q16 rows (layout in skinny.h) as a 3D tensor {128 bytes, rows, lines}:
+// one box = box_rows rows x the five lines of one 256-K stage, stored in
+// shared memory as [line][row][128 bytes] with the 128-byte swizzle.
+bool encode_q16_map(CUtensorMap* m, const void* base, int rows, int cols, int box_rows) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) return false;
+  const cuuint64_t rb = q16_row_bytes(cols);
+  cuuint64_t dims[3] = {(cuuint64_t)kQ16LineBytes, (cuuint64_t)rows, rb / kQ16LineBytes};
+  cuuint64_t strides[2] = {rb, (cuuint64_t)kQ16LineBytes};
+  cuuint32_t box[3] = {(cuuint32_t)kQ16LineBytes, (cuuint32_t)box_rows, (cuuint32_t)kQ16Lines};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box,
             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
          CUDA_SUCCESS;
@@ -951,35 +1084,6 @@ int g_skinny_rows = -1;  // -1: library default
 
 }  // namespace
 
-namespace wb {
-struct SkLaunch {
-  const uint8_t* prepared;
-  size_t p_maps_sk, p_zbits, p_scales, p_zeros, p_mat_sc_bytes;
-  const WispSegment* segs;
-  int nseg;
-  int n_entries;
-  const int32_t* units_gu;
-  const int32_t* units_dn;
-  int M, I, gs;
-  const CUtensorMap* xp_maps;
-  const CUtensorMap* h_maps;
-  __half* h;
-  const int* row_token;
-  const float* row_weight;
-  float* out;
-  int mode;
-  int* error_flag;
-  unsigned long long* counters;
-};
-int skinny_max_rows();
-int skinny_max_segs();
-int skinny_max_entries();
-int skinny_cols();
-int skinny_stages(int K);
-int skinny_units_gateup(int I);
-int skinny_units_down(int M);
-cudaError_t launch_skinny(const SkLaunch& L, int phase, int grid, cudaStream_t st);
-}  // namespace wb
 
 extern "C" void wisp_b200_set_skinny_max_rows(int rows) { g_skinny_rows = rows; }
 
@@ -1045,25 +1149,64 @@ extern "C" WispError wisp_b200_prepare_experts(const WispMoeConfig* cfg,
   transpose_scales_kernel<<<grid, 256, 0, stream>>>(d_experts, n_entries, M, I, cfg->group_size,
                                                     base, PL.scales, PL.zeros, PL.mat_sc_bytes);
   WB_CUDA_CHECK(cudaGetLastError());
+  skinny_scales_kernel<<<dim3(64, n_entries * 2), 256, 0, stream>>>(
+      d_experts, M, I, cfg->group_size, base, PL.sk_scales, PL.sk_zeros, PL.sk_gu_bytes,
+      PL.sk_dn_bytes);
+  WB_CUDA_CHECK(cudaGetLastError());
   // The host vectors are read by the copies above before they are freed.
   WB_CUDA_CHECK(cudaStreamSynchronize(stream));
   return WISP_OK;
 }
 
-// Workspace (int32 words): tensor-core gate/up and down tables [prefix S+1 |
-// bn S | K split] each, the register path's gate/up and down unit prefixes
-// [S+2] each, the split gate/up arrival counts [4 x kMaxSplitItems], then
-// (16-byte aligned) the split gate/up partial sums [kMaxSplitItems x 128 x
-// 128 x 2 floats].
+// Workspace of one grouped-FFN call: tensor-core gate/up and down tables
+// [prefix S+1 | bn S | K split] each, the register path's gate/up and down
+// unit prefixes [S+2] each, the split gate/up arrival counts [4 x
+// kMaxSplitItems] (int32 words); then, 256-byte aligned, the split gate/up
+// partial sums [kMaxSplitItems x 128 x 128 x 2 floats], and the q16 rows
+// (layout in skinny.h) of the register-path segments' input and of their
+// SwiGLU output H.
 namespace {
-size_t tiles_partial_offset(int n_segs) {
-  const size_t w = (size_t)2 * (2 * n_segs + 2) + (size_t)2 * (n_segs + 2) + 4 * kMaxSplitItems;
-  return (w + 3) & ~(size_t)3;
+struct GroupedWs {
+  int32_t* tiles_gu;
+  int32_t* tiles_dn;
+  int32_t* units_gu;
+  int32_t* units_dn;
+  int32_t* tickets;
+  float* partial;
+  uint8_t* xq;
+  uint8_t* hq;
+  size_t bytes;
+};
+
+GroupedWs carve_grouped(int n_segs, int rows, int M, int I, void* base) {
+  GroupedWs w;
+  size_t off = 0;
+  auto take = [&](size_t bytes) -> uint8_t* {
+    off = (off + 255) & ~(size_t)255;
+    uint8_t* q = base ? static_cast<uint8_t*>(base) + off : nullptr;
+    off += bytes;
+    return q;
+  };
+  const size_t tw = (size_t)(2 * n_segs + 2);
+  int32_t* words = reinterpret_cast<int32_t*>(
+      take(4 * (2 * tw + (size_t)2 * (n_segs + 2) + 4 * (size_t)kMaxSplitItems)));
+  w.tiles_gu = words;
+  w.tiles_dn = words ? words + tw : nullptr;
+  w.units_gu = words ? words + 2 * tw : nullptr;
+  w.units_dn = words ? w.units_gu + (n_segs + 2) : nullptr;
+  w.tickets = words ? w.units_dn + (n_segs + 2) : nullptr;
+  w.partial = reinterpret_cast<float*>(take((size_t)kMaxSplitItems * kPartialFloats * 4));
+  w.xq = take((size_t)rows * q16_row_bytes(M));
+  w.hq = take((size_t)rows * q16_row_bytes(I));
+  w.bytes = (off + 255) & ~(size_t)255;
+  return w;
 }
 }  // namespace
 
-extern "C" size_t wisp_b200_tiles_words(int n_segs) {
-  return tiles_partial_offset(n_segs) + (size_t)kMaxSplitItems * kPartialFloats;
+extern "C" size_t wisp_b200_grouped_workspace_bytes(const WispMoeConfig* cfg, int n_segs,
+                                                    int rows_capacity) {
+  if (!cfg || n_segs <= 0 || rows_capacity <= 0 || check_shapes(cfg, nullptr) != WISP_OK) return 0;
+  return carve_grouped(n_segs, rows_capacity, cfg->hidden, cfg->inter, nullptr).bytes;
 }
 
 extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void* d_prepared,
@@ -1072,9 +1215,10 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
                                            int rows_capacity, const uint16_t* d_xp, uint16_t* d_h,
                                            int mode, const int* d_row_token,
                                            const float* d_row_weight, float* d_out,
-                                           int32_t* d_tiles, int* d_error_flag,
-                                           cudaStream_t stream, WispErrCtx* err) {
-  if (!cfg || !d_prepared || !d_experts || !d_segs || !d_xp || !d_h || !d_out || !d_tiles ||
+                                           void* d_workspace, size_t workspace_bytes,
+                                           int* d_error_flag, cudaStream_t stream,
+                                           WispErrCtx* err) {
+  if (!cfg || !d_prepared || !d_experts || !d_segs || !d_xp || !d_h || !d_out || !d_workspace ||
       n_entries <= 0)
     return WB_FAIL(WISP_ERR_INVALID_ARG, "grouped_ffn: null pointer argument");
   WispError e = check_shapes(cfg, err);
@@ -1088,6 +1232,12 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
     return WB_FAIL(WISP_ERR_INVALID_ARG, "grouped_ffn: activation buffers must be 16-byte aligned");
   if ((uintptr_t)d_prepared & 255)
     return WB_FAIL(WISP_ERR_INVALID_ARG, "grouped_ffn: prepared weights must be 256-byte aligned");
+  if ((uintptr_t)d_workspace & 255)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "grouped_ffn: workspace must be 256-byte aligned");
+  const GroupedWs ws = carve_grouped(n_segs, rows_capacity, M, I, d_workspace);
+  if (workspace_bytes < ws.bytes)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "grouped_ffn: workspace %zu < required %zu",
+                   workspace_bytes, ws.bytes);
 
   const PreparedLayout PL = prepared_layout(cfg, n_entries);
   GemmParams gu, dn;
@@ -1120,20 +1270,15 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
   dn.out = d_out;
   dn.mode = mode;
 
-  const size_t tw = (size_t)(2 * n_segs + 2);
   int sk_rows = g_skinny_rows >= 0 ? std::min(g_skinny_rows, wb::skinny_max_rows())
                                    : wb::skinny_max_rows();
-  // The register-path kernel keeps the segment table in shared memory; larger
-  // launches run on the tensor-core kernel alone.
+  // The register-path kernel keeps the zero-point flags in shared memory;
+  // larger launches run on the tensor-core kernel alone.
   if (n_segs > wb::skinny_max_segs() || n_entries > wb::skinny_max_entries()) sk_rows = 0;
-  gu.tiles = d_tiles;
-  dn.tiles = d_tiles + tw;
-  int32_t* units_gu = d_tiles + 2 * tw;
-  int32_t* units_dn = units_gu + (n_segs + 2);
-  int32_t* tickets = units_dn + (n_segs + 2);
-  float* partial = reinterpret_cast<float*>(d_tiles + tiles_partial_offset(n_segs));
-  gu.tickets = tickets;
-  gu.partial = partial;
+  gu.tiles = ws.tiles_gu;
+  dn.tiles = ws.tiles_dn;
+  gu.tickets = ws.tickets;
+  gu.partial = ws.partial;
   // Register path: gate/up cannot split K (SwiGLU needs whole sums), nor can
   // mode 1 (plain row stores); the weighted down projection splits K when it
   // has fewer than two units per SM. Tensor-core path: both projections split
@@ -1159,36 +1304,40 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
   pa.split_dn = mode == 0 ? kMaxSplit : 1;
   pa.nraw_gu = M / kRawK;
   pa.nraw_dn = I / kRawK;
-  pa.tickets = tickets;
-  pa.tiles_gu = d_tiles;
-  pa.tiles_dn = d_tiles + tw;
-  pa.units_gu = units_gu;
-  pa.units_dn = units_dn;
-  wb::launch_k(plan_all_kernel, 4, 1024, 0, stream, pa);
-  CUtensorMap sk_xp[2], sk_h[2];
+  pa.tickets = ws.tickets;
+  pa.tiles_gu = ws.tiles_gu;
+  pa.tiles_dn = ws.tiles_dn;
+  pa.units_gu = ws.units_gu;
+  pa.units_dn = ws.units_dn;
+  pa.xp = reinterpret_cast<const __half*>(d_xp);
+  pa.M = M;
+  pa.xq = ws.xq;
+  wb::launch_k(plan_all_kernel, 4 + (sk_rows > 0 ? n_segs : 0), 1024, 0, stream, pa);
+  CUtensorMap sk_xq[2], sk_hq[2];
   for (int i = 0; i < 2; i++) {
-    if (!encode_rows_map(&sk_xp[i], d_xp, rows_capacity, M, 8 << i) ||
-        !encode_rows_map(&sk_h[i], d_h, rows_capacity, I, 8 << i))
+    if (!encode_q16_map(&sk_xq[i], ws.xq, rows_capacity, M, 8 << i) ||
+        !encode_q16_map(&sk_hq[i], ws.hq, rows_capacity, I, 8 << i))
       return WB_FAIL(WISP_ERR_CUDA, "grouped_ffn: cuTensorMapEncodeTiled failed (token rows)");
   }
   wb::SkLaunch sk;
   sk.prepared = gu.prepared;
   sk.p_maps_sk = PL.maps_sk;
   sk.p_zbits = PL.zbits;
-  sk.p_scales = PL.scales;
-  sk.p_zeros = PL.zeros;
-  sk.p_mat_sc_bytes = PL.mat_sc_bytes;
+  sk.p_sk_scales = PL.sk_scales;
+  sk.p_sk_zeros = PL.sk_zeros;
+  sk.sk_gu_bytes = PL.sk_gu_bytes;
+  sk.sk_dn_bytes = PL.sk_dn_bytes;
   sk.segs = d_segs;
   sk.nseg = n_segs;
   sk.n_entries = n_entries;
-  sk.units_gu = units_gu;
-  sk.units_dn = units_dn;
+  sk.units_gu = ws.units_gu;
+  sk.units_dn = ws.units_dn;
   sk.M = M;
   sk.I = I;
   sk.gs = gs;
-  sk.xp_maps = sk_xp;
-  sk.h_maps = sk_h;
-  sk.h = reinterpret_cast<__half*>(d_h);
+  sk.xq_maps = sk_xq;
+  sk.hq_maps = sk_hq;
+  sk.hq = ws.hq;
   sk.row_token = d_row_token;
   sk.row_weight = d_row_weight;
   sk.out = d_out;

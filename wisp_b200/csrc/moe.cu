@@ -46,7 +46,8 @@ struct Workspace {
   WispSegment* segs;
   int* row_token;
   float* row_weight;
-  int32_t* tiles;
+  void* grouped;
+  size_t grouped_bytes;
   int* error_flag;
   uint16_t* xp;
   uint16_t* h;
@@ -69,7 +70,8 @@ Workspace carve(const WispMoeConfig* c, void* base) {
   ws.segs = cv.take<WispSegment>(base, V);
   ws.row_token = cv.take<int>(base, ws.rows);
   ws.row_weight = cv.take<float>(base, ws.rows);
-  ws.tiles = cv.take<int32_t>(base, wisp_b200_tiles_words(V));
+  ws.grouped_bytes = wisp_b200_grouped_workspace_bytes(c, V, ws.rows);
+  ws.grouped = cv.take<uint8_t>(base, ws.grouped_bytes);
   ws.error_flag = cv.take<int>(base, 1);
   ws.xp = cv.take<uint16_t>(base, (size_t)ws.rows * M);
   ws.h = cv.take<uint16_t>(base, (size_t)ws.rows * I);
@@ -149,7 +151,8 @@ extern "C" WispError wisp_b200_moe_forward(const WispMoeConfig* cfg, const WispM
   WB_CUDA_CHECK(cudaMemsetAsync(ws.error_flag, 0, sizeof(int), stream));
   if (!w->experts) return WB_FAIL(WISP_ERR_INVALID_ARG, "moe_forward: null expert table");
   return wisp_b200_grouped_ffn(cfg, w->prepared, w->experts, V, ws.segs, V, ws.rows, ws.xp, ws.h, 0, ws.row_token,
-                               ws.row_weight, d_out, ws.tiles, ws.error_flag, stream, err);
+                               ws.row_weight, d_out, ws.grouped, ws.grouped_bytes, ws.error_flag,
+                               stream, err);
 }
 
 extern "C" int* wisp_b200_moe_error_word(const WispMoeConfig* cfg, void* d_workspace) {

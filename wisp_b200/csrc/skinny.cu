@@ -6,89 +6,108 @@
 // to stream the packed weights at HBM speed. A tcgen05.mma (M=128, K=16)
 // costs a fixed ~60-95 SM cycles whatever N <= 128 is (measured on B200), so
 // at small N the 5th-generation path tops out far below HBM speed; this
-// kernel feeds m16n8k16 tensor-core MMAs (~1.6 per cycle per SM) from
-// registers instead.
+// kernel feeds register-operand integer MMAs instead.
+//
+// Arithmetic. Each packed weight byte holds two nibbles n; the MMA's A
+// operand is the signed byte 16 (n - 8), which one LOP3 produces for the
+// high nibbles of a 32-bit word ((q ^ 0x88888888) & 0xF0F0F0F0: n ^ 8 is
+// the two's-complement nibble of n - 8) and a shift plus one LOP3 for the
+// low ones -- three instructions per eight weights, against nine for an
+// exact int4 -> fp16 conversion, which made the fp16 form of this kernel
+// instruction-issue bound. The activations are 16-bit integers with one
+// scale per (row, 128-K block) (see skinny.h), split into a signed high
+// byte and an unsigned low byte; m16n8k32 s8 x s8 and s8 x u8 MMAs (the
+// same issue rate as m16n8k16 fp16 on B200, twice the K) give exact int32
+// sums per scale group, and the fold adds
+//     w_scale * a_scale / 16 * float(256 * D_hi + D_lo)
+// (+ zero point * activation sum) into fp32 accumulators. A token's result
+// is therefore bit-identical whatever chunk of the segment it lands in,
+// and the 16-bit activations carry more precision than fp16.
 //
 // One persistent CTA per SM, warp-specialised:
-//   warp 8      producer: per 256-K stage, one TMA box of packed nibbles per
+//   warp 16     producer: per 256-K stage, one TMA box of packed nibbles per
 //               128-row weight block (128 rows x 128 bytes, 128-byte
-//               swizzle: a box row is one 128-byte request; narrower boxes
-//               left the TMA unit, not HBM, as the limit), one TMA box per
-//               64-K quarter of the unit's token rows (fp16, 128-byte
-//               swizzle), and bulk copies of the stage's scales (and zero
-//               points) from the prepared tile-transposed copy, into a
-//               5-deep shared-memory ring (44 KB per stage, up to 160 KB of
-//               weights in flight per SM: under full load a copy takes
-//               several microseconds from issue to arrival, so the bytes in
-//               flight per SM set the bandwidth). Units are looked up in a
-//               shared-memory copy of the unit prefix; the next unit's
-//               segment record is fetched one unit ahead.
-//   warps 0-7   consumers, each with two 16-row MMA tiles. Per 64-K quarter
-//               a warp reads its nibbles
-//               (conflict-free 8-byte loads: MMA row g lives in box row
-//               sigma(g) = 2(g%4) + g/4 (mod 8), so each half-warp's rows
-//               fall in distinct swizzle chunks) and the tokens' B fragments
-//               (conflict-free 16-byte loads), converts each 32-bit word of
-//               nibbles to exact (n - 8) fp16 pairs, runs a 4-MMA chain, and
-//               folds it into fp32 accumulators times the group's scale (and
-//               adds the zero-point term). The stage is released once its
-//               last quarter has been read; units of at most 8 tokens
-//               read a whole stage into registers and release it at once.
-//               (Sixteen one-tile warps, four per scheduler, measured
-//               slower: every warp re-reads the token fragments.)
+//               swizzle), one TMA box per 64-K quarter of the unit's token
+//               rows (128 bytes of q16 data per row), one box per 128-K block
+//               of the rows' metadata and bulk copies of the stage's weight
+//               scales (and zero points) from the prepared tile-transposed
+//               copy, into a 5-deep shared-memory ring (44 KB per stage, up
+//               to 160 KB of weights in flight per SM: under full load a copy
+//               takes several microseconds from issue to arrival, so the
+//               bytes in flight per SM set the bandwidth). Units are looked up
+//               in the unit prefix; the next unit's segment record is fetched
+//               one unit ahead.
+//   warps 0-15  consumers, one 16-row MMA tile each (four warps per
+//               scheduler: a stage's shared-memory reads and MMA chains are
+//               latency-bound, and eight two-tile warps left the schedulers
+//               idle two thirds of the time). Per 128-K group a thread reads
+//               2 x 8 bytes of each of its two weight rows (packed words 2t,
+//               2t+1 and 8+2t, 9+2t of the group; MMA row g lives in box row
+//               sigma(g) = 2(g%4) + g/4 (mod 8), so each half-warp's rows fall
+//               in distinct swizzle chunks) and one 16-byte chunk of each
+//               token row per MMA step (conflict-free: step s of thread t
+//               reads packed word 8(s/2) + 2t + s%2, whose chunk parity
+//               alternates between neighbouring token rows), runs four k32
+//               steps of high/low MMAs and folds them. Units of at most 8
+//               tokens read a whole stage into registers and release it
+//               before any arithmetic.
 //
 // Work unit = (segment, weight row block, chunk of up to 16 tokens, and for
 // a weighted down projection with fewer than two units per SM a part of a K
 // split, whose partial sums the epilogue adds atomically):
 //   GATEUP: 128 intermediate rows i of gate and of up; warp w takes rows
-//           16w..16w+15 of both -> h = silu(g) * u written to H (fp16,
-//           interleaved K order).
-//   DOWN:   256 output rows m (two 128-row blocks); warp w takes 32 rows ->
+//           8w..8w+7 of both (gate as MMA rows 0-7, up as rows 8-15) ->
+//           h = silu(g) * u, quantised per token over the unit's 128 rows
+//           (one q16 block of H: the warps exchange their column maxima and
+//           sums through shared memory) and written as q16 rows of H with
+//           their block metadata.
+//   DOWN:   256 output rows m (two 128-row blocks); warp w takes 16 rows ->
 //           out[token] += w * y (mode 0, fp32 atomics) or y rows (mode 1).
 // Chunks of one row block are consecutive units, so CTAs that run them at
-// the same time share the weight tile through L2. Every token runs the same
-// arithmetic in the same order whatever chunk it lands in, so a token's
-// result does not depend on the batch around it. Segments larger than the
-// routing threshold go to the tcgen05 kernel.
+// the same time share the weight tile through L2. Segments larger than the
+// routing threshold go to the tcgen05 kernel (grouped.cu), which keeps
+// fp16 activation rows; the two kernels work on disjoint rows.
 //
-// Fragment mapping. m16n8k16 gives thread (g = lane/4, t = lane%4) the A
-// pairs (row g, k 2t..2t+1), (row g+8, same), (row g, k 2t+8..2t+9),
-// (row g+8, same) and the B pairs (k 2t..2t+1, col g), (k 2t+8..2t+9, col g).
-// The logical k of one MMA may map to any physical K as long as A and B
-// agree. Per 64-K quarter, thread t owns packed words 2t and 2t+1 (bytes
-// 8t..8t+7); nib8_centered turns a word into the pairs (k0,k4) (k1,k5)
-// (k2,k6) (k3,k7). MMA m (0..3) of the quarter takes word m/2 and pair p =
-// 2(m&1) as its (2t,2t+1) slot and pair p+1 as its (2t+8,2t+9) slot. The
-// activation rows are stored interleaved (within 8 K: 0,4,1,5,2,6,3,7), so
-// pair q of word w is 32-bit element q of that word's 16 bytes: B slot 0 is
-// element p and B slot 1 element p+1 of the same activation word.
+// Fragment mapping (m16n8k32, 8-bit operands). Thread (g = lane/4, t =
+// lane%4) holds A bytes (row g, k 4t..4t+3) and (row g, k 16+4t..16+4t+3)
+// and the same for row g+8; B bytes (k 4t..4t+3, col g) and (k 16+4t..,
+// col g); D (row g, cols 2t, 2t+1) and (row g+8, same). The logical k of
+// one MMA may map to any physical K as long as A and B agree: in step s,
+// thread t's k 4t+i is physical K 2i and k 16+4t+i is K 2i+1 of packed word
+// 8(s/2) + 2t + s%2 of the 128-K group, so A is (even nibbles, odd nibbles)
+// of that word and B is the (evens, odds) byte quads of its q16 chunk.
 #include "common.cuh"
 #include "internal.h"
+#include "skinny.h"
 
 using namespace wb;
 
 namespace {
 
-constexpr int kCW = 8;                        // consumer warps, two 16-row tiles each
+// Consumer warps x 16-row MMA tiles per warp = 16 tiles per 256-K stage.
+#ifndef WB_SK_TILES_PER_WARP
+#define WB_SK_TILES_PER_WARP 2
+#endif
+constexpr int kTPW = WB_SK_TILES_PER_WARP;
+constexpr int kCW = 16 / kTPW;
+static_assert(kTPW == 1 || kTPW == 2, "one or two tiles per consumer warp");
 constexpr int kThreads = (kCW + 1) * 32;      // + one producer warp
-constexpr int kStages = 5;
+constexpr int kStages = 4;
 constexpr int kCols = 16;                     // tokens per unit
 // Default routing threshold: segments of up to 16 rows run here, larger ones
-// on the tcgen05 kernel (a larger segment costs this kernel one weight pass
-// per 16-token chunk; measured crossover on B200: prefill-shaped layers run
-// 1.5x faster at 16 than at 256, decode layers are within 3 %).
+// on the tcgen05 kernel.
 constexpr int kSkMaxRows = 16;
-constexpr int kKS = 256;                      // K per stage
-constexpr int kQ = kKS / 64;                  // 64-K quarters per stage
+constexpr int kKS = kQ16StageK;               // K per stage (256)
+constexpr int kAG = kKS / kQ16Block;          // 128-K activation groups per stage
 constexpr int kBoxRows = 128;
 constexpr int kBoxBytes = kBoxRows * 128;     // one weight block of a stage
-constexpr int kBQBytes = kCols * 128;         // one 64-K quarter of 16 token rows
-constexpr int kScRun = 4 * kBoxRows * 2;      // up to 4 scale groups x 128 rows
-// Stage layout (bytes): [weights 2 blocks][tokens 4 quarters]
-// [scales 2 blocks][zeros 2 blocks]; the stage headers live apart, so a
-// stage is a whole number of KB and every TMA box keeps 1024-byte alignment.
+constexpr int kTokBytes = kQ16Lines * kCols * kQ16LineBytes;  // one stage of 16 q16 rows
+constexpr int kScRun = 4 * kBoxRows * 2;      // up to 4 scale groups x 128 rows per block
+// Stage layout (bytes): [weights 2 blocks][token rows: 5 lines x rows x 128 B]
+// [scales 2 blocks][zeros 2 blocks]; the stage headers live apart, so a stage
+// is a whole number of KB and every TMA box keeps 1024-byte alignment.
 constexpr int kOffB = 2 * kBoxBytes;
-constexpr int kOffS = kOffB + kQ * kBQBytes;
+constexpr int kOffS = kOffB + kTokBytes;
 constexpr int kOffZ = kOffS + 2 * kScRun;
 constexpr int kStageBytes = kOffZ + 2 * kScRun;
 static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
@@ -110,22 +129,24 @@ struct __align__(16) StageHdr {
 struct SkSmem {
   uint64_t full[kStages];
   uint64_t empty[kStages];
+  uint64_t epi[2];        // GATEUP epilogue: column maxima, then column sums
   StageHdr hdr[kStages];
+  float red_max[kCW][kCols];
+  int red_sum[kCW][kCols];
   int abort;
-  int32_t units[kMaxSegs + 2];           // unit prefix per segment, then the K split
   uint32_t zbits[kMaxEntries * 3 / 32];  // zero-point flag per matrix entry
 };
 
 struct SkParams {
-  CUtensorMap act_map[2];  // token rows, boxes {64 halves, 8/16 rows}, 128-byte swizzle
+  CUtensorMap act_map[2];  // q16 token rows, boxes {128 bytes, 8/16 rows, 5 lines}, 128-byte swizzle
   const uint8_t* prepared;
-  size_t p_maps_sk, p_zbits, p_scales, p_zeros, p_mat_sc_bytes;
+  size_t p_maps_sk, p_zbits, p_sk_scales, p_sk_zeros, sk_gu_bytes, sk_dn_bytes;
   const WispSegment* segs;
-  const int32_t* units;  // [0, S]: unit prefix per segment
+  const int32_t* units;  // [0, S]: unit prefix per segment; [S + 1]: K split
   int nseg;
   int n_entries;
   int M, I, gs;
-  __half* h_out;
+  uint8_t* hq;      // q16 H rows
   const int* row_token;
   const float* row_weight;
   float* out;
@@ -139,23 +160,55 @@ struct SkParams {
 // and its total time.
 enum { SC_FULL_WAIT, SC_CONS_TOTAL, SC_EMPTY_WAIT, SC_PROD_TOTAL, SC_COUNT };
 
-__device__ __forceinline__ void hmma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+// ---------------------------------------------------------------------------
+// Integer MMAs and operand preparation.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void imma_ss(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                        uint32_t a3, uint32_t b0, uint32_t b1) {
   asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
-
-// The same with a zero accumulator input (the first MMA of a chain).
-__device__ __forceinline__ void hmma16816_z(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                            uint32_t a3, uint32_t b0, uint32_t b1) {
+__device__ __forceinline__ void imma_ss_z(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
   asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%10,%10,%10,%10};"
-      : "=f"(c[0]), "=f"(c[1]), "=f"(c[2]), "=f"(c[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
+      : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+__device__ __forceinline__ void imma_su(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                        uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void imma_su_z(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};"
+      : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// (a ^ b) & c in one LOP3 (immediate LUT 0x28).
+__device__ __forceinline__ uint32_t lop_xor_and(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0x28;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+// Signed bytes 16 (n - 8) of the even (K 0,2,4,6) and odd (K 1,3,5,7)
+// nibbles of a packed word.
+__device__ __forceinline__ uint32_t w_even(uint32_t q) {
+  return lop_xor_and(q << 4, 0x88888888u, 0xF0F0F0F0u);
+}
+__device__ __forceinline__ uint32_t w_odd(uint32_t q) {
+  return lop_xor_and(q, 0x88888888u, 0xF0F0F0F0u);
 }
 
 // Waits without the abort shortcut: used to let issued copies land before
@@ -166,121 +219,125 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, long 
     if (clock64() - t0 > limit) return;
 }
 
-// Nibbles of one 16-row tile for one 64-K quarter: MMA rows g and g+8.
-struct RawTile {
-  uint2 w[2];  // [row g / g+8]
-};
-
-// Token words of one 64-K quarter: [word 2t / 2t+1][n8 tile].
-template <int NT>
-struct BQuarter {
-  uint4 v[2][NT];
-};
-
-__device__ __forceinline__ uint32_t u4_get(const uint4& v, int i) {
-  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
-}
-
-// acc[nt] += s * (A x B) for one 16-row tile over one 64-K quarter; scales
-// of MMA rows g (sg) and g+8 (s8).
-template <int NT>
-__device__ __forceinline__ void tile_quarter(float (&acc)[2][4], const RawTile& w,
-                                             const BQuarter<NT>& b, float sg, float s8) {
-  __half2 ag[2][4], a8[2][4];
-  nib8_centered(w.w[0].x, ag[0]);
-  nib8_centered(w.w[0].y, ag[1]);
-  nib8_centered(w.w[1].x, a8[0]);
-  nib8_centered(w.w[1].y, a8[1]);
-  float ct[NT][4];
-#pragma unroll
-  for (int m = 0; m < 4; m++) {
-    const int wd = m >> 1, p = 2 * (m & 1);
-    const uint32_t a0 = h22u(ag[wd][p]), a2 = h22u(ag[wd][p + 1]);
-    const uint32_t a1 = h22u(a8[wd][p]), a3 = h22u(a8[wd][p + 1]);
-#pragma unroll
-    for (int nt = 0; nt < NT; nt++) {
-      if (m == 0)
-        hmma16816_z(ct[nt], a0, a1, a2, a3, u4_get(b.v[wd][nt], p), u4_get(b.v[wd][nt], p + 1));
-      else
-        hmma16816(ct[nt], a0, a1, a2, a3, u4_get(b.v[wd][nt], p), u4_get(b.v[wd][nt], p + 1));
-    }
-  }
-#pragma unroll
-  for (int nt = 0; nt < NT; nt++) {
-    acc[nt][0] = fmaf(sg, ct[nt][0], acc[nt][0]);
-    acc[nt][1] = fmaf(sg, ct[nt][1], acc[nt][1]);
-    acc[nt][2] = fmaf(s8, ct[nt][2], acc[nt][2]);
-    acc[nt][3] = fmaf(s8, ct[nt][3], acc[nt][3]);
-  }
-}
-
-// Zero points: acc[row, col] += z[row] * sum_k x[col, k] over the 64-K
-// quarter. xs[nt][j]: activation sum of column 2t+j of tile nt.
-template <int NT>
-__device__ __forceinline__ void quarter_sums(const BQuarter<NT>& b, float (&xs)[NT][2], int t) {
-#pragma unroll
-  for (int nt = 0; nt < NT; nt++) {
-    float s = 0.f;
-#pragma unroll
-    for (int wd = 0; wd < 2; wd++) {
-      const uint4 v = b.v[wd][nt];
-      const uint32_t e[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int i = 0; i < 4; i++) {
-        const float2 f = __half22float2(u2h2(e[i]));
-        s += f.x + f.y;
-      }
-    }
-    // the quad (same column g, t = 0..3) holds the 64 K of the quarter
-    s += __shfl_xor_sync(0xffffffffu, s, 1);
-    s += __shfl_xor_sync(0xffffffffu, s, 2);
-    // column 2t+j lives in quad 2t+j
-    xs[nt][0] = __shfl_sync(0xffffffffu, s, (2 * t) * 4);
-    xs[nt][1] = __shfl_sync(0xffffffffu, s, (2 * t + 1) * 4);
-  }
-}
-
-template <int NT>
-__device__ __forceinline__ void add_zeros(float (&acc)[2][4], const float (&xs)[NT][2], float zg,
-                                          float z8) {
-#pragma unroll
-  for (int nt = 0; nt < NT; nt++) {
-    acc[nt][0] = fmaf(zg, xs[nt][0], acc[nt][0]);
-    acc[nt][1] = fmaf(zg, xs[nt][1], acc[nt][1]);
-    acc[nt][2] = fmaf(z8, xs[nt][0], acc[nt][2]);
-    acc[nt][3] = fmaf(z8, xs[nt][1], acc[nt][3]);
-  }
-}
-
-// MMA rows g and g+8 of a tile for 64-K quarter q: box rows ra (block ba)
-// and rb (block bb), both = sigma(g) (mod 8). Thread t reads bytes
-// 8t..8t+7 of the quarter's 32 bytes, i.e. 16-byte chunk 2q + t/2, stored at
-// chunk ^ (row & 7).
-__device__ __forceinline__ void load_tile(RawTile& r, const uint8_t* st, int ba, int ra, int bb,
-                                          int rb, int q, int t) {
-  const int off = (((2 * q + (t >> 1)) ^ (ra & 7)) << 4) + 8 * (t & 1);
-  r.w[0] = *reinterpret_cast<const uint2*>(st + ba * kBoxBytes + ra * 128 + off);
-  r.w[1] = *reinterpret_cast<const uint2*>(st + bb * kBoxBytes + rb * 128 + off);
-}
-
-// Scale (or zero point) of box row `row` of a block for scale group grp.
+// Scale (or zero point) of box row `row` of a block for scale group grp of
+// the stage (G groups per block in the stage's run).
+template <int G>
 __device__ __forceinline__ float row_scale(const uint8_t* st, int off, int block, int grp,
                                            int row) {
   return __half2float(
-      reinterpret_cast<const __half*>(st + off + block * kScRun)[grp * kBoxRows + row]);
+      reinterpret_cast<const __half*>(st + off)[(block * G + grp) * kBoxRows + row]);
 }
 
-// Token row r's 16-byte chunk c of a 64-K quarter: the 128-byte swizzle puts
-// it at chunk c ^ (r & 7).
-template <int NT>
-__device__ __forceinline__ void load_b(BQuarter<NT>& b, const uint8_t* st, int q, int g, int t) {
+// A warp's MMA tile: MMA row g is box row rg of weight block bg, row g+8 box
+// row r8 of block b8.
+struct Tile {
+  int bg, rg, b8, r8;
+  bool hzg, hz8;
+};
+
+// Everything one 128-K activation group of a stage contributes to a warp's
+// tiles, in registers. GPS = weight scale groups per activation group (1:
+// group size 128, 2: group size 64, folded per 64-K half).
+template <int NT, int GPS, bool HZ>
+struct GroupIn {
+  uint2 a[kTPW][2][2];        // [tile][MMA row g / g+8][words 2t,2t+1 / 8+2t,9+2t]
+  uint4 b[4][NT];             // [step][n8 tile]: hi evens, hi odds, lo evens, lo odds
+  float ws[kTPW][2][GPS];     // weight scale [tile][row][scale group]
+  float as[NT][2];            // activation scale / 16 of columns 2t, 2t+1
+  float wz[kTPW][2][HZ ? GPS : 1];       // zero points
+  float asum[NT][2][HZ ? GPS : 1];       // activation sums over each scale group
+};
+
+// Loads activation group j of the stage at `st`; the stage's token rows are
+// [5 lines][brows rows][128 bytes] (lines 2j, 2j+1: group j's values; line
+// 4: the rows' block metadata).
+template <int NT, int GPS, bool HZ>
+__device__ __forceinline__ void load_group(GroupIn<NT, GPS, HZ>& in, const uint8_t* st, int brows,
+                                           int j, const Tile (&tl)[kTPW], int g, int t) {
+  constexpr int G = 2 * GPS;  // weight scale groups per 256-K stage
 #pragma unroll
-  for (int nt = 0; nt < NT; nt++) {
-    const int r = nt * 8 + g;
-    const uint8_t* row = st + kOffB + q * kBQBytes + r * 128;
+  for (int ti = 0; ti < kTPW; ti++)
 #pragma unroll
-    for (int wd = 0; wd < 2; wd++)
-      b.v[wd][nt] = *reinterpret_cast<const uint4*>(row + (((2 * t + wd) ^ (r & 7)) << 4));
+    for (int rr = 0; rr < 2; rr++) {
+      const int blk = rr ? tl[ti].b8 : tl[ti].bg, row = rr ? tl[ti].r8 : tl[ti].rg;
+      const uint8_t* base = st + blk * kBoxBytes + row * 128 + 8 * (t & 1);
+      const int sw = row & 7;
+      in.a[ti][rr][0] = *reinterpret_cast<const uint2*>(base + (((4 * j + (t >> 1)) ^ sw) << 4));
+      in.a[ti][rr][1] = *reinterpret_cast<const uint2*>(base + (((4 * j + 2 + (t >> 1)) ^ sw) << 4));
+#pragma unroll
+      for (int h = 0; h < GPS; h++) {
+        in.ws[ti][rr][h] = row_scale<G>(st, kOffS, blk, j * GPS + h, row);
+        if (HZ)
+          in.wz[ti][rr][HZ ? h : 0] =
+              (rr ? tl[ti].hz8 : tl[ti].hzg) ? row_scale<G>(st, kOffZ, blk, j * GPS + h, row) : 0.f;
+      }
+    }
+#pragma unroll
+  for (int s = 0; s < 4; s++)
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+      const int r = nt * 8 + g;
+      in.b[s][nt] = *reinterpret_cast<const uint4*>(
+          st + kOffB + ((2 * j + (s >> 1)) * brows + r) * 128 + (((2 * t + (s & 1)) ^ (r & 7)) << 4));
+    }
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+    for (int c = 0; c < 2; c++) {
+      const int r = nt * 8 + 2 * t + c;
+      const float* m = reinterpret_cast<const float*>(
+          st + kOffB + ((kQ16Lines - 1) * brows + r) * 128 + ((j ^ (r & 7)) << 4));
+      in.as[nt][c] = m[0];
+      if (HZ) {
+        if (GPS == 1) in.asum[nt][c][0] = m[1] + m[2];
+        else
+#pragma unroll
+          for (int h = 0; h < GPS; h++) in.asum[nt][c][HZ ? h : 0] = m[1 + h];
+      }
+    }
+}
+
+// acc += the group's contribution (K order: scale group by scale group).
+template <int NT, int GPS, bool HZ>
+__device__ __forceinline__ void compute_group(float (&acc)[kTPW][NT][4],
+                                              const GroupIn<NT, GPS, HZ>& in) {
+  constexpr int SPG = 4 / GPS;  // MMA steps per scale group
+#pragma unroll
+  for (int h = 0; h < GPS; h++) {
+    int dh[kTPW][NT][4], dl[kTPW][NT][4];
+#pragma unroll
+    for (int ss = 0; ss < SPG; ss++) {
+      const int s = h * SPG + ss;
+#pragma unroll
+      for (int ti = 0; ti < kTPW; ti++) {
+        const uint2 wg = in.a[ti][0][s >> 1], w8 = in.a[ti][1][s >> 1];
+        const uint32_t qg = (s & 1) ? wg.y : wg.x, q8 = (s & 1) ? w8.y : w8.x;
+        const uint32_t a0 = w_even(qg), a2 = w_odd(qg), a1 = w_even(q8), a3 = w_odd(q8);
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+          const uint4 b = in.b[s][nt];
+          if (ss == 0) {
+            imma_ss_z(dh[ti][nt], a0, a1, a2, a3, b.x, b.y);
+            imma_su_z(dl[ti][nt], a0, a1, a2, a3, b.z, b.w);
+          } else {
+            imma_ss(dh[ti][nt], a0, a1, a2, a3, b.x, b.y);
+            imma_su(dl[ti][nt], a0, a1, a2, a3, b.z, b.w);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int ti = 0; ti < kTPW; ti++)
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const int rr = e >> 1, c = e & 1;
+          const float f = (float)(dh[ti][nt][e] * 256 + dl[ti][nt][e]);
+          acc[ti][nt][e] = fmaf(in.ws[ti][rr][h] * in.as[nt][c], f, acc[ti][nt][e]);
+          if (HZ)
+            acc[ti][nt][e] = fmaf(in.wz[ti][rr][HZ ? h : 0], in.asum[nt][c][HZ ? h : 0], acc[ti][nt][e]);
+        }
   }
 }
 
@@ -292,19 +349,19 @@ __device__ void sk_producer(const SkParams& p, uint8_t* ring, SkSmem* L, int tot
   volatile int* abort = &L->abort;
   const int K = MODE == SK_GATEUP ? p.M : p.I;
   const int nk = (K + kKS - 1) / kKS;
-  const int gpr = K / p.gs;
-  const int ksplit = L->units[p.nseg + 1];
+  const uint32_t scb = 2u * (kKS / p.gs) * kBoxRows * 2;   // one stage's run of scales
+  const int ksplit = __ldg(p.units + p.nseg + 1);
   if (lane < 2) tma_prefetch_desc(&p.act_map[lane]);
   int slot = 0, item = 0;
   uint32_t phase = 0;
   const long long t_start = p.counters ? clock64() : 0;
   long long wait_cycles = 0;
   bool ok = true;
-  // Units are resolved from the shared-memory prefix; the segment record of
-  // the next unit is requested one unit ahead so its latency hides behind
+  // Units are resolved from the unit prefix (ascending); the segment record
+  // of the next unit is requested one unit ahead so its latency hides behind
   // the current unit's stages.
   int seg = 0;
-  while (L->units[seg + 1] <= (int)blockIdx.x) seg++;
+  while (__ldg(p.units + seg + 1) <= (int)blockIdx.x) seg++;
   WispSegment sg_next = p.segs[seg];
   int seg_next = seg;
   for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
@@ -312,11 +369,11 @@ __device__ void sk_producer(const SkParams& p, uint8_t* ring, SkSmem* L, int tot
     seg = seg_next;
     const int un = u + gridDim.x;
     if (un < total) {
-      while (L->units[seg_next + 1] <= un) seg_next++;
+      while (__ldg(p.units + seg_next + 1) <= un) seg_next++;
       sg_next = p.segs[seg_next];
     }
     const int chunks = (sg.rows + kCols - 1) / kCols;
-    const int l = u - L->units[seg];
+    const int l = u - __ldg(p.units + seg);
     // l = (row block * ksplit + K part) * chunks + chunk: the chunks of one
     // weight tile are consecutive units
     const int ch = l % chunks, rest = l / chunks;
@@ -325,7 +382,7 @@ __device__ void sk_producer(const SkParams& p, uint8_t* ring, SkSmem* L, int tot
     const int col0 = ch * kCols;
     const int n = min(kCols, sg.rows - col0);
     const int mi = n <= 8 ? 0 : 1;               // token box of 8 / 16 rows
-    const uint32_t bq = (8u << mi) * 128;        // bytes of one token quarter box
+    const uint32_t tb = (uint32_t)kQ16Lines * (8u << mi) * kQ16LineBytes;   // bytes of the token box
     const int row0 = rbk * (MODE == SK_GATEUP ? kBoxRows : 2 * kBoxRows);
     const int row1 = MODE == SK_GATEUP ? row0 : row0 + kBoxRows;
     const bool v1 = MODE == SK_GATEUP || row1 < p.M;
@@ -337,12 +394,11 @@ __device__ void sk_producer(const SkParams& p, uint8_t* ring, SkSmem* L, int tot
         reinterpret_cast<const CUtensorMap*>(p.prepared + p.p_maps_sk + (size_t)e0 * sizeof(CUtensorMap));
     const CUtensorMap* map1 =
         reinterpret_cast<const CUtensorMap*>(p.prepared + p.p_maps_sk + (size_t)e1 * sizeof(CUtensorMap));
-    const size_t t0off = (size_t)(row0 / kBoxRows) * gpr * kBoxRows * 2;
-    const size_t t1off = (size_t)(row1 / kBoxRows) * gpr * kBoxRows * 2;
-    const uint8_t* sc0 = p.prepared + p.p_scales + (size_t)e0 * p.p_mat_sc_bytes + t0off;
-    const uint8_t* sc1 = p.prepared + p.p_scales + (size_t)e1 * p.p_mat_sc_bytes + t1off;
-    const uint8_t* zr0 = p.prepared + p.p_zeros + (size_t)e0 * p.p_mat_sc_bytes + t0off;
-    const uint8_t* zr1 = p.prepared + p.p_zeros + (size_t)e1 * p.p_mat_sc_bytes + t1off;
+    // the unit's runs of weight scales (and zero points), one per stage
+    const size_t run0 = (size_t)sg.expert * (p.sk_gu_bytes + p.sk_dn_bytes) +
+                        (MODE == SK_GATEUP ? 0 : p.sk_gu_bytes) + (size_t)rbk * nk * scb;
+    const uint8_t* sc = p.prepared + p.p_sk_scales + run0;
+    const uint8_t* zr = p.prepared + p.p_sk_zeros + run0;
     StageHdr hdr;
     hdr.prow0 = sg.row_begin + col0;
     hdr.n = n;
@@ -355,11 +411,7 @@ __device__ void sk_producer(const SkParams& p, uint8_t* ring, SkSmem* L, int tot
       if (MODE == SK_GATEUP) tma_prefetch_desc(map1);
     }
     for (int kg = kg0; kg < kg1; kg++, item++) {
-      // quarters in this stage (the last one holds 2 when K % 256 == 128)
-      const int nq = min(kQ, (K - kg * kKS) / 64);
-      const uint32_t scb = (uint32_t)(nq * 64 / p.gs) * kBoxRows * 2;
-      const uint32_t bytes = (v1 ? 2 : 1) * kBoxBytes + nq * bq +
-                             scb * (1 + (v1 ? 1 : 0) + (hz0 ? 1 : 0) + (hz1 ? 1 : 0));
+      const uint32_t bytes = (v1 ? 2 : 1) * kBoxBytes + tb + scb * ((hz0 || hz1) ? 2 : 1);
       if (lane == 0 && item >= kStages) {
         const long long tw = p.counters ? clock64() : 0;
         ok = mbar_wait(&L->empty[slot], phase ^ 1, abort);
@@ -374,21 +426,16 @@ __device__ void sk_producer(const SkParams& p, uint8_t* ring, SkSmem* L, int tot
         mbar_arrive_expect_tx(fb, bytes);
       }
       __syncwarp();
-      const size_t goff = (size_t)(kg * kKS / p.gs) * kBoxRows * 2;
       if (lane < 2) {
         if (lane == 0 || v1)
           tma_load_2d(st + lane * kBoxBytes, lane ? map1 : map0, fb, kg * (kKS / 2),
                       lane ? row1 : row0);
-      } else if (lane < 2 + kQ) {
-        const int q = lane - 2;
-        if (q < nq)
-          tma_load_2d(st + kOffB + q * kBQBytes, &p.act_map[mi], fb, kg * kKS + q * 64, hdr.prow0);
-      } else if (lane == 2 + kQ) {
-        bulk_load(st + kOffS, sc0 + goff, scb, fb);
-        if (v1) bulk_load(st + kOffS + kScRun, sc1 + goff, scb, fb);
-      } else if (lane == 3 + kQ) {
-        if (hz0) bulk_load(st + kOffZ, zr0 + goff, scb, fb);
-        if (hz1) bulk_load(st + kOffZ + kScRun, zr1 + goff, scb, fb);
+      } else if (lane == 2) {
+        tma_load_3d(st + kOffB, &p.act_map[mi], fb, 0, hdr.prow0, kg * kQ16Lines);
+      } else if (lane == 3) {
+        bulk_load(st + kOffS, sc + (size_t)kg * scb, scb, fb);
+      } else if (lane == 4) {
+        if (hz0 || hz1) bulk_load(st + kOffZ, zr + (size_t)kg * scb, scb, fb);
       }
       if (++slot == kStages) { slot = 0; phase ^= 1; }
     }
@@ -406,120 +453,64 @@ __device__ void sk_producer(const SkParams& p, uint8_t* ring, SkSmem* L, int tot
   }
 }
 
-// One full stage for a unit of at most 8 tokens (the decode case): all of
-// the warp's nibbles, token fragments and scales are read first and the
-// stage is released before any conversion, so the producer can refill it
-// while the MMAs run (G scale groups per 256-K stage). Per quarter and tile
-// a 4-MMA chain (alternating register sets, so the next quarter's MMAs need
-// not wait for this quarter's fold) is folded into the accumulator times its
-// group's scale, then the zero-point term is added: the arithmetic, in the
-// same order, of the general path in sk_unit, so a token's result does not
-// depend on which path its unit took.
-template <int G>
-__device__ __forceinline__ void stage_single(float (&acc0)[2][4], float (&acc1)[2][4],
-                                             const uint8_t* st, int b0, int b1, int r0, int r1,
-                                             int g, int t, bool hz0, bool hz1, SkSmem* L, int slot,
-                                             int lane) {
-  constexpr int QPG = kQ / G;  // quarters per scale group
-  RawTile w0[kQ], w1[kQ];
-  BQuarter<1> bq[kQ];
-#pragma unroll
-  for (int q = 0; q < kQ; q++) {
-    load_tile(w0[q], st, b0, r0, b0, r0 + 8, q, t);
-    load_tile(w1[q], st, b1, r1, b1, r1 + 8, q, t);
-    load_b<1>(bq[q], st, q, g, t);
-  }
-  // scales and zero points of MMA rows g (low half) and g+8 (high half)
-  float2 s0[G], s1[G];
-  __half2 z0[G], z1[G];
-#pragma unroll
-  for (int j = 0; j < G; j++) {
-    s0[j] = make_float2(row_scale(st, kOffS, b0, j, r0), row_scale(st, kOffS, b0, j, r0 + 8));
-    s1[j] = make_float2(row_scale(st, kOffS, b1, j, r1), row_scale(st, kOffS, b1, j, r1 + 8));
-    z0[j] = hz0 ? __floats2half2_rn(row_scale(st, kOffZ, b0, j, r0), row_scale(st, kOffZ, b0, j, r0 + 8))
-                : __half2{};
-    z1[j] = hz1 ? __floats2half2_rn(row_scale(st, kOffZ, b1, j, r1), row_scale(st, kOffZ, b1, j, r1 + 8))
-                : __half2{};
-  }
+// One warp's arrival on an epilogue exchange barrier, then a bounded wait
+// for all kCW consumer warps.
+__device__ __forceinline__ bool epi_sync(SkSmem* L, int which, uint32_t parity, int lane) {
   __syncwarp();
-  if (lane == 0) mbar_arrive(&L->empty[slot]);
-
-  float c0[2][4], c1[2][4];
-#pragma unroll
-  for (int q = 0; q < kQ; q++) {
-    const int j = q / QPG, ci = q & 1;
-    __half2 ag0[2][4], a80[2][4], ag1[2][4], a81[2][4];
-    nib8_centered(w0[q].w[0].x, ag0[0]);
-    nib8_centered(w0[q].w[0].y, ag0[1]);
-    nib8_centered(w0[q].w[1].x, a80[0]);
-    nib8_centered(w0[q].w[1].y, a80[1]);
-    nib8_centered(w1[q].w[0].x, ag1[0]);
-    nib8_centered(w1[q].w[0].y, ag1[1]);
-    nib8_centered(w1[q].w[1].x, a81[0]);
-    nib8_centered(w1[q].w[1].y, a81[1]);
-#pragma unroll
-    for (int m = 0; m < 4; m++) {
-      const int wd = m >> 1, pp = 2 * (m & 1);
-      const uint32_t b0v = u4_get(bq[q].v[wd][0], pp), b1v = u4_get(bq[q].v[wd][0], pp + 1);
-      if (m == 0) {
-        hmma16816_z(c0[ci], h22u(ag0[wd][pp]), h22u(a80[wd][pp]), h22u(ag0[wd][pp + 1]),
-                    h22u(a80[wd][pp + 1]), b0v, b1v);
-        hmma16816_z(c1[ci], h22u(ag1[wd][pp]), h22u(a81[wd][pp]), h22u(ag1[wd][pp + 1]),
-                    h22u(a81[wd][pp + 1]), b0v, b1v);
-      } else {
-        hmma16816(c0[ci], h22u(ag0[wd][pp]), h22u(a80[wd][pp]), h22u(ag0[wd][pp + 1]),
-                  h22u(a80[wd][pp + 1]), b0v, b1v);
-        hmma16816(c1[ci], h22u(ag1[wd][pp]), h22u(a81[wd][pp]), h22u(ag1[wd][pp + 1]),
-                  h22u(a81[wd][pp + 1]), b0v, b1v);
-      }
-    }
-    const float2 f0 = s0[j], f1 = s1[j];
-    acc0[0][0] = fmaf(f0.x, c0[ci][0], acc0[0][0]);
-    acc0[0][1] = fmaf(f0.x, c0[ci][1], acc0[0][1]);
-    acc0[0][2] = fmaf(f0.y, c0[ci][2], acc0[0][2]);
-    acc0[0][3] = fmaf(f0.y, c0[ci][3], acc0[0][3]);
-    acc1[0][0] = fmaf(f1.x, c1[ci][0], acc1[0][0]);
-    acc1[0][1] = fmaf(f1.x, c1[ci][1], acc1[0][1]);
-    acc1[0][2] = fmaf(f1.y, c1[ci][2], acc1[0][2]);
-    acc1[0][3] = fmaf(f1.y, c1[ci][3], acc1[0][3]);
-    if (hz0 | hz1) {
-      float xs[1][2];
-      quarter_sums<1>(bq[q], xs, t);
-      const float2 g0 = __half22float2(z0[j]), g1 = __half22float2(z1[j]);
-      if (hz0) add_zeros<1>(acc0, xs, g0.x, g0.y);
-      if (hz1) add_zeros<1>(acc1, xs, g1.x, g1.y);
-    }
-  }
+  if (lane == 0) mbar_arrive(&L->epi[which]);
+  return mbar_wait(&L->epi[which], parity, &L->abort);
 }
 
 // ---------------------------------------------------------------------------
 // Consumer warps: one unit with NT n8 token tiles.
 // ---------------------------------------------------------------------------
-template <int MODE, int NT>
+template <int MODE, int NT, int GPS, bool HZ>
 __device__ bool sk_unit(const SkParams& p, uint8_t* ring, SkSmem* L, const StageHdr& hdr,
-                        int warp, int lane, int& slot, uint32_t& phase,
+                        int warp, int lane, int& slot, uint32_t& phase, uint32_t& epi_phase,
                         long long& wait_cycles) {
   volatile int* abort = &L->abort;
   const int g = lane >> 2, t = lane & 3;
   const int sig = ((g & 3) << 1) | (g >> 2);  // box row (mod 8) of MMA row g
   const int K = MODE == SK_GATEUP ? p.M : p.I;
-  const int qpg = p.gs / 64;  // quarters per scale group (1 or 2)
-  // Two tiles per warp; a tile's MMA rows g and g+8 are box rows r and r+8.
-  // GATEUP: gate rows 16w + sig (block 0) and the same up rows (block 1);
-  // DOWN: rows 32(w%4) + sig and +16 of block w/4.
-  const int b0 = MODE == SK_GATEUP ? 0 : warp >> 2;
-  const int b1 = MODE == SK_GATEUP ? 1 : warp >> 2;
-  const int r0 = (MODE == SK_GATEUP ? 16 * warp : 32 * (warp & 3)) + sig;
-  const int r1 = MODE == SK_GATEUP ? r0 : r0 + 16;
-  const bool active = MODE == SK_GATEUP || b0 == 0 || (hdr.flags & HF_V1);
-  const bool hz0 = hdr.flags & (b0 ? HF_HZ1 : HF_HZ0);
-  const bool hz1 = hdr.flags & (b1 ? HF_HZ1 : HF_HZ0);
+  // Rows of the warp's tiles (a tile's MMA rows g and g+8 sit 8 box rows
+  // apart, or in the gate and up blocks):
+  //   GATEUP, two tiles: gate rows 16w + sig, +8 (block 0) and the same up
+  //           rows (block 1); one tile: gate row 8w + sig as MMA row g, the
+  //           same up row as row g+8 -- either way a thread holds the gate
+  //           and up sums of its intermediate rows.
+  //   DOWN:   the warp's 16 * kTPW rows of block w / (kCW / 2).
+  Tile tl[kTPW];
+  const bool hz0 = hdr.flags & HF_HZ0, hz1 = hdr.flags & HF_HZ1;
+#pragma unroll
+  for (int ti = 0; ti < kTPW; ti++) {
+    if (MODE == SK_GATEUP) {
+      if (kTPW == 2) {
+        tl[ti].bg = tl[ti].b8 = ti;
+        tl[ti].rg = 16 * warp + sig;
+        tl[ti].r8 = tl[ti].rg + 8;
+      } else {
+        tl[ti].bg = 0;
+        tl[ti].b8 = 1;
+        tl[ti].rg = tl[ti].r8 = 8 * warp + sig;
+      }
+    } else {
+      const int wb = warp % (kCW / 2);
+      tl[ti].bg = tl[ti].b8 = warp / (kCW / 2);
+      tl[ti].rg = 16 * (kTPW * wb + ti) + sig;
+      tl[ti].r8 = tl[ti].rg + 8;
+    }
+    tl[ti].hzg = tl[ti].bg ? hz1 : hz0;
+    tl[ti].hz8 = tl[ti].b8 ? hz1 : hz0;
+  }
+  const bool active = MODE == SK_GATEUP || tl[0].bg == 0 || (hdr.flags & HF_V1);
 
-  float acc0[2][4], acc1[2][4];
+  float acc[kTPW][NT][4];
 #pragma unroll
-  for (int nt = 0; nt < 2; nt++)
+  for (int ti = 0; ti < kTPW; ti++)
 #pragma unroll
-    for (int e = 0; e < 4; e++) acc0[nt][e] = acc1[nt][e] = 0.f;
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) acc[ti][nt][e] = 0.f;
 
   // The down epilogue's token indices and router weights, requested now so
   // that their latency hides behind the unit's stages.
@@ -542,40 +533,27 @@ __device__ bool sk_unit(const SkParams& p, uint8_t* ring, SkSmem* L, const Stage
       if (p.counters) wait_cycles += clock64() - tw;
     }
     const uint8_t* st = ring + slot * kStageBytes;
-    const int nq = min(kQ, (K - (hdr.kg0 + kk) * kKS) / 64);
-    if (active && NT == 1 && nq == kQ) {
-      if (p.gs == 128)
-        stage_single<2>(acc0, acc1, st, b0, b1, r0, r1, g, t, hz0, hz1, L, slot, lane);
-      else
-        stage_single<4>(acc0, acc1, st, b0, b1, r0, r1, g, t, hz0, hz1, L, slot, lane);
+    const int ng = min(kAG, (K - (hdr.kg0 + kk) * kKS) / kQ16Block);
+    if (active && NT == 1 && ng == kAG) {
+      // Whole stage into registers, release, then the arithmetic.
+      GroupIn<NT, GPS, HZ> in[kAG];
+#pragma unroll
+      for (int j = 0; j < kAG; j++) load_group(in[j], st, 8 * NT, j, tl, g, t);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&L->empty[slot]);
+#pragma unroll
+      for (int j = 0; j < kAG; j++) compute_group(acc, in[j]);
     } else if (active) {
 #pragma unroll
-      for (int q = 0; q < kQ; q++) {
-        if (q < nq) {
-          RawTile w0, w1;
-          load_tile(w0, st, b0, r0, b0, r0 + 8, q, t);
-          load_tile(w1, st, b1, r1, b1, r1 + 8, q, t);
-          BQuarter<NT> bq;
-          load_b<NT>(bq, st, q, g, t);
-          const int grp = q / qpg;
-          const float sa = row_scale(st, kOffS, b0, grp, r0), sb = row_scale(st, kOffS, b0, grp, r0 + 8);
-          const float sc = row_scale(st, kOffS, b1, grp, r1), sd = row_scale(st, kOffS, b1, grp, r1 + 8);
-          const float za = hz0 ? row_scale(st, kOffZ, b0, grp, r0) : 0.f;
-          const float zb = hz0 ? row_scale(st, kOffZ, b0, grp, r0 + 8) : 0.f;
-          const float zc = hz1 ? row_scale(st, kOffZ, b1, grp, r1) : 0.f;
-          const float zd = hz1 ? row_scale(st, kOffZ, b1, grp, r1 + 8) : 0.f;
-          if (q == nq - 1) {
+      for (int j = 0; j < kAG; j++) {
+        if (j < ng) {
+          GroupIn<NT, GPS, HZ> in;
+          load_group(in, st, 8 * NT, j, tl, g, t);
+          if (j == ng - 1) {
             __syncwarp();
             if (lane == 0) mbar_arrive(&L->empty[slot]);
           }
-          tile_quarter<NT>(acc0, w0, bq, sa, sb);
-          tile_quarter<NT>(acc1, w1, bq, sc, sd);
-          if (hz0 | hz1) {
-            float xs[NT][2];
-            quarter_sums<NT>(bq, xs, t);
-            if (hz0) add_zeros<NT>(acc0, xs, za, zb);
-            if (hz1) add_zeros<NT>(acc1, xs, zc, zd);
-          }
+          compute_group(acc, in);
         }
       }
     } else {
@@ -586,30 +564,111 @@ __device__ bool sk_unit(const SkParams& p, uint8_t* ring, SkSmem* L, const Stage
   }
   if (!active) return true;
 
-  // Epilogue. acc[nt][0..1]: MMA row g (box row r), columns 2t, 2t+1;
-  // [2..3]: MMA row g+8 (box row r+8).
+  // Epilogue. acc[tile][nt][0..1]: MMA row g, columns 2t, 2t+1; [2..3]: row g+8.
+  if (MODE == SK_GATEUP) {
+    // h = silu(gate) * up for the thread's kTPW intermediate rows
+    // (i = row0 + hrow[q]) and its columns.
+    constexpr int NH = kTPW;
+    float hv[NH][NT][2];
+    int hrow[NH];
 #pragma unroll
-  for (int nt = 0; nt < NT; nt++) {
+    for (int q = 0; q < NH; q++) {
+      hrow[q] = kTPW == 2 ? 16 * warp + 8 * q + sig : 8 * warp + sig;
 #pragma unroll
-    for (int e = 0; e < 4; e++) {
-      const int j = e & 1, col = nt * 8 + 2 * t + j;
-      if (col >= hdr.n) continue;
-      const int rr = (e >> 1) ? 8 : 0;
-      const int prow = hdr.prow0 + col;
-      if (MODE == SK_GATEUP) {
-        const int i = hdr.row0 + r0 + rr;
-        const float hv = silu(acc0[nt][e]) * acc1[nt][e];
-        p.h_out[(size_t)prow * p.I + k_interleave_slot(i)] = __float2half(hv);
-      } else {
-        const int base = hdr.row0 + b0 * kBoxRows;
-        const int ma = base + r0 + rr, mb = base + r1 + rr;
-        const float y0 = acc0[nt][e], y1 = acc1[nt][e];
-        if (p.mode == 0) {
-          red_add_f32(p.out + (size_t)tok[nt][j] * p.M + ma, wgt[nt][j] * y0);
-          red_add_f32(p.out + (size_t)tok[nt][j] * p.M + mb, wgt[nt][j] * y1);
-        } else {
-          p.out[(size_t)prow * p.M + ma] = y0;
-          p.out[(size_t)prow * p.M + mb] = y1;
+      for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int c = 0; c < 2; c++)
+          hv[q][nt][c] = kTPW == 2 ? silu(acc[0][nt][2 * q + c]) * acc[kTPW - 1][nt][2 * q + c]
+                                   : silu(acc[0][nt][c]) * acc[0][nt][2 + c];
+    }
+    // Column maxima over the unit's 128 rows: the warp's, then all warps
+    // through shared memory.
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+      for (int c = 0; c < 2; c++) {
+        float m = 0.f;
+#pragma unroll
+        for (int q = 0; q < NH; q++) m = fmaxf(m, fabsf(hv[q][nt][c]));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+        if (g == 0) L->red_max[warp][nt * 8 + 2 * t + c] = m;
+      }
+    if (!epi_sync(L, 0, epi_phase, lane)) return false;
+    float mx[NT][2];
+    int vq[NH][NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+      for (int c = 0; c < 2; c++) {
+        float m = 0.f;
+#pragma unroll
+        for (int w = 0; w < kCW; w++) m = fmaxf(m, L->red_max[w][nt * 8 + 2 * t + c]);
+        mx[nt][c] = m;
+        const float inv = m > 0.f ? 32767.f / m : 0.f;
+        int s = 0;
+#pragma unroll
+        for (int q = 0; q < NH; q++) {
+          vq[q][nt][c] = max(-32767, min(32767, __float2int_rn(hv[q][nt][c] * inv)));
+          s += vq[q][nt][c];
+        }
+        // the warp's 8 * NH rows lie in one 64-K half of the block
+        s += __shfl_xor_sync(0xffffffffu, s, 4);
+        s += __shfl_xor_sync(0xffffffffu, s, 8);
+        s += __shfl_xor_sync(0xffffffffu, s, 16);
+        if (g == 0) L->red_sum[warp][nt * 8 + 2 * t + c] = s;
+      }
+    if (!epi_sync(L, 1, epi_phase, lane)) return false;
+    epi_phase ^= 1;
+    const int rbk = hdr.row0 / kQ16Block;          // the unit's q16 block of H
+    const size_t rbytes = q16_row_bytes(p.I);
+    size_t hb[NH];                                 // byte of each row's K index
+#pragma unroll
+    for (int q = 0; q < NH; q++) {
+      const int i = hdr.row0 + hrow[q];
+      hb[q] = q16_word_offset(i >> 3) + (sig & 1) * 4 + (sig >> 1);
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+      for (int c = 0; c < 2; c++) {
+        const int col = nt * 8 + 2 * t + c;
+        if (col >= hdr.n) continue;
+        uint8_t* hr = p.hq + (size_t)(hdr.prow0 + col) * rbytes;
+#pragma unroll
+        for (int q = 0; q < NH; q++) {
+          const int v = vq[q][nt][c];
+          hr[hb[q]] = (uint8_t)((v >> 8) & 0xFF);
+          hr[hb[q] + 8] = (uint8_t)(v & 0xFF);
+        }
+        if (warp == 0 && g == 0) {
+          int s0 = 0, s1 = 0;
+#pragma unroll
+          for (int w = 0; w < kCW / 2; w++) {
+            s0 += L->red_sum[w][col];
+            s1 += L->red_sum[kCW / 2 + w][col];
+          }
+          const float sc = mx[nt][c] / 32767.f;
+          *reinterpret_cast<float4*>(hr + q16_meta_offset(rbk)) =
+              make_float4(sc * 0.0625f, sc * (float)s0, sc * (float)s1, 0.f);
+        }
+      }
+  } else {
+#pragma unroll
+    for (int ti = 0; ti < kTPW; ti++) {
+      const int mg = hdr.row0 + tl[ti].bg * kBoxRows + tl[ti].rg;   // output row of MMA row g
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const int j = e & 1, col = nt * 8 + 2 * t + j;
+          if (col >= hdr.n) continue;
+          const int m = mg + 8 * (e >> 1);
+          if (p.mode == 0)
+            red_add_f32(p.out + (size_t)tok[nt][j] * p.M + m, wgt[nt][j] * acc[ti][nt][e]);
+          else
+            p.out[(size_t)(hdr.prow0 + col) * p.M + m] = acc[ti][nt][e];
         }
       }
     }
@@ -617,12 +676,41 @@ __device__ bool sk_unit(const SkParams& p, uint8_t* ring, SkSmem* L, const Stage
   return true;
 }
 
+// Units of experts with zero points or a 64-K scale group (neither occurs
+// in the benchmark configurations) run out of line, so their extra
+// registers do not raise the pressure on the common path.
+template <int MODE, int NT, int GPS, bool HZ>
+__device__ __noinline__ bool sk_unit_cold(const SkParams& p, uint8_t* ring, SkSmem* L,
+                                          const StageHdr& hdr, int warp, int lane, int& slot,
+                                          uint32_t& phase, uint32_t& epi_phase,
+                                          long long& wait_cycles) {
+  return sk_unit<MODE, NT, GPS, HZ>(p, ring, L, hdr, warp, lane, slot, phase, epi_phase, wait_cycles);
+}
+
+template <int MODE, int GPS>
+__device__ __forceinline__ bool sk_unit_any(const SkParams& p, uint8_t* ring, SkSmem* L,
+                                            const StageHdr& hdr, int warp, int lane, int& slot,
+                                            uint32_t& phase, uint32_t& epi_phase,
+                                            long long& wait_cycles) {
+  const bool hz = hdr.flags & (HF_HZ0 | HF_HZ1);
+  if (GPS == 1 && !hz) {
+    if (hdr.n <= 8)
+      return sk_unit<MODE, 1, GPS, false>(p, ring, L, hdr, warp, lane, slot, phase, epi_phase, wait_cycles);
+    return sk_unit<MODE, 2, GPS, false>(p, ring, L, hdr, warp, lane, slot, phase, epi_phase, wait_cycles);
+  }
+  if (hdr.n <= 8)
+    return hz ? sk_unit_cold<MODE, 1, GPS, true>(p, ring, L, hdr, warp, lane, slot, phase, epi_phase, wait_cycles)
+              : sk_unit_cold<MODE, 1, GPS, false>(p, ring, L, hdr, warp, lane, slot, phase, epi_phase, wait_cycles);
+  return hz ? sk_unit_cold<MODE, 2, GPS, true>(p, ring, L, hdr, warp, lane, slot, phase, epi_phase, wait_cycles)
+            : sk_unit_cold<MODE, 2, GPS, false>(p, ring, L, hdr, warp, lane, slot, phase, epi_phase, wait_cycles);
+}
+
 template <int MODE>
 __device__ void sk_consumer(const SkParams& p, uint8_t* ring, SkSmem* L, int total, int warp,
                             int lane) {
   volatile int* abort = &L->abort;
   int slot = 0;
-  uint32_t phase = 0;
+  uint32_t phase = 0, epi_phase = 0;
   const long long t_start = p.counters ? clock64() : 0;
   long long wait_cycles = 0;
   for (int u = blockIdx.x; u < total; u += gridDim.x) {
@@ -630,9 +718,9 @@ __device__ void sk_consumer(const SkParams& p, uint8_t* ring, SkSmem* L, int tot
     if (!mbar_wait(&L->full[slot], phase, abort)) return;
     if (p.counters) wait_cycles += clock64() - tw;
     const StageHdr hdr = L->hdr[slot];
-    bool ok;
-    if (hdr.n <= 8) ok = sk_unit<MODE, 1>(p, ring, L, hdr, warp, lane, slot, phase, wait_cycles);
-    else ok = sk_unit<MODE, 2>(p, ring, L, hdr, warp, lane, slot, phase, wait_cycles);
+    const bool ok = p.gs == 128
+        ? sk_unit_any<MODE, 1>(p, ring, L, hdr, warp, lane, slot, phase, epi_phase, wait_cycles)
+        : sk_unit_any<MODE, 2>(p, ring, L, hdr, warp, lane, slot, phase, epi_phase, wait_cycles);
     if (!ok) return;
   }
   if (p.counters && lane == 0) {
@@ -654,10 +742,11 @@ __global__ void __launch_bounds__(kThreads, 1) skinny_ffn_kernel(const __grid_co
       mbar_init(&L->full[i], 1);
       mbar_init(&L->empty[i], kCW);
     }
+    mbar_init(&L->epi[0], kCW);
+    mbar_init(&L->epi[1], kCW);
     L->abort = 0;
     fence_barrier_init();
   }
-  for (int i = threadIdx.x; i <= p.nseg + 1; i += blockDim.x) L->units[i] = __ldg(p.units + i);
   const uint32_t* zb = reinterpret_cast<const uint32_t*>(p.prepared + p.p_zbits);
   for (int w = threadIdx.x; w < (p.n_entries * 3 + 31) / 32; w += blockDim.x) L->zbits[w] = __ldg(zb + w);
   __syncthreads();
@@ -675,26 +764,6 @@ static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 }  // namespace
 
 namespace wb {
-
-struct SkLaunch {
-  const uint8_t* prepared;
-  size_t p_maps_sk, p_zbits, p_scales, p_zeros, p_mat_sc_bytes;
-  const WispSegment* segs;
-  int nseg;
-  int n_entries;
-  const int32_t* units_gu;
-  const int32_t* units_dn;
-  int M, I, gs;
-  const CUtensorMap* xp_maps;  // [2]: boxes of 8 / 16 rows
-  const CUtensorMap* h_maps;   // [2]
-  __half* h;
-  const int* row_token;
-  const float* row_weight;
-  float* out;
-  int mode;
-  int* error_flag;
-  unsigned long long* counters;
-};  // mirrored in grouped.cu
 
 int skinny_max_rows() { return kSkMaxRows; }
 int skinny_max_segs() { return kMaxSegs; }
@@ -717,23 +786,24 @@ cudaError_t launch_skinny(const SkLaunch& L, int phase, int grid, cudaStream_t s
   p.prepared = L.prepared;
   p.p_maps_sk = L.p_maps_sk;
   p.p_zbits = L.p_zbits;
-  p.p_scales = L.p_scales;
-  p.p_zeros = L.p_zeros;
-  p.p_mat_sc_bytes = L.p_mat_sc_bytes;
+  p.p_sk_scales = L.p_sk_scales;
+  p.p_sk_zeros = L.p_sk_zeros;
+  p.sk_gu_bytes = L.sk_gu_bytes;
+  p.sk_dn_bytes = L.sk_dn_bytes;
   p.segs = L.segs;
   p.nseg = L.nseg;
   p.n_entries = L.n_entries;
   p.M = L.M;
   p.I = L.I;
   p.gs = L.gs;
-  p.h_out = L.h;
+  p.hq = L.hq;
   p.row_token = L.row_token;
   p.row_weight = L.row_weight;
   p.out = L.out;
   p.mode = L.mode;
   p.error_flag = L.error_flag;
   p.counters = L.counters ? L.counters + phase * SC_COUNT : nullptr;
-  const CUtensorMap* maps = phase == 0 ? L.xp_maps : L.h_maps;
+  const CUtensorMap* maps = phase == 0 ? L.xq_maps : L.hq_maps;
   for (int i = 0; i < 2; i++) p.act_map[i] = maps[i];
   if (phase == 0) {
     p.units = L.units_gu;

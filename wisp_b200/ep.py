@@ -112,7 +112,7 @@ class CudaOps:
         abi.call("wisp_b200_pack_rows", x.data_ptr(), None if src is None else src.data_ptr(),
                  n_rows, x.shape[1], xp.data_ptr(), _stream())
 
-    def grouped(self, cfg, lw, segs, rows, xp, h, mode, row_token, row_weight, out, tiles, flag):
+    def grouped(self, cfg, lw, segs, rows, xp, h, mode, row_token, row_weight, out, ws, flag):
         dsegs = _segments_tensor(segs, xp.device)
         abi.call("wisp_b200_grouped_ffn", C.byref(cfg), lw.prepare().data_ptr(), lw.table.data_ptr(),
                  lw.n_entries,
@@ -120,7 +120,7 @@ class CudaOps:
                  max(rows, 1), xp.data_ptr(), h.data_ptr(), mode,
                  None if row_token is None else row_token.data_ptr(),
                  None if row_weight is None else row_weight.data_ptr(), out.data_ptr(),
-                 tiles.data_ptr(), flag.data_ptr(), _stream())
+                 ws.data_ptr(), ws.numel(), flag.data_ptr(), _stream())
 
     def combine(self, y, row_token, row_weight, n_rows, out):
         abi.call("wisp_b200_combine_rows", y.data_ptr(), row_token.data_ptr(), row_weight.data_ptr(),
@@ -140,12 +140,24 @@ class CudaOps:
                  src_pos.data_ptr(), total.data_ptr(), max_rows, sorted_rows.data_ptr(), _stream())
 
     def grouped_dev(self, cfg, lw, segs, n_segs, rows, xp, h, mode, row_token, row_weight, out,
-                    tiles, flag):
+                    ws, flag):
         abi.call("wisp_b200_grouped_ffn", C.byref(cfg), lw.prepare().data_ptr(), lw.table.data_ptr(),
                  lw.n_entries, segs.data_ptr(), n_segs, max(rows, 1), xp.data_ptr(), h.data_ptr(),
                  mode, None if row_token is None else row_token.data_ptr(),
                  None if row_weight is None else row_weight.data_ptr(), out.data_ptr(),
-                 tiles.data_ptr(), flag.data_ptr(), _stream())
+                 ws.data_ptr(), ws.numel(), flag.data_ptr(), _stream())
+
+    def workspace(self, cfg, n_segs, rows, device):
+        n = abi.lib().wisp_b200_grouped_workspace_bytes(C.byref(cfg), n_segs, max(rows, 1))
+        if n == 0:
+            raise RuntimeError(f"wisp engine error [{abi.WISP_ERR_INVALID_ARG}]: grouped workspace query failed")
+        return torch.empty(n, dtype=torch.uint8, device=device)
+
+    def clear_flag(self, flag):
+        flag.zero_()
+
+    def check_flag(self, flag):
+        abi.call("wisp_b200_check_error_flag", flag.data_ptr(), _stream())
 
     def ep_combine(self, yback, slot, tokens, world, cap, out):
         abi.call("wisp_b200_ep_combine", yback.data_ptr(), slot.data_ptr(), tokens, world, cap,
@@ -222,8 +234,9 @@ class EpLayer:
         self.total = torch.zeros(1, dtype=torch.int32, device=dev)
         self.n_rsegs = self.e_loc
         self.rsegs = torch.empty(16 * self.n_rsegs, dtype=torch.uint8, device=dev)
-        self.tiles = torch.empty(abi.lib().wisp_b200_tiles_words(self.n_rsegs + 1)
-                                 if adt == torch.float16 else 1, dtype=torch.int32, device=dev)
+        # one grouped-FFN workspace serves both calls of a layer (the shared
+        # expert's single segment of T rows, then the local experts)
+        self.gws = self.ops.workspace(self.cfg_loc, max(self.n_rsegs, 1), max(RK, T), dev)
         if spec.has_shared:
             self.xs = torch.empty((T, M), dtype=adt, device=dev)
             self.sh_token = torch.arange(T, dtype=torch.int32, device=dev)
@@ -233,35 +246,90 @@ class EpLayer:
             seg.expert, seg.row_begin, seg.rows = self.e_loc, 0, T
             self.sh_seg.copy_(torch.frombuffer(bytearray(bytes(seg)), dtype=torch.uint8))
 
-    def forward(self, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
-        """x: bf16 [T, M] (this rank's tokens) -> out fp32 [T, M]."""
-        spec, ops, T, k, world = self.spec, self.ops, self.T, self.spec.top_k, self.world
-        M = spec.hidden
+    # One layer is four local phases around two all-to-alls; forward() runs
+    # them over the process group, and a single-process caller can run the
+    # phases of several ranks itself with the exchanges done as copies
+    # (loopback_forward).
+
+    def dispatch_phase(self, x: torch.Tensor, out: torch.Tensor) -> None:
+        """Route this rank's tokens and fill the send blocks; zero the output
+        and the device error word."""
+        spec, ops = self.spec, self.ops
+        ops.clear_flag(self.flag)
         ops.route(self.cfg_route, self.lw, x, self.idx, self.w, self.logits)
         ops.plan(self.cfg_route, self.idx, self.w, self.counts, self.segs, self.row_token,
                  self.row_weight)
         ops.dispatch(x, self.idx, self.segs, self.row_token, self.row_weight, spec.n_experts,
-                     world, self.cap, self.send, self.slot)
-        # 1. the blocks to the owners; the shared expert runs on this rank's
-        #    own tokens while they travel
-        w_rows = dist.all_to_all_single(self.recv, self.send, group=self.group, async_op=True)
+                     self.world, self.cap, self.send, self.slot)
         out.zero_()
-        if spec.has_shared:
-            ops.pack(x, None, T, self.xs)
-            ops.grouped_dev(self.cfg_loc, self.lw, self.sh_seg, 1, T, self.xs, self.hr, 0,
-                            self.sh_token, self.sh_weight, out, self.tiles, self.flag)
-        w_rows.wait()
-        # 2. local experts over the received rows, gathered so that each
-        #    expert is one segment; the FFN adds w * y of every local expert
-        #    of a received token into that token's fp32 row
-        ops.recv_plan(self.recv, world, self.e_loc, self.cap, k, M, self.rsegs, self.src_pos,
+
+    def shared_phase(self, x: torch.Tensor, out: torch.Tensor) -> None:
+        """The shared expert on this rank's own tokens, added into out."""
+        if self.spec.has_shared:
+            T = self.T
+            self.ops.pack(x, None, T, self.xs)
+            self.ops.grouped_dev(self.cfg_loc, self.lw, self.sh_seg, 1, T, self.xs, self.hr, 0,
+                                 self.sh_token, self.sh_weight, out, self.gws, self.flag)
+
+    def expert_phase(self) -> None:
+        """Local experts over the received rows, gathered so that each expert
+        is one segment; the FFN adds w * y of every local expert of a received
+        token into that token's fp32 return row."""
+        ops, k, M = self.ops, self.spec.top_k, self.spec.hidden
+        ops.recv_plan(self.recv, self.world, self.e_loc, self.cap, k, M, self.rsegs, self.src_pos,
                       self.gw, self.total)
-        ops.gather_rows(self.recv, world, self.e_loc, self.cap, k, M, self.src_pos, self.total,
+        ops.gather_rows(self.recv, self.world, self.e_loc, self.cap, k, M, self.src_pos, self.total,
                         self.rk, self.xsorted)
         self.yr.zero_()
         ops.grouped_dev(self.cfg_loc, self.lw, self.rsegs, self.n_rsegs, self.rk, self.xsorted,
-                        self.hr, 0, self.src_pos, self.gw, self.yr, self.tiles, self.flag)
+                        self.hr, 0, self.src_pos, self.gw, self.yr, self.gws, self.flag)
+
+    def combine_phase(self, out: torch.Tensor) -> None:
+        """Each token adds its returned rows from the owners, in rank order."""
+        self.ops.ep_combine(self.yback, self.slot, self.T, self.world, self.cap, out)
+
+    def forward(self, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """x: bf16 [T, M] (this rank's tokens) -> out fp32 [T, M]."""
+        self.dispatch_phase(x, out)
+        # 1. the blocks to the owners; the shared expert runs on this rank's
+        #    own tokens while they travel
+        w_rows = dist.all_to_all_single(self.recv, self.send, group=self.group, async_op=True)
+        self.shared_phase(x, out)
+        w_rows.wait()
+        # 2. local experts over the received rows
+        self.expert_phase()
         # 3. the rows back to their tokens' ranks, added in rank order
         dist.all_to_all_single(self.yback, self.yr, group=self.group)
-        ops.ep_combine(self.yback, self.slot, T, world, self.cap, out)
+        self.combine_phase(out)
         return out
+
+    def check(self) -> None:
+        """Raise (WISP_ERR_TIMEOUT) if a kernel of the last forward gave up a
+        bounded wait; synchronises the current stream."""
+        self.ops.check_flag(self.flag)
+
+
+def loopback_forward(layers: list, xs: list, outs: list) -> None:
+    """Runs one layer of every rank of an expert-parallel group inside one
+    process: layers[r] / xs[r] / outs[r] belong to rank r. The two
+    all-to-alls become copies with all_to_all_single's block semantics
+    (block q of rank r's send buffer is block r of rank q's receive
+    buffer), so every device kernel of the exchange runs exactly as it does
+    across GPUs."""
+    W = len(layers)
+    for r in range(W):
+        layers[r].dispatch_phase(xs[r], outs[r])
+    nb = layers[0].layout.bytes
+    for r in range(W):
+        for q in range(W):
+            layers[q].recv[r * nb:(r + 1) * nb].copy_(layers[r].send[q * nb:(q + 1) * nb])
+    for r in range(W):
+        layers[r].shared_phase(xs[r], outs[r])
+    for r in range(W):
+        layers[r].expert_phase()
+    cap = layers[0].cap
+    for r in range(W):
+        for q in range(W):
+            layers[q].yback[r * cap:(r + 1) * cap].copy_(layers[r].yr[q * cap:(q + 1) * cap])
+    for r in range(W):
+        layers[r].combine_phase(outs[r])
