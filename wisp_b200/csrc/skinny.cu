@@ -219,21 +219,91 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, long 
     if (clock64() - t0 > limit) return;
 }
 
-// Scale (or zero point) of box row `row` of a block for scale group grp of
-// the stage (G groups per block in the stage's run).
-template <int G>
-__device__ __forceinline__ float row_scale(const uint8_t* st, int off, int block, int grp,
-                                           int row) {
-  return __half2float(
-      reinterpret_cast<const __half*>(st + off)[(block * G + grp) * kBoxRows + row]);
+// Shared-memory loads on 32-bit shared addresses (base + per-thread offset
+// + a compile-time constant, which the assembler folds into the instruction).
+__device__ __forceinline__ uint2 lds_v2(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint4 lds_v4(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float lds_f32(uint32_t a) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float lds_h2f(uint32_t a) {
+  unsigned short h;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(a));
+  return __half2float(__ushort_as_half(h));
 }
 
-// A warp's MMA tile: MMA row g is box row rg of weight block bg, row g+8 box
-// row r8 of block b8.
-struct Tile {
-  int bg, rg, b8, r8;
-  bool hzg, hz8;
+// Where a warp's MMA tiles sit in a stage. Tile 0's MMA row g is box row
+// rg0 of weight block bg0; the other rows differ by compile-time steps:
+//   GATEUP, two tiles: tile ti = block ti (gate, up), rows rg0 and rg0 + 8;
+//           one tile: MMA row g = gate row rg0, row g+8 = the same up row
+//           (block 1) -- either way a thread holds the gate and up sums of
+//           its intermediate rows;
+//   DOWN:   two tiles: rows rg0 (+8) and rg0 + 16 (+8); one tile: rg0 (+8).
+// Byte steps of (tile, MMA row g / g+8) in the weight boxes and in the
+// stage's run of scales (G scale groups per block and stage).
+template <int MODE>
+__device__ __forceinline__ constexpr uint32_t box_step(int ti, int rr) {
+  return MODE == SK_GATEUP ? (kTPW == 2 ? 16384u * ti + 1024u * rr : 16384u * rr)
+                           : (kTPW == 2 ? 2048u * ti + 1024u * rr : 1024u * rr);
+}
+template <int MODE, int G>
+__device__ __forceinline__ constexpr uint32_t scale_step(int ti, int rr) {
+  return MODE == SK_GATEUP ? (kTPW == 2 ? (uint32_t)G * 256u * ti + 16u * rr : (uint32_t)G * 256u * rr)
+                           : (kTPW == 2 ? 32u * ti + 16u * rr : 16u * rr);
+}
+// Weight block of (tile, row): GATEUP two tiles -> ti, one tile -> rr; DOWN -> bg0.
+template <int MODE>
+__device__ __forceinline__ constexpr int block_of(int ti, int rr) {
+  return MODE == SK_GATEUP ? (kTPW == 2 ? ti : rr) : 0;
+}
+
+// Per-thread stage offsets (bytes from the stage base), fixed for a warp.
+struct ThreadOffs {
+  uint32_t a[2][2];   // [group j][words 2t,2t+1 / 8+2t,9+2t] of tile 0's row g
+  uint32_t sc;        // tile 0 row g's scale in the stage's run
+  uint32_t b[2];      // [s % 2]: token row g's chunk 2t + s%2 (before the line offset)
+  uint32_t m[2][2];   // [c][j]: metadata of token row 2t + c for group j (before the line offset)
+  int bg0, rg0;
 };
+
+template <int MODE>
+__device__ __forceinline__ ThreadOffs thread_offs(int warp, int lane, int G) {
+  const int g = lane >> 2, t = lane & 3;
+  const int sig = ((g & 3) << 1) | (g >> 2);  // box row (mod 8) of MMA row g
+  ThreadOffs o;
+  if (MODE == SK_GATEUP) {
+    o.bg0 = 0;
+    o.rg0 = (kTPW == 2 ? 16 : 8) * warp + sig;
+  } else {
+    o.bg0 = warp / (kCW / 2);
+    o.rg0 = 16 * kTPW * (warp % (kCW / 2)) + sig;
+  }
+#pragma unroll
+  for (int j = 0; j < 2; j++)
+#pragma unroll
+    for (int h = 0; h < 2; h++)
+      o.a[j][h] = o.bg0 * kBoxBytes + o.rg0 * 128 + 8 * (t & 1) +
+                  ((((4 * j + 2 * h + (t >> 1)) ^ sig) & 7) << 4);
+  o.sc = (uint32_t)(o.bg0 * G * kBoxRows + o.rg0) * 2;
+#pragma unroll
+  for (int u = 0; u < 2; u++) o.b[u] = g * 128 + (((2 * t + u) ^ g) << 4);
+#pragma unroll
+  for (int c = 0; c < 2; c++)
+#pragma unroll
+    for (int j = 0; j < 2; j++) o.m[c][j] = (2 * t + c) * 128 + ((j ^ (2 * t + c)) << 4);
+  return o;
+}
 
 // Everything one 128-K activation group of a stage contributes to a warp's
 // tiles, in registers. GPS = weight scale groups per activation group (1:
@@ -248,51 +318,47 @@ struct GroupIn {
   float asum[NT][2][HZ ? GPS : 1];       // activation sums over each scale group
 };
 
-// Loads activation group j of the stage at `st`; the stage's token rows are
-// [5 lines][brows rows][128 bytes] (lines 2j, 2j+1: group j's values; line
-// 4: the rows' block metadata).
-template <int NT, int GPS, bool HZ>
-__device__ __forceinline__ void load_group(GroupIn<NT, GPS, HZ>& in, const uint8_t* st, int brows,
-                                           int j, const Tile (&tl)[kTPW], int g, int t) {
+// Loads activation group j of the stage at shared address st. The stage's
+// token rows are [5 lines][8 NT rows][128 bytes] (lines 2j, 2j+1: group j's
+// values; line 4: the rows' block metadata).
+template <int MODE, int NT, int GPS, bool HZ>
+__device__ __forceinline__ void load_group(GroupIn<NT, GPS, HZ>& in, uint32_t st, int j,
+                                           const ThreadOffs& o, bool hz0, bool hz1) {
   constexpr int G = 2 * GPS;  // weight scale groups per 256-K stage
+  constexpr int BR = 8 * NT;  // token rows in the box
 #pragma unroll
   for (int ti = 0; ti < kTPW; ti++)
 #pragma unroll
     for (int rr = 0; rr < 2; rr++) {
-      const int blk = rr ? tl[ti].b8 : tl[ti].bg, row = rr ? tl[ti].r8 : tl[ti].rg;
-      const uint8_t* base = st + blk * kBoxBytes + row * 128 + 8 * (t & 1);
-      const int sw = row & 7;
-      in.a[ti][rr][0] = *reinterpret_cast<const uint2*>(base + (((4 * j + (t >> 1)) ^ sw) << 4));
-      in.a[ti][rr][1] = *reinterpret_cast<const uint2*>(base + (((4 * j + 2 + (t >> 1)) ^ sw) << 4));
+      const uint32_t bs = box_step<MODE>(ti, rr);
+      in.a[ti][rr][0] = lds_v2(st + o.a[j][0] + bs);
+      in.a[ti][rr][1] = lds_v2(st + o.a[j][1] + bs);
+      const uint32_t ss = scale_step<MODE, G>(ti, rr);
 #pragma unroll
       for (int h = 0; h < GPS; h++) {
-        in.ws[ti][rr][h] = row_scale<G>(st, kOffS, blk, j * GPS + h, row);
-        if (HZ)
-          in.wz[ti][rr][HZ ? h : 0] =
-              (rr ? tl[ti].hz8 : tl[ti].hzg) ? row_scale<G>(st, kOffZ, blk, j * GPS + h, row) : 0.f;
+        in.ws[ti][rr][h] = lds_h2f(st + kOffS + o.sc + ss + (j * GPS + h) * 256);
+        if (HZ) {
+          const bool hz = (MODE == SK_GATEUP ? block_of<MODE>(ti, rr) : o.bg0) ? hz1 : hz0;
+          in.wz[ti][rr][HZ ? h : 0] = hz ? lds_h2f(st + kOffZ + o.sc + ss + (j * GPS + h) * 256) : 0.f;
+        }
       }
     }
 #pragma unroll
   for (int s = 0; s < 4; s++)
 #pragma unroll
-    for (int nt = 0; nt < NT; nt++) {
-      const int r = nt * 8 + g;
-      in.b[s][nt] = *reinterpret_cast<const uint4*>(
-          st + kOffB + ((2 * j + (s >> 1)) * brows + r) * 128 + (((2 * t + (s & 1)) ^ (r & 7)) << 4));
-    }
+    for (int nt = 0; nt < NT; nt++)
+      in.b[s][nt] = lds_v4(st + o.b[s & 1] + kOffB + ((2 * j + (s >> 1)) * BR + 8 * nt) * 128);
 #pragma unroll
   for (int nt = 0; nt < NT; nt++)
 #pragma unroll
     for (int c = 0; c < 2; c++) {
-      const int r = nt * 8 + 2 * t + c;
-      const float* m = reinterpret_cast<const float*>(
-          st + kOffB + ((kQ16Lines - 1) * brows + r) * 128 + ((j ^ (r & 7)) << 4));
-      in.as[nt][c] = m[0];
+      const uint32_t m = st + o.m[c][j] + kOffB + ((kQ16Lines - 1) * BR + 8 * nt) * 128;
+      in.as[nt][c] = lds_f32(m);
       if (HZ) {
-        if (GPS == 1) in.asum[nt][c][0] = m[1] + m[2];
+        if (GPS == 1) in.asum[nt][c][0] = lds_f32(m + 4) + lds_f32(m + 8);
         else
 #pragma unroll
-          for (int h = 0; h < GPS; h++) in.asum[nt][c][HZ ? h : 0] = m[1 + h];
+          for (int h = 0; h < GPS; h++) in.asum[nt][c][HZ ? h : 0] = lds_f32(m + 4 + 4 * h);
       }
     }
 }
@@ -472,37 +538,9 @@ __device__ bool sk_unit(const SkParams& p, uint8_t* ring, SkSmem* L, const Stage
   const int g = lane >> 2, t = lane & 3;
   const int sig = ((g & 3) << 1) | (g >> 2);  // box row (mod 8) of MMA row g
   const int K = MODE == SK_GATEUP ? p.M : p.I;
-  // Rows of the warp's tiles (a tile's MMA rows g and g+8 sit 8 box rows
-  // apart, or in the gate and up blocks):
-  //   GATEUP, two tiles: gate rows 16w + sig, +8 (block 0) and the same up
-  //           rows (block 1); one tile: gate row 8w + sig as MMA row g, the
-  //           same up row as row g+8 -- either way a thread holds the gate
-  //           and up sums of its intermediate rows.
-  //   DOWN:   the warp's 16 * kTPW rows of block w / (kCW / 2).
-  Tile tl[kTPW];
+  const ThreadOffs o = thread_offs<MODE>(warp, lane, 2 * GPS);
   const bool hz0 = hdr.flags & HF_HZ0, hz1 = hdr.flags & HF_HZ1;
-#pragma unroll
-  for (int ti = 0; ti < kTPW; ti++) {
-    if (MODE == SK_GATEUP) {
-      if (kTPW == 2) {
-        tl[ti].bg = tl[ti].b8 = ti;
-        tl[ti].rg = 16 * warp + sig;
-        tl[ti].r8 = tl[ti].rg + 8;
-      } else {
-        tl[ti].bg = 0;
-        tl[ti].b8 = 1;
-        tl[ti].rg = tl[ti].r8 = 8 * warp + sig;
-      }
-    } else {
-      const int wb = warp % (kCW / 2);
-      tl[ti].bg = tl[ti].b8 = warp / (kCW / 2);
-      tl[ti].rg = 16 * (kTPW * wb + ti) + sig;
-      tl[ti].r8 = tl[ti].rg + 8;
-    }
-    tl[ti].hzg = tl[ti].bg ? hz1 : hz0;
-    tl[ti].hz8 = tl[ti].b8 ? hz1 : hz0;
-  }
-  const bool active = MODE == SK_GATEUP || tl[0].bg == 0 || (hdr.flags & HF_V1);
+  const bool active = MODE == SK_GATEUP || o.bg0 == 0 || (hdr.flags & HF_V1);
 
   float acc[kTPW][NT][4];
 #pragma unroll
@@ -532,13 +570,13 @@ __device__ bool sk_unit(const SkParams& p, uint8_t* ring, SkSmem* L, const Stage
       if (!mbar_wait(&L->full[slot], phase, abort)) return false;
       if (p.counters) wait_cycles += clock64() - tw;
     }
-    const uint8_t* st = ring + slot * kStageBytes;
+    const uint32_t st = smem_u32(ring) + slot * kStageBytes;
     const int ng = min(kAG, (K - (hdr.kg0 + kk) * kKS) / kQ16Block);
     if (active && NT == 1 && ng == kAG) {
       // Whole stage into registers, release, then the arithmetic.
       GroupIn<NT, GPS, HZ> in[kAG];
 #pragma unroll
-      for (int j = 0; j < kAG; j++) load_group(in[j], st, 8 * NT, j, tl, g, t);
+      for (int j = 0; j < kAG; j++) load_group<MODE>(in[j], st, j, o, hz0, hz1);
       __syncwarp();
       if (lane == 0) mbar_arrive(&L->empty[slot]);
 #pragma unroll
@@ -548,7 +586,7 @@ __device__ bool sk_unit(const SkParams& p, uint8_t* ring, SkSmem* L, const Stage
       for (int j = 0; j < kAG; j++) {
         if (j < ng) {
           GroupIn<NT, GPS, HZ> in;
-          load_group(in, st, 8 * NT, j, tl, g, t);
+          load_group<MODE>(in, st, j, o, hz0, hz1);
           if (j == ng - 1) {
             __syncwarp();
             if (lane == 0) mbar_arrive(&L->empty[slot]);
@@ -573,7 +611,7 @@ __device__ bool sk_unit(const SkParams& p, uint8_t* ring, SkSmem* L, const Stage
     int hrow[NH];
 #pragma unroll
     for (int q = 0; q < NH; q++) {
-      hrow[q] = kTPW == 2 ? 16 * warp + 8 * q + sig : 8 * warp + sig;
+      hrow[q] = o.rg0 + 8 * q;
 #pragma unroll
       for (int nt = 0; nt < NT; nt++)
 #pragma unroll
@@ -657,7 +695,7 @@ __device__ bool sk_unit(const SkParams& p, uint8_t* ring, SkSmem* L, const Stage
   } else {
 #pragma unroll
     for (int ti = 0; ti < kTPW; ti++) {
-      const int mg = hdr.row0 + tl[ti].bg * kBoxRows + tl[ti].rg;   // output row of MMA row g
+      const int mg = hdr.row0 + o.bg0 * kBoxRows + o.rg0 + 16 * ti;   // output row of MMA row g
 #pragma unroll
       for (int nt = 0; nt < NT; nt++) {
 #pragma unroll
