@@ -407,6 +407,50 @@ __device__ __forceinline__ void compute_group(float (&acc)[kTPW][NT][4],
   }
 }
 
+// Both activation groups of a full stage, group size 128: the MMA chains
+// of the two groups are issued step by step side by side (twice the
+// independent work between dependent MMAs), then folded in K order (group
+// 0, then group 1), which is the same arithmetic as two compute_group calls.
+template <int NT, bool HZ>
+__device__ __forceinline__ void compute_stage(float (&acc)[kTPW][NT][4],
+                                              const GroupIn<NT, 1, HZ> (&in)[kAG]) {
+  int dh[kAG][kTPW][NT][4], dl[kAG][kTPW][NT][4];
+#pragma unroll
+  for (int s = 0; s < 4; s++)
+#pragma unroll
+    for (int j = 0; j < kAG; j++)
+#pragma unroll
+      for (int ti = 0; ti < kTPW; ti++) {
+        const uint2 wg = in[j].a[ti][0][s >> 1], w8 = in[j].a[ti][1][s >> 1];
+        const uint32_t qg = (s & 1) ? wg.y : wg.x, q8 = (s & 1) ? w8.y : w8.x;
+        const uint32_t a0 = w_even(qg), a2 = w_odd(qg), a1 = w_even(q8), a3 = w_odd(q8);
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+          const uint4 b = in[j].b[s][nt];
+          if (s == 0) {
+            imma_ss_z(dh[j][ti][nt], a0, a1, a2, a3, b.x, b.y);
+            imma_su_z(dl[j][ti][nt], a0, a1, a2, a3, b.z, b.w);
+          } else {
+            imma_ss(dh[j][ti][nt], a0, a1, a2, a3, b.x, b.y);
+            imma_su(dl[j][ti][nt], a0, a1, a2, a3, b.z, b.w);
+          }
+        }
+      }
+#pragma unroll
+  for (int j = 0; j < kAG; j++)
+#pragma unroll
+    for (int ti = 0; ti < kTPW; ti++)
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const int rr = e >> 1, c = e & 1;
+          const float f = (float)(dh[j][ti][nt][e] * 256 + dl[j][ti][nt][e]);
+          acc[ti][nt][e] = fmaf(in[j].ws[ti][rr][0] * in[j].as[nt][c], f, acc[ti][nt][e]);
+          if (HZ) acc[ti][nt][e] = fmaf(in[j].wz[ti][rr][0], in[j].asum[nt][c][0], acc[ti][nt][e]);
+        }
+}
+
 // ---------------------------------------------------------------------------
 // Producer warp.
 // ---------------------------------------------------------------------------
@@ -579,8 +623,12 @@ __device__ bool sk_unit(const SkParams& p, uint8_t* ring, SkSmem* L, const Stage
       for (int j = 0; j < kAG; j++) load_group<MODE>(in[j], st, j, o, hz0, hz1);
       __syncwarp();
       if (lane == 0) mbar_arrive(&L->empty[slot]);
+      if constexpr (GPS == 1) {
+        compute_stage(acc, in);
+      } else {
 #pragma unroll
-      for (int j = 0; j < kAG; j++) compute_group(acc, in[j]);
+        for (int j = 0; j < kAG; j++) compute_group(acc, in[j]);
+      }
     } else if (active) {
 #pragma unroll
       for (int j = 0; j < kAG; j++) {
