@@ -128,7 +128,8 @@ void wisp_gpu_scale_accum(float* acc, const float* x, float w, int n, cudaStream
  * top-k with renormalised weights; ties go to the lower expert index.
  * out_idx / out_w are host (pinned) buffers filled by async copies on `s`;
  * the caller synchronises `s` before reading them. top_k is clamped to 64;
- * n_experts must be <= 1024. */
+ * any n_experts (logits_scratch [n_experts] is working memory, as in the
+ * reference: it holds exp(logit - max) afterwards). */
 void wisp_gpu_router_topk(const wisp_half* W, const wisp_half* bias, const float* x,
                           float* logits_scratch, int n_experts, int hidden, int top_k,
                           int* out_idx, float* out_w, cudaStream_t s);
@@ -162,10 +163,12 @@ WispError wisp_b200_expert_ffn(const WispExpertMeta* meta, const void* const* d_
  * engine whose VRAM budget is fully committed to the expert cache, or a
  * host callback where cudaMalloc would synchronise the device). No
  * counterpart in the reference. The intermediate activations use a fixed
- * 256 KB array per device compiled into the library, so n_blobs * inter must
- * be <= 65536 (else WISP_ERR_INVALID_ARG). The first call on a device looks
- * up that array's device address; make it before any stream capture. Calls
- * share the array: calls that overlap on the GPU race on it. */
+ * 227 KB array per device compiled into the library, so n_blobs * inter must
+ * be <= 58112 (else WISP_ERR_INVALID_ARG). The first call on a device looks
+ * up that array's device address in the device's primary context; make it
+ * before any stream capture, and do not use this entry after a
+ * cudaDeviceReset or from another driver context. Calls share the array:
+ * calls that overlap on the GPU race on it. */
 WispError wisp_b200_expert_ffn_noalloc(const WispExpertMeta* meta, const void* const* d_blobs,
                                        const float* weights, int n_blobs, const float* d_x,
                                        float* d_acc, cudaStream_t stream, WispErrCtx* err);
@@ -180,7 +183,7 @@ typedef struct {
     int hidden;        /* M: multiple of 128 */
     int inter;         /* I: multiple of 128 */
     int n_experts;     /* routed experts E (<= 1024) */
-    int top_k;         /* <= 16 */
+    int top_k;         /* <= min(32, n_experts) */
     int group_size;    /* int4 quantisation group along K: 64 or 128 */
     int scoring;       /* WISP_SCORE_* */
     int n_groups;      /* sigmoid scoring: expert groups (E % n_groups == 0) */

@@ -292,19 +292,24 @@ extern "C" WispError wisp_b200_expert_ffn(const WispExpertMeta* meta, const void
 // evicting cached experts), or a host callback in a decode loop where a
 // cudaMalloc / cudaFree would implicitly synchronise the device. For them the
 // intermediate activations live in a fixed per-device array compiled into
-// this library: 65536 floats (256 KB), held by every GPU that loads the
-// library until the process exits. n_blobs * inter must fit in it.
+// this library: 58112 floats (227 KB, the most the down kernel can stage in
+// shared memory, so every size that fits the array also fits the kernel),
+// held by every GPU that loads the library until the process exits.
+// n_blobs * inter must fit in it.
 //
 // The array's host-side name is only a stand-in, so its device address is
 // looked up once per device (cudaGetSymbolAddress, with that device current)
 // on the first call made on that device; make that first call before any
-// stream capture. Every call shares the array: the gate/up kernel writes all
-// of the slots the down kernel reads, so nothing needs clearing, but calls
-// whose kernels overlap on the GPU (different streams, no ordering between
-// them) race on it.
+// stream capture. The cached address belongs to the device's primary
+// context (the runtime's): callers that switch to another driver context on
+// the device, or call cudaDeviceReset, must not use this entry afterwards.
+// Every call shares the array: the gate/up kernel writes all of the slots
+// the down kernel reads, so nothing needs clearing, but calls whose kernels
+// overlap on the GPU (different streams, no ordering between them) race on
+// it.
 // ---------------------------------------------------------------------------
 namespace {
-constexpr size_t kNoAllocScratchFloats = 65536;
+constexpr size_t kNoAllocScratchFloats = 227 * 1024 / sizeof(float);
 __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
 std::mutex g_noalloc_mu;
 void* g_noalloc_addr[64] = {nullptr};

@@ -240,6 +240,59 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int n_exper
     for (int k = 0; k < top_k; k++) out_w[k] /= wsum;
 }
 
+// Any number of experts: the same selection with the scratch row as working
+// memory, as the reference does (its softmax leaves exp(logit - max) in the
+// scratch). Each of the k rounds takes the largest remaining exp value (lower
+// index on ties, initial best -1) and marks the winner's slot -inf so no
+// later round can pick it; weights are value / sum, renormalised over the
+// winners.
+__global__ void router_topk_any_kernel(float* __restrict__ logits, int n_experts, int top_k,
+                                       int* __restrict__ out_idx, float* __restrict__ out_w) {
+  __shared__ float sv[8];
+  __shared__ int si[8];
+  float mx = -INFINITY;
+  for (int e = threadIdx.x; e < n_experts; e += blockDim.x) mx = fmaxf(mx, logits[e]);
+  float bv;
+  int bi;
+  block_argmax(mx, 0, sv, si, bv, bi);
+  const float gmax = bv;
+  float s = 0.f;
+  for (int e = threadIdx.x; e < n_experts; e += blockDim.x) {
+    const float v = expf(logits[e] - gmax);
+    logits[e] = v;
+    s += v;
+  }
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) sv[threadIdx.x >> 5] = s;
+  __syncthreads();
+  float den = 0.f;
+  for (int w = 0; w < 8; w++) den += sv[w];
+  __syncthreads();
+  const float inv = 1.f / (den > 0.f ? den : 1.f);
+  float wsum = 0.f;
+  for (int k = 0; k < top_k; k++) {
+    float v = -1.f;
+    int i = -1;
+    for (int e = threadIdx.x; e < n_experts; e += blockDim.x) {
+      const float q = logits[e];
+      if (q > v) {   // ascending e per thread: the lower index keeps a tie
+        v = q;
+        i = e;
+      }
+    }
+    block_argmax(v, i, sv, si, bv, bi);
+    if (threadIdx.x == 0) {
+      out_idx[k] = bi;
+      out_w[k] = bv * inv;
+      if (bi >= 0) logits[bi] = -INFINITY;
+    }
+    wsum += bv * inv;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0 && wsum > 0.f)
+    for (int k = 0; k < top_k; k++) out_w[k] /= wsum;
+}
+
 // Per-device staging for the router result (process-wide, as in the
 // reference: the engine runs one router per layer on one stream).
 std::mutex g_stage_mu;
@@ -312,7 +365,6 @@ extern "C" void wisp_gpu_router_topk(const wisp_half* W, const wisp_half* bias, 
                                      float* logits_scratch, int n_experts, int hidden,
                                      int top_k, int* out_idx, float* out_w, cudaStream_t s) {
   if (n_experts <= 0 || top_k <= 0) return;
-  if (n_experts > 1024) return;  // one block of 256 threads holds 4 experts each
   if (top_k > kRouterMaxTopK) top_k = kRouterMaxTopK;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return;
@@ -326,8 +378,12 @@ extern "C" void wisp_gpu_router_topk(const wisp_half* W, const wisp_half* bias, 
   router_gemv_kernel<<<(n_experts + 1) / 2, 256, 0, s>>>(reinterpret_cast<const __half*>(W),
                                                          reinterpret_cast<const __half*>(bias),
                                                          x, logits_scratch, n_experts, hidden);
-  router_topk_kernel<<<1, 256, 0, s>>>(logits_scratch, n_experts, top_k, g_stage_idx[dev],
-                                       g_stage_w[dev]);
+  if (n_experts <= 1024)   // one block of 256 threads holds 4 experts each in registers
+    router_topk_kernel<<<1, 256, 0, s>>>(logits_scratch, n_experts, top_k, g_stage_idx[dev],
+                                         g_stage_w[dev]);
+  else
+    router_topk_any_kernel<<<1, 256, 0, s>>>(logits_scratch, n_experts, top_k, g_stage_idx[dev],
+                                             g_stage_w[dev]);
   cudaMemcpyAsync(out_idx, g_stage_idx[dev], (size_t)top_k * sizeof(int), cudaMemcpyDeviceToHost,
                   s);
   cudaMemcpyAsync(out_w, g_stage_w[dev], (size_t)top_k * sizeof(float), cudaMemcpyDeviceToHost,

@@ -812,69 +812,72 @@ __device__ void plan_units(const WispSegment* __restrict__ segs, int nseg, int p
   }
 }
 
-// Rows of one register-path segment (0 < rows <= sk_rows): fp16 rows in
+// Rows of the register-path segments (0 < rows <= sk_rows): fp16 rows in
 // interleaved K order (within 8 K: 0,4,1,5,2,6,3,7) -> q16 rows (layout in
-// skinny.h). One warp per (row, 128-K block): lane l holds half l%2 of
-// packed word l/2, i.e. physical K {0,4,1,5} or {2,6,3,7} of that word; the
-// block's max |x| sets the scale, and the two lanes of a word exchange bytes
-// so each writes 8 contiguous bytes.
-__device__ void quant_segment(const WispSegment* __restrict__ segs, int s, int sk_rows,
-                              const __half* __restrict__ xp, int M, uint8_t* __restrict__ xq) {
-  const WispSegment sg = segs[s];
-  if (sg.rows <= 0 || sg.rows > sk_rows) return;
-  const int nblk = M / kQ16Block;
-  const size_t rb = q16_row_bytes(M);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  const int w = lane >> 1, half = lane & 1;
-  for (int pr = warp; pr < sg.rows * nblk; pr += nw) {
-    const int r = pr / nblk, b = pr - r * nblk;
-    const size_t p = (size_t)(sg.row_begin + r);
-    const uint2 raw = *reinterpret_cast<const uint2*>(xp + p * M + b * kQ16Block + w * 8 + half * 4);
-    const float2 f01 = __half22float2(u2h2(raw.x)), f23 = __half22float2(u2h2(raw.y));
-    const float f[4] = {f01.x, f01.y, f23.x, f23.y};
-    float m = fmaxf(fmaxf(fabsf(f[0]), fabsf(f[1])), fmaxf(fabsf(f[2]), fabsf(f[3])));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    const float inv = m > 0.f ? 32767.f / m : 0.f;
-    uint32_t oh = 0, ol = 0;
-    int sum = 0;
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const int v = max(-32767, min(32767, __float2int_rn(f[i] * inv)));
-      sum += v;
-      oh |= (uint32_t)((v >> 8) & 0xFF) << (8 * i);
-      ol |= (uint32_t)(v & 0xFF) << (8 * i);
-    }
-    const uint32_t ph = __shfl_xor_sync(0xffffffffu, oh, 1);
-    const uint32_t pl = __shfl_xor_sync(0xffffffffu, ol, 1);
-    // half 0 holds K {0,4,1,5}, half 1 K {2,6,3,7}: half 0 writes the high
-    // bytes (evens 0,2,4,6 then odds 1,3,5,7), half 1 the low bytes.
-    uint2 o;
-    if (half == 0) {
-      o.x = __byte_perm(oh, ph, 0x5140);
-      o.y = __byte_perm(oh, ph, 0x7362);
+// skinny.h). Block (s, r) converts row r of segment s with 128 threads: a
+// thread owns one packed-weight word (8 consecutive K) per 1024-K pass, so
+// each half-warp holds one 128-K block, whose max |x| (four shuffles) sets
+// its scale. Half-warps past the row's end take part in the shuffles with
+// zeros and store nothing.
+__global__ void __launch_bounds__(128) quant_rows_kernel(const WispSegment* __restrict__ segs,
+                                                         int sk_rows, const __half* __restrict__ xp,
+                                                         int M, uint8_t* __restrict__ xq) {
+  const WispSegment sg = segs[blockIdx.x];
+  const int r = blockIdx.y;
+  if (sg.rows <= 0 || sg.rows > sk_rows || r >= sg.rows) return;
+  const size_t p = (size_t)(sg.row_begin + r);
+  const __half* xr = xp + p * M;
+  uint8_t* qrow = xq + p * q16_row_bytes(M);
+  const int lane = threadIdx.x & 31;
+  for (int k0 = 0; k0 < M; k0 += 1024) {
+    const int w = k0 / 8 + threadIdx.x;
+    const bool in = 8 * w < M;
+    float f[8];   // physical K order
+    if (in) {
+      const uint4 v = *reinterpret_cast<const uint4*>(xr + 8 * w);
+      const float2 s04 = __half22float2(u2h2(v.x)), s15 = __half22float2(u2h2(v.y));
+      const float2 s26 = __half22float2(u2h2(v.z)), s37 = __half22float2(u2h2(v.w));
+      f[0] = s04.x; f[4] = s04.y; f[1] = s15.x; f[5] = s15.y;
+      f[2] = s26.x; f[6] = s26.y; f[3] = s37.x; f[7] = s37.y;
     } else {
-      o.x = __byte_perm(pl, ol, 0x5140);
-      o.y = __byte_perm(pl, ol, 0x7362);
-    }
-    uint8_t* row = xq + p * rb;
-    *reinterpret_cast<uint2*>(row + q16_word_offset(b * (kQ16Block / 8) + w) + half * 8) = o;
-    // sums over K 0-63 (lanes 0-15) and 64-127 (lanes 16-31)
 #pragma unroll
-    for (int o2 = 1; o2 < 16; o2 <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o2);
-    const int sum1 = __shfl_sync(0xffffffffu, sum, 16);
-    if (lane == 0) {
-      const float sc = m / 32767.f;
-      *reinterpret_cast<float4*>(row + q16_meta_offset(b)) =
-          make_float4(sc * 0.0625f, sc * (float)sum, sc * (float)sum1, 0.f);
+      for (int j = 0; j < 8; j++) f[j] = 0.f;
+    }
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) m = fmaxf(m, fabsf(f[j]));
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float inv = m > 0.f ? 32767.f / m : 0.f;
+    int v[8], sum = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      v[j] = max(-32767, min(32767, __float2int_rn(f[j] * inv)));
+      sum += v[j];
+    }
+    auto hi = [](int q) { return (uint32_t)((q >> 8) & 0xFF); };
+    auto lo = [](int q) { return (uint32_t)(q & 0xFF); };
+    const uint4 chunk = make_uint4(hi(v[0]) | hi(v[2]) << 8 | hi(v[4]) << 16 | hi(v[6]) << 24,
+                                   hi(v[1]) | hi(v[3]) << 8 | hi(v[5]) << 16 | hi(v[7]) << 24,
+                                   lo(v[0]) | lo(v[2]) << 8 | lo(v[4]) << 16 | lo(v[6]) << 24,
+                                   lo(v[1]) | lo(v[3]) << 8 | lo(v[5]) << 16 | lo(v[7]) << 24);
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const int sum1 = __shfl_sync(0xffffffffu, sum, (lane & 16) | 8);
+    if (in) {
+      *reinterpret_cast<uint4*>(qrow + q16_word_offset(w)) = chunk;
+      if ((lane & 15) == 0) {
+        const float sc = m / 32767.f;
+        *reinterpret_cast<float4*>(qrow + q16_meta_offset(w / 16)) =
+            make_float4(sc * 0.0625f, sc * (float)sum, sc * (float)sum1, 0.f);
+      }
     }
   }
 }
 
 // The four plans of one call in one launch: blocks 0 and 1 tile gate/up and
 // down for the tensor-core kernel, blocks 2 and 3 cut them into register-path
-// units; blocks 4.. (when the register path runs) quantise the rows of the
-// register-path segments, block 4 + s those of segment s.
+// units.
 struct PlanArgs {
   const WispSegment* segs;
   int nseg, sk_rows;
@@ -883,9 +886,6 @@ struct PlanArgs {
   int32_t* tickets;
   int per_gu, per_dn, cols, ks_dn, nk_dn, target;
   int32_t *tiles_gu, *tiles_dn, *units_gu, *units_dn;
-  const __half* xp;
-  int M;
-  uint8_t* xq;
 };
 
 __global__ void __launch_bounds__(1024) plan_all_kernel(const __grid_constant__ PlanArgs a) {
@@ -899,12 +899,9 @@ __global__ void __launch_bounds__(1024) plan_all_kernel(const __grid_constant__ 
                  a.tiles_dn, nullptr);
       break;
     case 2: plan_units(a.segs, a.nseg, a.per_gu, a.cols, a.sk_rows, 1, 1, 0, a.units_gu); break;
-    case 3:
+    default:
       plan_units(a.segs, a.nseg, a.per_dn, a.cols, a.sk_rows, a.ks_dn, a.nk_dn, a.target,
                  a.units_dn);
-      break;
-    default:
-      quant_segment(a.segs, (int)blockIdx.x - 4, a.sk_rows, a.xp, a.M, a.xq);
   }
 }
 
@@ -1209,6 +1206,22 @@ extern "C" size_t wisp_b200_grouped_workspace_bytes(const WispMoeConfig* cfg, in
   return carve_grouped(n_segs, rows_capacity, cfg->hidden, cfg->inter, nullptr).bytes;
 }
 
+namespace wb {
+// Where the q16 rows of the gate/up input live inside a grouped-FFN
+// workspace (a caller that packs them itself passes xq_ready to
+// grouped_ffn_impl).
+uint8_t* grouped_xq(void* d_workspace, int n_segs, int rows_capacity, int M, int I) {
+  return carve_grouped(n_segs, rows_capacity, M, I, d_workspace).xq;
+}
+WispError grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
+                           const WispInt4Expert* d_experts, int n_entries,
+                           const WispSegment* d_segs, int n_segs, int rows_capacity,
+                           const uint16_t* d_xp, uint16_t* d_h, int mode, const int* d_row_token,
+                           const float* d_row_weight, float* d_out, void* d_workspace,
+                           size_t workspace_bytes, int* d_error_flag, bool xq_ready,
+                           cudaStream_t stream, WispErrCtx* err);
+}  // namespace wb
+
 extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void* d_prepared,
                                            const WispInt4Expert* d_experts,
                                            int n_entries, const WispSegment* d_segs, int n_segs,
@@ -1218,6 +1231,18 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
                                            void* d_workspace, size_t workspace_bytes,
                                            int* d_error_flag, cudaStream_t stream,
                                            WispErrCtx* err) {
+  return wb::grouped_ffn_impl(cfg, d_prepared, d_experts, n_entries, d_segs, n_segs,
+                              rows_capacity, d_xp, d_h, mode, d_row_token, d_row_weight, d_out,
+                              d_workspace, workspace_bytes, d_error_flag, false, stream, err);
+}
+
+WispError wb::grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
+                               const WispInt4Expert* d_experts, int n_entries,
+                               const WispSegment* d_segs, int n_segs, int rows_capacity,
+                               const uint16_t* d_xp, uint16_t* d_h, int mode,
+                               const int* d_row_token, const float* d_row_weight, float* d_out,
+                               void* d_workspace, size_t workspace_bytes, int* d_error_flag,
+                               bool xq_ready, cudaStream_t stream, WispErrCtx* err) {
   if (!cfg || !d_prepared || !d_experts || !d_segs || !d_xp || !d_h || !d_out || !d_workspace ||
       n_entries <= 0)
     return WB_FAIL(WISP_ERR_INVALID_ARG, "grouped_ffn: null pointer argument");
@@ -1309,10 +1334,10 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
   pa.tiles_dn = ws.tiles_dn;
   pa.units_gu = ws.units_gu;
   pa.units_dn = ws.units_dn;
-  pa.xp = reinterpret_cast<const __half*>(d_xp);
-  pa.M = M;
-  pa.xq = ws.xq;
-  wb::launch_k(plan_all_kernel, 4 + (sk_rows > 0 ? n_segs : 0), 1024, 0, stream, pa);
+  wb::launch_k(plan_all_kernel, 4, 1024, 0, stream, pa);
+  if (sk_rows > 0 && !xq_ready)
+    wb::launch_k(quant_rows_kernel, dim3(n_segs, sk_rows), 128, 0, stream, d_segs, sk_rows,
+                 reinterpret_cast<const __half*>(d_xp), M, ws.xq);
   CUtensorMap sk_xq[2], sk_hq[2];
   for (int i = 0; i < 2; i++) {
     if (!encode_q16_map(&sk_xq[i], ws.xq, rows_capacity, M, 8 << i) ||

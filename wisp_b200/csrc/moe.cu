@@ -23,6 +23,16 @@ WispError launch_plan(const WispMoeConfig* c, const int* idx, const float* w, in
                       WispErrCtx* err);
 WispError launch_pack(const uint16_t* x, const int* src, int n_rows, int M, uint16_t* xp,
                       cudaStream_t st, WispErrCtx* err);
+WispError launch_pack_q16(const uint16_t* x, const int* src, int n_rows, int M, uint16_t* xp,
+                          uint8_t* xq, cudaStream_t st, WispErrCtx* err);
+uint8_t* grouped_xq(void* d_workspace, int n_segs, int rows_capacity, int M, int I);
+WispError grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
+                           const WispInt4Expert* d_experts, int n_entries,
+                           const WispSegment* d_segs, int n_segs, int rows_capacity,
+                           const uint16_t* d_xp, uint16_t* d_h, int mode, const int* d_row_token,
+                           const float* d_row_weight, float* d_out, void* d_workspace,
+                           size_t workspace_bytes, int* d_error_flag, bool xq_ready,
+                           cudaStream_t stream, WispErrCtx* err);
 }  // namespace wb
 
 namespace {
@@ -145,14 +155,18 @@ extern "C" WispError wisp_b200_moe_forward(const WispMoeConfig* cfg, const WispM
   if (e != WISP_OK) return e;
   e = wb::launch_plan(cfg, idx, wt, ws.counts, ws.segs, ws.row_token, ws.row_weight, stream, err);
   if (e != WISP_OK) return e;
-  e = wb::launch_pack(d_x, ws.row_token, ws.rows, cfg->hidden, ws.xp, stream, err);
+  // Both operand forms of the gathered rows in one pass: fp16 for the
+  // tensor-core kernel, q16 (into the grouped workspace) for the register path.
+  e = wb::launch_pack_q16(d_x, ws.row_token, ws.rows, cfg->hidden, ws.xp,
+                          wb::grouped_xq(ws.grouped, V, ws.rows, cfg->hidden, cfg->inter), stream,
+                          err);
   if (e != WISP_OK) return e;
   WB_CUDA_CHECK(cudaMemsetAsync(d_out, 0, (size_t)cfg->tokens * cfg->hidden * sizeof(float), stream));
   WB_CUDA_CHECK(cudaMemsetAsync(ws.error_flag, 0, sizeof(int), stream));
   if (!w->experts) return WB_FAIL(WISP_ERR_INVALID_ARG, "moe_forward: null expert table");
-  return wisp_b200_grouped_ffn(cfg, w->prepared, w->experts, V, ws.segs, V, ws.rows, ws.xp, ws.h, 0, ws.row_token,
-                               ws.row_weight, d_out, ws.grouped, ws.grouped_bytes, ws.error_flag,
-                               stream, err);
+  return wb::grouped_ffn_impl(cfg, w->prepared, w->experts, V, ws.segs, V, ws.rows, ws.xp, ws.h, 0,
+                              ws.row_token, ws.row_weight, d_out, ws.grouped, ws.grouped_bytes,
+                              ws.error_flag, true, stream, err);
 }
 
 extern "C" int* wisp_b200_moe_error_word(const WispMoeConfig* cfg, void* d_workspace) {

@@ -34,6 +34,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "skinny.h"
 
 using namespace wb;
 
@@ -605,6 +606,78 @@ __global__ void pack_rows_kernel(const uint16_t* __restrict__ x, const int* __re
   }
 }
 
+// The same rows gathered into both operand forms at once: xp[p] as above
+// and xq[p] as a q16 row (layout in skinny.h) for the register-path kernel.
+// One block of 128 threads per row; a thread owns one packed-weight word (8
+// consecutive K) per 1024-K pass, so each half-warp holds one 128-K block:
+// its max |x| (four shuffles) sets the block's scale, and every thread
+// writes its word's 16 bytes. Half-warps past the row's end take part in the
+// shuffles with zeros and store nothing.
+__global__ void __launch_bounds__(128) pack_rows_q16_kernel(const uint16_t* __restrict__ x,
+                                                            const int* __restrict__ src, int n_rows,
+                                                            int M, uint16_t* __restrict__ xp,
+                                                            uint8_t* __restrict__ xq) {
+  const int p = blockIdx.x;
+  if (p >= n_rows) return;
+  const int s = src ? src[p] : p;
+  const uint16_t* xr = x + (size_t)s * M;
+  uint16_t* orow = xp + (size_t)p * M;
+  uint8_t* qrow = xq + (size_t)p * q16_row_bytes(M);
+  const int lane = threadIdx.x & 31;
+  for (int k0 = 0; k0 < M; k0 += 1024) {
+    const int w = k0 / 8 + threadIdx.x;          // packed word of this thread
+    const bool in = 8 * w < M;
+    float f[8];
+    if (in) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(xr + 8 * w));
+      const uint32_t a[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        f[2 * j] = bf16f((uint16_t)(a[j] & 0xffff));
+        f[2 * j + 1] = bf16f((uint16_t)(a[j] >> 16));
+      }
+      const __half2 h0 = __floats2half2_rn(f[0], f[4]);
+      const __half2 h1 = __floats2half2_rn(f[1], f[5]);
+      const __half2 h2 = __floats2half2_rn(f[2], f[6]);
+      const __half2 h3 = __floats2half2_rn(f[3], f[7]);
+      *reinterpret_cast<uint4*>(orow + 8 * w) = make_uint4(h22u(h0), h22u(h1), h22u(h2), h22u(h3));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; j++) f[j] = 0.f;
+    }
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) m = fmaxf(m, fabsf(f[j]));
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float inv = m > 0.f ? 32767.f / m : 0.f;
+    int v[8], sum = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      v[j] = max(-32767, min(32767, __float2int_rn(f[j] * inv)));
+      sum += v[j];
+    }
+    auto hi = [](int q) { return (uint32_t)((q >> 8) & 0xFF); };
+    auto lo = [](int q) { return (uint32_t)(q & 0xFF); };
+    const uint4 chunk = make_uint4(hi(v[0]) | hi(v[2]) << 8 | hi(v[4]) << 16 | hi(v[6]) << 24,
+                                   hi(v[1]) | hi(v[3]) << 8 | hi(v[5]) << 16 | hi(v[7]) << 24,
+                                   lo(v[0]) | lo(v[2]) << 8 | lo(v[4]) << 16 | lo(v[6]) << 24,
+                                   lo(v[1]) | lo(v[3]) << 8 | lo(v[5]) << 16 | lo(v[7]) << 24);
+    // sums over the block's K 0-63 (its first 8 threads) and 64-127
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const int sum1 = __shfl_sync(0xffffffffu, sum, (lane & 16) | 8);
+    if (in) {
+      *reinterpret_cast<uint4*>(qrow + q16_word_offset(w)) = chunk;
+      if ((lane & 15) == 0) {
+        const float sc = m / 32767.f;
+        *reinterpret_cast<float4*>(qrow + q16_meta_offset(w / 16)) =
+            make_float4(sc * 0.0625f, sc * (float)sum, sc * (float)sum1, 0.f);
+      }
+    }
+  }
+}
+
 // y[t] = bf16(x[t] / rms(x[t])): per-token RMS normalisation (no weight)
 // between stacked MoE layers. One block per token.
 __global__ void rms_rescale_kernel(const float* __restrict__ x, uint16_t* __restrict__ y, int M,
@@ -692,7 +765,8 @@ WispError launch_route(const WispMoeConfig* c, const uint16_t* x, const uint16_t
   }
   auto topk = E <= 32 ? topk_kernel<1> : E <= 64 ? topk_kernel<2> : E <= 128 ? topk_kernel<4>
             : E <= 256 ? topk_kernel<8> : E <= 512 ? topk_kernel<16> : topk_kernel<32>;
-  wb::launch_k(topk, (T + 7) / 8, 256, 0, st, part, nsplit, bias, T, E, c->top_k, c->scoring,
+  // two tokens (warps) per block, so a few hundred tokens still spread over the SMs
+  wb::launch_k(topk, (T + 1) / 2, 64, 0, st, part, nsplit, bias, T, E, c->top_k, c->scoring,
                c->n_groups, c->topk_groups, c->routed_scaling, idx, w, logits_out);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
@@ -707,6 +781,14 @@ WispError launch_plan(const WispMoeConfig* c, const int* idx, const float* w, in
   wb::launch_k(segments_kernel, 1, 1024, 0, st, counts, V, segs);
   wb::launch_k(fill_kernel, V, kPlanWarps * 32, 0, st, idx, w, T * k, k, E, T, segs, row_token,
                row_weight);
+  WB_CUDA_CHECK(cudaGetLastError());
+  return WISP_OK;
+}
+
+WispError launch_pack_q16(const uint16_t* x, const int* src, int n_rows, int M, uint16_t* xp,
+                          uint8_t* xq, cudaStream_t st, WispErrCtx* err) {
+  if (n_rows <= 0) return WISP_OK;
+  wb::launch_k(pack_rows_q16_kernel, n_rows, 128, 0, st, x, src, n_rows, M, xp, xq);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
