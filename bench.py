@@ -200,6 +200,91 @@ def reference_arm(args, spec) -> None:
 
 
 # ---------------------------------------------------------------------------
+# The other BASELINE configurations (single GPU): one layer per step
+# ---------------------------------------------------------------------------
+
+SIDE_CONFIGS = ["mixtral_b1", "mixtral_b64", "ds_b1", "ds_b128", "ds_prefill"]
+
+
+def measure_side_config(name: str, steps: int, warmup: int, peaks: dict) -> dict:
+    """One MoE layer of configuration `name` (BASELINE configs[0]-[3]) as a
+    step: router, dispatch, grouped FFN and combine through MoeLayer (the C
+    ABI's wisp_b200_moe_forward). A single layer's touched weights (180-210
+    MB at batch 1) are close to the 126 MB L2, so every step is timed alone
+    with CUDA events and L2 is flushed (a 256 MB write) between steps,
+    outside the timed intervals. e2e adds the host->device copy of the
+    step's tokens and the device->host copy of its output."""
+    import torch
+    from wisp_b200 import synth
+    from wisp_b200.moe import MoeLayer
+
+    spec = synth.CONFIGS[name]
+    dev = torch.device("cuda", torch.cuda.current_device())
+    layers_w, x = synth.make_model(spec, dev)
+    layer = MoeLayer(layers_w[0], spec.tokens)
+    out = torch.empty((spec.tokens, spec.hidden), dtype=torch.float32, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def timed(fn, n):
+        ts = []
+        for _ in range(n):
+            flush.fill_(1)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            b.synchronize()
+            ts.append(a.elapsed_time(b))
+        return statistics.mean(ts)
+
+    for _ in range(warmup):
+        layer.forward(x, out)
+    ms = timed(lambda: layer.forward(x, out), steps)
+    layer.check()
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty((spec.tokens, spec.hidden), dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        x.copy_(x_host, non_blocking=True)
+        layer.forward(x, out)
+        out_host.copy_(out, non_blocking=True)
+
+    e2e_step()
+    ems = timed(e2e_step, steps)
+    used = int(torch.unique(layer.idx).numel()) + (1 if spec.has_shared else 0)
+    nbytes = used * spec.expert_bytes() + spec.n_experts * spec.hidden * 2
+    R = spec.tokens * spec.top_k + (spec.tokens if spec.has_shared else 0)
+    flops = 6.0 * spec.hidden * spec.inter * R + 2.0 * spec.tokens * spec.n_experts * spec.hidden
+    gbs = nbytes / (ms / 1e3) / 1e9
+    tfl = flops / (ms / 1e3) / 1e12
+    if flops / (peaks["bf16_tflops"] * 1e12) > nbytes / (peaks["hbm_gbs"] * 1e9):
+        roof = {"bound": "tensor", "achieved": round(tfl, 1), "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": round(tfl / peaks["bf16_tflops"], 4)}
+    else:
+        roof = {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4)}
+    roof.update({"kernel": "one MoE layer (router, dispatch, grouped int4 FFN, combine)",
+                 "algorithmic_bytes": nbytes, "algorithmic_flops": flops,
+                 "experts_touched": used, "vs_8tbs": round(gbs / 8000.0, 4),
+                 "peak_source": peaks["source"], "traffic": None})
+    res = {"value": round(spec.tokens / (ms / 1e3), 1), "unit": UNIT,
+           "ms_per_step": round(ms, 4), "tokens_per_step": spec.tokens,
+           "shape": {"hidden": spec.hidden, "inter": spec.inter, "experts": spec.n_experts,
+                     "shared_experts": int(spec.has_shared), "top_k": spec.top_k,
+                     "scoring": "softmax" if spec.scoring == 0 else "sigmoid group-limited",
+                     "skewed_router": spec.skew},
+           "l2": "flushed between steps (256 MB write, untimed)",
+           "roofline": roof,
+           "e2e": {"value": round(spec.tokens / (ems / 1e3), 1), "unit": UNIT,
+                   "h2d_bytes_per_step": x_host.numel() * 2,
+                   "d2h_bytes_per_step": out_host.numel() * 4}}
+    del layer, layers_w, x, out, flush
+    torch.cuda.empty_cache()
+    return res
+
+
+# ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
 
@@ -213,6 +298,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch every step eagerly")
     ap.add_argument("--kernel-reps", type=int, default=5)
+    ap.add_argument("--no-side-configs", action="store_true",
+                    help="skip the single-layer measurements of BASELINE configs[0]-[3]")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -490,6 +577,10 @@ def main() -> None:
         "roofline": roofline, "e2e": e2e, "clocks": clk,
         "gpu_launches": launches_per_step * args.steps,
     }
+    if world == 1 and not args.no_side_configs and args.config == "ep_stack":
+        # the stack (~35 GB) stays resident; each configuration adds a few GB
+        line["configs"] = {n: measure_side_config(n, args.steps, args.warmup, peaks)
+                           for n in SIDE_CONFIGS}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(spec)
     if rank == 0:

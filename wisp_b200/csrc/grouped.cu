@@ -1219,7 +1219,7 @@ WispError grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
                            const uint16_t* d_xp, uint16_t* d_h, int mode, const int* d_row_token,
                            const float* d_row_weight, float* d_out, void* d_workspace,
                            size_t workspace_bytes, int* d_error_flag, bool xq_ready,
-                           cudaStream_t stream, WispErrCtx* err);
+                           int max_seg_rows, cudaStream_t stream, WispErrCtx* err);
 }  // namespace wb
 
 extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void* d_prepared,
@@ -1233,7 +1233,8 @@ extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void*
                                            WispErrCtx* err) {
   return wb::grouped_ffn_impl(cfg, d_prepared, d_experts, n_entries, d_segs, n_segs,
                               rows_capacity, d_xp, d_h, mode, d_row_token, d_row_weight, d_out,
-                              d_workspace, workspace_bytes, d_error_flag, false, stream, err);
+                              d_workspace, workspace_bytes, d_error_flag, false, rows_capacity,
+                              stream, err);
 }
 
 WispError wb::grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
@@ -1242,7 +1243,8 @@ WispError wb::grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
                                const uint16_t* d_xp, uint16_t* d_h, int mode,
                                const int* d_row_token, const float* d_row_weight, float* d_out,
                                void* d_workspace, size_t workspace_bytes, int* d_error_flag,
-                               bool xq_ready, cudaStream_t stream, WispErrCtx* err) {
+                               bool xq_ready, int max_seg_rows, cudaStream_t stream,
+                               WispErrCtx* err) {
   if (!cfg || !d_prepared || !d_experts || !d_segs || !d_xp || !d_h || !d_out || !d_workspace ||
       n_entries <= 0)
     return WB_FAIL(WISP_ERR_INVALID_ARG, "grouped_ffn: null pointer argument");
@@ -1378,10 +1380,14 @@ WispError wb::grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_gu));
   WB_CUDA_CHECK(cudaFuncSetAttribute(grouped_ffn_kernel<DOWN>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_dn));
+  // When no segment can exceed the routing threshold (max_seg_rows, an upper
+  // bound the caller knows, e.g. the token count of a decode batch), the
+  // tensor-core kernels would find no tiles: they are not launched.
+  const bool tc = max_seg_rows > sk_rows;
   if (sk_rows > 0) WB_CUDA_CHECK(wb::launch_skinny(sk, 0, grid, stream));
-  wb::launch_k(grouped_ffn_kernel<GATEUP>, grid, kThreads, sm_gu, stream, gu);
+  if (tc) wb::launch_k(grouped_ffn_kernel<GATEUP>, grid, kThreads, sm_gu, stream, gu);
   if (sk_rows > 0) WB_CUDA_CHECK(wb::launch_skinny(sk, 1, grid, stream));
-  wb::launch_k(grouped_ffn_kernel<DOWN>, grid, kThreads, sm_dn, stream, dn);
+  if (tc) wb::launch_k(grouped_ffn_kernel<DOWN>, grid, kThreads, sm_dn, stream, dn);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }

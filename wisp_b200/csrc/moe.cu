@@ -32,7 +32,7 @@ WispError grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
                            const uint16_t* d_xp, uint16_t* d_h, int mode, const int* d_row_token,
                            const float* d_row_weight, float* d_out, void* d_workspace,
                            size_t workspace_bytes, int* d_error_flag, bool xq_ready,
-                           cudaStream_t stream, WispErrCtx* err);
+                           int max_seg_rows, cudaStream_t stream, WispErrCtx* err);
 }  // namespace wb
 
 namespace {
@@ -164,9 +164,11 @@ extern "C" WispError wisp_b200_moe_forward(const WispMoeConfig* cfg, const WispM
   WB_CUDA_CHECK(cudaMemsetAsync(d_out, 0, (size_t)cfg->tokens * cfg->hidden * sizeof(float), stream));
   WB_CUDA_CHECK(cudaMemsetAsync(ws.error_flag, 0, sizeof(int), stream));
   if (!w->experts) return WB_FAIL(WISP_ERR_INVALID_ARG, "moe_forward: null expert table");
+  // A routed expert gets at most one row per token and the shared expert T
+  // rows, so no segment exceeds T rows.
   return wb::grouped_ffn_impl(cfg, w->prepared, w->experts, V, ws.segs, V, ws.rows, ws.xp, ws.h, 0,
                               ws.row_token, ws.row_weight, d_out, ws.grouped, ws.grouped_bytes,
-                              ws.error_flag, true, stream, err);
+                              ws.error_flag, true, cfg->tokens, stream, err);
 }
 
 extern "C" int* wisp_b200_moe_error_word(const WispMoeConfig* cfg, void* d_workspace) {
