@@ -25,32 +25,36 @@
 // and the 16-bit activations carry more precision than fp16.
 //
 // One persistent CTA per SM, warp-specialised:
-//   warp 16     producer: per 256-K stage, one TMA box of packed nibbles per
-//               128-row weight block (128 rows x 128 bytes, 128-byte
-//               swizzle), one TMA box per 64-K quarter of the unit's token
-//               rows (128 bytes of q16 data per row), one box per 128-K block
-//               of the rows' metadata and bulk copies of the stage's weight
-//               scales (and zero points) from the prepared tile-transposed
-//               copy, into a 5-deep shared-memory ring (44 KB per stage, up
-//               to 160 KB of weights in flight per SM: under full load a copy
-//               takes several microseconds from issue to arrival, so the
-//               bytes in flight per SM set the bandwidth). Units are looked up
-//               in the unit prefix; the next unit's segment record is fetched
-//               one unit ahead.
-//   warps 0-15  consumers, one 16-row MMA tile each (four warps per
-//               scheduler: a stage's shared-memory reads and MMA chains are
-//               latency-bound, and eight two-tile warps left the schedulers
-//               idle two thirds of the time). Per 128-K group a thread reads
-//               2 x 8 bytes of each of its two weight rows (packed words 2t,
-//               2t+1 and 8+2t, 9+2t of the group; MMA row g lives in box row
-//               sigma(g) = 2(g%4) + g/4 (mod 8), so each half-warp's rows fall
-//               in distinct swizzle chunks) and one 16-byte chunk of each
-//               token row per MMA step (conflict-free: step s of thread t
-//               reads packed word 8(s/2) + 2t + s%2, whose chunk parity
-//               alternates between neighbouring token rows), runs four k32
-//               steps of high/low MMAs and folds them. Units of at most 8
-//               tokens read a whole stage into registers and release it
-//               before any arithmetic.
+//   producer    (the last warp) per 256-K stage four copies into a 4-deep
+//               shared-memory ring of 46 KB stages: one TMA box of packed
+//               nibbles per 128-row weight block (128 rows x 128 bytes,
+//               128-byte swizzle), one 3D TMA box of the unit's q16 token rows
+//               (five 128-byte lines per row: the stage's values and the rows'
+//               block scales), and one bulk copy of the stage's run of weight
+//               scales (zero points: one more) from the prepared per-unit
+//               copy. Each extra small copy per stage measurably cut the
+//               streaming rate (a probe of this ring: 7.2 TB/s with the two
+//               weight boxes alone, 3.5 TB/s with six more small copies), so
+//               everything else a stage needs rides in these four. Up to
+//               128 KB of weights are in flight per SM. Units are looked up
+//               in a shared-memory copy of the unit prefix; the next unit's
+//               segment record is fetched one unit ahead.
+//   consumers   8 warps with two 16-row MMA tiles each (by default; see
+//               WB_SK_TILES_PER_WARP -- sixteen one-tile warps measured
+//               slower: their 96-register cap spilled and every warp
+//               re-reads the token fragments). All shared-memory reads are
+//               a per-thread offset plus a compile-time constant from the
+//               stage base. Per 128-K group a thread reads 2 x 8 bytes of each
+//               of its weight rows (packed words 2t, 2t+1 and 8+2t, 9+2t of
+//               the group; MMA row g lives in box row sigma(g) = 2(g%4) + g/4
+//               (mod 8), so each half-warp's rows fall in distinct swizzle
+//               chunks) and one 16-byte chunk of each token row per MMA step
+//               (conflict-free: step s of thread t reads packed word 8(s/2) +
+//               2t + s%2, whose chunk parity alternates between neighbouring
+//               token rows), runs four k32 steps of high/low MMAs and folds
+//               them. Units of at most 8 tokens read a whole stage into
+//               registers and release it before any arithmetic, and issue the
+//               two groups' MMA chains side by side.
 //
 // Work unit = (segment, weight row block, chunk of up to 16 tokens, and for
 // a weighted down projection with fewer than two units per SM a part of a K
@@ -135,6 +139,7 @@ struct SkSmem {
   int red_sum[kCW][kCols];
   int abort;
   uint32_t zbits[kMaxEntries * 3 / 32];  // zero-point flag per matrix entry
+  int32_t units[kMaxSegs + 2];           // unit prefix per segment, then the K split
 };
 
 struct SkParams {
@@ -460,7 +465,7 @@ __device__ void sk_producer(const SkParams& p, uint8_t* ring, SkSmem* L, int tot
   const int K = MODE == SK_GATEUP ? p.M : p.I;
   const int nk = (K + kKS - 1) / kKS;
   const uint32_t scb = 2u * (kKS / p.gs) * kBoxRows * 2;   // one stage's run of scales
-  const int ksplit = __ldg(p.units + p.nseg + 1);
+  const int ksplit = L->units[p.nseg + 1];
   if (lane < 2) tma_prefetch_desc(&p.act_map[lane]);
   int slot = 0, item = 0;
   uint32_t phase = 0;
@@ -471,7 +476,7 @@ __device__ void sk_producer(const SkParams& p, uint8_t* ring, SkSmem* L, int tot
   // of the next unit is requested one unit ahead so its latency hides behind
   // the current unit's stages.
   int seg = 0;
-  while (__ldg(p.units + seg + 1) <= (int)blockIdx.x) seg++;
+  while (L->units[seg + 1] <= (int)blockIdx.x) seg++;
   WispSegment sg_next = p.segs[seg];
   int seg_next = seg;
   for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
@@ -479,11 +484,11 @@ __device__ void sk_producer(const SkParams& p, uint8_t* ring, SkSmem* L, int tot
     seg = seg_next;
     const int un = u + gridDim.x;
     if (un < total) {
-      while (__ldg(p.units + seg_next + 1) <= un) seg_next++;
+      while (L->units[seg_next + 1] <= un) seg_next++;
       sg_next = p.segs[seg_next];
     }
     const int chunks = (sg.rows + kCols - 1) / kCols;
-    const int l = u - __ldg(p.units + seg);
+    const int l = u - L->units[seg];
     // l = (row block * ksplit + K part) * chunks + chunk: the chunks of one
     // weight tile are consecutive units
     const int ch = l % chunks, rest = l / chunks;
@@ -835,6 +840,7 @@ __global__ void __launch_bounds__(kThreads, 1) skinny_ffn_kernel(const __grid_co
   }
   const uint32_t* zb = reinterpret_cast<const uint32_t*>(p.prepared + p.p_zbits);
   for (int w = threadIdx.x; w < (p.n_entries * 3 + 31) / 32; w += blockDim.x) L->zbits[w] = __ldg(zb + w);
+  for (int i = threadIdx.x; i <= p.nseg + 1; i += blockDim.x) L->units[i] = __ldg(p.units + i);
   __syncthreads();
   if (warp == kCW)
     sk_producer<MODE>(p, ring, L, total, lane);
