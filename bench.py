@@ -38,10 +38,11 @@ UNIT = "tokens/s"
 
 
 # DRAM bytes (read + write) per algorithmic byte of one grouped-FFN call,
-# from an ncu capture of the ep_profile workload (1,490.28 MB of traffic for
-# 1,476.03 MB of int4 weights and scales): the full-size layer is too large
-# for a multi-pass capture, and its traffic grows with the experts streamed.
-TRAFFIC_PER_ALGORITHMIC_BYTE = 1490.28 / 1476.03
+# from an ncu capture of the ep_profile workload (1,507.4 MB of traffic for
+# 1,476.03 MB of int4 weights and scales, profiles/grouped_ffn_ep_profile_traffic.md):
+# the full-size layer is too large for a multi-pass capture, and its traffic
+# grows with the experts streamed.
+TRAFFIC_PER_ALGORITHMIC_BYTE = 1507.4 / 1476.03
 
 
 def _peaks() -> dict:
