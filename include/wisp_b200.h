@@ -259,7 +259,7 @@ typedef struct {
 
 /* Grouped expert FFN over pre-permuted rows. d_prepared / d_experts /
  * n_entries: a prepared weight set and its device expert table (segment
- * experts index its entries). Segments of at most 16 rows (decode) run on
+ * experts index its entries). Segments of at most 32 rows (decode) run on
  * the register-fed integer tensor-core kernel, larger ones on the tcgen05
  * kernel.
  *   d_xp:   fp16 [R x M] activation rows in interleaved K order (within each
@@ -375,9 +375,10 @@ int* wisp_b200_moe_error_word(const WispMoeConfig* cfg, void* d_workspace);
  * profiling runs only. */
 void wisp_b200_debug_set_counters(unsigned long long* d_counters);
 
-/* Largest segment (rows) routed to the register-fed kernel; 0 sends every
- * segment to the tcgen05 kernel, a negative value restores the default (16).
- * Process-wide; for tests and tuning. */
+/* Largest segment (rows) routed to the register-fed kernel, which takes any
+ * segment in chunks of 16 rows; 0 sends every segment to the tcgen05 kernel,
+ * a negative value restores the default. Process-wide; for tests and
+ * tuning. */
 void wisp_b200_set_skinny_max_rows(int rows);
 
 /* Library version string. */

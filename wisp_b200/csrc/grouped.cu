@@ -1297,8 +1297,7 @@ WispError wb::grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
   dn.out = d_out;
   dn.mode = mode;
 
-  int sk_rows = g_skinny_rows >= 0 ? std::min(g_skinny_rows, wb::skinny_max_rows())
-                                   : wb::skinny_max_rows();
+  int sk_rows = g_skinny_rows >= 0 ? g_skinny_rows : wb::skinny_max_rows();
   // The register-path kernel keeps the zero-point flags in shared memory;
   // larger launches run on the tensor-core kernel alone.
   if (n_segs > wb::skinny_max_segs() || n_entries > wb::skinny_max_entries()) sk_rows = 0;

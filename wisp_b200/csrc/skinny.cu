@@ -98,9 +98,13 @@ static_assert(kTPW == 1 || kTPW == 2, "one or two tiles per consumer warp");
 constexpr int kThreads = (kCW + 1) * 32;      // + one producer warp
 constexpr int kStages = 4;
 constexpr int kCols = 16;                     // tokens per unit
-// Default routing threshold: segments of up to 16 rows run here, larger ones
-// on the tcgen05 kernel.
-constexpr int kSkMaxRows = 16;
+// Default routing threshold: segments of up to 32 rows run here (two 16-row
+// chunks, the second reading the weight tile through L2), larger ones on the
+// tcgen05 kernel. Measured on B200 with the layer's CUDA graph and L2 flushed
+// between steps: Mixtral b64 (segments of 12-21 rows) 449 us at 16 -> 342 us
+// at 24-128; DeepSeek prefill (4096 skewed tokens) best at 32 (7.60 ms
+// against 7.86 ms at 16 and 7.77 ms at 64).
+constexpr int kSkMaxRows = 32;
 constexpr int kKS = kQ16StageK;               // K per stage (256)
 constexpr int kAG = kKS / kQ16Block;          // 128-K activation groups per stage
 constexpr int kBoxRows = 128;
