@@ -14,6 +14,8 @@ the tensor cores with fp32 accumulation, whose logits differ from fp64 by
 """
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import torch
 
@@ -37,6 +39,9 @@ def rel_errors(got: np.ndarray, ref: np.ndarray) -> tuple[float, float]:
 
 def assert_close(got, ref, max_rel=MAX_REL, mean_rel=MEAN_REL, what=""):
     mr, me = rel_errors(got, ref)
+    if os.environ.get("WB_REPORT_ERRORS"):
+        # the measured errors, for the record (run pytest with -s)
+        print(f"[errors] {what}: max_rel={mr:.3e} mean_rel={me:.3e}")
     assert mr <= max_rel and me <= mean_rel, f"{what}: max_rel={mr:.3e} (<= {max_rel}) mean_rel={me:.3e} (<= {mean_rel})"
     return mr, me
 

@@ -4,35 +4,42 @@
 // of dequant -> fp16 GEMV -> scale_accum (csrc/core/wisp_engine.c:1507-1531
 // called from run_moe :1563-1674 and, for prefill, decode_step per token
 // :2292-2307). Rows of activations are pre-grouped by expert ("segments");
-// each CTA tile computes 128 weight rows x BN token rows:
+// each CTA tile computes 128 weight rows (the MMA's M, one TMEM lane each)
+// x BN token rows (its N):
 //
 //   GATEUP: H[p, i] = silu(gate[i] . x_p) * (up[i] . x_p)   (fp16 H out)
+//           over 64 intermediate rows: A rows 16j..16j+7 are gate rows
+//           8j..8j+7 of the tile, A rows 16j+8..16j+15 the matching up
+//           rows, so a gate lane's partner is lane ^ 8 of the same warp.
 //   DOWN:   out[token(p), m] += w_p * (down[m] . H_p)        (fp32 atomics)
 //           or y[p, m] = down[m] . H_p                        (mode 1)
 //
-// The weights are the MMA's A operand (M = 128 lanes), the tokens its B
-// operand (N = BN in {16, 32, 64, 128}, and 256 for the down projection,
-// chosen per segment so small groups do not pay for padding). Roles inside one persistent CTA per SM:
-//   warp 22     weight producer: per 128-K raw stage, one TMA box of packed
-//               nibbles per matrix (128 rows x 64 bytes, 64-byte swizzle)
-//               plus bulk copies of the tile's scales (and zero points) from
-//               the prepared tile-transposed copy -- whole cache lines per
-//               request, nothing for the dequant warps to address.
-//   warps 0-15  dequantise (four warpgroups, each covering all 128 rows =
-//               TMEM lanes): each thread reads 16 bytes of its row from the
-//               raw stage, converts them to fp16 ((n-8)*s + z, one rounding)
-//               and writes them straight into tensor memory with tcgen05.st
-//               -- the dequantised tile never touches shared memory, so the
-//               MMA's shared-memory bandwidth goes to the activation operand
-//               alone. The store of stage i drains while stage i+1 converts.
-//   warp 20     TMA producer for the activation tiles (128-byte swizzle).
-//   warp 21     MMA issuer: tcgen05.mma kind::f16, A from TMEM, B from smem,
+// BN is chosen per segment: the fewest tiles of at most 192 rows, each a
+// multiple of 16 (an M=128 tcgen05.mma costs ~96 SM cycles at N=128 and
+// ~141 at N=256 on B200, so wide tiles use the tensor pipe best; the cap
+// leaves room for two accumulators). Roles inside one persistent CTA per SM:
+//   warp 26     weight producer: per 128-K raw stage, one TMA box of packed
+//               nibbles per matrix (64 or 128 rows x 64 bytes, 64-byte
+//               swizzle) and bulk copies of the scales (and zero points) of
+//               the stage's groups from the prepared tile-transposed copy.
+//   warps 0-15  dequantise: warp w converts, for TMEM lane quadrant w % 4,
+//               32 K of every other A stage (64 K) -- one 16-byte read of its
+//               row from the raw stage, (n-8)*s + z in fp16 with one
+//               rounding, written straight into tensor memory with
+//               tcgen05.st, so shared-memory bandwidth goes to the
+//               activation operand alone. The store of one stage drains
+//               while the next converts.
+//   warp 24     TMA producer for the activation tiles (128-byte swizzle),
+//               one A stage of token rows per ring slot.
+//   warp 25     MMA issuer: tcgen05.mma kind::f16, A from TMEM, B from smem,
 //               fp32 accumulators in TMEM; completion via tcgen05.commit.
-//   warps 16-19 epilogue: tcgen05.ld of the accumulators, SwiGLU (GATEUP) or
-//               the weighted scatter-combine (DOWN).
-// TMEM columns: [0,128) gate / single accumulator, [128,256) up accumulator,
-// [256,512) four 64-column A stages. Every wait is bounded; a wait that gives
-// up raises a CTA-wide abort and the device error word.
+//   warps 16-23 epilogue, two warps per lane quadrant (alternate 16- or
+//               32-column chunks): tcgen05.ld of the accumulators, SwiGLU
+//               (GATEUP) or the weighted scatter-combine (DOWN).
+// TMEM columns: [0,192) and [192,384) two accumulator buffers (the epilogue
+// of one tile runs while the next accumulates), [384,512) four 32-column
+// A stages. Every wait is bounded; a wait that gives up raises a CTA-wide
+// abort and the device error word.
 //
 // The K order inside every group of 8 activations is 0,4,1,5,2,6,3,7: that
 // is the order the nibble conversion produces the weights in, so the
@@ -49,59 +56,50 @@ using namespace wb;
 
 namespace {
 
-constexpr int kDqWarps = 16;            // four warpgroups
-constexpr int kDqThreads = kDqWarps * 32;
-constexpr int kEpiWarp0 = kDqWarps;     // four epilogue warps
-constexpr int kTmaBWarp = kDqWarps + 4;
-constexpr int kMmaWarp = kDqWarps + 5;
-constexpr int kTmaWWarp = kDqWarps + 6;
-constexpr int kThreads = (kDqWarps + 7) * 32;
-constexpr int kAStages = 4;  // A stages in TMEM
-constexpr int BM = 128;
+constexpr int kDqWarps = 16;
+constexpr int kEpiWarps = 8;
+constexpr int kEpiWarp0 = kDqWarps;
+constexpr int kTmaBWarp = kDqWarps + kEpiWarps;
+constexpr int kMmaWarp = kTmaBWarp + 1;
+constexpr int kTmaWWarp = kTmaBWarp + 2;
+constexpr int kThreads = (kTmaWWarp + 1) * 32;
+constexpr int BM = 128;                      // A rows per tile (TMEM lanes)
+constexpr int kGuRows = 64;                  // intermediate rows per gate/up tile
+constexpr int kBNMax = 192;                  // token rows per tile
+constexpr int kAStages = 4;
+constexpr int kAStageCols = 32;              // 64 K of fp16 per lane
+constexpr int kAColBase = 2 * kBNMax;
 constexpr int kTmemCols = 512;
-constexpr int kAColBase = 256;
-constexpr int kRawK = 128;           // K per raw (weight) stage
+static_assert(kAColBase + kAStages * kAStageCols == kTmemCols, "TMEM columns");
+constexpr int KA = 64;                       // K per A stage
+constexpr int kRawK = 128;                   // K per raw (weight) stage = 2 A stages
+// raw stage: [nibbles: gate box, up box (4 KB each) | down box (8 KB)]
+//            [scales: 2 runs of up to 512 B][zero points: the same]
+constexpr int kRawStages = 6;
+constexpr int kScRun = 512;
+constexpr int kScOff = 8192;
+constexpr int kZOff = kScOff + 2 * kScRun;
+constexpr int kRawStageBytes = kZOff + 2 * kScRun;
+static_assert(kRawStageBytes % 1024 == 0, "raw stages keep 1024-byte alignment");
+constexpr int kBStages = 6;
+constexpr int kBStageBytes = kBNMax * 128;   // token rows of one A stage
 // Split K: a call with fewer tiles than half the SMs cuts each tile's K into
 // up to kMaxSplit ranges (work items) so more SMs take part; the down
 // projection's parts add into the output with its usual atomics, gate/up
-// parts go to a scratch buffer and the last part of a tile sums them in
-// order and applies SwiGLU. At most kMaxSplitItems split work items.
+// parts go to a scratch buffer and the last part of a tile's lane quadrant
+// sums them in order and applies SwiGLU. At most kMaxSplitItems items.
 constexpr int kMaxSplit = 8;
 constexpr int kMaxSplitItems = 256;
-constexpr int kMaxFix = 16;   // slices one CTA may complete (<= 4 per item, <= 2 items)
-constexpr size_t kPartialFloats = (size_t)BM * 128 * 2;   // one gate/up work item
-constexpr int kBoxBytes = BM * 64;   // one matrix's nibbles for a raw stage
-constexpr int kScBytes = 512;        // room for 2 scale groups x 128 rows (fp16)
+constexpr int kMaxFix = 16;   // quadrants one CTA may complete (<= 4 per item, <= 2 items)
+constexpr size_t kPartialFloats = (size_t)kBNMax * BM;   // one gate/up work item
 
 enum { GATEUP = 0, DOWN = 1 };
 
-template <int MODE>
-struct Shape {
-  // Tokens per tile. An M=128 tcgen05.mma with A from tensor memory costs
-  // ~96 SM cycles at N <= 128 and ~141 at N = 256 (measured on B200): the
-  // down projection, whose one accumulator leaves room, runs N = 256 tiles;
-  // gate/up keeps two N <= 128 accumulators beside the A stages.
-  static constexpr int kBNMax = MODE == GATEUP ? 128 : 256;
-  static constexpr int KA = MODE == GATEUP ? 64 : 128;            // K per A stage
-  static constexpr int kSub = kRawK / KA;                          // A stages per raw stage
-  static constexpr int kMats = MODE == GATEUP ? 2 : 1;
-  // raw stage: [boxes][scales][zeros], 1 KB multiple
-  static constexpr int kScOff = kMats * kBoxBytes;
-  static constexpr int kZOff = kScOff + kMats * kScBytes;
-  static constexpr int kRawStageBytes = ((kZOff + kMats * kScBytes) + 1023) / 1024 * 1024;
-  static constexpr int kRawStages = MODE == GATEUP ? 6 : 6;
-  static constexpr int kBoxes = KA / 64;                           // 64-K activation boxes per A stage
-  // An activation stage holds kBNMax/BN consecutive A stages' worth of boxes
-  // (BN rows x 128 bytes each), so its size does not depend on BN and small
-  // token groups get a deep prefetch (32 A stages at BN = 16).
-  static constexpr int kBStageBytes = kBoxes * kBNMax * 128;
-  static constexpr int kBStages = MODE == GATEUP ? 5 : 2;
-};
-
 // Prepared weights: per matrix entry (expert v, matrix m in gate/up/down) two
-// TMA descriptors of its packed nibbles (64-byte boxes with the 64-byte
-// swizzle for this kernel, 128-byte boxes with the 128-byte swizzle for the
-// register-path kernel), a zero-point flag, and its scales and zero points
+// TMA descriptors of its packed nibbles (64-byte boxes of 64 rows for gate
+// and up, 128 rows for down, with the 64-byte swizzle for this kernel;
+// 128-byte boxes of 128 rows with the 128-byte swizzle for the register-path
+// kernel), a zero-point flag, and its scales and zero points
 // transposed to [row tile][group][128 rows] so that the scales of one stage
 // are one contiguous run. For the register-path kernel, per expert a second
 // copy of the scales (and zero points) in its unit order: the gate/up pair
@@ -136,14 +134,15 @@ PreparedLayout prepared_layout(const WispMoeConfig* c, int n) {
   return L;
 }
 
+
 struct GemmParams {
-  CUtensorMap tmap[5];  // activation tensor, boxes {64, 16 << i}
+  CUtensorMap tmap[4];  // activation tensor, boxes {64, 16 << i}
   const uint8_t* prepared;
   size_t p_flags, p_scales, p_zeros, p_mat_sc_bytes;
   const WispSegment* segs;
   const int32_t* tiles;  // [0, S]: tile prefix; [S+1, 2S+1): bn per segment; [2S+1]: K split
-  float* partial;        // split gate/up: per work item 128 rows x 128 columns x (gate, up)
-  int* tickets;          // split gate/up: arrivals per tile
+  float* partial;        // split gate/up: per work item [column][128 A rows] floats
+  int* tickets;          // split gate/up: arrivals per (tile, lane quadrant)
   int nseg;
   int M, I, gs;
   __half* h_out;
@@ -184,20 +183,23 @@ struct Prof {
 };
 
 struct SmemLayout {
-  uint64_t rfull[16], rempty[16];
+  uint64_t rfull[kRawStages], rempty[kRawStages];
   uint64_t afull[kAStages], aempty[kAStages];
-  uint64_t bfull[8], bempty[8];
-  uint64_t accfull, accempty, final_bar;
+  uint64_t bfull[kBStages], bempty[kBStages];
+  uint64_t accfull[2], accempty[2], final_bar;
   uint32_t tmem_base;
   int abort;
-  int fix_n;            // split gate/up: 32-row slices this CTA completes
-  int fix[kMaxFix];     // tile * 4 + slice
+  int fix_n;            // split gate/up: lane quadrants this CTA completes
+  int fix[kMaxFix];     // tile * 4 + quadrant
 };
 
 struct TileInfo {
   int seg, expert, row0, nvalid, bn, mblk;
 };
 
+// Tiles are ordered (segment, weight row block, token block) with the token
+// blocks of one weight block adjacent, so CTAs that run them at the same
+// time share the weight tile through L2.
 __device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int tile) {
   // Largest segment s with tiles[s] <= tile (segments with no tiles are
   // skipped because their prefix equals the next one).
@@ -222,19 +224,19 @@ __device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int tile) {
   return t;
 }
 
-__device__ __forceinline__ int bn_slot(int bn) {
-  return bn == 16 ? 0 : bn == 32 ? 1 : bn == 64 ? 2 : bn == 128 ? 3 : 4;
-}
+// A row r of a gate/up tile: matrix (0 gate, 1 up) and row within the tile's
+// 64 intermediate rows.
+__device__ __forceinline__ int gu_matrix(int r) { return (r >> 3) & 1; }
+__device__ __forceinline__ int gu_row(int r) { return ((r >> 4) << 3) | (r & 7); }
 
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_constant__ GemmParams p) {
-  using S = Shape<MODE>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base_u32 = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (base_u32 & 1023)) & 1023);
-  uint8_t* raw_ring = smem;                                          // kRawStages * kRawStageBytes
-  uint8_t* b_ring = raw_ring + S::kRawStages * S::kRawStageBytes;    // kBStages * kBStageBytes
-  SmemLayout* L = reinterpret_cast<SmemLayout*>(b_ring + S::kBStages * S::kBStageBytes);
+  uint8_t* raw_ring = smem;                                   // kRawStages * kRawStageBytes
+  uint8_t* b_ring = raw_ring + kRawStages * kRawStageBytes;   // kBStages * kBStageBytes
+  SmemLayout* L = reinterpret_cast<SmemLayout*>(b_ring + kBStages * kBStageBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = __ldg(p.tiles + p.nseg);
@@ -244,7 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
   if ((int)blockIdx.x >= nitems) return;
   const int K = MODE == GATEUP ? p.M : p.I;
   const int nR = K / kRawK;           // raw stages of the whole K
-  // Raw stages [r0, r1) and A stages [a0, a1) of K part ks.
+  // Raw stages [r0, r1) of K part ks (each item has at least one).
   auto part_range = [&](int ks, int& r0, int& r1) {
     r0 = ks * nR / split;
     r1 = (ks + 1) * nR / split;
@@ -252,20 +254,22 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
   volatile int* abort = &L->abort;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < S::kRawStages; i++) {
+    for (int i = 0; i < kRawStages; i++) {
       mbar_init(&L->rfull[i], 1);
-      mbar_init(&L->rempty[i], kDqThreads / 32);
+      mbar_init(&L->rempty[i], kDqWarps);       // every dequant warp reads every raw stage
     }
     for (int i = 0; i < kAStages; i++) {
-      mbar_init(&L->afull[i], kDqThreads / 32);
+      mbar_init(&L->afull[i], kDqWarps / 2);    // the 8 warps of the stage's parity
       mbar_init(&L->aempty[i], 1);
     }
-    for (int i = 0; i < S::kBStages; i++) {
+    for (int i = 0; i < kBStages; i++) {
       mbar_init(&L->bfull[i], 1);
       mbar_init(&L->bempty[i], 1);
     }
-    mbar_init(&L->accfull, 1);
-    mbar_init(&L->accempty, 4);  // the four epilogue warps
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&L->accfull[i], 1);
+      mbar_init(&L->accempty[i], kEpiWarps);
+    }
     mbar_init(&L->final_bar, 1);
     L->abort = 0;
     L->fix_n = 0;
@@ -283,20 +287,24 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
 
   if (warp < kDqWarps) {
     // ------------------------------------------------------------------
-    // Dequantisation warps: thread = weight row of the tile = TMEM lane.
-    // Warpgroup q converts one 32-K quarter of each A stage:
-    //   GATEUP: q = 2*matrix + half (gate K 0-31, gate 32-63, up 0-31, up 32-63)
-    //   DOWN:   q = K quarter of the 128-K stage.
+    // Dequantisation. A stage j of the CTA (2 per raw stage) belongs to the
+    // warps of parity j % 2; warp w converts K half (w >> 2) & 1 of it for
+    // TMEM lanes 32 (w % 4) .. +31, one A row per thread.
     // ------------------------------------------------------------------
-    const int t = threadIdx.x;
-    const int q = t >> 7;
-    const int r = t & 127;
-    const int sw = (r >> 1) & 3;        // 64-byte swizzle of this row
-    const int mat = MODE == GATEUP ? (q >> 1) : 2;
-    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    int rslot = 0, sa = 0, prev_sa = -1;
-    uint32_t rphase = 0, aphase = 0;
-    int item = 0;
+    const int qd = warp & 3, hk = (warp >> 2) & 1, pg = warp >> 3;
+    const int r = qd * 32 + lane;
+    const int beta = MODE == GATEUP ? gu_matrix(r) : 0;
+    const int rho = MODE == GATEUP ? gu_row(r) : r;
+    // 16-byte chunk (K 32c..32c+31 of the raw stage) of this thread's row,
+    // under the box's 64-byte swizzle: conflict-free, the 8 threads of a
+    // quarter-warp read 8 rows of one box.
+    const int chunk = 2 * pg + hk;
+    const uint32_t rd_off = (uint32_t)(beta * 4096 + rho * 64 + ((chunk ^ ((rho >> 1) & 3)) << 4));
+    const int gl = (pg * KA + hk * 32) / p.gs;   // scale group inside the raw stage
+    const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
+    const uint32_t st_col = kAColBase + hk * 16;
+    int ir = 0;          // raw stages this CTA has consumed
+    int prev_sa = -1;
     bool ok = true;
     Prof pf(p.counters);
     for (int it = blockIdx.x; it < nitems && ok && !*abort; it += gridDim.x) {
@@ -304,27 +312,23 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       int r0, r1;
       part_range(it - tile * split, r0, r1);
       const TileInfo ti = decode_tile(p, tile);
+      const int mat = MODE == GATEUP ? beta : 2;
       const bool has_zero = __ldg(flags + ti.expert * 3 + mat) & 1;
-      for (int ks = r0 * S::kSub; ks < r1 * S::kSub; ks++, item++) {
-        const int sub = ks % S::kSub;
+      // row inside the stage's scale run (the 128-row tile of the prepared copy)
+      const int srow = MODE == GATEUP ? (ti.mblk & 1) * kGuRows + rho : rho;
+      const uint32_t s_off = (uint32_t)(kScOff + beta * kScRun + (gl * BM + srow) * 2);
+      for (int rs = r0; rs < r1; rs++, ir++) {
+        const int rslot = ir % kRawStages;
         long long t0 = pf.now();
-        if (sub == 0 && !mbar_wait(&L->rfull[rslot], rphase, abort)) { ok = false; break; }
+        if (!mbar_wait(&L->rfull[rslot], (uint32_t)(ir / kRawStages) & 1, abort)) { ok = false; break; }
         pf.add(0, t0);
-        const uint8_t* rs = raw_ring + rslot * S::kRawStageBytes;
-        const uint8_t* box = rs + (MODE == GATEUP ? mat * kBoxBytes : 0);
-        // 16-byte chunk of the 64-byte row this thread converts
-        const int c = MODE == GATEUP ? 2 * sub + (q & 1) : q;
-        const uint4 qv = *reinterpret_cast<const uint4*>(box + r * 64 + ((c ^ sw) << 4));
-        const int gl = (c * 32) / p.gs;
-        const int so = (MODE == GATEUP ? mat * kScBytes : 0) + (gl * BM + r) * 2;
-        const __half s = *reinterpret_cast<const __half*>(rs + S::kScOff + so);
-        const __half z = has_zero ? *reinterpret_cast<const __half*>(rs + S::kZOff + so)
+        const uint8_t* rsb = raw_ring + rslot * kRawStageBytes;
+        const uint4 qv = *reinterpret_cast<const uint4*>(rsb + rd_off);
+        const __half s = *reinterpret_cast<const __half*>(rsb + s_off);
+        const __half z = has_zero ? *reinterpret_cast<const __half*>(rsb + s_off + (kZOff - kScOff))
                                   : __float2half(0.f);
-        if (sub == S::kSub - 1) {
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&L->rempty[rslot]);
-          if (++rslot == S::kRawStages) { rslot = 0; rphase ^= 1; }
-        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&L->rempty[rslot]);
         const __half2 s2 = __halves2half2(s, s), z2 = __halves2half2(z, z);
         uint32_t v[16];
         const uint32_t words[4] = {qv.x, qv.y, qv.z, qv.w};
@@ -348,13 +352,17 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
           if (lane == 0) mbar_arrive(&L->afull[prev_sa]);
           prev_sa = -1;
         }
+        const int ia = 2 * ir + pg;
+        const int sa = ia % kAStages;
         t0 = pf.now();
-        if (item >= kAStages && !mbar_wait(&L->aempty[sa], aphase ^ 1, abort)) { ok = false; break; }
+        if (ia >= kAStages && !mbar_wait(&L->aempty[sa], (uint32_t)(ia / kAStages - 1) & 1, abort)) {
+          ok = false;
+          break;
+        }
         pf.add(1, t0);
         tc_fence_after();
-        tmem_st16(tmem + lane_base + (uint32_t)(kAColBase + sa * 64 + q * 16), v);
+        tmem_st16(tmem + lane_base + st_col + (uint32_t)(sa * kAStageCols), v);
         prev_sa = sa;
-        if (++sa == kAStages) { sa = 0; aphase ^= 1; }
       }
     }
     if (prev_sa >= 0) {
@@ -374,10 +382,9 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
     if (lane == 0) {
       const int ng = kRawK / p.gs;        // scale groups per raw stage (1 or 2)
       const int gpr = K / p.gs;           // groups per weight row
-      int rslot = 0, item = 0;
-      uint32_t rphase = 0;
-      int last_phase[16];
-      for (int i = 0; i < 16; i++) last_phase[i] = -1;
+      const int nm = MODE == GATEUP ? 2 : 1;
+      const uint32_t run = (uint32_t)(ng * BM * 2);
+      int ir = 0;
       bool ok = true;
       Prof pf(p.counters);
       for (int it = blockIdx.x; it < nitems && ok && !*abort; it += gridDim.x) {
@@ -385,38 +392,38 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
         int r0, r1;
         part_range(it - tile * split, r0, r1);
         const TileInfo ti = decode_tile(p, tile);
-        const int m0 = MODE == GATEUP ? 0 : 2;
+        const int tile128 = MODE == GATEUP ? ti.mblk >> 1 : ti.mblk;
+        const int wrow = MODE == GATEUP ? ti.mblk * kGuRows : ti.mblk * BM;
         uint32_t bytes = 0;
-        bool hz[2];
-        const CUtensorMap* map[2];
-        const uint8_t* sc[2];
-        const uint8_t* zr[2];
-#pragma unroll
-        for (int j = 0; j < S::kMats; j++) {
-          const int e = ti.expert * 3 + m0 + j;
+        bool hz[2] = {false, false};
+        const CUtensorMap* map[2] = {nullptr, nullptr};
+        const uint8_t* sc[2] = {nullptr, nullptr};
+        const uint8_t* zr[2] = {nullptr, nullptr};
+        for (int j = 0; j < nm; j++) {
+          const int e = ti.expert * 3 + (MODE == GATEUP ? j : 2);
           hz[j] = __ldg(flags + e) & 1;
           map[j] = reinterpret_cast<const CUtensorMap*>(p.prepared + (size_t)e * sizeof(CUtensorMap));
-          sc[j] = p.prepared + p.p_scales + (size_t)e * p.p_mat_sc_bytes +
-                  (size_t)ti.mblk * gpr * BM * 2;
-          zr[j] = p.prepared + p.p_zeros + (size_t)e * p.p_mat_sc_bytes +
-                  (size_t)ti.mblk * gpr * BM * 2;
-          bytes += kBoxBytes + ng * BM * 2 * (hz[j] ? 2 : 1);
+          sc[j] = p.prepared + p.p_scales + (size_t)e * p.p_mat_sc_bytes + (size_t)tile128 * gpr * BM * 2;
+          zr[j] = p.prepared + p.p_zeros + (size_t)e * p.p_mat_sc_bytes + (size_t)tile128 * gpr * BM * 2;
+          bytes += (MODE == GATEUP ? 4096u : 8192u) + run * (hz[j] ? 2u : 1u);
         }
-        for (int rs = r0; rs < r1; rs++, item++) {
+        for (int rs = r0; rs < r1; rs++, ir++) {
+          const int rslot = ir % kRawStages;
           const long long t0 = pf.now();
-          if (item >= S::kRawStages && !mbar_wait(&L->rempty[rslot], rphase ^ 1, abort)) { ok = false; break; }
-          pf.add(0, t0);
-          uint8_t* dst = raw_ring + rslot * S::kRawStageBytes;
-          mbar_arrive_expect_tx(&L->rfull[rslot], bytes);
-#pragma unroll
-          for (int j = 0; j < S::kMats; j++) {
-            tma_load_2d(dst + j * kBoxBytes, map[j], &L->rfull[rslot], rs * 64, ti.mblk * BM);
-            const size_t goff = (size_t)(rs * kRawK / p.gs) * BM * 2;
-            bulk_load(dst + S::kScOff + j * kScBytes, sc[j] + goff, ng * BM * 2, &L->rfull[rslot]);
-            if (hz[j]) bulk_load(dst + S::kZOff + j * kScBytes, zr[j] + goff, ng * BM * 2, &L->rfull[rslot]);
+          if (ir >= kRawStages &&
+              !mbar_wait(&L->rempty[rslot], (uint32_t)(ir / kRawStages - 1) & 1, abort)) {
+            ok = false;
+            break;
           }
-          last_phase[rslot] = (int)rphase;
-          if (++rslot == S::kRawStages) { rslot = 0; rphase ^= 1; }
+          pf.add(0, t0);
+          uint8_t* dst = raw_ring + rslot * kRawStageBytes;
+          mbar_arrive_expect_tx(&L->rfull[rslot], bytes);
+          const size_t goff = (size_t)rs * ng * BM * 2;
+          for (int j = 0; j < nm; j++) {
+            tma_load_2d(dst + j * 4096, map[j], &L->rfull[rslot], rs * (kRawK / 2), wrow);
+            bulk_load(dst + kScOff + j * kScRun, sc[j] + goff, run, &L->rfull[rslot]);
+            if (hz[j]) bulk_load(dst + kZOff + j * kScRun, zr[j] + goff, run, &L->rfull[rslot]);
+          }
         }
       }
       {
@@ -424,129 +431,100 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
         pf.flush(slots, C_TW_TOTAL, true);
       }
       // Let every issued copy land before the CTA can exit.
-      for (int i = 0; i < S::kRawStages; i++)
-        if (last_phase[i] >= 0) mbar_wait(&L->rfull[i], (uint32_t)last_phase[i], abort, 200000000LL);
+      for (int j = max(0, ir - kRawStages); j < ir; j++)
+        mbar_wait(&L->rfull[j % kRawStages], (uint32_t)(j / kRawStages) & 1, abort, 200000000LL);
     }
   } else if (warp == kTmaBWarp) {
     // ------------------------------------------------------------------
-    // Activation producer.
+    // Activation producer: per A stage, the tile's token rows x 64 K as up
+    // to four boxes (128, 64, 32, 16 rows) stacked in one ring slot.
     // ------------------------------------------------------------------
     if (lane == 0) {
-      for (int i = 0; i < 5; i++) tma_prefetch_desc(&p.tmap[i]);
-      int sb = 0;
-      uint32_t bphase = 0;
-      int item = 0;
-      int last_phase[8];
-      for (int i = 0; i < 8; i++) last_phase[i] = -1;
+      for (int i = 0; i < 4; i++) tma_prefetch_desc(&p.tmap[i]);
+      int ia = 0;
       bool ok = true;
       Prof pf(p.counters);
       for (int it = blockIdx.x; it < nitems && ok && !*abort; it += gridDim.x) {
         const int tile = it / split;
         int r0, r1;
         part_range(it - tile * split, r0, r1);
-        const int a_end = r1 * S::kSub;
         const TileInfo ti = decode_tile(p, tile);
-        const CUtensorMap* tm = &p.tmap[bn_slot(ti.bn)];
-        const int per_b = S::kBNMax / ti.bn;       // A stages per activation stage
-        const int box_bytes = ti.bn * 128;
-        for (int a0 = r0 * S::kSub; a0 < a_end; a0 += per_b, item++) {
-          const int na = min(per_b, a_end - a0);
+        for (int ka = 2 * r0; ka < 2 * r1; ka++, ia++) {
+          const int sb = ia % kBStages;
           const long long t0 = pf.now();
-          if (item >= S::kBStages && !mbar_wait(&L->bempty[sb], bphase ^ 1, abort)) { ok = false; break; }
+          if (ia >= kBStages &&
+              !mbar_wait(&L->bempty[sb], (uint32_t)(ia / kBStages - 1) & 1, abort)) {
+            ok = false;
+            break;
+          }
           pf.add(0, t0);
-          mbar_arrive_expect_tx(&L->bfull[sb], (uint32_t)(na * S::kBoxes * box_bytes));
-          uint8_t* dst = b_ring + sb * S::kBStageBytes;
-          for (int a = 0; a < na; a++)
+          mbar_arrive_expect_tx(&L->bfull[sb], (uint32_t)(ti.bn * 128));
+          uint8_t* dst = b_ring + sb * kBStageBytes;
+          int done = 0;
 #pragma unroll
-            for (int bx = 0; bx < S::kBoxes; bx++)
-              tma_load_2d(dst + (a * S::kBoxes + bx) * box_bytes, tm, &L->bfull[sb],
-                          (a0 + a) * S::KA + bx * 64, ti.row0);
-          last_phase[sb] = (int)bphase;
-          if (++sb == S::kBStages) { sb = 0; bphase ^= 1; }
+          for (int lg = 3; lg >= 0; lg--) {
+            if ((ti.bn >> 4) & (1 << lg)) {
+              tma_load_2d(dst + done * 128, &p.tmap[lg], &L->bfull[sb], ka * KA, ti.row0 + done);
+              done += 16 << lg;
+            }
+          }
         }
       }
       {
         const int slots[4] = {C_TB_BEMPTY, -1, -1, -1};
         pf.flush(slots, C_TB_TOTAL, true);
       }
-      for (int i = 0; i < S::kBStages; i++)
-        if (last_phase[i] >= 0) mbar_wait(&L->bfull[i], (uint32_t)last_phase[i], abort, 200000000LL);
+      for (int j = max(0, ia - kBStages); j < ia; j++)
+        mbar_wait(&L->bfull[j % kBStages], (uint32_t)(j / kBStages) & 1, abort, 200000000LL);
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------
-    // MMA issuer (one thread).
+    // MMA issuer (one thread): per A stage four M=128 x N=bn x K=16 MMAs
+    // into the item's accumulator buffer (items alternate buffers).
     // ------------------------------------------------------------------
     if (lane == 0) {
-      int sa = 0, sb = 0;
-      uint32_t aphase = 0, bphase = 0, accphase = 0;
       const uint64_t bdesc0 = smem_desc_sw128(smem_u32(b_ring));
-      int ntile_local = 0;
+      int ia = 0, nloc = 0;
       bool ok = true;
       Prof pf(p.counters);
-      for (int it = blockIdx.x; it < nitems && ok && !*abort; it += gridDim.x, ntile_local++) {
+      for (int it = blockIdx.x; it < nitems && ok && !*abort; it += gridDim.x, nloc++) {
         const int tile = it / split;
         int r0, r1;
         part_range(it - tile * split, r0, r1);
-        const int a_beg = r0 * S::kSub, a_end = r1 * S::kSub;
         const TileInfo ti = decode_tile(p, tile);
         const uint32_t idesc = idesc_f16_m128(ti.bn);
-        const int per_b = S::kBNMax / ti.bn;
-        const uint32_t box16 = (uint32_t)(ti.bn * 128) >> 4;   // one box, in descriptor units
+        const int ab = nloc & 1;
+        const uint32_t d_tmem = tmem + (uint32_t)(ab * kBNMax);
         long long t0 = pf.now();
-        if (ntile_local > 0 && !mbar_wait(&L->accempty, accphase ^ 1, abort)) break;
+        if (nloc >= 2 && !mbar_wait(&L->accempty[ab], (uint32_t)((nloc >> 1) - 1) & 1, abort)) break;
         pf.add(2, t0);
         tc_fence_after();
-        int a = 0;   // A stage within the current activation stage
-        for (int ks = a_beg; ks < a_end; ks++) {
-          if (a == 0) {
-            t0 = pf.now();
-            if (!mbar_wait(&L->bfull[sb], bphase, abort)) { ok = false; break; }
-            pf.add(1, t0);
-          }
+        const int na = 2 * (r1 - r0);
+        for (int a = 0; a < na; a++, ia++) {
+          const int sa = ia % kAStages, sb = ia % kBStages;
           t0 = pf.now();
-          if (!mbar_wait(&L->afull[sa], aphase, abort)) { ok = false; break; }
+          if (!mbar_wait(&L->bfull[sb], (uint32_t)(ia / kBStages) & 1, abort)) { ok = false; break; }
+          pf.add(1, t0);
+          t0 = pf.now();
+          if (!mbar_wait(&L->afull[sa], (uint32_t)(ia / kAStages) & 1, abort)) { ok = false; break; }
           pf.add(0, t0);
           tc_fence_after();
-          const uint32_t a_col = tmem + kAColBase + sa * 64;
-          const uint64_t bd = bdesc0 + (uint64_t)((sb * S::kBStageBytes) >> 4) +
-                              (uint64_t)(a * S::kBoxes) * box16;
-          if (MODE == GATEUP) {
-            if (ks == a_beg) {
-              mma_f16_ts_c<0>(tmem + 0, a_col, bd, idesc);
-              mma_f16_ts_c<0>(tmem + 128, a_col + 32, bd, idesc);
-            } else {
-              mma_f16_ts_c<1>(tmem + 0, a_col, bd, idesc);
-              mma_f16_ts_c<1>(tmem + 128, a_col + 32, bd, idesc);
-            }
+          const uint32_t a_col = tmem + (uint32_t)(kAColBase + sa * kAStageCols);
+          const uint64_t bd = bdesc0 + (uint64_t)((sb * kBStageBytes) >> 4);
+          if (a == 0) mma_f16_ts_c<0>(d_tmem, a_col, bd, idesc);
+          else mma_f16_ts_c<1>(d_tmem, a_col, bd, idesc);
 #pragma unroll
-            for (int kk = 1; kk < 4; kk++) {
-              mma_f16_ts_c<1>(tmem + 0, a_col + kk * 8, bd + 2 * kk, idesc);
-              mma_f16_ts_c<1>(tmem + 128, a_col + 32 + kk * 8, bd + 2 * kk, idesc);
-            }
-          } else {
-            if (ks == a_beg) mma_f16_ts_c<0>(tmem + 0, a_col, bd, idesc);
-            else mma_f16_ts_c<1>(tmem + 0, a_col, bd, idesc);
-#pragma unroll
-            for (int kk = 1; kk < 8; kk++)
-              mma_f16_ts_c<1>(tmem + 0, a_col + kk * 8,
-                              bd + (uint64_t)((kk >> 2) * box16 + 2 * (kk & 3)), idesc);
-          }
+          for (int kk = 1; kk < 4; kk++) mma_f16_ts_c<1>(d_tmem, a_col + kk * 8, bd + 2 * kk, idesc);
           mma_commit(&L->aempty[sa]);
-          if (++sa == kAStages) { sa = 0; aphase ^= 1; }
-          if (++a == per_b || ks == a_end - 1) {
-            mma_commit(&L->bempty[sb]);
-            a = 0;
-            if (++sb == S::kBStages) { sb = 0; bphase ^= 1; }
-          }
+          mma_commit(&L->bempty[sb]);
         }
         if (!ok) break;
-        mma_commit(&L->accfull);
-        accphase ^= 1;
+        mma_commit(&L->accfull[ab]);
       }
       {
         const int slots[4] = {C_MMA_AFULL, C_MMA_BFULL, C_MMA_ACCEMPTY, -1};
         pf.flush(slots, C_MMA_TOTAL, true);
-        if (p.counters) atomicAdd(p.counters + C_TILES, (unsigned long long)ntile_local);
+        if (p.counters) atomicAdd(p.counters + C_TILES, (unsigned long long)nloc);
       }
       // Drain: make sure no MMA is still running before TMEM is released.
       mma_commit(&L->final_bar);
@@ -554,90 +532,92 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
     }
   } else {
     // ------------------------------------------------------------------
-    // Epilogue warps 16-19: warp q owns accumulator rows 32q..32q+31.
+    // Epilogue warps 16-23: warp w reads accumulator lanes 32 (w % 4) ..
+    // +31; the two warps of a quadrant take alternate column chunks.
     // ------------------------------------------------------------------
-    const int q = warp & 3;
-    const int r = q * 32 + lane;
-    uint32_t accphase = 0;
+    const int qd = warp & 3, ch = (warp - kEpiWarp0) >> 2;
+    const int r = qd * 32 + lane;
+    const uint32_t lane_addr = tmem + ((uint32_t)(qd * 32) << 16);
+    int nloc = 0;
     Prof pf(p.counters);
-    for (int it = blockIdx.x; it < nitems && !*abort; it += gridDim.x) {
+    for (int it = blockIdx.x; it < nitems && !*abort; it += gridDim.x, nloc++) {
       const int tile = it / split;
       const TileInfo ti = decode_tile(p, tile);
+      const int ab = nloc & 1;
       const long long t0 = pf.now();
-      if (!mbar_wait(&L->accfull, accphase, abort)) break;
+      if (!mbar_wait(&L->accfull[ab], (uint32_t)(nloc >> 1) & 1, abort)) break;
       pf.add(0, t0);
-      accphase ^= 1;
       tc_fence_after();
-      const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+      const uint32_t acc = lane_addr + (uint32_t)(ab * kBNMax);
       bool released = false;
       if (MODE == GATEUP) {
-        const int i = ti.mblk * BM + r;
-        const int islot = k_interleave_slot(i);
+        const int beta = gu_matrix(r);
         if (split == 1) {
-          for (int c0 = 0; c0 < ti.bn; c0 += 16) {
-            uint32_t g[16], u[16];
-            tmem_ld16(lane_addr + c0, g);
-            tmem_ld16(lane_addr + 128 + c0, u);
+          const int islot = k_interleave_slot(ti.mblk * kGuRows + gu_row(r));
+          for (int c0 = 16 * ch; c0 < ti.bn; c0 += 32) {
+            uint32_t a[16];
+            tmem_ld16(acc + c0, a);
             tmem_wait_ld();
+            // Column pair (j, j+1): the gate lane finishes column j, its up
+            // partner (lane ^ 8) column j+1; one exchange serves both.
 #pragma unroll
-            for (int j = 0; j < 16; j++) {
-              const int tt = c0 + j;
-              if (tt < ti.nvalid) {
-                const float hv = silu(__uint_as_float(g[j])) * __uint_as_float(u[j]);
-                p.h_out[(size_t)(ti.row0 + tt) * p.I + islot] = __float2half(hv);
-              }
+            for (int j = 0; j < 16; j += 2) {
+              const float mine_lo = __uint_as_float(a[j]), mine_hi = __uint_as_float(a[j + 1]);
+              const float got = __shfl_xor_sync(0xffffffffu, beta ? mine_lo : mine_hi, 8);
+              const float g = beta ? got : mine_lo;
+              const float u = beta ? mine_hi : got;
+              const int col = c0 + j + beta;
+              if (col < ti.nvalid)
+                p.h_out[(size_t)(ti.row0 + col) * p.I + islot] = __float2half(silu(g) * u);
             }
           }
         } else {
-          // This K part's (gate, up) sums go to the scratch item, laid out
-          // [column][gate/up][row] so that a warp's 32 rows are one
-          // contiguous run; the CTA that completes the tile's rows 32q..
-          // (a per-tile, per-warp arrival count decides which) sums all
-          // parts in order after its last item.
+          // This K part's sums go to the scratch item, laid out [column][A
+          // row]; the CTA whose arrival completes the tile's quadrant (both
+          // of its warps, every part) sums all parts in order after its
+          // last item.
           float* pit = p.partial + (size_t)it * kPartialFloats + r;
-          for (int c0 = 0; c0 < ti.bn; c0 += 16) {
-            uint32_t g[16], u[16];
-            tmem_ld16(lane_addr + c0, g);
-            tmem_ld16(lane_addr + 128 + c0, u);
+          for (int c0 = 16 * ch; c0 < ti.bn; c0 += 32) {
+            uint32_t a[16];
+            tmem_ld16(acc + c0, a);
             tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 16; j++) {
-              pit[((c0 + j) * 2 + 0) * BM] = __uint_as_float(g[j]);
-              pit[((c0 + j) * 2 + 1) * BM] = __uint_as_float(u[j]);
-            }
+            for (int j = 0; j < 16; j++) pit[(size_t)(c0 + j) * BM] = __uint_as_float(a[j]);
           }
           tc_fence_before();
           __threadfence();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&L->accempty);
+          if (lane == 0) mbar_arrive(&L->accempty[ab]);
           released = true;
           int old = 0;
           if (lane == 0) {
             __threadfence();
-            old = atomicAdd(p.tickets + tile * 4 + q, 1);
+            old = atomicAdd(p.tickets + tile * 4 + qd, 1);
             __threadfence();
           }
           old = __shfl_sync(0xffffffffu, old, 0);
-          if (old == split - 1 && lane == 0) {
+          if (old == 2 * split - 1 && lane == 0) {
             const int slot = atomicAdd(&L->fix_n, 1);
-            if (slot < kMaxFix) L->fix[slot] = tile * 4 + q;
+            if (slot < kMaxFix) L->fix[slot] = tile * 4 + qd;
             else atomicExch(&L->abort, 1);  // cannot happen: items per CTA are bounded
           }
         }
       } else {
         const int m = ti.mblk * BM + r;
-        for (int c0 = 0; c0 < ti.bn; c0 += 32) {
+        for (int c0 = 32 * ch; c0 < ti.bn; c0 += 64) {
           // tokens and router weights of these 32 columns: one per lane,
           // broadcast below (no dependent loads inside the store loop)
           const int myrow = ti.row0 + c0 + lane;
           const bool mine = c0 + lane < ti.nvalid;
           const int tok_l = (p.mode == 0 && mine) ? __ldg(p.row_token + myrow) : 0;
           const float w_l = (p.mode == 0 && mine) ? __ldg(p.row_weight + myrow) : 0.f;
-          // columns c0..c0+31 (past bn they are other accumulator columns,
-          // never stored)
           uint32_t ya[16], yb[16];
-          tmem_ld16(lane_addr + c0, ya);
-          tmem_ld16(lane_addr + c0 + 16, yb);
+          tmem_ld16(acc + c0, ya);
+          if (c0 + 16 < ti.bn) tmem_ld16(acc + c0 + 16, yb);
+          else {
+#pragma unroll
+            for (int j = 0; j < 16; j++) yb[j] = 0u;
+          }
           tmem_wait_ld();
 #pragma unroll
           for (int j = 0; j < 32; j++) {
@@ -657,7 +637,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       if (!released) {
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&L->accempty);
+        if (lane == 0) mbar_arrive(&L->accempty[ab]);
       }
     }
     const int slots[4] = {C_EPI_ACCFULL, -1, -1, -1};
@@ -666,25 +646,27 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
 
   tc_fence_before();
   __syncthreads();
-  // Split gate/up: every thread of the CTA sums the parts of the slices it
-  // completes (K parts in order), applies SwiGLU and writes H; the partial
+  // Split gate/up: every thread of the CTA sums the parts of the quadrants
+  // it completes (K parts in order), applies SwiGLU and writes H; the partial
   // sums were published before the arrival counts (fence, then the count;
   // the completing warp fenced after reading it, then the CTA barrier).
   if (MODE == GATEUP && split > 1 && !L->abort) {
     const int nfix = min(L->fix_n, kMaxFix);
     for (int f = 0; f < nfix; f++) {
-      const int tile = L->fix[f] >> 2, q = L->fix[f] & 3;
+      const int tile = L->fix[f] >> 2, qd = L->fix[f] & 3;
       const TileInfo ti = decode_tile(p, tile);
-      const float* base = p.partial + (size_t)tile * split * kPartialFloats + q * 32;
-      for (int i = threadIdx.x; i < 32 * ti.nvalid; i += blockDim.x) {
-        const int rr = i & 31, c = i >> 5;
-        const float* pc = base + (size_t)c * 2 * BM + rr;
-        float g = __ldcg(pc), u = __ldcg(pc + BM);
+      const float* base = p.partial + (size_t)tile * split * kPartialFloats;
+      // 16 (gate, up) row pairs per quadrant
+      for (int i = threadIdx.x; i < 16 * ti.nvalid; i += blockDim.x) {
+        const int pr = i & 15, c = i >> 4;
+        const int rg = qd * 32 + ((pr >> 3) << 4) + (pr & 7);   // gate lane; up lane rg + 8
+        const float* pc = base + (size_t)c * BM + rg;
+        float g = __ldcg(pc), u = __ldcg(pc + 8);
         for (int ks = 1; ks < split; ks++) {
           g += __ldcg(pc + ks * kPartialFloats);
-          u += __ldcg(pc + ks * kPartialFloats + BM);
+          u += __ldcg(pc + ks * kPartialFloats + 8);
         }
-        const int row = ti.mblk * BM + q * 32 + rr;
+        const int row = ti.mblk * kGuRows + gu_row(rg);
         p.h_out[(size_t)(ti.row0 + c) * p.I + k_interleave_slot(row)] = __float2half(silu(g) * u);
       }
     }
@@ -696,7 +678,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
   }
 }
 
-// Per segment: BN (16/32/64/128/256 by row count, at most max_bn) and the
+// Per segment: BN (the fewest tiles of at most kBNMax rows, rounded up to
+// a multiple of 16) and the
 // prefix sum of tiles; then the K split (tiles[2 nseg + 1]): when the tiles
 // fill fewer than half of `target` SMs, each is cut into up to max_split K
 // parts of at least one raw stage (nraw stages in all), at most
@@ -704,7 +687,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
 // tile) are zeroed. Segments of at most skip_rows rows belong to the
 // register-path kernel and get no tiles here.
 __device__ void plan_tiles(const WispSegment* __restrict__ segs, int nseg, int mblocks,
-                           int skip_rows, int max_bn, int max_split, int target, int nraw,
+                           int skip_rows, int max_split, int target, int nraw,
                            int32_t* __restrict__ tiles, int32_t* __restrict__ tickets) {
   __shared__ int32_t warp_tot[32];
   __shared__ int32_t carry;
@@ -715,7 +698,8 @@ __device__ void plan_tiles(const WispSegment* __restrict__ segs, int nseg, int m
     int n = 0, bn = 16;
     if (s < nseg) {
       const int rows = segs[s].rows;
-      bn = rows <= 16 ? 16 : rows <= 32 ? 32 : rows <= 64 ? 64 : rows <= 128 || max_bn < 256 ? 128 : 256;
+      const int nt = (max(rows, 1) + kBNMax - 1) / kBNMax;
+      bn = ((max(rows, 1) + nt - 1) / nt + 15) & ~15;
       n = rows > skip_rows ? ((rows + bn - 1) / bn) * mblocks : 0;
       tiles[nseg + 1 + s] = bn;
     }
@@ -881,7 +865,7 @@ __global__ void __launch_bounds__(128) quant_rows_kernel(const WispSegment* __re
 struct PlanArgs {
   const WispSegment* segs;
   int nseg, sk_rows;
-  int mb_gu, mb_dn, bn_gu, bn_dn;
+  int mb_gu, mb_dn;
   int split_gu, split_dn, nraw_gu, nraw_dn, sms;
   int32_t* tickets;
   int per_gu, per_dn, cols, ks_dn, nk_dn, target;
@@ -891,11 +875,11 @@ struct PlanArgs {
 __global__ void __launch_bounds__(1024) plan_all_kernel(const __grid_constant__ PlanArgs a) {
   switch (blockIdx.x) {
     case 0:
-      plan_tiles(a.segs, a.nseg, a.mb_gu, a.sk_rows, a.bn_gu, a.split_gu, a.sms, a.nraw_gu,
+      plan_tiles(a.segs, a.nseg, a.mb_gu, a.sk_rows, a.split_gu, a.sms, a.nraw_gu,
                  a.tiles_gu, a.tickets);
       break;
     case 1:
-      plan_tiles(a.segs, a.nseg, a.mb_dn, a.sk_rows, a.bn_dn, a.split_dn, a.sms, a.nraw_dn,
+      plan_tiles(a.segs, a.nseg, a.mb_dn, a.sk_rows, a.split_dn, a.sms, a.nraw_dn,
                  a.tiles_dn, nullptr);
       break;
     case 2: plan_units(a.segs, a.nseg, a.per_gu, a.cols, a.sk_rows, 1, 1, 0, a.units_gu); break;
@@ -1021,14 +1005,15 @@ bool encode_q16_map(CUtensorMap* m, const void* base, int rows, int cols, int bo
          CUDA_SUCCESS;
 }
 
-// Packed nibbles of one matrix [rows x cols/2 bytes]: boxes of 64 bytes x
-// 128 rows with the 64-byte swizzle (conflict-free 16-byte reads per row).
-bool encode_packed_map(CUtensorMap* m, const void* base, int rows, int cols) {
+// Packed nibbles of one matrix [rows x cols/2 bytes] for the tensor-core
+// kernel: boxes of 64 bytes x box_rows rows (64 for gate and up, 128 for
+// down) with the 64-byte swizzle (conflict-free 16-byte reads per row).
+bool encode_packed_map(CUtensorMap* m, const void* base, int rows, int cols, int box_rows) {
   EncodeTiledFn fn = get_encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols / 2, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)cols / 2};
-  cuuint32_t box[2] = {64, (cuuint32_t)BM};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
@@ -1051,10 +1036,8 @@ bool encode_packed_map_sk(CUtensorMap* m, const void* base, int rows, int cols) 
          CUDA_SUCCESS;
 }
 
-template <int MODE>
 size_t smem_bytes() {
-  using S = Shape<MODE>;
-  return 1024 + (size_t)S::kRawStages * S::kRawStageBytes + (size_t)S::kBStages * S::kBStageBytes +
+  return 1024 + (size_t)kRawStages * kRawStageBytes + (size_t)kBStages * kBStageBytes +
          sizeof(SmemLayout);
 }
 
@@ -1123,7 +1106,8 @@ extern "C" WispError wisp_b200_prepare_experts(const WispMoeConfig* cfg,
       if (((uintptr_t)mt.packed & 15) || ((uintptr_t)mt.scales & 1) || ((uintptr_t)mt.zeros & 1))
         return WB_FAIL(WISP_ERR_INVALID_ARG,
                        "prepare_experts: entry %d matrix %d: packed must be 16-byte aligned", v, m);
-      if (!encode_packed_map(&maps[(size_t)v * 3 + m], mt.packed, rows, cols) ||
+      if (!encode_packed_map(&maps[(size_t)v * 3 + m], mt.packed, rows, cols,
+                             m == 2 ? BM : kGuRows) ||
           !encode_packed_map_sk(&maps_sk[(size_t)v * 3 + m], mt.packed, rows, cols))
         return WB_FAIL(WISP_ERR_CUDA, "prepare_experts: cuTensorMapEncodeTiled failed (entry %d)", v);
       flags[(size_t)v * 3 + m] = mt.zeros ? 1 : 0;
@@ -1159,7 +1143,7 @@ extern "C" WispError wisp_b200_prepare_experts(const WispMoeConfig* cfg,
 // [prefix S+1 | bn S | K split] each, the register path's gate/up and down
 // unit prefixes [S+2] each, the split gate/up arrival counts [4 x
 // kMaxSplitItems] (int32 words); then, 256-byte aligned, the split gate/up
-// partial sums [kMaxSplitItems x 128 x 128 x 2 floats], and the q16 rows
+// partial sums [kMaxSplitItems x 192 columns x 128 A rows floats], and the q16 rows
 // (layout in skinny.h) of the register-path segments' input and of their
 // SwiGLU output H.
 namespace {
@@ -1269,7 +1253,7 @@ WispError wb::grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
   const PreparedLayout PL = prepared_layout(cfg, n_entries);
   GemmParams gu, dn;
   memset(&gu, 0, sizeof gu);
-  for (int i = 0; i < 5; i++) {
+  for (int i = 0; i < 4; i++) {
     if (!encode_rows_map(&gu.tmap[i], d_xp, rows_capacity, M, 16 << i))
       return WB_FAIL(WISP_ERR_CUDA, "grouped_ffn: cuTensorMapEncodeTiled failed (activations)");
   }
@@ -1288,7 +1272,7 @@ WispError wb::grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
   gu.counters = g_counters;
   dn = gu;
   dn.counters = g_counters ? g_counters + C_COUNT : nullptr;
-  for (int i = 0; i < 5; i++) {
+  for (int i = 0; i < 4; i++) {
     if (!encode_rows_map(&dn.tmap[i], d_h, rows_capacity, I, 16 << i))
       return WB_FAIL(WISP_ERR_CUDA, "grouped_ffn: cuTensorMapEncodeTiled failed (H)");
   }
@@ -1315,10 +1299,8 @@ WispError wb::grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
   pa.segs = d_segs;
   pa.nseg = n_segs;
   pa.sk_rows = sk_rows;
-  pa.mb_gu = I / BM;
+  pa.mb_gu = I / kGuRows;
   pa.mb_dn = M / BM;
-  pa.bn_gu = Shape<GATEUP>::kBNMax;
-  pa.bn_dn = Shape<DOWN>::kBNMax;
   pa.per_gu = wb::skinny_units_gateup(I);
   pa.per_dn = wb::skinny_units_down(M);
   pa.cols = wb::skinny_cols();
@@ -1374,7 +1356,7 @@ WispError wb::grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
   sk.counters = g_counters ? g_counters + 2 * C_COUNT : nullptr;
 
   const int grid = num_sms();
-  const size_t sm_gu = smem_bytes<GATEUP>(), sm_dn = smem_bytes<DOWN>();
+  const size_t sm_gu = smem_bytes(), sm_dn = smem_bytes();
   WB_CUDA_CHECK(cudaFuncSetAttribute(grouped_ffn_kernel<GATEUP>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_gu));
   WB_CUDA_CHECK(cudaFuncSetAttribute(grouped_ffn_kernel<DOWN>,
