@@ -1,7 +1,8 @@
 // common.cuh -- device helpers shared by the wisp_b200 kernels (sm_100a only).
 //
 // Inline-PTX wrappers for the Blackwell pieces the kernels use: mbarriers,
-// TMA tensor loads (no cluster multicast anywhere in this library), tcgen05
+// TMA tensor loads (no TMA or bulk load with cluster multicast anywhere in
+// this library; only tcgen05.commit signals both CTAs of a pair), tcgen05
 // tensor-memory allocation / load / store / MMA / commit, cp.async, plus the
 // int4 -> fp16 conversion used by every int4 kernel.
 #pragma once
@@ -134,6 +135,63 @@ WB_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
   }
 }
 
+// The same wait with cluster-scope acquire: for barriers that threads of the
+// other CTA of a cluster arrive on.
+WB_DEV bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(20000u) : "memory");
+  return ok != 0;
+}
+
+WB_DEV bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort,
+                              long long limit_cycles = 4000000000LL) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  long long t0 = clock64();
+  for (int it = 0;; ++it) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((it & 63) == 63) {
+      if (*abort) return false;
+      if (clock64() - t0 > limit_cycles) {
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Thread-block clusters.
+// ---------------------------------------------------------------------------
+WB_DEV uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the same shared-memory location in CTA `rank`.
+WB_DEV uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+// Arrive on an mbarrier of another CTA of this cluster (the default
+// semantics of the instruction; what the waiting side reads is tensor memory
+// and shared memory that the tcgen05 and TMA fences already order).
+WB_DEV void mbar_arrive_remote(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
+// All threads of every CTA of the cluster.
+WB_DEV void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+
 // ---------------------------------------------------------------------------
 // TMA (tensor map loads into shared memory, completion on an mbarrier).
 // ---------------------------------------------------------------------------
@@ -200,6 +258,19 @@ WB_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
                : "memory");
 }
+// The same for a CTA pair (cta_group::2): issued by the same warp of both
+// CTAs, which get the same columns.
+WB_DEV void tmem_alloc_pair(uint32_t* smem_result, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+               ::"r"(smem_u32(smem_result)), "r"(ncols) : "memory");
+}
+WB_DEV void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+WB_DEV void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
 WB_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 WB_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 WB_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
@@ -263,6 +334,35 @@ WB_DEV void mma_f16_ts_c(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
       ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "n"(ACC)
       : "memory");
+}
+
+// Pair MMA (cta_group::2, issued by the even CTA of the pair): D[tmem] (+)=
+// A[tmem] * B[smem]^T with M = 256, rows 0-127 in the even CTA's tensor
+// memory and 128-255 in the odd one's (A and D at the same addresses in
+// both); B's N rows are split in halves, the first in the even CTA's shared
+// memory at the descriptor's address, the second at the same address in the
+// odd CTA.
+template <int ACC>
+WB_DEV void mma_f16_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "n"(ACC)
+      : "memory");
+}
+
+// Arrive on the mbarrier at this shared-memory offset in both CTAs of the
+// pair once all pair MMAs issued by this thread have completed.
+WB_DEV void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)), "h"((uint16_t)3) : "memory");
+}
+
+// Instruction descriptor for a pair MMA: as below with M = 256.
+WB_DEV uint32_t idesc_f16_m256(int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
 }
 
 // Arrive on an mbarrier once all tcgen05.mma previously issued by this

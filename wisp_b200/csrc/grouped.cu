@@ -4,42 +4,49 @@
 // of dequant -> fp16 GEMV -> scale_accum (csrc/core/wisp_engine.c:1507-1531
 // called from run_moe :1563-1674 and, for prefill, decode_step per token
 // :2292-2307). Rows of activations are pre-grouped by expert ("segments");
-// each CTA tile computes 128 weight rows (the MMA's M, one TMEM lane each)
-// x BN token rows (its N):
+// the kernel runs as persistent pairs of CTAs (clusters of 2) whose tiles
+// compute 256 weight rows (the pair MMA's M; 128 per CTA, one TMEM lane
+// each) x BN token rows (its N):
 //
 //   GATEUP: H[p, i] = silu(gate[i] . x_p) * (up[i] . x_p)   (fp16 H out)
-//           over 64 intermediate rows: A rows 16j..16j+7 are gate rows
-//           8j..8j+7 of the tile, A rows 16j+8..16j+15 the matching up
-//           rows, so a gate lane's partner is lane ^ 8 of the same warp.
+//           over 128 intermediate rows, 64 per CTA: in a CTA, A rows
+//           16j..16j+7 are gate rows 8j..8j+7 of its block, A rows
+//           16j+8..16j+15 the matching up rows, so a gate lane's partner is
+//           lane ^ 8 of the same warp.
 //   DOWN:   out[token(p), m] += w_p * (down[m] . H_p)        (fp32 atomics)
 //           or y[p, m] = down[m] . H_p                        (mode 1)
 //
 // BN is chosen per segment: the fewest tiles of at most 192 rows, each a
-// multiple of 16 (an M=128 tcgen05.mma costs ~96 SM cycles at N=128 and
+// multiple of 32 (an M=128 tcgen05.mma costs ~96 SM cycles at N=128 and
 // ~141 at N=256 on B200, so wide tiles use the tensor pipe best; the cap
-// leaves room for two accumulators). Roles inside one persistent CTA per SM:
-//   warp 26     weight producer: per 128-K raw stage, one TMA box of packed
-//               nibbles per matrix (64 or 128 rows x 64 bytes, 64-byte
-//               swizzle) and bulk copies of the scales (and zero points) of
-//               the stage's groups from the prepared tile-transposed copy.
+// leaves room for two accumulators). The pair MMA (cta_group::2, issued by
+// the even CTA) reads each CTA's A from its own tensor memory and the token
+// rows half from each CTA's shared memory, so every SM loads half of a
+// tile's activations and one issuing thread drives two tensor cores. Roles
+// inside each CTA:
+//   warp 26     weight producer: per 128-K raw stage, one TMA box of this
+//               CTA's packed nibbles per matrix (64 or 128 rows x 64 bytes,
+//               64-byte swizzle) and bulk copies of the scales (and zero
+//               points) of the stage's groups from the prepared copy.
 //   warps 0-15  dequantise: warp w converts, for TMEM lane quadrant w % 4,
 //               32 K of every other A stage (64 K) -- one 16-byte read of its
 //               row from the raw stage, (n-8)*s + z in fp16 with one
 //               rounding, written straight into tensor memory with
-//               tcgen05.st, so shared-memory bandwidth goes to the
-//               activation operand alone. The store of one stage drains
-//               while the next converts.
-//   warp 24     TMA producer for the activation tiles (128-byte swizzle),
-//               one A stage of token rows per ring slot.
-//   warp 25     MMA issuer: tcgen05.mma kind::f16, A from TMEM, B from smem,
-//               fp32 accumulators in TMEM; completion via tcgen05.commit.
+//               tcgen05.st -- and reports the stage to the even CTA's
+//               barrier as soon as the store has completed.
+//   warp 24     TMA producer for this CTA's half of the activation rows
+//               (128-byte swizzle), one A stage per ring slot.
+//   warp 25     even CTA: MMA issuer (tcgen05.mma kind::f16, A from TMEM, B
+//               from smem, fp32 accumulators in TMEM; tcgen05.commit
+//               multicast to both CTAs' barriers). Odd CTA: forwards each
+//               landed activation stage to the even CTA's barrier.
 //   warps 16-23 epilogue, two warps per lane quadrant (alternate 16- or
 //               32-column chunks): tcgen05.ld of the accumulators, SwiGLU
 //               (GATEUP) or the weighted scatter-combine (DOWN).
-// TMEM columns: [0,192) and [192,384) two accumulator buffers (the epilogue
-// of one tile runs while the next accumulates), [384,512) four 32-column
-// A stages. Every wait is bounded; a wait that gives up raises a CTA-wide
-// abort and the device error word.
+// TMEM columns (the same in both CTAs): [0,192) and [192,384) two
+// accumulator buffers (the epilogue of one tile runs while the next
+// accumulates), [384,512) four 32-column A stages. Every wait is bounded; a
+// wait that gives up raises a CTA-wide abort and the device error word.
 //
 // The K order inside every group of 8 activations is 0,4,1,5,2,6,3,7: that
 // is the order the nibble conversion produces the weights in, so the
@@ -65,14 +72,17 @@ constexpr int kTmaWWarp = kTmaBWarp + 2;
 constexpr int kThreads = (kTmaWWarp + 1) * 32;
 constexpr int BM = 128;                      // A rows per tile (TMEM lanes)
 constexpr int kGuRows = 64;                  // intermediate rows per gate/up tile
-constexpr int kBNMax = 192;                  // token rows per tile
-constexpr int kAStages = 4;
-constexpr int kAStageCols = 32;              // 64 K of fp16 per lane
+#ifndef WB_TC_BN
+#define WB_TC_BN 192
+#endif
+constexpr int kBNMax = WB_TC_BN;             // token rows per tile
+constexpr int KA = 128;                      // K per stage (A stage = raw stage = B stage)
+constexpr int kAStageCols = KA / 2;          // 128 K of fp16 per lane
 constexpr int kAColBase = 2 * kBNMax;
 constexpr int kTmemCols = 512;
-static_assert(kAColBase + kAStages * kAStageCols == kTmemCols, "TMEM columns");
-constexpr int KA = 64;                       // K per A stage
-constexpr int kRawK = 128;                   // K per raw (weight) stage = 2 A stages
+constexpr int kAStages = (kTmemCols - kAColBase) / kAStageCols;
+static_assert(kAStages >= 2, "TMEM columns");
+constexpr int kRawK = KA;
 // raw stage: [nibbles: gate box, up box (4 KB each) | down box (8 KB)]
 //            [scales: 2 runs of up to 512 B][zero points: the same]
 constexpr int kRawStages = 6;
@@ -81,17 +91,21 @@ constexpr int kScOff = 8192;
 constexpr int kZOff = kScOff + 2 * kScRun;
 constexpr int kRawStageBytes = kZOff + 2 * kScRun;
 static_assert(kRawStageBytes % 1024 == 0, "raw stages keep 1024-byte alignment");
-constexpr int kBStages = 6;
-constexpr int kBStageBytes = kBNMax * 128;   // token rows of one A stage
+constexpr int kBStages = 5;
+// one CTA's token rows of a stage: two 64-K halves of kBNMax/2 rows x 128 B
+constexpr int kBStageBytes = kBNMax / 2 * 256;
+// Completion of stage j (one commit per stage) frees A slot j % kAStages and
+// B slot j % kBStages: one barrier ring whose length both divide.
+constexpr int kDoneRing = kAStages * kBStages;
 // Split K: a call with fewer tiles than half the SMs cuts each tile's K into
 // up to kMaxSplit ranges (work items) so more SMs take part; the down
 // projection's parts add into the output with its usual atomics, gate/up
 // parts go to a scratch buffer and the last part of a tile's lane quadrant
 // sums them in order and applies SwiGLU. At most kMaxSplitItems items.
 constexpr int kMaxSplit = 8;
-constexpr int kMaxSplitItems = 256;
-constexpr int kMaxFix = 16;   // quadrants one CTA may complete (<= 4 per item, <= 2 items)
-constexpr size_t kPartialFloats = (size_t)kBNMax * BM;   // one gate/up work item
+constexpr int kMaxSplitItems = 128;
+constexpr int kMaxFix = 16;   // quadrants one CTA may complete (<= 4 per item, <= 2 items per pair)
+constexpr size_t kPartialFloats = (size_t)kBNMax * BM;   // one CTA's part of a gate/up work item
 
 enum { GATEUP = 0, DOWN = 1 };
 
@@ -136,7 +150,7 @@ PreparedLayout prepared_layout(const WispMoeConfig* c, int n) {
 
 
 struct GemmParams {
-  CUtensorMap tmap[4];  // activation tensor, boxes {64, 16 << i}
+  CUtensorMap tmap[6];  // activation rows as {64 K, rows, K / 64}: boxes {64, 16 (i + 1), 2}
   const uint8_t* prepared;
   size_t p_flags, p_scales, p_zeros, p_mat_sc_bytes;
   const WispSegment* segs;
@@ -184,8 +198,9 @@ struct Prof {
 
 struct SmemLayout {
   uint64_t rfull[kRawStages], rempty[kRawStages];
-  uint64_t afull[kAStages], aempty[kAStages];
-  uint64_t bfull[kBStages], bempty[kBStages];
+  uint64_t afull[kAStages];
+  uint64_t bfull[kBStages];
+  uint64_t done[kDoneRing];
   uint64_t accfull[2], accempty[2], final_bar;
   uint32_t tmem_base;
   int abort;
@@ -239,18 +254,24 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
   SmemLayout* L = reinterpret_cast<SmemLayout*>(b_ring + kBStages * kBStageBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rank = (int)cluster_rank();      // 0: issues the pair's MMAs
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int ntiles = __ldg(p.tiles + p.nseg);
   const int split = __ldg(p.tiles + 2 * p.nseg + 1);
   const int nitems = ntiles * split;  // work item = (tile, K part), parts of a tile adjacent
-  // A CTA without work leaves before any set-up, tensor memory included.
-  if ((int)blockIdx.x >= nitems) return;
+  // A pair without work leaves before any set-up, tensor memory included
+  // (both CTAs of the pair take the same branch).
+  if (pair >= nitems) return;
   const int K = MODE == GATEUP ? p.M : p.I;
-  const int nR = K / kRawK;           // raw stages of the whole K
-  // Raw stages [r0, r1) of K part ks (each item has at least one).
+  const int nR = K / KA;              // stages of the whole K
+  // Stages [r0, r1) of K part ks (each item has at least one).
   auto part_range = [&](int ks, int& r0, int& r1) {
     r0 = ks * nR / split;
     r1 = (ks + 1) * nR / split;
   };
+  // This CTA's weight-row block of a pair tile: 64 intermediate rows
+  // (gate/up) or 128 output rows (down).
+  auto cta_block = [&](const TileInfo& ti) { return 2 * ti.mblk + rank; };
   volatile int* abort = &L->abort;
 
   if (threadIdx.x == 0) {
@@ -258,17 +279,13 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       mbar_init(&L->rfull[i], 1);
       mbar_init(&L->rempty[i], kDqWarps);       // every dequant warp reads every raw stage
     }
-    for (int i = 0; i < kAStages; i++) {
-      mbar_init(&L->afull[i], kDqWarps / 2);    // the 8 warps of the stage's parity
-      mbar_init(&L->aempty[i], 1);
-    }
-    for (int i = 0; i < kBStages; i++) {
-      mbar_init(&L->bfull[i], 1);
-      mbar_init(&L->bempty[i], 1);
-    }
+    for (int i = 0; i < kAStages; i++) mbar_init(&L->afull[i], 2 * kDqWarps);  // both CTAs' warps
+    // even CTA: its own copy's arrival + the odd CTA's relay; odd CTA: its copy
+    for (int i = 0; i < kBStages; i++) mbar_init(&L->bfull[i], rank == 0 ? 2 : 1);
+    for (int i = 0; i < kDoneRing; i++) mbar_init(&L->done[i], 1);
     for (int i = 0; i < 2; i++) {
       mbar_init(&L->accfull[i], 1);
-      mbar_init(&L->accempty[i], kEpiWarps);
+      mbar_init(&L->accempty[i], 2 * kEpiWarps);  // both CTAs' epilogue warps (even CTA's)
     }
     mbar_init(&L->final_bar, 1);
     L->abort = 0;
@@ -276,46 +293,47 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
     fence_barrier_init();
   }
   if (warp == kMmaWarp) {
-    tmem_alloc(&L->tmem_base, kTmemCols);
-    tmem_relinquish();
+    tmem_alloc_pair(&L->tmem_base, kTmemCols);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();
   tc_fence_after();
   const uint32_t tmem = L->tmem_base;
   const int32_t* flags = reinterpret_cast<const int32_t*>(p.prepared + p.p_flags);
 
   if (warp < kDqWarps) {
     // ------------------------------------------------------------------
-    // Dequantisation. A stage j of the CTA (2 per raw stage) belongs to the
-    // warps of parity j % 2; warp w converts K half (w >> 2) & 1 of it for
-    // TMEM lanes 32 (w % 4) .. +31, one A row per thread.
+    // Dequantisation: warp w converts K quarter w >> 2 (32 K) of every
+    // stage for TMEM lanes 32 (w % 4) .. +31, one A row per thread, and
+    // reports the stage to the even CTA's MMA issuer as soon as its store
+    // has completed.
     // ------------------------------------------------------------------
-    const int qd = warp & 3, hk = (warp >> 2) & 1, pg = warp >> 3;
+    const int qd = warp & 3, kq = warp >> 2;
     const int r = qd * 32 + lane;
     const int beta = MODE == GATEUP ? gu_matrix(r) : 0;
     const int rho = MODE == GATEUP ? gu_row(r) : r;
-    // 16-byte chunk (K 32c..32c+31 of the raw stage) of this thread's row,
-    // under the box's 64-byte swizzle: conflict-free, the 8 threads of a
-    // quarter-warp read 8 rows of one box.
-    const int chunk = 2 * pg + hk;
-    const uint32_t rd_off = (uint32_t)(beta * 4096 + rho * 64 + ((chunk ^ ((rho >> 1) & 3)) << 4));
-    const int gl = (pg * KA + hk * 32) / p.gs;   // scale group inside the raw stage
+    // 16-byte chunk kq of this thread's 64-byte row under the box's 64-byte
+    // swizzle: conflict-free, the 8 threads of a quarter-warp read 8 rows of
+    // one box.
+    const uint32_t rd_off = (uint32_t)(beta * 4096 + rho * 64 + ((kq ^ ((rho >> 1) & 3)) << 4));
+    const int gl = (kq * 32) / p.gs;             // scale group inside the stage
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
-    const uint32_t st_col = kAColBase + hk * 16;
-    int ir = 0;          // raw stages this CTA has consumed
-    int prev_sa = -1;
+    const uint32_t st_col = kAColBase + kq * 16;
+    const uint32_t afull_remote = rank ? cluster_addr(&L->afull[0], 0) : 0u;
+    int ir = 0;          // stages this CTA has consumed
     bool ok = true;
     Prof pf(p.counters);
-    for (int it = blockIdx.x; it < nitems && ok && !*abort; it += gridDim.x) {
+    for (int it = pair; it < nitems && ok && !*abort; it += npairs) {
       const int tile = it / split;
       int r0, r1;
       part_range(it - tile * split, r0, r1);
       const TileInfo ti = decode_tile(p, tile);
+      const int cb = cta_block(ti);
       const int mat = MODE == GATEUP ? beta : 2;
       const bool has_zero = __ldg(flags + ti.expert * 3 + mat) & 1;
       // row inside the stage's scale run (the 128-row tile of the prepared copy)
-      const int srow = MODE == GATEUP ? (ti.mblk & 1) * kGuRows + rho : rho;
+      const int srow = MODE == GATEUP ? (cb & 1) * kGuRows + rho : rho;
       const uint32_t s_off = (uint32_t)(kScOff + beta * kScRun + (gl * BM + srow) * 2);
       for (int rs = r0; rs < r1; rs++, ir++) {
         const int rslot = ir % kRawStages;
@@ -341,35 +359,28 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
           v[4 * w + 2] = o[2];
           v[4 * w + 3] = o[3];
         }
-        // Publish the previous stage now that its store had a stage of work
-        // to drain behind.
-        if (prev_sa >= 0) {
-          t0 = pf.now();
-          tmem_wait_st();
-          pf.add(2, t0);
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&L->afull[prev_sa]);
-          prev_sa = -1;
-        }
-        const int ia = 2 * ir + pg;
-        const int sa = ia % kAStages;
+        const int sa = ir % kAStages;
         t0 = pf.now();
-        if (ia >= kAStages && !mbar_wait(&L->aempty[sa], (uint32_t)(ia / kAStages - 1) & 1, abort)) {
-          ok = false;
-          break;
+        if (ir >= kAStages) {
+          const int j = ir - kAStages;   // the stage whose completion frees this slot
+          if (!mbar_wait(&L->done[j % kDoneRing], (uint32_t)(j / kDoneRing) & 1, abort)) {
+            ok = false;
+            break;
+          }
         }
         pf.add(1, t0);
         tc_fence_after();
         tmem_st16(tmem + lane_base + st_col + (uint32_t)(sa * kAStageCols), v);
-        prev_sa = sa;
+        t0 = pf.now();
+        tmem_wait_st();
+        pf.add(2, t0);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (rank == 0) mbar_arrive(&L->afull[sa]);
+          else mbar_arrive_remote(afull_remote + (uint32_t)(sa * sizeof(uint64_t)));
+        }
       }
-    }
-    if (prev_sa >= 0) {
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&L->afull[prev_sa]);
     }
     {
       const int slots[4] = {C_DQ_RFULL, C_DQ_AEMPTY, C_DQ_WAITST, -1};
@@ -377,29 +388,32 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
     }
   } else if (warp == kTmaWWarp) {
     // ------------------------------------------------------------------
-    // Weight producer: nibble boxes + scale / zero runs per raw stage.
+    // Weight producer: this CTA's nibble boxes + scale / zero runs per
+    // stage (a down block past the matrix's last row loads nothing).
     // ------------------------------------------------------------------
     if (lane == 0) {
-      const int ng = kRawK / p.gs;        // scale groups per raw stage (1 or 2)
+      const int ng = KA / p.gs;           // scale groups per stage (1 or 2)
       const int gpr = K / p.gs;           // groups per weight row
       const int nm = MODE == GATEUP ? 2 : 1;
       const uint32_t run = (uint32_t)(ng * BM * 2);
       int ir = 0;
       bool ok = true;
       Prof pf(p.counters);
-      for (int it = blockIdx.x; it < nitems && ok && !*abort; it += gridDim.x) {
+      for (int it = pair; it < nitems && ok && !*abort; it += npairs) {
         const int tile = it / split;
         int r0, r1;
         part_range(it - tile * split, r0, r1);
         const TileInfo ti = decode_tile(p, tile);
-        const int tile128 = MODE == GATEUP ? ti.mblk >> 1 : ti.mblk;
-        const int wrow = MODE == GATEUP ? ti.mblk * kGuRows : ti.mblk * BM;
+        const int cb = cta_block(ti);
+        const int tile128 = MODE == GATEUP ? cb >> 1 : cb;
+        const int wrow = MODE == GATEUP ? cb * kGuRows : cb * BM;
+        const bool in = MODE == GATEUP || wrow < p.M;
         uint32_t bytes = 0;
         bool hz[2] = {false, false};
         const CUtensorMap* map[2] = {nullptr, nullptr};
         const uint8_t* sc[2] = {nullptr, nullptr};
         const uint8_t* zr[2] = {nullptr, nullptr};
-        for (int j = 0; j < nm; j++) {
+        for (int j = 0; j < nm && in; j++) {
           const int e = ti.expert * 3 + (MODE == GATEUP ? j : 2);
           hz[j] = __ldg(flags + e) & 1;
           map[j] = reinterpret_cast<const CUtensorMap*>(p.prepared + (size_t)e * sizeof(CUtensorMap));
@@ -419,8 +433,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
           uint8_t* dst = raw_ring + rslot * kRawStageBytes;
           mbar_arrive_expect_tx(&L->rfull[rslot], bytes);
           const size_t goff = (size_t)rs * ng * BM * 2;
-          for (int j = 0; j < nm; j++) {
-            tma_load_2d(dst + j * 4096, map[j], &L->rfull[rslot], rs * (kRawK / 2), wrow);
+          for (int j = 0; j < nm && in; j++) {
+            tma_load_2d(dst + j * 4096, map[j], &L->rfull[rslot], rs * (KA / 2), wrow);
             bulk_load(dst + kScOff + j * kScRun, sc[j] + goff, run, &L->rfull[rslot]);
             if (hz[j]) bulk_load(dst + kZOff + j * kScRun, zr[j] + goff, run, &L->rfull[rslot]);
           }
@@ -436,113 +450,142 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
     }
   } else if (warp == kTmaBWarp) {
     // ------------------------------------------------------------------
-    // Activation producer: per A stage, the tile's token rows x 64 K as up
-    // to four boxes (128, 64, 32, 16 rows) stacked in one ring slot.
+    // Activation producer: per stage, this CTA's half of the tile's token
+    // rows (the even CTA the first bn/2, the odd one the rest) x 128 K, as
+    // one 3D box laid out [64-K half][row][128 B] in one ring slot.
     // ------------------------------------------------------------------
     if (lane == 0) {
-      for (int i = 0; i < 4; i++) tma_prefetch_desc(&p.tmap[i]);
+      for (int i = 0; i < 6; i++) tma_prefetch_desc(&p.tmap[i]);
       int ia = 0;
       bool ok = true;
       Prof pf(p.counters);
-      for (int it = blockIdx.x; it < nitems && ok && !*abort; it += gridDim.x) {
+      for (int it = pair; it < nitems && ok && !*abort; it += npairs) {
         const int tile = it / split;
         int r0, r1;
         part_range(it - tile * split, r0, r1);
         const TileInfo ti = decode_tile(p, tile);
-        for (int ka = 2 * r0; ka < 2 * r1; ka++, ia++) {
+        const int half = ti.bn >> 1;
+        const CUtensorMap* tm = &p.tmap[(half >> 4) - 1];
+        const int row0 = ti.row0 + rank * half;
+        for (int ka = r0; ka < r1; ka++, ia++) {
           const int sb = ia % kBStages;
           const long long t0 = pf.now();
-          if (ia >= kBStages &&
-              !mbar_wait(&L->bempty[sb], (uint32_t)(ia / kBStages - 1) & 1, abort)) {
-            ok = false;
-            break;
-          }
-          pf.add(0, t0);
-          mbar_arrive_expect_tx(&L->bfull[sb], (uint32_t)(ti.bn * 128));
-          uint8_t* dst = b_ring + sb * kBStageBytes;
-          int done = 0;
-#pragma unroll
-          for (int lg = 3; lg >= 0; lg--) {
-            if ((ti.bn >> 4) & (1 << lg)) {
-              tma_load_2d(dst + done * 128, &p.tmap[lg], &L->bfull[sb], ka * KA, ti.row0 + done);
-              done += 16 << lg;
+          if (ia >= kBStages) {
+            const int j = ia - kBStages;   // the stage whose completion frees this slot
+            if (!mbar_wait(&L->done[j % kDoneRing], (uint32_t)(j / kDoneRing) & 1, abort)) {
+              ok = false;
+              break;
             }
           }
+          pf.add(0, t0);
+          mbar_arrive_expect_tx(&L->bfull[sb], (uint32_t)(half * 256));
+          tma_load_3d(b_ring + sb * kBStageBytes, tm, &L->bfull[sb], 0, row0, 2 * ka);
         }
       }
       {
         const int slots[4] = {C_TB_BEMPTY, -1, -1, -1};
         pf.flush(slots, C_TB_TOTAL, true);
       }
+      // Let this CTA's last copies land before it can exit (the even CTA's
+      // barrier phases also need the odd CTA's relay).
       for (int j = max(0, ia - kBStages); j < ia; j++)
         mbar_wait(&L->bfull[j % kBStages], (uint32_t)(j / kBStages) & 1, abort, 200000000LL);
     }
   } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------------
-    // MMA issuer (one thread): per A stage four M=128 x N=bn x K=16 MMAs
-    // into the item's accumulator buffer (items alternate buffers).
-    // ------------------------------------------------------------------
-    if (lane == 0) {
-      const uint64_t bdesc0 = smem_desc_sw128(smem_u32(b_ring));
-      int ia = 0, nloc = 0;
+    if (rank == 0) {
+      // ----------------------------------------------------------------
+      // MMA issuer (one thread of the even CTA): per stage eight M=256 x
+      // N=bn x K=16 pair MMAs into the item's accumulator buffer (items
+      // alternate buffers) and one commit that frees the stage's A and B
+      // slots in both CTAs. Ring positions advance without divisions.
+      // ----------------------------------------------------------------
+      if (lane == 0) {
+        const uint32_t b0 = smem_u32(b_ring);
+        int sa = 0, sb = 0, sd = 0, nloc = 0;
+        uint32_t pa = 0, pb = 0;
+        bool ok = true;
+        Prof pf(p.counters);
+        for (int it = pair; it < nitems && ok && !*abort; it += npairs, nloc++) {
+          const int tile = it / split;
+          int r0, r1;
+          part_range(it - tile * split, r0, r1);
+          const TileInfo ti = decode_tile(p, tile);
+          const uint32_t idesc = idesc_f16_m256(ti.bn);
+          const uint32_t khalf = (uint32_t)((ti.bn >> 1) * 128) >> 4;   // second 64-K half
+          const int ab = nloc & 1;
+          const uint32_t d_tmem = tmem + (uint32_t)(ab * kBNMax);
+          long long t0 = pf.now();
+          if (nloc >= 2 && !mbar_wait(&L->accempty[ab], (uint32_t)((nloc >> 1) - 1) & 1, abort)) break;
+          pf.add(2, t0);
+          tc_fence_after();
+          for (int a = r0; a < r1; a++) {
+            t0 = pf.now();
+            if (!mbar_wait(&L->bfull[sb], pb, abort)) { ok = false; break; }
+            pf.add(1, t0);
+            t0 = pf.now();
+            if (!mbar_wait(&L->afull[sa], pa, abort)) { ok = false; break; }
+            pf.add(0, t0);
+            tc_fence_after();
+            const uint32_t a_col = tmem + (uint32_t)(kAColBase + sa * kAStageCols);
+            const uint64_t bd = smem_desc_sw128(b0 + (uint32_t)(sb * kBStageBytes));
+            if (a == r0) mma_f16_ts_pair<0>(d_tmem, a_col, bd, idesc);
+            else mma_f16_ts_pair<1>(d_tmem, a_col, bd, idesc);
+#pragma unroll
+            for (int kk = 1; kk < 8; kk++)
+              mma_f16_ts_pair<1>(d_tmem, a_col + kk * 8, bd + (kk >> 2) * khalf + 2 * (kk & 3), idesc);
+            mma_commit_pair(&L->done[sd]);
+            if (++sa == kAStages) { sa = 0; pa ^= 1; }
+            if (++sb == kBStages) { sb = 0; pb ^= 1; }
+            if (++sd == kDoneRing) sd = 0;
+          }
+          if (!ok) break;
+          mma_commit_pair(&L->accfull[ab]);
+        }
+        {
+          const int slots[4] = {C_MMA_AFULL, C_MMA_BFULL, C_MMA_ACCEMPTY, -1};
+          pf.flush(slots, C_MMA_TOTAL, true);
+          if (p.counters) atomicAdd(p.counters + C_TILES, (unsigned long long)nloc);
+        }
+        // Drain: make sure no MMA is still running before either CTA moves
+        // on to release its tensor memory.
+        mma_commit_pair(&L->final_bar);
+        mbar_wait(&L->final_bar, 0, abort, 200000000LL);
+      }
+    } else if (lane == 0) {
+      // ----------------------------------------------------------------
+      // Relay (odd CTA): forward each of this CTA's landed activation
+      // stages to the even CTA's barrier, in stage order.
+      // ----------------------------------------------------------------
+      const uint32_t bfull_remote = cluster_addr(&L->bfull[0], 0);
+      int sb = 0;
+      uint32_t pb = 0;
       bool ok = true;
-      Prof pf(p.counters);
-      for (int it = blockIdx.x; it < nitems && ok && !*abort; it += gridDim.x, nloc++) {
+      for (int it = pair; it < nitems && ok && !*abort; it += npairs) {
         const int tile = it / split;
         int r0, r1;
         part_range(it - tile * split, r0, r1);
-        const TileInfo ti = decode_tile(p, tile);
-        const uint32_t idesc = idesc_f16_m128(ti.bn);
-        const int ab = nloc & 1;
-        const uint32_t d_tmem = tmem + (uint32_t)(ab * kBNMax);
-        long long t0 = pf.now();
-        if (nloc >= 2 && !mbar_wait(&L->accempty[ab], (uint32_t)((nloc >> 1) - 1) & 1, abort)) break;
-        pf.add(2, t0);
-        tc_fence_after();
-        const int na = 2 * (r1 - r0);
-        for (int a = 0; a < na; a++, ia++) {
-          const int sa = ia % kAStages, sb = ia % kBStages;
-          t0 = pf.now();
-          if (!mbar_wait(&L->bfull[sb], (uint32_t)(ia / kBStages) & 1, abort)) { ok = false; break; }
-          pf.add(1, t0);
-          t0 = pf.now();
-          if (!mbar_wait(&L->afull[sa], (uint32_t)(ia / kAStages) & 1, abort)) { ok = false; break; }
-          pf.add(0, t0);
-          tc_fence_after();
-          const uint32_t a_col = tmem + (uint32_t)(kAColBase + sa * kAStageCols);
-          const uint64_t bd = bdesc0 + (uint64_t)((sb * kBStageBytes) >> 4);
-          if (a == 0) mma_f16_ts_c<0>(d_tmem, a_col, bd, idesc);
-          else mma_f16_ts_c<1>(d_tmem, a_col, bd, idesc);
-#pragma unroll
-          for (int kk = 1; kk < 4; kk++) mma_f16_ts_c<1>(d_tmem, a_col + kk * 8, bd + 2 * kk, idesc);
-          mma_commit(&L->aempty[sa]);
-          mma_commit(&L->bempty[sb]);
+        for (int ka = r0; ka < r1; ka++) {
+          if (!mbar_wait(&L->bfull[sb], pb, abort)) { ok = false; break; }
+          mbar_arrive_remote(bfull_remote + (uint32_t)(sb * sizeof(uint64_t)));
+          if (++sb == kBStages) { sb = 0; pb ^= 1; }
         }
-        if (!ok) break;
-        mma_commit(&L->accfull[ab]);
       }
-      {
-        const int slots[4] = {C_MMA_AFULL, C_MMA_BFULL, C_MMA_ACCEMPTY, -1};
-        pf.flush(slots, C_MMA_TOTAL, true);
-        if (p.counters) atomicAdd(p.counters + C_TILES, (unsigned long long)nloc);
-      }
-      // Drain: make sure no MMA is still running before TMEM is released.
-      mma_commit(&L->final_bar);
-      mbar_wait(&L->final_bar, 0, abort, 200000000LL);
     }
   } else {
     // ------------------------------------------------------------------
     // Epilogue warps 16-23: warp w reads accumulator lanes 32 (w % 4) ..
-    // +31; the two warps of a quadrant take alternate column chunks.
+    // +31 of this CTA's rows; the two warps of a quadrant take alternate
+    // column chunks. Both CTAs report a drained buffer to the even CTA.
     // ------------------------------------------------------------------
     const int qd = warp & 3, ch = (warp - kEpiWarp0) >> 2;
     const int r = qd * 32 + lane;
     const uint32_t lane_addr = tmem + ((uint32_t)(qd * 32) << 16);
     int nloc = 0;
     Prof pf(p.counters);
-    for (int it = blockIdx.x; it < nitems && !*abort; it += gridDim.x, nloc++) {
+    for (int it = pair; it < nitems && !*abort; it += npairs, nloc++) {
       const int tile = it / split;
       const TileInfo ti = decode_tile(p, tile);
+      const int cb = cta_block(ti);
       const int ab = nloc & 1;
       const long long t0 = pf.now();
       if (!mbar_wait(&L->accfull[ab], (uint32_t)(nloc >> 1) & 1, abort)) break;
@@ -553,7 +596,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       if (MODE == GATEUP) {
         const int beta = gu_matrix(r);
         if (split == 1) {
-          const int islot = k_interleave_slot(ti.mblk * kGuRows + gu_row(r));
+          const int islot = k_interleave_slot(cb * kGuRows + gu_row(r));
           for (int c0 = 16 * ch; c0 < ti.bn; c0 += 32) {
             uint32_t a[16];
             tmem_ld16(acc + c0, a);
@@ -572,11 +615,11 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
             }
           }
         } else {
-          // This K part's sums go to the scratch item, laid out [column][A
-          // row]; the CTA whose arrival completes the tile's quadrant (both
-          // of its warps, every part) sums all parts in order after its
-          // last item.
-          float* pit = p.partial + (size_t)it * kPartialFloats + r;
+          // This K part's sums go to the scratch item of this CTA, laid out
+          // [column][A row]; the CTA whose arrival completes the quadrant
+          // (both of its warps, every part) sums all parts in order after
+          // its last item.
+          float* pit = p.partial + (size_t)(2 * it + rank) * kPartialFloats + r;
           for (int c0 = 16 * ch; c0 < ti.bn; c0 += 32) {
             uint32_t a[16];
             tmem_ld16(acc + c0, a);
@@ -587,23 +630,27 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
           tc_fence_before();
           __threadfence();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&L->accempty[ab]);
+          if (lane == 0) {
+            if (rank == 0) mbar_arrive(&L->accempty[ab]);
+            else mbar_arrive_remote(cluster_addr(&L->accempty[ab], 0));
+          }
           released = true;
           int old = 0;
           if (lane == 0) {
             __threadfence();
-            old = atomicAdd(p.tickets + tile * 4 + qd, 1);
+            old = atomicAdd(p.tickets + (2 * tile + rank) * 4 + qd, 1);
             __threadfence();
           }
           old = __shfl_sync(0xffffffffu, old, 0);
           if (old == 2 * split - 1 && lane == 0) {
             const int slot = atomicAdd(&L->fix_n, 1);
             if (slot < kMaxFix) L->fix[slot] = tile * 4 + qd;
-            else atomicExch(&L->abort, 1);  // cannot happen: items per CTA are bounded
+            else atomicExch(&L->abort, 1);  // cannot happen: items per pair are bounded
           }
         }
       } else {
-        const int m = ti.mblk * BM + r;
+        const int m = cb * BM + r;
+        const bool row_in = m < p.M;
         for (int c0 = 32 * ch; c0 < ti.bn; c0 += 64) {
           // tokens and router weights of these 32 columns: one per lane,
           // broadcast below (no dependent loads inside the store loop)
@@ -624,7 +671,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
             const int tt = c0 + j;
             const int tok = __shfl_sync(0xffffffffu, tok_l, j);
             const float wgt = __shfl_sync(0xffffffffu, w_l, j);
-            if (tt < ti.nvalid) {
+            if (tt < ti.nvalid && row_in) {
               const float yv = __uint_as_float(j < 16 ? ya[j] : yb[j - 16]);
               if (p.mode == 0)
                 red_add_f32(p.out + (size_t)tok * p.M + m, wgt * yv);
@@ -637,7 +684,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       if (!released) {
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&L->accempty[ab]);
+        if (lane == 0) {
+          if (rank == 0) mbar_arrive(&L->accempty[ab]);
+          else mbar_arrive_remote(cluster_addr(&L->accempty[ab], 0));
+        }
       }
     }
     const int slots[4] = {C_EPI_ACCFULL, -1, -1, -1};
@@ -645,28 +695,32 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
   }
 
   tc_fence_before();
-  __syncthreads();
+  // Neither CTA leaves (or frees tensor memory) while the pair's MMAs or
+  // the other CTA's arrivals may still touch it.
+  cluster_sync();
   // Split gate/up: every thread of the CTA sums the parts of the quadrants
   // it completes (K parts in order), applies SwiGLU and writes H; the partial
   // sums were published before the arrival counts (fence, then the count;
-  // the completing warp fenced after reading it, then the CTA barrier).
+  // the completing warp fenced after reading it, then the cluster barrier).
   if (MODE == GATEUP && split > 1 && !L->abort) {
     const int nfix = min(L->fix_n, kMaxFix);
     for (int f = 0; f < nfix; f++) {
       const int tile = L->fix[f] >> 2, qd = L->fix[f] & 3;
       const TileInfo ti = decode_tile(p, tile);
-      const float* base = p.partial + (size_t)tile * split * kPartialFloats;
-      // 16 (gate, up) row pairs per quadrant
+      const int cb = cta_block(ti);
+      // 16 (gate, up) row pairs per quadrant; part ks of this CTA's rows is
+      // scratch item 2 (tile * split + ks) + rank
       for (int i = threadIdx.x; i < 16 * ti.nvalid; i += blockDim.x) {
         const int pr = i & 15, c = i >> 4;
         const int rg = qd * 32 + ((pr >> 3) << 4) + (pr & 7);   // gate lane; up lane rg + 8
-        const float* pc = base + (size_t)c * BM + rg;
-        float g = __ldcg(pc), u = __ldcg(pc + 8);
-        for (int ks = 1; ks < split; ks++) {
-          g += __ldcg(pc + ks * kPartialFloats);
-          u += __ldcg(pc + ks * kPartialFloats + 8);
+        float g = 0.f, u = 0.f;
+        for (int ks = 0; ks < split; ks++) {
+          const float* pc = p.partial + (size_t)(2 * (tile * split + ks) + rank) * kPartialFloats +
+                            (size_t)c * BM + rg;
+          g += __ldcg(pc);
+          u += __ldcg(pc + 8);
         }
-        const int row = ti.mblk * kGuRows + gu_row(rg);
+        const int row = cb * kGuRows + gu_row(rg);
         p.h_out[(size_t)(ti.row0 + c) * p.I + k_interleave_slot(row)] = __float2half(silu(g) * u);
       }
     }
@@ -674,7 +728,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
   if (threadIdx.x == 0 && L->abort && p.error_flag) atomicExch(p.error_flag, 1);
   if (warp == kMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    tmem_dealloc_pair(tmem, kTmemCols);
   }
 }
 
@@ -699,7 +753,7 @@ __device__ void plan_tiles(const WispSegment* __restrict__ segs, int nseg, int m
     if (s < nseg) {
       const int rows = segs[s].rows;
       const int nt = (max(rows, 1) + kBNMax - 1) / kBNMax;
-      bn = ((max(rows, 1) + nt - 1) / nt + 15) & ~15;
+      bn = ((max(rows, 1) + nt - 1) / nt + 31) & ~31;   // pair MMAs: N % 32 == 0
       n = rows > skip_rows ? ((rows + bn - 1) / bn) * mblocks : 0;
       tiles[nseg + 1 + s] = bn;
     }
@@ -737,7 +791,7 @@ __device__ void plan_tiles(const WispSegment* __restrict__ segs, int nseg, int m
     tiles[2 * nseg + 1] = max(split, 1);
   }
   if (tickets)
-    for (int i = threadIdx.x; i < 4 * kMaxSplitItems; i += blockDim.x) tickets[i] = 0;
+    for (int i = threadIdx.x; i < 8 * kMaxSplitItems; i += blockDim.x) tickets[i] = 0;
 }
 
 // Units of the register-path kernel: `per_seg` row blocks per chunk of `cols`
@@ -973,16 +1027,18 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// fp16 activation rows [rows x cols]: boxes of 64 columns x box_rows rows,
-// 128-byte swizzle (the canonical K-major layout of the MMA's B operand).
-bool encode_rows_map(CUtensorMap* m, const void* base, int rows, int cols, int box_rows) {
+// fp16 activation rows [rows x cols] as a 3D tensor {64 K, rows, K / 64} for
+// the tensor-core kernel: one box = box_rows rows x 128 K, stored as two [box_rows][128 B]
+// halves (one per 64 K) with the 128-byte swizzle -- the MMA's B operand of
+// one stage in a single copy.
+bool encode_rows_map3(CUtensorMap* m, const void* base, int rows, int cols, int box_rows) {
   EncodeTiledFn fn = get_encode_fn();
   if (!fn) return false;
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+  cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)cols / 64};
+  cuuint64_t strides[2] = {(cuuint64_t)cols * 2, 128};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box,
             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
          CUDA_SUCCESS;
@@ -1039,6 +1095,58 @@ bool encode_packed_map_sk(CUtensorMap* m, const void* base, int rows, int cols) 
 size_t smem_bytes() {
   return 1024 + (size_t)kRawStages * kRawStageBytes + (size_t)kBStages * kBStageBytes +
          sizeof(SmemLayout);
+}
+
+int num_sms();
+
+// The tensor-core kernels run as persistent CTA pairs (clusters of 2), as
+// many pairs as can be resident at once on this device (a GPC with an odd
+// number of free SMs leaves one idle).
+template <int MODE>
+cudaLaunchConfig_t pair_config(int npairs, cudaStream_t st, cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * npairs);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem_bytes();
+  cfg.stream = st;
+  attr->id = cudaLaunchAttributeClusterDimension;
+  attr->val.clusterDim.x = 2;
+  attr->val.clusterDim.y = 1;
+  attr->val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+int grouped_pairs() {
+  static int pairs[64] = {0};
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!pairs[dev]) {
+    int n = 0;
+    cudaFuncSetAttribute(grouped_ffn_kernel<GATEUP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem_bytes());
+    cudaFuncSetAttribute(grouped_ffn_kernel<DOWN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem_bytes());
+    cudaLaunchAttribute attr;
+    cudaLaunchConfig_t cfg = pair_config<GATEUP>(num_sms() / 2, nullptr, &attr);
+    if (cudaOccupancyMaxActiveClusters(&n, grouped_ffn_kernel<GATEUP>, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = num_sms() / 2;
+    }
+    pairs[dev] = std::min(n, num_sms() / 2);
+  }
+  return pairs[dev];
+}
+
+template <int MODE>
+cudaError_t launch_pairs(int npairs, cudaStream_t st, const GemmParams& p) {
+  cudaLaunchAttribute attr;
+  cudaLaunchConfig_t cfg = pair_config<MODE>(npairs, st, &attr);
+  return cudaLaunchKernelEx(&cfg, grouped_ffn_kernel<MODE>, p);
 }
 
 int num_sms() {
@@ -1170,13 +1278,13 @@ GroupedWs carve_grouped(int n_segs, int rows, int M, int I, void* base) {
   };
   const size_t tw = (size_t)(2 * n_segs + 2);
   int32_t* words = reinterpret_cast<int32_t*>(
-      take(4 * (2 * tw + (size_t)2 * (n_segs + 2) + 4 * (size_t)kMaxSplitItems)));
+      take(4 * (2 * tw + (size_t)2 * (n_segs + 2) + 8 * (size_t)kMaxSplitItems)));
   w.tiles_gu = words;
   w.tiles_dn = words ? words + tw : nullptr;
   w.units_gu = words ? words + 2 * tw : nullptr;
   w.units_dn = words ? w.units_gu + (n_segs + 2) : nullptr;
   w.tickets = words ? w.units_dn + (n_segs + 2) : nullptr;
-  w.partial = reinterpret_cast<float*>(take((size_t)kMaxSplitItems * kPartialFloats * 4));
+  w.partial = reinterpret_cast<float*>(take((size_t)2 * kMaxSplitItems * kPartialFloats * 4));
   w.xq = take((size_t)rows * q16_row_bytes(M));
   w.hq = take((size_t)rows * q16_row_bytes(I));
   w.bytes = (off + 255) & ~(size_t)255;
@@ -1253,8 +1361,8 @@ WispError wb::grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
   const PreparedLayout PL = prepared_layout(cfg, n_entries);
   GemmParams gu, dn;
   memset(&gu, 0, sizeof gu);
-  for (int i = 0; i < 4; i++) {
-    if (!encode_rows_map(&gu.tmap[i], d_xp, rows_capacity, M, 16 << i))
+  for (int i = 0; i < 6; i++) {
+    if (!encode_rows_map3(&gu.tmap[i], d_xp, rows_capacity, M, 16 * (i + 1)))
       return WB_FAIL(WISP_ERR_CUDA, "grouped_ffn: cuTensorMapEncodeTiled failed (activations)");
   }
   gu.prepared = static_cast<const uint8_t*>(d_prepared);
@@ -1272,8 +1380,8 @@ WispError wb::grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
   gu.counters = g_counters;
   dn = gu;
   dn.counters = g_counters ? g_counters + C_COUNT : nullptr;
-  for (int i = 0; i < 4; i++) {
-    if (!encode_rows_map(&dn.tmap[i], d_h, rows_capacity, I, 16 << i))
+  for (int i = 0; i < 6; i++) {
+    if (!encode_rows_map3(&dn.tmap[i], d_h, rows_capacity, I, 16 * (i + 1)))
       return WB_FAIL(WISP_ERR_CUDA, "grouped_ffn: cuTensorMapEncodeTiled failed (H)");
   }
   dn.row_token = d_row_token;
@@ -1299,15 +1407,16 @@ WispError wb::grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
   pa.segs = d_segs;
   pa.nseg = n_segs;
   pa.sk_rows = sk_rows;
-  pa.mb_gu = I / kGuRows;
-  pa.mb_dn = M / BM;
+  pa.mb_gu = I / (2 * kGuRows);           // pair tiles: 128 intermediate rows
+  pa.mb_dn = (M + 2 * BM - 1) / (2 * BM);  // pair tiles: 256 output rows
   pa.per_gu = wb::skinny_units_gateup(I);
   pa.per_dn = wb::skinny_units_down(M);
   pa.cols = wb::skinny_cols();
   pa.ks_dn = mode == 0 ? 8 : 1;
   pa.nk_dn = wb::skinny_stages(I);
   pa.target = 2 * num_sms();
-  pa.sms = num_sms();
+  const int npairs = grouped_pairs();
+  pa.sms = npairs;   // the tensor-core kernels' K split fills the CTA pairs
   pa.split_gu = kMaxSplit;
   pa.split_dn = mode == 0 ? kMaxSplit : 1;
   pa.nraw_gu = M / kRawK;
@@ -1356,19 +1465,14 @@ WispError wb::grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
   sk.counters = g_counters ? g_counters + 2 * C_COUNT : nullptr;
 
   const int grid = num_sms();
-  const size_t sm_gu = smem_bytes(), sm_dn = smem_bytes();
-  WB_CUDA_CHECK(cudaFuncSetAttribute(grouped_ffn_kernel<GATEUP>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_gu));
-  WB_CUDA_CHECK(cudaFuncSetAttribute(grouped_ffn_kernel<DOWN>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_dn));
   // When no segment can exceed the routing threshold (max_seg_rows, an upper
   // bound the caller knows, e.g. the token count of a decode batch), the
   // tensor-core kernels would find no tiles: they are not launched.
   const bool tc = max_seg_rows > sk_rows;
   if (sk_rows > 0) WB_CUDA_CHECK(wb::launch_skinny(sk, 0, grid, stream));
-  if (tc) wb::launch_k(grouped_ffn_kernel<GATEUP>, grid, kThreads, sm_gu, stream, gu);
+  if (tc) WB_CUDA_CHECK(launch_pairs<GATEUP>(npairs, stream, gu));
   if (sk_rows > 0) WB_CUDA_CHECK(wb::launch_skinny(sk, 1, grid, stream));
-  if (tc) wb::launch_k(grouped_ffn_kernel<DOWN>, grid, kThreads, sm_dn, stream, dn);
+  if (tc) WB_CUDA_CHECK(launch_pairs<DOWN>(npairs, stream, dn));
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
