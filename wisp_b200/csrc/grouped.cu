@@ -94,9 +94,12 @@ static_assert(kRawStageBytes % 1024 == 0, "raw stages keep 1024-byte alignment")
 constexpr int kBStages = 5;
 // one CTA's token rows of a stage: two 64-K halves of kBNMax/2 rows x 128 B
 constexpr int kBStageBytes = kBNMax / 2 * 256;
-// Completion of stage j (one commit per stage) frees A slot j % kAStages and
-// B slot j % kBStages: one barrier ring whose length both divide.
-constexpr int kDoneRing = kAStages * kBStages;
+// Stage j is ready when full[j % kRing] completes (in the even CTA: both
+// CTAs' dequant warps and both halves of the token rows; in the odd CTA: its
+// own token rows, which a relay forwards) and consumed when done[j % kRing]
+// completes (one commit per stage), which frees A slot j % kAStages and B
+// slot j % kBStages: one ring whose length both divide.
+constexpr int kRing = kAStages * kBStages;
 // Split K: a call with fewer tiles than half the SMs cuts each tile's K into
 // up to kMaxSplit ranges (work items) so more SMs take part; the down
 // projection's parts add into the output with its usual atomics, gate/up
@@ -198,9 +201,8 @@ struct Prof {
 
 struct SmemLayout {
   uint64_t rfull[kRawStages], rempty[kRawStages];
-  uint64_t afull[kAStages];
-  uint64_t bfull[kBStages];
-  uint64_t done[kDoneRing];
+  uint64_t full[kRing];
+  uint64_t done[kRing];
   uint64_t accfull[2], accempty[2], final_bar;
   uint32_t tmem_base;
   int abort;
@@ -279,10 +281,12 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       mbar_init(&L->rfull[i], 1);
       mbar_init(&L->rempty[i], kDqWarps);       // every dequant warp reads every raw stage
     }
-    for (int i = 0; i < kAStages; i++) mbar_init(&L->afull[i], 2 * kDqWarps);  // both CTAs' warps
-    // even CTA: its own copy's arrival + the odd CTA's relay; odd CTA: its copy
-    for (int i = 0; i < kBStages; i++) mbar_init(&L->bfull[i], rank == 0 ? 2 : 1);
-    for (int i = 0; i < kDoneRing; i++) mbar_init(&L->done[i], 1);
+    // even CTA: both CTAs' dequant warps + its token copy + the odd CTA's
+    // relay; odd CTA: its token copy
+    for (int i = 0; i < kRing; i++) {
+      mbar_init(&L->full[i], rank == 0 ? 2 * kDqWarps + 2 : 1);
+      mbar_init(&L->done[i], 1);
+    }
     for (int i = 0; i < 2; i++) {
       mbar_init(&L->accfull[i], 1);
       mbar_init(&L->accempty[i], 2 * kEpiWarps);  // both CTAs' epilogue warps (even CTA's)
@@ -320,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
     const int gl = (kq * 32) / p.gs;             // scale group inside the stage
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
     const uint32_t st_col = kAColBase + kq * 16;
-    const uint32_t afull_remote = rank ? cluster_addr(&L->afull[0], 0) : 0u;
+    const uint32_t full_remote = rank ? cluster_addr(&L->full[0], 0) : 0u;
     int ir = 0;          // stages this CTA has consumed
     bool ok = true;
     Prof pf(p.counters);
@@ -363,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
         t0 = pf.now();
         if (ir >= kAStages) {
           const int j = ir - kAStages;   // the stage whose completion frees this slot
-          if (!mbar_wait(&L->done[j % kDoneRing], (uint32_t)(j / kDoneRing) & 1, abort)) {
+          if (!mbar_wait(&L->done[j % kRing], (uint32_t)(j / kRing) & 1, abort)) {
             ok = false;
             break;
           }
@@ -377,8 +381,9 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          if (rank == 0) mbar_arrive(&L->afull[sa]);
-          else mbar_arrive_remote(afull_remote + (uint32_t)(sa * sizeof(uint64_t)));
+          const int f = ir % kRing;
+          if (rank == 0) mbar_arrive(&L->full[f]);
+          else mbar_arrive_remote(full_remote + (uint32_t)(f * sizeof(uint64_t)));
         }
       }
     }
@@ -472,14 +477,15 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
           const long long t0 = pf.now();
           if (ia >= kBStages) {
             const int j = ia - kBStages;   // the stage whose completion frees this slot
-            if (!mbar_wait(&L->done[j % kDoneRing], (uint32_t)(j / kDoneRing) & 1, abort)) {
+            if (!mbar_wait(&L->done[j % kRing], (uint32_t)(j / kRing) & 1, abort)) {
               ok = false;
               break;
             }
           }
           pf.add(0, t0);
-          mbar_arrive_expect_tx(&L->bfull[sb], (uint32_t)(half * 256));
-          tma_load_3d(b_ring + sb * kBStageBytes, tm, &L->bfull[sb], 0, row0, 2 * ka);
+          uint64_t* fb = &L->full[ia % kRing];
+          mbar_arrive_expect_tx(fb, (uint32_t)(half * 256));
+          tma_load_3d(b_ring + sb * kBStageBytes, tm, fb, 0, row0, 2 * ka);
         }
       }
       {
@@ -487,9 +493,9 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
         pf.flush(slots, C_TB_TOTAL, true);
       }
       // Let this CTA's last copies land before it can exit (the even CTA's
-      // barrier phases also need the odd CTA's relay).
+      // phases also need the dequant warps and the odd CTA's relay).
       for (int j = max(0, ia - kBStages); j < ia; j++)
-        mbar_wait(&L->bfull[j % kBStages], (uint32_t)(j / kBStages) & 1, abort, 200000000LL);
+        mbar_wait(&L->full[j % kRing], (uint32_t)(j / kRing) & 1, abort, 200000000LL);
     }
   } else if (warp == kMmaWarp) {
     if (rank == 0) {
@@ -501,8 +507,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       // ----------------------------------------------------------------
       if (lane == 0) {
         const uint32_t b0 = smem_u32(b_ring);
-        int sa = 0, sb = 0, sd = 0, nloc = 0;
-        uint32_t pa = 0, pb = 0;
+        const uint32_t a0 = tmem + (uint32_t)kAColBase;
+        // ring positions of the next stage, advanced without divisions
+        int sa = 0, sb = 0, sf = 0, nloc = 0;
+        uint32_t pf_phase = 0;
         bool ok = true;
         Prof pf(p.counters);
         for (int it = pair; it < nitems && ok && !*abort; it += npairs, nloc++) {
@@ -520,23 +528,20 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
           tc_fence_after();
           for (int a = r0; a < r1; a++) {
             t0 = pf.now();
-            if (!mbar_wait(&L->bfull[sb], pb, abort)) { ok = false; break; }
-            pf.add(1, t0);
-            t0 = pf.now();
-            if (!mbar_wait(&L->afull[sa], pa, abort)) { ok = false; break; }
+            if (!mbar_wait(&L->full[sf], pf_phase, abort)) { ok = false; break; }
             pf.add(0, t0);
             tc_fence_after();
-            const uint32_t a_col = tmem + (uint32_t)(kAColBase + sa * kAStageCols);
+            const uint32_t a_col = a0 + (uint32_t)(sa * kAStageCols);
             const uint64_t bd = smem_desc_sw128(b0 + (uint32_t)(sb * kBStageBytes));
             if (a == r0) mma_f16_ts_pair<0>(d_tmem, a_col, bd, idesc);
             else mma_f16_ts_pair<1>(d_tmem, a_col, bd, idesc);
 #pragma unroll
             for (int kk = 1; kk < 8; kk++)
               mma_f16_ts_pair<1>(d_tmem, a_col + kk * 8, bd + (kk >> 2) * khalf + 2 * (kk & 3), idesc);
-            mma_commit_pair(&L->done[sd]);
-            if (++sa == kAStages) { sa = 0; pa ^= 1; }
-            if (++sb == kBStages) { sb = 0; pb ^= 1; }
-            if (++sd == kDoneRing) sd = 0;
+            mma_commit_pair(&L->done[sf]);
+            sa = sa + 1 == kAStages ? 0 : sa + 1;
+            sb = sb + 1 == kBStages ? 0 : sb + 1;
+            if (++sf == kRing) { sf = 0; pf_phase ^= 1; }
           }
           if (!ok) break;
           mma_commit_pair(&L->accfull[ab]);
@@ -556,18 +561,18 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_ffn_kernel(const __grid_c
       // Relay (odd CTA): forward each of this CTA's landed activation
       // stages to the even CTA's barrier, in stage order.
       // ----------------------------------------------------------------
-      const uint32_t bfull_remote = cluster_addr(&L->bfull[0], 0);
-      int sb = 0;
-      uint32_t pb = 0;
+      const uint32_t full_remote = cluster_addr(&L->full[0], 0);
+      int sf = 0;
+      uint32_t pf_phase = 0;
       bool ok = true;
       for (int it = pair; it < nitems && ok && !*abort; it += npairs) {
         const int tile = it / split;
         int r0, r1;
         part_range(it - tile * split, r0, r1);
         for (int ka = r0; ka < r1; ka++) {
-          if (!mbar_wait(&L->bfull[sb], pb, abort)) { ok = false; break; }
-          mbar_arrive_remote(bfull_remote + (uint32_t)(sb * sizeof(uint64_t)));
-          if (++sb == kBStages) { sb = 0; pb ^= 1; }
+          if (!mbar_wait(&L->full[sf], pf_phase, abort)) { ok = false; break; }
+          mbar_arrive_remote(full_remote + (uint32_t)(sf * sizeof(uint64_t)));
+          if (++sf == kRing) { sf = 0; pf_phase ^= 1; }
         }
       }
     }
