@@ -23,7 +23,7 @@ DEV = "cuda"
 
 @pytest.fixture(params=["mixed", "tcgen05"])
 def path(request):
-    """mixed: segments of <= 16 rows on the register-fed kernel, larger ones
+    """mixed: segments of <= 32 rows on the register-fed kernel, larger ones
     on tcgen05 (the library default); tcgen05: every segment on tcgen05."""
     abi.lib().wisp_b200_set_skinny_max_rows(0 if request.param == "tcgen05" else -1)
     yield request.param
@@ -136,6 +136,56 @@ def test_router_topk_launcher(orc, E, M, k):
                            bias.float().numpy().astype(np.float64), x.numpy()[None, :].astype(np.float64))
     i_ref, w_ref, mg = orc.topk(lg, k)
     check_routing(idx.numpy()[None, :], w.numpy()[None, :], i_ref, w_ref, mg)
+
+
+@pytest.mark.parametrize("T,E,k,shared,skew", [(1, 8, 2, False, False), (300, 8, 2, True, False),
+                                               (4096, 256, 8, True, True), (2048, 1024, 8, True, True),
+                                               (5000, 64, 8, False, True), (64, 1100, 4, True, False)])
+def test_dispatch_plan_layout(T, E, k, shared, skew):
+    """wisp_b200_dispatch_plan: each expert's rows are its (token, slot)
+    pairs in order, the shared expert holds every token with weight 1 --
+    exactly, for the one-block count and the chunked fill (up to 1024 routed
+    experts, chunks larger than one block's above 32k slots) and for the
+    per-expert kernels beyond that. Expert-parallel dispatch relies on this
+    order. Indices out of range (a malformed caller table) match no expert."""
+    rng = np.random.default_rng(T * 7 + E)
+    p = rng.gamma(0.3, size=E) if skew else np.ones(E)
+    p = p / p.sum()
+    idx = np.stack([rng.choice(E, size=k, replace=False, p=p) for _ in range(T)]).astype(np.int32)
+    if T > 1:
+        idx[0, 0] = E + 3          # out of range
+    w = rng.random((T, k)).astype(np.float32)
+    cfg = abi.WispMoeConfig(tokens=T, hidden=128, inter=128, n_experts=E, top_k=k, group_size=128,
+                            has_shared=int(shared))
+    V = E + int(shared)
+    d_idx = torch.from_numpy(idx).to(DEV)
+    d_w = torch.from_numpy(w).to(DEV)
+    counts = torch.full((V,), -1, dtype=torch.int32, device=DEV)
+    segs = torch.zeros((V, 4), dtype=torch.int32, device=DEV)
+    rows = T * k + (T if shared else 0)
+    row_token = torch.full((rows,), -1, dtype=torch.int32, device=DEV)
+    row_weight = torch.zeros((rows,), dtype=torch.float32, device=DEV)
+    abi.call("wisp_b200_dispatch_plan", C.byref(cfg), d_idx.data_ptr(), d_w.data_ptr(),
+             counts.data_ptr(), segs.data_ptr(), row_token.data_ptr(), row_weight.data_ptr(),
+             _stream())
+    torch.cuda.synchronize()
+    flat_i, flat_w = idx.reshape(-1), w.reshape(-1)
+    want_tok, want_w, want_segs = [], [], []
+    for e in range(E):
+        sel = np.nonzero(flat_i == e)[0]
+        want_segs.append((e, len(want_tok), len(sel)))
+        want_tok += list(sel // k)
+        want_w += list(flat_w[sel])
+    if shared:
+        want_segs.append((E, len(want_tok), T))
+        want_tok += list(range(T))
+        want_w += [1.0] * T
+    n = len(want_tok)
+    got_segs = segs.cpu().numpy()[:, :3]
+    np.testing.assert_array_equal(got_segs, np.array(want_segs, dtype=np.int32))
+    np.testing.assert_array_equal(counts.cpu().numpy(), np.array([sg[2] for sg in want_segs]))
+    np.testing.assert_array_equal(row_token.cpu().numpy()[:n], np.array(want_tok, dtype=np.int32))
+    np.testing.assert_array_equal(row_weight.cpu().numpy()[:n], np.array(want_w, dtype=np.float32))
 
 
 @pytest.mark.parametrize("T", [1, 2, 4, 5, 70])

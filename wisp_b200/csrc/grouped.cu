@@ -1304,6 +1304,14 @@ extern "C" size_t wisp_b200_grouped_workspace_bytes(const WispMoeConfig* cfg, in
 }
 
 namespace wb {
+// The routing threshold of a grouped-FFN call: segments of at most this many
+// rows run on the register path. The register-path kernel keeps the
+// zero-point flags in shared memory; larger launches run on the tensor-core
+// kernel alone.
+int grouped_sk_rows(int n_segs, int n_entries) {
+  if (n_segs > skinny_max_segs() || n_entries > skinny_max_entries()) return 0;
+  return g_skinny_rows >= 0 ? g_skinny_rows : skinny_max_rows();
+}
 // Where the q16 rows of the gate/up input live inside a grouped-FFN
 // workspace (a caller that packs them itself passes xq_ready to
 // grouped_ffn_impl).
@@ -1394,10 +1402,7 @@ WispError wb::grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
   dn.out = d_out;
   dn.mode = mode;
 
-  int sk_rows = g_skinny_rows >= 0 ? g_skinny_rows : wb::skinny_max_rows();
-  // The register-path kernel keeps the zero-point flags in shared memory;
-  // larger launches run on the tensor-core kernel alone.
-  if (n_segs > wb::skinny_max_segs() || n_entries > wb::skinny_max_entries()) sk_rows = 0;
+  const int sk_rows = wb::grouped_sk_rows(n_segs, n_entries);
   gu.tiles = ws.tiles_gu;
   dn.tiles = ws.tiles_dn;
   gu.tickets = ws.tickets;

@@ -24,7 +24,9 @@ WispError launch_plan(const WispMoeConfig* c, const int* idx, const float* w, in
 WispError launch_pack(const uint16_t* x, const int* src, int n_rows, int M, uint16_t* xp,
                       cudaStream_t st, WispErrCtx* err);
 WispError launch_pack_q16(const uint16_t* x, const int* src, int n_rows, int M, uint16_t* xp,
-                          uint8_t* xq, cudaStream_t st, WispErrCtx* err);
+                          uint8_t* xq, const WispSegment* segs, int nseg, int sk_rows,
+                          cudaStream_t st, WispErrCtx* err);
+int grouped_sk_rows(int n_segs, int n_entries);
 uint8_t* grouped_xq(void* d_workspace, int n_segs, int rows_capacity, int M, int I);
 WispError grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
                            const WispInt4Expert* d_experts, int n_entries,
@@ -155,11 +157,12 @@ extern "C" WispError wisp_b200_moe_forward(const WispMoeConfig* cfg, const WispM
   if (e != WISP_OK) return e;
   e = wb::launch_plan(cfg, idx, wt, ws.counts, ws.segs, ws.row_token, ws.row_weight, stream, err);
   if (e != WISP_OK) return e;
-  // Both operand forms of the gathered rows in one pass: fp16 for the
-  // tensor-core kernel, q16 (into the grouped workspace) for the register path.
+  // The gathered rows in the operand form of the kernel their segment runs
+  // on: fp16 for the tensor-core kernel, q16 (into the grouped workspace) for
+  // the register path.
   e = wb::launch_pack_q16(d_x, ws.row_token, ws.rows, cfg->hidden, ws.xp,
-                          wb::grouped_xq(ws.grouped, V, ws.rows, cfg->hidden, cfg->inter), stream,
-                          err);
+                          wb::grouped_xq(ws.grouped, V, ws.rows, cfg->hidden, cfg->inter), ws.segs,
+                          V, wb::grouped_sk_rows(V, V), stream, err);
   if (e != WISP_OK) return e;
   WB_CUDA_CHECK(cudaMemsetAsync(d_out, 0, (size_t)cfg->tokens * cfg->hidden * sizeof(float), stream));
   WB_CUDA_CHECK(cudaMemsetAsync(ws.error_flag, 0, sizeof(int), stream));

@@ -32,6 +32,8 @@
 //                         interleaved K order the tensor-core kernel expects.
 #include <cuda_bf16.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "internal.h"
 #include "skinny.h"
@@ -580,6 +582,149 @@ __global__ void __launch_bounds__(kPlanWarps * 32) fill_kernel(
   }
 }
 
+// The plan for up to kPlanMaxV experts (routed + shared) in two launches.
+// count_segments_kernel (one block): per-expert counters in shared memory,
+// filled with one atomic per (warp, expert) (__match_any_sync groups the
+// lanes that hold the same expert), then the exclusive scan into segments.
+// fill_ordered_kernel (one block per chunk of slots): the rows of expert v
+// are its slots in (token, slot) order, so a slot's row is v's first row +
+// the matches of v before the chunk (counted by the block) + the matches
+// before it inside the chunk (per-warp counts, then ranks within each
+// 32-slot group).
+constexpr int kPlanMaxV = 1025;
+constexpr int kFillWarps = 8;
+
+__device__ __forceinline__ void count_groups(int e, int lane, int* cnt) {
+  const unsigned m = __match_any_sync(0xffffffffu, e);
+  if (e >= 0 && (m & ((1u << lane) - 1u)) == 0) atomicAdd(&cnt[e], __popc(m));
+}
+
+__global__ void __launch_bounds__(1024) count_segments_kernel(const int* __restrict__ idx,
+                                                              int nslots, int E, int T, int V,
+                                                              int* __restrict__ counts,
+                                                              WispSegment* __restrict__ segs) {
+  __shared__ int cnt[kPlanMaxV];
+  __shared__ int warp_tot[32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  for (int v = threadIdx.x; v < V; v += blockDim.x) cnt[v] = 0;
+  __syncthreads();
+  for (int base = 0; base < nslots; base += blockDim.x) {
+    const int s = base + threadIdx.x;
+    int e = s < nslots ? __ldg(idx + s) : -1;
+    if (e >= E) e = -1;   // out-of-range indices match no expert
+    count_groups(e, lane, cnt);
+  }
+  __syncthreads();
+  if (V > E && threadIdx.x == 0) cnt[E] = T;   // the shared expert holds every token
+  __syncthreads();
+  __shared__ int carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (int base = 0; base < V; base += blockDim.x) {
+    const int v = base + threadIdx.x;
+    const int n = v < V ? cnt[v] : 0;
+    int x = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_tot[w] = x;
+    __syncthreads();
+    if (w == 0) {
+      int tv = lane < (int)(blockDim.x >> 5) ? warp_tot[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, tv, o);
+        if (lane >= o) tv += y;
+      }
+      warp_tot[lane] = tv;
+    }
+    __syncthreads();
+    const int incl = x + (w > 0 ? warp_tot[w - 1] : 0) + carry;
+    if (v < V) {
+      WispSegment sg;
+      sg.expert = v;
+      sg.row_begin = incl - n;
+      sg.rows = n;
+      sg.reserved = 0;
+      segs[v] = sg;
+      counts[v] = n;
+    }
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = incl;
+    __syncthreads();
+  }
+}
+
+__global__ void __launch_bounds__(kFillWarps * 32) fill_ordered_kernel(
+    const int* __restrict__ idx, const float* __restrict__ w, int nslots, int chunk, int k, int E,
+    int T, int V, const WispSegment* __restrict__ segs, int* __restrict__ row_token,
+    float* __restrict__ row_weight) {
+  __shared__ int before[kPlanMaxV];
+  __shared__ int wcnt[kFillWarps][kPlanMaxV];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c0 = blockIdx.x * chunk;
+  const int per_warp = chunk / kFillWarps;            // a multiple of 32
+  const int wb = c0 + warp * per_warp;
+  // the shared expert's rows: every token once, in token order
+  if (V > E) {
+    const int begin = segs[E].row_begin;
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < T; t += gridDim.x * blockDim.x) {
+      row_token[begin + t] = t;
+      row_weight[begin + t] = 1.f;
+    }
+  }
+  for (int v = threadIdx.x; v < E; v += blockDim.x) {
+    before[v] = 0;
+#pragma unroll
+    for (int q = 0; q < kFillWarps; q++) wcnt[q][v] = 0;
+  }
+  __syncthreads();
+  // matches before the chunk (c0 is a multiple of the block size)
+  for (int s = threadIdx.x; s < c0; s += blockDim.x) {
+    int e = __ldg(idx + s);
+    if (e >= E) e = -1;
+    count_groups(e, lane, before);
+  }
+  // this warp's matches in its range
+  for (int g = 0; g < per_warp; g += 32) {
+    const int s = wb + g + lane;
+    int e = s < nslots ? __ldg(idx + s) : -1;
+    if (e >= E) e = -1;
+    const unsigned m = __match_any_sync(0xffffffffu, e);
+    if (e >= 0 && (m & ((1u << lane) - 1u)) == 0) wcnt[warp][e] += __popc(m);
+    __syncwarp();
+  }
+  __syncthreads();
+  // first row of each (warp, expert) run
+  for (int v = threadIdx.x; v < E; v += blockDim.x) {
+    int run = segs[v].row_begin + before[v];
+#pragma unroll
+    for (int q = 0; q < kFillWarps; q++) {
+      const int t = wcnt[q][v];
+      wcnt[q][v] = run;
+      run += t;
+    }
+  }
+  __syncthreads();
+  for (int g = 0; g < per_warp; g += 32) {
+    const int s = wb + g + lane;
+    int e = s < nslots ? __ldg(idx + s) : -1;
+    if (e >= E) e = -1;
+    const unsigned m = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(m & ((1u << lane) - 1u));
+    const int base = e >= 0 ? wcnt[warp][e] : 0;
+    __syncwarp();
+    if (e >= 0) {
+      row_token[base + rank] = s / k;
+      row_weight[base + rank] = w[s];
+      if (rank == 0) wcnt[warp][e] = base + __popc(m);
+    }
+    __syncwarp();
+  }
+}
+
 // xp[p] = fp16(x[src[p]]) in interleaved K order; each thread moves 8 values.
 __global__ void pack_rows_kernel(const uint16_t* __restrict__ x, const int* __restrict__ src, int n_rows,
                                  int M, uint16_t* __restrict__ xp) {
@@ -606,19 +751,33 @@ __global__ void pack_rows_kernel(const uint16_t* __restrict__ x, const int* __re
   }
 }
 
-// The same rows gathered into both operand forms at once: xp[p] as above
-// and xq[p] as a q16 row (layout in skinny.h) for the register-path kernel.
-// One block of 128 threads per row; a thread owns one packed-weight word (8
-// consecutive K) per 1024-K pass, so each half-warp holds one 128-K block:
-// its max |x| (four shuffles) sets the block's scale, and every thread
-// writes its word's 16 bytes. Half-warps past the row's end take part in the
-// shuffles with zeros and store nothing.
+// The same rows gathered into the operand form of the kernel that computes
+// them: xp[p] as above for rows of segments larger than sk_rows (tensor-core
+// kernel), xq[p] as a q16 row (layout in skinny.h) for the others (register
+// path). The row's segment is found by binary search over the segments'
+// first rows. One block of 128 threads per row; a thread owns one
+// packed-weight word (8 consecutive K) per 1024-K pass, so each half-warp
+// holds one 128-K block: its max |x| (four shuffles) sets the block's scale,
+// and every thread writes its word's 16 bytes. Half-warps past the row's
+// end take part in the shuffles with zeros and store nothing.
 __global__ void __launch_bounds__(128) pack_rows_q16_kernel(const uint16_t* __restrict__ x,
                                                             const int* __restrict__ src, int n_rows,
                                                             int M, uint16_t* __restrict__ xp,
-                                                            uint8_t* __restrict__ xq) {
+                                                            uint8_t* __restrict__ xq,
+                                                            const WispSegment* __restrict__ segs,
+                                                            int nseg, int sk_rows) {
   const int p = blockIdx.x;
   if (p >= n_rows) return;
+  // last segment whose first row is <= p (empty segments share a first row
+  // with the next one and are skipped)
+  int lo = 0, hi = nseg - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(&segs[mid].row_begin) <= p) lo = mid; else hi = mid - 1;
+  }
+  const WispSegment sg = segs[lo];
+  if (p >= sg.row_begin + sg.rows) return;   // a padding row of no segment
+  const bool want_q16 = sg.rows <= sk_rows;
   const int s = src ? src[p] : p;
   const uint16_t* xr = x + (size_t)s * M;
   uint16_t* orow = xp + (size_t)p * M;
@@ -640,11 +799,13 @@ __global__ void __launch_bounds__(128) pack_rows_q16_kernel(const uint16_t* __re
       const __half2 h1 = __floats2half2_rn(f[1], f[5]);
       const __half2 h2 = __floats2half2_rn(f[2], f[6]);
       const __half2 h3 = __floats2half2_rn(f[3], f[7]);
-      *reinterpret_cast<uint4*>(orow + 8 * w) = make_uint4(h22u(h0), h22u(h1), h22u(h2), h22u(h3));
+      if (!want_q16)
+        *reinterpret_cast<uint4*>(orow + 8 * w) = make_uint4(h22u(h0), h22u(h1), h22u(h2), h22u(h3));
     } else {
 #pragma unroll
       for (int j = 0; j < 8; j++) f[j] = 0.f;
     }
+    if (!want_q16) continue;   // block-uniform
     float m = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; j++) m = fmaxf(m, fabsf(f[j]));
@@ -777,18 +938,30 @@ WispError launch_plan(const WispMoeConfig* c, const int* idx, const float* w, in
                       WispErrCtx* err) {
   const int T = c->tokens, E = c->n_experts, k = c->top_k, sh = c->has_shared ? 1 : 0;
   const int V = E + sh;
-  wb::launch_k(count_kernel, V, kPlanWarps * 32, 0, st, idx, T * k, E, T, counts);
-  wb::launch_k(segments_kernel, 1, 1024, 0, st, counts, V, segs);
-  wb::launch_k(fill_kernel, V, kPlanWarps * 32, 0, st, idx, w, T * k, k, E, T, segs, row_token,
-               row_weight);
+  const int nslots = T * k;
+  if (V <= kPlanMaxV) {
+    // chunks of 1024 slots, larger for large batches so that at most 32
+    // blocks count the slots before their chunk
+    const int chunk = 1024 * std::max(1, (nslots + 32 * 1024 - 1) / (32 * 1024));
+    wb::launch_k(count_segments_kernel, 1, 1024, 0, st, idx, nslots, E, T, V, counts, segs);
+    wb::launch_k(fill_ordered_kernel, (nslots + chunk - 1) / chunk, kFillWarps * 32, 0, st, idx, w,
+                 nslots, chunk, k, E, T, V, segs, row_token, row_weight);
+  } else {
+    wb::launch_k(count_kernel, V, kPlanWarps * 32, 0, st, idx, nslots, E, T, counts);
+    wb::launch_k(segments_kernel, 1, 1024, 0, st, counts, V, segs);
+    wb::launch_k(fill_kernel, V, kPlanWarps * 32, 0, st, idx, w, nslots, k, E, T, segs, row_token,
+                 row_weight);
+  }
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
 
 WispError launch_pack_q16(const uint16_t* x, const int* src, int n_rows, int M, uint16_t* xp,
-                          uint8_t* xq, cudaStream_t st, WispErrCtx* err) {
+                          uint8_t* xq, const WispSegment* segs, int nseg, int sk_rows,
+                          cudaStream_t st, WispErrCtx* err) {
   if (n_rows <= 0) return WISP_OK;
-  wb::launch_k(pack_rows_q16_kernel, n_rows, 128, 0, st, x, src, n_rows, M, xp, xq);
+  wb::launch_k(pack_rows_q16_kernel, n_rows, 128, 0, st, x, src, n_rows, M, xp, xq, segs, nseg,
+               sk_rows);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
