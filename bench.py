@@ -553,13 +553,13 @@ def main() -> None:
            "h2d_bytes_per_step": x_host.numel() * 2 * world,
            "d2h_bytes_per_step": out_host.numel() * 4 * world}
 
-    # Our kernels per layer: route 2 (logits, top-k) + plan 3 (count,
-    # segments, fill) + grouped FFN 5 (one tile/unit planner, register-path
-    # and tensor-core kernels for gate/up and down); single GPU: + pack 1;
-    # expert-parallel: + dispatch 2 (slots and entries, rows), receive-plan,
-    # gather, combine, and for the shared expert pack 1 + grouped 5. Plus one
-    # rms_rescale between layers.
-    per_layer = 11 if world == 1 else 15 + (6 if spec.has_shared else 0)
+    # Our kernels per layer: route 2 (logits, top-k) + plan 2 (count and
+    # segments, ordered fill) + grouped FFN 5 (one tile/unit planner,
+    # register-path and tensor-core kernels for gate/up and down); single GPU:
+    # + pack 1; expert-parallel: + dispatch 2 (slots and entries, rows),
+    # receive-plan, gather, combine, and for the shared expert pack 1 +
+    # grouped 5. Plus one rms_rescale between layers.
+    per_layer = 10 if world == 1 else 14 + (6 if spec.has_shared else 0)
     launches_per_step = per_layer * L + (L - 1)
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
