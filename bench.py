@@ -289,6 +289,61 @@ def measure_side_config(name: str, steps: int, warmup: int, peaks: dict) -> dict
 # GPU arm
 # ---------------------------------------------------------------------------
 
+PHASES = ("dispatch", "shared", "exchange", "gather", "ffn", "return", "combine")
+
+
+def ep_phase_report(layers, xs, outs, step_eager, spec, T, L, world, dev, reps: int = 5) -> dict:
+    """Per-phase device time of one step on every rank (eager launches with
+    CUDA events between the phases of each layer; the timed step itself
+    replays as a CUDA graph), and the per-rank load: received (token,
+    expert) rows and touched local experts per layer."""
+    import torch
+    import torch.distributed as dist
+    from wisp_b200 import abi
+    acc = {k: 0.0 for k in PHASES}
+    marks = []
+
+    def mark(name):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        marks.append((name, ev))
+
+    for _ in range(reps):
+        for l in range(L):
+            marks.clear()
+            mark("start")
+            layers[l].forward(xs[l], outs[l], mark=mark)
+            torch.cuda.synchronize()
+            for (_, a), (name, b) in zip(marks[:-1], marks[1:]):
+                acc[name] += a.elapsed_time(b)
+            if l + 1 < L:
+                abi.call("wisp_b200_rms_rescale", outs[l].data_ptr(), xs[l + 1].data_ptr(), T,
+                         spec.hidden, 1e-6, torch.cuda.current_stream().cuda_stream)
+    mine = torch.tensor([acc[k] / reps for k in PHASES], dtype=torch.float64, device=dev)
+    every = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(every, mine)
+    rows, touched = [], []
+    for lay in layers:
+        r = lay.total.to(torch.int64).reshape(1)
+        seg = lay.rsegs.view(torch.int32).reshape(-1, 4)
+        u = (seg[:, 2] > 0).to(torch.int64).sum().reshape(1)
+        rr = [torch.empty_like(r) for _ in range(world)]
+        uu = [torch.empty_like(u) for _ in range(world)]
+        dist.all_gather(rr, r)
+        dist.all_gather(uu, u)
+        rows.append([int(v.item()) for v in rr])
+        touched.append([int(v.item()) for v in uu])
+    per_rank = torch.stack(every).cpu().numpy()
+    return {
+        "how": f"eager step with CUDA events between phases, mean of {reps}, summed over the "
+               f"{L} layers; the timed step replays as a graph",
+        "ms_per_step_max_over_ranks": {k: round(float(per_rank[:, i].max()), 4) for i, k in enumerate(PHASES)},
+        "ms_per_step_rank0": {k: round(float(per_rank[0, i]), 4) for i, k in enumerate(PHASES)},
+        "received_rows_per_layer": rows,
+        "touched_local_experts_per_layer": touched,
+    }
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -426,6 +481,11 @@ def main() -> None:
     # error words of the bounded waits (every kernel of the step)
     for lay in layers:
         lay.check()
+
+    # -- expert parallelism: per-phase device times and per-rank load -------
+    ep_phases = None
+    if world > 1:
+        ep_phases = ep_phase_report(layers, xs, outs, step_eager, spec, T, L, world, dev)
 
     # -- algorithmic bytes of one step (routing is identical every step) --
     used = []
@@ -577,6 +637,7 @@ def main() -> None:
                 "frac_of_8tbs": round(hbm_gbs / 8000.0, 4), "experts_touched_per_layer": used},
         "roofline": roofline, "e2e": e2e, "clocks": clk,
         "gpu_launches": launches_per_step * args.steps,
+        **({"ep_phases": ep_phases} if ep_phases else {}),
     }
     if world == 1 and not args.no_side_configs and args.config == "ep_stack":
         # the stack (~35 GB) stays resident; each configuration adds a few GB

@@ -271,15 +271,18 @@ class EpLayer:
             self.ops.grouped_dev(self.cfg_loc, self.lw, self.sh_seg, 1, T, self.xs, self.hr, 0,
                                  self.sh_token, self.sh_weight, out, self.gws, self.flag)
 
-    def expert_phase(self) -> None:
+    def expert_phase(self, mark=None) -> None:
         """Local experts over the received rows, gathered so that each expert
         is one segment; the FFN adds w * y of every local expert of a received
-        token into that token's fp32 return row."""
+        token into that token's fp32 return row. ``mark(name)``, if given, is
+        called after the receive plan and gather."""
         ops, k, M = self.ops, self.spec.top_k, self.spec.hidden
         ops.recv_plan(self.recv, self.world, self.e_loc, self.cap, k, M, self.rsegs, self.src_pos,
                       self.gw, self.total)
         ops.gather_rows(self.recv, self.world, self.e_loc, self.cap, k, M, self.src_pos, self.total,
                         self.rk, self.xsorted)
+        if mark:
+            mark("gather")
         self.yr.zero_()
         ops.grouped_dev(self.cfg_loc, self.lw, self.rsegs, self.n_rsegs, self.rk, self.xsorted,
                         self.hr, 0, self.src_pos, self.gw, self.yr, self.gws, self.flag)
@@ -288,19 +291,33 @@ class EpLayer:
         """Each token adds its returned rows from the owners, in rank order."""
         self.ops.ep_combine(self.yback, self.slot, self.T, self.world, self.cap, out)
 
-    def forward(self, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
-        """x: bf16 [T, M] (this rank's tokens) -> out fp32 [T, M]."""
+    def forward(self, x: torch.Tensor, out: torch.Tensor, mark=None) -> torch.Tensor:
+        """x: bf16 [T, M] (this rank's tokens) -> out fp32 [T, M].
+
+        ``mark(name)``, if given, is called on the host after each phase has
+        been issued (for per-phase CUDA events on the current stream): after
+        route + plan + dispatch ("dispatch"), the shared expert ("shared"),
+        the wait for the first exchange ("exchange"), the receive plan and
+        gather ("gather"), the local experts' FFN ("ffn"), the return exchange
+        ("return") and the combine ("combine")."""
+        m = mark or (lambda name: None)
         self.dispatch_phase(x, out)
+        m("dispatch")
         # 1. the blocks to the owners; the shared expert runs on this rank's
         #    own tokens while they travel
         w_rows = dist.all_to_all_single(self.recv, self.send, group=self.group, async_op=True)
         self.shared_phase(x, out)
+        m("shared")
         w_rows.wait()
+        m("exchange")
         # 2. local experts over the received rows
-        self.expert_phase()
+        self.expert_phase(mark)
+        m("ffn")
         # 3. the rows back to their tokens' ranks, added in rank order
         dist.all_to_all_single(self.yback, self.yr, group=self.group)
+        m("return")
         self.combine_phase(out)
+        m("combine")
         return out
 
     def check(self) -> None:
