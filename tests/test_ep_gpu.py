@@ -7,7 +7,9 @@ grouped FFN (register-path and tensor-core kernels) on the received rows.
 The concatenated output must match the fp64 oracle within the parity
 tolerance, and the single-GPU MoeLayer output for the same tokens within
 max_rel 1e-3 / mean_rel 1e-4: each local expert is one segment of the same
-rows as on one GPU and runs on the same kernel, but the tensor-core kernel
+rows as on one GPU and runs on the same kernel (the routing threshold is set
+to 16 rows in both runs, so that the shared expert's 32 rows per rank and 64
+rows on one GPU both take the tensor-core kernel), but the tensor-core kernel
 cuts K into a number of parts that follows its tile count (the shared
 expert has half the rows per rank), so fp32 sums run in another order and
 an H element may round to the neighbouring fp16 value. A misrouted or
@@ -26,8 +28,11 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from wisp_b200 import synth
+from wisp_b200 import abi, synth
 from wisp_b200.ep import EpLayer, block_range
+
+# Segments of at most this many rows take the register path in both runs.
+SK_ROWS = 16
 
 pytestmark = pytest.mark.gpu
 
@@ -54,6 +59,7 @@ def _worker(rank, world, port, outdir, spec):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
+    abi.lib().wisp_b200_set_skinny_max_rows(SK_ROWS)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
                             device_id=dev)
     try:
@@ -88,7 +94,11 @@ def test_ep_two_gpus_matches_single_gpu_and_oracle(orc, spec):
             assert not os.path.exists(err), open(err).read()
         got = np.concatenate([np.load(os.path.join(td, f"out{r}.npy")) for r in range(2)])
     layers, x = synth.make_model(spec, "cuda:0")
-    single = MoeLayer(layers[0], spec.tokens).forward(x).cpu().numpy()
+    abi.lib().wisp_b200_set_skinny_max_rows(SK_ROWS)
+    try:
+        single = MoeLayer(layers[0], spec.tokens).forward(x).cpu().numpy()
+    finally:
+        abi.lib().wisp_b200_set_skinny_max_rows(-1)
     idx, w, margin = oracle_route(orc, layers[0], x)
     # Tokens whose routing is a near-tie may pick different experts when the
     # router's fp32 sums run in another order (the split-K depth follows the
