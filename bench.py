@@ -293,32 +293,60 @@ PHASES = ("dispatch", "shared", "exchange", "gather", "ffn", "return", "combine"
 
 
 def ep_phase_report(layers, xs, outs, step_eager, spec, T, L, world, dev, reps: int = 5) -> dict:
-    """Per-phase device time of one step on every rank (eager launches with
-    CUDA events between the phases of each layer; the timed step itself
-    replays as a CUDA graph), and the per-rank load: received (token,
-    expert) rows and touched local experts per layer."""
+    """Per-phase device time of one step on every rank, and the per-rank load
+    (received (token, expert) rows and touched local experts per layer).
+
+    The step is captured as a CUDA graph with timing events recorded as graph
+    nodes (external events) at the phase boundaries of every layer, then
+    replayed `reps` times; phases are summed over the layers (the rms_rescale
+    between layers is not counted). Falls back to eager launches if the
+    capture fails."""
     import torch
     import torch.distributed as dist
     from wisp_b200 import abi
-    acc = {k: 0.0 for k in PHASES}
     marks = []
 
     def mark(name):
-        ev = torch.cuda.Event(enable_timing=True)
+        ev = torch.cuda.Event(enable_timing=True, external=True)
         ev.record()
         marks.append((name, ev))
 
-    for _ in range(reps):
+    def one_step():
         for l in range(L):
-            marks.clear()
             mark("start")
             layers[l].forward(xs[l], outs[l], mark=mark)
-            torch.cuda.synchronize()
-            for (_, a), (name, b) in zip(marks[:-1], marks[1:]):
-                acc[name] += a.elapsed_time(b)
             if l + 1 < L:
                 abi.call("wisp_b200_rms_rescale", outs[l].data_ptr(), xs[l + 1].data_ptr(), T,
                          spec.hidden, 1e-6, torch.cuda.current_stream().cuda_stream)
+
+    graph, how = None, "CUDA graph"
+    try:
+        torch.cuda.synchronize()
+        dist.barrier()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            one_step()
+        torch.cuda.synchronize()
+    except Exception as exc:  # noqa: BLE001 - reported in the line
+        graph, how = None, f"eager (capture failed: {type(exc).__name__})"
+    ok = torch.tensor([1 if graph is not None else 0], device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if int(ok.item()) == 0 and graph is not None:
+        graph.reset()
+        graph, how = None, "eager (another rank failed to capture)"
+    acc = {k: 0.0 for k in PHASES}
+    for _ in range(reps):
+        if graph is not None:
+            graph.replay()
+        else:
+            marks.clear()
+            one_step()
+        torch.cuda.synchronize()
+        for (_, a), (name, b) in zip(marks[:-1], marks[1:]):
+            if name != "start":
+                acc[name] += a.elapsed_time(b)
+    if graph is not None:
+        graph.reset()   # it holds NCCL calls: released before the group
     mine = torch.tensor([acc[k] / reps for k in PHASES], dtype=torch.float64, device=dev)
     every = [torch.empty_like(mine) for _ in range(world)]
     dist.all_gather(every, mine)
@@ -335,8 +363,8 @@ def ep_phase_report(layers, xs, outs, step_eager, spec, T, L, world, dev, reps: 
         touched.append([int(v.item()) for v in uu])
     per_rank = torch.stack(every).cpu().numpy()
     return {
-        "how": f"eager step with CUDA events between phases, mean of {reps}, summed over the "
-               f"{L} layers; the timed step replays as a graph",
+        "how": f"{how} of one step with timing events between the phases of every layer, "
+               f"mean of {reps} replays, summed over the {L} layers",
         "ms_per_step_max_over_ranks": {k: round(float(per_rank[:, i].max()), 4) for i, k in enumerate(PHASES)},
         "ms_per_step_rank0": {k: round(float(per_rank[0, i]), 4) for i, k in enumerate(PHASES)},
         "received_rows_per_layer": rows,
