@@ -229,6 +229,32 @@ WispError wisp_b200_prepare_experts(const WispMoeConfig* cfg, const WispInt4Expe
                                     int n_entries, void* d_prepared, size_t prepared_bytes,
                                     cudaStream_t stream, WispErrCtx* err);
 
+/* Re-prepares entry `slot` (0 <= slot < n_entries) of a prepared set in
+ * place from a HOST copy of its expert-table entry and leaves every other
+ * entry as it is: the hook for an expert blob that has just been promoted
+ * into a VRAM slot (csrc/core/wisp_engine.c:1164-1203 copies the blob into
+ * VRAM; this call then builds that slot's TMA descriptors and transposed
+ * scales). The bytes it writes equal those wisp_b200_prepare_experts writes
+ * for the same entry. The packed nibbles are used where they lie, in the
+ * blob's own layout. Asynchronous on `stream`, with no host staging (the
+ * descriptors travel as kernel parameters); updating the device expert
+ * table entry itself is the caller's part. */
+WispError wisp_b200_prepare_expert_slot(const WispMoeConfig* cfg, int n_entries, int slot,
+                                        const WispInt4Expert* entry, void* d_prepared,
+                                        size_t prepared_bytes, cudaStream_t stream,
+                                        WispErrCtx* err);
+
+/* The expert-table entry of a reference expert blob that lies at device
+ * address d_blob: pointers to its gate, up and down packed nibbles, scales
+ * and (when the blob carries them) zero points, at the offsets of the
+ * parsed header (csrc/core/wisp_engine.c:268-303). Host-only pointer
+ * arithmetic: d_blob is never dereferenced. WISP_ERR_INVALID_ARG when meta
+ * is invalid or a matrix's packed data or scales would not be 16-byte
+ * aligned (a blob placed at an address = 8 mod 16 has both aligned, since
+ * its packed data starts at offset 120). */
+WispError wisp_b200_blob_expert(const WispExpertMeta* meta, const void* d_blob,
+                                WispInt4Expert* out, WispErrCtx* err);
+
 size_t wisp_b200_moe_workspace_bytes(const WispMoeConfig* cfg);
 
 /* out[T x M] (fp32) = sum_k w[t,k] * expert_{idx[t,k]}(x_t) + shared(x_t).
@@ -238,6 +264,21 @@ WispError wisp_b200_moe_forward(const WispMoeConfig* cfg, const WispMoeWeights* 
                                 const uint16_t* d_x, float* d_out, int* d_topk_idx,
                                 float* d_topk_w, void* d_workspace, size_t workspace_bytes,
                                 cudaStream_t stream, WispErrCtx* err);
+
+/* Dense int4 MLP over T tokens (the MLP of the first dense layers of
+ * DeepSeek/GLM models, csrc/core/wisp_engine.c:1676-1686, and any
+ * always-on MLP quantised to int4):
+ *   d_out[T x M] (fp32) = down(silu(gate x) * up x), x bf16 [T x M].
+ * d_mlp is a DEVICE array holding the MLP's one WispInt4Expert entry and
+ * d_prepared its prepared set (wisp_b200_prepare_experts over that entry).
+ * Uses cfg's tokens, hidden, inter and group_size only. The output rows are
+ * written, not accumulated. d_error_flag as for wisp_b200_grouped_ffn (may
+ * be NULL). One call at a time per workspace. */
+size_t wisp_b200_dense_mlp_workspace_bytes(const WispMoeConfig* cfg);
+WispError wisp_b200_dense_mlp(const WispMoeConfig* cfg, const void* d_prepared,
+                              const WispInt4Expert* d_mlp, const uint16_t* d_x, float* d_out,
+                              void* d_workspace, size_t workspace_bytes, int* d_error_flag,
+                              cudaStream_t stream, WispErrCtx* err);
 
 /* --------------------------------------------------------------------------
  * Building blocks (used by the expert-parallel path and by tests).
@@ -348,6 +389,17 @@ WispError wisp_b200_ep_gather_rows(const uint8_t* d_recv, int world, int e_loc, 
 WispError wisp_b200_ep_combine(const float* d_yback, const int* d_slot, int tokens, int world,
                                int cap, int hidden, float* d_out, cudaStream_t stream,
                                WispErrCtx* err);
+
+/* The return exchange in fp16 (half the bytes of fp32 rows): the owner
+ * rounds its fp32 return rows to fp16 (d_y16[i] = fp16(d_y[i]) for rows x
+ * hidden values), the rows travel, and the home rank adds them in rank
+ * order with wisp_b200_ep_combine_f16 (same contract as wisp_b200_ep_combine
+ * with fp16 rows). */
+WispError wisp_b200_ep_return_rows(const float* d_y, int rows, int hidden, uint16_t* d_y16,
+                                   cudaStream_t stream, WispErrCtx* err);
+WispError wisp_b200_ep_combine_f16(const uint16_t* d_yback, const int* d_slot, int tokens,
+                                   int world, int cap, int hidden, float* d_out,
+                                   cudaStream_t stream, WispErrCtx* err);
 
 /* Between stacked layers: d_out[t] = bf16(d_in[t] / rms(d_in[t])), fp32 in. */
 WispError wisp_b200_rms_rescale(const float* d_in, uint16_t* d_out, int tokens, int hidden,

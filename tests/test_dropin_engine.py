@@ -47,6 +47,16 @@ def _load():
     for f in (L.eh_run_moe, L.eh_run_moe_fused):
         f.restype = C.c_int
         f.argtypes = [_P] * 5
+    L.eh_prefill_moe.restype = C.c_int
+    L.eh_prefill_moe.argtypes = [_P, _P, C.c_int, _P, _P, _P]
+    L.eh_move_expert.restype = C.c_int
+    L.eh_move_expert.argtypes = [_P, C.c_int]
+    L.eh_batched_state.restype = C.c_int
+    L.eh_batched_state.argtypes = [_P, C.POINTER(_P), C.POINTER(_P), C.POINTER(C.c_size_t)]
+    L.eh_copy_prepared.restype = C.c_int
+    L.eh_copy_prepared.argtypes = [_P, _P]
+    L.eh_dense_mlp_int4.restype = C.c_int
+    L.eh_dense_mlp_int4.argtypes = [_P, _P, C.c_size_t, _P, _P]
     L.eh_destroy.argtypes = [_P]
     return L
 
@@ -108,5 +118,144 @@ def test_reference_run_moe_on_dropin_launchers_and_fused_entry(orc):
                     assert_close(out, want, what=f"{name} token {t}")
                 else:
                     assert_close(out, want, tol, tol, what=f"{name} token {t}")
+    finally:
+        L.eh_destroy(h)
+
+
+def _bf16_exact(rng, shape):
+    """float32 values that bf16 represents exactly (the batched entry's input
+    format), so the per-token reference sees the same activations."""
+    v = rng.standard_normal(shape).astype(np.float32)
+    return (v.view(np.uint32) & np.uint32(0xFFFF0000)).view(np.float32)
+
+
+def _ref_margins(router16, bias16, x, k):
+    """Gap between the k-th and (k+1)-th logit per token (fp64)."""
+    W = router16.view(np.float16).astype(np.float64)
+    lg = x.astype(np.float64) @ W.T + bias16.view(np.float16).astype(np.float64)
+    s = -np.sort(-lg, axis=1)
+    return s[:, k - 1] - s[:, k]
+
+
+def test_batched_prefill_layer_through_engine_tiers():
+    """The batched replacement of wisp_prefill's per-token loop for one MoE
+    layer, run inside the reference engine: routing of all prompt tokens at
+    once, expert residency through the engine's own tier fetch, slot-wise
+    preparation that follows each blob's VRAM address, the grouped int4 FFN.
+    Checked per token against the reference's own CPU router and expert FFN
+    (reference blobs with zero points), at a prompt length that keeps every
+    segment on the register path (48 tokens) and one that puts them on
+    tcgen05 (300); then the prepared set against a whole-table preparation,
+    and again after two blobs moved to new VRAM addresses."""
+    import torch
+    from oracle.oracle import RefCPU
+    from wisp_b200 import abi
+
+    L = _load()
+    ref = RefCPU()
+    rng = np.random.default_rng(57)
+    M, I, E, k, gs = 512, 256, 16, 4, 128
+
+    def mat(rows, cols):
+        n = rows * cols
+        return Int4Matrix(rng.integers(0, 256, n // 2, dtype=np.uint8),
+                          np.float16(rng.uniform(0.004, 0.02, n // gs)).view(np.uint16),
+                          np.float16(rng.uniform(-0.01, 0.01, n // gs)).view(np.uint16), rows, cols)
+
+    blobs = [np.frombuffer(pack_blob(mat(I, M), mat(I, M), mat(M, I), group_size=gs), np.uint8).copy()
+             for _ in range(E)]
+    router = np.float16(rng.standard_normal((E, M)) * 0.05).view(np.uint16)
+    bias = np.float16(rng.standard_normal(E) * 0.1).view(np.uint16)
+    h = L.eh_create(M, I, E, k, gs, 0, _ptr(router), _ptr(bias), None, None, None)
+    assert h, "engine harness set-up failed"
+    d_tab, d_prep, nbytes = _P(), _P(), C.c_size_t()
+    try:
+        for e in range(E):
+            assert L.eh_put_expert(h, e, _ptr(blobs[e]), blobs[e].size) == 0
+
+        def prefill(x):
+            T = x.shape[0]
+            out = np.empty((T, M), np.float32)
+            idx = np.empty((T, k), np.int32)
+            w = np.empty((T, k), np.float32)
+            assert L.eh_prefill_moe(h, _ptr(x), T, _ptr(out), _ptr(idx), _ptr(w)) == 0
+            return out, idx, w
+
+        for T in (48, 300):
+            x = _bf16_exact(rng, (T, M))
+            out, idx, w = prefill(x)
+            margin = _ref_margins(router, bias, x, k)
+            tokens = range(T) if T <= 48 else range(0, T, 7)
+            for t in tokens:
+                idx_ref, w_ref = ref.router_topk(router, bias, x[t], k)
+                if margin[t] >= 1e-4:
+                    np.testing.assert_array_equal(idx[t], idx_ref, err_msg=f"T={T} token {t}")
+                    np.testing.assert_allclose(w[t], w_ref, rtol=1e-4, err_msg=f"T={T} token {t}")
+                want = np.zeros(M, np.float32)
+                for j in range(k):   # the reference CPU FFN under the batched routing
+                    ref.expert_ffn(blobs[idx[t, j]].tobytes(), x[t], want, float(w[t, j]))
+                assert_close(out[t], want, what=f"prefill T={T} token {t}")
+            prepares = L.eh_batched_state(h, C.byref(d_tab), C.byref(d_prep), C.byref(nbytes))
+            assert prepares == len(np.unique(idx)) or T > 48
+
+        # every expert is resident and prepared: the slot-built set equals a
+        # whole-table preparation over the same table
+        def check_whole_set():
+            got = np.empty(nbytes.value, np.uint8)
+            assert L.eh_copy_prepared(h, _ptr(got)) == 0
+            cfg = abi.WispMoeConfig(tokens=1, hidden=M, inter=I, n_experts=E, top_k=k,
+                                    group_size=gs, router_fp16=1)
+            fresh = torch.zeros(nbytes.value, dtype=torch.uint8, device="cuda")
+            abi.call("wisp_b200_prepare_experts", C.byref(cfg), d_tab.value, E, fresh.data_ptr(),
+                     nbytes.value, torch.cuda.current_stream().cuda_stream)
+            np.testing.assert_array_equal(got, fresh.cpu().numpy())
+
+        prepares = L.eh_batched_state(h, C.byref(d_tab), C.byref(d_prep), C.byref(nbytes))
+        assert prepares == E
+        check_whole_set()
+        out1, idx1, _ = prefill(x)
+        assert L.eh_batched_state(h, C.byref(d_tab), C.byref(d_prep), C.byref(nbytes)) == E
+        for e in (3, 11):
+            assert L.eh_move_expert(h, e) == 0
+        out2, idx2, _ = prefill(x)
+        assert L.eh_batched_state(h, C.byref(d_tab), C.byref(d_prep), C.byref(nbytes)) == E + 2
+        check_whole_set()
+        np.testing.assert_array_equal(idx2, idx1)
+        assert_close(out2, out1, 1e-5, 1e-6, "after two blobs moved")
+    finally:
+        L.eh_destroy(h)
+
+
+def test_int4_dense_mlp_on_engine():
+    """run_dense_mlp with the MLP quantised to int4 (a reference blob with zero
+    points), through wisp_b200_expert_ffn with weight 1.0 inside the engine,
+    against the reference's own CPU expert FFN on the same blob."""
+    import torch  # noqa: F401
+    from oracle.oracle import RefCPU
+
+    L = _load()
+    ref = RefCPU()
+    rng = np.random.default_rng(8)
+    M, I, E, k, gs, DI = 512, 256, 4, 2, 64, 384
+
+    def mat(rows, cols):
+        n = rows * cols
+        return Int4Matrix(rng.integers(0, 256, n // 2, dtype=np.uint8),
+                          np.float16(rng.uniform(0.004, 0.02, n // gs)).view(np.uint16),
+                          np.float16(rng.uniform(-0.01, 0.01, n // gs)).view(np.uint16), rows, cols)
+
+    dense = np.frombuffer(pack_blob(mat(DI, M), mat(DI, M), mat(M, DI), group_size=gs),
+                          np.uint8).copy()
+    router = np.float16(rng.standard_normal((E, M)) * 0.05).view(np.uint16)
+    h = L.eh_create(M, DI, E, k, gs, 0, _ptr(router), None, None, None, None)
+    assert h, "engine harness set-up failed"
+    try:
+        for t in range(3):
+            x = rng.standard_normal(M).astype(np.float32)
+            out = np.empty(M, np.float32)
+            assert L.eh_dense_mlp_int4(h, _ptr(dense), dense.size, _ptr(x), _ptr(out)) == 0
+            want = np.zeros(M, np.float32)
+            ref.expert_ffn(dense.tobytes(), x, want, 1.0)
+            assert_close(out, want, 1e-5, 1e-5, what=f"dense int4 token {t}")
     finally:
         L.eh_destroy(h)

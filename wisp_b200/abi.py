@@ -100,6 +100,11 @@ SIGNATURES = {
     "wisp_b200_set_skinny_max_rows": (None, [_I]),
     "wisp_b200_prepared_bytes": (_SZ, [C.POINTER(WispMoeConfig), _I]),
     "wisp_b200_prepare_experts": (_I, [C.POINTER(WispMoeConfig), _P, _I, _P, _SZ, _P, _E]),
+    "wisp_b200_prepare_expert_slot": (_I, [C.POINTER(WispMoeConfig), _I, _I,
+                                           C.POINTER(WispInt4Expert), _P, _SZ, _P, _E]),
+    "wisp_b200_blob_expert": (_I, [C.POINTER(WispExpertMeta), _P, C.POINTER(WispInt4Expert), _E]),
+    "wisp_b200_dense_mlp_workspace_bytes": (_SZ, [C.POINTER(WispMoeConfig)]),
+    "wisp_b200_dense_mlp": (_I, [C.POINTER(WispMoeConfig), _P, _P, _P, _P, _P, _SZ, _P, _P, _E]),
     "wisp_b200_pack_rows": (_I, [_P, _P, _I, _I, _P, _P, _E]),
     "wisp_b200_dispatch_plan": (_I, [C.POINTER(WispMoeConfig), _P, _P, _P, _P, _P, _P, _P, _E]),
     "wisp_b200_rms_rescale": (_I, [_P, _P, _I, _I, _F, _P, _E]),
@@ -109,6 +114,8 @@ SIGNATURES = {
     "wisp_b200_ep_recv_plan": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _E]),
     "wisp_b200_ep_gather_rows": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _E]),
     "wisp_b200_ep_combine": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _E]),
+    "wisp_b200_ep_combine_f16": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _E]),
+    "wisp_b200_ep_return_rows": (_I, [_P, _I, _I, _P, _P, _E]),
     "wisp_b200_check_error_flag": (_I, [_P, _P, _E]),
     "wisp_b200_moe_error_word": (_P, [C.POINTER(WispMoeConfig), _P]),
     "wisp_b200_debug_set_counters": (None, [_P]),

@@ -950,12 +950,16 @@ __global__ void __launch_bounds__(1024) plan_all_kernel(const __grid_constant__ 
 
 // Scales (and zero points) of every prepared matrix, transposed from
 // [rows][groups] to [row tile][group][128 rows].
+// With experts == nullptr the launch covers the one entry `one`, written as
+// entry `slot` of the prepared set (gridDim.y = 3).
 __global__ void transpose_scales_kernel(const WispInt4Expert* __restrict__ experts, int n, int M,
                                         int I, int gs, uint8_t* __restrict__ prepared,
-                                        size_t off_scales, size_t off_zeros, size_t mat_bytes) {
-  const int e = blockIdx.y;  // matrix entry v*3 + m
-  const int v = e / 3, m = e % 3;
-  const WispInt4Expert ex = experts[v];
+                                        size_t off_scales, size_t off_zeros, size_t mat_bytes,
+                                        WispInt4Expert one, int slot) {
+  const int m = blockIdx.y % 3;
+  const int v = experts ? (int)blockIdx.y / 3 : slot;
+  const int e = v * 3 + m;  // matrix entry
+  const WispInt4Expert ex = experts ? experts[v] : one;
   const WispInt4Mat mt = m == 0 ? ex.gate : m == 1 ? ex.up : ex.down;
   const int rows = m == 2 ? M : I;
   const int gpr = (m == 2 ? I : M) / gs;
@@ -977,11 +981,13 @@ __global__ void transpose_scales_kernel(const WispInt4Expert* __restrict__ exper
 
 // The register-path kernel's per-stage runs of scales and zero points (see
 // PreparedLayout): blockIdx.y = expert * 2 + (0: gate/up pair, 1: down).
+// With experts == nullptr: the one entry `one` as entry `slot` (gridDim.y = 2).
 __global__ void skinny_scales_kernel(const WispInt4Expert* __restrict__ experts, int M, int I,
                                      int gs, uint8_t* __restrict__ prepared, size_t off_scales,
-                                     size_t off_zeros, size_t gu_bytes, size_t dn_bytes) {
-  const int v = blockIdx.y >> 1, part = blockIdx.y & 1;
-  const WispInt4Expert ex = experts[v];
+                                     size_t off_zeros, size_t gu_bytes, size_t dn_bytes,
+                                     WispInt4Expert one, int slot) {
+  const int v = experts ? (int)(blockIdx.y >> 1) : slot, part = blockIdx.y & 1;
+  const WispInt4Expert ex = experts ? experts[v] : one;
   const int G = 256 / gs;
   const size_t base = (size_t)v * (gu_bytes + dn_bytes) + (part ? gu_bytes : 0);
   uint16_t* so = reinterpret_cast<uint16_t*>(prepared + off_scales + base);
@@ -1184,6 +1190,57 @@ extern "C" void wisp_b200_debug_set_counters(unsigned long long* d_counters) {
   g_counters = d_counters;
 }
 
+namespace {
+// Host side of one entry's preparation: its three matrices' TMA descriptors
+// (tensor-core and register-path boxes) and zero-point flags.
+WispError encode_entry(const WispInt4Expert& x, int M, int I, int v, CUtensorMap* maps,
+                       CUtensorMap* maps_sk, int32_t* flags, WispErrCtx* err) {
+  const WispInt4Mat* mats[3] = {&x.gate, &x.up, &x.down};
+  for (int m = 0; m < 3; m++) {
+    const int rows = m == 2 ? M : I, cols = m == 2 ? I : M;
+    const WispInt4Mat& mt = *mats[m];
+    if (!mt.packed || !mt.scales)
+      return WB_FAIL(WISP_ERR_INVALID_ARG, "prepare_experts: entry %d matrix %d has no data", v, m);
+    if (((uintptr_t)mt.packed & 15) || ((uintptr_t)mt.scales & 1) || ((uintptr_t)mt.zeros & 1))
+      return WB_FAIL(WISP_ERR_INVALID_ARG,
+                     "prepare_experts: entry %d matrix %d: packed must be 16-byte aligned", v, m);
+    if (!encode_packed_map(&maps[m], mt.packed, rows, cols, m == 2 ? BM : kGuRows) ||
+        !encode_packed_map_sk(&maps_sk[m], mt.packed, rows, cols))
+      return WB_FAIL(WISP_ERR_CUDA, "prepare_experts: cuTensorMapEncodeTiled failed (entry %d)", v);
+    flags[m] = mt.zeros ? 1 : 0;
+  }
+  return WISP_OK;
+}
+
+// One slot's descriptors and flags, passed by value, written into the
+// prepared set: 6 x 128-byte descriptors copied as 16-byte words, the three
+// flag words, and the slot's three bits of the flag bitmap (atomic, since a
+// bitmap word is shared with neighbouring slots).
+struct SlotMeta {
+  CUtensorMap maps[3];
+  CUtensorMap maps_sk[3];
+  int32_t flags[3];
+};
+
+__global__ void write_slot_kernel(const __grid_constant__ SlotMeta sm, uint8_t* __restrict__ prepared,
+                                  size_t off_maps, size_t off_maps_sk, size_t off_flags,
+                                  size_t off_zbits, int slot) {
+  const int t = threadIdx.x;  // 48 threads: 8 words per descriptor
+  const uint4* src = reinterpret_cast<const uint4*>(t < 24 ? sm.maps : sm.maps_sk);
+  uint4* dst = reinterpret_cast<uint4*>(prepared + (t < 24 ? off_maps : off_maps_sk) +
+                                        (size_t)slot * 3 * sizeof(CUtensorMap));
+  const int w = t % 24;
+  dst[w] = src[w];
+  if (t < 3) {
+    const int i = slot * 3 + t;
+    reinterpret_cast<int32_t*>(prepared + off_flags)[i] = sm.flags[t];
+    unsigned int* zb = reinterpret_cast<unsigned int*>(prepared + off_zbits) + i / 32;
+    if (sm.flags[t]) atomicOr(zb, 1u << (i % 32));
+    else atomicAnd(zb, ~(1u << (i % 32)));
+  }
+}
+}  // namespace
+
 extern "C" size_t wisp_b200_prepared_bytes(const WispMoeConfig* cfg, int n_entries) {
   if (!cfg || n_entries <= 0 || check_shapes(cfg, nullptr) != WISP_OK) return 0;
   return prepared_layout(cfg, n_entries).total;
@@ -1210,21 +1267,9 @@ extern "C" WispError wisp_b200_prepare_experts(const WispMoeConfig* cfg,
   std::vector<CUtensorMap> maps((size_t)n_entries * 3), maps_sk((size_t)n_entries * 3);
   std::vector<int32_t> flags((size_t)n_entries * 3);
   for (int v = 0; v < n_entries; v++) {
-    const WispInt4Mat* mats[3] = {&h[v].gate, &h[v].up, &h[v].down};
-    for (int m = 0; m < 3; m++) {
-      const int rows = m == 2 ? M : I, cols = m == 2 ? I : M;
-      const WispInt4Mat& mt = *mats[m];
-      if (!mt.packed || !mt.scales)
-        return WB_FAIL(WISP_ERR_INVALID_ARG, "prepare_experts: entry %d matrix %d has no data", v, m);
-      if (((uintptr_t)mt.packed & 15) || ((uintptr_t)mt.scales & 1) || ((uintptr_t)mt.zeros & 1))
-        return WB_FAIL(WISP_ERR_INVALID_ARG,
-                       "prepare_experts: entry %d matrix %d: packed must be 16-byte aligned", v, m);
-      if (!encode_packed_map(&maps[(size_t)v * 3 + m], mt.packed, rows, cols,
-                             m == 2 ? BM : kGuRows) ||
-          !encode_packed_map_sk(&maps_sk[(size_t)v * 3 + m], mt.packed, rows, cols))
-        return WB_FAIL(WISP_ERR_CUDA, "prepare_experts: cuTensorMapEncodeTiled failed (entry %d)", v);
-      flags[(size_t)v * 3 + m] = mt.zeros ? 1 : 0;
-    }
+    e = encode_entry(h[v], M, I, v, &maps[(size_t)v * 3], &maps_sk[(size_t)v * 3],
+                     &flags[(size_t)v * 3], err);
+    if (e != WISP_OK) return e;
   }
   uint8_t* base = static_cast<uint8_t*>(d_prepared);
   WB_CUDA_CHECK(cudaMemcpyAsync(base + PL.maps, maps.data(), maps.size() * sizeof(CUtensorMap),
@@ -1241,14 +1286,49 @@ extern "C" WispError wisp_b200_prepare_experts(const WispMoeConfig* cfg,
                                 cudaMemcpyHostToDevice, stream));
   dim3 grid(64, n_entries * 3);
   transpose_scales_kernel<<<grid, 256, 0, stream>>>(d_experts, n_entries, M, I, cfg->group_size,
-                                                    base, PL.scales, PL.zeros, PL.mat_sc_bytes);
+                                                    base, PL.scales, PL.zeros, PL.mat_sc_bytes,
+                                                    WispInt4Expert{}, 0);
   WB_CUDA_CHECK(cudaGetLastError());
   skinny_scales_kernel<<<dim3(64, n_entries * 2), 256, 0, stream>>>(
       d_experts, M, I, cfg->group_size, base, PL.sk_scales, PL.sk_zeros, PL.sk_gu_bytes,
-      PL.sk_dn_bytes);
+      PL.sk_dn_bytes, WispInt4Expert{}, 0);
   WB_CUDA_CHECK(cudaGetLastError());
   // The host vectors are read by the copies above before they are freed.
   WB_CUDA_CHECK(cudaStreamSynchronize(stream));
+  return WISP_OK;
+}
+
+extern "C" WispError wisp_b200_prepare_expert_slot(const WispMoeConfig* cfg, int n_entries,
+                                                   int slot, const WispInt4Expert* entry,
+                                                   void* d_prepared, size_t prepared_bytes,
+                                                   cudaStream_t stream, WispErrCtx* err) {
+  if (!cfg || !entry || !d_prepared || n_entries <= 0 || slot < 0 || slot >= n_entries)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "prepare_expert_slot: bad arguments (slot %d of %d)",
+                   slot, n_entries);
+  WispError e = check_shapes(cfg, err);
+  if (e != WISP_OK) return e;
+  const PreparedLayout PL = prepared_layout(cfg, n_entries);
+  if (prepared_bytes < PL.total)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "prepare_expert_slot: buffer %zu < required %zu",
+                   prepared_bytes, PL.total);
+  if ((uintptr_t)d_prepared & 255)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "prepare_expert_slot: buffer must be 256-byte aligned");
+  const int M = cfg->hidden, I = cfg->inter;
+  SlotMeta sm;
+  memset(&sm, 0, sizeof sm);
+  e = encode_entry(*entry, M, I, slot, sm.maps, sm.maps_sk, sm.flags, err);
+  if (e != WISP_OK) return e;
+  uint8_t* base = static_cast<uint8_t*>(d_prepared);
+  write_slot_kernel<<<1, 48, 0, stream>>>(sm, base, PL.maps, PL.maps_sk, PL.flags, PL.zbits, slot);
+  WB_CUDA_CHECK(cudaGetLastError());
+  transpose_scales_kernel<<<dim3(64, 3), 256, 0, stream>>>(nullptr, n_entries, M, I,
+                                                           cfg->group_size, base, PL.scales,
+                                                           PL.zeros, PL.mat_sc_bytes, *entry, slot);
+  WB_CUDA_CHECK(cudaGetLastError());
+  skinny_scales_kernel<<<dim3(64, 2), 256, 0, stream>>>(
+      nullptr, M, I, cfg->group_size, base, PL.sk_scales, PL.sk_zeros, PL.sk_gu_bytes,
+      PL.sk_dn_bytes, *entry, slot);
+  WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
 

@@ -174,6 +174,114 @@ extern "C" WispError wisp_b200_moe_forward(const WispMoeConfig* cfg, const WispM
                               ws.error_flag, true, cfg->tokens, stream, err);
 }
 
+// ---------------------------------------------------------------------------
+// Dense int4 MLP: the MLP as the one segment of a one-entry weight set, run
+// through the grouped kernels in mode 1 (plain fp32 row stores, no weights,
+// no atomics). The reference runs this MLP in fp16 through op_swiglu_ffn +
+// op_gemv (csrc/core/wisp_engine.c:1676-1686).
+// ---------------------------------------------------------------------------
+namespace {
+
+__global__ void one_segment_kernel(WispSegment* s, int rows) {
+  WispSegment v;
+  v.expert = 0;
+  v.row_begin = 0;
+  v.rows = rows;
+  v.reserved = 0;
+  *s = v;
+}
+
+struct DenseWs {
+  WispSegment* seg;
+  void* grouped;
+  size_t grouped_bytes;
+  uint16_t* xp;
+  uint16_t* h;
+  size_t bytes;
+};
+
+DenseWs carve_dense(const WispMoeConfig* c, void* base) {
+  DenseWs ws;
+  Carve cv;
+  const int T = c->tokens;
+  ws.seg = cv.take<WispSegment>(base, 1);
+  ws.grouped_bytes = wisp_b200_grouped_workspace_bytes(c, 1, T);
+  ws.grouped = cv.take<uint8_t>(base, ws.grouped_bytes);
+  ws.xp = cv.take<uint16_t>(base, (size_t)T * c->hidden);
+  ws.h = cv.take<uint16_t>(base, (size_t)T * c->inter);
+  ws.bytes = (cv.off + 255) & ~(size_t)255;
+  return ws;
+}
+
+WispError validate_dense(const WispMoeConfig* c, WispErrCtx* err) {
+  if (!c) return WB_FAIL(WISP_ERR_INVALID_ARG, "dense_mlp: null config");
+  if (c->tokens <= 0 || c->hidden <= 0 || c->inter <= 0 || c->hidden % 128 || c->inter % 128)
+    return WB_FAIL(WISP_ERR_INVALID_ARG,
+                   "dense_mlp: tokens=%d hidden=%d inter=%d (hidden, inter multiples of 128)",
+                   c->tokens, c->hidden, c->inter);
+  if (c->group_size != 64 && c->group_size != 128)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "dense_mlp: group_size=%d (64 or 128)", c->group_size);
+  return WISP_OK;
+}
+
+}  // namespace
+
+extern "C" size_t wisp_b200_dense_mlp_workspace_bytes(const WispMoeConfig* cfg) {
+  if (validate_dense(cfg, nullptr) != WISP_OK) return 0;
+  return carve_dense(cfg, nullptr).bytes;
+}
+
+extern "C" WispError wisp_b200_dense_mlp(const WispMoeConfig* cfg, const void* d_prepared,
+                                         const WispInt4Expert* d_mlp, const uint16_t* d_x,
+                                         float* d_out, void* d_workspace, size_t workspace_bytes,
+                                         int* d_error_flag, cudaStream_t stream, WispErrCtx* err) {
+  WispError e = validate_dense(cfg, err);
+  if (e != WISP_OK) return e;
+  if (!d_prepared || !d_mlp || !d_x || !d_out || !d_workspace)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "dense_mlp: null pointer argument");
+  if (((uintptr_t)d_x | (uintptr_t)d_workspace) & 15)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "dense_mlp: x and workspace must be 16-byte aligned");
+  const DenseWs ws = carve_dense(cfg, d_workspace);
+  if (workspace_bytes < ws.bytes)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "dense_mlp: workspace %zu < required %zu",
+                   workspace_bytes, ws.bytes);
+  const int T = cfg->tokens;
+  one_segment_kernel<<<1, 1, 0, stream>>>(ws.seg, T);
+  WB_CUDA_CHECK(cudaGetLastError());
+  e = wb::launch_pack_q16(d_x, nullptr, T, cfg->hidden, ws.xp,
+                          wb::grouped_xq(ws.grouped, 1, T, cfg->hidden, cfg->inter), ws.seg, 1,
+                          wb::grouped_sk_rows(1, 1), stream, err);
+  if (e != WISP_OK) return e;
+  return wb::grouped_ffn_impl(cfg, d_prepared, d_mlp, 1, ws.seg, 1, T, ws.xp, ws.h, 1, nullptr,
+                              nullptr, d_out, ws.grouped, ws.grouped_bytes, d_error_flag, true, T,
+                              stream, err);
+}
+
+// Pointers into a reference blob (header at offset 0) from its parsed meta.
+extern "C" WispError wisp_b200_blob_expert(const WispExpertMeta* meta, const void* d_blob,
+                                           WispInt4Expert* out, WispErrCtx* err) {
+  if (!meta || !d_blob || !out) return WB_FAIL(WISP_ERR_INVALID_ARG, "blob_expert: null pointer");
+  if (!meta->valid) return WB_FAIL(WISP_ERR_INVALID_ARG, "blob_expert: meta not valid");
+  const uint8_t* base = static_cast<const uint8_t*>(d_blob);
+  WispInt4Mat* mats[3] = {&out->gate, &out->up, &out->down};
+  for (int m = 0; m < 3; m++) {
+    const uint8_t* packed = base + meta->packed_off[m];
+    const uint8_t* scales = base + meta->scales_off[m];
+    // Zero points are present when bytes remain between zeros_off and the
+    // next matrix's packed data (the end of the blob for down).
+    const size_t end = m < 2 ? meta->packed_off[m + 1] : meta->total_bytes;
+    const uint8_t* zeros = end > meta->zeros_off[m] ? base + meta->zeros_off[m] : nullptr;
+    if (((uintptr_t)packed | (uintptr_t)scales | (uintptr_t)zeros) & 15)
+      return WB_FAIL(WISP_ERR_INVALID_ARG,
+                     "blob_expert: matrix %d data not 16-byte aligned (place the blob at an "
+                     "address = 8 mod 16)", m);
+    mats[m]->packed = packed;
+    mats[m]->scales = reinterpret_cast<const wisp_half*>(scales);
+    mats[m]->zeros = reinterpret_cast<const wisp_half*>(zeros);
+  }
+  return WISP_OK;
+}
+
 extern "C" int* wisp_b200_moe_error_word(const WispMoeConfig* cfg, void* d_workspace) {
   if (validate(cfg, nullptr) != WISP_OK || !d_workspace) return nullptr;
   return carve(cfg, d_workspace).error_flag;
