@@ -133,6 +133,12 @@ class CpuOps:
         self.grouped(cfg, lw, [(int(e), int(b), int(r)) for e, b, r, _ in sv], rows, xp, h, mode,
                      row_token, row_weight, out, tiles, flag)
 
+    def ret_dtype(self):
+        return torch.float64
+
+    def return_rows(self, yr, yr16):
+        yr16.copy_(yr)
+
     def ep_combine(self, yback, slot, tokens, world, cap, out):
         sl = slot.numpy()
         for t in range(tokens):

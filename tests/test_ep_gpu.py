@@ -6,7 +6,9 @@ half of the tokens; EpLayer exchanges rows with NCCL all-to-all and runs the
 grouped FFN (register-path and tensor-core kernels) on the received rows.
 The concatenated output must match the fp64 oracle within the parity
 tolerance, and the single-GPU MoeLayer output for the same tokens within
-max_rel 1e-3 / mean_rel 1e-4: each local expert is one segment of the same
+max_rel 2e-3 / mean_rel 3e-4: the owners return their rows in fp16 (a
+relative rounding of at most 2^-11 on each returned partial sum), and each
+local expert is one segment of the same
 rows as on one GPU and runs on the same kernel (the routing threshold is set
 to 16 rows in both runs, so that the shared expert's 32 rows per rank and 64
 rows on one GPU both take the tensor-core kernel), but the tensor-core kernel
@@ -107,7 +109,7 @@ def test_ep_two_gpus_matches_single_gpu_and_oracle(orc, spec):
     assert len(clear) >= spec.tokens * 0.95
     # Same kernels per segment; fp32 summation order differs (K split, final
     # weighted adds), see the module docstring.
-    assert_close(got[clear], single[clear], 1e-3, 1e-4, "EP vs single GPU")
+    assert_close(got[clear], single[clear], 2e-3, 3e-4, "EP vs single GPU")
     toks = [int(t) for t in clear[:: max(1, len(clear) // 32)]]
     ref = oracle_outputs(orc, layers[0], x, idx, w, toks)
     assert_close(got[toks], ref, what="EP vs oracle")

@@ -31,8 +31,13 @@
 //                        one segment per local expert over the gathered
 //                        rows, the receive row and weight of each.
 //   ep_gather_kernel     gathered fp16 rows from the receive blocks.
+//   ep_to_half_kernel    the owner's fp32 return rows rounded to fp16 (the
+//                        return exchange carries half the bytes).
 //   ep_combine_kernel    out[t] += the returned rows of token t, in rank order.
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "internal.h"
@@ -241,8 +246,18 @@ __global__ void ep_gather_kernel(const uint8_t* __restrict__ recv, Layout L, int
   for (int i = threadIdx.x; i < M / 8; i += blockDim.x) dst[i] = __ldg(src + i);
 }
 
+// Four consecutive values of a returned row as floats (fp32 or fp16 rows).
+__device__ __forceinline__ float4 load4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+__device__ __forceinline__ float4 load4(const __half* p) {
+  const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
 // One block per token: out[t] += yback[q * cap + slot[t][q]] for q = 0..world-1.
-__global__ void ep_combine_kernel(const float* __restrict__ y, const int* __restrict__ slot,
+template <typename T>
+__global__ void ep_combine_kernel(const T* __restrict__ y, const int* __restrict__ slot,
                                   int world, int cap, int M, float* __restrict__ out) {
   __shared__ int sl[kMaxWorld];
   const int t = blockIdx.x;
@@ -253,13 +268,27 @@ __global__ void ep_combine_kernel(const float* __restrict__ y, const int* __rest
     float4 acc = *reinterpret_cast<const float4*>(orow + i);
     for (int q = 0; q < world; q++) {
       if (sl[q] < 0) continue;
-      const float4 v = __ldg(reinterpret_cast<const float4*>(y + ((size_t)q * cap + sl[q]) * M + i));
+      const float4 v = load4(y + ((size_t)q * cap + sl[q]) * M + i);
       acc.x += v.x;
       acc.y += v.y;
       acc.z += v.z;
       acc.w += v.w;
     }
     *reinterpret_cast<float4*>(orow + i) = acc;
+  }
+}
+
+// The owner's fp32 return rows rounded to fp16 for the return exchange
+// (half its bytes); four values per thread.
+__global__ void ep_to_half_kernel(const float* __restrict__ y, size_t n4, __half* __restrict__ o) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(y) + i);
+    const __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+    uint2 u;
+    u.x = *reinterpret_cast<const uint32_t*>(&a);
+    u.y = *reinterpret_cast<const uint32_t*>(&b);
+    reinterpret_cast<uint2*>(o)[i] = u;
   }
 }
 
@@ -344,8 +373,39 @@ extern "C" WispError wisp_b200_ep_combine(const float* d_yback, const int* d_slo
     return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_combine: world=%d tokens=%d cap=%d hidden=%d", world,
                    tokens, cap, hidden);
   if (tokens == 0) return WISP_OK;
-  wb::launch_k(ep_combine_kernel, tokens, 256, 0, stream, d_yback, d_slot, world, cap, hidden,
-               d_out);
+  wb::launch_k(ep_combine_kernel<float>, tokens, 256, 0, stream, d_yback, d_slot, world, cap,
+               hidden, d_out);
+  WB_CUDA_CHECK(cudaGetLastError());
+  return WISP_OK;
+}
+
+extern "C" WispError wisp_b200_ep_combine_f16(const uint16_t* d_yback, const int* d_slot,
+                                             int tokens, int world, int cap, int hidden,
+                                             float* d_out, cudaStream_t stream, WispErrCtx* err) {
+  if (!d_yback || !d_slot || !d_out)
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_combine_f16: null pointer argument");
+  if (world < 1 || world > kMaxWorld || cap < 1 || tokens < 0 || tokens > cap || hidden % 4 ||
+      ((uintptr_t)d_yback & 7) || ((uintptr_t)d_out & 15))
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_combine_f16: world=%d tokens=%d cap=%d hidden=%d",
+                   world, tokens, cap, hidden);
+  if (tokens == 0) return WISP_OK;
+  wb::launch_k(ep_combine_kernel<__half>, tokens, 256, 0, stream,
+               reinterpret_cast<const __half*>(d_yback), d_slot, world, cap, hidden, d_out);
+  WB_CUDA_CHECK(cudaGetLastError());
+  return WISP_OK;
+}
+
+extern "C" WispError wisp_b200_ep_return_rows(const float* d_y, int rows, int hidden,
+                                             uint16_t* d_y16, cudaStream_t stream,
+                                             WispErrCtx* err) {
+  if (!d_y || !d_y16) return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_return_rows: null pointer argument");
+  if (rows < 0 || hidden < 4 || hidden % 4 || ((uintptr_t)d_y & 15) || ((uintptr_t)d_y16 & 7))
+    return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_return_rows: rows=%d hidden=%d", rows, hidden);
+  const size_t n4 = (size_t)rows * hidden / 4;
+  if (n4 == 0) return WISP_OK;
+  const int blocks = (int)std::min<size_t>((n4 + 255) / 256, (size_t)4 * 148);
+  wb::launch_k(ep_to_half_kernel, blocks, 256, 0, stream, d_y, n4,
+               reinterpret_cast<__half*>(d_y16));
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }

@@ -17,8 +17,9 @@ trip between routing and the expert FFN):
   (wisp_b200_ep_dispatch) -> all_to_all of the blocks, meanwhile the shared
   expert on own tokens -> gather the received rows expert-contiguous (one
   segment per local expert, as on one GPU) -> grouped FFN in mode 0 with the
-  routing weights, into one fp32 row per received token -> all_to_all of
-  those rows back -> each token adds its rows from the owners, in rank order.
+  routing weights, into one fp32 row per received token -> those rows
+  rounded to fp16 and sent back with one all_to_all -> each token adds its
+  rows from the owners, in rank order.
 cap = the most tokens any rank holds (a token fills at most one row of a
 block); padding rows are exchanged but never computed or read.
 
@@ -160,8 +161,15 @@ class CudaOps:
         abi.call("wisp_b200_check_error_flag", flag.data_ptr(), _stream())
 
     def ep_combine(self, yback, slot, tokens, world, cap, out):
-        abi.call("wisp_b200_ep_combine", yback.data_ptr(), slot.data_ptr(), tokens, world, cap,
+        abi.call("wisp_b200_ep_combine_f16", yback.data_ptr(), slot.data_ptr(), tokens, world, cap,
                  out.shape[1], out.data_ptr(), _stream())
+
+    def return_rows(self, yr, yr16):
+        abi.call("wisp_b200_ep_return_rows", yr.data_ptr(), yr.shape[0], yr.shape[1],
+                 yr16.data_ptr(), _stream())
+
+    def ret_dtype(self):
+        return torch.float16
 
     def block_layout(self, hidden, e_loc, cap, k):
         lay = BlockLayout(hidden, e_loc, cap, k, 2)
@@ -227,8 +235,11 @@ class EpLayer:
         self.recv = torch.zeros(world * nb, dtype=torch.uint8, device=dev)
         self.xsorted = torch.empty((RK, M), dtype=adt, device=dev)
         self.hr = torch.empty((max(RK, T), I), dtype=adt, device=dev)
+        # return rows: fp32 where the FFN accumulates them, then in the
+        # exchange dtype (fp16 on GPUs) for the trip back
         self.yr = torch.empty((world * self.cap, M), dtype=torch.float32, device=dev)
-        self.yback = torch.empty((world * self.cap, M), dtype=torch.float32, device=dev)
+        self.yr16 = torch.empty((world * self.cap, M), dtype=self.ops.ret_dtype(), device=dev)
+        self.yback = torch.empty((world * self.cap, M), dtype=self.ops.ret_dtype(), device=dev)
         self.src_pos = torch.empty(RK, dtype=torch.int32, device=dev)
         self.gw = torch.empty(RK, dtype=torch.float32, device=dev)
         self.total = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -286,6 +297,7 @@ class EpLayer:
         self.yr.zero_()
         ops.grouped_dev(self.cfg_loc, self.lw, self.rsegs, self.n_rsegs, self.rk, self.xsorted,
                         self.hr, 0, self.src_pos, self.gw, self.yr, self.gws, self.flag)
+        ops.return_rows(self.yr, self.yr16)
 
     def combine_phase(self, out: torch.Tensor) -> None:
         """Each token adds its returned rows from the owners, in rank order."""
@@ -314,7 +326,7 @@ class EpLayer:
         self.expert_phase(mark)
         m("ffn")
         # 3. the rows back to their tokens' ranks, added in rank order
-        dist.all_to_all_single(self.yback, self.yr, group=self.group)
+        dist.all_to_all_single(self.yback, self.yr16, group=self.group)
         m("return")
         self.combine_phase(out)
         m("combine")
@@ -347,6 +359,6 @@ def loopback_forward(layers: list, xs: list, outs: list) -> None:
     cap = layers[0].cap
     for r in range(W):
         for q in range(W):
-            layers[q].yback[r * cap:(r + 1) * cap].copy_(layers[r].yr[q * cap:(q + 1) * cap])
+            layers[q].yback[r * cap:(r + 1) * cap].copy_(layers[r].yr16[q * cap:(q + 1) * cap])
     for r in range(W):
         layers[r].combine_phase(outs[r])
