@@ -210,7 +210,8 @@ SIDE_CONFIGS = ["mixtral_b1", "mixtral_b64", "ds_b1", "ds_b128", "ds_prefill"]
 def measure_side_config(name: str, steps: int, warmup: int, peaks: dict) -> dict:
     """One MoE layer of configuration `name` (BASELINE configs[0]-[3]) as a
     step: router, dispatch, grouped FFN and combine through MoeLayer (the C
-    ABI's wisp_b200_moe_forward). A single layer's touched weights (180-210
+    ABI's wisp_b200_moe_forward), captured once as a CUDA graph and replayed
+    (eager launches if the capture fails; reported). A single layer's touched weights (180-210
     MB at batch 1) are close to the 126 MB L2, so every step is timed alone
     with CUDA events and L2 is flushed (a 256 MB write) between steps,
     outside the timed intervals. e2e adds the host->device copy of the
@@ -241,14 +242,39 @@ def measure_side_config(name: str, steps: int, warmup: int, peaks: dict) -> dict
 
     for _ in range(warmup):
         layer.forward(x, out)
-    ms = timed(lambda: layer.forward(x, out), steps)
+    # The layer as one CUDA graph (as a serving loop replays its decode step):
+    # its launches follow each other without host work between them.
+    graph, graph_note = None, "on"
+    try:
+        side = torch.cuda.Stream()
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            layer.forward(x, out)
+        stream.wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            layer.forward(x, out)
+        torch.cuda.synchronize()
+    except Exception as exc:  # noqa: BLE001 - reported in the result
+        graph, graph_note = None, f"capture failed: {type(exc).__name__}: {str(exc)[:120]}"
+
+    def run_layer():
+        if graph is not None:
+            graph.replay()
+        else:
+            layer.forward(x, out)
+
+    for _ in range(warmup):
+        run_layer()
+    ms = timed(run_layer, steps)
     layer.check()
     x_host = x.cpu().pin_memory()
     out_host = torch.empty((spec.tokens, spec.hidden), dtype=torch.float32).pin_memory()
 
     def e2e_step():
         x.copy_(x_host, non_blocking=True)
-        layer.forward(x, out)
+        run_layer()
         out_host.copy_(out, non_blocking=True)
 
     e2e_step()
@@ -276,11 +302,12 @@ def measure_side_config(name: str, steps: int, warmup: int, peaks: dict) -> dict
                      "scoring": "softmax" if spec.scoring == 0 else "sigmoid group-limited",
                      "skewed_router": spec.skew},
            "l2": "flushed between steps (256 MB write, untimed)",
+           "cuda_graph": graph_note,
            "roofline": roof,
            "e2e": {"value": round(spec.tokens / (ems / 1e3), 1), "unit": UNIT,
                    "h2d_bytes_per_step": x_host.numel() * 2,
                    "d2h_bytes_per_step": out_host.numel() * 4}}
-    del layer, layers_w, x, out, flush
+    del graph, layer, layers_w, x, out, flush
     torch.cuda.empty_cache()
     return res
 
