@@ -359,6 +359,41 @@ def test_moe_forward_small(orc, si, T, zeros, path):
     assert_close(out.cpu().numpy()[tokens], ref, what=spec.name)
 
 
+DECODE = [
+    dict(hidden=256, inter=256, n_experts=8, top_k=2, group_size=128),
+    dict(hidden=512, inter=256, n_experts=256, top_k=8, group_size=128, has_shared=True,
+         scoring=abi.WISP_SCORE_SIGMOID_GROUPED, n_groups=8, topk_groups=4, routed_scaling=2.5),
+    dict(hidden=256, inter=128, n_experts=384, top_k=8, group_size=64, has_shared=True),
+    dict(hidden=256, inter=128, n_experts=1024, top_k=32, group_size=128, has_shared=True),
+]
+
+
+@pytest.mark.parametrize("zeros", [False, True])
+@pytest.mark.parametrize("T", [1, 2, 3, 4])
+@pytest.mark.parametrize("di", range(len(DECODE)))
+def test_moe_forward_decode_batches(orc, di, T, zeros):
+    """Batches of 1-4 tokens take the decode chain (router logits, one
+    planner launch, register-path gate/up and down): routing and every
+    token's output against the oracle, twice over the same workspace, for
+    softmax and sigmoid scoring and expert counts from 8 to 1024 (+ shared)."""
+    spec = synth.MoeSpec(f"decode{di}", tokens=T, seed=300 + di, **DECODE[di])
+    layers, x = synth.make_model(spec, DEV, zeros=zeros)
+    lw = layers[0]
+    layer = MoeLayer(lw, T)
+    out = torch.full((T, spec.hidden), float("nan"), dtype=torch.float32, device=DEV)
+    for _ in range(2):   # the second call reuses the workspace (plans, rows, output)
+        layer.forward(x, out)
+        torch.cuda.synchronize()
+        layer.check()
+        idx = layer.idx.cpu().numpy()
+        w = layer.wt.cpu().numpy()
+        i_ref, w_ref, mg = oracle_route(orc, lw, x)
+        check_routing(idx, w, i_ref, w_ref, mg,
+                      near_tie=NEAR_TIE if spec.scoring == abi.WISP_SCORE_SOFTMAX else NEAR_TIE_SIGMOID)
+        ref = oracle_outputs(orc, lw, x, idx, w.astype(np.float64), list(range(T)))
+        assert_close(out.cpu().numpy(), ref, what=f"{spec.name} T={T}")
+
+
 def _segments_device(segs):
     arr = (abi.WispSegment * len(segs))()
     for i, (e, b, r) in enumerate(segs):

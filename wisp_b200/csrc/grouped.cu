@@ -57,6 +57,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "plan.cuh"
 #include "skinny.h"
 
 using namespace wb;
@@ -799,62 +800,6 @@ __device__ void plan_tiles(const WispSegment* __restrict__ segs, int nseg, int m
     for (int i = threadIdx.x; i < 8 * kMaxSplitItems; i += blockDim.x) tickets[i] = 0;
 }
 
-// Units of the register-path kernel: `per_seg` row blocks per chunk of `cols`
-// rows, for every segment of 1..max_rows rows, times a K split: when fewer
-// than `target` units would exist, each is cut into up to `max_ksplit`
-// K ranges (at most `nk`, one stage each at least), whose partial sums the
-// down epilogue adds atomically. units[nseg + 1] receives the split.
-__device__ void plan_units(const WispSegment* __restrict__ segs, int nseg, int per_seg,
-                           int cols, int max_rows, int max_ksplit, int nk, int target,
-                           int32_t* __restrict__ units) {
-  __shared__ int32_t warp_tot[32];
-  __shared__ int32_t carry;
-  if (threadIdx.x == 0) carry = 0;
-  __syncthreads();
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  for (int base = 0; base < nseg; base += blockDim.x) {
-    const int s = base + threadIdx.x;
-    int n = 0;
-    if (s < nseg) {
-      const int rows = segs[s].rows;
-      n = (rows > 0 && rows <= max_rows) ? per_seg * ((rows + cols - 1) / cols) : 0;
-    }
-    int v = n;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, v, o);
-      if (lane >= o) v += y;
-    }
-    if (lane == 31) warp_tot[w] = v;
-    __syncthreads();
-    if (w == 0) {
-      int tv = lane < (int)(blockDim.x >> 5) ? warp_tot[lane] : 0;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, tv, o);
-        if (lane >= o) tv += y;
-      }
-      warp_tot[lane] = tv;
-    }
-    __syncthreads();
-    const int incl = v + (w > 0 ? warp_tot[w - 1] : 0) + carry;
-    if (s < nseg) units[s] = incl - n;
-    __syncthreads();
-    if (threadIdx.x == blockDim.x - 1) carry = incl;
-    __syncthreads();
-  }
-  __syncthreads();
-  const int total = carry;
-  int ks = 1;
-  if (total > 0 && total < target) ks = min(min(max_ksplit, nk), (target + total - 1) / total);
-  if (ks < 1) ks = 1;
-  for (int i = threadIdx.x; i < nseg; i += blockDim.x) units[i] *= ks;
-  if (threadIdx.x == 0) {
-    units[nseg] = total * ks;
-    units[nseg + 1] = ks;
-  }
-}
-
 // Rows of the register-path segments (0 < rows <= sk_rows): fp16 rows in
 // interleaved K order (within 8 K: 0,4,1,5,2,6,3,7) -> q16 rows (layout in
 // skinny.h). Block (s, r) converts row r of segment s with 128 threads: a
@@ -1404,8 +1349,30 @@ WispError grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
                            const uint16_t* d_xp, uint16_t* d_h, int mode, const int* d_row_token,
                            const float* d_row_weight, float* d_out, void* d_workspace,
                            size_t workspace_bytes, int* d_error_flag, bool xq_ready,
-                           int max_seg_rows, cudaStream_t stream, WispErrCtx* err);
+                           int max_seg_rows, cudaStream_t stream, WispErrCtx* err,
+                           bool plans_ready = false);
+void decode_units(const WispMoeConfig* cfg, int n_segs, int n_entries, int rows_capacity, int mode,
+                  void* d_workspace, DecodeUnits* du);
 }  // namespace wb
+
+// The register path's plan arrays and plan numbers of a grouped call in mode
+// `mode` over n_segs segments, for a planner that runs before the call
+// (grouped_ffn_impl with plans_ready); the same numbers the call's own
+// planner uses.
+void wb::decode_units(const WispMoeConfig* cfg, int n_segs, int n_entries, int rows_capacity,
+                      int mode, void* d_workspace, DecodeUnits* du) {
+  const GroupedWs ws = carve_grouped(n_segs, rows_capacity, cfg->hidden, cfg->inter, d_workspace);
+  du->units_gu = ws.units_gu;
+  du->units_dn = ws.units_dn;
+  du->xq = ws.xq;
+  du->per_gu = wb::skinny_units_gateup(cfg->inter);
+  du->per_dn = wb::skinny_units_down(cfg->hidden);
+  du->cols = wb::skinny_cols();
+  du->sk_rows = wb::grouped_sk_rows(n_segs, n_entries);
+  du->ks_dn = mode == 0 ? 8 : 1;
+  du->nk_dn = wb::skinny_stages(cfg->inter);
+  du->target = 2 * num_sms();
+}
 
 extern "C" WispError wisp_b200_grouped_ffn(const WispMoeConfig* cfg, const void* d_prepared,
                                            const WispInt4Expert* d_experts,
@@ -1429,7 +1396,7 @@ WispError wb::grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
                                const int* d_row_token, const float* d_row_weight, float* d_out,
                                void* d_workspace, size_t workspace_bytes, int* d_error_flag,
                                bool xq_ready, int max_seg_rows, cudaStream_t stream,
-                               WispErrCtx* err) {
+                               WispErrCtx* err, bool plans_ready) {
   if (!cfg || !d_prepared || !d_experts || !d_segs || !d_xp || !d_h || !d_out || !d_workspace ||
       n_entries <= 0)
     return WB_FAIL(WISP_ERR_INVALID_ARG, "grouped_ffn: null pointer argument");
@@ -1516,7 +1483,8 @@ WispError wb::grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
   pa.tiles_dn = ws.tiles_dn;
   pa.units_gu = ws.units_gu;
   pa.units_dn = ws.units_dn;
-  wb::launch_k(plan_all_kernel, 4, 1024, 0, stream, pa);
+  // (the decode planner has written the register path's plans already)
+  if (!plans_ready) wb::launch_k(plan_all_kernel, 4, 1024, 0, stream, pa);
   if (sk_rows > 0 && !xq_ready)
     wb::launch_k(quant_rows_kernel, dim3(n_segs, sk_rows), 128, 0, stream, d_segs, sk_rows,
                  reinterpret_cast<const __half*>(d_xp), M, ws.xq);

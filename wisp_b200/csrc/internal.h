@@ -27,6 +27,17 @@ inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, siz
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// The register path's unit plans of one grouped call, as the decode planner
+// (route.cu) writes them in place of the grouped call's own planner
+// (grouped.cu): the plan arrays in the call's workspace and the numbers that
+// shape them.
+struct DecodeUnits {
+  int32_t* units_gu;
+  int32_t* units_dn;
+  uint8_t* xq;   // q16 input rows in the same workspace
+  int per_gu, per_dn, cols, sk_rows, ks_dn, nk_dn, target;
+};
+
 // Fill a WispErrCtx the way the reference's WISP_ERR_SET does
 // (csrc/core/wisp_engine.h:66-72) and return the code.
 inline WispError set_err(WispErrCtx* err, WispError code, const char* file, int line,

@@ -3,9 +3,14 @@
 //
 // wisp_b200_moe_forward runs, on one stream and without any host sync:
 //   route (logits + top-k) -> dispatch plan (segments, row -> token map)
-//   -> pack rows (bf16 -> fp16 interleaved) -> zero out
-//   -> grouped gate/up + SwiGLU (tcgen05) -> grouped down + weighted
-//      scatter-combine (tcgen05, fp32 atomics into out).
+//   -> pack rows (q16 rows for register-path segments, fp16 interleaved
+//      rows for tensor-core ones) -> zero out
+//   -> grouped gate/up + SwiGLU -> grouped down + weighted scatter-combine
+//      (fp32 atomics into out), each on the register-path kernel for
+//      segments of up to 32 rows and on the tcgen05 kernel for larger ones.
+// Decode batches of at most 4 tokens take a shorter chain: router logits,
+// one planner launch (top-k, plan, q16 rows, zeroing, unit plans), then the
+// register-path gate/up and down launches.
 // It is the batched counterpart of run_moe (csrc/core/wisp_engine.c:
 // 1563-1674), which the reference can only run one token at a time.
 #include <algorithm>
@@ -34,7 +39,17 @@ WispError grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
                            const uint16_t* d_xp, uint16_t* d_h, int mode, const int* d_row_token,
                            const float* d_row_weight, float* d_out, void* d_workspace,
                            size_t workspace_bytes, int* d_error_flag, bool xq_ready,
-                           int max_seg_rows, cudaStream_t stream, WispErrCtx* err);
+                           int max_seg_rows, cudaStream_t stream, WispErrCtx* err,
+                           bool plans_ready = false);
+void decode_units(const WispMoeConfig* cfg, int n_segs, int n_entries, int rows_capacity, int mode,
+                  void* d_workspace, DecodeUnits* du);
+WispError launch_router_gemv(const WispMoeConfig* c, const uint16_t* x, const uint16_t* W,
+                             float* logits, cudaStream_t st, WispErrCtx* err);
+bool decode_plan_fits(const WispMoeConfig* c, int sk_rows);
+WispError launch_decode_plan(const WispMoeConfig* c, const float* logits, const float* bias,
+                             int* idx, float* w, int* counts, WispSegment* segs, int* row_token,
+                             float* row_weight, const uint16_t* x, float* out, int* error_flag,
+                             const DecodeUnits& du, cudaStream_t st, WispErrCtx* err);
 }  // namespace wb
 
 namespace {
@@ -151,6 +166,26 @@ extern "C" WispError wisp_b200_moe_forward(const WispMoeConfig* cfg, const WispM
   int* idx = d_topk_idx ? d_topk_idx : ws.idx;
   float* wt = d_topk_w ? d_topk_w : ws.w;
   const int V = cfg->n_experts + (cfg->has_shared ? 1 : 0);
+  if (!w->experts) return WB_FAIL(WISP_ERR_INVALID_ARG, "moe_forward: null expert table");
+
+  // Decode batches (T <= 4): router logits, then one planner launch for
+  // top-k, dispatch plan, q16 rows, output zeroing and the register path's
+  // unit plans, then the register-path gate/up and down launches.
+  if (wb::decode_plan_fits(cfg, wb::grouped_sk_rows(V, V))) {
+    // ws.part holds splits * T * E floats, splits >= 1: room for the logits
+    e = wb::launch_router_gemv(cfg, d_x, w->router_w, ws.part, stream, err);
+    if (e != WISP_OK) return e;
+    wb::DecodeUnits du;
+    wb::decode_units(cfg, V, V, ws.rows, 0, ws.grouped, &du);
+    e = wb::launch_decode_plan(cfg, ws.part, w->router_bias, idx, wt, ws.counts, ws.segs,
+                               ws.row_token, ws.row_weight, d_x, d_out, ws.error_flag, du, stream,
+                               err);
+    if (e != WISP_OK) return e;
+    return wb::grouped_ffn_impl(cfg, w->prepared, w->experts, V, ws.segs, V, ws.rows, ws.xp, ws.h,
+                                0, ws.row_token, ws.row_weight, d_out, ws.grouped,
+                                ws.grouped_bytes, ws.error_flag, true, cfg->tokens, stream, err,
+                                true);
+  }
 
   e = wb::launch_route(cfg, d_x, w->router_w, w->router_bias, ws.part, ws.splits, nullptr, idx, wt,
                        stream, err);
@@ -166,7 +201,6 @@ extern "C" WispError wisp_b200_moe_forward(const WispMoeConfig* cfg, const WispM
   if (e != WISP_OK) return e;
   WB_CUDA_CHECK(cudaMemsetAsync(d_out, 0, (size_t)cfg->tokens * cfg->hidden * sizeof(float), stream));
   WB_CUDA_CHECK(cudaMemsetAsync(ws.error_flag, 0, sizeof(int), stream));
-  if (!w->experts) return WB_FAIL(WISP_ERR_INVALID_ARG, "moe_forward: null expert table");
   // A routed expert gets at most one row per token and the shared expert T
   // rows, so no segment exceeds T rows.
   return wb::grouped_ffn_impl(cfg, w->prepared, w->experts, V, ws.segs, V, ws.rows, ws.xp, ws.h, 0,

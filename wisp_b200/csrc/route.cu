@@ -36,6 +36,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "plan.cuh"
 #include "skinny.h"
 
 using namespace wb;
@@ -314,14 +315,13 @@ __device__ __forceinline__ int pad32(int e) { return e + (e >> 5); }
 
 // One warp per token; lane l holds experts l + 32 j for j < PER (E <= 32 PER).
 // Writes idx/w [T x k] and, optionally, the fp32 logits.
+// The routing of token t by one warp (warp index < 8 inside its block).
 template <int PER>
-__global__ void topk_kernel(const float* __restrict__ part, int splits, const float* __restrict__ bias,
-                            int T, int E, int k, int scoring, int n_groups, int topk_groups,
-                            float scaling, int* __restrict__ idx, float* __restrict__ wout,
-                            float* __restrict__ logits_out) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * (blockDim.x >> 5) + warp;
-  if (t >= T) return;
+__device__ __forceinline__ void topk_token(const float* __restrict__ part, int splits,
+                                           const float* __restrict__ bias, int T, int t, int E,
+                                           int k, int scoring, int n_groups, int topk_groups,
+                                           float scaling, int* idx, float* wout,
+                                           float* logits_out, int warp, int lane) {
   const int per = (E + 31) / 32;
   float v[PER];
 #pragma unroll
@@ -460,6 +460,18 @@ __global__ void topk_kernel(const float* __restrict__ part, int splits, const fl
       wout[(size_t)t * k + lane] = myw / ssum * scaling;
     }
   }
+}
+
+template <int PER>
+__global__ void topk_kernel(const float* __restrict__ part, int splits, const float* __restrict__ bias,
+                            int T, int E, int k, int scoring, int n_groups, int topk_groups,
+                            float scaling, int* __restrict__ idx, float* __restrict__ wout,
+                            float* __restrict__ logits_out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (t >= T) return;
+  topk_token<PER>(part, splits, bias, T, t, E, k, scoring, n_groups, topk_groups, scaling, idx,
+                  wout, logits_out, warp, lane);
 }
 
 // One block of kPlanWarps warps per expert v: warp w scans the w-th
@@ -839,6 +851,192 @@ __global__ void __launch_bounds__(128) pack_rows_q16_kernel(const uint16_t* __re
   }
 }
 
+// ---------------------------------------------------------------------------
+// Decode planner: for a batch of at most kGemvMaxT tokens, everything between
+// the router logits and the register-path FFN in one block of 1024 threads
+// (the separate path takes six launches and two memsets for the same work,
+// each a few microseconds of fixed cost at batch 1):
+//   1. top-k of every token (one warp per token, the same code as
+//      topk_kernel); the other warps zero the output rows and the error word;
+//   2. per-expert counts and segments (a block scan over the V experts), the
+//      shared expert holding every token;
+//   3. the rows: slot s of expert e lands at begin[e] + (earlier slots of e),
+//      so each expert's rows are in token order, as in the general plan;
+//   4. every row as a q16 row (one half-warp per 128-K block);
+//   5. the register path's unit plans for gate/up and down.
+// Every segment has at most T <= 4 rows, so all of them run on the register
+// path and no fp16 rows or tensor-core plans are needed.
+// ---------------------------------------------------------------------------
+struct DecodePlan {
+  const float* logits;   // [T x E] from router_gemv_kernel (no bias)
+  const float* bias;
+  int T, E, k, scoring, n_groups, topk_groups;
+  float scaling;
+  int V;                 // E, + 1 with a shared expert
+  int* idx;
+  float* w;
+  int* counts;
+  WispSegment* segs;
+  int* row_token;
+  float* row_weight;
+  const uint16_t* x;
+  int M;
+  uint8_t* xq;
+  float* out;
+  int* error_flag;
+  int32_t* units_gu;
+  int32_t* units_dn;
+  int per_gu, per_dn, cols, sk_rows, ks_dn, nk_dn, target;
+};
+
+constexpr int kDecodeMaxSlots = kGemvMaxT * 32;         // tokens x top_k (k <= 32)
+constexpr int kDecodeMaxRows = kDecodeMaxSlots + kGemvMaxT;
+
+template <int PER>
+__global__ void __launch_bounds__(1024) decode_plan_kernel(const DecodePlan p) {
+  __shared__ int s_idx[kDecodeMaxSlots];
+  __shared__ int s_begin[kPlanMaxV];
+  __shared__ int s_tok[kDecodeMaxRows];
+  __shared__ int warp_tot[32];
+  __shared__ int carry;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int T = p.T, k = p.k, E = p.E, V = p.V, M = p.M, nslots = T * k;
+  if (warp < T) {
+    topk_token<PER>(p.logits, 1, p.bias, T, warp, E, k, p.scoring, p.n_groups, p.topk_groups,
+                    p.scaling, p.idx, p.w, nullptr, warp, lane);
+  } else {
+    for (int i = tid - 32 * T; i < T * M; i += blockDim.x - 32 * T) p.out[i] = 0.f;
+    if (tid == blockDim.x - 1) *p.error_flag = 0;
+  }
+  if (tid == 0) carry = 0;
+  __syncthreads();
+  for (int s = tid; s < nslots; s += blockDim.x) {
+    const int e = p.idx[s];
+    s_idx[s] = (e >= 0 && e < E) ? e : -1;
+  }
+  __syncthreads();
+  // counts and segments
+  for (int base = 0; base < V; base += blockDim.x) {
+    const int v = base + tid;
+    int n = 0;
+    if (v < E) {
+      for (int q = 0; q < nslots; q++) n += s_idx[q] == v;
+    } else if (v < V) {
+      n = T;
+    }
+    int xs = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, xs, o);
+      if (lane >= o) xs += y;
+    }
+    if (lane == 31) warp_tot[warp] = xs;
+    __syncthreads();
+    if (warp == 0) {
+      int tv = lane < (int)(blockDim.x >> 5) ? warp_tot[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, tv, o);
+        if (lane >= o) tv += y;
+      }
+      warp_tot[lane] = tv;
+    }
+    __syncthreads();
+    const int incl = xs + (warp > 0 ? warp_tot[warp - 1] : 0) + carry;
+    if (v < V) {
+      WispSegment sg;
+      sg.expert = v;
+      sg.row_begin = incl - n;
+      sg.rows = n;
+      sg.reserved = 0;
+      p.segs[v] = sg;
+      p.counts[v] = n;
+      s_begin[v] = incl - n;
+    }
+    __syncthreads();
+    if (tid == blockDim.x - 1) carry = incl;
+    __syncthreads();
+  }
+  const int rows = carry;
+  // rows in token order within each expert
+  for (int s = tid; s < nslots; s += blockDim.x) {
+    const int e = s_idx[s];
+    if (e < 0) continue;
+    int r = 0;
+    for (int q = 0; q < s; q++) r += s_idx[q] == e;
+    const int pos = s_begin[e] + r;
+    p.row_token[pos] = s / k;
+    p.row_weight[pos] = p.w[s];
+    s_tok[pos] = s / k;
+  }
+  if (V > E) {
+    for (int t = tid; t < T; t += blockDim.x) {
+      const int pos = s_begin[E] + t;
+      p.row_token[pos] = t;
+      p.row_weight[pos] = 1.f;
+      s_tok[pos] = t;
+    }
+  }
+  __syncthreads();
+  // q16 rows: half-warp h of warp w takes (row, 128-K block) tasks 2w + h,
+  // 2w + h + 64, ...; both halves of a warp run the same number of rounds
+  // (the shuffles span the warp).
+  const int nblk = M / kQ16Block, ntask = rows * nblk, half = (lane >> 4) & 1, hl = lane & 15;
+  for (int base = 2 * warp; base < ntask; base += 2 * (blockDim.x >> 5)) {
+    const int task = base + half;
+    const bool valid = task < ntask;
+    const int row = valid ? task / nblk : 0, b = valid ? task % nblk : 0;
+    const int wd = b * (kQ16Block / 8) + hl;   // packed word: K 8 wd .. 8 wd + 7
+    float f[8];
+    if (valid) {
+      const uint4 v = *reinterpret_cast<const uint4*>(p.x + (size_t)s_tok[row] * M + 8 * wd);
+      const uint32_t a[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        f[2 * j] = bf16f((uint16_t)(a[j] & 0xffff));
+        f[2 * j + 1] = bf16f((uint16_t)(a[j] >> 16));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; j++) f[j] = 0.f;
+    }
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) m = fmaxf(m, fabsf(f[j]));
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float inv = m > 0.f ? 32767.f / m : 0.f;
+    int v[8], sum = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      v[j] = max(-32767, min(32767, __float2int_rn(f[j] * inv)));
+      sum += v[j];
+    }
+    auto hi = [](int q) { return (uint32_t)((q >> 8) & 0xFF); };
+    auto lo = [](int q) { return (uint32_t)(q & 0xFF); };
+    const uint4 chunk = make_uint4(hi(v[0]) | hi(v[2]) << 8 | hi(v[4]) << 16 | hi(v[6]) << 24,
+                                   hi(v[1]) | hi(v[3]) << 8 | hi(v[5]) << 16 | hi(v[7]) << 24,
+                                   lo(v[0]) | lo(v[2]) << 8 | lo(v[4]) << 16 | lo(v[6]) << 24,
+                                   lo(v[1]) | lo(v[3]) << 8 | lo(v[5]) << 16 | lo(v[7]) << 24);
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const int sum1 = __shfl_sync(0xffffffffu, sum, (lane & 16) | 8);
+    if (valid) {
+      uint8_t* qrow = p.xq + (size_t)row * q16_row_bytes(M);
+      *reinterpret_cast<uint4*>(qrow + q16_word_offset(wd)) = chunk;
+      if (hl == 0) {
+        const float sc = m / 32767.f;
+        *reinterpret_cast<float4*>(qrow + q16_meta_offset(b)) =
+            make_float4(sc * 0.0625f, sc * (float)sum, sc * (float)sum1, 0.f);
+      }
+    }
+  }
+  __syncthreads();
+  plan_units(p.segs, V, p.per_gu, p.cols, p.sk_rows, 1, 1, 0, p.units_gu);
+  __syncthreads();
+  plan_units(p.segs, V, p.per_dn, p.cols, p.sk_rows, p.ks_dn, p.nk_dn, p.target, p.units_dn);
+}
+
 // y[t] = bf16(x[t] / rms(x[t])): per-token RMS normalisation (no weight)
 // between stacked MoE layers. One block per token.
 __global__ void rms_rescale_kernel(const float* __restrict__ x, uint16_t* __restrict__ y, int M,
@@ -962,6 +1160,69 @@ WispError launch_pack_q16(const uint16_t* x, const int* src, int n_rows, int M, 
   if (n_rows <= 0) return WISP_OK;
   wb::launch_k(pack_rows_q16_kernel, n_rows, 128, 0, st, x, src, n_rows, M, xp, xq, segs, nseg,
                sk_rows);
+  WB_CUDA_CHECK(cudaGetLastError());
+  return WISP_OK;
+}
+
+WispError launch_router_gemv(const WispMoeConfig* c, const uint16_t* x, const uint16_t* W,
+                             float* logits, cudaStream_t st, WispErrCtx* err) {
+  const int g = (c->n_experts + 1) / 2;
+  if (c->router_fp16)
+    wb::launch_k(router_gemv_kernel<true>, g, 256, 0, st, x, W, logits, c->tokens, c->n_experts,
+                 c->hidden);
+  else
+    wb::launch_k(router_gemv_kernel<false>, g, 256, 0, st, x, W, logits, c->tokens, c->n_experts,
+                 c->hidden);
+  WB_CUDA_CHECK(cudaGetLastError());
+  return WISP_OK;
+}
+
+bool decode_plan_fits(const WispMoeConfig* c, int sk_rows) {
+  const int V = c->n_experts + (c->has_shared ? 1 : 0);
+  return c->tokens >= 1 && c->tokens <= kGemvMaxT && c->tokens <= sk_rows && V <= kPlanMaxV &&
+         c->top_k <= 32 && c->n_experts <= 1024;
+}
+
+WispError launch_decode_plan(const WispMoeConfig* c, const float* logits, const float* bias,
+                             int* idx, float* w, int* counts, WispSegment* segs, int* row_token,
+                             float* row_weight, const uint16_t* x, float* out, int* error_flag,
+                             const DecodeUnits& du, cudaStream_t st, WispErrCtx* err) {
+  DecodePlan p;
+  p.logits = logits;
+  p.bias = bias;
+  p.T = c->tokens;
+  p.E = c->n_experts;
+  p.k = c->top_k;
+  p.scoring = c->scoring;
+  p.n_groups = c->n_groups;
+  p.topk_groups = c->topk_groups;
+  p.scaling = c->routed_scaling;
+  p.V = c->n_experts + (c->has_shared ? 1 : 0);
+  p.idx = idx;
+  p.w = w;
+  p.counts = counts;
+  p.segs = segs;
+  p.row_token = row_token;
+  p.row_weight = row_weight;
+  p.x = x;
+  p.M = c->hidden;
+  p.xq = du.xq;
+  p.out = out;
+  p.error_flag = error_flag;
+  p.units_gu = du.units_gu;
+  p.units_dn = du.units_dn;
+  p.per_gu = du.per_gu;
+  p.per_dn = du.per_dn;
+  p.cols = du.cols;
+  p.sk_rows = du.sk_rows;
+  p.ks_dn = du.ks_dn;
+  p.nk_dn = du.nk_dn;
+  p.target = du.target;
+  const int E = c->n_experts;
+  auto kern = E <= 32 ? decode_plan_kernel<1> : E <= 64 ? decode_plan_kernel<2>
+            : E <= 128 ? decode_plan_kernel<4> : E <= 256 ? decode_plan_kernel<8>
+            : E <= 512 ? decode_plan_kernel<16> : decode_plan_kernel<32>;
+  wb::launch_k(kern, 1, 1024, 0, st, p);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
