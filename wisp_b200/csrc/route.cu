@@ -309,19 +309,15 @@ __device__ __forceinline__ void warp_argmax(float& v, int& i) {
   }
 }
 
-// Shared-memory index of expert e in a warp's score row: one pad word per 32
-// so that lanes scanning different groups hit different banks.
-__device__ __forceinline__ int pad32(int e) { return e + (e >> 5); }
-
-// One warp per token; lane l holds experts l + 32 j for j < PER (E <= 32 PER).
-// Writes idx/w [T x k] and, optionally, the fp32 logits.
-// The routing of token t by one warp (warp index < 8 inside its block).
+// The routing of token t by one warp; lane l holds experts l + 32 j for
+// j < PER (E <= 32 PER). Writes idx/w [T x k] (global or shared memory) and,
+// optionally, the fp32 logits.
 template <int PER>
 __device__ __forceinline__ void topk_token(const float* __restrict__ part, int splits,
                                            const float* __restrict__ bias, int T, int t, int E,
                                            int k, int scoring, int n_groups, int topk_groups,
                                            float scaling, int* idx, float* wout,
-                                           float* logits_out, int warp, int lane) {
+                                           float* logits_out, int lane) {
   const int per = (E + 31) / 32;
   float v[PER];
 #pragma unroll
@@ -399,26 +395,31 @@ __device__ __forceinline__ void topk_token(const float* __restrict__ part, int s
 #pragma unroll
     for (int j = 0; j < PER; j++)
       if (j < per && lane + 32 * j < E) v[j] = 1.f / (1.f + expf(-v[j]));
-    // Group scores: lane g scans its group through shared memory.
-    __shared__ float sval[8][1024 + 32];
-    float* mys = sval[warp];
+    // Group scores, in registers: per group, every lane's top two of its
+    // experts in the group, then a warp-wide top-2 merge; lane g keeps group
+    // g's score (the sum of its two largest scores, ties counted twice).
+    int gid[PER];
 #pragma unroll
-    for (int j = 0; j < PER; j++)
-      if (j < per && lane + 32 * j < E) mys[pad32(lane + 32 * j)] = v[j];
-    __syncwarp();
+    for (int j = 0; j < PER; j++) gid[j] = (j < per && lane + 32 * j < E) ? (lane + 32 * j) / gsz : -1;
     float gscore = -INFINITY;
-    if (lane < n_groups) {
+    for (int g = 0; g < n_groups; g++) {
       float a = -INFINITY, b = -INFINITY;
-      for (int q = 0; q < gsz; q++) {
-        const float s = mys[pad32(lane * gsz + q)];
-        if (s > a) {
-          b = a;
-          a = s;
-        } else if (s > b) {
-          b = s;
+#pragma unroll
+      for (int j = 0; j < PER; j++) {
+        if (gid[j] == g) {
+          const float s = v[j];
+          b = fmaxf(b, fminf(a, s));
+          a = fmaxf(a, s);
         }
       }
-      gscore = a + (gsz > 1 ? b : 0.f);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float oa = __shfl_xor_sync(0xffffffffu, a, o);
+        const float ob = __shfl_xor_sync(0xffffffffu, b, o);
+        b = fmaxf(fminf(a, oa), fmaxf(b, ob));
+        a = fmaxf(a, oa);
+      }
+      if (lane == g) gscore = a + (gsz > 1 ? b : 0.f);
     }
     bool gsel = false;  // lane g: is group g kept
     for (int r = 0; r < topk_groups; r++) {
@@ -471,7 +472,7 @@ __global__ void topk_kernel(const float* __restrict__ part, int splits, const fl
   const int t = blockIdx.x * (blockDim.x >> 5) + warp;
   if (t >= T) return;
   topk_token<PER>(part, splits, bias, T, t, E, k, scoring, n_groups, topk_groups, scaling, idx,
-                  wout, logits_out, warp, lane);
+                  wout, logits_out, lane);
 }
 
 // One block of kPlanWarps warps per expert v: warp w scans the w-th
@@ -854,16 +855,21 @@ __global__ void __launch_bounds__(128) pack_rows_q16_kernel(const uint16_t* __re
 // ---------------------------------------------------------------------------
 // Decode planner: for a batch of at most kGemvMaxT tokens, everything between
 // the router logits and the register-path FFN in one block of 1024 threads
-// (the separate path takes six launches and two memsets for the same work,
-// each a few microseconds of fixed cost at batch 1):
-//   1. top-k of every token (one warp per token, the same code as
-//      topk_kernel); the other warps zero the output rows and the error word;
+// (the general path takes six launches and two memsets for the same work,
+// each a few microseconds of fixed cost at batch 1). Apart from the logits
+// and the token rows, which are read at the start, it works in shared memory:
+//   1. warps 0..T-1: top-k of their token (the code of topk_kernel) into
+//      shared memory; the other warps meanwhile quantise the T token rows to
+//      q16 rows in (dynamic) shared memory -- a row's q16 form depends only
+//      on its token -- and zero the output rows and the error word;
 //   2. per-expert counts and segments (a block scan over the V experts), the
 //      shared expert holding every token;
 //   3. the rows: slot s of expert e lands at begin[e] + (earlier slots of e),
 //      so each expert's rows are in token order, as in the general plan;
-//   4. every row as a q16 row (one half-warp per 128-K block);
-//   5. the register path's unit plans for gate/up and down.
+//   4. every row's q16 row copied from its token's (coalesced 16-byte
+//      stores);
+//   5. the register path's unit plans for gate/up and down, from the
+//      segments in shared memory.
 // Every segment has at most T <= 4 rows, so all of them run on the register
 // path and no fp16 rows or tensor-core plans are needed.
 // ---------------------------------------------------------------------------
@@ -892,30 +898,97 @@ struct DecodePlan {
 constexpr int kDecodeMaxSlots = kGemvMaxT * 32;         // tokens x top_k (k <= 32)
 constexpr int kDecodeMaxRows = kDecodeMaxSlots + kGemvMaxT;
 
+// Quantises one 128-K block of a bf16 row to q16 (layout in skinny.h) with
+// a half-warp: lane hl of the half owns packed word 16 b + hl. All 32 lanes
+// of the warp call it together; `valid` false contributes zeros and stores
+// nothing.
+__device__ __forceinline__ void q16_block(const uint16_t* __restrict__ xr, int b, bool valid,
+                                          int lane, uint8_t* qrow) {
+  const int hl = lane & 15;
+  const int wd = b * (kQ16Block / 8) + hl;
+  float f[8];
+  if (valid) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(xr + 8 * wd));
+    const uint32_t a[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      f[2 * j] = bf16f((uint16_t)(a[j] & 0xffff));
+      f[2 * j + 1] = bf16f((uint16_t)(a[j] >> 16));
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; j++) f[j] = 0.f;
+  }
+  float m = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; j++) m = fmaxf(m, fabsf(f[j]));
+#pragma unroll
+  for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const float inv = m > 0.f ? 32767.f / m : 0.f;
+  int v[8], sum = 0;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    v[j] = max(-32767, min(32767, __float2int_rn(f[j] * inv)));
+    sum += v[j];
+  }
+  auto hi = [](int q) { return (uint32_t)((q >> 8) & 0xFF); };
+  auto lo = [](int q) { return (uint32_t)(q & 0xFF); };
+  const uint4 chunk = make_uint4(hi(v[0]) | hi(v[2]) << 8 | hi(v[4]) << 16 | hi(v[6]) << 24,
+                                 hi(v[1]) | hi(v[3]) << 8 | hi(v[5]) << 16 | hi(v[7]) << 24,
+                                 lo(v[0]) | lo(v[2]) << 8 | lo(v[4]) << 16 | lo(v[6]) << 24,
+                                 lo(v[1]) | lo(v[3]) << 8 | lo(v[5]) << 16 | lo(v[7]) << 24);
+  // sums over the block's K 0-63 (its first 8 lanes) and 64-127
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const int sum1 = __shfl_sync(0xffffffffu, sum, (lane & 16) | 8);
+  if (valid) {
+    *reinterpret_cast<uint4*>(qrow + q16_word_offset(wd)) = chunk;
+    if (hl == 0) {
+      const float sc = m / 32767.f;
+      *reinterpret_cast<float4*>(qrow + q16_meta_offset(b)) =
+          make_float4(sc * 0.0625f, sc * (float)sum, sc * (float)sum1, 0.f);
+    }
+  }
+}
+
 template <int PER>
 __global__ void __launch_bounds__(1024) decode_plan_kernel(const DecodePlan p) {
+  extern __shared__ __align__(16) uint8_t s_q16[];   // T q16 token rows
   __shared__ int s_idx[kDecodeMaxSlots];
-  __shared__ int s_begin[kPlanMaxV];
+  __shared__ float s_w[kDecodeMaxSlots];
+  __shared__ WispSegment s_segs[kPlanMaxV];
   __shared__ int s_tok[kDecodeMaxRows];
   __shared__ int warp_tot[32];
   __shared__ int carry;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarp = blockDim.x >> 5;
   const int T = p.T, k = p.k, E = p.E, V = p.V, M = p.M, nslots = T * k;
+  const size_t qbytes = q16_row_bytes(M);
+  const int nblk = M / kQ16Block;
+  // 1. routing | token rows to q16, output zeroed
   if (warp < T) {
     topk_token<PER>(p.logits, 1, p.bias, T, warp, E, k, p.scoring, p.n_groups, p.topk_groups,
-                    p.scaling, p.idx, p.w, nullptr, warp, lane);
+                    p.scaling, s_idx, s_w, nullptr, lane);
   } else {
+    const int ntask = T * nblk, half = (lane >> 4) & 1;
+    // warp-uniform rounds: both halves of a warp run the same number
+    for (int base = 2 * (warp - T); base < ntask; base += 2 * (nwarp - T)) {
+      const int task = base + half;
+      const bool valid = task < ntask;
+      const int t = valid ? task / nblk : 0;
+      q16_block(p.x + (size_t)t * M, valid ? task % nblk : 0, valid, lane, s_q16 + t * qbytes);
+    }
     for (int i = tid - 32 * T; i < T * M; i += blockDim.x - 32 * T) p.out[i] = 0.f;
     if (tid == blockDim.x - 1) *p.error_flag = 0;
   }
   if (tid == 0) carry = 0;
   __syncthreads();
   for (int s = tid; s < nslots; s += blockDim.x) {
-    const int e = p.idx[s];
-    s_idx[s] = (e >= 0 && e < E) ? e : -1;
+    p.idx[s] = s_idx[s];
+    p.w[s] = s_w[s];
+    if (s_idx[s] < 0 || s_idx[s] >= E) s_idx[s] = -1;
   }
   __syncthreads();
-  // counts and segments
+  // 2. counts and segments
   for (int base = 0; base < V; base += blockDim.x) {
     const int v = base + tid;
     int n = 0;
@@ -933,7 +1006,7 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const DecodePlan p) {
     if (lane == 31) warp_tot[warp] = xs;
     __syncthreads();
     if (warp == 0) {
-      int tv = lane < (int)(blockDim.x >> 5) ? warp_tot[lane] : 0;
+      int tv = lane < nwarp ? warp_tot[lane] : 0;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int y = __shfl_up_sync(0xffffffffu, tv, o);
@@ -949,92 +1022,46 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const DecodePlan p) {
       sg.row_begin = incl - n;
       sg.rows = n;
       sg.reserved = 0;
+      s_segs[v] = sg;
       p.segs[v] = sg;
       p.counts[v] = n;
-      s_begin[v] = incl - n;
     }
     __syncthreads();
     if (tid == blockDim.x - 1) carry = incl;
     __syncthreads();
   }
   const int rows = carry;
-  // rows in token order within each expert
+  // 3. rows in token order within each expert
   for (int s = tid; s < nslots; s += blockDim.x) {
     const int e = s_idx[s];
     if (e < 0) continue;
     int r = 0;
     for (int q = 0; q < s; q++) r += s_idx[q] == e;
-    const int pos = s_begin[e] + r;
+    const int pos = s_segs[e].row_begin + r;
     p.row_token[pos] = s / k;
-    p.row_weight[pos] = p.w[s];
+    p.row_weight[pos] = s_w[s];
     s_tok[pos] = s / k;
   }
   if (V > E) {
     for (int t = tid; t < T; t += blockDim.x) {
-      const int pos = s_begin[E] + t;
+      const int pos = s_segs[E].row_begin + t;
       p.row_token[pos] = t;
       p.row_weight[pos] = 1.f;
       s_tok[pos] = t;
     }
   }
   __syncthreads();
-  // q16 rows: half-warp h of warp w takes (row, 128-K block) tasks 2w + h,
-  // 2w + h + 64, ...; both halves of a warp run the same number of rounds
-  // (the shuffles span the warp).
-  const int nblk = M / kQ16Block, ntask = rows * nblk, half = (lane >> 4) & 1, hl = lane & 15;
-  for (int base = 2 * warp; base < ntask; base += 2 * (blockDim.x >> 5)) {
-    const int task = base + half;
-    const bool valid = task < ntask;
-    const int row = valid ? task / nblk : 0, b = valid ? task % nblk : 0;
-    const int wd = b * (kQ16Block / 8) + hl;   // packed word: K 8 wd .. 8 wd + 7
-    float f[8];
-    if (valid) {
-      const uint4 v = *reinterpret_cast<const uint4*>(p.x + (size_t)s_tok[row] * M + 8 * wd);
-      const uint32_t a[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        f[2 * j] = bf16f((uint16_t)(a[j] & 0xffff));
-        f[2 * j + 1] = bf16f((uint16_t)(a[j] >> 16));
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; j++) f[j] = 0.f;
-    }
-    float m = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; j++) m = fmaxf(m, fabsf(f[j]));
-#pragma unroll
-    for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    const float inv = m > 0.f ? 32767.f / m : 0.f;
-    int v[8], sum = 0;
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-      v[j] = max(-32767, min(32767, __float2int_rn(f[j] * inv)));
-      sum += v[j];
-    }
-    auto hi = [](int q) { return (uint32_t)((q >> 8) & 0xFF); };
-    auto lo = [](int q) { return (uint32_t)(q & 0xFF); };
-    const uint4 chunk = make_uint4(hi(v[0]) | hi(v[2]) << 8 | hi(v[4]) << 16 | hi(v[6]) << 24,
-                                   hi(v[1]) | hi(v[3]) << 8 | hi(v[5]) << 16 | hi(v[7]) << 24,
-                                   lo(v[0]) | lo(v[2]) << 8 | lo(v[4]) << 16 | lo(v[6]) << 24,
-                                   lo(v[1]) | lo(v[3]) << 8 | lo(v[5]) << 16 | lo(v[7]) << 24);
-#pragma unroll
-    for (int o = 1; o < 8; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    const int sum1 = __shfl_sync(0xffffffffu, sum, (lane & 16) | 8);
-    if (valid) {
-      uint8_t* qrow = p.xq + (size_t)row * q16_row_bytes(M);
-      *reinterpret_cast<uint4*>(qrow + q16_word_offset(wd)) = chunk;
-      if (hl == 0) {
-        const float sc = m / 32767.f;
-        *reinterpret_cast<float4*>(qrow + q16_meta_offset(b)) =
-            make_float4(sc * 0.0625f, sc * (float)sum, sc * (float)sum1, 0.f);
-      }
-    }
+  // 4. each row's q16 row from its token's
+  const int wpr = (int)(qbytes / 16);   // 16-byte words per q16 row
+  for (int i = tid; i < rows * wpr; i += blockDim.x) {
+    const int row = i / wpr, wd = i - row * wpr;
+    reinterpret_cast<uint4*>(p.xq + (size_t)row * qbytes)[wd] =
+        reinterpret_cast<const uint4*>(s_q16 + (size_t)s_tok[row] * qbytes)[wd];
   }
+  // 5. unit plans (segments read from shared memory)
+  plan_units(s_segs, V, p.per_gu, p.cols, p.sk_rows, 1, 1, 0, p.units_gu);
   __syncthreads();
-  plan_units(p.segs, V, p.per_gu, p.cols, p.sk_rows, 1, 1, 0, p.units_gu);
-  __syncthreads();
-  plan_units(p.segs, V, p.per_dn, p.cols, p.sk_rows, p.ks_dn, p.nk_dn, p.target, p.units_dn);
+  plan_units(s_segs, V, p.per_dn, p.cols, p.sk_rows, p.ks_dn, p.nk_dn, p.target, p.units_dn);
 }
 
 // y[t] = bf16(x[t] / rms(x[t])): per-token RMS normalisation (no weight)
@@ -1177,10 +1204,16 @@ WispError launch_router_gemv(const WispMoeConfig* c, const uint16_t* x, const ui
   return WISP_OK;
 }
 
+// Dynamic shared memory of the decode planner: the T tokens' q16 rows.
+static size_t decode_plan_smem(const WispMoeConfig* c) {
+  return (size_t)c->tokens * q16_row_bytes(c->hidden);
+}
+
 bool decode_plan_fits(const WispMoeConfig* c, int sk_rows) {
   const int V = c->n_experts + (c->has_shared ? 1 : 0);
+  // the q16 token rows next to ~18 KB of static shared memory
   return c->tokens >= 1 && c->tokens <= kGemvMaxT && c->tokens <= sk_rows && V <= kPlanMaxV &&
-         c->top_k <= 32 && c->n_experts <= 1024;
+         c->top_k <= 32 && c->n_experts <= 1024 && decode_plan_smem(c) <= 160 * 1024;
 }
 
 WispError launch_decode_plan(const WispMoeConfig* c, const float* logits, const float* bias,
@@ -1222,7 +1255,9 @@ WispError launch_decode_plan(const WispMoeConfig* c, const float* logits, const 
   auto kern = E <= 32 ? decode_plan_kernel<1> : E <= 64 ? decode_plan_kernel<2>
             : E <= 128 ? decode_plan_kernel<4> : E <= 256 ? decode_plan_kernel<8>
             : E <= 512 ? decode_plan_kernel<16> : decode_plan_kernel<32>;
-  wb::launch_k(kern, 1, 1024, 0, st, p);
+  const size_t smem = decode_plan_smem(c);
+  WB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  wb::launch_k(kern, 1, 1024, smem, st, p);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
