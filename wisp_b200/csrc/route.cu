@@ -858,10 +858,12 @@ __global__ void __launch_bounds__(128) pack_rows_q16_kernel(const uint16_t* __re
 // (the general path takes six launches and two memsets for the same work,
 // each a few microseconds of fixed cost at batch 1). Apart from the logits
 // and the token rows, which are read at the start, it works in shared memory:
-//   1. warps 0..T-1: top-k of their token (the code of topk_kernel) into
-//      shared memory; the other warps meanwhile quantise the T token rows to
-//      q16 rows in (dynamic) shared memory -- a row's q16 form depends only
-//      on its token -- and zero the output rows and the error word;
+//   1. the routing into shared memory -- softmax: warps 0..T-1, one per
+//      token (the code of topk_kernel); sigmoid group-limited: the first 256
+//      threads together (route_sigmoid_block) -- while the other warps
+//      quantise the T token rows to q16 rows in (dynamic) shared memory (a
+//      row's q16 form depends only on its token) and zero the output rows
+//      and the error word;
 //   2. per-expert counts and segments (a block scan over the V experts), the
 //      shared expert holding every token;
 //   3. the rows: slot s of expert e lands at begin[e] + (earlier slots of e),
@@ -951,6 +953,93 @@ __device__ __forceinline__ void q16_block(const uint16_t* __restrict__ xr, int b
   }
 }
 
+// Sigmoid group-limited routing of T <= kGemvMaxT tokens by the first
+// kRouteThreads threads of the block (named barrier 1), in parallel instead
+// of one warp's serial rounds: scores, then one warp per (token, group) for
+// the group scores (sum of the top two), then ranks -- a group is kept when
+// fewer than topk_groups groups beat it, an expert in a kept group is picked
+// at position r when r experts of the kept groups beat it, where "beat"
+// means a higher score or an equal score at a lower index. That is exactly
+// the order of topk_token's rounds (largest first, lower index on a tie), so
+// indices and weights are identical to it.
+constexpr int kRouteThreads = 256;
+
+__device__ __forceinline__ void route_bar() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kRouteThreads) : "memory");
+}
+
+__device__ void route_sigmoid_block(const DecodePlan& p, float (*s_score)[1024],
+                                    float (*s_gscore)[32], uint32_t* s_gkeep, int* s_sel,
+                                    float* s_sels, int* s_idx, float* s_w) {
+  const int rt = threadIdx.x, lane = rt & 31, w = rt >> 5;
+  const int T = p.T, E = p.E, k = p.k, G = p.n_groups, gsz = E / G;
+  if (rt < T) s_gkeep[rt] = 0u;
+  for (int i = rt; i < T * E; i += kRouteThreads) {
+    const int t = i / E, e = i - t * E;
+    float v = p.logits[i];
+    if (p.bias) v += p.bias[e];
+    s_score[t][e] = 1.f / (1.f + expf(-v));
+  }
+  route_bar();
+  for (int pr = w; pr < T * G; pr += kRouteThreads / 32) {
+    const int t = pr / G, g = pr - t * G;
+    float a = -INFINITY, b = -INFINITY;
+    for (int q = lane; q < gsz; q += 32) {
+      const float v = s_score[t][g * gsz + q];
+      b = fmaxf(b, fminf(a, v));
+      a = fmaxf(a, v);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float oa = __shfl_xor_sync(0xffffffffu, a, o);
+      const float ob = __shfl_xor_sync(0xffffffffu, b, o);
+      b = fmaxf(fminf(a, oa), fmaxf(b, ob));
+      a = fmaxf(a, oa);
+    }
+    if (lane == 0) s_gscore[t][g] = a + (gsz > 1 ? b : 0.f);
+  }
+  route_bar();
+  for (int pr = rt; pr < T * G; pr += kRouteThreads) {
+    const int t = pr / G, g = pr - t * G;
+    const float gs = s_gscore[t][g];
+    int rank = 0;
+    for (int q = 0; q < G; q++) {
+      const float o = s_gscore[t][q];
+      rank += (o > gs) || (o == gs && q < g);
+    }
+    if (rank < p.topk_groups) atomicOr(&s_gkeep[t], 1u << g);
+  }
+  route_bar();
+  for (int i = rt; i < T * E; i += kRouteThreads) {
+    const int t = i / E, e = i - t * E;
+    const uint32_t keep = s_gkeep[t];
+    if (!((keep >> (e / gsz)) & 1u)) continue;
+    const float v = s_score[t][e];
+    int rank = 0;
+    for (uint32_t m = keep; m; m &= m - 1) {
+      const int g = __ffs(m) - 1;
+      const float* row = &s_score[t][g * gsz];
+      for (int q = 0; q < gsz; q++) {
+        const float o = row[q];
+        rank += (o > v) || (o == v && g * gsz + q < e);
+      }
+    }
+    if (rank < k) {
+      s_sel[t * 32 + rank] = e;
+      s_sels[t * 32 + rank] = v;
+    }
+  }
+  route_bar();
+  if (rt < T) {
+    float ssum = 0.f;
+    for (int r = 0; r < k; r++) ssum += s_sels[rt * 32 + r];
+    for (int r = 0; r < k; r++) {
+      s_idx[rt * k + r] = s_sel[rt * 32 + r];
+      s_w[rt * k + r] = s_sels[rt * 32 + r] / ssum * p.scaling;
+    }
+  }
+}
+
 template <int PER>
 __global__ void __launch_bounds__(1024) decode_plan_kernel(const DecodePlan p) {
   extern __shared__ __align__(16) uint8_t s_q16[];   // T q16 token rows
@@ -960,24 +1049,36 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const DecodePlan p) {
   __shared__ int s_tok[kDecodeMaxRows];
   __shared__ int warp_tot[32];
   __shared__ int carry;
+  // sigmoid routing
+  __shared__ float s_score[kGemvMaxT][1024];
+  __shared__ float s_gscore[kGemvMaxT][32];
+  __shared__ uint32_t s_gkeep[kGemvMaxT];
+  __shared__ int s_sel[kGemvMaxT * 32];
+  __shared__ float s_sels[kGemvMaxT * 32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarp = blockDim.x >> 5;
   const int T = p.T, k = p.k, E = p.E, V = p.V, M = p.M, nslots = T * k;
   const size_t qbytes = q16_row_bytes(M);
   const int nblk = M / kQ16Block;
-  // 1. routing | token rows to q16, output zeroed
-  if (warp < T) {
-    topk_token<PER>(p.logits, 1, p.bias, T, warp, E, k, p.scoring, p.n_groups, p.topk_groups,
-                    p.scaling, s_idx, s_w, nullptr, lane);
+  // 1. routing | token rows to q16, output zeroed. Softmax: one warp per
+  // token; sigmoid group-limited: the first 256 threads together.
+  const bool sigmoid = p.scoring == WISP_SCORE_SIGMOID_GROUPED;
+  const int nrw = sigmoid ? kRouteThreads / 32 : T;   // routing warps
+  if (warp < nrw) {
+    if (sigmoid)
+      route_sigmoid_block(p, s_score, s_gscore, s_gkeep, s_sel, s_sels, s_idx, s_w);
+    else
+      topk_token<PER>(p.logits, 1, p.bias, T, warp, E, k, p.scoring, p.n_groups, p.topk_groups,
+                      p.scaling, s_idx, s_w, nullptr, lane);
   } else {
     const int ntask = T * nblk, half = (lane >> 4) & 1;
     // warp-uniform rounds: both halves of a warp run the same number
-    for (int base = 2 * (warp - T); base < ntask; base += 2 * (nwarp - T)) {
+    for (int base = 2 * (warp - nrw); base < ntask; base += 2 * (nwarp - nrw)) {
       const int task = base + half;
       const bool valid = task < ntask;
       const int t = valid ? task / nblk : 0;
       q16_block(p.x + (size_t)t * M, valid ? task % nblk : 0, valid, lane, s_q16 + t * qbytes);
     }
-    for (int i = tid - 32 * T; i < T * M; i += blockDim.x - 32 * T) p.out[i] = 0.f;
+    for (int i = tid - 32 * nrw; i < T * M; i += blockDim.x - 32 * nrw) p.out[i] = 0.f;
     if (tid == blockDim.x - 1) *p.error_flag = 0;
   }
   if (tid == 0) carry = 0;
@@ -1053,10 +1154,10 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const DecodePlan p) {
   __syncthreads();
   // 4. each row's q16 row from its token's
   const int wpr = (int)(qbytes / 16);   // 16-byte words per q16 row
-  for (int i = tid; i < rows * wpr; i += blockDim.x) {
-    const int row = i / wpr, wd = i - row * wpr;
-    reinterpret_cast<uint4*>(p.xq + (size_t)row * qbytes)[wd] =
-        reinterpret_cast<const uint4*>(s_q16 + (size_t)s_tok[row] * qbytes)[wd];
+  for (int row = 0; row < rows; row++) {
+    const uint4* src = reinterpret_cast<const uint4*>(s_q16 + (size_t)s_tok[row] * qbytes);
+    uint4* dst = reinterpret_cast<uint4*>(p.xq + (size_t)row * qbytes);
+    for (int wd = tid; wd < wpr; wd += blockDim.x) dst[wd] = src[wd];
   }
   // 5. unit plans (segments read from shared memory)
   plan_units(s_segs, V, p.per_gu, p.cols, p.sk_rows, 1, 1, 0, p.units_gu);
@@ -1211,7 +1312,7 @@ static size_t decode_plan_smem(const WispMoeConfig* c) {
 
 bool decode_plan_fits(const WispMoeConfig* c, int sk_rows) {
   const int V = c->n_experts + (c->has_shared ? 1 : 0);
-  // the q16 token rows next to ~18 KB of static shared memory
+  // the q16 token rows next to ~36 KB of static shared memory
   return c->tokens >= 1 && c->tokens <= kGemvMaxT && c->tokens <= sk_rows && V <= kPlanMaxV &&
          c->top_k <= 32 && c->n_experts <= 1024 && decode_plan_smem(c) <= 160 * 1024;
 }
