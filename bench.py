@@ -200,6 +200,27 @@ def reference_arm(args, spec) -> None:
     print(json.dumps(line))
 
 
+def layer_launches(T: int, world: int, has_shared: bool) -> int:
+    """Our kernel launches per layer call (plus one rms_rescale between
+    stacked layers, counted by the caller).
+
+    Single GPU, T <= 4 tokens (decode chain): router logits, the decode
+    planner, register-path gate/up and down = 4. Otherwise: route 2 (logits,
+    top-k) + plan 2 (count and segments, ordered fill) + row pack 1 + grouped
+    FFN (one tile/unit planner, register-path gate/up and down, and, when a
+    segment can exceed the 32-row routing threshold, the tensor-core gate/up
+    and down). Expert-parallel: route 2 + plan 2 + dispatch 2 (slots and
+    entries, rows) + receive plan + gather + grouped FFN 5 + fp16 return rows +
+    combine, and for the shared expert pack 1 + grouped FFN 3 (5 above 32
+    tokens per rank)."""
+    if world == 1:
+        if T <= 4:
+            return 4
+        return 5 + (5 if T > 32 else 3)
+    shared = (1 + (5 if T > 32 else 3)) if has_shared else 0
+    return 2 + 2 + 2 + 1 + 1 + 5 + 1 + 1 + shared
+
+
 # ---------------------------------------------------------------------------
 # The other BASELINE configurations (single GPU): one layer per step
 # ---------------------------------------------------------------------------
@@ -304,6 +325,7 @@ def measure_side_config(name: str, steps: int, warmup: int, peaks: dict) -> dict
            "l2": "flushed between steps (256 MB write, untimed)",
            "cuda_graph": graph_note,
            "roofline": roof,
+           "gpu_launches": layer_launches(spec.tokens, 1, spec.has_shared) * steps,
            "e2e": {"value": round(spec.tokens / (ems / 1e3), 1), "unit": UNIT,
                    "h2d_bytes_per_step": x_host.numel() * 2,
                    "d2h_bytes_per_step": out_host.numel() * 4}}
@@ -668,14 +690,7 @@ def main() -> None:
            "h2d_bytes_per_step": x_host.numel() * 2 * world,
            "d2h_bytes_per_step": out_host.numel() * 4 * world}
 
-    # Our kernels per layer: route 2 (logits, top-k) + plan 2 (count and
-    # segments, ordered fill) + grouped FFN 5 (one tile/unit planner,
-    # register-path and tensor-core kernels for gate/up and down); single GPU:
-    # + pack 1; expert-parallel: + dispatch 2 (slots and entries, rows),
-    # receive-plan, gather, combine, and for the shared expert pack 1 +
-    # grouped 5. Plus one rms_rescale between layers.
-    per_layer = 10 if world == 1 else 14 + (6 if spec.has_shared else 0)
-    launches_per_step = per_layer * L + (L - 1)
+    launches_per_step = layer_launches(T, world, spec.has_shared) * L + (L - 1)
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),

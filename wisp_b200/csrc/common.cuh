@@ -16,6 +16,13 @@
 
 namespace wb {
 
+// Programmatic dependent launch (router -> decode planner): a kernel
+// launched with launch_k_pdl waits here before its first read of anything
+// the kernels before it write; pdl_trigger lets the next kernel's CTAs start
+// (both are no-ops for kernels launched in plain stream order).
+WB_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+WB_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------------------
 // int4 nibble -> fp16 conversion.
 //

@@ -27,6 +27,31 @@ inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, siz
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// The same launch as a programmatic dependent of the kernel before it on the
+// stream: its CTAs may start while that kernel is still running (once all of
+// that kernel's CTAs have started and triggered), and must execute
+// griddepcontrol.wait (wb::pdl_wait) before they read anything that kernel,
+// or any kernel before it, writes. Used for one edge only, router logits ->
+// decode planner in the single-GPU decode chain: measured on B200 (CUDA
+// graph, L2 flushed), making the gate/up kernel a dependent of the planner
+// cost Mixtral b1 6 us, and the down kernel a dependent of gate/up gained
+// nothing.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // The register path's unit plans of one grouped call, as the decode planner
 // (route.cu) writes them in place of the grouped call's own planner
 // (grouped.cu): the plan arrays in the call's workspace and the numbers that

@@ -242,6 +242,7 @@ __global__ void __launch_bounds__(256) router_gemv_kernel(const uint16_t* __rest
                                                           float* __restrict__ logits, int T, int E,
                                                           int M) {
   __shared__ float red[8][kGemvMaxT];
+  pdl_trigger();   // the decode planner may start; it waits for these logits
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.x * 2 + warp / kGemvQ, q = warp % kGemvQ;
   const int n8 = M / 8;
@@ -1059,11 +1060,16 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const DecodePlan p) {
   const int T = p.T, k = p.k, E = p.E, V = p.V, M = p.M, nslots = T * k;
   const size_t qbytes = q16_row_bytes(M);
   const int nblk = M / kQ16Block;
+  // Launched as a programmatic dependent of the router: the routing warps
+  // wait for the logits; the others only read the token rows, which the
+  // kernels before the router wrote, and write buffers the router does not
+  // touch.
   // 1. routing | token rows to q16, output zeroed. Softmax: one warp per
   // token; sigmoid group-limited: the first 256 threads together.
   const bool sigmoid = p.scoring == WISP_SCORE_SIGMOID_GROUPED;
   const int nrw = sigmoid ? kRouteThreads / 32 : T;   // routing warps
   if (warp < nrw) {
+    pdl_wait();
     if (sigmoid)
       route_sigmoid_block(p, s_score, s_gscore, s_gkeep, s_sel, s_sels, s_idx, s_w);
     else
@@ -1358,7 +1364,7 @@ WispError launch_decode_plan(const WispMoeConfig* c, const float* logits, const 
             : E <= 512 ? decode_plan_kernel<16> : decode_plan_kernel<32>;
   const size_t smem = decode_plan_smem(c);
   WB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  wb::launch_k(kern, 1, 1024, smem, st, p);
+  wb::launch_k_pdl(kern, 1, 1024, smem, st, p);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
