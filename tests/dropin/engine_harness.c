@@ -385,6 +385,9 @@ int eh_prefill_moe(EngineHarness* h, const float* x, int T, float* out, int* idx
     if ((rc = wisp_b200_check_error_flag(d_flag, st, &err))) goto done;
     rc = cudaMemcpy(out, d_out, (size_t)T * M * 4, cudaMemcpyDeviceToHost) ? WISP_ERR_CUDA : 0;
 done:
+    if (rc)   /* the failing step, for the test log */
+        fprintf(stderr, "eh_prefill_moe: error %d: %s (last CUDA error: %s)\n", rc, err.message,
+                cudaGetErrorString(cudaGetLastError()));
     cudaStreamSynchronize(st);
     free(xb);
     cudaFree(d_x); cudaFree(d_logits); cudaFree(d_idx); cudaFree(d_w); cudaFree(d_counts);

@@ -35,7 +35,10 @@ class CpuOps:
     def act_dtype(self):
         return torch.float64
 
-    def route(self, cfg, lw, x, idx, w, logits):
+    def route_scratch(self, cfg, device):
+        return torch.empty(1)
+
+    def route(self, cfg, lw, x, idx, w, scratch):
         from helpers import oracle_route
         i, ww, _ = oracle_route(self.orc, lw, x)
         idx.copy_(torch.from_numpy(i))

@@ -94,6 +94,9 @@ SIGNATURES = {
                                    _P, _P, _P, _SZ, _P, _E]),
     "wisp_b200_route": (_I, [C.POINTER(WispMoeConfig), C.POINTER(WispMoeWeights), _P, _P, _P,
                              _P, _P, _E]),
+    "wisp_b200_route_workspace_bytes": (_SZ, [C.POINTER(WispMoeConfig)]),
+    "wisp_b200_route_ws": (_I, [C.POINTER(WispMoeConfig), C.POINTER(WispMoeWeights), _P, _P, _P,
+                                _P, _P, _SZ, _P, _E]),
     "wisp_b200_grouped_workspace_bytes": (_SZ, [C.POINTER(WispMoeConfig), _I, _I]),
     "wisp_b200_grouped_ffn": (_I, [C.POINTER(WispMoeConfig), _P, _P, _I, _P, _I, _I, _P, _P, _I,
                                    _P, _P, _P, _P, _SZ, _P, _P, _E]),

@@ -172,10 +172,13 @@ __global__ void ep_pack_kernel(const uint16_t* __restrict__ x, int M, const int*
   }
 }
 
-// Single block. Gathered order: local expert, then source rank, then the
-// source's entry order. src_pos[j] = receive row (s * cap + block row) of
-// gathered row j, weight[j] its routing weight; counts and rows are clamped
-// to the block's capacity.
+// Single block of 1024 threads (world * e_loc <= 1024 chunks, chunk (s, e) =
+// the entries of local expert e in source block s). Gathered order: local
+// expert, then source rank, then the source's entry order. src_pos[j] =
+// receive row (s * cap + block row) of gathered row j, weight[j] its routing
+// weight; a source's entries are clamped to its block's capacity (cap * k)
+// in expert order. Two block scans give every chunk its source offset and
+// its gathered offset; warps then copy the chunks' entries.
 __global__ void __launch_bounds__(1024) ep_recv_plan_kernel(const uint8_t* __restrict__ recv,
                                                             int world, int e_loc, int k, Layout L,
                                                             WispSegment* __restrict__ segs,
@@ -184,51 +187,65 @@ __global__ void __launch_bounds__(1024) ep_recv_plan_kernel(const uint8_t* __res
                                                             int* __restrict__ total_out) {
   __shared__ int src_off[1024];  // [s][e]: first entry of the chunk in block s
   __shared__ int dst_off[1024];  // [s][e]: gathered position of the chunk
-  __shared__ int cnt[1024];
+  __shared__ int cnt[1024];      // [s][e]: entries of the chunk (clamped)
+  __shared__ int warp_tot[32];
   const int n = world * e_loc;
   const int max_ent = L.cap * k;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+  const int i = threadIdx.x;
+  // 1. counts, clamped per source: chunk (s, e) starts at min(sum of the
+  //    source's earlier counts, cap * k) and ends at min(that + its count,
+  //    cap * k) -- a scan over the source-major order minus the source's base
+  int c = 0;
+  if (i < n) {
     const int s = i / e_loc, e = i - s * e_loc;
-    const int c = reinterpret_cast<const int*>(recv + s * L.bytes + 16)[e];
-    cnt[i] = min(max(c, 0), max_ent);
+    c = min(max(reinterpret_cast<const int*>(recv + s * L.bytes + 16)[e], 0), max_ent);
   }
+  int tot;
+  const int ex = block_scan(c, warp_tot, &tot);   // exclusive, source-major
+  if (i < n) cnt[i] = ex;                          // staged: the prefix
   __syncthreads();
-  if (threadIdx.x < world) {  // prefix over the experts of one source
-    const int s = threadIdx.x;
-    int off = 0;
-    for (int e = 0; e < e_loc; e++) {
-      const int c = min(cnt[s * e_loc + e], max_ent - off);
-      cnt[s * e_loc + e] = c;
-      src_off[s * e_loc + e] = off;
-      off += c;
-    }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {  // gathered order
-    int off = 0;
-    for (int e = 0; e < e_loc; e++) {
-      WispSegment sg;
-      sg.expert = e;
-      sg.row_begin = off;
-      sg.reserved = 0;
-      for (int s = 0; s < world; s++) {
-        dst_off[s * e_loc + e] = off;
-        off += cnt[s * e_loc + e];
-      }
-      sg.rows = off - sg.row_begin;
-      segs[e] = sg;
-    }
-    *total_out = off;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+  if (i < n) {
     const int s = i / e_loc;
+    const int base = cnt[s * e_loc];               // the source's first prefix
+    const int b = min(ex - base, max_ent), e2 = min(ex - base + c, max_ent);
+    src_off[i] = b;
+    dst_off[i] = e2 - b;                           // staged: the clamped count
+  }
+  __syncthreads();
+  if (i < n) cnt[i] = dst_off[i];
+  __syncthreads();
+  // 2. gathered offsets: a scan over the expert-major order (e, s)
+  int ct = 0, s_t = 0, e_t = 0;
+  if (i < n) {
+    e_t = i / world;
+    s_t = i - e_t * world;
+    ct = cnt[s_t * e_loc + e_t];
+  }
+  const int ex2 = block_scan(ct, warp_tot, &tot);
+  if (i < n) dst_off[s_t * e_loc + e_t] = ex2;
+  if (i == 0) *total_out = tot;
+  __syncthreads();
+  if (i < e_loc) {
+    int rows = 0;
+    for (int s = 0; s < world; s++) rows += cnt[s * e_loc + i];
+    WispSegment sg;
+    sg.expert = i;
+    sg.row_begin = dst_off[i];   // source 0 of expert i
+    sg.rows = rows;
+    sg.reserved = 0;
+    segs[i] = sg;
+  }
+  // 3. the entries, one warp per chunk
+  const int warp = i >> 5, lane = i & 31;
+  for (int q = warp; q < n; q += blockDim.x >> 5) {
+    const int s = q / e_loc;
     const int* ent = reinterpret_cast<const int*>(recv + s * L.bytes + L.off_ent);
     const float* ew = reinterpret_cast<const float*>(recv + s * L.bytes + L.off_w);
-    for (int j = 0; j < cnt[i]; j++) {
-      const int row = ent[src_off[i] + j];
-      src_pos[dst_off[i] + j] = s * L.cap + min(max(row, 0), L.cap - 1);
-      weight[dst_off[i] + j] = ew[src_off[i] + j];
+    const int so = src_off[q], d = dst_off[q], m = cnt[q];
+    for (int j = lane; j < m; j += 32) {
+      const int row = ent[so + j];
+      src_pos[d + j] = s * L.cap + min(max(row, 0), L.cap - 1);
+      weight[d + j] = ew[so + j];
     }
   }
 }
@@ -255,7 +272,8 @@ __device__ __forceinline__ float4 load4(const __half* p) {
   return make_float4(a.x, a.y, b.x, b.y);
 }
 
-// One block per token: out[t] += yback[q * cap + slot[t][q]] for q = 0..world-1.
+// Block (t, c): out[t] += yback[q * cap + slot[t][q]] for q = 0..world-1 over
+// the c-th run of 1024 values of the row.
 template <typename T>
 __global__ void ep_combine_kernel(const T* __restrict__ y, const int* __restrict__ slot,
                                   int world, int cap, int M, float* __restrict__ out) {
@@ -264,7 +282,8 @@ __global__ void ep_combine_kernel(const T* __restrict__ y, const int* __restrict
   if (threadIdx.x < world) sl[threadIdx.x] = slot[(size_t)t * world + threadIdx.x];
   __syncthreads();
   float* orow = out + (size_t)t * M;
-  for (int i = threadIdx.x * 4; i < M; i += blockDim.x * 4) {
+  const int end = min(M, ((int)blockIdx.y + 1) * (int)blockDim.x * 4);
+  for (int i = blockIdx.y * blockDim.x * 4 + threadIdx.x * 4; i < end; i += blockDim.x * 4) {
     float4 acc = *reinterpret_cast<const float4*>(orow + i);
     for (int q = 0; q < world; q++) {
       if (sl[q] < 0) continue;
@@ -373,8 +392,8 @@ extern "C" WispError wisp_b200_ep_combine(const float* d_yback, const int* d_slo
     return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_combine: world=%d tokens=%d cap=%d hidden=%d", world,
                    tokens, cap, hidden);
   if (tokens == 0) return WISP_OK;
-  wb::launch_k(ep_combine_kernel<float>, tokens, 256, 0, stream, d_yback, d_slot, world, cap,
-               hidden, d_out);
+  wb::launch_k(ep_combine_kernel<float>, dim3(tokens, (hidden + 1023) / 1024), 256, 0, stream,
+               d_yback, d_slot, world, cap, hidden, d_out);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
@@ -389,7 +408,7 @@ extern "C" WispError wisp_b200_ep_combine_f16(const uint16_t* d_yback, const int
     return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_combine_f16: world=%d tokens=%d cap=%d hidden=%d",
                    world, tokens, cap, hidden);
   if (tokens == 0) return WISP_OK;
-  wb::launch_k(ep_combine_kernel<__half>, tokens, 256, 0, stream,
+  wb::launch_k(ep_combine_kernel<__half>, dim3(tokens, (hidden + 1023) / 1024), 256, 0, stream,
                reinterpret_cast<const __half*>(d_yback), d_slot, world, cap, hidden, d_out);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;

@@ -2,8 +2,9 @@
 //
 //   router_logits_kernel  logits = x W^T (+ bias), bf16 inputs, fp32 sums.
 //                         Tiled 64x64 with a deterministic split-K so small
-//                         token counts still fill the GPU (partials are
-//                         summed in a fixed order by the top-k kernel).
+//                         token counts still fill the GPU (the CTA that
+//                         finishes a tile last sums its partials in split
+//                         order).
 //   router_mma_kernel     the same with a bf16 router weight on the tensor
 //                         cores (mma.sync m16n8k16 bf16, fp32 accumulate):
 //                         64x64 tiles, 64-K stages double-buffered by
@@ -51,15 +52,49 @@ __device__ __forceinline__ float bf16f(uint16_t b) { return __uint_as_float((uin
 
 __device__ __forceinline__ float f16f(uint16_t b) { return __half2float(__ushort_as_half(b)); }
 
+// Split-K fixup of one 64 x 64 logits tile: after every split of the tile
+// has stored its partial sums, the CTA that stores the last one adds them,
+// split 0 first, into split 0's slot (element by element, each read before
+// it is overwritten), so the top-k reads one value per expert. The order of
+// the additions is the one the top-k kernel would use. The tile's counter
+// (zeroed before the launch) is reset for the next call.
+__device__ __forceinline__ void splitk_fixup(float* part, int T, int E, int t0, int e0, int nsplit,
+                                             int* counters) {
+  if (nsplit <= 1) return;
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+  if (threadIdx.x == 0) {
+    const int prev = atomicAdd(counters + tile, 1);
+    s_last = prev == nsplit - 1;
+    if (s_last) counters[tile] = 0;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const size_t stride = (size_t)T * E;
+  for (int i = threadIdx.x; i < 64 * 64; i += blockDim.x) {
+    const int t = t0 + (i >> 6), e = e0 + (i & 63);
+    if (t >= T || e >= E) continue;
+    float* p0 = part + (size_t)t * E + e;
+    float v = 0.f;
+    for (int z = 0; z < nsplit; z++) v += __ldcg(p0 + z * stride);
+    *p0 = v;
+  }
+}
+
 // grid (ceil(E/64), ceil(T/64), splits); 256 threads compute 4x4 each.
 // W_FP16 selects the router weight dtype (bf16 or fp16); x is bf16.
 template <bool W_FP16>
 __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __restrict__ x,
                                                             const uint16_t* __restrict__ W,
                                                             float* __restrict__ part, int T, int E,
-                                                            int M, int kspan) {
-  __shared__ float xs[kRK][kRT + 4];
-  __shared__ float ws[kRK][kRE + 4];
+                                                            int M, int kspan, int* counters) {
+  // read as float4 below: 16-byte alignment must not depend on the layout
+  // of the kernel's other shared variables
+  __shared__ __align__(16) float xs[kRK][kRT + 4];
+  __shared__ __align__(16) float ws[kRK][kRE + 4];
   const int e0 = blockIdx.x * kRE, t0 = blockIdx.y * kRT;
   const int kb = blockIdx.z * kspan, ke = min(M, kb + kspan);
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // 16 x 16 threads
@@ -105,6 +140,7 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __re
       if (e < E) out[(size_t)t * E + e] = acc[i][j];
     }
   }
+  splitk_fixup(part, T, E, t0, e0, gridDim.z, counters);
 }
 
 constexpr int kMT = 64, kME = 64, kMK = 64;   // tensor-core router tile: tokens, experts, K
@@ -139,7 +175,7 @@ __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a
 __global__ void __launch_bounds__(128) router_mma_kernel(const uint16_t* __restrict__ x,
                                                          const uint16_t* __restrict__ W,
                                                          float* __restrict__ part, int T, int E,
-                                                         int M, int kspan) {
+                                                         int M, int kspan, int* counters) {
   __shared__ __align__(128) uint16_t sa[2][kMT * kMK];
   __shared__ __align__(128) uint16_t sb[2][kME * kMK];
   const int e0 = blockIdx.x * kME, t0 = blockIdx.y * kMT;
@@ -215,6 +251,7 @@ __global__ void __launch_bounds__(128) router_mma_kernel(const uint16_t* __restr
         const int e = e0 + wn * 32 + ni * 8 + 2 * t4 + (v & 1);
         if (tok < T && e < E) out[(size_t)tok * E + e] = c[mi][ni][v];
       }
+  splitk_fixup(part, T, E, t0, e0, gridDim.z, counters);
 }
 
 constexpr int kGemvMaxT = 4;   // tokens per launch of the GEMV router
@@ -1046,7 +1083,7 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const DecodePlan p) {
   extern __shared__ __align__(16) uint8_t s_q16[];   // T q16 token rows
   __shared__ int s_idx[kDecodeMaxSlots];
   __shared__ float s_w[kDecodeMaxSlots];
-  __shared__ WispSegment s_segs[kPlanMaxV];
+  __shared__ __align__(16) WispSegment s_segs[kPlanMaxV];
   __shared__ int s_tok[kDecodeMaxRows];
   __shared__ int warp_tot[32];
   __shared__ int carry;
@@ -1232,11 +1269,13 @@ size_t router_splits(int T, int E, int M) {
   return (size_t)splits;
 }
 
+// Tiles of the split-K router launch (one completion counter each).
+int router_tiles(int T, int E) { return ((E + kRE - 1) / kRE) * ((T + kRT - 1) / kRT); }
+
 WispError launch_route(const WispMoeConfig* c, const uint16_t* x, const uint16_t* W,
                        const float* bias, float* part, size_t splits, float* logits_out, int* idx,
-                       float* w, cudaStream_t st, WispErrCtx* err) {
+                       float* w, int* counters, cudaStream_t st, WispErrCtx* err) {
   const int T = c->tokens, E = c->n_experts, M = c->hidden;
-  int nsplit = 1;
   if (T <= kGemvMaxT) {
     const int g = (E + 1) / 2;
     if (c->router_fp16)
@@ -1249,17 +1288,25 @@ WispError launch_route(const WispMoeConfig* c, const uint16_t* x, const uint16_t
     const int gran = c->router_fp16 ? kRK : kMK;
     int kspan = (M + (int)splits - 1) / (int)splits;
     kspan = (kspan + gran - 1) / gran * gran;
-    nsplit = (M + kspan - 1) / kspan;
+    const int nsplit = (M + kspan - 1) / kspan;
+    if (nsplit > 1) {
+      // the last split of each tile sums the partials into split 0
+      if (!counters)
+        return WB_FAIL(WISP_ERR_INVALID_ARG, "route: split-K logits need tile counters");
+      WB_CUDA_CHECK(cudaMemsetAsync(counters, 0, sizeof(int) * router_tiles(T, E), st));
+    }
     dim3 g1((E + kRE - 1) / kRE, (T + kRT - 1) / kRT, nsplit);
     if (c->router_fp16)
-      wb::launch_k(router_logits_kernel<true>, g1, 256, 0, st, x, W, part, T, E, M, kspan);
+      wb::launch_k(router_logits_kernel<true>, g1, 256, 0, st, x, W, part, T, E, M, kspan,
+                   counters);
     else
-      wb::launch_k(router_mma_kernel, g1, 128, 0, st, x, W, part, T, E, M, kspan);
+      wb::launch_k(router_mma_kernel, g1, 128, 0, st, x, W, part, T, E, M, kspan, counters);
   }
   auto topk = E <= 32 ? topk_kernel<1> : E <= 64 ? topk_kernel<2> : E <= 128 ? topk_kernel<4>
             : E <= 256 ? topk_kernel<8> : E <= 512 ? topk_kernel<16> : topk_kernel<32>;
-  // two tokens (warps) per block, so a few hundred tokens still spread over the SMs
-  wb::launch_k(topk, (T + 1) / 2, 64, 0, st, part, nsplit, bias, T, E, c->top_k, c->scoring,
+  // two tokens (warps) per block, so a few hundred tokens still spread over
+  // the SMs; the logits are final (split 0 after the fixup)
+  wb::launch_k(topk, (T + 1) / 2, 64, 0, st, part, 1, bias, T, E, c->top_k, c->scoring,
                c->n_groups, c->topk_groups, c->routed_scaling, idx, w, logits_out);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;

@@ -99,10 +99,17 @@ def _segments_tensor(segs, device) -> torch.Tensor:
 class CudaOps:
     """Compute steps of one EP layer on the GPU, through libwisp_b200.so."""
 
-    def route(self, cfg, lw: LayerWeights, x, idx, w, logits):
+    def route_scratch(self, cfg, device):
+        """Split-K partial sums of the router logits (wisp_b200_route_ws)."""
+        n = abi.lib().wisp_b200_route_workspace_bytes(C.byref(cfg))
+        if n == 0:
+            raise RuntimeError(f"wisp engine error [{abi.WISP_ERR_INVALID_ARG}]: route workspace query failed")
+        return torch.empty(n, dtype=torch.uint8, device=device)
+
+    def route(self, cfg, lw: LayerWeights, x, idx, w, scratch):
         ws = lw.weights_struct()
-        abi.call("wisp_b200_route", C.byref(cfg), C.byref(ws), x.data_ptr(), logits.data_ptr(),
-                 idx.data_ptr(), w.data_ptr(), _stream())
+        abi.call("wisp_b200_route_ws", C.byref(cfg), C.byref(ws), x.data_ptr(), None,
+                 idx.data_ptr(), w.data_ptr(), scratch.data_ptr(), scratch.numel(), _stream())
 
     def plan(self, cfg, idx, w, counts, segs, row_token, row_weight):
         abi.call("wisp_b200_dispatch_plan", C.byref(cfg), idx.data_ptr(), w.data_ptr(),
@@ -213,7 +220,7 @@ class EpLayer:
         adt = self.ops.act_dtype()
         self.idx = torch.empty((T, k), dtype=torch.int32, device=dev)
         self.w = torch.empty((T, k), dtype=torch.float32, device=dev)
-        self.logits = torch.empty((T, spec.n_experts), dtype=torch.float32, device=dev)
+        self.route_scratch = self.ops.route_scratch(self.cfg_route, dev)
         self.counts = torch.empty(spec.n_experts, dtype=torch.int32, device=dev)
         self.segs = torch.empty(16 * spec.n_experts, dtype=torch.uint8, device=dev)
         self.row_token = torch.empty(T * k, dtype=torch.int32, device=dev)
@@ -267,7 +274,7 @@ class EpLayer:
         and the device error word."""
         spec, ops = self.spec, self.ops
         ops.clear_flag(self.flag)
-        ops.route(self.cfg_route, self.lw, x, self.idx, self.w, self.logits)
+        ops.route(self.cfg_route, self.lw, x, self.idx, self.w, self.route_scratch)
         ops.plan(self.cfg_route, self.idx, self.w, self.counts, self.segs, self.row_token,
                  self.row_weight)
         ops.dispatch(x, self.idx, self.segs, self.row_token, self.row_weight, spec.n_experts,
