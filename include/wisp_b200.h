@@ -293,10 +293,9 @@ WispError wisp_b200_route(const WispMoeConfig* cfg, const WispMoeWeights* w, con
 /* The same routing with the logits summed over K splits, so that a few
  * tokens still spread over the SMs (wisp_b200_route computes each token
  * tile's logits in one pass over K). d_workspace holds the split partial
- * sums and one completion counter per 64 x 64 logits tile
- * (wisp_b200_route_workspace_bytes, 16-byte aligned; one call at a time per
- * workspace); d_logits may be NULL. Same results as wisp_b200_route within
- * fp32 summation order. */
+ * sums (wisp_b200_route_workspace_bytes, 16-byte aligned; one call at a
+ * time per workspace); d_logits may be NULL. Same results as
+ * wisp_b200_route within fp32 summation order. */
 size_t wisp_b200_route_workspace_bytes(const WispMoeConfig* cfg);
 WispError wisp_b200_route_ws(const WispMoeConfig* cfg, const WispMoeWeights* w,
                              const uint16_t* d_x, float* d_logits, int* d_idx, float* d_w,

@@ -22,8 +22,7 @@ namespace wb {
 size_t router_splits(int T, int E, int M);
 WispError launch_route(const WispMoeConfig* c, const uint16_t* x, const uint16_t* W,
                        const float* bias, float* part, size_t splits, float* logits_out, int* idx,
-                       float* w, int* counters, cudaStream_t st, WispErrCtx* err);
-int router_tiles(int T, int E);
+                       float* w, cudaStream_t st, WispErrCtx* err);
 WispError launch_plan(const WispMoeConfig* c, const int* idx, const float* w, int* counts,
                       WispSegment* segs, int* row_token, float* row_weight, cudaStream_t st,
                       WispErrCtx* err);
@@ -68,7 +67,6 @@ struct Carve {
 
 struct Workspace {
   float* part;
-  int* counters;
   int* idx;
   float* w;
   int* counts;
@@ -93,7 +91,6 @@ Workspace carve(const WispMoeConfig* c, void* base) {
   ws.rows = T * k + (c->has_shared ? T : 0);
   ws.splits = wb::router_splits(T, E, M);
   ws.part = cv.take<float>(base, ws.splits * (size_t)T * E);
-  ws.counters = cv.take<int>(base, wb::router_tiles(T, E));
   ws.idx = cv.take<int>(base, (size_t)T * k);
   ws.w = cv.take<float>(base, (size_t)T * k);
   ws.counts = cv.take<int>(base, V);
@@ -149,11 +146,11 @@ extern "C" WispError wisp_b200_route(const WispMoeConfig* cfg, const WispMoeWeig
   // the final logits (bias included); each token's row is read before it
   // is rewritten by the same thread.
   return wb::launch_route(cfg, d_x, w->router_w, w->router_bias, d_logits, 1, d_logits, d_idx, d_w,
-                          nullptr, stream, err);
+                          stream, err);
 }
 
 namespace {
-// wisp_b200_route_ws workspace: the split partials, then one counter per tile.
+// wisp_b200_route_ws workspace: the split partial sums.
 size_t route_part_bytes(const WispMoeConfig* cfg) {
   const size_t n = wb::router_splits(cfg->tokens, cfg->n_experts, cfg->hidden) *
                    (size_t)cfg->tokens * cfg->n_experts * sizeof(float);
@@ -163,7 +160,7 @@ size_t route_part_bytes(const WispMoeConfig* cfg) {
 
 extern "C" size_t wisp_b200_route_workspace_bytes(const WispMoeConfig* cfg) {
   if (validate(cfg, nullptr) != WISP_OK) return 0;
-  return route_part_bytes(cfg) + (size_t)wb::router_tiles(cfg->tokens, cfg->n_experts) * sizeof(int);
+  return route_part_bytes(cfg);
 }
 
 extern "C" WispError wisp_b200_route_ws(const WispMoeConfig* cfg, const WispMoeWeights* w,
@@ -181,10 +178,8 @@ extern "C" WispError wisp_b200_route_ws(const WispMoeConfig* cfg, const WispMoeW
                    need);
   if (((uintptr_t)d_x | (uintptr_t)w->router_w | (uintptr_t)d_workspace) & 15)
     return WB_FAIL(WISP_ERR_INVALID_ARG, "route_ws: x, router_w and workspace must be 16-byte aligned");
-  uint8_t* base = static_cast<uint8_t*>(d_workspace);
-  return wb::launch_route(cfg, d_x, w->router_w, w->router_bias, reinterpret_cast<float*>(base),
-                          splits, d_logits, d_idx, d_w,
-                          reinterpret_cast<int*>(base + route_part_bytes(cfg)), stream, err);
+  return wb::launch_route(cfg, d_x, w->router_w, w->router_bias, static_cast<float*>(d_workspace),
+                          splits, d_logits, d_idx, d_w, stream, err);
 }
 
 extern "C" WispError wisp_b200_moe_forward(const WispMoeConfig* cfg, const WispMoeWeights* w,
@@ -226,7 +221,7 @@ extern "C" WispError wisp_b200_moe_forward(const WispMoeConfig* cfg, const WispM
   }
 
   e = wb::launch_route(cfg, d_x, w->router_w, w->router_bias, ws.part, ws.splits, nullptr, idx, wt,
-                       ws.counters, stream, err);
+                       stream, err);
   if (e != WISP_OK) return e;
   e = wb::launch_plan(cfg, idx, wt, ws.counts, ws.segs, ws.row_token, ws.row_weight, stream, err);
   if (e != WISP_OK) return e;

@@ -2,9 +2,8 @@
 //
 //   router_logits_kernel  logits = x W^T (+ bias), bf16 inputs, fp32 sums.
 //                         Tiled 64x64 with a deterministic split-K so small
-//                         token counts still fill the GPU (the CTA that
-//                         finishes a tile last sums its partials in split
-//                         order).
+//                         token counts still fill the GPU (the top-k kernel
+//                         sums the partials in a fixed order).
 //   router_mma_kernel     the same with a bf16 router weight on the tensor
 //                         cores (mma.sync m16n8k16 bf16, fp32 accumulate):
 //                         64x64 tiles, 64-K stages double-buffered by
@@ -52,45 +51,13 @@ __device__ __forceinline__ float bf16f(uint16_t b) { return __uint_as_float((uin
 
 __device__ __forceinline__ float f16f(uint16_t b) { return __half2float(__ushort_as_half(b)); }
 
-// Split-K fixup of one 64 x 64 logits tile: after every split of the tile
-// has stored its partial sums, the CTA that stores the last one adds them,
-// split 0 first, into split 0's slot (element by element, each read before
-// it is overwritten), so the top-k reads one value per expert. The order of
-// the additions is the one the top-k kernel would use. The tile's counter
-// (zeroed before the launch) is reset for the next call.
-__device__ __forceinline__ void splitk_fixup(float* part, int T, int E, int t0, int e0, int nsplit,
-                                             int* counters) {
-  if (nsplit <= 1) return;
-  __shared__ int s_last;
-  __threadfence();
-  __syncthreads();
-  const int tile = blockIdx.y * gridDim.x + blockIdx.x;
-  if (threadIdx.x == 0) {
-    const int prev = atomicAdd(counters + tile, 1);
-    s_last = prev == nsplit - 1;
-    if (s_last) counters[tile] = 0;
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  const size_t stride = (size_t)T * E;
-  for (int i = threadIdx.x; i < 64 * 64; i += blockDim.x) {
-    const int t = t0 + (i >> 6), e = e0 + (i & 63);
-    if (t >= T || e >= E) continue;
-    float* p0 = part + (size_t)t * E + e;
-    float v = 0.f;
-    for (int z = 0; z < nsplit; z++) v += __ldcg(p0 + z * stride);
-    *p0 = v;
-  }
-}
-
 // grid (ceil(E/64), ceil(T/64), splits); 256 threads compute 4x4 each.
 // W_FP16 selects the router weight dtype (bf16 or fp16); x is bf16.
 template <bool W_FP16>
 __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __restrict__ x,
                                                             const uint16_t* __restrict__ W,
                                                             float* __restrict__ part, int T, int E,
-                                                            int M, int kspan, int* counters) {
+                                                            int M, int kspan) {
   // read as float4 below: 16-byte alignment must not depend on the layout
   // of the kernel's other shared variables
   __shared__ __align__(16) float xs[kRK][kRT + 4];
@@ -140,7 +107,6 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __re
       if (e < E) out[(size_t)t * E + e] = acc[i][j];
     }
   }
-  splitk_fixup(part, T, E, t0, e0, gridDim.z, counters);
 }
 
 constexpr int kMT = 64, kME = 64, kMK = 64;   // tensor-core router tile: tokens, experts, K
@@ -175,7 +141,7 @@ __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a
 __global__ void __launch_bounds__(128) router_mma_kernel(const uint16_t* __restrict__ x,
                                                          const uint16_t* __restrict__ W,
                                                          float* __restrict__ part, int T, int E,
-                                                         int M, int kspan, int* counters) {
+                                                         int M, int kspan) {
   __shared__ __align__(128) uint16_t sa[2][kMT * kMK];
   __shared__ __align__(128) uint16_t sb[2][kME * kMK];
   const int e0 = blockIdx.x * kME, t0 = blockIdx.y * kMT;
@@ -251,7 +217,6 @@ __global__ void __launch_bounds__(128) router_mma_kernel(const uint16_t* __restr
         const int e = e0 + wn * 32 + ni * 8 + 2 * t4 + (v & 1);
         if (tok < T && e < E) out[(size_t)tok * E + e] = c[mi][ni][v];
       }
-  splitk_fixup(part, T, E, t0, e0, gridDim.z, counters);
 }
 
 constexpr int kGemvMaxT = 4;   // tokens per launch of the GEMV router
@@ -355,20 +320,31 @@ __device__ __forceinline__ void topk_token(const float* __restrict__ part, int s
                                            const float* __restrict__ bias, int T, int t, int E,
                                            int k, int scoring, int n_groups, int topk_groups,
                                            float scaling, int* idx, float* wout,
-                                           float* logits_out, int lane) {
+                                           float* logits_out, int lane,
+                                           const float* presum = nullptr) {
   const int per = (E + 31) / 32;
   float v[PER];
 #pragma unroll
   for (int j = 0; j < PER; j++) v[j] = 0.f;
-  // Split-K partials: split-major, all of a split's loads in flight together
-  // (a per-expert loop over the splits would wait one L2 round trip per
-  // split and expert).
-  for (int z = 0; z < splits; z++) {
-    const float* pz = part + ((size_t)z * T + t) * E;
+  if (presum) {
+    // the logits were summed over the splits already (topk_kernel's helper
+    // warps): one value per expert from shared memory
 #pragma unroll
     for (int j = 0; j < PER; j++) {
       const int e = lane + 32 * j;
-      if (j < per && e < E) v[j] += __ldg(pz + e);
+      if (j < per && e < E) v[j] = presum[e];
+    }
+  } else {
+    // Split-K partials: split-major, all of a split's loads in flight
+    // together (a per-expert loop over the splits would wait one L2 round
+    // trip per split and expert).
+    for (int z = 0; z < splits; z++) {
+      const float* pz = part + ((size_t)z * T + t) * E;
+#pragma unroll
+      for (int j = 0; j < PER; j++) {
+        const int e = lane + 32 * j;
+        if (j < per && e < E) v[j] += __ldg(pz + e);
+      }
     }
   }
 #pragma unroll
@@ -501,16 +477,53 @@ __device__ __forceinline__ void topk_token(const float* __restrict__ part, int s
   }
 }
 
+// Block of kTopkTok tokens x kTopkQ warps: with split-K partials, warp q of
+// a token sums splits q, q + kTopkQ, ... (loads of a split in flight
+// together) and the token's warp 0 adds the kTopkQ sums in order, so a
+// token waits for ceil(splits / kTopkQ) L2 round trips, not splits; warp 0
+// then routes the token.
+constexpr int kTopkTok = 2, kTopkQ = 4;
+
 template <int PER>
-__global__ void topk_kernel(const float* __restrict__ part, int splits, const float* __restrict__ bias,
-                            int T, int E, int k, int scoring, int n_groups, int topk_groups,
-                            float scaling, int* __restrict__ idx, float* __restrict__ wout,
-                            float* __restrict__ logits_out) {
+__global__ void __launch_bounds__(kTopkTok * kTopkQ * 32) topk_kernel(
+    const float* __restrict__ part, int splits, const float* __restrict__ bias, int T, int E, int k,
+    int scoring, int n_groups, int topk_groups, float scaling, int* __restrict__ idx,
+    float* __restrict__ wout, float* __restrict__ logits_out) {
+  __shared__ float sums[kTopkTok][kTopkQ][PER * 32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * (blockDim.x >> 5) + warp;
-  if (t >= T) return;
+  const int tw = warp / kTopkQ, q = warp % kTopkQ;
+  const int t = blockIdx.x * kTopkTok + tw;
+  const int per = (E + 31) / 32;
+  if (splits > 1) {
+    if (t < T) {
+      float v[PER];
+#pragma unroll
+      for (int j = 0; j < PER; j++) v[j] = 0.f;
+      for (int z = q; z < splits; z += kTopkQ) {
+        const float* pz = part + ((size_t)z * T + t) * E;
+#pragma unroll
+        for (int j = 0; j < PER; j++) {
+          const int e = lane + 32 * j;
+          if (j < per && e < E) v[j] += __ldg(pz + e);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < PER; j++) sums[tw][q][lane + 32 * j] = v[j];
+    }
+    __syncthreads();
+    if (q == 0 && t < T) {
+#pragma unroll
+      for (int j = 0; j < PER; j++) {
+        float a = sums[tw][0][lane + 32 * j];
+        for (int qq = 1; qq < kTopkQ; qq++) a += sums[tw][qq][lane + 32 * j];
+        sums[tw][0][lane + 32 * j] = a;
+      }
+    }
+    __syncwarp();
+  }
+  if (q != 0 || t >= T) return;
   topk_token<PER>(part, splits, bias, T, t, E, k, scoring, n_groups, topk_groups, scaling, idx,
-                  wout, logits_out, lane);
+                  wout, logits_out, lane, splits > 1 ? &sums[tw][0][0] : nullptr);
 }
 
 // One block of kPlanWarps warps per expert v: warp w scans the w-th
@@ -1269,13 +1282,11 @@ size_t router_splits(int T, int E, int M) {
   return (size_t)splits;
 }
 
-// Tiles of the split-K router launch (one completion counter each).
-int router_tiles(int T, int E) { return ((E + kRE - 1) / kRE) * ((T + kRT - 1) / kRT); }
-
 WispError launch_route(const WispMoeConfig* c, const uint16_t* x, const uint16_t* W,
                        const float* bias, float* part, size_t splits, float* logits_out, int* idx,
-                       float* w, int* counters, cudaStream_t st, WispErrCtx* err) {
+                       float* w, cudaStream_t st, WispErrCtx* err) {
   const int T = c->tokens, E = c->n_experts, M = c->hidden;
+  int nsplit = 1;
   if (T <= kGemvMaxT) {
     const int g = (E + 1) / 2;
     if (c->router_fp16)
@@ -1288,26 +1299,20 @@ WispError launch_route(const WispMoeConfig* c, const uint16_t* x, const uint16_t
     const int gran = c->router_fp16 ? kRK : kMK;
     int kspan = (M + (int)splits - 1) / (int)splits;
     kspan = (kspan + gran - 1) / gran * gran;
-    const int nsplit = (M + kspan - 1) / kspan;
-    if (nsplit > 1) {
-      // the last split of each tile sums the partials into split 0
-      if (!counters)
-        return WB_FAIL(WISP_ERR_INVALID_ARG, "route: split-K logits need tile counters");
-      WB_CUDA_CHECK(cudaMemsetAsync(counters, 0, sizeof(int) * router_tiles(T, E), st));
-    }
+    nsplit = (M + kspan - 1) / kspan;
     dim3 g1((E + kRE - 1) / kRE, (T + kRT - 1) / kRT, nsplit);
     if (c->router_fp16)
-      wb::launch_k(router_logits_kernel<true>, g1, 256, 0, st, x, W, part, T, E, M, kspan,
-                   counters);
+      wb::launch_k(router_logits_kernel<true>, g1, 256, 0, st, x, W, part, T, E, M, kspan);
     else
-      wb::launch_k(router_mma_kernel, g1, 128, 0, st, x, W, part, T, E, M, kspan, counters);
+      wb::launch_k(router_mma_kernel, g1, 128, 0, st, x, W, part, T, E, M, kspan);
   }
   auto topk = E <= 32 ? topk_kernel<1> : E <= 64 ? topk_kernel<2> : E <= 128 ? topk_kernel<4>
             : E <= 256 ? topk_kernel<8> : E <= 512 ? topk_kernel<16> : topk_kernel<32>;
-  // two tokens (warps) per block, so a few hundred tokens still spread over
-  // the SMs; the logits are final (split 0 after the fixup)
-  wb::launch_k(topk, (T + 1) / 2, 64, 0, st, part, 1, bias, T, E, c->top_k, c->scoring,
-               c->n_groups, c->topk_groups, c->routed_scaling, idx, w, logits_out);
+  // two tokens per block (four warps each), so a few hundred tokens still
+  // spread over the SMs
+  wb::launch_k(topk, (T + kTopkTok - 1) / kTopkTok, kTopkTok * kTopkQ * 32, 0, st, part, nsplit,
+               bias, T, E, c->top_k, c->scoring, c->n_groups, c->topk_groups, c->routed_scaling,
+               idx, w, logits_out);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
