@@ -421,6 +421,46 @@ def ep_phase_report(layers, xs, outs, step_eager, spec, T, L, world, dev, reps: 
     }
 
 
+def ep_loopback_run(args, spec) -> None:
+    """The expert-parallel layer of `args.ep_loopback` ranks run on one GPU
+    (EpLayer.loopback_forward: every rank's kernels in turn, the two
+    all-to-alls as block copies), for launch lists and kernel profiles of
+    one rank's expert-parallel kernels without a multi-rank process. One
+    JSON line: device time per loopback step of the first layer (all ranks'
+    work, so not a throughput figure)."""
+    import torch
+    from wisp_b200 import synth
+    from wisp_b200.ep import EpLayer, block_range, loopback_forward
+    W = args.ep_loopback
+    dev = torch.device("cuda", 0)
+    one = synth.small(spec, layers=1)
+    E, T = one.n_experts, one.tokens
+    t_max = max(b - a for a, b in (block_range(T, W, q) for q in range(W)))
+    layers, xs, outs = [], [], []
+    for r in range(W):
+        lw, x = synth.make_model(one, dev, keep=range(*block_range(E, W, r)))
+        t0, t1 = block_range(T, W, r)
+        layers.append(EpLayer(one, lw[0], t1 - t0, r, W, max_tokens=t_max))
+        xs.append(x[t0:t1].contiguous())
+        outs.append(torch.empty((t1 - t0, one.hidden), dtype=torch.float32, device=dev))
+    for _ in range(args.warmup):
+        loopback_forward(layers, xs, outs)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")
+    a.record()
+    for _ in range(args.steps):
+        loopback_forward(layers, xs, outs)
+    b.record()
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    for lay in layers:
+        lay.check()
+    print(json.dumps({"ep_loopback": {"ranks": W, "workload": spec.name, "layer": 0,
+                                      "ms_per_loopback_step": round(a.elapsed_time(b) / args.steps, 4),
+                                      "note": "every rank's kernels on one GPU, exchanges as copies"}}))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -431,6 +471,9 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch every step eagerly")
     ap.add_argument("--kernel-reps", type=int, default=5)
+    ap.add_argument("--ep-loopback", type=int, default=0, metavar="W",
+                    help="profiling aid: run the expert-parallel layer of W ranks on one GPU "
+                         "(loopback exchanges) instead of the benchmark")
     ap.add_argument("--no-side-configs", action="store_true",
                     help="skip the single-layer measurements of BASELINE configs[0]-[3]")
     args = ap.parse_args()
@@ -440,6 +483,9 @@ def main() -> None:
     spec = synth.CONFIGS[args.config]
     if args.impl == "reference":
         reference_arm(args, spec)
+        return
+    if args.ep_loopback:
+        ep_loopback_run(args, spec)
         return
 
     import numpy as np

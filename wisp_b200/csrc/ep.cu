@@ -22,9 +22,10 @@
 // weighted output into an fp32 row per received token, and one all-to-all
 // returns those rows; the home rank adds its rows from each owner.
 //
-//   ep_dispatch_kernel   one block: per destination the token -> row slots
-//                        (a scan over tokens), the block headers and the
-//                        entries from the dispatch plan.
+//   ep_dispatch_kernel   one block: per destination (one warp each) the
+//                        token -> row slots (a ballot scan over tokens), the
+//                        block headers and the entries from the dispatch
+//                        plan.
 //   ep_pack_kernel       token rows (bf16 -> fp16 interleaved) into every
 //                        block that holds them.
 //   ep_recv_plan_kernel  one block: from the received headers and entries,
@@ -99,47 +100,74 @@ __device__ int block_scan(int f, int* warp_tot, int* total) {
 // Single block. idx [T x k] (global experts); the plan (plan_segs over the E
 // global experts, row_token / row_weight sorted by expert then token) comes
 // from the dispatch plan of the same routing. slot[t * world + q] = row of
-// token t in block q, or -1.
+// token t in block q, or -1. The routing, the plan's segments and the slots
+// are staged in shared memory (when they fit), so every phase is one round
+// of parallel loads: slots by one warp per destination, then the entries by
+// one thread per plan row.
+constexpr int kDispStage = 4096;   // idx / slot entries staged in shared memory
+
 __global__ void __launch_bounds__(1024) ep_dispatch_kernel(
     const int* __restrict__ idx, const WispSegment* __restrict__ plan_segs,
     const int* __restrict__ row_token, const float* __restrict__ row_weight, int T, int k, int E,
     int world, Layout L, uint8_t* __restrict__ send, int* __restrict__ slot) {
-  __shared__ int warp_tot[32];
+  __shared__ int s_idx[kDispStage];
+  __shared__ int s_slot[kDispStage];
+  __shared__ int s_begin[1024];
+  __shared__ int s_rows[1024];
   const int e_loc = E / world;
-  for (int q = 0; q < world; q++) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool idx_sm = T * k <= kDispStage, slot_sm = T * world <= kDispStage;
+  if (idx_sm)
+    for (int i = threadIdx.x; i < T * k; i += blockDim.x) s_idx[i] = __ldg(idx + i);
+  for (int g = threadIdx.x; g < E; g += blockDim.x) {
+    s_begin[g] = __ldg(&plan_segs[g].row_begin);
+    s_rows[g] = __ldg(&plan_segs[g].rows);
+  }
+  __syncthreads();
+  const int* ix = idx_sm ? s_idx : idx;
+  // one warp per destination q: a token's slot in q's block is the number
+  // of earlier tokens with an expert on q (ballot prefix over 32-token runs)
+  for (int q = warp; q < world; q += blockDim.x >> 5) {
     int carry = 0;
-    for (int base = 0; base < T; base += blockDim.x) {
-      const int t = base + threadIdx.x;
-      int f = 0;
+    for (int base = 0; base < T; base += 32) {
+      const int t = base + lane;
+      bool f = false;
       if (t < T)
         for (int j = 0; j < k; j++) {
-          const int e = __ldg(idx + (size_t)t * k + j);
-          if (e >= 0 && e < E && e / e_loc == q) f = 1;
+          const int e = ix[(size_t)t * k + j];
+          if (e >= 0 && e < E && e / e_loc == q) f = true;
         }
-      int tot;
-      const int ex = block_scan(f, warp_tot, &tot);
-      if (t < T) slot[(size_t)t * world + q] = f ? carry + ex : -1;
-      carry += tot;
+      const unsigned m = __ballot_sync(0xffffffffu, f);
+      if (t < T) {
+        const int v = f ? carry + __popc(m & ((1u << lane) - 1u)) : -1;
+        slot[(size_t)t * world + q] = v;
+        if (slot_sm) s_slot[t * world + q] = v;
+      }
+      carry += __popc(m);
     }
-    if (threadIdx.x == 0) reinterpret_cast<int*>(send + q * L.bytes)[0] = carry;
+    if (lane == 0) reinterpret_cast<int*>(send + q * L.bytes)[0] = carry;
   }
   for (int g = threadIdx.x; g < E; g += blockDim.x) {
     const int q = g / e_loc;
-    reinterpret_cast<int*>(send + q * L.bytes + 16)[g - q * e_loc] = __ldg(&plan_segs[g].rows);
+    reinterpret_cast<int*>(send + q * L.bytes + 16)[g - q * e_loc] = s_rows[g];
   }
   __syncthreads();  // the slots above are read back below
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int g = warp; g < E; g += blockDim.x >> 5) {
-    const int q = g / e_loc;
-    const int first = __ldg(&plan_segs[q * e_loc].row_begin);  // q's first plan row
-    const int b = __ldg(&plan_segs[g].row_begin), r = __ldg(&plan_segs[g].rows);
+  // entries: plan row p (expert g = the last segment starting at or before
+  // p) goes to block q = g / e_loc at position p - (q's first plan row)
+  const int nrows = s_begin[E - 1] + s_rows[E - 1];
+  for (int p = threadIdx.x; p < nrows; p += blockDim.x) {
+    int lo = 0, hi = E - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_begin[mid] <= p) lo = mid; else hi = mid - 1;
+    }
+    const int q = lo / e_loc;
+    const int first = s_begin[q * e_loc];
     int* ent = reinterpret_cast<int*>(send + q * L.bytes + L.off_ent);
     float* ew = reinterpret_cast<float*>(send + q * L.bytes + L.off_w);
-    for (int i = lane; i < r; i += 32) {
-      const int p = b + i;
-      ent[p - first] = slot[(size_t)__ldg(row_token + p) * world + q];
-      ew[p - first] = __ldg(row_weight + p);
-    }
+    const int t = __ldg(row_token + p);
+    ent[p - first] = slot_sm ? s_slot[t * world + q] : slot[(size_t)t * world + q];
+    ew[p - first] = __ldg(row_weight + p);
   }
 }
 
