@@ -80,6 +80,10 @@ CONFIGS: dict[str, MoeSpec] = {
     # still larger than L2): the small case for ncu captures.
     "ep_profile": MoeSpec("ep_profile", 7168, 2048, 64, 8, has_shared=True, tokens=40, layers=1,
                           seed=3),
+    # The DeepSeek b1 decode layer with 16 routed experts (+ shared): the
+    # same 9 touched experts and register-path launches as ds_b1 with
+    # 386 MB of weights on the device, the small case for ncu captures.
+    "ds_b1_profile": MoeSpec("ds_b1_profile", tokens=1, seed=1, **dict(_DS, n_experts=16)),
     # A prefill-shaped layer small enough for ncu: 64 DeepSeek-shaped experts
     # (1.45 GB), 1024 skewed tokens -> segments of ~100-600 rows.
     "prefill_profile": MoeSpec("prefill_profile", tokens=1024, seed=2, skew=True,
