@@ -381,20 +381,28 @@ WispError wisp_b200_ep_dispatch(const uint16_t* d_x, int tokens, int hidden, con
  * so each local expert is one segment: d_segs [e_loc] over the gathered
  * rows, d_src_pos[j] = receive row (source * cap + block row) and
  * d_weight[j] = routing weight of gathered row j, *d_total = entries.
- * d_src_pos and d_weight hold world * cap * top_k entries. */
+ * own_rows > 0 (<= cap) appends this rank's own own_rows token rows as
+ * segment e_loc (the shared expert's entry of the local table), with
+ * d_src_pos = world * cap + t and weight 1, so the shared expert runs in the
+ * same grouped call as the routed experts. d_src_pos and d_weight hold
+ * world * cap * top_k + own_rows entries, d_segs e_loc (+1). */
 WispError wisp_b200_ep_recv_plan(const uint8_t* d_recv, int world, int e_loc, int cap, int top_k,
-                                 int hidden, WispSegment* d_segs, int* d_src_pos, float* d_weight,
-                                 int* d_total, cudaStream_t stream, WispErrCtx* err);
+                                 int hidden, int own_rows, WispSegment* d_segs, int* d_src_pos,
+                                 float* d_weight, int* d_total, cudaStream_t stream,
+                                 WispErrCtx* err);
 
-/* d_sorted[j] = receive row d_src_pos[j] for j < *d_total (fp16 rows;
- * max_rows bounds the launch, normally world * cap * top_k). The grouped FFN
- * then runs in mode 0 with row_token = d_src_pos and row_weight = d_weight
- * into fp32 rows [world * cap x hidden] (zeroed first): one row per received
- * token, which the return exchange sends back. */
+/* d_sorted[j] = receive row d_src_pos[j] for j < *d_total + own_rows (fp16
+ * rows; a d_src_pos of world * cap + t reads row t of d_own, this rank's own
+ * token rows packed with wisp_b200_pack_rows; max_rows bounds the launch,
+ * normally world * cap * top_k + own_rows). The grouped FFN then runs in
+ * mode 0 with row_token = d_src_pos and row_weight = d_weight into fp32 rows
+ * [(world * cap + own_rows) x hidden] (zeroed first): one row per received
+ * token, which the return exchange sends back, then the shared expert's
+ * output for each own token. */
 WispError wisp_b200_ep_gather_rows(const uint8_t* d_recv, int world, int e_loc, int cap, int top_k,
                                    int hidden, const int* d_src_pos, const int* d_total,
-                                   int max_rows, uint16_t* d_sorted, cudaStream_t stream,
-                                   WispErrCtx* err);
+                                   const uint16_t* d_own, int own_rows, int max_rows,
+                                   uint16_t* d_sorted, cudaStream_t stream, WispErrCtx* err);
 
 /* d_out[t] += d_yback[q * cap + d_slot[t * world + q]] over q = 0..world-1
  * with a slot >= 0, in rank order (fp32 rows; one block per token). */
@@ -405,13 +413,15 @@ WispError wisp_b200_ep_combine(const float* d_yback, const int* d_slot, int toke
 /* The return exchange in fp16 (half the bytes of fp32 rows): the owner
  * rounds its fp32 return rows to fp16 (d_y16[i] = fp16(d_y[i]) for rows x
  * hidden values), the rows travel, and the home rank adds them in rank
- * order with wisp_b200_ep_combine_f16 (same contract as wisp_b200_ep_combine
- * with fp16 rows). */
+ * order with wisp_b200_ep_combine_f16 (wisp_b200_ep_combine's contract with
+ * fp16 rows; with d_local non-NULL, fp32 [tokens x hidden], the result is
+ * d_out[t] = d_local[t] + the returned rows, written rather than added). */
 WispError wisp_b200_ep_return_rows(const float* d_y, int rows, int hidden, uint16_t* d_y16,
                                    cudaStream_t stream, WispErrCtx* err);
-WispError wisp_b200_ep_combine_f16(const uint16_t* d_yback, const int* d_slot, int tokens,
-                                   int world, int cap, int hidden, float* d_out,
-                                   cudaStream_t stream, WispErrCtx* err);
+WispError wisp_b200_ep_combine_f16(const uint16_t* d_yback, const int* d_slot,
+                                   const float* d_local, int tokens, int world, int cap,
+                                   int hidden, float* d_out, cudaStream_t stream,
+                                   WispErrCtx* err);
 
 /* Between stacked layers: d_out[t] = bf16(d_in[t] / rms(d_in[t])), fp32 in. */
 WispError wisp_b200_rms_rescale(const float* d_in, uint16_t* d_out, int tokens, int hidden,

@@ -182,9 +182,15 @@ def test_ep_exchange_argument_checks():
     rc = L.wisp_b200_ep_dispatch(None, 4, 256, P, 2, P, P, P, 8, 2, 4, P, P, None, C.byref(err))
     assert rc == abi.WISP_ERR_INVALID_ARG
     # too many (rank, local expert) pairs for the single-block receive plan
-    rc = L.wisp_b200_ep_recv_plan(P, 8, 200, 4, 2, 256, P, P, P, P, None, C.byref(err))
+    rc = L.wisp_b200_ep_recv_plan(P, 8, 200, 4, 2, 256, 0, P, P, P, P, None, C.byref(err))
     assert rc == abi.WISP_ERR_INVALID_ARG and b"1024" in err.message
-    rc = L.wisp_b200_ep_gather_rows(P, 2, 4, 4, 2, 260, P, P, 16, P, None, C.byref(err))
+    # own rows beyond the block capacity
+    rc = L.wisp_b200_ep_recv_plan(P, 2, 4, 4, 2, 256, 5, P, P, P, P, None, C.byref(err))
+    assert rc == abi.WISP_ERR_INVALID_ARG and b"own_rows" in err.message
+    rc = L.wisp_b200_ep_gather_rows(P, 2, 4, 4, 2, 260, P, P, None, 0, 16, P, None, C.byref(err))
+    assert rc == abi.WISP_ERR_INVALID_ARG
+    # own rows without their buffer
+    rc = L.wisp_b200_ep_gather_rows(P, 2, 4, 4, 2, 256, P, P, None, 3, 16, P, None, C.byref(err))
     assert rc == abi.WISP_ERR_INVALID_ARG
     rc = L.wisp_b200_ep_combine(P, P, 5, 2, 4, 256, P, None, C.byref(err))
     assert rc == abi.WISP_ERR_INVALID_ARG

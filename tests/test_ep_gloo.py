@@ -98,7 +98,7 @@ class CpuOps:
                 if slot_ref[t, q] >= 0:
                     rows[slot_ref[t, q]] = xd[t]
 
-    def recv_plan(self, recv, world, e_loc, cap, k, hidden, segs, src_pos, weight, total):
+    def recv_plan(self, recv, world, e_loc, cap, k, hidden, own, segs, src_pos, weight, total):
         lay = self.lay
         sv = segs.numpy().view(np.int32).reshape(-1, 4)
         views = [self._views(recv, s, lay) for s in range(world)]
@@ -114,12 +114,21 @@ class CpuOps:
                     j += 1
             sv[e] = (e, b, j - b, 0)
         total[0] = j
+        if own:   # the rank's own rows, the shared expert's segment
+            sv[e_loc] = (e_loc, j, own, 0)
+            for t in range(own):
+                src_pos[j + t] = world * cap + t
+                weight[j + t] = 1.0
 
-    def gather_rows(self, recv, world, e_loc, cap, k, hidden, src_pos, total, max_rows, sorted_rows):
+    def gather_rows(self, recv, world, e_loc, cap, k, hidden, src_pos, total, own_rows, own,
+                    max_rows, sorted_rows):
         lay = self.lay
-        for j in range(int(total[0])):
+        for j in range(int(total[0]) + own):
             r = int(src_pos[j])
-            sorted_rows[j] = torch.from_numpy(self._views(recv, r // cap, lay)[3][r % cap].copy())
+            if r >= world * cap:
+                sorted_rows[j] = own_rows[r - world * cap]
+            else:
+                sorted_rows[j] = torch.from_numpy(self._views(recv, r // cap, lay)[3][r % cap].copy())
 
     def workspace(self, cfg, n_segs, rows, device):
         return torch.empty(1, dtype=torch.uint8)
@@ -142,8 +151,10 @@ class CpuOps:
     def return_rows(self, yr, yr16):
         yr16.copy_(yr)
 
-    def ep_combine(self, yback, slot, tokens, world, cap, out):
+    def ep_combine(self, yback, slot, local, tokens, world, cap, out):
         sl = slot.numpy()
+        if local is not None:
+            out[:tokens] = local[:tokens]
         for t in range(tokens):
             for q in range(world):
                 if sl[t, q] >= 0:

@@ -31,7 +31,8 @@
 //   ep_recv_plan_kernel  one block: from the received headers and entries,
 //                        one segment per local expert over the gathered
 //                        rows, the receive row and weight of each.
-//   ep_gather_kernel     gathered fp16 rows from the receive blocks.
+//   ep_gather_kernel     gathered fp16 rows from the receive blocks (and the
+//                        rank's own rows for the shared expert).
 //   ep_to_half_kernel    the owner's fp32 return rows rounded to fp16 (the
 //                        return exchange carries half the bytes).
 //   ep_combine_kernel    out[t] += the returned rows of token t, in rank order.
@@ -202,13 +203,15 @@ __global__ void ep_pack_kernel(const uint16_t* __restrict__ x, int M, const int*
 
 // Single block of 1024 threads (world * e_loc <= 1024 chunks, chunk (s, e) =
 // the entries of local expert e in source block s). Gathered order: local
-// expert, then source rank, then the source's entry order. src_pos[j] =
+// expert, then source rank, then the source's entry order; with own > 0 the
+// rank's own own token rows follow as segment e_loc (the shared expert). src_pos[j] =
 // receive row (s * cap + block row) of gathered row j, weight[j] its routing
 // weight; a source's entries are clamped to its block's capacity (cap * k)
 // in expert order. Two block scans give every chunk its source offset and
 // its gathered offset; warps then copy the chunks' entries.
 __global__ void __launch_bounds__(1024) ep_recv_plan_kernel(const uint8_t* __restrict__ recv,
                                                             int world, int e_loc, int k, Layout L,
+                                                            int own,
                                                             WispSegment* __restrict__ segs,
                                                             int* __restrict__ src_pos,
                                                             float* __restrict__ weight,
@@ -252,6 +255,22 @@ __global__ void __launch_bounds__(1024) ep_recv_plan_kernel(const uint8_t* __res
   const int ex2 = block_scan(ct, warp_tot, &tot);
   if (i < n) dst_off[s_t * e_loc + e_t] = ex2;
   if (i == 0) *total_out = tot;
+  // this rank's own token rows for the shared expert (local entry e_loc):
+  // one more segment after the received rows, source row world * cap + t
+  if (own > 0) {
+    if (i == 0) {
+      WispSegment sg;
+      sg.expert = e_loc;
+      sg.row_begin = tot;
+      sg.rows = own;
+      sg.reserved = 0;
+      segs[e_loc] = sg;
+    }
+    for (int t = i; t < own; t += blockDim.x) {
+      src_pos[tot + t] = world * L.cap + t;
+      weight[tot + t] = 1.f;
+    }
+  }
   __syncthreads();
   if (i < e_loc) {
     int rows = 0;
@@ -278,15 +297,23 @@ __global__ void __launch_bounds__(1024) ep_recv_plan_kernel(const uint8_t* __res
   }
 }
 
-// One block per gathered row j < *total: sorted[j] = receive row src_pos[j].
-__global__ void ep_gather_kernel(const uint8_t* __restrict__ recv, Layout L, int M,
+// One block per gathered row j < *total + own: sorted[j] = receive row
+// src_pos[j], or, for src_pos[j] >= world * cap, own row src_pos[j] - world *
+// cap (fp16 rows of this rank's tokens, already in the interleaved order).
+__global__ void ep_gather_kernel(const uint8_t* __restrict__ recv, Layout L, int M, int world,
                                  const int* __restrict__ src_pos, const int* __restrict__ total,
+                                 const uint16_t* __restrict__ own_rows, int own,
                                  uint16_t* __restrict__ sorted) {
   const int j = blockIdx.x;
-  if (j >= __ldg(total)) return;
+  if (j >= __ldg(total) + own) return;
   const int r = __ldg(src_pos + j);
-  const int s = r / L.cap, row = r - s * L.cap;
-  const uint4* src = reinterpret_cast<const uint4*>(recv + s * L.bytes + L.off_rows + (size_t)row * M * 2);
+  const uint4* src;
+  if (r >= world * L.cap) {
+    src = reinterpret_cast<const uint4*>(own_rows + (size_t)(r - world * L.cap) * M);
+  } else {
+    const int s = r / L.cap, row = r - s * L.cap;
+    src = reinterpret_cast<const uint4*>(recv + s * L.bytes + L.off_rows + (size_t)row * M * 2);
+  }
   uint4* dst = reinterpret_cast<uint4*>(sorted + (size_t)j * M);
   for (int i = threadIdx.x; i < M / 8; i += blockDim.x) dst[i] = __ldg(src + i);
 }
@@ -302,9 +329,11 @@ __device__ __forceinline__ float4 load4(const __half* p) {
 
 // Block (t, c): out[t] += yback[q * cap + slot[t][q]] for q = 0..world-1 over
 // the c-th run of 1024 values of the row.
+// With `local` (fp32 [T x M]), out[t] = local[t] + the returned rows instead.
 template <typename T>
 __global__ void ep_combine_kernel(const T* __restrict__ y, const int* __restrict__ slot,
-                                  int world, int cap, int M, float* __restrict__ out) {
+                                  const float* __restrict__ local, int world, int cap, int M,
+                                  float* __restrict__ out) {
   __shared__ int sl[kMaxWorld];
   const int t = blockIdx.x;
   if (threadIdx.x < world) sl[threadIdx.x] = slot[(size_t)t * world + threadIdx.x];
@@ -312,7 +341,8 @@ __global__ void ep_combine_kernel(const T* __restrict__ y, const int* __restrict
   float* orow = out + (size_t)t * M;
   const int end = min(M, ((int)blockIdx.y + 1) * (int)blockDim.x * 4);
   for (int i = blockIdx.y * blockDim.x * 4 + threadIdx.x * 4; i < end; i += blockDim.x * 4) {
-    float4 acc = *reinterpret_cast<const float4*>(orow + i);
+    float4 acc = local ? __ldg(reinterpret_cast<const float4*>(local + (size_t)t * M + i))
+                       : *reinterpret_cast<const float4*>(orow + i);
     for (int q = 0; q < world; q++) {
       if (sl[q] < 0) continue;
       const float4 v = load4(y + ((size_t)q * cap + sl[q]) * M + i);
@@ -376,36 +406,39 @@ extern "C" WispError wisp_b200_ep_dispatch(const uint16_t* d_x, int tokens, int 
 }
 
 extern "C" WispError wisp_b200_ep_recv_plan(const uint8_t* d_recv, int world, int e_loc, int cap,
-                                            int top_k, int hidden, WispSegment* d_segs,
-                                            int* d_src_pos, float* d_weight, int* d_total,
-                                            cudaStream_t stream, WispErrCtx* err) {
+                                            int top_k, int hidden, int own_rows,
+                                            WispSegment* d_segs, int* d_src_pos, float* d_weight,
+                                            int* d_total, cudaStream_t stream, WispErrCtx* err) {
   if (!d_recv || !d_segs || !d_src_pos || !d_weight || !d_total)
     return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_recv_plan: null pointer argument");
-  if (bad_shape(world, e_loc, cap, top_k, hidden))
+  if (bad_shape(world, e_loc, cap, top_k, hidden) || own_rows < 0 || own_rows > cap)
     return WB_FAIL(WISP_ERR_INVALID_ARG,
-                   "ep_recv_plan: world=%d e_loc=%d cap=%d top_k=%d hidden=%d (world*e_loc <= 1024)",
-                   world, e_loc, cap, top_k, hidden);
+                   "ep_recv_plan: world=%d e_loc=%d cap=%d top_k=%d hidden=%d own_rows=%d "
+                   "(world*e_loc <= 1024, own_rows <= cap)",
+                   world, e_loc, cap, top_k, hidden, own_rows);
   const Layout L = ep_layout(hidden, e_loc, cap, top_k, 2);
-  wb::launch_k(ep_recv_plan_kernel, 1, 1024, 0, stream, d_recv, world, e_loc, top_k, L, d_segs,
-               d_src_pos, d_weight, d_total);
+  wb::launch_k(ep_recv_plan_kernel, 1, 1024, 0, stream, d_recv, world, e_loc, top_k, L, own_rows,
+               d_segs, d_src_pos, d_weight, d_total);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
 
 extern "C" WispError wisp_b200_ep_gather_rows(const uint8_t* d_recv, int world, int e_loc, int cap,
                                              int top_k, int hidden, const int* d_src_pos,
-                                             const int* d_total, int max_rows, uint16_t* d_sorted,
+                                             const int* d_total, const uint16_t* d_own,
+                                             int own_rows, int max_rows, uint16_t* d_sorted,
                                              cudaStream_t stream, WispErrCtx* err) {
-  if (!d_recv || !d_src_pos || !d_total || !d_sorted)
+  if (!d_recv || !d_src_pos || !d_total || !d_sorted || (own_rows > 0 && !d_own))
     return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_gather_rows: null pointer argument");
-  if (bad_shape(world, e_loc, cap, top_k, hidden) || max_rows < 0 ||
-      (((uintptr_t)d_recv | (uintptr_t)d_sorted) & 15))
-    return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_gather_rows: hidden=%d max_rows=%d (16-byte aligned rows)",
-                   hidden, max_rows);
+  if (bad_shape(world, e_loc, cap, top_k, hidden) || max_rows < 0 || own_rows < 0 ||
+      own_rows > cap || (((uintptr_t)d_recv | (uintptr_t)d_sorted | (uintptr_t)d_own) & 15))
+    return WB_FAIL(WISP_ERR_INVALID_ARG,
+                   "ep_gather_rows: hidden=%d max_rows=%d own_rows=%d (16-byte aligned rows)",
+                   hidden, max_rows, own_rows);
   if (max_rows == 0) return WISP_OK;
   const Layout L = ep_layout(hidden, e_loc, cap, top_k, 2);
-  wb::launch_k(ep_gather_kernel, max_rows, 128, 0, stream, d_recv, L, hidden, d_src_pos, d_total,
-               d_sorted);
+  wb::launch_k(ep_gather_kernel, max_rows, 128, 0, stream, d_recv, L, hidden, world, d_src_pos,
+               d_total, d_own, own_rows, d_sorted);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
@@ -421,23 +454,24 @@ extern "C" WispError wisp_b200_ep_combine(const float* d_yback, const int* d_slo
                    tokens, cap, hidden);
   if (tokens == 0) return WISP_OK;
   wb::launch_k(ep_combine_kernel<float>, dim3(tokens, (hidden + 1023) / 1024), 256, 0, stream,
-               d_yback, d_slot, world, cap, hidden, d_out);
+               d_yback, d_slot, static_cast<const float*>(nullptr), world, cap, hidden, d_out);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
 
 extern "C" WispError wisp_b200_ep_combine_f16(const uint16_t* d_yback, const int* d_slot,
-                                             int tokens, int world, int cap, int hidden,
-                                             float* d_out, cudaStream_t stream, WispErrCtx* err) {
+                                             const float* d_local, int tokens, int world, int cap,
+                                             int hidden, float* d_out, cudaStream_t stream,
+                                             WispErrCtx* err) {
   if (!d_yback || !d_slot || !d_out)
     return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_combine_f16: null pointer argument");
   if (world < 1 || world > kMaxWorld || cap < 1 || tokens < 0 || tokens > cap || hidden % 4 ||
-      ((uintptr_t)d_yback & 7) || ((uintptr_t)d_out & 15))
+      ((uintptr_t)d_yback & 7) || (((uintptr_t)d_out | (uintptr_t)d_local) & 15))
     return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_combine_f16: world=%d tokens=%d cap=%d hidden=%d",
                    world, tokens, cap, hidden);
   if (tokens == 0) return WISP_OK;
   wb::launch_k(ep_combine_kernel<__half>, dim3(tokens, (hidden + 1023) / 1024), 256, 0, stream,
-               reinterpret_cast<const __half*>(d_yback), d_slot, world, cap, hidden, d_out);
+               reinterpret_cast<const __half*>(d_yback), d_slot, d_local, world, cap, hidden, d_out);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }

@@ -14,12 +14,14 @@ trip between routing and the expert FFN):
   route own tokens -> plan (rows grouped by expert) -> one fixed-size block
   per destination rank: a token's row once per destination that owns any of
   its experts, plus the (row, weight) entries of its experts there
-  (wisp_b200_ep_dispatch) -> all_to_all of the blocks, meanwhile the shared
-  expert on own tokens -> gather the received rows expert-contiguous (one
-  segment per local expert, as on one GPU) -> grouped FFN in mode 0 with the
-  routing weights, into one fp32 row per received token -> those rows
-  rounded to fp16 and sent back with one all_to_all -> each token adds its
-  rows from the owners, in rank order.
+  (wisp_b200_ep_dispatch) -> all_to_all of the blocks, meanwhile the rank's
+  own rows are packed -> gather the received rows expert-contiguous (one
+  segment per local expert, as on one GPU), the own rows after them as the
+  shared expert's segment -> one grouped FFN in mode 0 with the routing
+  weights, into one fp32 row per received token (and one per own token for
+  the shared expert) -> the return rows rounded to fp16 and sent back with
+  one all_to_all -> out[t] = the shared expert's row + the rows from the
+  owners, in rank order.
 cap = the most tokens any rank holds (a token fills at most one row of a
 block); padding rows are exchanged but never computed or read.
 
@@ -139,13 +141,16 @@ class CudaOps:
                  idx.shape[1], plan_segs.data_ptr(), row_token.data_ptr(), row_weight.data_ptr(),
                  n_experts, world, cap, send.data_ptr(), slot.data_ptr(), _stream())
 
-    def recv_plan(self, recv, world, e_loc, cap, k, hidden, segs, src_pos, weight, total):
-        abi.call("wisp_b200_ep_recv_plan", recv.data_ptr(), world, e_loc, cap, k, hidden,
+    def recv_plan(self, recv, world, e_loc, cap, k, hidden, own, segs, src_pos, weight, total):
+        abi.call("wisp_b200_ep_recv_plan", recv.data_ptr(), world, e_loc, cap, k, hidden, own,
                  segs.data_ptr(), src_pos.data_ptr(), weight.data_ptr(), total.data_ptr(), _stream())
 
-    def gather_rows(self, recv, world, e_loc, cap, k, hidden, src_pos, total, max_rows, sorted_rows):
+    def gather_rows(self, recv, world, e_loc, cap, k, hidden, src_pos, total, own_rows, own,
+                    max_rows, sorted_rows):
         abi.call("wisp_b200_ep_gather_rows", recv.data_ptr(), world, e_loc, cap, k, hidden,
-                 src_pos.data_ptr(), total.data_ptr(), max_rows, sorted_rows.data_ptr(), _stream())
+                 src_pos.data_ptr(), total.data_ptr(),
+                 None if own_rows is None else own_rows.data_ptr(), own, max_rows,
+                 sorted_rows.data_ptr(), _stream())
 
     def grouped_dev(self, cfg, lw, segs, n_segs, rows, xp, h, mode, row_token, row_weight, out,
                     ws, flag):
@@ -167,9 +172,10 @@ class CudaOps:
     def check_flag(self, flag):
         abi.call("wisp_b200_check_error_flag", flag.data_ptr(), _stream())
 
-    def ep_combine(self, yback, slot, tokens, world, cap, out):
-        abi.call("wisp_b200_ep_combine_f16", yback.data_ptr(), slot.data_ptr(), tokens, world, cap,
-                 out.shape[1], out.data_ptr(), _stream())
+    def ep_combine(self, yback, slot, local, tokens, world, cap, out):
+        abi.call("wisp_b200_ep_combine_f16", yback.data_ptr(), slot.data_ptr(),
+                 None if local is None else local.data_ptr(), tokens, world, cap, out.shape[1],
+                 out.data_ptr(), _stream())
 
     def return_rows(self, yr, yr16):
         abi.call("wisp_b200_ep_return_rows", yr.data_ptr(), yr.shape[0], yr.shape[1],
@@ -236,33 +242,32 @@ class EpLayer:
         self.layout = self.ops.block_layout(M, self.e_loc, self.cap, k)
         nb = self.layout.bytes
         RK = world * self.cap * k          # most (token, local expert) rows received
-        self.rk = RK
+        # The shared expert runs in the same grouped call as the local experts:
+        # this rank's own T token rows follow the received rows as one more
+        # segment, and its output rows follow the return rows in yr.
+        self.own = T if spec.has_shared else 0
+        self.rk = RK + self.own
         self.slot = torch.empty((T, world), dtype=torch.int32, device=dev)
         self.send = torch.zeros(world * nb, dtype=torch.uint8, device=dev)
         self.recv = torch.zeros(world * nb, dtype=torch.uint8, device=dev)
-        self.xsorted = torch.empty((RK, M), dtype=adt, device=dev)
-        self.hr = torch.empty((max(RK, T), I), dtype=adt, device=dev)
-        # return rows: fp32 where the FFN accumulates them, then in the
-        # exchange dtype (fp16 on GPUs) for the trip back
-        self.yr = torch.empty((world * self.cap, M), dtype=torch.float32, device=dev)
-        self.yr16 = torch.empty((world * self.cap, M), dtype=self.ops.ret_dtype(), device=dev)
-        self.yback = torch.empty((world * self.cap, M), dtype=self.ops.ret_dtype(), device=dev)
-        self.src_pos = torch.empty(RK, dtype=torch.int32, device=dev)
-        self.gw = torch.empty(RK, dtype=torch.float32, device=dev)
+        self.xsorted = torch.empty((self.rk, M), dtype=adt, device=dev)
+        self.hr = torch.empty((self.rk, I), dtype=adt, device=dev)
+        # return rows (then the shared expert's own rows): fp32 where the FFN
+        # accumulates them, the return rows then in the exchange dtype (fp16
+        # on GPUs) for the trip back
+        nret = world * self.cap
+        self.yr = torch.empty((nret + self.own, M), dtype=torch.float32, device=dev)
+        self.yr_ret = self.yr[:nret]
+        self.yr_own = self.yr[nret:] if self.own else None
+        self.yr16 = torch.empty((nret, M), dtype=self.ops.ret_dtype(), device=dev)
+        self.yback = torch.empty((nret, M), dtype=self.ops.ret_dtype(), device=dev)
+        self.src_pos = torch.empty(self.rk, dtype=torch.int32, device=dev)
+        self.gw = torch.empty(self.rk, dtype=torch.float32, device=dev)
         self.total = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.n_rsegs = self.e_loc
+        self.n_rsegs = self.e_loc + (1 if self.own else 0)
         self.rsegs = torch.empty(16 * self.n_rsegs, dtype=torch.uint8, device=dev)
-        # one grouped-FFN workspace serves both calls of a layer (the shared
-        # expert's single segment of T rows, then the local experts)
-        self.gws = self.ops.workspace(self.cfg_loc, max(self.n_rsegs, 1), max(RK, T), dev)
-        if spec.has_shared:
-            self.xs = torch.empty((T, M), dtype=adt, device=dev)
-            self.sh_token = torch.arange(T, dtype=torch.int32, device=dev)
-            self.sh_weight = torch.ones(T, dtype=torch.float32, device=dev)
-            self.sh_seg = torch.empty(16, dtype=torch.uint8, device=dev)
-            seg = abi.WispSegment()
-            seg.expert, seg.row_begin, seg.rows = self.e_loc, 0, T
-            self.sh_seg.copy_(torch.frombuffer(bytearray(bytes(seg)), dtype=torch.uint8))
+        self.gws = self.ops.workspace(self.cfg_loc, max(self.n_rsegs, 1), self.rk, dev)
+        self.xs = torch.empty((T, M), dtype=adt, device=dev) if self.own else None
 
     # One layer is four local phases around two all-to-alls; forward() runs
     # them over the process group, and a single-process caller can run the
@@ -270,8 +275,8 @@ class EpLayer:
     # (loopback_forward).
 
     def dispatch_phase(self, x: torch.Tensor, out: torch.Tensor) -> None:
-        """Route this rank's tokens and fill the send blocks; zero the output
-        and the device error word."""
+        """Route this rank's tokens and fill the send blocks; clear the device
+        error word."""
         spec, ops = self.spec, self.ops
         ops.clear_flag(self.flag)
         ops.route(self.cfg_route, self.lw, x, self.idx, self.w, self.route_scratch)
@@ -279,57 +284,64 @@ class EpLayer:
                  self.row_weight)
         ops.dispatch(x, self.idx, self.segs, self.row_token, self.row_weight, spec.n_experts,
                      self.world, self.cap, self.send, self.slot)
-        out.zero_()
 
-    def shared_phase(self, x: torch.Tensor, out: torch.Tensor) -> None:
-        """The shared expert on this rank's own tokens, added into out."""
-        if self.spec.has_shared:
-            T = self.T
-            self.ops.pack(x, None, T, self.xs)
-            self.ops.grouped_dev(self.cfg_loc, self.lw, self.sh_seg, 1, T, self.xs, self.hr, 0,
-                                 self.sh_token, self.sh_weight, out, self.gws, self.flag)
+    def own_phase(self, x: torch.Tensor) -> None:
+        """This rank's own token rows in the FFN's input form, for the shared
+        expert's segment (runs while the blocks travel)."""
+        if self.own:
+            self.ops.pack(x, None, self.T, self.xs)
 
     def expert_phase(self, mark=None) -> None:
         """Local experts over the received rows, gathered so that each expert
-        is one segment; the FFN adds w * y of every local expert of a received
-        token into that token's fp32 return row. ``mark(name)``, if given, is
-        called after the receive plan and gather."""
+        is one segment, and the shared expert over this rank's own rows as one
+        more segment, in one grouped call: the FFN adds w * y of every local
+        expert of a received token into that token's fp32 return row, and the
+        shared expert's output of own token t into row world * cap + t.
+        ``mark(name)``, if given, is called after the receive plan and
+        gather."""
         ops, k, M = self.ops, self.spec.top_k, self.spec.hidden
-        ops.recv_plan(self.recv, self.world, self.e_loc, self.cap, k, M, self.rsegs, self.src_pos,
-                      self.gw, self.total)
+        ops.recv_plan(self.recv, self.world, self.e_loc, self.cap, k, M, self.own, self.rsegs,
+                      self.src_pos, self.gw, self.total)
         ops.gather_rows(self.recv, self.world, self.e_loc, self.cap, k, M, self.src_pos, self.total,
-                        self.rk, self.xsorted)
+                        self.xs, self.own, self.rk, self.xsorted)
         if mark:
             mark("gather")
         self.yr.zero_()
         ops.grouped_dev(self.cfg_loc, self.lw, self.rsegs, self.n_rsegs, self.rk, self.xsorted,
                         self.hr, 0, self.src_pos, self.gw, self.yr, self.gws, self.flag)
-        ops.return_rows(self.yr, self.yr16)
+        ops.return_rows(self.yr_ret, self.yr16)
 
     def combine_phase(self, out: torch.Tensor) -> None:
-        """Each token adds its returned rows from the owners, in rank order."""
-        self.ops.ep_combine(self.yback, self.slot, self.T, self.world, self.cap, out)
+        """out = the shared expert's row (if any) + the returned rows from the
+        owners, in rank order."""
+        if self.own:
+            self.ops.ep_combine(self.yback, self.slot, self.yr_own, self.T, self.world, self.cap,
+                                out)
+        else:
+            out.zero_()
+            self.ops.ep_combine(self.yback, self.slot, None, self.T, self.world, self.cap, out)
 
     def forward(self, x: torch.Tensor, out: torch.Tensor, mark=None) -> torch.Tensor:
         """x: bf16 [T, M] (this rank's tokens) -> out fp32 [T, M].
 
         ``mark(name)``, if given, is called on the host after each phase has
         been issued (for per-phase CUDA events on the current stream): after
-        route + plan + dispatch ("dispatch"), the shared expert ("shared"),
+        route + plan + dispatch ("dispatch"), the own rows' pack ("own_rows"),
         the wait for the first exchange ("exchange"), the receive plan and
-        gather ("gather"), the local experts' FFN ("ffn"), the return exchange
-        ("return") and the combine ("combine")."""
+        gather ("gather"), the FFN of the local and shared experts ("ffn"), the
+        return exchange ("return") and the combine ("combine")."""
         m = mark or (lambda name: None)
         self.dispatch_phase(x, out)
         m("dispatch")
-        # 1. the blocks to the owners; the shared expert runs on this rank's
-        #    own tokens while they travel
+        # 1. the blocks to the owners; this rank's own rows are packed for
+        #    the shared expert while they travel
         w_rows = dist.all_to_all_single(self.recv, self.send, group=self.group, async_op=True)
-        self.shared_phase(x, out)
-        m("shared")
+        self.own_phase(x)
+        m("own_rows")
         w_rows.wait()
         m("exchange")
-        # 2. local experts over the received rows
+        # 2. local experts over the received rows and the shared expert over
+        #    the own rows, one grouped call
         self.expert_phase(mark)
         m("ffn")
         # 3. the rows back to their tokens' ranks, added in rank order
@@ -360,7 +372,7 @@ def loopback_forward(layers: list, xs: list, outs: list) -> None:
         for q in range(W):
             layers[q].recv[r * nb:(r + 1) * nb].copy_(layers[r].send[q * nb:(q + 1) * nb])
     for r in range(W):
-        layers[r].shared_phase(xs[r], outs[r])
+        layers[r].own_phase(xs[r])
     for r in range(W):
         layers[r].expert_phase()
     cap = layers[0].cap
