@@ -401,7 +401,7 @@ def ep_phase_report(layers, xs, outs, step_eager, spec, T, L, world, dev, reps: 
     rows, touched = [], []
     for lay in layers:
         r = lay.total.to(torch.int64).reshape(1)
-        seg = lay.rsegs.view(torch.int32).reshape(-1, 4)
+        seg = lay.rsegs.view(torch.int32).reshape(-1, 4)[:lay.e_loc]   # routed experts only
         u = (seg[:, 2] > 0).to(torch.int64).sum().reshape(1)
         rr = [torch.empty_like(r) for _ in range(world)]
         uu = [torch.empty_like(u) for _ in range(world)]
