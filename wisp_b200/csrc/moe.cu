@@ -25,7 +25,8 @@ WispError launch_route(const WispMoeConfig* c, const uint16_t* x, const uint16_t
                        float* w, cudaStream_t st, WispErrCtx* err);
 WispError launch_plan(const WispMoeConfig* c, const int* idx, const float* w, int* counts,
                       WispSegment* segs, int* row_token, float* row_weight, cudaStream_t st,
-                      WispErrCtx* err);
+                      WispErrCtx* err, int* scratch);
+size_t plan_scratch_ints(const WispMoeConfig* c);
 WispError launch_pack(const uint16_t* x, const int* src, int n_rows, int M, uint16_t* xp,
                       cudaStream_t st, WispErrCtx* err);
 WispError launch_pack_q16(const uint16_t* x, const int* src, int n_rows, int M, uint16_t* xp,
@@ -67,6 +68,7 @@ struct Carve {
 
 struct Workspace {
   float* part;
+  int* plan_scratch;
   int* idx;
   float* w;
   int* counts;
@@ -91,6 +93,7 @@ Workspace carve(const WispMoeConfig* c, void* base) {
   ws.rows = T * k + (c->has_shared ? T : 0);
   ws.splits = wb::router_splits(T, E, M);
   ws.part = cv.take<float>(base, ws.splits * (size_t)T * E);
+  ws.plan_scratch = cv.take<int>(base, std::max<size_t>(1, wb::plan_scratch_ints(c)));
   ws.idx = cv.take<int>(base, (size_t)T * k);
   ws.w = cv.take<float>(base, (size_t)T * k);
   ws.counts = cv.take<int>(base, V);
@@ -223,7 +226,8 @@ extern "C" WispError wisp_b200_moe_forward(const WispMoeConfig* cfg, const WispM
   e = wb::launch_route(cfg, d_x, w->router_w, w->router_bias, ws.part, ws.splits, nullptr, idx, wt,
                        stream, err);
   if (e != WISP_OK) return e;
-  e = wb::launch_plan(cfg, idx, wt, ws.counts, ws.segs, ws.row_token, ws.row_weight, stream, err);
+  e = wb::launch_plan(cfg, idx, wt, ws.counts, ws.segs, ws.row_token, ws.row_weight, stream, err,
+                      ws.plan_scratch);
   if (e != WISP_OK) return e;
   // The gathered rows in the operand form of the kernel their segment runs
   // on: fp16 for the tensor-core kernel, q16 (into the grouped workspace) for

@@ -477,11 +477,12 @@ __device__ __forceinline__ void topk_token(const float* __restrict__ part, int s
   }
 }
 
-// Block of kTopkTok tokens x kTopkQ warps: with split-K partials, warp q of
-// a token sums splits q, q + kTopkQ, ... (loads of a split in flight
-// together) and the token's warp 0 adds the kTopkQ sums in order, so a
-// token waits for ceil(splits / kTopkQ) L2 round trips, not splits; warp 0
-// then routes the token.
+// Block of kTopkTok tokens x Q warps (Q = blockDim.x / (32 kTopkTok), at
+// most kTopkQ): with split-K partials, warp q of a token sums splits q, q +
+// Q, ... (loads of a split in flight together) and the token's warp 0 adds
+// the Q sums in order, so a token waits for ceil(splits / Q) L2 round trips,
+// not splits; warp 0 then routes the token. The launch picks Q = 1 for few
+// splits (many tokens) and kTopkQ for many.
 constexpr int kTopkTok = 2, kTopkQ = 4;
 
 template <int PER>
@@ -491,15 +492,16 @@ __global__ void __launch_bounds__(kTopkTok * kTopkQ * 32) topk_kernel(
     float* __restrict__ wout, float* __restrict__ logits_out) {
   __shared__ float sums[kTopkTok][kTopkQ][PER * 32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tw = warp / kTopkQ, q = warp % kTopkQ;
+  const int Q = blockDim.x / (32 * kTopkTok);
+  const int tw = warp / Q, q = warp % Q;
   const int t = blockIdx.x * kTopkTok + tw;
   const int per = (E + 31) / 32;
-  if (splits > 1) {
+  if (splits > 1 && Q > 1) {
     if (t < T) {
       float v[PER];
 #pragma unroll
       for (int j = 0; j < PER; j++) v[j] = 0.f;
-      for (int z = q; z < splits; z += kTopkQ) {
+      for (int z = q; z < splits; z += Q) {
         const float* pz = part + ((size_t)z * T + t) * E;
 #pragma unroll
         for (int j = 0; j < PER; j++) {
@@ -515,7 +517,7 @@ __global__ void __launch_bounds__(kTopkTok * kTopkQ * 32) topk_kernel(
 #pragma unroll
       for (int j = 0; j < PER; j++) {
         float a = sums[tw][0][lane + 32 * j];
-        for (int qq = 1; qq < kTopkQ; qq++) a += sums[tw][qq][lane + 32 * j];
+        for (int qq = 1; qq < Q; qq++) a += sums[tw][qq][lane + 32 * j];
         sums[tw][0][lane + 32 * j] = a;
       }
     }
@@ -523,7 +525,7 @@ __global__ void __launch_bounds__(kTopkTok * kTopkQ * 32) topk_kernel(
   }
   if (q != 0 || t >= T) return;
   topk_token<PER>(part, splits, bias, T, t, E, k, scoring, n_groups, topk_groups, scaling, idx,
-                  wout, logits_out, lane, splits > 1 ? &sums[tw][0][0] : nullptr);
+                  wout, logits_out, lane, (splits > 1 && Q > 1) ? &sums[tw][0][0] : nullptr);
 }
 
 // One block of kPlanWarps warps per expert v: warp w scans the w-th
@@ -656,6 +658,7 @@ __global__ void __launch_bounds__(kPlanWarps * 32) fill_kernel(
 // before it inside the chunk (per-warp counts, then ranks within each
 // 32-slot group).
 constexpr int kPlanMaxV = 1025;
+constexpr int kChunkedPlanMin = 8192;   // slots above which the chunked plan runs
 constexpr int kFillWarps = 8;
 
 __device__ __forceinline__ void count_groups(int e, int lane, int* cnt) {
@@ -721,10 +724,13 @@ __global__ void __launch_bounds__(1024) count_segments_kernel(const int* __restr
   }
 }
 
+// With `base` (the chunked plan), base[blockIdx.x * E + v] is the first row
+// of expert v's rows from this chunk (segment start + the expert's matches in
+// earlier chunks) and the scan of the earlier slots is skipped.
 __global__ void __launch_bounds__(kFillWarps * 32) fill_ordered_kernel(
     const int* __restrict__ idx, const float* __restrict__ w, int nslots, int chunk, int k, int E,
     int T, int V, const WispSegment* __restrict__ segs, int* __restrict__ row_token,
-    float* __restrict__ row_weight) {
+    float* __restrict__ row_weight, const int* __restrict__ base) {
   __shared__ int before[kPlanMaxV];
   __shared__ int wcnt[kFillWarps][kPlanMaxV];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -746,7 +752,7 @@ __global__ void __launch_bounds__(kFillWarps * 32) fill_ordered_kernel(
   }
   __syncthreads();
   // matches before the chunk (c0 is a multiple of the block size)
-  for (int s = threadIdx.x; s < c0; s += blockDim.x) {
+  for (int s = threadIdx.x; s < (base ? 0 : c0); s += blockDim.x) {
     int e = __ldg(idx + s);
     if (e >= E) e = -1;
     count_groups(e, lane, before);
@@ -763,7 +769,7 @@ __global__ void __launch_bounds__(kFillWarps * 32) fill_ordered_kernel(
   __syncthreads();
   // first row of each (warp, expert) run
   for (int v = threadIdx.x; v < E; v += blockDim.x) {
-    int run = segs[v].row_begin + before[v];
+    int run = base ? __ldg(base + (size_t)blockIdx.x * E + v) : segs[v].row_begin + before[v];
 #pragma unroll
     for (int q = 0; q < kFillWarps; q++) {
       const int t = wcnt[q][v];
@@ -786,6 +792,90 @@ __global__ void __launch_bounds__(kFillWarps * 32) fill_ordered_kernel(
       if (rank == 0) wcnt[warp][e] = base + __popc(m);
     }
     __syncwarp();
+  }
+}
+
+// Chunked plan for many slots (prefill): one block per chunk of kChunkSlots
+// slots counts its chunk per expert; one block then turns the counts into
+// the segments and, per chunk and expert, the first row of the chunk's
+// matches; fill_ordered_kernel places the rows with those bases. Three
+// launches, each one pass over its data, instead of every fill block
+// rescanning all slots before its chunk.
+constexpr int kChunkSlots = 1024;
+
+__global__ void __launch_bounds__(kChunkSlots) chunk_count_kernel(const int* __restrict__ idx,
+                                                                  int nslots, int E,
+                                                                  int* __restrict__ ccount) {
+  __shared__ int cnt[kPlanMaxV];
+  for (int v = threadIdx.x; v < E; v += blockDim.x) cnt[v] = 0;
+  __syncthreads();
+  const int s = blockIdx.x * kChunkSlots + threadIdx.x;
+  int e = s < nslots ? __ldg(idx + s) : -1;
+  if (e >= E) e = -1;
+  count_groups(e, threadIdx.x & 31, cnt);
+  __syncthreads();
+  for (int v = threadIdx.x; v < E; v += blockDim.x) ccount[(size_t)blockIdx.x * E + v] = cnt[v];
+}
+
+// One block: totals per expert (chunk order), segments by a block scan (the
+// shared expert, v = E, holds every token), then the per-chunk bases, in
+// place of the counts.
+__global__ void __launch_bounds__(1024) chunk_scan_kernel(int* __restrict__ ccount, int nchunk,
+                                                          int E, int T, int V,
+                                                          int* __restrict__ counts,
+                                                          WispSegment* __restrict__ segs) {
+  __shared__ int warp_tot[32];
+  __shared__ int carry;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (int b0 = 0; b0 < V; b0 += blockDim.x) {
+    const int v = b0 + threadIdx.x;
+    int n = 0;
+    if (v < E) {
+      for (int c = 0; c < nchunk; c++) n += ccount[(size_t)c * E + v];
+    } else if (v < V) {
+      n = T;
+    }
+    int x = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_tot[w] = x;
+    __syncthreads();
+    if (w == 0) {
+      int tv = lane < (int)(blockDim.x >> 5) ? warp_tot[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, tv, o);
+        if (lane >= o) tv += y;
+      }
+      warp_tot[lane] = tv;
+    }
+    __syncthreads();
+    const int begin = x + (w > 0 ? warp_tot[w - 1] : 0) + carry - n;
+    if (v < V) {
+      WispSegment sg;
+      sg.expert = v;
+      sg.row_begin = begin;
+      sg.rows = n;
+      sg.reserved = 0;
+      segs[v] = sg;
+      counts[v] = n;
+    }
+    if (v < E) {   // chunk bases: the expert's first row of each chunk's matches
+      int run = begin;
+      for (int c = 0; c < nchunk; c++) {
+        const int m = ccount[(size_t)c * E + v];
+        ccount[(size_t)c * E + v] = run;
+        run += m;
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = begin + n;
+    __syncthreads();
   }
 }
 
@@ -1308,28 +1398,45 @@ WispError launch_route(const WispMoeConfig* c, const uint16_t* x, const uint16_t
   }
   auto topk = E <= 32 ? topk_kernel<1> : E <= 64 ? topk_kernel<2> : E <= 128 ? topk_kernel<4>
             : E <= 256 ? topk_kernel<8> : E <= 512 ? topk_kernel<16> : topk_kernel<32>;
-  // two tokens per block (four warps each), so a few hundred tokens still
-  // spread over the SMs
-  wb::launch_k(topk, (T + kTopkTok - 1) / kTopkTok, kTopkTok * kTopkQ * 32, 0, st, part, nsplit,
+  // two tokens per block, so a few hundred tokens still spread over the
+  // SMs; four warps per token to sum many splits
+  const int q = nsplit > 2 ? kTopkQ : 1;
+  wb::launch_k(topk, (T + kTopkTok - 1) / kTopkTok, kTopkTok * q * 32, 0, st, part, nsplit,
                bias, T, E, c->top_k, c->scoring, c->n_groups, c->topk_groups, c->routed_scaling,
                idx, w, logits_out);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }
 
+// Scratch of the chunked plan (ints), 0 when the two-launch plan is used.
+size_t plan_scratch_ints(const WispMoeConfig* c) {
+  const int nslots = c->tokens * c->top_k;
+  const int V = c->n_experts + (c->has_shared ? 1 : 0);
+  if (nslots <= kChunkedPlanMin || V > kPlanMaxV) return 0;
+  return (size_t)((nslots + kChunkSlots - 1) / kChunkSlots) * c->n_experts;
+}
+
 WispError launch_plan(const WispMoeConfig* c, const int* idx, const float* w, int* counts,
                       WispSegment* segs, int* row_token, float* row_weight, cudaStream_t st,
-                      WispErrCtx* err) {
+                      WispErrCtx* err, int* scratch) {
   const int T = c->tokens, E = c->n_experts, k = c->top_k, sh = c->has_shared ? 1 : 0;
   const int V = E + sh;
   const int nslots = T * k;
-  if (V <= kPlanMaxV) {
+  if (scratch && plan_scratch_ints(c) > 0) {
+    const int nchunk = (nslots + kChunkSlots - 1) / kChunkSlots;
+    wb::launch_k(chunk_count_kernel, nchunk, kChunkSlots, 0, st, idx, nslots, E, scratch);
+    wb::launch_k(chunk_scan_kernel, 1, 1024, 0, st, scratch, nchunk, E, T, V, counts, segs);
+    wb::launch_k(fill_ordered_kernel, nchunk, kFillWarps * 32, 0, st, idx, w, nslots,
+                 kChunkSlots, k, E, T, V, segs, row_token, row_weight,
+                 static_cast<const int*>(scratch));
+  } else if (V <= kPlanMaxV) {
     // chunks of 1024 slots, larger for large batches so that at most 32
     // blocks count the slots before their chunk
     const int chunk = 1024 * std::max(1, (nslots + 32 * 1024 - 1) / (32 * 1024));
     wb::launch_k(count_segments_kernel, 1, 1024, 0, st, idx, nslots, E, T, V, counts, segs);
     wb::launch_k(fill_ordered_kernel, (nslots + chunk - 1) / chunk, kFillWarps * 32, 0, st, idx, w,
-                 nslots, chunk, k, E, T, V, segs, row_token, row_weight);
+                 nslots, chunk, k, E, T, V, segs, row_token, row_weight,
+                 static_cast<const int*>(nullptr));
   } else {
     wb::launch_k(count_kernel, V, kPlanWarps * 32, 0, st, idx, nslots, E, T, counts);
     wb::launch_k(segments_kernel, 1, 1024, 0, st, counts, V, segs);
@@ -1450,7 +1557,8 @@ extern "C" WispError wisp_b200_dispatch_plan(const WispMoeConfig* cfg, const int
   if (cfg->tokens <= 0 || cfg->top_k <= 0 || cfg->n_experts <= 0)
     return WB_FAIL(WISP_ERR_INVALID_ARG, "dispatch_plan: tokens=%d top_k=%d n_experts=%d",
                    cfg->tokens, cfg->top_k, cfg->n_experts);
-  return wb::launch_plan(cfg, d_idx, d_w, d_counts, d_segs, d_row_token, d_row_weight, stream, err);
+  return wb::launch_plan(cfg, d_idx, d_w, d_counts, d_segs, d_row_token, d_row_weight, stream, err,
+                         nullptr);
 }
 
 extern "C" WispError wisp_b200_rms_rescale(const float* d_in, uint16_t* d_out, int tokens,
