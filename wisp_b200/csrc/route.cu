@@ -1009,10 +1009,9 @@ __global__ void __launch_bounds__(128) pack_rows_q16_kernel(const uint16_t* __re
 //      shared expert holding every token;
 //   3. the rows: slot s of expert e lands at begin[e] + (earlier slots of e),
 //      so each expert's rows are in token order, as in the general plan;
-//   4. every row's q16 row copied from its token's (coalesced 16-byte
-//      stores);
-//   5. the register path's unit plans for gate/up and down, from the
-//      segments in shared memory.
+//   4. the register path's unit plans for gate/up and down, one warp each,
+//      from the segments in shared memory, while the other warps copy every
+//      row's q16 row from its token's (coalesced 16-byte stores).
 // Every segment has at most T <= 4 rows, so all of them run on the register
 // path and no fp16 rows or tensor-core plans are needed.
 // ---------------------------------------------------------------------------
@@ -1298,17 +1297,21 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const DecodePlan p) {
     }
   }
   __syncthreads();
-  // 4. each row's q16 row from its token's
-  const int wpr = (int)(qbytes / 16);   // 16-byte words per q16 row
-  for (int row = 0; row < rows; row++) {
-    const uint4* src = reinterpret_cast<const uint4*>(s_q16 + (size_t)s_tok[row] * qbytes);
-    uint4* dst = reinterpret_cast<uint4*>(p.xq + (size_t)row * qbytes);
-    for (int wd = tid; wd < wpr; wd += blockDim.x) dst[wd] = src[wd];
+  // 4. the unit plans on warps 0 and 1 (segments read from shared memory)
+  // while the other warps copy each row's q16 row from its token's
+  if (warp == 0) {
+    plan_units_warp(s_segs, V, p.per_gu, p.cols, p.sk_rows, 1, 1, 0, p.units_gu, lane);
+  } else if (warp == 1) {
+    plan_units_warp(s_segs, V, p.per_dn, p.cols, p.sk_rows, p.ks_dn, p.nk_dn, p.target,
+                    p.units_dn, lane);
+  } else {
+    const int wpr = (int)(qbytes / 16);   // 16-byte words per q16 row
+    for (int row = 0; row < rows; row++) {
+      const uint4* src = reinterpret_cast<const uint4*>(s_q16 + (size_t)s_tok[row] * qbytes);
+      uint4* dst = reinterpret_cast<uint4*>(p.xq + (size_t)row * qbytes);
+      for (int wd = tid - 64; wd < wpr; wd += blockDim.x - 64) dst[wd] = src[wd];
+    }
   }
-  // 5. unit plans (segments read from shared memory)
-  plan_units(s_segs, V, p.per_gu, p.cols, p.sk_rows, 1, 1, 0, p.units_gu);
-  __syncthreads();
-  plan_units(s_segs, V, p.per_dn, p.cols, p.sk_rows, p.ks_dn, p.nk_dn, p.target, p.units_dn);
 }
 
 // y[t] = bf16(x[t] / rms(x[t])): per-token RMS normalisation (no weight)
