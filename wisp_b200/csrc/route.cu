@@ -477,31 +477,30 @@ __device__ __forceinline__ void topk_token(const float* __restrict__ part, int s
   }
 }
 
-// Block of kTopkTok tokens x Q warps (Q = blockDim.x / (32 kTopkTok), at
-// most kTopkQ): with split-K partials, warp q of a token sums splits q, q +
-// Q, ... (loads of a split in flight together) and the token's warp 0 adds
-// the Q sums in order, so a token waits for ceil(splits / Q) L2 round trips,
-// not splits; warp 0 then routes the token. The launch picks Q = 1 for few
-// splits (many tokens) and kTopkQ for many.
-constexpr int kTopkTok = 2, kTopkQ = 4;
+// Block of 64 threads = two tokens x one warp, or, for many split partials,
+// of kTopkQ warps for one token: warp q sums splits q, q + kTopkQ, ...
+// (loads of a split in flight together) and warp 0 adds the kTopkQ sums in
+// order, so the token waits for ceil(splits / kTopkQ) L2 round trips, not
+// splits; warp 0 then routes the token.
+constexpr int kTopkQ = 8;
 
 template <int PER>
-__global__ void __launch_bounds__(kTopkTok * kTopkQ * 32) topk_kernel(
+__global__ void __launch_bounds__(kTopkQ * 32) topk_kernel(
     const float* __restrict__ part, int splits, const float* __restrict__ bias, int T, int E, int k,
     int scoring, int n_groups, int topk_groups, float scaling, int* __restrict__ idx,
     float* __restrict__ wout, float* __restrict__ logits_out) {
-  __shared__ float sums[kTopkTok][kTopkQ][PER * 32];
+  __shared__ float sums[kTopkQ][PER * 32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int Q = blockDim.x / (32 * kTopkTok);
-  const int tw = warp / Q, q = warp % Q;
-  const int t = blockIdx.x * kTopkTok + tw;
+  const bool split_warps = blockDim.x == kTopkQ * 32;
+  const int t = split_warps ? (int)blockIdx.x : (int)blockIdx.x * 2 + warp;
+  const int q = split_warps ? warp : 0;
   const int per = (E + 31) / 32;
-  if (splits > 1 && Q > 1) {
+  if (split_warps) {
     if (t < T) {
       float v[PER];
 #pragma unroll
       for (int j = 0; j < PER; j++) v[j] = 0.f;
-      for (int z = q; z < splits; z += Q) {
+      for (int z = q; z < splits; z += kTopkQ) {
         const float* pz = part + ((size_t)z * T + t) * E;
 #pragma unroll
         for (int j = 0; j < PER; j++) {
@@ -510,22 +509,22 @@ __global__ void __launch_bounds__(kTopkTok * kTopkQ * 32) topk_kernel(
         }
       }
 #pragma unroll
-      for (int j = 0; j < PER; j++) sums[tw][q][lane + 32 * j] = v[j];
+      for (int j = 0; j < PER; j++) sums[q][lane + 32 * j] = v[j];
     }
     __syncthreads();
     if (q == 0 && t < T) {
 #pragma unroll
       for (int j = 0; j < PER; j++) {
-        float a = sums[tw][0][lane + 32 * j];
-        for (int qq = 1; qq < Q; qq++) a += sums[tw][qq][lane + 32 * j];
-        sums[tw][0][lane + 32 * j] = a;
+        float a = sums[0][lane + 32 * j];
+        for (int qq = 1; qq < kTopkQ; qq++) a += sums[qq][lane + 32 * j];
+        sums[0][lane + 32 * j] = a;
       }
     }
     __syncwarp();
   }
   if (q != 0 || t >= T) return;
   topk_token<PER>(part, splits, bias, T, t, E, k, scoring, n_groups, topk_groups, scaling, idx,
-                  wout, logits_out, lane, (splits > 1 && Q > 1) ? &sums[tw][0][0] : nullptr);
+                  wout, logits_out, lane, split_warps ? &sums[0][0] : nullptr);
 }
 
 // One block of kPlanWarps warps per expert v: warp w scans the w-th
@@ -1401,10 +1400,11 @@ WispError launch_route(const WispMoeConfig* c, const uint16_t* x, const uint16_t
   }
   auto topk = E <= 32 ? topk_kernel<1> : E <= 64 ? topk_kernel<2> : E <= 128 ? topk_kernel<4>
             : E <= 256 ? topk_kernel<8> : E <= 512 ? topk_kernel<16> : topk_kernel<32>;
-  // two tokens per block, so a few hundred tokens still spread over the
-  // SMs; four warps per token to sum many splits
-  const int q = nsplit > 2 ? kTopkQ : 1;
-  wb::launch_k(topk, (T + kTopkTok - 1) / kTopkTok, kTopkTok * q * 32, 0, st, part, nsplit,
+  // two tokens per block (one warp each), so a few hundred tokens still
+  // spread over the SMs; kTopkQ warps per token to sum more than two splits
+  const bool split_warps = nsplit > 2;
+  wb::launch_k(topk, split_warps ? T : (T + 1) / 2, split_warps ? kTopkQ * 32 : 64, 0, st, part,
+               nsplit,
                bias, T, E, c->top_k, c->scoring, c->n_groups, c->topk_groups, c->routed_scaling,
                idx, w, logits_out);
   WB_CUDA_CHECK(cudaGetLastError());
