@@ -210,14 +210,14 @@ def layer_launches(T: int, world: int, has_shared: bool) -> int:
     FFN (one tile/unit planner, register-path gate/up and down, and, when a
     segment can exceed the 32-row routing threshold, the tensor-core gate/up
     and down). Expert-parallel: route 2 + plan 2 + dispatch 2 (slots and
-    entries, rows) + receive plan + gather + one grouped FFN 5 (local experts
-    and, over this rank's own rows, the shared expert) + fp16 return rows +
-    combine, + the own rows' pack with a shared expert."""
+    entries; rows, with the rank's own rows for the shared expert) + receive
+    plan + gather + one grouped FFN 5 (local experts and, over the own rows,
+    the shared expert) + fp16 return rows + combine."""
     if world == 1:
         if T <= 4:
             return 4
         return 5 + (5 if T > 32 else 3)
-    return 2 + 2 + 2 + 1 + 1 + 5 + 1 + 1 + (1 if has_shared else 0)
+    return 2 + 2 + 2 + 1 + 1 + 5 + 1 + 1
 
 
 # ---------------------------------------------------------------------------
@@ -337,7 +337,7 @@ def measure_side_config(name: str, steps: int, warmup: int, peaks: dict) -> dict
 # GPU arm
 # ---------------------------------------------------------------------------
 
-PHASES = ("dispatch", "own_rows", "exchange", "gather", "ffn", "return", "combine")
+PHASES = ("dispatch", "exchange", "gather", "ffn", "return", "combine")
 
 
 def ep_phase_report(layers, xs, outs, step_eager, spec, T, L, world, dev, reps: int = 5) -> dict:

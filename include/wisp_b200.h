@@ -370,11 +370,14 @@ size_t wisp_b200_ep_block_bytes(int hidden, int e_loc, int cap, int top_k);
  * [tokens x top_k], global experts) and its dispatch plan over the n_experts
  * routed experts (d_plan_segs, d_row_token, d_row_weight from
  * wisp_b200_dispatch_plan with has_shared = 0). d_slot [tokens x world]
- * receives the row of each token in each block (-1: not sent there). */
+ * receives the row of each token in each block (-1: not sent there). d_own
+ * (may be NULL) receives the same rows for this rank's own tokens [tokens x
+ * hidden] (fp16, interleaved K order), the shared expert's input. */
 WispError wisp_b200_ep_dispatch(const uint16_t* d_x, int tokens, int hidden, const int* d_topk_idx,
                                 int top_k, const WispSegment* d_plan_segs, const int* d_row_token,
                                 const float* d_row_weight, int n_experts, int world, int cap,
-                                uint8_t* d_send, int* d_slot, cudaStream_t stream, WispErrCtx* err);
+                                uint8_t* d_send, int* d_slot, uint16_t* d_own,
+                                cudaStream_t stream, WispErrCtx* err);
 
 /* Receive side, from the received blocks d_recv [world blocks] (world * e_loc
  * <= 1024): the entries are gathered expert-contiguous (expert, then source)

@@ -170,16 +170,16 @@ def test_ep_exchange_argument_checks():
     assert L.wisp_b200_ep_block_bytes(7168, 48, 32, 33) == 0       # top_k > 32
     assert L.wisp_b200_ep_block_bytes(100, 48, 32, 8) == 0          # hidden % 8
     # experts do not split over the ranks
-    rc = L.wisp_b200_ep_dispatch(P, 4, 256, P, 2, P, P, P, 8, 3, 4, P, P, None, C.byref(err))
+    rc = L.wisp_b200_ep_dispatch(P, 4, 256, P, 2, P, P, P, 8, 3, 4, P, P, None, None, C.byref(err))
     assert rc == abi.WISP_ERR_INVALID_ARG and b"ep_dispatch" in err.message
     # more tokens than the block capacity
-    rc = L.wisp_b200_ep_dispatch(P, 5, 256, P, 2, P, P, P, 8, 2, 4, P, P, None, C.byref(err))
+    rc = L.wisp_b200_ep_dispatch(P, 5, 256, P, 2, P, P, P, 8, 2, 4, P, P, None, None, C.byref(err))
     assert rc == abi.WISP_ERR_INVALID_ARG
     # misaligned send buffer
-    rc = L.wisp_b200_ep_dispatch(P, 4, 256, P, 2, P, P, P, 8, 2, 4, P + 8, P, None, C.byref(err))
+    rc = L.wisp_b200_ep_dispatch(P, 4, 256, P, 2, P, P, P, 8, 2, 4, P + 8, P, None, None, C.byref(err))
     assert rc == abi.WISP_ERR_INVALID_ARG and b"16-byte" in err.message
     # null pointer
-    rc = L.wisp_b200_ep_dispatch(None, 4, 256, P, 2, P, P, P, 8, 2, 4, P, P, None, C.byref(err))
+    rc = L.wisp_b200_ep_dispatch(None, 4, 256, P, 2, P, P, P, 8, 2, 4, P, P, None, None, C.byref(err))
     assert rc == abi.WISP_ERR_INVALID_ARG
     # too many (rank, local expert) pairs for the single-block receive plan
     rc = L.wisp_b200_ep_recv_plan(P, 8, 200, 4, 2, 256, 0, P, P, P, P, None, C.byref(err))

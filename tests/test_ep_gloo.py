@@ -74,8 +74,11 @@ class CpuOps:
         rows = b[lay.off_rows:lay.off_rows + lay.cap * lay.hidden * 8].view(np.float64)
         return hdr, ent, ew, rows.reshape(lay.cap, lay.hidden)
 
-    def dispatch(self, x, idx, plan_segs, row_token, row_weight, n_experts, world, cap, send, slot):
+    def dispatch(self, x, idx, plan_segs, row_token, row_weight, n_experts, world, cap, send, slot,
+                 own_rows=None):
         lay = self.lay
+        if own_rows is not None:
+            own_rows[:x.shape[0]] = x.double()
         T = x.shape[0]
         slot_ref, entries = dispatch_reference(idx.numpy(), n_experts, world)
         slot.copy_(torch.from_numpy(slot_ref).int())

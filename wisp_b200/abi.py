@@ -113,7 +113,8 @@ SIGNATURES = {
     "wisp_b200_rms_rescale": (_I, [_P, _P, _I, _I, _F, _P, _E]),
     "wisp_b200_combine_rows": (_I, [_P, _P, _P, _I, _I, _P, _P, _E]),
     "wisp_b200_ep_block_bytes": (_SZ, [_I, _I, _I, _I]),
-    "wisp_b200_ep_dispatch": (_I, [_P, _I, _I, _P, _I, _P, _P, _P, _I, _I, _I, _P, _P, _P, _E]),
+    "wisp_b200_ep_dispatch": (_I, [_P, _I, _I, _P, _I, _P, _P, _P, _I, _I, _I, _P, _P, _P, _P,
+                                   _E]),
     "wisp_b200_ep_recv_plan": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _E]),
     "wisp_b200_ep_gather_rows": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _P, _I, _I, _P, _P, _E]),
     "wisp_b200_ep_combine": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _E]),

@@ -27,7 +27,8 @@
 //                        block headers and the entries from the dispatch
 //                        plan.
 //   ep_pack_kernel       token rows (bf16 -> fp16 interleaved) into every
-//                        block that holds them.
+//                        block that holds them (and into the rank's own rows
+//                        for the shared expert).
 //   ep_recv_plan_kernel  one block: from the received headers and entries,
 //                        one segment per local expert over the gathered
 //                        rows, the receive row and weight of each.
@@ -174,8 +175,11 @@ __global__ void __launch_bounds__(1024) ep_dispatch_kernel(
 
 // One block per token: its bf16 row, converted once, into each block that
 // holds it.
+// With own_rows, the converted row also goes there (this rank's own rows for
+// the shared expert's segment).
 __global__ void ep_pack_kernel(const uint16_t* __restrict__ x, int M, const int* __restrict__ slot,
-                               int world, Layout L, uint8_t* __restrict__ send) {
+                               int world, Layout L, uint8_t* __restrict__ send,
+                               uint16_t* __restrict__ own_rows) {
   __shared__ int sl[kMaxWorld];
   const int t = blockIdx.x;
   if (threadIdx.x < world) sl[threadIdx.x] = slot[(size_t)t * world + threadIdx.x];
@@ -198,6 +202,7 @@ __global__ void ep_pack_kernel(const uint16_t* __restrict__ x, int M, const int*
       if (s >= 0)
         *reinterpret_cast<uint4*>(send + q * L.bytes + L.off_rows + ((size_t)s * M + k8) * 2) = o;
     }
+    if (own_rows) *reinterpret_cast<uint4*>(own_rows + (size_t)t * M + k8) = o;
   }
 }
 
@@ -386,7 +391,8 @@ extern "C" WispError wisp_b200_ep_dispatch(const uint16_t* d_x, int tokens, int 
                                            const WispSegment* d_plan_segs, const int* d_row_token,
                                            const float* d_row_weight, int n_experts, int world,
                                            int cap, uint8_t* d_send, int* d_slot,
-                                           cudaStream_t stream, WispErrCtx* err) {
+                                           uint16_t* d_own, cudaStream_t stream,
+                                           WispErrCtx* err) {
   if (!d_x || !d_topk_idx || !d_plan_segs || !d_row_token || !d_row_weight || !d_send || !d_slot)
     return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_dispatch: null pointer argument");
   if (world < 1 || n_experts % world || bad_shape(world, n_experts / world, cap, top_k, hidden) ||
@@ -394,13 +400,14 @@ extern "C" WispError wisp_b200_ep_dispatch(const uint16_t* d_x, int tokens, int 
     return WB_FAIL(WISP_ERR_INVALID_ARG,
                    "ep_dispatch: world=%d experts=%d hidden=%d tokens=%d cap=%d top_k=%d", world,
                    n_experts, hidden, tokens, cap, top_k);
-  if (((uintptr_t)d_x | (uintptr_t)d_send) & 15)
+  if (((uintptr_t)d_x | (uintptr_t)d_send | (uintptr_t)d_own) & 15)
     return WB_FAIL(WISP_ERR_INVALID_ARG, "ep_dispatch: x and the send buffer must be 16-byte aligned");
   const Layout L = ep_layout(hidden, n_experts / world, cap, top_k, 2);
   wb::launch_k(ep_dispatch_kernel, 1, 1024, 0, stream, d_topk_idx, d_plan_segs, d_row_token,
                d_row_weight, tokens, top_k, n_experts, world, L, d_send, d_slot);
   if (tokens > 0)
-    wb::launch_k(ep_pack_kernel, tokens, 128, 0, stream, d_x, hidden, d_slot, world, L, d_send);
+    wb::launch_k(ep_pack_kernel, tokens, 128, 0, stream, d_x, hidden, d_slot, world, L, d_send,
+                 d_own);
   WB_CUDA_CHECK(cudaGetLastError());
   return WISP_OK;
 }

@@ -14,8 +14,8 @@ trip between routing and the expert FFN):
   route own tokens -> plan (rows grouped by expert) -> one fixed-size block
   per destination rank: a token's row once per destination that owns any of
   its experts, plus the (row, weight) entries of its experts there
-  (wisp_b200_ep_dispatch) -> all_to_all of the blocks, meanwhile the rank's
-  own rows are packed -> gather the received rows expert-contiguous (one
+  (wisp_b200_ep_dispatch, which also packs the rank's own rows) -> all_to_all
+  of the blocks -> gather the received rows expert-contiguous (one
   segment per local expert, as on one GPU), the own rows after them as the
   shared expert's segment -> one grouped FFN in mode 0 with the routing
   weights, into one fp32 row per received token (and one per own token for
@@ -136,10 +136,12 @@ class CudaOps:
         abi.call("wisp_b200_combine_rows", y.data_ptr(), row_token.data_ptr(), row_weight.data_ptr(),
                  n_rows, out.shape[1], out.data_ptr(), _stream())
 
-    def dispatch(self, x, idx, plan_segs, row_token, row_weight, n_experts, world, cap, send, slot):
+    def dispatch(self, x, idx, plan_segs, row_token, row_weight, n_experts, world, cap, send, slot,
+                 own_rows=None):
         abi.call("wisp_b200_ep_dispatch", x.data_ptr(), x.shape[0], x.shape[1], idx.data_ptr(),
                  idx.shape[1], plan_segs.data_ptr(), row_token.data_ptr(), row_weight.data_ptr(),
-                 n_experts, world, cap, send.data_ptr(), slot.data_ptr(), _stream())
+                 n_experts, world, cap, send.data_ptr(), slot.data_ptr(),
+                 None if own_rows is None else own_rows.data_ptr(), _stream())
 
     def recv_plan(self, recv, world, e_loc, cap, k, hidden, own, segs, src_pos, weight, total):
         abi.call("wisp_b200_ep_recv_plan", recv.data_ptr(), world, e_loc, cap, k, hidden, own,
@@ -275,21 +277,16 @@ class EpLayer:
     # (loopback_forward).
 
     def dispatch_phase(self, x: torch.Tensor, out: torch.Tensor) -> None:
-        """Route this rank's tokens and fill the send blocks; clear the device
-        error word."""
+        """Route this rank's tokens and fill the send blocks (and, with a
+        shared expert, this rank's own rows in the FFN's input form); clear
+        the device error word."""
         spec, ops = self.spec, self.ops
         ops.clear_flag(self.flag)
         ops.route(self.cfg_route, self.lw, x, self.idx, self.w, self.route_scratch)
         ops.plan(self.cfg_route, self.idx, self.w, self.counts, self.segs, self.row_token,
                  self.row_weight)
         ops.dispatch(x, self.idx, self.segs, self.row_token, self.row_weight, spec.n_experts,
-                     self.world, self.cap, self.send, self.slot)
-
-    def own_phase(self, x: torch.Tensor) -> None:
-        """This rank's own token rows in the FFN's input form, for the shared
-        expert's segment (runs while the blocks travel)."""
-        if self.own:
-            self.ops.pack(x, None, self.T, self.xs)
+                     self.world, self.cap, self.send, self.slot, self.xs)
 
     def expert_phase(self, mark=None) -> None:
         """Local experts over the received rows, gathered so that each expert
@@ -326,19 +323,15 @@ class EpLayer:
 
         ``mark(name)``, if given, is called on the host after each phase has
         been issued (for per-phase CUDA events on the current stream): after
-        route + plan + dispatch ("dispatch"), the own rows' pack ("own_rows"),
-        the wait for the first exchange ("exchange"), the receive plan and
+        route + plan + dispatch ("dispatch"), the first exchange
+        ("exchange"), the receive plan and
         gather ("gather"), the FFN of the local and shared experts ("ffn"), the
         return exchange ("return") and the combine ("combine")."""
         m = mark or (lambda name: None)
         self.dispatch_phase(x, out)
         m("dispatch")
-        # 1. the blocks to the owners; this rank's own rows are packed for
-        #    the shared expert while they travel
-        w_rows = dist.all_to_all_single(self.recv, self.send, group=self.group, async_op=True)
-        self.own_phase(x)
-        m("own_rows")
-        w_rows.wait()
+        # 1. the blocks to the owners
+        dist.all_to_all_single(self.recv, self.send, group=self.group)
         m("exchange")
         # 2. local experts over the received rows and the shared expert over
         #    the own rows, one grouped call
@@ -371,8 +364,6 @@ def loopback_forward(layers: list, xs: list, outs: list) -> None:
     for r in range(W):
         for q in range(W):
             layers[q].recv[r * nb:(r + 1) * nb].copy_(layers[r].send[q * nb:(q + 1) * nb])
-    for r in range(W):
-        layers[r].own_phase(xs[r])
     for r in range(W):
         layers[r].expert_phase()
     cap = layers[0].cap
