@@ -1522,29 +1522,8 @@ WispError wb::grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
   // tensor-core kernels' blocks
   sk.counters = g_counters ? g_counters + 2 * C_COUNT : nullptr;
 
-  int grid_gu = num_sms(), grid_dn = num_sms();
-  if (plans_ready) {
-    // Decode batches (plans from the decode planner): every touched expert's
-    // segment has at most T <= 4 rows, one chunk, so the unit counts are
-    // bounded by the touched experts (exact at one token). Each grid is the
-    // fewest CTAs that keep the same number of units per CTA, so no SM sits
-    // out the last round while the others stream (Mixtral b1: 224 gate/up
-    // units on 112 CTAs instead of 76 CTAs with two and 72 with one).
-    const long long segs = std::min(cfg->n_experts, cfg->tokens * cfg->top_k) +
-                           (cfg->has_shared ? 1 : 0);
-    const long long ugu = segs * pa.per_gu;
-    long long udn = segs * pa.per_dn;
-    long long ks = 1;
-    if (udn > 0 && udn < pa.target)
-      ks = std::min<long long>(std::min(pa.ks_dn, pa.nk_dn), (pa.target + udn - 1) / udn);
-    udn *= std::max(ks, 1LL);
-    auto balanced = [](long long u, int sms) {
-      const long long per = std::max(1LL, (u + sms - 1) / sms);
-      return (int)std::max(1LL, std::min<long long>(sms, (u + per - 1) / per));
-    };
-    grid_gu = balanced(ugu, num_sms());
-    grid_dn = balanced(udn, num_sms());
-  }
+  // (the kernel itself balances its units over the CTAs it keeps)
+  const int grid_gu = num_sms(), grid_dn = num_sms();
   // When no segment can exceed the routing threshold (max_seg_rows, an upper
   // bound the caller knows, e.g. the token count of a decode batch), the
   // tensor-core kernels would find no tiles: they are not launched.
