@@ -464,6 +464,21 @@ __device__ __forceinline__ void compute_stage(float (&acc)[kTPW][NT][4],
 // ---------------------------------------------------------------------------
 // Producer warp.
 // ---------------------------------------------------------------------------
+// The segment of unit u: the last segment at or after `lo` whose first unit
+// is <= u (units is the prefix, units[lo] <= u < units[nseg]; empty
+// segments share the next one's start). A binary search: at batch 1 the
+// touched experts lie scattered among hundreds of empty segments, and a
+// linear scan over them cost each CTA microseconds before its first copy.
+__device__ __forceinline__ int unit_segment(const int32_t* units, int lo, int nseg, int u) {
+  int hi = nseg;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (units[mid] <= u) lo = mid;
+    else hi = mid;
+  }
+  return lo;
+}
+
 template <int MODE>
 __device__ void sk_producer(const SkParams& p, uint8_t* ring, SkSmem* L, int total, int stride,
                             int lane) {
@@ -481,8 +496,7 @@ __device__ void sk_producer(const SkParams& p, uint8_t* ring, SkSmem* L, int tot
   // Units are resolved from the unit prefix (ascending); the segment record
   // of the next unit is requested one unit ahead so its latency hides behind
   // the current unit's stages.
-  int seg = 0;
-  while (L->units[seg + 1] <= (int)blockIdx.x) seg++;
+  int seg = unit_segment(L->units, 0, p.nseg, blockIdx.x);
   WispSegment sg_next = p.segs[seg];
   int seg_next = seg;
   for (int u = blockIdx.x; u < total && ok; u += stride) {
@@ -490,7 +504,9 @@ __device__ void sk_producer(const SkParams& p, uint8_t* ring, SkSmem* L, int tot
     seg = seg_next;
     const int un = u + stride;
     if (un < total) {
-      while (L->units[seg_next + 1] <= un) seg_next++;
+      // a few steps forward (dense segments), else a binary search
+      for (int hop = 0; hop < 4 && L->units[seg_next + 1] <= un; hop++) seg_next++;
+      if (L->units[seg_next + 1] <= un) seg_next = unit_segment(L->units, seg_next + 1, p.nseg, un);
       sg_next = p.segs[seg_next];
     }
     const int chunks = (sg.rows + kCols - 1) / kCols;
