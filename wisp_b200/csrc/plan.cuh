@@ -1,5 +1,6 @@
-// plan.cuh -- the register-path kernel's unit plan, shared by the grouped
-// FFN's planner (grouped.cu) and the decode planner (route.cu).
+// plan.cuh -- the register-path kernel's unit plan, for the grouped FFN's
+// planner (grouped.cu). The decode planner (route.cu) computes the same plan
+// for its one-chunk segments from its own segment scan.
 #pragma once
 
 #include <stdint.h>
@@ -13,8 +14,6 @@ namespace wb {
 // than `target` units would exist, each is cut into up to `max_ksplit`
 // K ranges (at most `nk`, one stage each at least), whose partial sums the
 // down epilogue adds atomically. units[nseg + 1] receives the split.
-// segs is read with plain loads: the decode planner calls this on segments
-// it has just written in the same launch.
 static __device__ void plan_units(const WispSegment* segs, int nseg, int per_seg,
                            int cols, int max_rows, int max_ksplit, int nk, int target,
                            int32_t* __restrict__ units) {
@@ -61,41 +60,6 @@ static __device__ void plan_units(const WispSegment* segs, int nseg, int per_seg
   if (ks < 1) ks = 1;
   for (int i = threadIdx.x; i < nseg; i += blockDim.x) units[i] *= ks;
   if (threadIdx.x == 0) {
-    units[nseg] = total * ks;
-    units[nseg + 1] = ks;
-  }
-}
-
-// The same plan computed by one warp (the decode planner runs the gate/up
-// and down plans on two warps while its other warps copy rows): a warp scan
-// over 32-segment runs with a carry, then the K split.
-static __device__ void plan_units_warp(const WispSegment* segs, int nseg, int per_seg, int cols,
-                                       int max_rows, int max_ksplit, int nk, int target,
-                                       int32_t* __restrict__ units, int lane) {
-  int carry = 0;
-  for (int base = 0; base < nseg; base += 32) {
-    const int s = base + lane;
-    int n = 0;
-    if (s < nseg) {
-      const int rows = segs[s].rows;
-      n = (rows > 0 && rows <= max_rows) ? per_seg * ((rows + cols - 1) / cols) : 0;
-    }
-    int v = n;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, v, o);
-      if (lane >= o) v += y;
-    }
-    if (s < nseg) units[s] = carry + v - n;
-    carry += __shfl_sync(0xffffffffu, v, 31);
-  }
-  const int total = carry;
-  int ks = 1;
-  if (total > 0 && total < target) ks = min(min(max_ksplit, nk), (target + total - 1) / total);
-  if (ks < 1) ks = 1;
-  if (ks > 1)   // each lane scales the entries it wrote
-    for (int i = lane; i < nseg; i += 32) units[i] *= ks;
-  if (lane == 0) {
     units[nseg] = total * ks;
     units[nseg + 1] = ks;
   }

@@ -36,7 +36,6 @@
 
 #include "common.cuh"
 #include "internal.h"
-#include "plan.cuh"
 #include "skinny.h"
 
 using namespace wb;
@@ -1006,11 +1005,12 @@ __global__ void __launch_bounds__(128) pack_rows_q16_kernel(const uint16_t* __re
 //      and the error word;
 //   2. per-expert counts and segments (a block scan over the V experts), the
 //      shared expert holding every token;
-//   3. the rows: slot s of expert e lands at begin[e] + (earlier slots of e),
-//      so each expert's rows are in token order, as in the general plan;
-//   4. the register path's unit plans for gate/up and down, one warp each,
-//      from the segments in shared memory, while the other warps copy every
-//      row's q16 row from its token's (coalesced 16-byte stores).
+//   3. the register path's unit plans for gate/up and down, from the chunk
+//      prefix the scan of step 2 carried along; the rows: slot s of expert e
+//      lands at begin[e] + (earlier slots of e), so each expert's rows are in
+//      token order, as in the general plan;
+//   4. every row's q16 row, copied from its token's (coalesced 16-byte
+//      stores).
 // Every segment has at most T <= 4 rows, so all of them run on the register
 // path and no fp16 rows or tensor-core plans are needed.
 // ---------------------------------------------------------------------------
@@ -1185,6 +1185,7 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const DecodePlan p) {
   __shared__ int s_idx[kDecodeMaxSlots];
   __shared__ float s_w[kDecodeMaxSlots];
   __shared__ __align__(16) WispSegment s_segs[kPlanMaxV];
+  __shared__ int s_cpre[kPlanMaxV];   // register-path chunks before each segment
   __shared__ int s_tok[kDecodeMaxRows];
   __shared__ int warp_tot[32];
   __shared__ int carry;
@@ -1233,7 +1234,8 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const DecodePlan p) {
     if (s_idx[s] < 0 || s_idx[s] >= E) s_idx[s] = -1;
   }
   __syncthreads();
-  // 2. counts and segments
+  // 2. counts and segments; the same scan counts each segment's register-path
+  // chunks (low 16 bits: rows, high bits: chunks; rows <= 132, chunks <= V)
   for (int base = 0; base < V; base += blockDim.x) {
     const int v = base + tid;
     int n = 0;
@@ -1242,7 +1244,8 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const DecodePlan p) {
     } else if (v < V) {
       n = T;
     }
-    int xs = n;
+    const int c = (n > 0 && n <= p.sk_rows) ? (n + p.cols - 1) / p.cols : 0;
+    int xs = n | (c << 16);
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int y = __shfl_up_sync(0xffffffffu, xs, o);
@@ -1264,19 +1267,40 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const DecodePlan p) {
     if (v < V) {
       WispSegment sg;
       sg.expert = v;
-      sg.row_begin = incl - n;
+      sg.row_begin = (incl & 0xFFFF) - n;
       sg.rows = n;
       sg.reserved = 0;
       s_segs[v] = sg;
       p.segs[v] = sg;
       p.counts[v] = n;
+      s_cpre[v] = (incl >> 16) - c;
     }
     __syncthreads();
     if (tid == blockDim.x - 1) carry = incl;
     __syncthreads();
   }
-  const int rows = carry;
-  // 3. rows in token order within each expert
+  const int rows = carry & 0xFFFF, chunks = carry >> 16;
+  // 3. the register path's unit plans (the grouped call's plan_units: per
+  // segment its chunks times the row blocks per chunk; the down projection's
+  // K split when its units would not reach the target), and the rows in
+  // token order within each expert
+  {
+    const int tot_dn = chunks * p.per_dn;
+    int ks = 1;
+    if (tot_dn > 0 && tot_dn < p.target)
+      ks = min(min(p.ks_dn, p.nk_dn), (p.target + tot_dn - 1) / tot_dn);
+    if (ks < 1) ks = 1;
+    for (int v = tid; v < V; v += blockDim.x) {
+      p.units_gu[v] = s_cpre[v] * p.per_gu;
+      p.units_dn[v] = s_cpre[v] * p.per_dn * ks;
+    }
+    if (tid == 0) {
+      p.units_gu[V] = chunks * p.per_gu;
+      p.units_gu[V + 1] = 1;
+      p.units_dn[V] = tot_dn * ks;
+      p.units_dn[V + 1] = ks;
+    }
+  }
   for (int s = tid; s < nslots; s += blockDim.x) {
     const int e = s_idx[s];
     if (e < 0) continue;
@@ -1296,20 +1320,12 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const DecodePlan p) {
     }
   }
   __syncthreads();
-  // 4. the unit plans on warps 0 and 1 (segments read from shared memory)
-  // while the other warps copy each row's q16 row from its token's
-  if (warp == 0) {
-    plan_units_warp(s_segs, V, p.per_gu, p.cols, p.sk_rows, 1, 1, 0, p.units_gu, lane);
-  } else if (warp == 1) {
-    plan_units_warp(s_segs, V, p.per_dn, p.cols, p.sk_rows, p.ks_dn, p.nk_dn, p.target,
-                    p.units_dn, lane);
-  } else {
-    const int wpr = (int)(qbytes / 16);   // 16-byte words per q16 row
-    for (int row = 0; row < rows; row++) {
-      const uint4* src = reinterpret_cast<const uint4*>(s_q16 + (size_t)s_tok[row] * qbytes);
-      uint4* dst = reinterpret_cast<uint4*>(p.xq + (size_t)row * qbytes);
-      for (int wd = tid - 64; wd < wpr; wd += blockDim.x - 64) dst[wd] = src[wd];
-    }
+  // 4. every row's q16 row, copied from its token's
+  const int wpr = (int)(qbytes / 16);   // 16-byte words per q16 row
+  for (int row = 0; row < rows; row++) {
+    const uint4* src = reinterpret_cast<const uint4*>(s_q16 + (size_t)s_tok[row] * qbytes);
+    uint4* dst = reinterpret_cast<uint4*>(p.xq + (size_t)row * qbytes);
+    for (int wd = tid; wd < wpr; wd += blockDim.x) dst[wd] = src[wd];
   }
 }
 
