@@ -1518,6 +1518,8 @@ WispError wb::grouped_ffn_impl(const WispMoeConfig* cfg, const void* d_prepared,
   sk.out = d_out;
   sk.mode = mode;
   sk.error_flag = d_error_flag;
+  // a one-token decode call: the decode planner wrote only q16 row 0
+  sk.tok_row0 = (plans_ready && cfg->tokens == 1) ? 1 : 0;
   // diagnostics: the register-path kernel's counters follow the two
   // tensor-core kernels' blocks
   sk.counters = g_counters ? g_counters + 2 * C_COUNT : nullptr;

@@ -1010,7 +1010,7 @@ __global__ void __launch_bounds__(128) pack_rows_q16_kernel(const uint16_t* __re
 //      lands at begin[e] + (earlier slots of e), so each expert's rows are in
 //      token order, as in the general plan;
 //   4. every row's q16 row, copied from its token's (coalesced 16-byte
-//      stores).
+//      stores); with one token, row 0 alone.
 // Every segment has at most T <= 4 rows, so all of them run on the register
 // path and no fp16 rows or tensor-core plans are needed.
 // ---------------------------------------------------------------------------
@@ -1320,9 +1320,12 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const DecodePlan p) {
     }
   }
   __syncthreads();
-  // 4. every row's q16 row, copied from its token's
+  // 4. every row's q16 row, copied from its token's. With one token every row
+  // is token 0: only row 0 is written, and the gate/up kernel reads its token
+  // rows there (SkLaunch::tok_row0).
   const int wpr = (int)(qbytes / 16);   // 16-byte words per q16 row
-  for (int row = 0; row < rows; row++) {
+  const int ncopy = T == 1 ? min(rows, 1) : rows;
+  for (int row = 0; row < ncopy; row++) {
     const uint4* src = reinterpret_cast<const uint4*>(s_q16 + (size_t)s_tok[row] * qbytes);
     uint4* dst = reinterpret_cast<uint4*>(p.xq + (size_t)row * qbytes);
     for (int wd = tid; wd < wpr; wd += blockDim.x) dst[wd] = src[wd];

@@ -163,6 +163,7 @@ struct SkParams {
   int mode;
   int* error_flag;
   unsigned long long* counters;  // optional wait-cycle counters (diagnostics)
+  int tok_row0;                  // gate/up token rows from row 0 (see SkLaunch)
 };
 
 // Diagnostic counters (cycles summed over warps): consumers' waits for a
@@ -568,7 +569,8 @@ __device__ void sk_producer(const SkParams& p, uint8_t* ring, SkSmem* L, int tot
           tma_load_2d(st + lane * kBoxBytes, lane ? map1 : map0, fb, kg * (kKS / 2),
                       lane ? row1 : row0);
       } else if (lane == 2) {
-        tma_load_3d(st + kOffB, &p.act_map[mi], fb, 0, hdr.prow0, kg * kQ16Lines);
+        tma_load_3d(st + kOffB, &p.act_map[mi], fb, 0,
+                    (MODE == SK_GATEUP && p.tok_row0) ? 0 : hdr.prow0, kg * kQ16Lines);
       } else if (lane == 3) {
         bulk_load(st + kOffS, sc + (size_t)kg * scb, scb, fb);
       } else if (lane == 4) {
@@ -923,6 +925,7 @@ cudaError_t launch_skinny(const SkLaunch& L, int phase, int grid, cudaStream_t s
   p.out = L.out;
   p.mode = L.mode;
   p.error_flag = L.error_flag;
+  p.tok_row0 = L.tok_row0;
   p.counters = L.counters ? L.counters + phase * SC_COUNT : nullptr;
   const CUtensorMap* maps = phase == 0 ? L.xq_maps : L.hq_maps;
   for (int i = 0; i < 2; i++) p.act_map[i] = maps[i];

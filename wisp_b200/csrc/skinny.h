@@ -66,6 +66,10 @@ struct SkLaunch {
   int mode;
   int* error_flag;
   unsigned long long* counters;
+  // 1: a single-token decode call, whose rows all hold token 0; the gate/up
+  // phase reads its token rows from row 0 of the q16 input, the only row the
+  // decode planner writes.
+  int tok_row0;
 };
 
 int skinny_max_rows();
