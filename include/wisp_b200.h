@@ -192,6 +192,14 @@ typedef struct {
     int has_shared;    /* 1: an always-on shared expert of the same shape */
     int router_fp16;   /* router weight dtype: 0 = bf16, 1 = fp16 (the
                           reference's router ABI, wisp_engine.h:534-537) */
+    int deterministic; /* wisp_b200_moe_forward only (other entry points
+                          ignore it). 0: expert outputs meet in fp32 atomics,
+                          so results may differ in the last bits from run to
+                          run. 1: the expert outputs are written as rows and
+                          each token's are summed in a fixed order, so every
+                          run gives the same bits; costs a (T x (top_k +
+                          shared)) x hidden fp32 buffer in the workspace and
+                          the single-token decode fast path. */
 } WispMoeConfig;
 
 /* One int4 matrix in the reference's packing (low nibble = even index,

@@ -81,6 +81,16 @@ def _cfg(**kw):
     return c
 
 
+def test_deterministic_layer_workspace_holds_its_rows():
+    """A deterministic layer's workspace adds one fp32 row per routed row
+    (tokens x (top_k + shared) x hidden) and the per-token row lists."""
+    for shared in (0, 1):
+        base = abi.lib().wisp_b200_moe_workspace_bytes(C.byref(_cfg(has_shared=shared)))
+        det = abi.lib().wisp_b200_moe_workspace_bytes(C.byref(_cfg(has_shared=shared, deterministic=1)))
+        rows = 4 * (2 + shared)
+        assert base > 0 and det >= base + rows * 256 * 4 + 4 * 4 + 4 * rows
+
+
 @pytest.mark.parametrize("kw", [
     dict(hidden=200), dict(inter=100), dict(group_size=32), dict(top_k=0), dict(top_k=9),
     dict(n_experts=2000), dict(tokens=0), dict(scoring=5),

@@ -359,6 +359,37 @@ def test_moe_forward_small(orc, si, T, zeros, path):
     assert_close(out.cpu().numpy()[tokens], ref, what=spec.name)
 
 
+@pytest.mark.parametrize("T", [1, 3, 300])
+@pytest.mark.parametrize("si", [1, 2, 4])
+def test_moe_forward_deterministic(orc, si, T, path):
+    """WispMoeConfig.deterministic: the expert outputs as rows, then each
+    token's rows summed in a fixed order. Two calls give the same bits, the
+    outputs match the oracle, and they agree with the default (atomic)
+    combine within the parity tolerance; top_k 32 + shared is 33 rows a token."""
+    spec = synth.MoeSpec(f"det{si}", tokens=T, seed=500 + si, **SMALL[si])
+    layers, x = synth.make_model(spec, DEV)
+    lw = layers[0]
+    det = MoeLayer(lw, T, deterministic=True)
+    outs = []
+    for _ in range(2):
+        outs.append(det.forward(x).clone())
+        torch.cuda.synchronize()
+        det.check()
+    assert torch.equal(outs[0], outs[1]), "deterministic layer: two calls differ"
+    idx = det.idx.cpu().numpy()
+    w = det.wt.cpu().numpy()
+    i_ref, w_ref, mg = oracle_route(orc, lw, x)
+    check_routing(idx, w, i_ref, w_ref, mg,
+                  near_tie=NEAR_TIE if spec.scoring == abi.WISP_SCORE_SOFTMAX else NEAR_TIE_SIGMOID)
+    tokens = list(range(T)) if T <= 40 else list(range(0, T, 13))
+    ref = oracle_outputs(orc, lw, x, idx, w.astype(np.float64), tokens)
+    got = outs[0].cpu().numpy()
+    assert_close(got[tokens], ref, what=f"{spec.name} deterministic")
+    fused = MoeLayer(lw, T).forward(x)
+    torch.cuda.synchronize()
+    assert_close(got, fused.cpu().numpy().astype(np.float64), what=f"{spec.name} vs fused combine")
+
+
 DECODE = [
     dict(hidden=256, inter=256, n_experts=8, top_k=2, group_size=128),
     dict(hidden=512, inter=256, n_experts=256, top_k=8, group_size=128, has_shared=True,

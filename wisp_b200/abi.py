@@ -45,7 +45,7 @@ class WispMoeConfig(C.Structure):
                 ("n_experts", C.c_int), ("top_k", C.c_int), ("group_size", C.c_int),
                 ("scoring", C.c_int), ("n_groups", C.c_int), ("topk_groups", C.c_int),
                 ("routed_scaling", C.c_float), ("has_shared", C.c_int),
-                ("router_fp16", C.c_int)]
+                ("router_fp16", C.c_int), ("deterministic", C.c_int)]
 
 
 class WispInt4Mat(C.Structure):

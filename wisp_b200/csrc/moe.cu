@@ -80,6 +80,12 @@ struct Workspace {
   int* error_flag;
   uint16_t* xp;
   uint16_t* h;
+  // deterministic layers only: the expert outputs, one fp32 row per routed
+  // row, and each token's rows
+  float* y;
+  int* tok_cnt;
+  int* tok_list;
+  int lanes;   // rows per token: top_k (+ 1 with a shared expert)
   size_t bytes;
   size_t splits;
   int rows;
@@ -105,8 +111,69 @@ Workspace carve(const WispMoeConfig* c, void* base) {
   ws.error_flag = cv.take<int>(base, 1);
   ws.xp = cv.take<uint16_t>(base, (size_t)ws.rows * M);
   ws.h = cv.take<uint16_t>(base, (size_t)ws.rows * I);
+  ws.lanes = k + (c->has_shared ? 1 : 0);
+  ws.y = nullptr;
+  ws.tok_cnt = ws.tok_list = nullptr;
+  if (c->deterministic) {
+    ws.y = cv.take<float>(base, (size_t)ws.rows * M);
+    ws.tok_cnt = cv.take<int>(base, T);
+    ws.tok_list = cv.take<int>(base, (size_t)T * ws.lanes);
+  }
   ws.bytes = (cv.off + 255) & ~(size_t)255;
   return ws;
+}
+
+// Deterministic combine (WispMoeConfig.deterministic). The expert outputs
+// arrive as plain fp32 rows (grouped FFN mode 1: no weights, no atomics, no
+// K split of the down projection); each token's output is then the sum of
+// its rows in ascending row order -- routed experts by index, then the
+// shared expert -- so every run produces the same bits, where the atomics
+// of the fused combine add in whatever order the hardware picks.
+// Step 1: each token's rows into a per-token list (in any order).
+__global__ void token_rows_kernel(const int* __restrict__ row_token,
+                                  const WispSegment* __restrict__ segs, int V, int cap, int lanes,
+                                  int* __restrict__ cnt, int* __restrict__ list) {
+  const int total = min(cap, segs[V - 1].row_begin + segs[V - 1].rows);
+  for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < total; p += gridDim.x * blockDim.x) {
+    const int t = row_token[p];
+    const int j = atomicAdd(cnt + t, 1);
+    if (j < lanes) list[(size_t)t * lanes + j] = p;
+  }
+}
+
+// Step 2: one block per (token, 1024 columns): the token's rows sorted by
+// position, then out[t][m] = sum over them, in that order, of weight * y.
+constexpr int kDetMaxLanes = 64;
+__global__ void combine_ordered_kernel(const float* __restrict__ y,
+                                       const float* __restrict__ row_weight,
+                                       const int* __restrict__ cnt, const int* __restrict__ list,
+                                       int lanes, int M, float* __restrict__ out) {
+  __shared__ int s_p[kDetMaxLanes];
+  __shared__ float s_w[kDetMaxLanes];
+  __shared__ int s_n;
+  const int t = blockIdx.x;
+  if (threadIdx.x == 0) {
+    const int n = min(cnt[t], lanes);
+    for (int i = 0; i < n; i++) {   // insertion sort of at most 33 positions
+      const int v = list[(size_t)t * lanes + i];
+      int j = i;
+      while (j > 0 && s_p[j - 1] > v) {
+        s_p[j] = s_p[j - 1];
+        j--;
+      }
+      s_p[j] = v;
+    }
+    for (int i = 0; i < n; i++) s_w[i] = row_weight[s_p[i]];
+    s_n = n;
+  }
+  __syncthreads();
+  const int n = s_n;
+  const int m1 = min(M, (int)(blockIdx.y + 1) * 1024);
+  for (int m = (int)blockIdx.y * 1024 + threadIdx.x; m < m1; m += blockDim.x) {
+    float acc = 0.f;
+    for (int i = 0; i < n; i++) acc = fmaf(s_w[i], y[(size_t)s_p[i] * M + m], acc);
+    out[(size_t)t * M + m] = acc;
+  }
 }
 
 WispError validate(const WispMoeConfig* c, WispErrCtx* err) {
@@ -207,7 +274,8 @@ extern "C" WispError wisp_b200_moe_forward(const WispMoeConfig* cfg, const WispM
   // Decode batches (T <= 4): router logits, then one planner launch for
   // top-k, dispatch plan, q16 rows, output zeroing and the register path's
   // unit plans, then the register-path gate/up and down launches.
-  if (wb::decode_plan_fits(cfg, wb::grouped_sk_rows(V, V))) {
+  const bool det = cfg->deterministic != 0;
+  if (!det && wb::decode_plan_fits(cfg, wb::grouped_sk_rows(V, V))) {
     // ws.part holds splits * T * E floats, splits >= 1: room for the logits
     e = wb::launch_router_gemv(cfg, d_x, w->router_w, ws.part, stream, err);
     if (e != WISP_OK) return e;
@@ -236,8 +304,22 @@ extern "C" WispError wisp_b200_moe_forward(const WispMoeConfig* cfg, const WispM
                           wb::grouped_xq(ws.grouped, V, ws.rows, cfg->hidden, cfg->inter), ws.segs,
                           V, wb::grouped_sk_rows(V, V), stream, err);
   if (e != WISP_OK) return e;
-  WB_CUDA_CHECK(cudaMemsetAsync(d_out, 0, (size_t)cfg->tokens * cfg->hidden * sizeof(float), stream));
   WB_CUDA_CHECK(cudaMemsetAsync(ws.error_flag, 0, sizeof(int), stream));
+  if (det) {
+    // expert outputs as rows, then the fixed-order combine
+    e = wb::grouped_ffn_impl(cfg, w->prepared, w->experts, V, ws.segs, V, ws.rows, ws.xp, ws.h, 1,
+                             ws.row_token, ws.row_weight, ws.y, ws.grouped, ws.grouped_bytes,
+                             ws.error_flag, true, cfg->tokens, stream, err);
+    if (e != WISP_OK) return e;
+    WB_CUDA_CHECK(cudaMemsetAsync(ws.tok_cnt, 0, (size_t)cfg->tokens * sizeof(int), stream));
+    wb::launch_k(token_rows_kernel, (ws.rows + 255) / 256, 256, 0, stream, ws.row_token, ws.segs, V,
+                 ws.rows, ws.lanes, ws.tok_cnt, ws.tok_list);
+    wb::launch_k(combine_ordered_kernel, dim3(cfg->tokens, (cfg->hidden + 1023) / 1024), 256, 0,
+                 stream, ws.y, ws.row_weight, ws.tok_cnt, ws.tok_list, ws.lanes, cfg->hidden, d_out);
+    WB_CUDA_CHECK(cudaGetLastError());
+    return WISP_OK;
+  }
+  WB_CUDA_CHECK(cudaMemsetAsync(d_out, 0, (size_t)cfg->tokens * cfg->hidden * sizeof(float), stream));
   // A routed expert gets at most one row per token and the shared expert T
   // rows, so no segment exceeds T rows.
   return wb::grouped_ffn_impl(cfg, w->prepared, w->experts, V, ws.segs, V, ws.rows, ws.xp, ws.h, 0,

@@ -22,10 +22,13 @@ class MoeLayer:
     """One routed-expert MoE layer over int4 weights (router, dispatch,
     grouped gate/up + SwiGLU, grouped down + weighted combine)."""
 
-    def __init__(self, weights: LayerWeights, tokens: int):
+    def __init__(self, weights: LayerWeights, tokens: int, deterministic: bool = False):
+        """deterministic: sum each token's expert outputs in a fixed order, so
+        that repeated calls give the same bits (WispMoeConfig.deterministic)."""
         self.w = weights
         self.spec: MoeSpec = weights.spec
         self.cfg = self.spec.cfg(tokens)
+        self.cfg.deterministic = 1 if deterministic else 0
         weights.prepare()
         self._wstruct = weights.weights_struct()
         nbytes = abi.lib().wisp_b200_moe_workspace_bytes(C.byref(self.cfg))
