@@ -1100,7 +1100,9 @@ __device__ __forceinline__ void q16_block(const uint16_t* __restrict__ xr, int b
 // at position r when r experts of the kept groups beat it, where "beat"
 // means a higher score or an equal score at a lower index. That is exactly
 // the order of topk_token's rounds (largest first, lower index on a tie), so
-// indices and weights are identical to it.
+// indices and weights are identical to it. The picks land in s_sel / s_sels
+// (32 per token, in order); sigmoid_slot turns them into a slot's index and
+// weight after the block's next barrier, one thread per slot.
 constexpr int kRouteThreads = 256;
 
 __device__ __forceinline__ void route_bar() {
@@ -1109,7 +1111,7 @@ __device__ __forceinline__ void route_bar() {
 
 __device__ void route_sigmoid_block(const DecodePlan& p, float (*s_score)[1024],
                                     float (*s_gscore)[32], uint32_t* s_gkeep, int* s_sel,
-                                    float* s_sels, int* s_idx, float* s_w) {
+                                    float* s_sels) {
   const int rt = threadIdx.x, lane = rt & 31, w = rt >> 5;
   const int T = p.T, E = p.E, k = p.k, G = p.n_groups, gsz = E / G;
   if (rt < T) s_gkeep[rt] = 0u;
@@ -1168,15 +1170,19 @@ __device__ void route_sigmoid_block(const DecodePlan& p, float (*s_score)[1024],
       s_sels[t * 32 + rank] = v;
     }
   }
-  route_bar();
-  if (rt < T) {
-    float ssum = 0.f;
-    for (int r = 0; r < k; r++) ssum += s_sels[rt * 32 + r];
-    for (int r = 0; r < k; r++) {
-      s_idx[rt * k + r] = s_sel[rt * 32 + r];
-      s_w[rt * k + r] = s_sels[rt * 32 + r] / ssum * p.scaling;
-    }
-  }
+  // (the weights are normalised by the caller, one thread per slot)
+}
+
+// Slot s of a sigmoid-routed token: its expert and its weight, the selected
+// scores normalised over the token's k picks (summed in pick order) times
+// routed_scaling.
+__device__ __forceinline__ void sigmoid_slot(const DecodePlan& p, const int* s_sel,
+                                             const float* s_sels, int s, int& e, float& w) {
+  const int t = s / p.k, r = s - t * p.k;
+  float ssum = 0.f;
+  for (int q = 0; q < p.k; q++) ssum += s_sels[t * 32 + q];
+  e = s_sel[t * 32 + r];
+  w = s_sels[t * 32 + r] / ssum * p.scaling;
 }
 
 template <int PER>
@@ -1210,7 +1216,7 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const DecodePlan p) {
   if (warp < nrw) {
     pdl_wait();
     if (sigmoid)
-      route_sigmoid_block(p, s_score, s_gscore, s_gkeep, s_sel, s_sels, s_idx, s_w);
+      route_sigmoid_block(p, s_score, s_gscore, s_gkeep, s_sel, s_sels);
     else
       topk_token<PER>(p.logits, 1, p.bias, T, warp, E, k, p.scoring, p.n_groups, p.topk_groups,
                       p.scaling, s_idx, s_w, nullptr, lane);
@@ -1229,6 +1235,7 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const DecodePlan p) {
   if (tid == 0) carry = 0;
   __syncthreads();
   for (int s = tid; s < nslots; s += blockDim.x) {
+    if (sigmoid) sigmoid_slot(p, s_sel, s_sels, s, s_idx[s], s_w[s]);
     p.idx[s] = s_idx[s];
     p.w[s] = s_w[s];
     if (s_idx[s] < 0 || s_idx[s] >= E) s_idx[s] = -1;
