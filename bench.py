@@ -42,7 +42,7 @@ UNIT = "tokens/s"
 # 1,476.03 MB of int4 weights and scales, profiles/grouped_ffn_ep_profile_traffic.md):
 # the full-size layer is too large for a multi-pass capture, and its traffic
 # grows with the experts streamed.
-TRAFFIC_PER_ALGORITHMIC_BYTE = 1507.13 / 1476.03
+TRAFFIC_PER_ALGORITHMIC_BYTE = 1507.58 / 1476.03
 
 
 def _peaks() -> dict:
